@@ -1,0 +1,444 @@
+"""Benchmark of the scan hot path: tokens/s of one forward+backward step.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c4] [--impl ours|reference]
+
+A step is one forward and one backward pass of the configured scan through
+the public API (torch.autograd over libmlrec.so) on one batch of synthetic
+inputs. The default workload is config c4 (SSD, bf16, B=32, L=16384, H=32,
+Dh=64, N=128, seg=32), the configuration the scaling target is quoted on.
+Under torchrun (N > 1) every rank takes a contiguous batch range of the same
+global problem (strong scaling, no collective on the data path); the timed
+region is bracketed by a barrier and device synchronisation and the reported
+time is the maximum over ranks.
+
+Printed (rank 0, one JSON line): value = whole-job tokens/s with inputs
+resident in HBM; e2e = the same step with host->device copies of the inputs
+from pinned memory and a device->host read of the result inside the timed
+region; roofline of the dominant kernel (algorithmic bytes / CUDA-event time);
+cpu_baseline = the float32 C restatement of the reference algorithm
+(oracle/ckpt_scan.c) on a bounded sample; clocks sampled during timing.
+
+``--impl reference`` times that CPU restatement on this host's cores (the
+reference itself is MLX/Metal and cannot run here) on the same metric.
+"""
+
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+
+def _env_int(k, d):
+    try:
+        return int(os.environ.get(k, d))
+    except ValueError:
+        return d
+
+
+def _peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            j = json.load(f)
+        return float(j["hbm_gbs"]), float(j["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+# --------------------------------------------------------------------------- #
+# algorithmic bytes per step (compulsory traffic; checkpoints excluded)
+# --------------------------------------------------------------------------- #
+
+def algorithmic_bytes(cfg, batch):
+    """(forward_bytes, backward_bytes): inputs read once and y written (fp32)
+    in the forward; inputs and grad_y (fp32) read and every gradient written
+    in the input dtype in the backward."""
+    es = 4 if cfg["dtype"].itemsize == 4 else 2
+    B, L = batch, cfg["L"]
+    k = cfg["kind"]
+    if k == "ssd":
+        H, Dh, N = cfg["H"], cfg["Dh"], cfg["N"]
+        inp = B * L * H * (Dh + 1 + 2 * N) * es
+        y = B * L * H * Dh * 4
+    elif k == "gla":
+        H, Dh = cfg["H"], cfg["Dh"]
+        inp = B * L * H * (3 * Dh + 1) * es
+        y = B * L * H * Dh * 4
+    elif k == "rglru":
+        inp = B * L * cfg["D"] * 2 * es
+        y = B * L * cfg["D"] * 4
+    else:
+        Dp = cfg["Dp"]
+        inp = B * L * Dp * 5 * es
+        y = B * L * 2 * Dp * 4
+    return inp + y, inp + y + inp
+
+
+# --------------------------------------------------------------------------- #
+# clocks sampled during the timed region
+# --------------------------------------------------------------------------- #
+
+class ClockSampler:
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id):
+        self.gpu_id = gpu_id
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                   "-lms", "200"]
+            if self.gpu_id is not None:
+                cmd.insert(1, f"--id={self.gpu_id}")
+            self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.out = ""
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in (self.out or "").strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx.append(float(parts[1]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[4:8]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def _gpu_uuid(dev):
+    import torch
+    try:
+        u = torch.cuda.get_device_properties(dev).uuid
+        return f"GPU-{u}"
+    except Exception:
+        return None
+
+
+# --------------------------------------------------------------------------- #
+# CPU baseline: the C restatement of the reference algorithm on a sample
+# --------------------------------------------------------------------------- #
+
+def cpu_sample(name):
+    """(inputs, grad_y, fraction of the config's units, description)."""
+    import numpy as np
+    import torch
+    W = importlib.import_module("mlx-recurrence_b200.workloads")
+    cfg = W.CONFIGS[name]
+    k = cfg["kind"]
+    threads = os.cpu_count() or 1
+    if k in ("ssd", "gla") and cfg["B"] * cfg["H"] > 2 * threads and cfg["L"] * cfg["Dh"] > 2 ** 18:
+        hs = min(cfg["H"], max(1, threads))
+        ins = W.make_inputs(name, "cpu", seed=1000, batch=1)
+        ins = [t[:, :, :hs] if t.dim() >= 3 else t[:hs] for t in ins]
+        frac = hs / (cfg["B"] * cfg["H"])
+        desc = f"1 batch row x {hs} of {cfg['H']} heads (full L), scaled by units"
+    elif k in ("rglru", "rotlru") and cfg["B"] > 1 and cfg["B"] * cfg["L"] > 2 ** 15:
+        nb = 1
+        ins = W.make_inputs(name, "cpu", seed=1000, batch=nb)
+        frac = nb / cfg["B"]
+        desc = f"{nb} of {cfg['B']} batch rows (full L and width), scaled by units"
+    else:
+        ins = W.make_inputs(name, "cpu", seed=1000)
+        frac = 1.0
+        desc = "full config"
+    ins = [t.float().contiguous().numpy() for t in ins]
+    g = torch.Generator().manual_seed(7)
+    yshape = ins[0].shape if k != "rotlru" else ins[3].shape
+    gy = torch.randn(yshape, generator=g).numpy()
+    return ins, gy, frac, desc
+
+
+def cpu_baseline(name, reps=1):
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import c_oracle  # float32 C restatement (test infrastructure)
+    W = importlib.import_module("mlx-recurrence_b200.workloads")
+    cfg = W.CONFIGS[name]
+    ins, gy, frac, desc = cpu_sample(name)
+    c_oracle.lib()
+    c_oracle.run(cfg["kind"], ins, cfg["seg"], gy=gy)  # warm-up
+    times = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        c_oracle.run(cfg["kind"], ins, cfg["seg"], gy=gy)
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    tok = W.tokens(cfg) * frac
+    cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+    return {"value": tok / t, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"{desc}; fwd+bwd of oracle/ckpt_scan.c (float32, OpenMP), median of {reps}",
+            "seconds_per_sample": t}
+
+
+# --------------------------------------------------------------------------- #
+# GPU arm
+# --------------------------------------------------------------------------- #
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    pkg = importlib.import_module("mlx-recurrence_b200")
+    W = importlib.import_module("mlx-recurrence_b200.workloads")
+    lib = importlib.import_module("mlx-recurrence_b200._lib").load()
+    rank, world = _env_int("RANK", 0), _env_int("WORLD_SIZE", 1)
+    local = _env_int("LOCAL_RANK", 0)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    name = args.config
+    cfg = W.CONFIGS[name]
+    b0, b1 = W.shard_batch(cfg["B"], rank, world)
+    nb = b1 - b0
+    ins = W.make_inputs(name, dev, seed=1000 + rank, batch=nb)
+    gen = torch.Generator(device=dev).manual_seed(2000 + rank)
+    gy = torch.randn(W.output_shape(name, nb), generator=gen, device=dev, dtype=torch.float32)
+    fn = W.scan_fn(pkg, name)
+    leaves = [t.detach().requires_grad_(True) if t.dtype.is_floating_point else t for t in ins]
+    # A_neg as an expanded view: differentiate w.r.t. its base
+    stream = torch.cuda.current_stream(dev)
+
+    def step(xs, g):
+        y = fn(*xs)
+        torch.autograd.backward(y, g)
+        return y
+
+    ev = lambda: torch.cuda.Event(enable_timing=True)
+
+    # ---- warm-up
+    for _ in range(args.warmup):
+        for x in leaves:
+            x.grad = None
+        step(leaves, gy)
+    torch.cuda.synchronize()
+
+    # ---- timed: inputs resident in HBM
+    fwd_ms, bwd_ms = [], []
+    n_launch0 = lib.mr_launch_count()
+    torch.cuda.reset_peak_memory_stats(dev)
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(_gpu_uuid(dev)) as clk:
+        e_start, e_end = ev(), ev()
+        e_start.record(stream)
+        marks = []
+        for _ in range(args.steps):
+            for x in leaves:
+                x.grad = None
+            a, b, c = ev(), ev(), ev()
+            a.record(stream)
+            y = fn(*leaves)
+            b.record(stream)
+            torch.autograd.backward(y, gy)
+            c.record(stream)
+            marks.append((a, b, c))
+            del y
+        e_end.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+    launches = lib.mr_launch_count() - n_launch0
+    total_ms = e_start.elapsed_time(e_end)
+    for a, b, c in marks:
+        fwd_ms.append(a.elapsed_time(b))
+        bwd_ms.append(b.elapsed_time(c))
+    peak_mb = torch.cuda.max_memory_allocated(dev) / 2 ** 20
+
+    # ---- timed: end to end from pinned host memory
+    # A tensor broadcast along its last axis (SSD's per-head A_neg) travels as
+    # its [.., 1] base and is re-expanded on the device, as a caller would.
+    def compact(t):
+        t = t.detach()
+        if t.dim() > 0 and t.stride(-1) == 0:
+            return t[..., :1].contiguous(), tuple(t.shape)
+        return t.contiguous(), None
+
+    packed = [compact(t) for t in ins]
+    host_ins = [c.to("cpu").pin_memory() for c, _ in packed]
+    shapes = [s for _, s in packed]
+    host_gy = gy.to("cpu").pin_memory()
+    dev_ins = [torch.empty_like(h, device=dev) for h in host_ins]
+    dev_gy = torch.empty_like(gy)
+    y_probe = fn(*leaves)
+    res_host = torch.empty(y_probe[:, -1].shape, dtype=y_probe.dtype, pin_memory=True)
+    del y_probe
+    h2d = sum(t.numel() * t.element_size() for t in host_ins) + host_gy.numel() * 4
+    d2h = res_host.numel() * res_host.element_size()
+    with torch.no_grad():
+        for _ in range(2):  # warm the copy path
+            for d, h in zip(dev_ins, host_ins):
+                d.copy_(h, non_blocking=True)
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    e2e_s, e2e_e = ev(), ev()
+    e2e_s.record(stream)
+    for _ in range(args.steps):
+        with torch.no_grad():
+            for d, h in zip(dev_ins, host_ins):
+                d.copy_(h, non_blocking=True)
+            dev_gy.copy_(host_gy, non_blocking=True)
+        xs = []
+        for d, s in zip(dev_ins, shapes):
+            x = d.detach().requires_grad_(True)
+            xs.append(x.expand(s) if s is not None else x)
+        y = fn(*xs)
+        torch.autograd.backward(y, dev_gy)
+        res_host.copy_(y[:, -1].detach(), non_blocking=True)
+        del y
+    e2e_e.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = e2e_s.elapsed_time(e2e_e)
+
+    # ---- max over ranks
+    t = torch.tensor([total_ms, e2e_ms, statistics.mean(fwd_ms), statistics.mean(bwd_ms)],
+                     dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms, e2e_ms, f_ms, b_ms = t.tolist()
+
+    if rank == 0:
+        hbm, tc, peak_kind = _peaks()
+        tok = W.tokens(cfg)  # whole job: all ranks together process the config
+        fb, bb = algorithmic_bytes(cfg, nb)
+        dom = ("backward", bb, b_ms) if b_ms >= f_ms else ("forward", fb, f_ms)
+        achieved = dom[1] / (dom[2] * 1e-3) / 1e9
+        out = {
+            "metric": "tokens/s fwd+bwd",
+            "value": tok * args.steps / (total_ms * 1e-3),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": total_ms / args.steps,
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": {4: "f32", 2: "bf16"}[cfg["dtype"].itemsize] + " inputs, f32 state",
+            "data": "synthetic (seeded, BASELINE config distributions)",
+            "config": {"workload": W.DESCRIPTION[name], "name": name, "global_batch": cfg["B"],
+                       "seq_len": cfg["L"], "parallelism": f"batch-shard x{world}",
+                       "l2": "inputs larger than L2" if fb > 126e6 else "inputs smaller than L2 (no flush)"},
+            "fwd_ms": f_ms,
+            "bwd_ms": b_ms,
+            "fwd_tokens_per_s": tok / (f_ms * 1e-3),
+            "peak_mb": peak_mb,
+            "e2e": {"value": tok * args.steps / (e2e_ms * 1e-3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "roofline": {"bound": "hbm", "kernel": f"{cfg['kind']} {dom[0]}",
+                         "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                         "frac": achieved / hbm, "traffic": None,
+                         "algorithmic_bytes_per_launch": dom[1],
+                         "peak_source": f"{peak_kind} hbm_gbs"},
+            "gpu_launches": int(launches),
+            "clocks": clk.summary(),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            out["cpu_baseline"] = cpu_baseline(name)
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_reference(args):
+    rank = _env_int("RANK", 0)
+    if rank != 0:
+        return
+    W = importlib.import_module("mlx-recurrence_b200.workloads")
+    name = args.config
+    cfg = W.CONFIGS[name]
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import c_oracle
+    ins, gy, frac, desc = cpu_sample(name)
+    c_oracle.lib()
+    for _ in range(args.warmup):
+        c_oracle.run(cfg["kind"], ins, cfg["seg"], gy=gy)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        c_oracle.run(cfg["kind"], ins, cfg["seg"], gy=gy)
+    dt = time.perf_counter() - t0
+    tok = W.tokens(cfg) * frac
+    v = tok * args.steps / dt
+    cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+    out = {
+        "impl": "reference",
+        "metric": "tokens/s fwd+bwd",
+        "value": v,
+        "unit": "tokens/s",
+        "n_gpus": _env_int("WORLD_SIZE", 1),
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": dt * 1e3 / args.steps,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded, BASELINE config distributions)",
+        "config": {"workload": W.DESCRIPTION[name], "name": name, "global_batch": cfg["B"],
+                   "seq_len": cfg["L"]},
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"{desc}; the reference (MLX/Metal) cannot run on this host, so its "
+                                   "algorithm is timed as the float32 C restatement oracle/ckpt_scan.c"},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(out), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", default="c4", choices=["c0", "c1", "c2", "c3", "c4"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

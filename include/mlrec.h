@@ -1,0 +1,158 @@
+/*
+ * mlrec.h - C ABI of the B200 scan library (libmlrec.so).
+ *
+ * One forward and one backward entry point per scan plug-in of
+ * mlx-recurrence v0.3.0. Each pair replaces one reference plug-in's Metal
+ * kernel launch plus its MLX epilogue:
+ *
+ *   mr_ssd_fwd     <- mlx_recurrence/ssd.py:54-135     (_ssd_forward_kernel)
+ *   mr_ssd_bwd     <- mlx_recurrence/ssd.py:142-307    (_ssd_backward_kernel + mx.sum epilogue)
+ *   mr_gla_fwd     <- mlx_recurrence/gla.py:49-123     (_gla_forward_kernel)
+ *   mr_gla_bwd     <- mlx_recurrence/gla.py:130-270    (_gla_backward_kernel + mx.sum epilogue)
+ *   mr_rglru_fwd   <- mlx_recurrence/rglru.py:64-123   (_rglru_forward_kernel)
+ *   mr_rglru_bwd   <- mlx_recurrence/rglru.py:130-203  (_rglru_backward_kernel)
+ *   mr_rotlru_fwd  <- mlx_recurrence/rotlru.py:80-146  (_rotlru_forward_kernel)
+ *   mr_rotlru_bwd  <- mlx_recurrence/rotlru.py:153-266 (_rotlru_backward_kernel)
+ *   mr_check_segment_shape <- mlx_recurrence/_chassis.py:92-115 (check_segment_shape)
+ *
+ * Conventions (all entry points):
+ *   - Every data pointer is a CUDA device pointer owned by the caller;
+ *     tensors are dense row-major in the shapes given below.
+ *   - `dtype` selects the element type of the primal inputs and of the
+ *     gradients written for them: MR_F32, MR_BF16 or MR_F16. Outputs y,
+ *     h_ckpt and every state are float32, as in the reference (its
+ *     output_dtypes are always mx.float32, e.g. ssd.py:128). All state
+ *     and accumulation is float32.
+ *   - `stream` is a cudaStream_t (passed as void*). Work is enqueued on it;
+ *     no entry point synchronises the device or allocates memory.
+ *   - Return value: MR_OK, or an MR_E_* code with a message available from
+ *     mr_last_error() (thread-local). Shape errors are detected on the host
+ *     before any launch, with the reference's messages.
+ *   - Checkpoints h_ckpt hold the state at the end of every `seg`-step
+ *     segment, in the reference's layouts; the last one is the final state.
+ *   - `grad_final` (nullable) is the cotangent of the final state. The
+ *     reference's VJPs drop it (ssd.py:334, gla.py:293, rglru.py:226,
+ *     rotlru.py:571); here it seeds the adjoint, matching the reference's
+ *     pure per-step loops.
+ */
+#ifndef MLREC_H_
+#define MLREC_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MR_API __attribute__((visibility("default")))
+#else
+#define MR_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  MR_OK = 0,
+  MR_E_SHAPE = 1,     /* shape rule violated (reference: ValueError)        */
+  MR_E_DTYPE = 2,     /* unsupported dtype code                             */
+  MR_E_ALIGN = 3,     /* a pointer is not 16-byte aligned                   */
+  MR_E_LAUNCH = 4,    /* a CUDA launch failed                               */
+  MR_E_WORKSPACE = 5, /* workspace missing or smaller than required         */
+  MR_E_DEVICE = 6     /* no usable sm_100 device                             */
+};
+
+enum { MR_F32 = 0, MR_BF16 = 1, MR_F16 = 2 };
+
+/* ABI revision of this header. */
+MR_API int mr_abi_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+MR_API const char* mr_last_error(void);
+
+/* Number of kernels this library has launched in this process (all threads). */
+MR_API uint64_t mr_launch_count(void);
+
+/* Shape rule of the checkpoint/recompute pattern: seg > 0, L % seg == 0 and
+ * lane_dim % 32 == 0 (mlx_recurrence/_chassis.py:92-115). lane_name names
+ * lane_dim in the message. Host-only, launches nothing. */
+MR_API int mr_check_segment_shape(int64_t L, int64_t seg, int64_t lane_dim, const char* lane_name);
+
+/* ---------------------------------------------------------------- SSD ---
+ * u [B,L,H,Dh], delta [B,L,H], Bm/Cm [B,L,H,N] in `dtype`;
+ * A_neg float32, element (h,n) at A_neg[h*a_stride_h + n*a_stride_n]
+ *   (a_stride_n == 0: one decay rate per head, the Mamba-2 case);
+ * y [B,L,H,Dh] f32; h_ckpt [B,L/seg,H,N,Dh] f32 (reference layout, ssd.py:67). */
+MR_API int mr_ssd_fwd(const void* u, const void* delta, const void* Bm, const void* Cm,
+               const float* A_neg, int64_t a_stride_h, int64_t a_stride_n, int dtype,
+               int64_t batch, int64_t L, int64_t H, int64_t Dh, int64_t N, int64_t seg,
+               float* y, float* h_ckpt, void* stream);
+
+/* Bytes of device workspace mr_ssd_bwd needs for these arguments. */
+MR_API size_t mr_ssd_bwd_workspace_bytes(int dtype, int64_t batch, int64_t L, int64_t H, int64_t Dh,
+                                  int64_t N, int64_t seg, int64_t a_stride_n);
+
+/* grad_y [B,L,H,Dh] f32; grad_final [B,H,Dh,N] f32 or NULL;
+ * grad_u/grad_delta/grad_B/grad_C in `dtype`; grad_A [H,N] f32 (summed over
+ * the batch, ssd.py:305). */
+MR_API int mr_ssd_bwd(const float* grad_y, const float* grad_final, const float* h_ckpt,
+               const void* u, const void* delta, const void* Bm, const void* Cm,
+               const float* A_neg, int64_t a_stride_h, int64_t a_stride_n, int dtype,
+               int64_t batch, int64_t L, int64_t H, int64_t Dh, int64_t N, int64_t seg,
+               void* grad_u, void* grad_delta, void* grad_B, void* grad_C, float* grad_A,
+               void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------- GLA ---
+ * q,k,v [B,L,H,Dh], gates [B,L,H] in `dtype`; y [B,L,H,Dh] f32;
+ * h_ckpt [B,L/seg,H,Dh(i),Dh(j)] f32 (gla.py:62). */
+MR_API int mr_gla_fwd(const void* q, const void* k, const void* v, const void* gates, int dtype,
+               int64_t batch, int64_t L, int64_t H, int64_t Dh, int64_t seg,
+               float* y, float* h_ckpt, void* stream);
+
+MR_API size_t mr_gla_bwd_workspace_bytes(int dtype, int64_t batch, int64_t L, int64_t H, int64_t Dh,
+                                  int64_t seg);
+
+/* grad_y [B,L,H,Dh] f32; grad_final [B,H,Dh,Dh] f32 or NULL; grads in `dtype`. */
+MR_API int mr_gla_bwd(const float* grad_y, const float* grad_final, const float* h_ckpt,
+               const void* q, const void* k, const void* v, const void* gates, int dtype,
+               int64_t batch, int64_t L, int64_t H, int64_t Dh, int64_t seg,
+               void* grad_q, void* grad_k, void* grad_v, void* grad_gates,
+               void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------- RG-LRU ---
+ * a, x [B,L,D] in `dtype`; y [B,L,D] f32; h_ckpt [B,L/seg,D] f32 (rglru.py:76). */
+MR_API int mr_rglru_fwd(const void* a, const void* x, int dtype, int64_t batch, int64_t L, int64_t D,
+                 int64_t seg, float* y, float* h_ckpt, void* stream);
+
+/* Bytes of device workspace mr_rglru_bwd needs (0 unless seg > 64). */
+MR_API size_t mr_rglru_bwd_workspace_bytes(int dtype, int64_t batch, int64_t L, int64_t D, int64_t seg);
+
+/* grad_y [B,L,D] f32; grad_final [B,D] f32 or NULL; grad_a, grad_x in `dtype`.
+ * workspace may be NULL when mr_rglru_bwd_workspace_bytes() returns 0. */
+MR_API int mr_rglru_bwd(const float* grad_y, const float* grad_final, const float* h_ckpt,
+                 const void* a, const void* x, int dtype, int64_t batch, int64_t L, int64_t D,
+                 int64_t seg, void* grad_a, void* grad_x, void* workspace,
+                 size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------- rotLRU ---
+ * a, cs, sn [B,L,Dp], x [B,L,2*Dp] (pairs interleaved) in `dtype`;
+ * y [B,L,2*Dp] f32; h_ckpt [B,L/seg,2*Dp] f32 (rotlru.py:369). */
+MR_API int mr_rotlru_fwd(const void* a, const void* cs, const void* sn, const void* x, int dtype,
+                  int64_t batch, int64_t L, int64_t Dp, int64_t seg,
+                  float* y, float* h_ckpt, void* stream);
+
+/* Bytes of device workspace mr_rotlru_bwd needs (0 unless seg > 64). */
+MR_API size_t mr_rotlru_bwd_workspace_bytes(int dtype, int64_t batch, int64_t L, int64_t Dp, int64_t seg);
+
+/* grad_y [B,L,2Dp] f32; grad_final [B,2Dp] f32 or NULL; grads in `dtype`.
+ * workspace may be NULL when mr_rotlru_bwd_workspace_bytes() returns 0. */
+MR_API int mr_rotlru_bwd(const float* grad_y, const float* grad_final, const float* h_ckpt,
+                  const void* a, const void* cs, const void* sn, const void* x, int dtype,
+                  int64_t batch, int64_t L, int64_t Dp, int64_t seg,
+                  void* grad_a, void* grad_cs, void* grad_sn, void* grad_x,
+                  void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MLREC_H_ */

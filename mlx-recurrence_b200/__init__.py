@@ -1,0 +1,45 @@
+"""mlx-recurrence for NVIDIA B200: the four v2 linear-recurrence scan plug-ins
+of mlx-recurrence v0.3.0 (``mlx_recurrence/__init__.py:21-90``), rebuilt as
+torch.autograd.Functions over a C-ABI library of sm_100a CUDA kernels
+(``libmlrec.so``, ABI in ``include/mlrec.h``).
+
+    ssd     - Mamba-2-style head-wise SSD selective scan
+    gla     - gated linear attention recurrence
+    rglru   - RG-LRU diagonal recurrence
+    rotlru  - rotational LRU (complex-diagonal over interleaved pairs)
+
+Import with ``importlib.import_module("mlx-recurrence_b200")`` (the directory
+name carries a hyphen); after that the package is also registered as
+``mlx_recurrence_b200``.
+"""
+
+import sys as _sys
+
+from ._chassis import DEFAULT_SEG, check_segment_shape, get_or_build_kernel, parity_check
+from .gla import gla_scan, gla_scan_reference, gla_scan_with_state
+from .rglru import rglru_scan, rglru_scan_reference, rglru_scan_with_state
+from .rotlru import rotlru_scan, rotlru_scan_reference, rotlru_scan_with_state
+from .ssd import ssd_scan, ssd_scan_reference, ssd_scan_with_state
+
+__all__ = [
+    "ssd_scan",
+    "ssd_scan_with_state",
+    "ssd_scan_reference",
+    "gla_scan",
+    "gla_scan_with_state",
+    "gla_scan_reference",
+    "rglru_scan",
+    "rglru_scan_with_state",
+    "rglru_scan_reference",
+    "rotlru_scan",
+    "rotlru_scan_with_state",
+    "rotlru_scan_reference",
+    "DEFAULT_SEG",
+    "get_or_build_kernel",
+    "check_segment_shape",
+    "parity_check",
+]
+
+__version__ = "0.3.0+b200.1"
+
+_sys.modules.setdefault("mlx_recurrence_b200", _sys.modules[__name__])

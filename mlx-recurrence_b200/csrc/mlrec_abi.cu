@@ -1,0 +1,316 @@
+// extern "C" entry points of libmlrec.so (declared in include/mlrec.h):
+// host-side validation with the reference's messages, dtype dispatch and
+// launch of the scan kernels. Nothing here allocates or synchronises.
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <atomic>
+
+#include "common.cuh"
+
+namespace mr {
+
+static thread_local char g_err[512] = "";
+
+int set_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+static std::atomic<uint64_t> g_launches{0};
+
+int check_launch(const char* what) {
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(MR_E_LAUNCH, "%s: %s", what, cudaGetErrorString(e));
+  return MR_OK;
+}
+
+// ---- launchers defined in the kernel translation units ----------------------
+template <typename T> int rglru_fwd_launch(const void*, const void*, int64_t, int64_t, int64_t, int64_t, float*, float*, cudaStream_t);
+template <typename T> int rglru_bwd_launch(const float*, const float*, const float*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, void*, void*, float*, cudaStream_t);
+template <typename T> int rotlru_fwd_launch(const void*, const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, float*, float*, cudaStream_t);
+template <typename T> int rotlru_bwd_launch(const float*, const float*, const float*, const void*, const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, void*, void*, void*, void*, float*, cudaStream_t);
+template <typename T> int ssd_seq_fwd_launch(const void*, const void*, const void*, const void*, const float*, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, float*, float*, cudaStream_t);
+template <typename T> int ssd_seq_bwd_launch(const float*, const float*, const float*, const void*, const void*, const void*, const void*, const float*, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, void*, void*, void*, void*, float*, void*, cudaStream_t);
+template <typename T> int gla_seq_fwd_launch(const void*, const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, int64_t, float*, float*, cudaStream_t);
+template <typename T> int gla_seq_bwd_launch(const float*, const float*, const float*, const void*, const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, int64_t, void*, void*, void*, void*, void*, cudaStream_t);
+size_t rglru_bwd_ws_bytes(int64_t, int64_t, int64_t, int64_t);
+size_t rotlru_bwd_ws_bytes(int64_t, int64_t, int64_t, int64_t);
+size_t ssd_seq_bwd_ws_bytes(int64_t, int64_t, int64_t, int64_t, int64_t, int64_t);
+size_t gla_seq_bwd_ws_bytes(int64_t, int64_t, int64_t, int64_t, int64_t);
+bool ssd_seq_supported(int64_t Dh, int64_t N);
+bool gla_seq_supported(int64_t Dh);
+
+// ---- validation helpers -----------------------------------------------------
+static int check_seg(int64_t L, int64_t seg, int64_t lane_dim, const char* lane_name) {
+  // messages: mlx_recurrence/_chassis.py:104-115
+  if (seg <= 0) return set_error(MR_E_SHAPE, "seg must be positive, got %lld", (long long)seg);
+  if (L % seg != 0)
+    return set_error(MR_E_SHAPE,
+                     "sequence length L=%lld must be divisible by seg=%lld (segment-checkpoint "
+                     "pattern tiles L into L/seg segments)",
+                     (long long)L, (long long)seg);
+  if (lane_dim % 32 != 0)
+    return set_error(MR_E_SHAPE,
+                     "%s=%lld must be a multiple of 32 (fused gradient reductions use 32-lane "
+                     "simdgroups)",
+                     lane_name, (long long)lane_dim);
+  return MR_OK;
+}
+
+static int check_dims(const char* what, int64_t batch, int64_t L, int64_t other) {
+  if (batch <= 0 || L <= 0 || other <= 0)
+    return set_error(MR_E_SHAPE, "%s: every dimension must be positive", what);
+  if (L > (int64_t)INT32_MAX / 2) return set_error(MR_E_SHAPE, "%s: L=%lld too large", what, (long long)L);
+  if (batch > 65535) return set_error(MR_E_SHAPE, "%s: batch=%lld exceeds 65535", what, (long long)batch);
+  return MR_OK;
+}
+
+static int check_dtype(int dtype) {
+  if (dtype != MR_F32 && dtype != MR_BF16 && dtype != MR_F16)
+    return set_error(MR_E_DTYPE, "unsupported dtype code %d (0=f32, 1=bf16, 2=f16)", dtype);
+  return MR_OK;
+}
+
+static int check_ptrs(const char* what, std::initializer_list<const void*> ps) {
+  int i = 0;
+  for (const void* p : ps) {
+    if (p == nullptr) return set_error(MR_E_ALIGN, "%s: pointer argument %d is NULL", what, i);
+    if (((uintptr_t)p) & 15u)
+      return set_error(MR_E_ALIGN, "%s: pointer argument %d is not 16-byte aligned", what, i);
+    ++i;
+  }
+  return MR_OK;
+}
+
+static int check_opt_ptr(const char* what, const void* p) {
+  if (p != nullptr && (((uintptr_t)p) & 15u))
+    return set_error(MR_E_ALIGN, "%s: optional pointer is not 16-byte aligned", what);
+  return MR_OK;
+}
+
+#define MR_TRY(x)              \
+  do {                         \
+    const int rc_ = (x);       \
+    if (rc_ != MR_OK) return rc_; \
+  } while (0)
+
+#define MR_DTYPE_SWITCH(dtype, CALL)                 \
+  switch (dtype) {                                   \
+    case MR_F32: { using T = float; return CALL; }   \
+    case MR_BF16: { using T = __nv_bfloat16; return CALL; } \
+    default: { using T = __half; return CALL; }      \
+  }
+
+}  // namespace mr
+
+using namespace mr;
+
+extern "C" {
+
+int mr_abi_version(void) { return 1; }
+
+const char* mr_last_error(void) { return g_err; }
+
+uint64_t mr_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int mr_check_segment_shape(int64_t L, int64_t seg, int64_t lane_dim, const char* lane_name) {
+  g_err[0] = 0;
+  return check_seg(L, seg, lane_dim, lane_name ? lane_name : "lane dimension");
+}
+
+// ------------------------------------------------------------------ RG-LRU ---
+int mr_rglru_fwd(const void* a, const void* x, int dtype, int64_t batch, int64_t L, int64_t D,
+                 int64_t seg, float* y, float* h_ckpt, void* stream) {
+  g_err[0] = 0;
+  MR_TRY(check_dims("mr_rglru_fwd", batch, L, D));
+  MR_TRY(check_seg(L, seg, D, "D"));
+  MR_TRY(check_dtype(dtype));
+  MR_TRY(check_ptrs("mr_rglru_fwd", {a, x, y, h_ckpt}));
+  cudaStream_t st = (cudaStream_t)stream;
+  MR_DTYPE_SWITCH(dtype, rglru_fwd_launch<T>(a, x, batch, L, D, seg, y, h_ckpt, st));
+}
+
+size_t mr_rglru_bwd_workspace_bytes(int dtype, int64_t batch, int64_t L, int64_t D, int64_t seg) {
+  (void)dtype;
+  if (batch <= 0 || L <= 0 || D <= 0 || seg <= 0) return 0;
+  return rglru_bwd_ws_bytes(batch, L, D, seg);
+}
+
+int mr_rglru_bwd(const float* grad_y, const float* grad_final, const float* h_ckpt,
+                    const void* a, const void* x, int dtype, int64_t batch, int64_t L, int64_t D,
+                    int64_t seg, void* grad_a, void* grad_x, void* workspace,
+                    size_t workspace_bytes, void* stream) {
+  g_err[0] = 0;
+  MR_TRY(check_dims("mr_rglru_bwd", batch, L, D));
+  MR_TRY(check_seg(L, seg, D, "D"));
+  MR_TRY(check_dtype(dtype));
+  MR_TRY(check_ptrs("mr_rglru_bwd", {grad_y, h_ckpt, a, x, grad_a, grad_x}));
+  MR_TRY(check_opt_ptr("mr_rglru_bwd", grad_final));
+  const size_t need = rglru_bwd_ws_bytes(batch, L, D, seg);
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need))
+    return set_error(MR_E_WORKSPACE, "mr_rglru_bwd: workspace of %zu bytes required, got %zu",
+                     need, workspace_bytes);
+  MR_TRY(check_opt_ptr("mr_rglru_bwd", workspace));
+  cudaStream_t st = (cudaStream_t)stream;
+  MR_DTYPE_SWITCH(dtype, rglru_bwd_launch<T>(grad_y, grad_final, h_ckpt, a, x, batch, L, D, seg,
+                                             grad_a, grad_x, (float*)workspace, st));
+}
+
+// ------------------------------------------------------------------ rotLRU ---
+int mr_rotlru_fwd(const void* a, const void* cs, const void* sn, const void* x, int dtype,
+                  int64_t batch, int64_t L, int64_t Dp, int64_t seg, float* y, float* h_ckpt,
+                  void* stream) {
+  g_err[0] = 0;
+  MR_TRY(check_dims("mr_rotlru_fwd", batch, L, Dp));
+  MR_TRY(check_seg(L, seg, 2 * Dp, "D"));
+  MR_TRY(check_dtype(dtype));
+  MR_TRY(check_ptrs("mr_rotlru_fwd", {a, cs, sn, x, y, h_ckpt}));
+  cudaStream_t st = (cudaStream_t)stream;
+  MR_DTYPE_SWITCH(dtype, rotlru_fwd_launch<T>(a, cs, sn, x, batch, L, Dp, seg, y, h_ckpt, st));
+}
+
+size_t mr_rotlru_bwd_workspace_bytes(int dtype, int64_t batch, int64_t L, int64_t Dp, int64_t seg) {
+  (void)dtype;
+  if (batch <= 0 || L <= 0 || Dp <= 0 || seg <= 0) return 0;
+  return rotlru_bwd_ws_bytes(batch, L, Dp, seg);
+}
+
+int mr_rotlru_bwd(const float* grad_y, const float* grad_final, const float* h_ckpt,
+                     const void* a, const void* cs, const void* sn, const void* x, int dtype,
+                     int64_t batch, int64_t L, int64_t Dp, int64_t seg, void* grad_a,
+                     void* grad_cs, void* grad_sn, void* grad_x, void* workspace,
+                     size_t workspace_bytes, void* stream) {
+  g_err[0] = 0;
+  MR_TRY(check_dims("mr_rotlru_bwd", batch, L, Dp));
+  MR_TRY(check_seg(L, seg, 2 * Dp, "D"));
+  MR_TRY(check_dtype(dtype));
+  MR_TRY(check_ptrs("mr_rotlru_bwd", {grad_y, h_ckpt, a, cs, sn, x, grad_a, grad_cs, grad_sn, grad_x}));
+  MR_TRY(check_opt_ptr("mr_rotlru_bwd", grad_final));
+  const size_t need = rotlru_bwd_ws_bytes(batch, L, Dp, seg);
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need))
+    return set_error(MR_E_WORKSPACE, "mr_rotlru_bwd: workspace of %zu bytes required, got %zu",
+                     need, workspace_bytes);
+  MR_TRY(check_opt_ptr("mr_rotlru_bwd", workspace));
+  cudaStream_t st = (cudaStream_t)stream;
+  MR_DTYPE_SWITCH(dtype, rotlru_bwd_launch<T>(grad_y, grad_final, h_ckpt, a, cs, sn, x, batch, L,
+                                              Dp, seg, grad_a, grad_cs, grad_sn, grad_x,
+                                              (float*)workspace, st));
+}
+
+// --------------------------------------------------------------------- SSD ---
+static int ssd_common_checks(const char* what, int dtype, int64_t batch, int64_t L, int64_t H,
+                             int64_t Dh, int64_t N, int64_t seg) {
+  MR_TRY(check_dims(what, batch, L, H));
+  if (Dh <= 0 || N <= 0) return set_error(MR_E_SHAPE, "%s: every dimension must be positive", what);
+  MR_TRY(check_seg(L, seg, Dh, "Dh"));
+  MR_TRY(check_dtype(dtype));
+  if (!ssd_seq_supported(Dh, N))
+    return set_error(MR_E_SHAPE, "%s: this build supports Dh in {32,64,96,128} and N <= 128, got Dh=%lld N=%lld",
+                     what, (long long)Dh, (long long)N);
+  if (batch * H > (int64_t)INT32_MAX) return set_error(MR_E_SHAPE, "%s: batch*H too large", what);
+  return MR_OK;
+}
+
+int mr_ssd_fwd(const void* u, const void* delta, const void* Bm, const void* Cm, const float* A_neg,
+               int64_t a_stride_h, int64_t a_stride_n, int dtype, int64_t batch, int64_t L,
+               int64_t H, int64_t Dh, int64_t N, int64_t seg, float* y, float* h_ckpt,
+               void* stream) {
+  g_err[0] = 0;
+  MR_TRY(ssd_common_checks("mr_ssd_fwd", dtype, batch, L, H, Dh, N, seg));
+  MR_TRY(check_ptrs("mr_ssd_fwd", {u, delta, Bm, Cm, y, h_ckpt}));
+  if (A_neg == nullptr) return set_error(MR_E_ALIGN, "mr_ssd_fwd: A_neg is NULL");
+  cudaStream_t st = (cudaStream_t)stream;
+  MR_DTYPE_SWITCH(dtype, ssd_seq_fwd_launch<T>(u, delta, Bm, Cm, A_neg, a_stride_h, a_stride_n,
+                                               batch, L, H, Dh, N, seg, y, h_ckpt, st));
+}
+
+size_t mr_ssd_bwd_workspace_bytes(int dtype, int64_t batch, int64_t L, int64_t H, int64_t Dh,
+                                  int64_t N, int64_t seg, int64_t a_stride_n) {
+  (void)dtype;
+  (void)a_stride_n;
+  if (batch <= 0 || L <= 0 || H <= 0 || Dh <= 0 || N <= 0 || seg <= 0) return 0;
+  return ssd_seq_bwd_ws_bytes(batch, L, H, Dh, N, seg);
+}
+
+int mr_ssd_bwd(const float* grad_y, const float* grad_final, const float* h_ckpt, const void* u,
+               const void* delta, const void* Bm, const void* Cm, const float* A_neg,
+               int64_t a_stride_h, int64_t a_stride_n, int dtype, int64_t batch, int64_t L,
+               int64_t H, int64_t Dh, int64_t N, int64_t seg, void* grad_u, void* grad_delta,
+               void* grad_B, void* grad_C, float* grad_A, void* workspace,
+               size_t workspace_bytes, void* stream) {
+  g_err[0] = 0;
+  MR_TRY(ssd_common_checks("mr_ssd_bwd", dtype, batch, L, H, Dh, N, seg));
+  MR_TRY(check_ptrs("mr_ssd_bwd", {grad_y, h_ckpt, u, delta, Bm, Cm, grad_u, grad_delta, grad_B, grad_C}));
+  MR_TRY(check_opt_ptr("mr_ssd_bwd", grad_final));
+  if (A_neg == nullptr || grad_A == nullptr)
+    return set_error(MR_E_ALIGN, "mr_ssd_bwd: A_neg / grad_A is NULL");
+  const size_t need = ssd_seq_bwd_ws_bytes(batch, L, H, Dh, N, seg);
+  if (workspace == nullptr || workspace_bytes < need)
+    return set_error(MR_E_WORKSPACE, "mr_ssd_bwd: workspace of %zu bytes required, got %zu", need,
+                     workspace_bytes);
+  MR_TRY(check_opt_ptr("mr_ssd_bwd", workspace));
+  cudaStream_t st = (cudaStream_t)stream;
+  MR_DTYPE_SWITCH(dtype, ssd_seq_bwd_launch<T>(grad_y, grad_final, h_ckpt, u, delta, Bm, Cm, A_neg,
+                                               a_stride_h, a_stride_n, batch, L, H, Dh, N, seg,
+                                               grad_u, grad_delta, grad_B, grad_C, grad_A,
+                                               workspace, st));
+}
+
+// --------------------------------------------------------------------- GLA ---
+static int gla_common_checks(const char* what, int dtype, int64_t batch, int64_t L, int64_t H,
+                             int64_t Dh, int64_t seg) {
+  MR_TRY(check_dims(what, batch, L, H));
+  if (Dh <= 0) return set_error(MR_E_SHAPE, "%s: every dimension must be positive", what);
+  MR_TRY(check_seg(L, seg, Dh, "Dh"));
+  MR_TRY(check_dtype(dtype));
+  if (!gla_seq_supported(Dh))
+    return set_error(MR_E_SHAPE, "%s: this build supports Dh in {32,64,96,128}, got Dh=%lld", what,
+                     (long long)Dh);
+  if (batch * H > (int64_t)INT32_MAX) return set_error(MR_E_SHAPE, "%s: batch*H too large", what);
+  return MR_OK;
+}
+
+int mr_gla_fwd(const void* q, const void* k, const void* v, const void* gates, int dtype,
+               int64_t batch, int64_t L, int64_t H, int64_t Dh, int64_t seg, float* y,
+               float* h_ckpt, void* stream) {
+  g_err[0] = 0;
+  MR_TRY(gla_common_checks("mr_gla_fwd", dtype, batch, L, H, Dh, seg));
+  MR_TRY(check_ptrs("mr_gla_fwd", {q, k, v, gates, y, h_ckpt}));
+  cudaStream_t st = (cudaStream_t)stream;
+  MR_DTYPE_SWITCH(dtype, gla_seq_fwd_launch<T>(q, k, v, gates, batch, L, H, Dh, seg, y, h_ckpt, st));
+}
+
+size_t mr_gla_bwd_workspace_bytes(int dtype, int64_t batch, int64_t L, int64_t H, int64_t Dh,
+                                  int64_t seg) {
+  (void)dtype;
+  if (batch <= 0 || L <= 0 || H <= 0 || Dh <= 0 || seg <= 0) return 0;
+  return gla_seq_bwd_ws_bytes(batch, L, H, Dh, seg);
+}
+
+int mr_gla_bwd(const float* grad_y, const float* grad_final, const float* h_ckpt, const void* q,
+               const void* k, const void* v, const void* gates, int dtype, int64_t batch,
+               int64_t L, int64_t H, int64_t Dh, int64_t seg, void* grad_q, void* grad_k,
+               void* grad_v, void* grad_gates, void* workspace, size_t workspace_bytes,
+               void* stream) {
+  g_err[0] = 0;
+  MR_TRY(gla_common_checks("mr_gla_bwd", dtype, batch, L, H, Dh, seg));
+  MR_TRY(check_ptrs("mr_gla_bwd", {grad_y, h_ckpt, q, k, v, gates, grad_q, grad_k, grad_v, grad_gates}));
+  MR_TRY(check_opt_ptr("mr_gla_bwd", grad_final));
+  const size_t need = gla_seq_bwd_ws_bytes(batch, L, H, Dh, seg);
+  if (workspace == nullptr || workspace_bytes < need)
+    return set_error(MR_E_WORKSPACE, "mr_gla_bwd: workspace of %zu bytes required, got %zu", need,
+                     workspace_bytes);
+  MR_TRY(check_opt_ptr("mr_gla_bwd", workspace));
+  cudaStream_t st = (cudaStream_t)stream;
+  MR_DTYPE_SWITCH(dtype, gla_seq_bwd_launch<T>(grad_y, grad_final, h_ckpt, q, k, v, gates, batch, L,
+                                               H, Dh, seg, grad_q, grad_k, grad_v, grad_gates,
+                                               workspace, st));
+}
+
+}  // extern "C"

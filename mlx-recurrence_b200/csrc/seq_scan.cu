@@ -1,0 +1,600 @@
+// SSD and GLA on CUDA cores, step by step in fp32: the exact-arithmetic
+// path. It serves fp32 inputs (parity 1e-5), SSD with a decay rate that
+// varies along N, and every shape the tensor-core path does not take.
+//
+// Reference kernels: mlx_recurrence/ssd.py:54-307, gla.py:49-270.
+// One CTA (8 warps) owns one (batch, head). The state matrix is spread over
+// the CTA: lane l holds state columns l, l+32, ... (the N axis for SSD, the
+// i axis for GLA) and warp w holds rows w, w+8, ... (Dh for SSD, j for GLA),
+// so the per-step contraction over the lane axis is a warp shuffle reduction
+// and each thread carries R*NK state values in registers. The backward
+// recomputes each segment from its checkpoint into a per-thread slice of
+// the workspace (coalesced: element e of thread tid sits at e*256 + tid), then
+// runs the reference's reverse sweep (ssd.py:204-260, gla.py:185-235).
+// Sums over the warp axis (SSD grad_B/grad_C, GLA grad_q/grad_k) go through
+// shared memory TS steps at a time; grad_A partials per batch row are
+// reduced by a second small kernel.
+#include "common.cuh"
+
+namespace mr {
+
+constexpr int kSeqThreads = 256;
+constexpr int kTS = 4;  // steps per cross-warp partial flush
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// ============================================================================
+// SSD
+// ============================================================================
+
+template <typename T, int R, int NK>
+__global__ void __launch_bounds__(kSeqThreads)
+ssd_seq_fwd_kernel(const T* __restrict__ u, const T* __restrict__ delta, const T* __restrict__ Bm,
+                   const T* __restrict__ Cm, const float* __restrict__ A, int64_t ash, int64_t asn,
+                   int L, int H, int Dh, int N, int seg, float* __restrict__ y,
+                   float* __restrict__ ckpt) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t b = blockIdx.x / H;
+  const int h = blockIdx.x % H;
+  const int nseg = L / seg;
+
+  float An[NK];
+#pragma unroll
+  for (int k = 0; k < NK; ++k) {
+    const int n = lane + 32 * k;
+    An[k] = n < N ? A[h * ash + n * asn] : 0.f;
+  }
+  float st[R][NK];
+#pragma unroll
+  for (int r = 0; r < R; ++r)
+#pragma unroll
+    for (int k = 0; k < NK; ++k) st[r][k] = 0.f;
+
+  for (int t = 0; t < L; ++t) {
+    const int64_t row = (b * L + t) * H + h;
+    const float dt = to_f(delta[row]);
+    float dB[NK], cv[NK], dec[NK];
+#pragma unroll
+    for (int k = 0; k < NK; ++k) {
+      const int n = lane + 32 * k;
+      const bool ok = n < N;
+      dB[k] = ok ? dt * to_f(Bm[row * N + n]) : 0.f;
+      cv[k] = ok ? to_f(Cm[row * N + n]) : 0.f;
+      dec[k] = ok ? expf(dt * An[k]) : 0.f;
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int d = warp + 8 * r;
+      const float ud = to_f(u[row * Dh + d]);
+      float acc = 0.f;
+#pragma unroll
+      for (int k = 0; k < NK; ++k) {
+        st[r][k] = dec[k] * st[r][k] + dB[k] * ud;  // ssd.py:97-98
+        acc += st[r][k] * cv[k];                    // ssd.py:99
+      }
+      acc = warp_sum(acc);
+      if (lane == 0) y[row * Dh + d] = acc;
+    }
+    if ((t + 1) % seg == 0) {
+      const int64_t s = (t + 1) / seg - 1;
+      float* ck = ckpt + ((b * nseg + s) * H + h) * (int64_t)N * Dh;
+#pragma unroll
+      for (int r = 0; r < R; ++r)
+#pragma unroll
+        for (int k = 0; k < NK; ++k) {
+          const int n = lane + 32 * k;
+          if (n < N) ck[(int64_t)n * Dh + warp + 8 * r] = st[r][k];
+        }
+    }
+  }
+}
+
+template <typename T, int R, int NK>
+__global__ void __launch_bounds__(kSeqThreads)
+ssd_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfinal,
+                   const float* __restrict__ ckpt, const T* __restrict__ u,
+                   const T* __restrict__ delta, const T* __restrict__ Bm, const T* __restrict__ Cm,
+                   const float* __restrict__ A, int64_t ash, int64_t asn, int L, int H, int Dh,
+                   int N, int seg, T* __restrict__ gu, T* __restrict__ gdelta, T* __restrict__ gB,
+                   T* __restrict__ gC, float* __restrict__ gA_part, float* __restrict__ scratch) {
+  constexpr int NP = 32 * NK;
+  __shared__ float pB[kTS][8][NP];
+  __shared__ float pC[kTS][8][NP];
+  __shared__ float pdt[kTS][8];
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t b = blockIdx.x / H;
+  const int h = blockIdx.x % H;
+  const int nseg = L / seg;
+  constexpr int E = R * NK;  // state values per thread
+  float* scr = scratch + (int64_t)blockIdx.x * (seg + 1) * E * kSeqThreads + tid;
+
+  float An[NK];
+#pragma unroll
+  for (int k = 0; k < NK; ++k) {
+    const int n = lane + 32 * k;
+    An[k] = n < N ? A[h * ash + n * asn] : 0.f;
+  }
+  float adj[R][NK], gAacc[NK];
+#pragma unroll
+  for (int k = 0; k < NK; ++k) gAacc[k] = 0.f;
+#pragma unroll
+  for (int r = 0; r < R; ++r)
+#pragma unroll
+    for (int k = 0; k < NK; ++k) {
+      const int n = lane + 32 * k;
+      const int d = warp + 8 * r;
+      adj[r][k] = (gfinal != nullptr && n < N) ? gfinal[((b * H + h) * Dh + d) * (int64_t)N + n] : 0.f;
+    }
+
+  for (int s = nseg - 1; s >= 0; --s) {
+    // ---- recompute this segment's states into the thread's scratch slice
+    {
+      float st[R][NK];
+      const float* ck = ckpt + ((b * nseg + (s - 1)) * H + h) * (int64_t)N * Dh;
+#pragma unroll
+      for (int r = 0; r < R; ++r)
+#pragma unroll
+        for (int k = 0; k < NK; ++k) {
+          const int n = lane + 32 * k;
+          st[r][k] = (s > 0 && n < N) ? ck[(int64_t)n * Dh + warp + 8 * r] : 0.f;
+          scr[(int64_t)(r * NK + k) * kSeqThreads] = st[r][k];
+        }
+      for (int tl = 0; tl < seg; ++tl) {
+        const int64_t row = (b * L + (int64_t)s * seg + tl) * H + h;
+        const float dt = to_f(delta[row]);
+        float dB[NK], dec[NK];
+#pragma unroll
+        for (int k = 0; k < NK; ++k) {
+          const int n = lane + 32 * k;
+          dB[k] = n < N ? dt * to_f(Bm[row * N + n]) : 0.f;
+          dec[k] = n < N ? expf(dt * An[k]) : 0.f;
+        }
+        float* sp = scr + (int64_t)(tl + 1) * E * kSeqThreads;
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          const float ud = to_f(u[row * Dh + warp + 8 * r]);
+#pragma unroll
+          for (int k = 0; k < NK; ++k) {
+            st[r][k] = dec[k] * st[r][k] + dB[k] * ud;
+            sp[(int64_t)(r * NK + k) * kSeqThreads] = st[r][k];
+          }
+        }
+      }
+    }
+
+    // ---- adjoint sweep, newest -> oldest (ssd.py:204-260)
+    for (int tl = seg - 1; tl >= 0; --tl) {
+      const int slot = (seg - 1 - tl) % kTS;
+      const int64_t t = (int64_t)s * seg + tl;
+      const int64_t row = (b * L + t) * H + h;
+      const float dt = to_f(delta[row]);
+      float bv[NK], cv[NK], dec[NK];
+#pragma unroll
+      for (int k = 0; k < NK; ++k) {
+        const int n = lane + 32 * k;
+        const bool ok = n < N;
+        bv[k] = ok ? to_f(Bm[row * N + n]) : 0.f;
+        cv[k] = ok ? to_f(Cm[row * N + n]) : 0.f;
+        dec[k] = ok ? expf(dt * An[k]) : 0.f;
+      }
+      const float* sc = scr + (int64_t)(tl + 1) * E * kSeqThreads;
+      const float* sprev = scr + (int64_t)tl * E * kSeqThreads;
+      float gdt = 0.f, pb[NK], pc[NK];
+#pragma unroll
+      for (int k = 0; k < NK; ++k) pb[k] = pc[k] = 0.f;
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const int d = warp + 8 * r;
+        const float ud = to_f(u[row * Dh + d]);
+        const float g = gy[row * Dh + d];
+        float gu_r = 0.f;
+#pragma unroll
+        for (int k = 0; k < NK; ++k) {
+          const float hc = sc[(int64_t)(r * NK + k) * kSeqThreads];
+          const float hp = sprev[(int64_t)(r * NK + k) * kSeqThreads];
+          float ad = adj[r][k] + g * cv[k];
+          gu_r += ad * dt * bv[k];
+          gdt += ad * (An[k] * dec[k] * hp + bv[k] * ud);
+          gAacc[k] += ad * dt * dec[k] * hp;
+          pb[k] += ad * dt * ud;
+          pc[k] += hc * g;
+          adj[r][k] = ad * dec[k];
+        }
+        gu_r = warp_sum(gu_r);
+        if (lane == 0) gu[row * Dh + d] = from_f<T>(gu_r);
+      }
+      gdt = warp_sum(gdt);
+      if (lane == 0) pdt[slot][warp] = gdt;
+#pragma unroll
+      for (int k = 0; k < NK; ++k) {
+        pB[slot][warp][lane + 32 * k] = pb[k];
+        pC[slot][warp][lane + 32 * k] = pc[k];
+      }
+      if (slot == kTS - 1 || tl == 0) {
+        __syncthreads();
+        const int nsl = slot + 1;
+        for (int idx = tid; idx < nsl * N; idx += kSeqThreads) {
+          const int sl = idx / N, n = idx % N;
+          float sb = 0.f, scc = 0.f;
+#pragma unroll
+          for (int w = 0; w < 8; ++w) {
+            sb += pB[sl][w][n];
+            scc += pC[sl][w][n];
+          }
+          const int64_t tt = t + (slot - sl);  // slot sl was step t + (slot - sl)
+          const int64_t rr = (b * L + tt) * H + h;
+          gB[rr * N + n] = from_f<T>(sb);
+          gC[rr * N + n] = from_f<T>(scc);
+        }
+        if (tid < nsl) {
+          float sd = 0.f;
+#pragma unroll
+          for (int w = 0; w < 8; ++w) sd += pdt[tid][w];
+          const int64_t tt = t + (slot - tid);
+          gdelta[(b * L + tt) * H + h] = from_f<T>(sd);
+        }
+        __syncthreads();
+      }
+    }
+  }
+
+  // grad_A partial for this (b, h): sum over rows (in-thread) and warps
+  __syncthreads();
+#pragma unroll
+  for (int k = 0; k < NK; ++k) pB[0][warp][lane + 32 * k] = gAacc[k];
+  __syncthreads();
+  for (int n = tid; n < N; n += kSeqThreads) {
+    float sa = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) sa += pB[0][w][n];
+    gA_part[(b * H + h) * (int64_t)N + n] = sa;
+  }
+}
+
+// grad_A[h,n] = sum_b part[b,h,n]   (ssd.py:305)
+__global__ void sum_over_batch_kernel(const float* __restrict__ part, int64_t batch, int64_t HN,
+                                      float* __restrict__ out) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= HN) return;
+  float s = 0.f;
+  for (int64_t b = 0; b < batch; ++b) s += part[b * HN + i];
+  out[i] = s;
+}
+
+// ============================================================================
+// GLA
+// ============================================================================
+
+template <typename T, int R, int IK>
+__global__ void __launch_bounds__(kSeqThreads)
+gla_seq_fwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
+                   const T* __restrict__ gates, int L, int H, int Dh, int seg,
+                   float* __restrict__ y, float* __restrict__ ckpt) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t b = blockIdx.x / H;
+  const int h = blockIdx.x % H;
+  const int nseg = L / seg;
+  float S[IK][R];
+#pragma unroll
+  for (int i = 0; i < IK; ++i)
+#pragma unroll
+    for (int r = 0; r < R; ++r) S[i][r] = 0.f;
+
+  for (int t = 0; t < L; ++t) {
+    const int64_t row = (b * L + t) * H + h;
+    const float g = to_f(gates[row]);
+    float ki[IK], qi[IK];
+#pragma unroll
+    for (int i = 0; i < IK; ++i) {
+      ki[i] = to_f(k[row * Dh + lane + 32 * i]);
+      qi[i] = to_f(q[row * Dh + lane + 32 * i]);
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int j = warp + 8 * r;
+      const float vj = to_f(v[row * Dh + j]);
+      float o = 0.f;
+#pragma unroll
+      for (int i = 0; i < IK; ++i) {
+        S[i][r] = g * S[i][r] + ki[i] * vj;  // gla.py:87
+        o += qi[i] * S[i][r];                // gla.py:88
+      }
+      o = warp_sum(o);
+      if (lane == 0) y[row * Dh + j] = o;
+    }
+    if ((t + 1) % seg == 0) {
+      const int64_t s = (t + 1) / seg - 1;
+      float* ck = ckpt + ((b * nseg + s) * H + h) * (int64_t)Dh * Dh;
+#pragma unroll
+      for (int i = 0; i < IK; ++i)
+#pragma unroll
+        for (int r = 0; r < R; ++r) ck[(int64_t)(lane + 32 * i) * Dh + warp + 8 * r] = S[i][r];
+    }
+  }
+}
+
+template <typename T, int R, int IK>
+__global__ void __launch_bounds__(kSeqThreads)
+gla_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfinal,
+                   const float* __restrict__ ckpt, const T* __restrict__ q,
+                   const T* __restrict__ k, const T* __restrict__ v, const T* __restrict__ gates,
+                   int L, int H, int Dh, int seg, T* __restrict__ gq, T* __restrict__ gk,
+                   T* __restrict__ gv, T* __restrict__ gg, float* __restrict__ scratch) {
+  constexpr int NP = 32 * IK;
+  __shared__ float pQ[kTS][8][NP];
+  __shared__ float pK[kTS][8][NP];
+  __shared__ float pg[kTS][8];
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t b = blockIdx.x / H;
+  const int h = blockIdx.x % H;
+  const int nseg = L / seg;
+  constexpr int E = R * IK;
+  float* scr = scratch + (int64_t)blockIdx.x * (seg + 1) * E * kSeqThreads + tid;
+
+  float adj[IK][R];
+#pragma unroll
+  for (int i = 0; i < IK; ++i)
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+      adj[i][r] = gfinal != nullptr
+                      ? gfinal[((b * H + h) * Dh + lane + 32 * i) * (int64_t)Dh + warp + 8 * r]
+                      : 0.f;
+
+  for (int s = nseg - 1; s >= 0; --s) {
+    {
+      float S[IK][R];
+      const float* ck = ckpt + ((b * nseg + (s - 1)) * H + h) * (int64_t)Dh * Dh;
+#pragma unroll
+      for (int i = 0; i < IK; ++i)
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          S[i][r] = s > 0 ? ck[(int64_t)(lane + 32 * i) * Dh + warp + 8 * r] : 0.f;
+          scr[(int64_t)(i * R + r) * kSeqThreads] = S[i][r];
+        }
+      for (int tl = 0; tl < seg; ++tl) {
+        const int64_t row = (b * L + (int64_t)s * seg + tl) * H + h;
+        const float g = to_f(gates[row]);
+        float ki[IK];
+#pragma unroll
+        for (int i = 0; i < IK; ++i) ki[i] = to_f(k[row * Dh + lane + 32 * i]);
+        float* sp = scr + (int64_t)(tl + 1) * E * kSeqThreads;
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          const float vj = to_f(v[row * Dh + warp + 8 * r]);
+#pragma unroll
+          for (int i = 0; i < IK; ++i) {
+            S[i][r] = g * S[i][r] + ki[i] * vj;
+            sp[(int64_t)(i * R + r) * kSeqThreads] = S[i][r];
+          }
+        }
+      }
+    }
+
+    for (int tl = seg - 1; tl >= 0; --tl) {
+      const int slot = (seg - 1 - tl) % kTS;
+      const int64_t t = (int64_t)s * seg + tl;
+      const int64_t row = (b * L + t) * H + h;
+      const float g = to_f(gates[row]);
+      float ki[IK], qi[IK];
+#pragma unroll
+      for (int i = 0; i < IK; ++i) {
+        ki[i] = to_f(k[row * Dh + lane + 32 * i]);
+        qi[i] = to_f(q[row * Dh + lane + 32 * i]);
+      }
+      const float* sc = scr + (int64_t)(tl + 1) * E * kSeqThreads;
+      const float* sprev = scr + (int64_t)tl * E * kSeqThreads;
+      float ggs = 0.f, pq[IK], pk[IK];
+#pragma unroll
+      for (int i = 0; i < IK; ++i) pq[i] = pk[i] = 0.f;
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const int j = warp + 8 * r;
+        const float vj = to_f(v[row * Dh + j]);
+        const float go = gy[row * Dh + j];
+        float gv_r = 0.f;
+#pragma unroll
+        for (int i = 0; i < IK; ++i) {
+          const float hc = sc[(int64_t)(i * R + r) * kSeqThreads];
+          const float hp = sprev[(int64_t)(i * R + r) * kSeqThreads];
+          const float ad = adj[i][r] + qi[i] * go;  // gla.py:213
+          gv_r += ad * ki[i];
+          ggs += ad * hp;
+          pq[i] += go * hc;
+          pk[i] += ad * vj;
+          adj[i][r] = ad * g;
+        }
+        gv_r = warp_sum(gv_r);
+        if (lane == 0) gv[row * Dh + j] = from_f<T>(gv_r);
+      }
+      ggs = warp_sum(ggs);
+      if (lane == 0) pg[slot][warp] = ggs;
+#pragma unroll
+      for (int i = 0; i < IK; ++i) {
+        pQ[slot][warp][lane + 32 * i] = pq[i];
+        pK[slot][warp][lane + 32 * i] = pk[i];
+      }
+      if (slot == kTS - 1 || tl == 0) {
+        __syncthreads();
+        const int nsl = slot + 1;
+        for (int idx = tid; idx < nsl * Dh; idx += kSeqThreads) {
+          const int sl = idx / Dh, i = idx % Dh;
+          float sq = 0.f, sk = 0.f;
+#pragma unroll
+          for (int w = 0; w < 8; ++w) {
+            sq += pQ[sl][w][i];
+            sk += pK[sl][w][i];
+          }
+          const int64_t rr = (b * L + t + (slot - sl)) * H + h;
+          gq[rr * Dh + i] = from_f<T>(sq);
+          gk[rr * Dh + i] = from_f<T>(sk);
+        }
+        if (tid < nsl) {
+          float sd = 0.f;
+#pragma unroll
+          for (int w = 0; w < 8; ++w) sd += pg[tid][w];
+          gg[(b * L + t + (slot - tid)) * H + h] = from_f<T>(sd);
+        }
+        __syncthreads();
+      }
+    }
+  }
+}
+
+// ============================================================================
+// host launchers
+// ============================================================================
+
+static int ceil32(int n) { return (n + 31) / 32; }
+// lanes hold 1, 2 or 4 state columns (N <= 32, 64, 128)
+static int nk_of(int64_t N) { const int c = ceil32((int)N); return c <= 1 ? 1 : c <= 2 ? 2 : 4; }
+
+size_t ssd_seq_bwd_ws_bytes(int64_t batch, int64_t L, int64_t H, int64_t Dh, int64_t N, int64_t seg) {
+  const int64_t R = Dh / 8, NK = nk_of(N);
+  const size_t scr = (size_t)batch * H * (seg + 1) * R * NK * kSeqThreads * sizeof(float);
+  const size_t part = (size_t)batch * H * N * sizeof(float);
+  return ((scr + 255) / 256) * 256 + part;
+}
+
+size_t gla_seq_bwd_ws_bytes(int64_t batch, int64_t L, int64_t H, int64_t Dh, int64_t seg) {
+  const int64_t R = Dh / 8, IK = Dh / 32;
+  return (size_t)batch * H * (seg + 1) * R * IK * kSeqThreads * sizeof(float);
+}
+
+bool ssd_seq_supported(int64_t Dh, int64_t N) {
+  return (Dh == 32 || Dh == 64 || Dh == 96 || Dh == 128) && N >= 1 && N <= 128;
+}
+bool gla_seq_supported(int64_t Dh) { return Dh == 32 || Dh == 64 || Dh == 96 || Dh == 128; }
+
+#define MR_SSD_DISPATCH(Dh, N, MACRO)                \
+  do {                                               \
+    const int nk2_ = nk_of(N);                       \
+    switch ((int)(Dh) / 8) {                         \
+      case 4: MACRO(4, nk2_); break;                 \
+      case 8: MACRO(8, nk2_); break;                 \
+      case 12: MACRO(12, nk2_); break;               \
+      default: MACRO(16, nk2_); break;               \
+    }                                                \
+  } while (0)
+
+template <typename T, int R>
+static void ssd_fwd_nk(int nk, dim3 g, cudaStream_t st, const T* u, const T* dl, const T* Bm,
+                       const T* Cm, const float* A, int64_t ash, int64_t asn, int L, int H, int Dh,
+                       int N, int seg, float* y, float* ck) {
+  if (nk == 1)
+    ssd_seq_fwd_kernel<T, R, 1><<<g, kSeqThreads, 0, st>>>(u, dl, Bm, Cm, A, ash, asn, L, H, Dh, N, seg, y, ck);
+  else if (nk == 2)
+    ssd_seq_fwd_kernel<T, R, 2><<<g, kSeqThreads, 0, st>>>(u, dl, Bm, Cm, A, ash, asn, L, H, Dh, N, seg, y, ck);
+  else
+    ssd_seq_fwd_kernel<T, R, 4><<<g, kSeqThreads, 0, st>>>(u, dl, Bm, Cm, A, ash, asn, L, H, Dh, N, seg, y, ck);
+}
+
+template <typename T>
+int ssd_seq_fwd_launch(const void* u, const void* delta, const void* Bm, const void* Cm,
+                       const float* A, int64_t ash, int64_t asn, int64_t batch, int64_t L, int64_t H,
+                       int64_t Dh, int64_t N, int64_t seg, float* y, float* ckpt, cudaStream_t st) {
+  dim3 g((unsigned)(batch * H));
+#define MR_CALL(R_, NK_)                                                                       \
+  ssd_fwd_nk<T, R_>(NK_, g, st, (const T*)u, (const T*)delta, (const T*)Bm, (const T*)Cm, A, ash, \
+                    asn, (int)L, (int)H, (int)Dh, (int)N, (int)seg, y, ckpt)
+  MR_SSD_DISPATCH(Dh, N, MR_CALL);
+#undef MR_CALL
+  return check_launch("ssd_seq_fwd_kernel");
+}
+
+template <typename T, int R>
+static void ssd_bwd_nk(int nk, dim3 g, cudaStream_t st, const float* gy, const float* gf,
+                       const float* ck, const T* u, const T* dl, const T* Bm, const T* Cm,
+                       const float* A, int64_t ash, int64_t asn, int L, int H, int Dh, int N, int seg,
+                       T* gu, T* gd, T* gB, T* gC, float* gAp, float* scr) {
+  if (nk == 1)
+    ssd_seq_bwd_kernel<T, R, 1><<<g, kSeqThreads, 0, st>>>(gy, gf, ck, u, dl, Bm, Cm, A, ash, asn, L, H, Dh, N, seg, gu, gd, gB, gC, gAp, scr);
+  else if (nk == 2)
+    ssd_seq_bwd_kernel<T, R, 2><<<g, kSeqThreads, 0, st>>>(gy, gf, ck, u, dl, Bm, Cm, A, ash, asn, L, H, Dh, N, seg, gu, gd, gB, gC, gAp, scr);
+  else
+    ssd_seq_bwd_kernel<T, R, 4><<<g, kSeqThreads, 0, st>>>(gy, gf, ck, u, dl, Bm, Cm, A, ash, asn, L, H, Dh, N, seg, gu, gd, gB, gC, gAp, scr);
+}
+
+template <typename T>
+int ssd_seq_bwd_launch(const float* gy, const float* gf, const float* ckpt, const void* u,
+                       const void* delta, const void* Bm, const void* Cm, const float* A,
+                       int64_t ash, int64_t asn, int64_t batch, int64_t L, int64_t H, int64_t Dh,
+                       int64_t N, int64_t seg, void* gu, void* gd, void* gB, void* gC, float* gA,
+                       void* ws, cudaStream_t st) {
+  const int64_t R = Dh / 8, NK = nk_of(N);
+  const size_t scr_bytes = (size_t)batch * H * (seg + 1) * R * NK * kSeqThreads * sizeof(float);
+  float* scr = (float*)ws;
+  float* gAp = (float*)((char*)ws + ((scr_bytes + 255) / 256) * 256);
+  dim3 g((unsigned)(batch * H));
+#define MR_CALL(R_, NK_)                                                                        \
+  ssd_bwd_nk<T, R_>(NK_, g, st, gy, gf, ckpt, (const T*)u, (const T*)delta, (const T*)Bm,         \
+                    (const T*)Cm, A, ash, asn, (int)L, (int)H, (int)Dh, (int)N, (int)seg, (T*)gu,  \
+                    (T*)gd, (T*)gB, (T*)gC, gAp, scr)
+  MR_SSD_DISPATCH(Dh, N, MR_CALL);
+#undef MR_CALL
+  int rc = check_launch("ssd_seq_bwd_kernel");
+  if (rc) return rc;
+  const int64_t HN = H * N;
+  sum_over_batch_kernel<<<(unsigned)((HN + 255) / 256), 256, 0, st>>>(gAp, batch, HN, gA);
+  return check_launch("sum_over_batch_kernel");
+}
+
+template <typename T>
+int gla_seq_fwd_launch(const void* q, const void* k, const void* v, const void* g, int64_t batch,
+                       int64_t L, int64_t H, int64_t Dh, int64_t seg, float* y, float* ckpt,
+                       cudaStream_t st) {
+  dim3 grid((unsigned)(batch * H));
+  const T *q_ = (const T*)q, *k_ = (const T*)k, *v_ = (const T*)v, *g_ = (const T*)g;
+  switch ((int)Dh) {
+    case 32: gla_seq_fwd_kernel<T, 4, 1><<<grid, kSeqThreads, 0, st>>>(q_, k_, v_, g_, (int)L, (int)H, 32, (int)seg, y, ckpt); break;
+    case 64: gla_seq_fwd_kernel<T, 8, 2><<<grid, kSeqThreads, 0, st>>>(q_, k_, v_, g_, (int)L, (int)H, 64, (int)seg, y, ckpt); break;
+    case 96: gla_seq_fwd_kernel<T, 12, 3><<<grid, kSeqThreads, 0, st>>>(q_, k_, v_, g_, (int)L, (int)H, 96, (int)seg, y, ckpt); break;
+    default: gla_seq_fwd_kernel<T, 16, 4><<<grid, kSeqThreads, 0, st>>>(q_, k_, v_, g_, (int)L, (int)H, 128, (int)seg, y, ckpt); break;
+  }
+  return check_launch("gla_seq_fwd_kernel");
+}
+
+template <typename T>
+int gla_seq_bwd_launch(const float* gy, const float* gf, const float* ckpt, const void* q,
+                       const void* k, const void* v, const void* g, int64_t batch, int64_t L,
+                       int64_t H, int64_t Dh, int64_t seg, void* gq, void* gk, void* gv, void* gg,
+                       void* ws, cudaStream_t st) {
+  dim3 grid((unsigned)(batch * H));
+  const T *q_ = (const T*)q, *k_ = (const T*)k, *v_ = (const T*)v, *g_ = (const T*)g;
+  T *gq_ = (T*)gq, *gk_ = (T*)gk, *gv_ = (T*)gv, *gg_ = (T*)gg;
+  float* scr = (float*)ws;
+  switch ((int)Dh) {
+    case 32: gla_seq_bwd_kernel<T, 4, 1><<<grid, kSeqThreads, 0, st>>>(gy, gf, ckpt, q_, k_, v_, g_, (int)L, (int)H, 32, (int)seg, gq_, gk_, gv_, gg_, scr); break;
+    case 64: gla_seq_bwd_kernel<T, 8, 2><<<grid, kSeqThreads, 0, st>>>(gy, gf, ckpt, q_, k_, v_, g_, (int)L, (int)H, 64, (int)seg, gq_, gk_, gv_, gg_, scr); break;
+    case 96: gla_seq_bwd_kernel<T, 12, 3><<<grid, kSeqThreads, 0, st>>>(gy, gf, ckpt, q_, k_, v_, g_, (int)L, (int)H, 96, (int)seg, gq_, gk_, gv_, gg_, scr); break;
+    default: gla_seq_bwd_kernel<T, 16, 4><<<grid, kSeqThreads, 0, st>>>(gy, gf, ckpt, q_, k_, v_, g_, (int)L, (int)H, 128, (int)seg, gq_, gk_, gv_, gg_, scr); break;
+  }
+  return check_launch("gla_seq_bwd_kernel");
+}
+
+#define MR_INST(T)                                                                                  \
+  template int ssd_seq_fwd_launch<T>(const void*, const void*, const void*, const void*,           \
+                                     const float*, int64_t, int64_t, int64_t, int64_t, int64_t,   \
+                                     int64_t, int64_t, int64_t, float*, float*, cudaStream_t);    \
+  template int ssd_seq_bwd_launch<T>(const float*, const float*, const float*, const void*,        \
+                                     const void*, const void*, const void*, const float*, int64_t, \
+                                     int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, \
+                                     void*, void*, void*, void*, float*, void*, cudaStream_t);    \
+  template int gla_seq_fwd_launch<T>(const void*, const void*, const void*, const void*, int64_t,  \
+                                     int64_t, int64_t, int64_t, int64_t, float*, float*,           \
+                                     cudaStream_t);                                                \
+  template int gla_seq_bwd_launch<T>(const float*, const float*, const float*, const void*,        \
+                                     const void*, const void*, const void*, int64_t, int64_t,      \
+                                     int64_t, int64_t, int64_t, void*, void*, void*, void*, void*, \
+                                     cudaStream_t);
+MR_INST(float)
+MR_INST(__nv_bfloat16)
+MR_INST(__half)
+#undef MR_INST
+
+}  // namespace mr

@@ -1,0 +1,104 @@
+"""Gated linear attention recurrence with a scalar forget gate per head.
+
+Drop-in for ``mlx_recurrence/gla.py`` (v0.3.0). Per head the state is the
+``Dh x Dh`` matrix ``h[i, j]``::
+
+    h[i, j] = gate[b,t,head] * h[i, j] + k[b,t,head,i] * v[b,t,head,j]
+    o[b,t,head,j] = sum_i q[b,t,head,i] * h[i, j]      (post-update state)
+
+Same functions, argument meaning and shape rules (``L % seg == 0``,
+``Dh % 32 == 0``) as the reference, backed by the sm_100a kernels of
+``libmlrec.so``. Outputs are float32; state and accumulation float32;
+gradients come back in the input dtype.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._chassis import DEFAULT_SEG, check_segment_shape, common_dtype, grad_out, prep
+
+
+def _validate(q, k, v, gates):
+    if q.dim() != 4:
+        raise ValueError(f"q must be [B, L, H, Dh], got shape {tuple(q.shape)}")
+    Bt, L, H, Dh = q.shape
+    for name, t in (("k", k), ("v", v)):
+        if t.shape != q.shape:
+            raise ValueError(f"{name} must match q's shape {tuple(q.shape)}, got {tuple(t.shape)}")
+    if tuple(gates.shape) != (Bt, L, H):
+        raise ValueError(f"gates must be [B, L, H] = [{Bt}, {L}, {H}], got {tuple(gates.shape)}")
+    return Bt, L, H, Dh
+
+
+class _GLAScan(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, gates, seg):
+        Bt, L, H, Dh = _validate(q, k, v, gates)
+        check_segment_shape(L, seg, Dh, "Dh")  # gla.py:287
+        dev = _lib.require_cuda(q, k, v, gates)
+        dt = common_dtype(q, k, v, gates)
+        q_, k_, v_, g_ = (prep(t, dt) for t in (q, k, v, gates))
+        y = torch.empty((Bt, L, H, Dh), dtype=torch.float32, device=dev)
+        ckpt = torch.empty((Bt, L // seg, H, Dh, Dh), dtype=torch.float32, device=dev)
+        with torch.cuda.device(dev):
+            _lib.call("mr_gla_fwd", _lib.ptr(q_), _lib.ptr(k_), _lib.ptr(v_), _lib.ptr(g_),
+                      _lib.DTYPE_CODE[dt], Bt, L, H, Dh, seg, _lib.ptr(y), _lib.ptr(ckpt),
+                      _lib.stream_of(dev))
+        ctx.save_for_backward(q_, k_, v_, g_, ckpt)
+        ctx.seg = seg
+        return y, ckpt[:, -1].clone()
+
+    @staticmethod
+    def backward(ctx, gy, gfinal):
+        q_, k_, v_, g_, ckpt = ctx.saved_tensors
+        Bt, L, H, Dh = q_.shape
+        dev = q_.device
+        code = _lib.DTYPE_CODE[q_.dtype]
+        gy = grad_out(gy, (Bt, L, H, Dh), dev)
+        gf = None if gfinal is None else gfinal.to(torch.float32).contiguous()
+        gq, gk, gv, gg = (torch.empty_like(t) for t in (q_, k_, v_, g_))
+        with torch.cuda.device(dev):
+            lib = _lib.load()
+            nws = lib.mr_gla_bwd_workspace_bytes(code, Bt, L, H, Dh, ctx.seg)
+            ws = torch.empty(max(nws, 16), dtype=torch.uint8, device=dev)
+            _lib.call("mr_gla_bwd", _lib.ptr(gy), _lib.ptr(gf), _lib.ptr(ckpt), _lib.ptr(q_),
+                      _lib.ptr(k_), _lib.ptr(v_), _lib.ptr(g_), code, Bt, L, H, Dh, ctx.seg,
+                      _lib.ptr(gq), _lib.ptr(gk), _lib.ptr(gv), _lib.ptr(gg), _lib.ptr(ws),
+                      ws.numel(), _lib.stream_of(dev))
+        return gq, gk, gv, gg, None
+
+
+def gla_scan(q, k, v, gates, seg=DEFAULT_SEG):
+    """Gated linear attention recurrence (``gla.py:301-318``).
+
+    Args:
+        q, k, v: [B, L, H, Dh] (q pre-scaled / post-RoPE)
+        gates:   [B, L, H] scalar forget gate per head
+        seg:     checkpoint segment length (L % seg == 0; default 32)
+
+    Returns:
+        y:       [B, L, H, Dh] float32
+    """
+    y, _ = _GLAScan.apply(q, k, v, gates, seg)
+    return y
+
+
+def gla_scan_with_state(q, k, v, gates, seg=DEFAULT_SEG):
+    """GLA scan that also returns the final state ``[B, H, Dh, Dh]`` (``gla.py:321-329``)."""
+    return _GLAScan.apply(q, k, v, gates, seg)
+
+
+def gla_scan_reference(q, k, v, gates):
+    """Per-step torch loop (``gla.py:336-346``). Differentiable, any device."""
+    Bt, L, H, Dh = q.shape
+    ft = torch.promote_types(q.dtype, torch.float32)
+    h = torch.zeros((Bt, H, Dh, Dh), dtype=ft, device=q.device)
+    ys = []
+    for t in range(L):
+        g = gates[:, t, :, None, None]
+        kv = k[:, t, :, :, None] * v[:, t, :, None, :]
+        h = g * h + kv
+        ys.append(torch.sum(q[:, t, :, :, None] * h, dim=-2))
+    return torch.stack(ys, dim=1)

@@ -1,0 +1,95 @@
+"""RG-LRU diagonal recurrence ``h_t = a_t * h_{t-1} + x_t``, ``y_t = h_t``.
+
+Drop-in for ``mlx_recurrence/rglru.py`` (v0.3.0): same functions, argument
+meaning, shape rules and errors, backed by the sm_100a kernels in
+``csrc/diag_scan.cu`` through ``libmlrec.so``. The gates ``a`` and the gated
+input ``x = sqrt(1 - a^2) * (i * x_raw)`` are computed by the caller, as in
+the reference (``rglru.py:19-27``).
+
+VJP (``rglru.py:36-39``): ``adj_t = gy_t + a_{t+1} adj_{t+1}``,
+``grad_x[t] = adj_t``, ``grad_a[t] = adj_t * h_{t-1}``. A cotangent on the
+final state of ``rglru_scan_with_state`` seeds ``adj`` (the reference's VJP
+drops it, ``rglru.py:226``; its pure loop does not).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._chassis import DEFAULT_SEG, check_segment_shape, common_dtype, grad_out, prep
+
+
+class _RGLRUScan(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, a, x, seg):
+        if a.dim() != 3 or x.shape != a.shape:
+            raise ValueError(f"a and x must both be [B, L, D], got {tuple(a.shape)} and {tuple(x.shape)}")
+        Bt, L, D = a.shape
+        check_segment_shape(L, seg, D, "D")  # rglru.py:220
+        dev = _lib.require_cuda(a, x)
+        dt = common_dtype(a, x)
+        a_, x_ = prep(a, dt), prep(x, dt)
+        y = torch.empty((Bt, L, D), dtype=torch.float32, device=dev)
+        ckpt = torch.empty((Bt, L // seg, D), dtype=torch.float32, device=dev)
+        with torch.cuda.device(dev):
+            _lib.call("mr_rglru_fwd", _lib.ptr(a_), _lib.ptr(x_), _lib.DTYPE_CODE[dt], Bt, L, D, seg,
+                      _lib.ptr(y), _lib.ptr(ckpt), _lib.stream_of(dev))
+        ctx.save_for_backward(a_, x_, ckpt)
+        ctx.seg = seg
+        return y, ckpt[:, -1].clone()
+
+    @staticmethod
+    def backward(ctx, gy, gfinal):
+        a_, x_, ckpt = ctx.saved_tensors
+        Bt, L, D = a_.shape
+        dev = a_.device
+        dt = a_.dtype
+        gy = grad_out(gy, (Bt, L, D), dev)
+        gf = None if gfinal is None else gfinal.to(torch.float32).contiguous()
+        ga = torch.empty_like(a_)
+        gx = torch.empty_like(x_)
+        code = _lib.DTYPE_CODE[dt]
+        with torch.cuda.device(dev):
+            lib = _lib.load()
+            nws = lib.mr_rglru_bwd_workspace_bytes(code, Bt, L, D, ctx.seg)
+            ws = torch.empty(max(nws, 1), dtype=torch.uint8, device=dev) if nws else None
+            _lib.call("mr_rglru_bwd", _lib.ptr(gy), _lib.ptr(gf), _lib.ptr(ckpt), _lib.ptr(a_),
+                      _lib.ptr(x_), code, Bt, L, D, ctx.seg, _lib.ptr(ga), _lib.ptr(gx), _lib.ptr(ws),
+                      nws, _lib.stream_of(dev))
+        return ga, gx, None
+
+
+def rglru_scan(a, x, seg=DEFAULT_SEG):
+    """RG-LRU diagonal linear scan (``rglru.py:234-256``).
+
+    Args:
+        a:   [B, L, D] per-channel recurrent gate (any real value).
+        x:   [B, L, D] the already-gated input.
+        seg: checkpoint segment length (L % seg == 0; default 32).
+
+    Returns:
+        y:   [B, L, D] float32, ``y_t = h_t``.
+
+    ``D`` must be a multiple of 32. State and accumulation are float32; bf16
+    and fp16 inputs are widened on read and their gradients are returned in
+    the input dtype.
+    """
+    y, _ = _RGLRUScan.apply(a, x, seg)
+    return y
+
+
+def rglru_scan_with_state(a, x, seg=DEFAULT_SEG):
+    """RG-LRU scan that also returns the final state [B, D] (``rglru.py:259-267``)."""
+    return _RGLRUScan.apply(a, x, seg)
+
+
+def rglru_scan_reference(a, x):
+    """Per-step torch loop (``rglru.py:274-282``). Differentiable, any device."""
+    Bt, L, D = a.shape
+    h = torch.zeros((Bt, D), dtype=torch.promote_types(a.dtype, torch.float32), device=a.device)
+    ys = []
+    for t in range(L):
+        h = a[:, t, :] * h + x[:, t, :]
+        ys.append(h)
+    return torch.stack(ys, dim=1)

@@ -1,0 +1,131 @@
+"""Mamba-2-style head-wise SSD selective scan.
+
+Drop-in for ``mlx_recurrence/ssd.py`` (v0.3.0). Per head and channel the
+state is ``h[Dh, N]``::
+
+    decay = exp(delta[b,t,head] * A_neg[head,n])
+    h[d,n] = decay * h[d,n] + delta[b,t,head] * B[b,t,head,n] * u[b,t,head,d]
+    y[b,t,head,d] = sum_n h[d,n] * C[b,t,head,n]
+
+Same functions, argument meaning and shape rules (``L % seg == 0``,
+``Dh % 32 == 0``) as the reference; the work runs in the sm_100a kernels of
+``libmlrec.so``. ``A_neg`` is ``[H, N]``; a view that is constant along N
+(``A.unsqueeze(-1).expand(H, N)``, stride 0) selects the one-rate-per-head
+(Mamba-2) path without a device synchronisation. Outputs are float32; state
+and accumulation are float32 for every input dtype; gradients come back in
+the input dtype (``grad_A`` is summed over the batch, ``ssd.py:305``).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._chassis import DEFAULT_SEG, check_segment_shape, common_dtype, grad_out, prep
+
+
+def _validate(u, delta, B, C, A_neg):
+    if u.dim() != 4:
+        raise ValueError(f"u must be [B, L, H, Dh], got shape {tuple(u.shape)}")
+    Bt, L, H, Dh = u.shape
+    if A_neg.dim() != 2 or A_neg.shape[0] != H:
+        raise ValueError(f"A_neg must be [H, N] = [{H}, N], got {tuple(A_neg.shape)}")
+    N = A_neg.shape[1]
+    if tuple(delta.shape) != (Bt, L, H):
+        raise ValueError(f"delta must be [B, L, H] = [{Bt}, {L}, {H}], got {tuple(delta.shape)}")
+    for name, t in (("B", B), ("C", C)):
+        if tuple(t.shape) != (Bt, L, H, N):
+            raise ValueError(f"{name} must be [B, L, H, N] = [{Bt}, {L}, {H}, {N}], got {tuple(t.shape)}")
+    return Bt, L, H, Dh, N
+
+
+def _a_f32(A_neg):
+    """float32 decay rates with (stride_h, stride_n) in elements; stride_n 0
+    when the caller's view is constant along N."""
+    H, N = A_neg.shape
+    if A_neg.stride(1) == 0:
+        a = A_neg[:, :1].to(torch.float32).contiguous()
+        return a, 1, 0
+    return A_neg.to(torch.float32).contiguous(), N, 1
+
+
+class _SSDScan(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, u, delta, B, C, A_neg, seg):
+        Bt, L, H, Dh, N = _validate(u, delta, B, C, A_neg)
+        check_segment_shape(L, seg, Dh, "Dh")  # ssd.py:328
+        dev = _lib.require_cuda(u, delta, B, C, A_neg)
+        dt = common_dtype(u, delta, B, C)
+        u_, d_, B_, C_ = (prep(t, dt) for t in (u, delta, B, C))
+        A32, ash, asn = _a_f32(A_neg)
+        y = torch.empty((Bt, L, H, Dh), dtype=torch.float32, device=dev)
+        ckpt = torch.empty((Bt, L // seg, H, N, Dh), dtype=torch.float32, device=dev)
+        with torch.cuda.device(dev):
+            _lib.call("mr_ssd_fwd", _lib.ptr(u_), _lib.ptr(d_), _lib.ptr(B_), _lib.ptr(C_),
+                      _lib.ptr(A32), ash, asn, _lib.DTYPE_CODE[dt], Bt, L, H, Dh, N, seg,
+                      _lib.ptr(y), _lib.ptr(ckpt), _lib.stream_of(dev))
+        ctx.save_for_backward(u_, d_, B_, C_, A32, ckpt)
+        ctx.meta = (seg, ash, asn, N)
+        # last checkpoint [B, H, N, Dh] -> conceptual state [B, H, Dh, N] (ssd.py:373-374)
+        final = ckpt[:, -1].transpose(-1, -2).contiguous()
+        return y, final
+
+    @staticmethod
+    def backward(ctx, gy, gfinal):
+        u_, d_, B_, C_, A32, ckpt = ctx.saved_tensors
+        seg, ash, asn, N = ctx.meta
+        Bt, L, H, Dh = u_.shape
+        dev = u_.device
+        code = _lib.DTYPE_CODE[u_.dtype]
+        gy = grad_out(gy, (Bt, L, H, Dh), dev)
+        gf = None if gfinal is None else gfinal.to(torch.float32).contiguous()
+        gu, gd, gB, gC = (torch.empty_like(t) for t in (u_, d_, B_, C_))
+        gA = torch.empty((H, N), dtype=torch.float32, device=dev)
+        with torch.cuda.device(dev):
+            lib = _lib.load()
+            nws = lib.mr_ssd_bwd_workspace_bytes(code, Bt, L, H, Dh, N, seg, asn)
+            ws = torch.empty(max(nws, 16), dtype=torch.uint8, device=dev)
+            _lib.call("mr_ssd_bwd", _lib.ptr(gy), _lib.ptr(gf), _lib.ptr(ckpt), _lib.ptr(u_),
+                      _lib.ptr(d_), _lib.ptr(B_), _lib.ptr(C_), _lib.ptr(A32), ash, asn, code, Bt, L,
+                      H, Dh, N, seg, _lib.ptr(gu), _lib.ptr(gd), _lib.ptr(gB), _lib.ptr(gC),
+                      _lib.ptr(gA), _lib.ptr(ws), ws.numel(), _lib.stream_of(dev))
+        return gu, gd, gB, gC, gA, None
+
+
+def ssd_scan(u, delta, B, C, A_neg, seg=DEFAULT_SEG):
+    """Head-wise SSD (Mamba-2) selective scan (``ssd.py:344-362``).
+
+    Args:
+        u:      [B, L, H, Dh] input projected to heads x channels
+        delta:  [B, L, H]     per-token, per-head step size (>= 0)
+        B:      [B, L, H, N]  input projection
+        C:      [B, L, H, N]  output projection
+        A_neg:  [H, N]        decay rates (negative)
+        seg:    checkpoint segment length (L % seg == 0; default 32)
+
+    Returns:
+        y:      [B, L, H, Dh] float32
+    """
+    y, _ = _SSDScan.apply(u, delta, B, C, A_neg, seg)
+    return y
+
+
+def ssd_scan_with_state(u, delta, B, C, A_neg, seg=DEFAULT_SEG):
+    """SSD scan that also returns the final state ``[B, H, Dh, N]`` (``ssd.py:365-375``)."""
+    return _SSDScan.apply(u, delta, B, C, A_neg, seg)
+
+
+def ssd_scan_reference(u, delta, B, C, A_neg):
+    """Per-step torch loop (``ssd.py:382-394``). Differentiable, any device."""
+    Bt, L, H, Dh = u.shape
+    N = A_neg.shape[-1]
+    ft = torch.promote_types(u.dtype, torch.float32)
+    h = torch.zeros((Bt, H, Dh, N), dtype=ft, device=u.device)
+    ys = []
+    for t in range(L):
+        dt = delta[:, t, :, None, None]
+        decay = torch.exp(dt * A_neg[None, :, None, :])
+        inp = dt * B[:, t, :, None, :] * u[:, t, :, :, None]
+        h = decay * h + inp
+        ys.append(torch.sum(h * C[:, t, :, None, :], dim=-1))
+    return torch.stack(ys, dim=1)

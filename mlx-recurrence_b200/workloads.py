@@ -1,0 +1,107 @@
+"""Seeded synthetic inputs for the benchmark configurations c0-c4.
+
+The reference measures on no public dataset; these generators draw inputs
+with the shapes and value distributions of its published configurations
+(from the reference's own test inputs and
+``docs/validation``). ``shard=(rank, world)`` returns one rank's slice of the
+independent units: a contiguous batch range when ``world`` divides B.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+CONFIGS = {
+    "c0": dict(kind="ssd", B=3, L=512, H=12, Dh=64, N=16, seg=32, dtype=torch.float32),
+    "c1": dict(kind="gla", B=3, L=512, H=12, Dh=64, seg=32, dtype=torch.bfloat16),
+    "c2": dict(kind="rglru", B=8, L=4096, D=2560, seg=32, dtype=torch.bfloat16),
+    "c3": dict(kind="rotlru", B=16, L=8192, Dp=1024, seg=32, dtype=torch.bfloat16),
+    "c4": dict(kind="ssd", B=32, L=16384, H=32, Dh=64, N=128, seg=32, dtype=torch.bfloat16),
+}
+
+DESCRIPTION = {
+    "c0": "ssd_scan fp32 B=3 L=512 H=12 Dh=64 N=16 seg=32",
+    "c1": "gla_scan bf16 B=3 L=512 H=12 Dh=64 seg=32",
+    "c2": "rglru_scan bf16 B=8 L=4096 D=2560 seg=32",
+    "c3": "rotlru_scan bf16 B=16 L=8192 D=2048 seg=32",
+    "c4": "ssd_scan bf16 B=32 L=16384 H=32 Dh=64 N=128 seg=32",
+}
+
+
+def tokens(cfg):
+    return cfg["B"] * cfg["L"]
+
+
+def shard_batch(B, rank, world):
+    """Contiguous batch range [b0, b1) of one rank."""
+    per = B // world
+    rem = B % world
+    b0 = rank * per + min(rank, rem)
+    return b0, b0 + per + (1 if rank < rem else 0)
+
+
+def make_inputs(name, device, seed=0, batch=None):
+    """Primal inputs of config ``name`` (tuple, in kernel order) on ``device``.
+
+    ``batch`` overrides B (a rank's shard size). Values are drawn in float32
+    from a generator on ``device`` and then cast to the config dtype.
+    """
+    cfg = dict(CONFIGS[name])
+    if batch is not None:
+        cfg["B"] = batch
+    g = torch.Generator(device=device).manual_seed(seed)
+    f32 = dict(dtype=torch.float32, device=device, generator=g)
+    dt = cfg["dtype"]
+    B, L = cfg["B"], cfg["L"]
+    if cfg["kind"] == "ssd":
+        H, Dh, N = cfg["H"], cfg["Dh"], cfg["N"]
+        u = torch.randn((B, L, H, Dh), **f32)
+        delta = torch.randn((B, L, H), **f32).abs_().mul_(0.1).add_(0.01)
+        Bm = torch.randn((B, L, H, N), **f32)
+        Cm = torch.randn((B, L, H, N), **f32)
+        A = -torch.exp(torch.randn((H,), **f32) * 0.5)
+        A_neg = A[:, None].expand(H, N)  # one rate per head, broadcast over N
+        return (u.to(dt), delta.to(dt), Bm.to(dt), Cm.to(dt), A_neg)
+    if cfg["kind"] == "gla":
+        H, Dh = cfg["H"], cfg["Dh"]
+        s = 1.0 / math.sqrt(Dh)
+        q = torch.randn((B, L, H, Dh), **f32) * s
+        k = torch.randn((B, L, H, Dh), **f32) * s
+        v = torch.randn((B, L, H, Dh), **f32) * s
+        g_ = torch.sigmoid(torch.randn((B, L, H), **f32) + 2.0)
+        return tuple(t.to(dt) for t in (q, k, v, g_))
+    if cfg["kind"] == "rglru":
+        D = cfg["D"]
+        x = torch.randn((B, L, D), **f32)
+        r = torch.sigmoid(torch.randn((B, L, D), **f32))
+        i = torch.sigmoid(torch.randn((B, L, D), **f32))
+        lam = torch.rand((D,), **f32) * (6.9 - 2.2) + 2.2
+        a = torch.sigmoid(lam) ** (8.0 * r)
+        b = torch.sqrt(1.0 - a * a) * (i * x)
+        return (a.to(dt), b.to(dt))
+    if cfg["kind"] == "rotlru":
+        Dp = cfg["Dp"]
+        x = torch.randn((B, L, 2 * Dp), **f32)
+        a = torch.sigmoid(torch.randn((B, L, Dp), **f32) + 3.0)
+        th = (torch.rand((B, L, Dp), **f32) * 2.0 - 1.0) * (math.pi / 16)
+        return (a.to(dt), torch.cos(th).to(dt), torch.sin(th).to(dt), x.to(dt))
+    raise KeyError(name)
+
+
+def output_shape(name, batch=None):
+    cfg = CONFIGS[name]
+    B = cfg["B"] if batch is None else batch
+    if cfg["kind"] in ("ssd", "gla"):
+        return (B, cfg["L"], cfg["H"], cfg["Dh"])
+    if cfg["kind"] == "rglru":
+        return (B, cfg["L"], cfg["D"])
+    return (B, cfg["L"], 2 * cfg["Dp"])
+
+
+def scan_fn(pkg, name):
+    kind = CONFIGS[name]["kind"]
+    seg = CONFIGS[name]["seg"]
+    f = getattr(pkg, f"{kind}_scan")
+    return lambda *xs: f(*xs, seg=seg)
