@@ -94,32 +94,46 @@ class ClockSampler:
     def __init__(self, gpu_id):
         self.gpu_id = gpu_id
         self.proc = None
+        self.lines = []  # (wall time, csv line)
+
+    def _reader(self):
+        for line in self.proc.stdout:
+            self.lines.append((time.time(), line))
 
     def __enter__(self):
+        import threading
         try:
             cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                   "-lms", "200"]
+                   "-lms", "50"]
             if self.gpu_id is not None:
                 cmd.insert(1, f"--id={self.gpu_id}")
             self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._reader, daemon=True).start()
+            t_end = time.time() + 3.0
+            while not self.lines and time.time() < t_end and self.proc.poll() is None:
+                time.sleep(0.01)
         except (OSError, ValueError):
             self.proc = None
+        self.t0 = time.time()
         return self
 
     def __exit__(self, *a):
-        self.out = ""
+        self.t1 = time.time()
+        time.sleep(0.06)
         if self.proc is not None:
             self.proc.terminate()
             try:
-                self.out, _ = self.proc.communicate(timeout=5)
+                self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
-                self.out, _ = self.proc.communicate()
 
     def summary(self):
         sm, mx, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in (self.out or "").strip().splitlines():
+        inside = [l for ts, l in self.lines if self.t0 - 0.03 <= ts <= self.t1 + 0.06]
+        if not inside:  # region shorter than the sampling interval: nearest sample after start
+            inside = [l for ts, l in self.lines if ts >= self.t0][:1]
+        for line in inside:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 8:
                 continue

@@ -72,6 +72,12 @@ MR_API const char* mr_last_error(void);
 /* Number of kernels this library has launched in this process (all threads). */
 MR_API uint64_t mr_launch_count(void);
 
+/* Device-side error word of the current device's kernels: 0 = none,
+ * 1 = a bounded wait on an asynchronous copy timed out (results invalid),
+ * -1 = the word could not be read. Synchronises with the device; clear != 0
+ * resets the word. For diagnostics and tests. */
+MR_API int mr_device_error_status(int clear);
+
 /* Shape rule of the checkpoint/recompute pattern: seg > 0, L % seg == 0 and
  * lane_dim % 32 == 0 (mlx_recurrence/_chassis.py:92-115). lane_name names
  * lane_dim in the message. Host-only, launches nothing. */

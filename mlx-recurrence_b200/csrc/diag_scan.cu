@@ -4,316 +4,38 @@
 //
 // Reference kernels: mlx_recurrence/rglru.py:64-203, rotlru.py:80-266.
 // The reference walks all L steps with one thread per channel (rglru.py:81-101);
-// at B*D = 20,480 channels that leaves a B200 far from HBM saturation. Here a
-// CTA owns a tile of W = 32*V adjacent channels of one batch row and walks L
-// in blocks of 8*TW steps; inside a block each of the 8 warps owns TW
-// consecutive steps, so every warp-wide load is one contiguous row segment
-// (coalesced, V elements per lane) and 8 steps' worth of loads are in flight
-// per thread, with the next block prefetched into registers.
+// at B*D = 20,480 channels that leaves a B200 far from HBM saturation.
 //
-// Within a block the scan is the classic three-phase chunk scan over the
-// affine step maps h -> a*h + x:
+// Layout of the work. A CTA (8 warps) owns a tile of W adjacent channels
+// (pairs for rotLRU) of one batch row and walks L in blocks of TB steps.
+// Each block's input rows are streamed global -> shared memory by the TMA
+// unit (one cp.async.bulk per row and input, completing on a per-stage
+// mbarrier) through an S-stage ring, so S-1 blocks are in flight while one
+// is computed and the registers stay free. Inside a block warp w owns TW =
+// TB/8 consecutive steps and lane l owns W/32 adjacent channels.
+//
+// The scan inside a block is the three-phase chunk scan over the affine step
+// maps h -> a*h + x:
 //   1. each thread folds its TW steps into one map (A, H),
-//   2. the 8 per-warp maps are exchanged through shared memory and each thread
-//      folds the maps of the warps before it into its carry-in,
-//   3. each thread re-runs its TW steps from the carry-in with the reference's
-//      exact per-step update (rglru.py:92), writing y and the checkpoints.
-// The backward applies the same three phases twice per block: forward to
-// regenerate h_{t-1} from the block's starting checkpoint, then in reverse
-// to run the adjoint c_{t-1} = a_t * (gy_t + c_t) (rglru.py:36-39).
+//   2. the 8 per-warp maps go through shared memory and each thread folds
+//      the maps of the warps before it into its carry-in,
+//   3. each thread re-runs its steps from the carry-in with the reference's
+//      exact per-step update (rglru.py:92, rotlru.py:392-393), writing y and
+//      the segment checkpoints.
+// The backward walks blocks newest -> oldest. Blocks are aligned to segments
+// so each block starts from a checkpoint; it regenerates h_{t-1} with the
+// same three phases forward, then runs the adjoint c_{t-1} = a_t (gy_t + c_t)
+// (rotLRU: conj(z_t) (gy_t + c_t)) with the three phases in reverse.
+// Segments longer than one block first regenerate the state at each of
+// their block starts (plain loads) into the workspace.
 #include "common.cuh"
+#include "tma.cuh"
+#include "tmap.cuh"
 
 namespace mr {
 
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
-
-// ============================================================================
-// RG-LRU
-// ============================================================================
-
-template <typename T, int V, int TW>
-__global__ void __launch_bounds__(kThreads)
-rglru_fwd_kernel(const T* __restrict__ a, const T* __restrict__ x, int L, int64_t D, int seg,
-                 float* __restrict__ y, float* __restrict__ ckpt) {
-  constexpr int W = 32 * V;
-  constexpr int TB = kWarps * TW;
-  __shared__ float sA[2][kWarps][W];
-  __shared__ float sH[2][kWarps][W];
-
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int64_t b = blockIdx.y;
-  const int64_t c = (int64_t)blockIdx.x * W + lane * V;
-  const bool act = c < D;
-  const int64_t base = b * (int64_t)L * D + c;
-  const int nseg = L / seg;
-  const int nblk = (L + TB - 1) / TB;
-
-  Vec<T, V> ca[TW], cx[TW];
-  auto load = [&](int blk, Vec<T, V>(&ra)[TW], Vec<T, V>(&rx)[TW]) {
-    const int t0 = blk * TB + warp * TW;
-#pragma unroll
-    for (int i = 0; i < TW; ++i) {
-      if (act && t0 + i < L) {
-        ra[i] = ld_stream<T, V>(a + base + (int64_t)(t0 + i) * D);
-        rx[i] = ld_stream<T, V>(x + base + (int64_t)(t0 + i) * D);
-      }
-    }
-  };
-  load(0, ca, cx);
-
-  float carry[V];
-#pragma unroll
-  for (int v = 0; v < V; ++v) carry[v] = 0.f;
-
-  for (int blk = 0; blk < nblk; ++blk) {
-    Vec<T, V> na[TW], nx[TW];
-    if (blk + 1 < nblk) load(blk + 1, na, nx);
-    const int buf = blk & 1;
-    const int t0 = blk * TB + warp * TW;
-
-    // phase 1: fold this thread's TW steps
-#pragma unroll
-    for (int v = 0; v < V; ++v) {
-      float A = 1.f, H = 0.f;
-#pragma unroll
-      for (int i = 0; i < TW; ++i) {
-        if (t0 + i < L) {
-          const float av = to_f(ca[i].v[v]);
-          H = av * H + to_f(cx[i].v[v]);
-          A = av * A;
-        }
-      }
-      sA[buf][warp][lane * V + v] = A;
-      sH[buf][warp][lane * V + v] = H;
-    }
-    __syncthreads();
-
-    // phase 2: carry-in for this warp, carry-out of the block
-    float cin[V];
-#pragma unroll
-    for (int v = 0; v < V; ++v) {
-      float cur = carry[v];
-#pragma unroll
-      for (int w = 0; w < kWarps; ++w) {
-        if (w == warp) cin[v] = cur;
-        cur = sA[buf][w][lane * V + v] * cur + sH[buf][w][lane * V + v];
-      }
-      carry[v] = cur;
-    }
-
-    // phase 3: exact per-step recurrence from the carry-in (rglru.py:92-99)
-    if (act) {
-#pragma unroll
-      for (int i = 0; i < TW; ++i) {
-        const int t = t0 + i;
-        if (t < L) {
-          float hv[V];
-#pragma unroll
-          for (int v = 0; v < V; ++v) {
-            cin[v] = to_f(ca[i].v[v]) * cin[v] + to_f(cx[i].v[v]);
-            hv[v] = cin[v];
-          }
-          st_stream_f32<V>(y + base + (int64_t)t * D, hv);
-          if ((t + 1) % seg == 0) {
-            const int64_t s = (t + 1) / seg - 1;
-            st_stream_f32<V>(ckpt + (b * nseg + s) * D + c, hv);
-          }
-        }
-      }
-    }
-#pragma unroll
-    for (int i = 0; i < TW; ++i) {
-      ca[i] = na[i];
-      cx[i] = nx[i];
-    }
-  }
-}
-
-template <typename T, int V, int TW>
-__global__ void __launch_bounds__(kThreads)
-rglru_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfinal,
-                 const float* __restrict__ ckpt, const T* __restrict__ a, const T* __restrict__ x,
-                 int L, int64_t D, int seg, int grp, T* __restrict__ ga, T* __restrict__ gx,
-                 float* __restrict__ ws) {
-  constexpr int W = 32 * V;
-  constexpr int TB = kWarps * TW;
-  __shared__ float sA[2][kWarps][W];
-  __shared__ float sH[2][kWarps][W];
-  __shared__ float sR[2][kWarps][W];
-  __shared__ float sG[2][kWarps][W];
-
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int64_t b = blockIdx.y;
-  const int64_t c = (int64_t)blockIdx.x * W + lane * V;
-  const bool act = c < D;
-  const int64_t base = b * (int64_t)L * D + c;
-  const int nseg = L / seg;
-  const int glen = grp * seg;                  // steps per segment group
-  const int ngrp = (nseg + grp - 1) / grp;
-  const int nsub_max = (glen + TB - 1) / TB;   // > 1 only when seg > TB
-  float* wsb = ws + ((b * gridDim.x + blockIdx.x) * (int64_t)nsub_max) * W + lane * V;
-  int it = 0;                                  // shared-buffer parity counter
-
-  // incoming adjoint carry c_L = dL/dh_final (rglru.py drops it; see mlrec.h)
-  float cr[V];
-#pragma unroll
-  for (int v = 0; v < V; ++v) cr[v] = (gfinal != nullptr && act) ? gfinal[b * D + c + v] : 0.f;
-
-  for (int g = ngrp - 1; g >= 0; --g) {
-    const int g0 = g * glen;
-    const int gl = min(glen, L - g0);
-    const int nsub = (gl + TB - 1) / TB;
-    float hstart[V];
-#pragma unroll
-    for (int v = 0; v < V; ++v)
-      hstart[v] = (g0 > 0 && act) ? ckpt[(b * nseg + g0 / seg - 1) * D + c + v] : 0.f;
-
-    // pass 1 (segments longer than one block): states at sub-block starts
-    if (nsub > 1) {
-      float cur[V];
-#pragma unroll
-      for (int v = 0; v < V; ++v) cur[v] = hstart[v];
-      for (int j = 0; j + 1 < nsub; ++j, ++it) {
-        const int buf = it & 1;
-        const int t0 = g0 + j * TB + warp * TW;
-        const int tend = g0 + gl;
-#pragma unroll
-        for (int v = 0; v < V; ++v) {
-          float A = 1.f, H = 0.f;
-#pragma unroll
-          for (int i = 0; i < TW; ++i) {
-            if (act && t0 + i < tend) {
-              const float av = to_f(a[base + (int64_t)(t0 + i) * D + v]);
-              H = av * H + to_f(x[base + (int64_t)(t0 + i) * D + v]);
-              A = av * A;
-            }
-          }
-          sA[buf][warp][lane * V + v] = A;
-          sH[buf][warp][lane * V + v] = H;
-        }
-        __syncthreads();
-#pragma unroll
-        for (int v = 0; v < V; ++v) {
-#pragma unroll
-          for (int w = 0; w < kWarps; ++w) cur[v] = sA[buf][w][lane * V + v] * cur[v] + sH[buf][w][lane * V + v];
-          if (warp == 0 && act) wsb[(int64_t)(j + 1) * W + v] = cur[v];
-        }
-      }
-      __syncthreads();
-    }
-
-    // pass 2: sub-blocks newest -> oldest
-    for (int j = nsub - 1; j >= 0; --j, ++it) {
-      const int buf = it & 1;
-      const int s0 = g0 + j * TB;
-      const int sl = min(TB, g0 + gl - s0);
-      const int t0 = s0 + warp * TW;
-      const int tend = s0 + sl;
-
-      float fa[TW][V], fxv[TW][V], fg[TW][V];
-#pragma unroll
-      for (int i = 0; i < TW; ++i) {
-        const bool ok = act && (t0 + i < tend);
-        if (ok) {
-          const int64_t off = base + (int64_t)(t0 + i) * D;
-          Vec<T, V> ra = ld_stream<T, V>(a + off);
-          Vec<T, V> rx = ld_stream<T, V>(x + off);
-          Vec<float, V> rg = ld_stream<float, V>(gy + off);
-#pragma unroll
-          for (int v = 0; v < V; ++v) {
-            fa[i][v] = to_f(ra.v[v]);
-            fxv[i][v] = to_f(rx.v[v]);
-            fg[i][v] = rg.v[v];
-          }
-        } else {
-#pragma unroll
-          for (int v = 0; v < V; ++v) {
-            fa[i][v] = 1.f;
-            fxv[i][v] = 0.f;
-            fg[i][v] = 0.f;
-          }
-        }
-      }
-      float hs[V];
-#pragma unroll
-      for (int v = 0; v < V; ++v) hs[v] = (j == 0) ? hstart[v] : (act ? wsb[(int64_t)j * W + v] : 0.f);
-
-      // forward phase 1
-#pragma unroll
-      for (int v = 0; v < V; ++v) {
-        float A = 1.f, H = 0.f;
-#pragma unroll
-        for (int i = 0; i < TW; ++i) {
-          H = fa[i][v] * H + fxv[i][v];
-          A = fa[i][v] * A;
-        }
-        sA[buf][warp][lane * V + v] = A;
-        sH[buf][warp][lane * V + v] = H;
-      }
-      // reverse phase 1: c_out = a*(gy + c_in), folded newest -> oldest
-#pragma unroll
-      for (int v = 0; v < V; ++v) {
-        float A = 1.f, G = 0.f;
-#pragma unroll
-        for (int i = TW - 1; i >= 0; --i) {
-          G = fa[i][v] * (fg[i][v] + G);
-          A = fa[i][v] * A;
-        }
-        sR[buf][warp][lane * V + v] = A;
-        sG[buf][warp][lane * V + v] = G;
-      }
-      __syncthreads();
-
-      float hp[TW][V];   // h_{t-1} for each owned step
-      float crin[V];
-#pragma unroll
-      for (int v = 0; v < V; ++v) {
-        float cur = hs[v];
-#pragma unroll
-        for (int w = 0; w < kWarps; ++w) {
-          if (w == warp) break;
-          cur = sA[buf][w][lane * V + v] * cur + sH[buf][w][lane * V + v];
-        }
-#pragma unroll
-        for (int i = 0; i < TW; ++i) {
-          hp[i][v] = cur;
-          cur = fa[i][v] * cur + fxv[i][v];
-        }
-        float rc = cr[v];
-#pragma unroll
-        for (int w = kWarps - 1; w >= 0; --w) {
-          if (w == warp) crin[v] = rc;
-          rc = sR[buf][w][lane * V + v] * rc + sG[buf][w][lane * V + v];
-        }
-        cr[v] = rc;
-      }
-
-      // reverse phase 3: adjoint per step (rglru.py:173-178)
-#pragma unroll
-      for (int i = TW - 1; i >= 0; --i) {
-        const int t = t0 + i;
-        float gxa[V], gaa[V];
-#pragma unroll
-        for (int v = 0; v < V; ++v) {
-          const float adj = fg[i][v] + crin[v];
-          gxa[v] = adj;
-          gaa[v] = adj * hp[i][v];
-          crin[v] = adj * fa[i][v];
-        }
-        if (act && t < tend) {
-          const int64_t off = base + (int64_t)t * D;
-          st_vec<T, V>(gx + off, gxa);
-          st_vec<T, V>(ga + off, gaa);
-        }
-      }
-    }
-  }
-}
-
-// ============================================================================
-// Rotational LRU (complex pair per channel; rotlru.py:80-266)
-// ============================================================================
 
 struct cf {
   float r, i;
@@ -323,71 +45,472 @@ __device__ __forceinline__ cf cfma(cf p, cf q, cf s) {  // p*q + s
   return {p.r * q.r - p.i * q.i + s.r, p.r * q.i + p.i * q.r + s.i};
 }
 
-template <typename T, int V, int TW>
-__global__ void __launch_bounds__(kThreads)
-rotlru_fwd_kernel(const T* __restrict__ a, const T* __restrict__ cs, const T* __restrict__ sn,
-                  const T* __restrict__ x, int L, int64_t Dp, int seg, float* __restrict__ y,
-                  float* __restrict__ ckpt) {
-  constexpr int W = 32 * V;
-  constexpr int TB = kWarps * TW;
-  __shared__ cf sZ[2][kWarps][W];
-  __shared__ cf sH[2][kWarps][W];
+// Block q of the backward's block sequence (segment aligned). Small segments:
+// blocks of tbe = (TB/seg)*seg steps. Long segments: nsub blocks per
+// segment, the last one possibly short.
+struct BlockMap {
+  int L, seg, TB, tbe, nsub, nq;
+  __device__ __host__ BlockMap(int L_, int seg_, int TB_) : L(L_), seg(seg_), TB(TB_) {
+    if (seg <= TB) {
+      tbe = (TB / seg) * seg;
+      nsub = 1;
+      nq = (L + tbe - 1) / tbe;
+    } else {
+      tbe = TB;
+      nsub = (seg + TB - 1) / TB;
+      nq = (L / seg) * nsub;
+    }
+  }
+  __device__ void range(int q, int& t0, int& nt, int& j) const {
+    if (nsub == 1) {
+      t0 = q * tbe;
+      nt = min(tbe, L - t0);
+      j = 0;
+    } else {
+      const int s = q / nsub;
+      j = q % nsub;
+      t0 = s * seg + j * TB;
+      nt = min(TB, (s + 1) * seg - t0);
+    }
+  }
+};
+
+// ============================================================================
+// RG-LRU forward
+// ============================================================================
+
+template <typename T, int W, int TB, int S>
+struct RgFwdSmem {
+  static constexpr size_t bytes = (size_t)2 * S * TB * W * sizeof(T) + 2 * 2 * kWarps * W * 4 + S * 8;
+};
+
+template <typename T, int W, int TB, int S>
+__global__ void __launch_bounds__(kThreads, 3)
+rglru_fwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_x,
+                 int L, int64_t D, int seg, float* __restrict__ y, float* __restrict__ ckpt) {
+  constexpr int V = W / 32, TW = TB / kWarps;
+  extern __shared__ __align__(128) unsigned char smem[];
+  T* sa = reinterpret_cast<T*>(smem);
+  T* sx = sa + S * TB * W;
+  float* sA = reinterpret_cast<float*>(sx + S * TB * W);
+  float* sH = sA + 2 * kWarps * W;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sH + 2 * kWarps * W);
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t b = blockIdx.y;
-  const int64_t p = (int64_t)blockIdx.x * W + lane * V;  // first pair
-  const bool act = p < Dp;
-  const int64_t D = 2 * Dp;
-  const int64_t pbase = b * (int64_t)L * Dp + p;
-  const int64_t xbase = b * (int64_t)L * D + 2 * p;
+  const int64_t c0 = (int64_t)blockIdx.x * W;
+  const int Wv = (int)min((int64_t)W, D - c0);
+  const int cl = lane * V;
+  const bool act = cl < Wv;
   const int nseg = L / seg;
   const int nblk = (L + TB - 1) / TB;
+  const int64_t gbase = b * (int64_t)L * D + c0;
 
-  Vec<T, V> ca[TW], cc[TW], cs_[TW];
-  Vec<T, 2 * V> cx[TW];
-  auto load = [&](int blk, Vec<T, V>(&ra)[TW], Vec<T, V>(&rc)[TW], Vec<T, V>(&rs)[TW],
-                  Vec<T, 2 * V>(&rx)[TW]) {
-    const int t0 = blk * TB + warp * TW;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) mbar_init(&bar[s], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  auto issue = [&](int blk) {  // one thread: a [TB x W] box per input
+    const int s = blk % S, row = (int)(b * L) + blk * TB;
+    mbar_arrive_expect_tx(&bar[s], 2u * TB * W * sizeof(T));
+    tma_load_2d(sa + s * TB * W, &tm_a, (int)c0, row, &bar[s]);
+    tma_load_2d(sx + s * TB * W, &tm_x, (int)c0, row, &bar[s]);
+  };
+  if (threadIdx.x == 0)
+    for (int k = 0; k < S - 1 && k < nblk; ++k) issue(k);
+
+  float carry[V];
+#pragma unroll
+  for (int v = 0; v < V; ++v) carry[v] = 0.f;
+
+  for (int blk = 0; blk < nblk; ++blk) {
+    const int s = blk % S;
+    mbar_wait(&bar[s], (blk / S) & 1);
+    const int buf = blk & 1;
+    const int r0 = warp * TW;
+    const int t0 = blk * TB + r0;
+    const T* ra = sa + (s * TB + r0) * W + cl;
+    const T* rx = sx + (s * TB + r0) * W + cl;
+
+    float fa[TW][V], fx[TW][V];
 #pragma unroll
     for (int i = 0; i < TW; ++i) {
-      if (act && t0 + i < L) {
-        const int64_t o = pbase + (int64_t)(t0 + i) * Dp;
-        ra[i] = ld_stream<T, V>(a + o);
-        rc[i] = ld_stream<T, V>(cs + o);
-        rs[i] = ld_stream<T, V>(sn + o);
-        rx[i] = ld_stream<T, 2 * V>(x + xbase + (int64_t)(t0 + i) * D);
+      const bool ok = t0 + i < L;
+      const Vec<T, V> va = ld_vec<T, V>(ra + i * W);
+      const Vec<T, V> vx = ld_vec<T, V>(rx + i * W);
+#pragma unroll
+      for (int v = 0; v < V; ++v) {
+        fa[i][v] = ok ? to_f(va.v[v]) : 1.f;
+        fx[i][v] = ok ? to_f(vx.v[v]) : 0.f;
       }
     }
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      float A = 1.f, H = 0.f;
+#pragma unroll
+      for (int i = 0; i < TW; ++i) {
+        H = fa[i][v] * H + fx[i][v];
+        A = fa[i][v] * A;
+      }
+      sA[(buf * kWarps + warp) * W + cl + v] = A;
+      sH[(buf * kWarps + warp) * W + cl + v] = H;
+    }
+    __syncthreads();
+    // every thread is past block blk-1: its stage can be refilled
+    if (threadIdx.x == 0 && blk + S - 1 < nblk) {
+      fence_proxy_async_smem();
+      issue(blk + S - 1);
+    }
+
+    float cin[V];
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      float cur = carry[v];
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) {
+        if (w == warp) cin[v] = cur;
+        cur = sA[(buf * kWarps + w) * W + cl + v] * cur + sH[(buf * kWarps + w) * W + cl + v];
+      }
+      carry[v] = cur;
+    }
+
+    if (act) {
+      float* yr = y + gbase + (int64_t)t0 * D + cl;
+      int rem = (t0 + 1) % seg;  // (t + 1) mod seg, advanced per step
+      int sidx = (t0 + 1) / seg;
+#pragma unroll
+      for (int i = 0; i < TW; ++i) {
+        const int t = t0 + i;
+        if (t < L) {
+          float hv[V];
+#pragma unroll
+          for (int v = 0; v < V; ++v) {
+            cin[v] = fa[i][v] * cin[v] + fx[i][v];  // rglru.py:92
+            hv[v] = cin[v];
+          }
+          st_stream_f32<V>(yr, hv);
+          if (rem == 0) st_stream_f32<V>(ckpt + (b * nseg + sidx - 1) * D + c0 + cl, hv);
+        }
+        yr += D;
+        if (++rem == seg) {
+          rem = 0;
+          ++sidx;
+        }
+      }
+    }
+  }
+}
+
+// ============================================================================
+// RG-LRU backward
+// ============================================================================
+
+template <typename T, int W, int TB, int S>
+struct RgBwdSmem {
+  static constexpr size_t bytes =
+      (size_t)S * TB * W * (2 * sizeof(T) + 4) + 4 * 2 * kWarps * W * 4 + S * 8;
+};
+
+template <typename T, int W, int TB, int S>
+__global__ void __launch_bounds__(kThreads, 3)
+rglru_bwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_x,
+                 const __grid_constant__ CUtensorMap tm_g, const float* __restrict__ gfinal,
+                 const float* __restrict__ ckpt, const T* __restrict__ a, const T* __restrict__ x,
+                 int L, int64_t D, int seg, T* __restrict__ ga, T* __restrict__ gx,
+                 float* __restrict__ ws) {
+  constexpr int V = W / 32, TW = TB / kWarps;
+  extern __shared__ __align__(128) unsigned char smem[];
+  T* sa = reinterpret_cast<T*>(smem);
+  T* sx = sa + S * TB * W;
+  float* sg = reinterpret_cast<float*>(sx + S * TB * W);
+  float* sA = sg + S * TB * W;
+  float* sH = sA + 2 * kWarps * W;
+  float* sR = sH + 2 * kWarps * W;
+  float* sG = sR + 2 * kWarps * W;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sG + 2 * kWarps * W);
+
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t b = blockIdx.y;
+  const int64_t c0 = (int64_t)blockIdx.x * W;
+  const int Wv = (int)min((int64_t)W, D - c0);
+  const int cl = lane * V;
+  const bool act = cl < Wv;
+  const int nseg = L / seg;
+  const BlockMap bm(L, seg, TB);
+  const int64_t gbase = b * (int64_t)L * D + c0;
+  float* wsb = ws + ((b * gridDim.x + blockIdx.x) * (int64_t)bm.nsub) * W + cl;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) mbar_init(&bar[s], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  // pipeline position p streams block q = nq-1-p
+  auto issue = [&](int p) {  // one thread: [TB x W] boxes of a, x, grad_y
+    const int s = p % S;
+    int t0, nt, j;
+    bm.range(bm.nq - 1 - p, t0, nt, j);
+    const int row = (int)(b * L) + t0;
+    mbar_arrive_expect_tx(&bar[s], (uint32_t)TB * W * (2u * sizeof(T) + 4u));
+    tma_load_2d(sa + s * TB * W, &tm_a, (int)c0, row, &bar[s]);
+    tma_load_2d(sx + s * TB * W, &tm_x, (int)c0, row, &bar[s]);
+    tma_load_2d(sg + s * TB * W, &tm_g, (int)c0, row, &bar[s]);
   };
-  load(0, ca, cc, cs_, cx);
+  if (threadIdx.x == 0)
+    for (int k = 0; k < S - 1 && k < bm.nq; ++k) issue(k);
+
+  float cr[V];
+#pragma unroll
+  for (int v = 0; v < V; ++v) cr[v] = (gfinal != nullptr && act) ? gfinal[b * D + c0 + cl + v] : 0.f;
+  int it = 0;  // exchange-buffer parity
+
+  for (int p = 0; p < bm.nq; ++p) {
+    const int q = bm.nq - 1 - p;
+    int tb0, ntb, j;
+    bm.range(q, tb0, ntb, j);
+
+    // long segments: regenerate the state at every block start of the segment
+    if (bm.nsub > 1 && j == bm.nsub - 1) {
+      const int sidx = tb0 / seg;
+      const int s0 = sidx * seg;
+      float cur[V];
+#pragma unroll
+      for (int v = 0; v < V; ++v)
+        cur[v] = (sidx > 0 && act) ? ckpt[(b * nseg + sidx - 1) * D + c0 + cl + v] : 0.f;
+      for (int jj = 0; jj + 1 < bm.nsub; ++jj, ++it) {
+        const int buf = it & 1;
+        const int t0 = s0 + jj * TB + warp * TW;
+        const int tend = min(s0 + (jj + 1) * TB, s0 + seg);
+#pragma unroll
+        for (int v = 0; v < V; ++v) {
+          float A = 1.f, H = 0.f;
+#pragma unroll
+          for (int i = 0; i < TW; ++i) {
+            if (act && t0 + i < tend) {
+              const float av = to_f(a[gbase + (int64_t)(t0 + i) * D + cl + v]);
+              H = av * H + to_f(x[gbase + (int64_t)(t0 + i) * D + cl + v]);
+              A = av * A;
+            }
+          }
+          sA[(buf * kWarps + warp) * W + cl + v] = A;
+          sH[(buf * kWarps + warp) * W + cl + v] = H;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int v = 0; v < V; ++v) {
+#pragma unroll
+          for (int w = 0; w < kWarps; ++w)
+            cur[v] = sA[(buf * kWarps + w) * W + cl + v] * cur[v] + sH[(buf * kWarps + w) * W + cl + v];
+          if (warp == 0 && act) wsb[(int64_t)(jj + 1) * W + v] = cur[v];
+        }
+      }
+      __syncthreads();
+    }
+
+    const int s = p % S;
+    mbar_wait(&bar[s], (p / S) & 1);
+    const int buf = it & 1;
+    ++it;
+    const int r0 = warp * TW;
+    const int t0 = tb0 + r0;
+    const int tend = tb0 + ntb;
+    const T* ra = sa + (s * TB + r0) * W + cl;
+    const T* rx = sx + (s * TB + r0) * W + cl;
+    const float* rg = sg + (s * TB + r0) * W + cl;
+
+    float fa[TW][V], fx[TW][V], fg[TW][V];
+#pragma unroll
+    for (int i = 0; i < TW; ++i) {
+      const bool ok = t0 + i < tend;
+      const Vec<T, V> va = ld_vec<T, V>(ra + i * W);
+      const Vec<T, V> vx = ld_vec<T, V>(rx + i * W);
+      const Vec<float, V> vg = ld_vec<float, V>(rg + i * W);
+#pragma unroll
+      for (int v = 0; v < V; ++v) {
+        fa[i][v] = ok ? to_f(va.v[v]) : 1.f;
+        fx[i][v] = ok ? to_f(vx.v[v]) : 0.f;
+        fg[i][v] = ok ? vg.v[v] : 0.f;
+      }
+    }
+    float hs[V];
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      if (j > 0)
+        hs[v] = act ? wsb[(int64_t)j * W + v] : 0.f;
+      else
+        hs[v] = (tb0 > 0 && act) ? ckpt[(b * nseg + tb0 / seg - 1) * D + c0 + cl + v] : 0.f;
+    }
+
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      float A = 1.f, H = 0.f, R = 1.f, G = 0.f;
+#pragma unroll
+      for (int i = 0; i < TW; ++i) {
+        H = fa[i][v] * H + fx[i][v];
+        A = fa[i][v] * A;
+      }
+#pragma unroll
+      for (int i = TW - 1; i >= 0; --i) {  // c_out = a * (gy + c_in)
+        G = fa[i][v] * (fg[i][v] + G);
+        R = fa[i][v] * R;
+      }
+      sA[(buf * kWarps + warp) * W + cl + v] = A;
+      sH[(buf * kWarps + warp) * W + cl + v] = H;
+      sR[(buf * kWarps + warp) * W + cl + v] = R;
+      sG[(buf * kWarps + warp) * W + cl + v] = G;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && p + S - 1 < bm.nq) {
+      fence_proxy_async_smem();
+      issue(p + S - 1);
+    }
+
+    float hp[TW][V], crin[V];
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      float cur = hs[v];
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) {
+        if (w == warp) break;
+        cur = sA[(buf * kWarps + w) * W + cl + v] * cur + sH[(buf * kWarps + w) * W + cl + v];
+      }
+#pragma unroll
+      for (int i = 0; i < TW; ++i) {
+        hp[i][v] = cur;
+        cur = fa[i][v] * cur + fx[i][v];
+      }
+      float rc = cr[v];
+#pragma unroll
+      for (int w = kWarps - 1; w >= 0; --w) {
+        if (w == warp) crin[v] = rc;
+        rc = sR[(buf * kWarps + w) * W + cl + v] * rc + sG[(buf * kWarps + w) * W + cl + v];
+      }
+      cr[v] = rc;
+    }
+
+    // adjoint per step, newest -> oldest (rglru.py:173-178)
+#pragma unroll
+    for (int i = TW - 1; i >= 0; --i) {
+      const int t = t0 + i;
+      float o_x[V], o_a[V];
+#pragma unroll
+      for (int v = 0; v < V; ++v) {
+        const float adj = fg[i][v] + crin[v];
+        o_x[v] = adj;
+        o_a[v] = adj * hp[i][v];
+        crin[v] = adj * fa[i][v];
+      }
+      if (act && t < tend) {
+        const int64_t o = gbase + (int64_t)t * D + cl;
+        st_vec<T, V>(gx + o, o_x);
+        st_vec<T, V>(ga + o, o_a);
+      }
+    }
+  }
+}
+
+// ============================================================================
+// rotLRU forward (pairs interleaved in x / y; rotlru.py:80-146)
+// ============================================================================
+
+template <typename T, int W, int TB, int S>
+struct RotFwdSmem {
+  static constexpr size_t bytes = (size_t)S * TB * W * 5 * sizeof(T) + 2 * 2 * kWarps * W * 8 + S * 8;
+};
+
+template <typename T, int W, int TB, int S>
+__global__ void __launch_bounds__(kThreads, 2)
+rotlru_fwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_c,
+                  const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_x,
+                  int L, int64_t Dp, int seg, float* __restrict__ y, float* __restrict__ ckpt) {
+  constexpr int V = W / 32, TW = TB / kWarps;
+  extern __shared__ __align__(128) unsigned char smem[];
+  T* sa = reinterpret_cast<T*>(smem);
+  T* sc = sa + S * TB * W;
+  T* ss = sc + S * TB * W;
+  T* sx = ss + S * TB * W;  // [S][TB][2W]
+  cf* sZ = reinterpret_cast<cf*>(sx + S * TB * 2 * W);
+  cf* sH = sZ + 2 * kWarps * W;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sH + 2 * kWarps * W);
+
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t b = blockIdx.y;
+  const int64_t p0 = (int64_t)blockIdx.x * W;
+  const int Wv = (int)min((int64_t)W, Dp - p0);
+  const int pl = lane * V;
+  const bool act = pl < Wv;
+  const int64_t D = 2 * Dp;
+  const int nseg = L / seg;
+  const int nblk = (L + TB - 1) / TB;
+  const int64_t pbase = b * (int64_t)L * Dp + p0;
+  const int64_t xbase = b * (int64_t)L * D + 2 * p0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) mbar_init(&bar[s], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  auto issue = [&](int blk) {  // one thread: [TB x W] boxes of a, cs, sn; [TB x 2W] of x
+    const int s = blk % S, row = (int)(b * L) + blk * TB;
+    mbar_arrive_expect_tx(&bar[s], (uint32_t)TB * W * 5u * sizeof(T));
+    tma_load_2d(sa + s * TB * W, &tm_a, (int)p0, row, &bar[s]);
+    tma_load_2d(sc + s * TB * W, &tm_c, (int)p0, row, &bar[s]);
+    tma_load_2d(ss + s * TB * W, &tm_s, (int)p0, row, &bar[s]);
+    tma_load_2d(sx + s * TB * 2 * W, &tm_x, (int)(2 * p0), row, &bar[s]);
+  };
+  if (threadIdx.x == 0)
+    for (int k = 0; k < S - 1 && k < nblk; ++k) issue(k);
 
   cf carry[V];
 #pragma unroll
   for (int v = 0; v < V; ++v) carry[v] = {0.f, 0.f};
 
   for (int blk = 0; blk < nblk; ++blk) {
-    Vec<T, V> na[TW], nc[TW], ns[TW];
-    Vec<T, 2 * V> nx[TW];
-    if (blk + 1 < nblk) load(blk + 1, na, nc, ns, nx);
+    const int s = blk % S;
+    mbar_wait(&bar[s], (blk / S) & 1);
     const int buf = blk & 1;
-    const int t0 = blk * TB + warp * TW;
+    const int r0 = warp * TW;
+    const int t0 = blk * TB + r0;
 
+    float fa[TW][V], fc[TW][V], fs[TW][V];
+    cf fx[TW][V];
+#pragma unroll
+    for (int i = 0; i < TW; ++i) {
+      const bool ok = t0 + i < L;
+      const int row = s * TB + r0 + i;
+      const Vec<T, V> va = ld_vec<T, V>(sa + row * W + pl);
+      const Vec<T, V> vc = ld_vec<T, V>(sc + row * W + pl);
+      const Vec<T, V> vs = ld_vec<T, V>(ss + row * W + pl);
+      const Vec<T, 2 * V> vx = ld_vec<T, 2 * V>(sx + row * 2 * W + 2 * pl);
+#pragma unroll
+      for (int v = 0; v < V; ++v) {
+        fa[i][v] = ok ? to_f(va.v[v]) : 1.f;
+        fc[i][v] = ok ? to_f(vc.v[v]) : 1.f;
+        fs[i][v] = ok ? to_f(vs.v[v]) : 0.f;
+        fx[i][v] = ok ? cf{to_f(vx.v[2 * v]), to_f(vx.v[2 * v + 1])} : cf{0.f, 0.f};
+      }
+    }
 #pragma unroll
     for (int v = 0; v < V; ++v) {
       cf Z = {1.f, 0.f}, H = {0.f, 0.f};
 #pragma unroll
       for (int i = 0; i < TW; ++i) {
-        if (t0 + i < L) {
-          const float av = to_f(ca[i].v[v]);
-          const cf z = {av * to_f(cc[i].v[v]), av * to_f(cs_[i].v[v])};
-          H = cfma(z, H, {to_f(cx[i].v[2 * v]), to_f(cx[i].v[2 * v + 1])});
-          Z = cmul(z, Z);
-        }
+        const cf z = {fa[i][v] * fc[i][v], fa[i][v] * fs[i][v]};
+        H = cfma(z, H, fx[i][v]);
+        Z = cmul(z, Z);
       }
-      sZ[buf][warp][lane * V + v] = Z;
-      sH[buf][warp][lane * V + v] = H;
+      sZ[(buf * kWarps + warp) * W + pl + v] = Z;
+      sH[(buf * kWarps + warp) * W + pl + v] = H;
     }
     __syncthreads();
+    if (threadIdx.x == 0 && blk + S - 1 < nblk) {
+      fence_proxy_async_smem();
+      issue(blk + S - 1);
+    }
 
     cf cin[V];
 #pragma unroll
@@ -396,262 +519,286 @@ rotlru_fwd_kernel(const T* __restrict__ a, const T* __restrict__ cs, const T* __
 #pragma unroll
       for (int w = 0; w < kWarps; ++w) {
         if (w == warp) cin[v] = cur;
-        cur = cfma(sZ[buf][w][lane * V + v], cur, sH[buf][w][lane * V + v]);
+        cur = cfma(sZ[(buf * kWarps + w) * W + pl + v], cur, sH[(buf * kWarps + w) * W + pl + v]);
       }
       carry[v] = cur;
     }
 
     if (act) {
+      int rem = (t0 + 1) % seg;  // (t + 1) mod seg, advanced per step
+      int sidx = (t0 + 1) / seg;
 #pragma unroll
-      for (int i = 0; i < TW; ++i) {
+      for (int i = 0; i < TW; ++i, ++rem) {
+        if (rem == seg) {
+          rem = 0;
+          ++sidx;
+        }
         const int t = t0 + i;
         if (t < L) {
           float hv[2 * V];
 #pragma unroll
           for (int v = 0; v < V; ++v) {
-            const float av = to_f(ca[i].v[v]), c = to_f(cc[i].v[v]), s = to_f(cs_[i].v[v]);
+            const float av = fa[i][v], c = fc[i][v], sv = fs[i][v];
             const float u = cin[v].r, w = cin[v].i;
-            // rotlru.py:110-111, same operation order
-            const float un = av * (c * u - s * w) + to_f(cx[i].v[2 * v]);
-            const float wn = av * (s * u + c * w) + to_f(cx[i].v[2 * v + 1]);
+            const float un = av * (c * u - sv * w) + fx[i][v].r;  // rotlru.py:392
+            const float wn = av * (sv * u + c * w) + fx[i][v].i;  // rotlru.py:393
             cin[v] = {un, wn};
             hv[2 * v] = un;
             hv[2 * v + 1] = wn;
           }
-          st_stream_f32<2 * V>(y + xbase + (int64_t)t * D, hv);
-          if ((t + 1) % seg == 0) {
-            const int64_t s = (t + 1) / seg - 1;
-            st_stream_f32<2 * V>(ckpt + (b * nseg + s) * D + 2 * p, hv);
-          }
+          st_stream_f32<2 * V>(y + xbase + (int64_t)t * D + 2 * pl, hv);
+          if (rem == 0) st_stream_f32<2 * V>(ckpt + (b * nseg + sidx - 1) * D + 2 * (p0 + pl), hv);
         }
       }
-    }
-#pragma unroll
-    for (int i = 0; i < TW; ++i) {
-      ca[i] = na[i];
-      cc[i] = nc[i];
-      cs_[i] = ns[i];
-      cx[i] = nx[i];
     }
   }
 }
 
-template <typename T, int V, int TW>
-__global__ void __launch_bounds__(kThreads)
-rotlru_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfinal,
+// ============================================================================
+// rotLRU backward (rotlru.py:153-266)
+// ============================================================================
+
+template <typename T, int W, int TB, int S>
+struct RotBwdSmem {
+  static constexpr size_t bytes =
+      (size_t)S * TB * W * (5 * sizeof(T) + 8) + 4 * 2 * kWarps * W * 8 + S * 8;
+};
+
+template <typename T, int W, int TB, int S>
+__global__ void __launch_bounds__(kThreads, 2)
+rotlru_bwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_c,
+                  const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_x,
+                  const __grid_constant__ CUtensorMap tm_g, const float* __restrict__ gfinal,
                   const float* __restrict__ ckpt, const T* __restrict__ a, const T* __restrict__ cs,
                   const T* __restrict__ sn, const T* __restrict__ x, int L, int64_t Dp, int seg,
-                  int grp, T* __restrict__ ga, T* __restrict__ gcs, T* __restrict__ gsn,
-                  T* __restrict__ gx, float* __restrict__ ws) {
-  constexpr int W = 32 * V;
-  constexpr int TB = kWarps * TW;
-  __shared__ cf sZ[2][kWarps][W];
-  __shared__ cf sH[2][kWarps][W];
-  __shared__ cf sR[2][kWarps][W];
-  __shared__ cf sG[2][kWarps][W];
+                  T* __restrict__ ga, T* __restrict__ gcs, T* __restrict__ gsn, T* __restrict__ gx,
+                  float* __restrict__ ws) {
+  constexpr int V = W / 32, TW = TB / kWarps;
+  extern __shared__ __align__(128) unsigned char smem[];
+  T* sa = reinterpret_cast<T*>(smem);
+  T* sc = sa + S * TB * W;
+  T* ss = sc + S * TB * W;
+  T* sx = ss + S * TB * W;                                  // [S][TB][2W]
+  float* sg = reinterpret_cast<float*>(sx + S * TB * 2 * W);  // [S][TB][2W]
+  cf* sZ = reinterpret_cast<cf*>(sg + S * TB * 2 * W);
+  cf* sH = sZ + 2 * kWarps * W;
+  cf* sR = sH + 2 * kWarps * W;
+  cf* sG = sR + 2 * kWarps * W;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sG + 2 * kWarps * W);
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t b = blockIdx.y;
-  const int64_t p = (int64_t)blockIdx.x * W + lane * V;
-  const bool act = p < Dp;
+  const int64_t p0 = (int64_t)blockIdx.x * W;
+  const int Wv = (int)min((int64_t)W, Dp - p0);
+  const int pl = lane * V;
+  const bool act = pl < Wv;
   const int64_t D = 2 * Dp;
-  const int64_t pbase = b * (int64_t)L * Dp + p;
-  const int64_t xbase = b * (int64_t)L * D + 2 * p;
   const int nseg = L / seg;
-  const int glen = grp * seg;
-  const int ngrp = (nseg + grp - 1) / grp;
-  const int nsub_max = (glen + TB - 1) / TB;
-  float* wsb = ws + ((b * gridDim.x + blockIdx.x) * (int64_t)nsub_max) * (2 * W) + 2 * lane * V;
-  int it = 0;
+  const BlockMap bm(L, seg, TB);
+  const int64_t pbase = b * (int64_t)L * Dp + p0;
+  const int64_t xbase = b * (int64_t)L * D + 2 * p0;
+  float* wsb = ws + ((b * gridDim.x + blockIdx.x) * (int64_t)bm.nsub) * (2 * W) + 2 * pl;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) mbar_init(&bar[s], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  auto issue = [&](int p) {  // one thread: boxes of a, cs, sn, x and grad_y
+    const int s = p % S;
+    int t0, nt, j;
+    bm.range(bm.nq - 1 - p, t0, nt, j);
+    const int row = (int)(b * L) + t0;
+    mbar_arrive_expect_tx(&bar[s], (uint32_t)TB * W * (5u * sizeof(T) + 8u));
+    tma_load_2d(sa + s * TB * W, &tm_a, (int)p0, row, &bar[s]);
+    tma_load_2d(sc + s * TB * W, &tm_c, (int)p0, row, &bar[s]);
+    tma_load_2d(ss + s * TB * W, &tm_s, (int)p0, row, &bar[s]);
+    tma_load_2d(sx + s * TB * 2 * W, &tm_x, (int)(2 * p0), row, &bar[s]);
+    tma_load_2d(sg + s * TB * 2 * W, &tm_g, (int)(2 * p0), row, &bar[s]);
+  };
+  if (threadIdx.x == 0)
+    for (int k = 0; k < S - 1 && k < bm.nq; ++k) issue(k);
 
   cf cr[V];
 #pragma unroll
   for (int v = 0; v < V; ++v)
-    cr[v] = (gfinal != nullptr && act) ? cf{gfinal[b * D + 2 * (p + v)], gfinal[b * D + 2 * (p + v) + 1]}
-                                       : cf{0.f, 0.f};
+    cr[v] = (gfinal != nullptr && act)
+                ? cf{gfinal[b * D + 2 * (p0 + pl + v)], gfinal[b * D + 2 * (p0 + pl + v) + 1]}
+                : cf{0.f, 0.f};
+  int it = 0;
 
-  for (int g = ngrp - 1; g >= 0; --g) {
-    const int g0 = g * glen;
-    const int gl = min(glen, L - g0);
-    const int nsub = (gl + TB - 1) / TB;
-    cf hstart[V];
-#pragma unroll
-    for (int v = 0; v < V; ++v) {
-      if (g0 > 0 && act) {
-        const float* ck = ckpt + (b * nseg + g0 / seg - 1) * D + 2 * (p + v);
-        hstart[v] = {ck[0], ck[1]};
-      } else {
-        hstart[v] = {0.f, 0.f};
-      }
-    }
+  for (int p = 0; p < bm.nq; ++p) {
+    const int q = bm.nq - 1 - p;
+    int tb0, ntb, j;
+    bm.range(q, tb0, ntb, j);
 
-    if (nsub > 1) {
+    if (bm.nsub > 1 && j == bm.nsub - 1) {
+      const int sidx = tb0 / seg;
+      const int s0 = sidx * seg;
       cf cur[V];
 #pragma unroll
-      for (int v = 0; v < V; ++v) cur[v] = hstart[v];
-      for (int j = 0; j + 1 < nsub; ++j, ++it) {
+      for (int v = 0; v < V; ++v) {
+        if (sidx > 0 && act) {
+          const float* ck = ckpt + (b * nseg + sidx - 1) * D + 2 * (p0 + pl + v);
+          cur[v] = {ck[0], ck[1]};
+        } else {
+          cur[v] = {0.f, 0.f};
+        }
+      }
+      for (int jj = 0; jj + 1 < bm.nsub; ++jj, ++it) {
         const int buf = it & 1;
-        const int t0 = g0 + j * TB + warp * TW;
-        const int tend = g0 + gl;
+        const int t0 = s0 + jj * TB + warp * TW;
+        const int tend = min(s0 + (jj + 1) * TB, s0 + seg);
 #pragma unroll
         for (int v = 0; v < V; ++v) {
           cf Z = {1.f, 0.f}, H = {0.f, 0.f};
 #pragma unroll
           for (int i = 0; i < TW; ++i) {
             if (act && t0 + i < tend) {
-              const int64_t o = pbase + (int64_t)(t0 + i) * Dp + v;
+              const int64_t o = pbase + (int64_t)(t0 + i) * Dp + pl + v;
+              const int64_t ox = xbase + (int64_t)(t0 + i) * D + 2 * (pl + v);
               const float av = to_f(a[o]);
               const cf z = {av * to_f(cs[o]), av * to_f(sn[o])};
-              const int64_t ox = xbase + (int64_t)(t0 + i) * D + 2 * v;
               H = cfma(z, H, {to_f(x[ox]), to_f(x[ox + 1])});
               Z = cmul(z, Z);
             }
           }
-          sZ[buf][warp][lane * V + v] = Z;
-          sH[buf][warp][lane * V + v] = H;
+          sZ[(buf * kWarps + warp) * W + pl + v] = Z;
+          sH[(buf * kWarps + warp) * W + pl + v] = H;
         }
         __syncthreads();
 #pragma unroll
         for (int v = 0; v < V; ++v) {
 #pragma unroll
-          for (int w = 0; w < kWarps; ++w) cur[v] = cfma(sZ[buf][w][lane * V + v], cur[v], sH[buf][w][lane * V + v]);
+          for (int w = 0; w < kWarps; ++w)
+            cur[v] = cfma(sZ[(buf * kWarps + w) * W + pl + v], cur[v], sH[(buf * kWarps + w) * W + pl + v]);
           if (warp == 0 && act) {
-            wsb[(int64_t)(j + 1) * 2 * W + 2 * v] = cur[v].r;
-            wsb[(int64_t)(j + 1) * 2 * W + 2 * v + 1] = cur[v].i;
+            wsb[(int64_t)(jj + 1) * 2 * W + 2 * v] = cur[v].r;
+            wsb[(int64_t)(jj + 1) * 2 * W + 2 * v + 1] = cur[v].i;
           }
         }
       }
       __syncthreads();
     }
 
-    for (int j = nsub - 1; j >= 0; --j, ++it) {
-      const int buf = it & 1;
-      const int s0 = g0 + j * TB;
-      const int sl = min(TB, g0 + gl - s0);
-      const int t0 = s0 + warp * TW;
-      const int tend = s0 + sl;
+    const int s = p % S;
+    mbar_wait(&bar[s], (p / S) & 1);
+    const int buf = it & 1;
+    ++it;
+    const int r0 = warp * TW;
+    const int t0 = tb0 + r0;
+    const int tend = tb0 + ntb;
 
-      float fa[TW][V], fc[TW][V], fs[TW][V];
-      cf fx[TW][V], fg[TW][V];
+    float fa[TW][V], fc[TW][V], fs[TW][V];
+    cf fx[TW][V], fg[TW][V];
+#pragma unroll
+    for (int i = 0; i < TW; ++i) {
+      const bool ok = t0 + i < tend;
+      const int row = s * TB + r0 + i;
+      const Vec<T, V> va = ld_vec<T, V>(sa + row * W + pl);
+      const Vec<T, V> vc = ld_vec<T, V>(sc + row * W + pl);
+      const Vec<T, V> vs = ld_vec<T, V>(ss + row * W + pl);
+      const Vec<T, 2 * V> vx = ld_vec<T, 2 * V>(sx + row * 2 * W + 2 * pl);
+      const Vec<float, 2 * V> vg = ld_vec<float, 2 * V>(sg + row * 2 * W + 2 * pl);
+#pragma unroll
+      for (int v = 0; v < V; ++v) {
+        fa[i][v] = ok ? to_f(va.v[v]) : 1.f;
+        fc[i][v] = ok ? to_f(vc.v[v]) : 1.f;
+        fs[i][v] = ok ? to_f(vs.v[v]) : 0.f;
+        fx[i][v] = ok ? cf{to_f(vx.v[2 * v]), to_f(vx.v[2 * v + 1])} : cf{0.f, 0.f};
+        fg[i][v] = ok ? cf{vg.v[2 * v], vg.v[2 * v + 1]} : cf{0.f, 0.f};
+      }
+    }
+    cf hs[V];
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      if (j > 0) {
+        hs[v] = act ? cf{wsb[(int64_t)j * 2 * W + 2 * v], wsb[(int64_t)j * 2 * W + 2 * v + 1]} : cf{0.f, 0.f};
+      } else if (tb0 > 0 && act) {
+        const float* ck = ckpt + (b * nseg + tb0 / seg - 1) * D + 2 * (p0 + pl + v);
+        hs[v] = {ck[0], ck[1]};
+      } else {
+        hs[v] = {0.f, 0.f};
+      }
+    }
+
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      cf Z = {1.f, 0.f}, H = {0.f, 0.f}, R = {1.f, 0.f}, G = {0.f, 0.f};
 #pragma unroll
       for (int i = 0; i < TW; ++i) {
-        const bool ok = act && (t0 + i < tend);
-        if (ok) {
-          const int64_t o = pbase + (int64_t)(t0 + i) * Dp;
-          const int64_t ox = xbase + (int64_t)(t0 + i) * D;
-          Vec<T, V> ra = ld_stream<T, V>(a + o);
-          Vec<T, V> rc = ld_stream<T, V>(cs + o);
-          Vec<T, V> rs = ld_stream<T, V>(sn + o);
-          Vec<T, 2 * V> rx = ld_stream<T, 2 * V>(x + ox);
-          Vec<float, 2 * V> rg = ld_stream<float, 2 * V>(gy + ox);
-#pragma unroll
-          for (int v = 0; v < V; ++v) {
-            fa[i][v] = to_f(ra.v[v]);
-            fc[i][v] = to_f(rc.v[v]);
-            fs[i][v] = to_f(rs.v[v]);
-            fx[i][v] = {to_f(rx.v[2 * v]), to_f(rx.v[2 * v + 1])};
-            fg[i][v] = {rg.v[2 * v], rg.v[2 * v + 1]};
-          }
-        } else {
-#pragma unroll
-          for (int v = 0; v < V; ++v) {
-            fa[i][v] = 1.f;
-            fc[i][v] = 1.f;
-            fs[i][v] = 0.f;
-            fx[i][v] = {0.f, 0.f};
-            fg[i][v] = {0.f, 0.f};
-          }
-        }
+        const cf z = {fa[i][v] * fc[i][v], fa[i][v] * fs[i][v]};
+        H = cfma(z, H, fx[i][v]);
+        Z = cmul(z, Z);
       }
-      cf hs[V];
+#pragma unroll
+      for (int i = TW - 1; i >= 0; --i) {  // c_out = conj(z) * (gy + c_in)
+        const cf zc = {fa[i][v] * fc[i][v], -fa[i][v] * fs[i][v]};
+        G = cmul(zc, {fg[i][v].r + G.r, fg[i][v].i + G.i});
+        R = cmul(zc, R);
+      }
+      sZ[(buf * kWarps + warp) * W + pl + v] = Z;
+      sH[(buf * kWarps + warp) * W + pl + v] = H;
+      sR[(buf * kWarps + warp) * W + pl + v] = R;
+      sG[(buf * kWarps + warp) * W + pl + v] = G;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && p + S - 1 < bm.nq) {
+      fence_proxy_async_smem();
+      issue(p + S - 1);
+    }
+
+    cf hp[TW][V], crin[V];
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      cf cur = hs[v];
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) {
+        if (w == warp) break;
+        cur = cfma(sZ[(buf * kWarps + w) * W + pl + v], cur, sH[(buf * kWarps + w) * W + pl + v]);
+      }
+#pragma unroll
+      for (int i = 0; i < TW; ++i) {
+        hp[i][v] = cur;
+        const float u = cur.r, w = cur.i, c = fc[i][v], sv = fs[i][v], av = fa[i][v];
+        cur = {av * (c * u - sv * w) + fx[i][v].r, av * (sv * u + c * w) + fx[i][v].i};
+      }
+      cf rc = cr[v];
+#pragma unroll
+      for (int w = kWarps - 1; w >= 0; --w) {
+        if (w == warp) crin[v] = rc;
+        rc = cfma(sR[(buf * kWarps + w) * W + pl + v], rc, sG[(buf * kWarps + w) * W + pl + v]);
+      }
+      cr[v] = rc;
+    }
+
+    // adjoint per step (rotlru.py:499-516)
+#pragma unroll
+    for (int i = TW - 1; i >= 0; --i) {
+      const int t = t0 + i;
+      float o_a[V], o_c[V], o_s[V], o_x[2 * V];
 #pragma unroll
       for (int v = 0; v < V; ++v) {
-        if (j == 0) {
-          hs[v] = hstart[v];
-        } else if (act) {
-          hs[v] = {wsb[(int64_t)j * 2 * W + 2 * v], wsb[(int64_t)j * 2 * W + 2 * v + 1]};
-        } else {
-          hs[v] = {0.f, 0.f};
-        }
+        const float aU = fg[i][v].r + crin[v].r;
+        const float aW = fg[i][v].i + crin[v].i;
+        const float up = hp[i][v].r, wp = hp[i][v].i;
+        const float c = fc[i][v], sv = fs[i][v], av = fa[i][v];
+        o_x[2 * v] = aU;
+        o_x[2 * v + 1] = aW;
+        const float ru = c * up - sv * wp;
+        const float rw = sv * up + c * wp;
+        o_a[v] = aU * ru + aW * rw;
+        o_c[v] = av * (aU * up + aW * wp);
+        o_s[v] = av * (aW * up - aU * wp);
+        crin[v] = {av * (c * aU + sv * aW), av * (-sv * aU + c * aW)};
       }
-
-#pragma unroll
-      for (int v = 0; v < V; ++v) {
-        cf Z = {1.f, 0.f}, H = {0.f, 0.f};
-#pragma unroll
-        for (int i = 0; i < TW; ++i) {
-          const cf z = {fa[i][v] * fc[i][v], fa[i][v] * fs[i][v]};
-          H = cfma(z, H, fx[i][v]);
-          Z = cmul(z, Z);
-        }
-        sZ[buf][warp][lane * V + v] = Z;
-        sH[buf][warp][lane * V + v] = H;
-        // reverse map: c_out = conj(z) * (gy + c_in)
-        cf R = {1.f, 0.f}, G = {0.f, 0.f};
-#pragma unroll
-        for (int i = TW - 1; i >= 0; --i) {
-          const cf zc = {fa[i][v] * fc[i][v], -fa[i][v] * fs[i][v]};
-          G = cmul(zc, {fg[i][v].r + G.r, fg[i][v].i + G.i});
-          R = cmul(zc, R);
-        }
-        sR[buf][warp][lane * V + v] = R;
-        sG[buf][warp][lane * V + v] = G;
-      }
-      __syncthreads();
-
-      cf hp[TW][V];
-      cf crin[V];
-#pragma unroll
-      for (int v = 0; v < V; ++v) {
-        cf cur = hs[v];
-#pragma unroll
-        for (int w = 0; w < kWarps; ++w) {
-          if (w == warp) break;
-          cur = cfma(sZ[buf][w][lane * V + v], cur, sH[buf][w][lane * V + v]);
-        }
-#pragma unroll
-        for (int i = 0; i < TW; ++i) {
-          hp[i][v] = cur;
-          const float u = cur.r, w = cur.i;
-          const float c = fc[i][v], s = fs[i][v], av = fa[i][v];
-          cur = {av * (c * u - s * w) + fx[i][v].r, av * (s * u + c * w) + fx[i][v].i};
-        }
-        cf rc = cr[v];
-#pragma unroll
-        for (int w = kWarps - 1; w >= 0; --w) {
-          if (w == warp) crin[v] = rc;
-          rc = cfma(sR[buf][w][lane * V + v], rc, sG[buf][w][lane * V + v]);
-        }
-        cr[v] = rc;
-      }
-
-      // adjoint per step (rotlru.py:499-516)
-#pragma unroll
-      for (int i = TW - 1; i >= 0; --i) {
-        const int t = t0 + i;
-        float o_a[V], o_c[V], o_s[V], o_x[2 * V];
-#pragma unroll
-        for (int v = 0; v < V; ++v) {
-          const float aU = fg[i][v].r + crin[v].r;
-          const float aW = fg[i][v].i + crin[v].i;
-          const float up = hp[i][v].r, wp = hp[i][v].i;
-          const float c = fc[i][v], s = fs[i][v], av = fa[i][v];
-          o_x[2 * v] = aU;
-          o_x[2 * v + 1] = aW;
-          const float ru = c * up - s * wp;
-          const float rw = s * up + c * wp;
-          o_a[v] = aU * ru + aW * rw;
-          o_c[v] = av * (aU * up + aW * wp);
-          o_s[v] = av * (aW * up - aU * wp);
-          crin[v] = {av * (c * aU + s * aW), av * (-s * aU + c * aW)};
-        }
-        if (act && t < tend) {
-          const int64_t o = pbase + (int64_t)t * Dp;
-          st_vec<T, V>(ga + o, o_a);
-          st_vec<T, V>(gcs + o, o_c);
-          st_vec<T, V>(gsn + o, o_s);
-          st_vec<T, 2 * V>(gx + xbase + (int64_t)t * D, o_x);
-        }
+      if (act && t < tend) {
+        const int64_t o = pbase + (int64_t)t * Dp + pl;
+        st_vec<T, V>(ga + o, o_a);
+        st_vec<T, V>(gcs + o, o_c);
+        st_vec<T, V>(gsn + o, o_s);
+        st_vec<T, 2 * V>(gx + xbase + (int64_t)t * D + 2 * pl, o_x);
       }
     }
   }
@@ -661,37 +808,59 @@ rotlru_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfinal
 // host launchers
 // ============================================================================
 
-// Forward tiles: V channels per lane (W = 32*V per CTA), TW steps per warp.
-constexpr int kRgFwdV = 2, kRgFwdTW = 16;
-constexpr int kRgBwdV = 2, kRgBwdTW = 8;
-constexpr int kRotFwdV = 2, kRotFwdTW = 8;
-constexpr int kRotBwdV = 1, kRotBwdTW = 8;
+// Tile shapes (channels per CTA W, steps per block TB, pipeline stages S),
+// chosen so three (forward) or two (backward) CTAs fit an SM and S-1 blocks
+// stay in flight per CTA.
+template <typename T> struct DiagCfg {
+  static constexpr int RgFW = 64, RgFTB = 64, RgFS = sizeof(T) == 4 ? 2 : 4;
+  static constexpr int RgBW = 64, RgBTB = 32, RgBS = sizeof(T) == 4 ? 2 : 3;
+  static constexpr int RotFW = 64, RotFTB = 32, RotFS = sizeof(T) == 4 ? 2 : 4;
+  static constexpr int RotBW = 64, RotBTB = 32, RotBS = 2;
+};
 
-static int seg_group(int seg, int TB) { return seg >= TB ? 1 : TB / seg; }
+template <typename K>
+static int set_smem(K kernel, size_t bytes) {
+  const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (e != cudaSuccess) return set_error(MR_E_LAUNCH, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  return MR_OK;
+}
+
+int diag_device_error(bool clear) { return read_device_error(clear); }
 
 size_t rglru_bwd_ws_bytes(int64_t batch, int64_t L, int64_t D, int64_t seg) {
-  constexpr int W = 32 * kRgBwdV, TB = kWarps * kRgBwdTW;
-  const int grp = seg_group((int)seg, TB);
-  const int64_t nsub = (grp * seg + TB - 1) / TB;
-  if (nsub <= 1) return 0;
-  return (size_t)batch * ((D + W - 1) / W) * nsub * W * sizeof(float);
+  using C = DiagCfg<__nv_bfloat16>;
+  static_assert(DiagCfg<float>::RgBTB == C::RgBTB && DiagCfg<float>::RgBW == C::RgBW, "");
+  const BlockMap bm((int)L, (int)seg, C::RgBTB);
+  if (bm.nsub <= 1) return 0;
+  return (size_t)batch * ((D + C::RgBW - 1) / C::RgBW) * bm.nsub * C::RgBW * sizeof(float);
 }
 
 size_t rotlru_bwd_ws_bytes(int64_t batch, int64_t L, int64_t Dp, int64_t seg) {
-  constexpr int W = 32 * kRotBwdV, TB = kWarps * kRotBwdTW;
-  const int grp = seg_group((int)seg, TB);
-  const int64_t nsub = (grp * seg + TB - 1) / TB;
-  if (nsub <= 1) return 0;
-  return (size_t)batch * ((Dp + W - 1) / W) * nsub * 2 * W * sizeof(float);
+  using C = DiagCfg<__nv_bfloat16>;
+  const BlockMap bm((int)L, (int)seg, C::RotBTB);
+  if (bm.nsub <= 1) return 0;
+  return (size_t)batch * ((Dp + C::RotBW - 1) / C::RotBW) * bm.nsub * 2 * C::RotBW * sizeof(float);
+}
+
+template <typename T>
+static int tmap_rows(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int W, int TB) {
+  return make_tmap_2d(m, base, TmapType<T>::v, sizeof(T), (uint64_t)cols, (uint64_t)rows,
+                      (uint64_t)cols * sizeof(T), (uint32_t)W, (uint32_t)TB);
 }
 
 template <typename T>
 int rglru_fwd_launch(const void* a, const void* x, int64_t batch, int64_t L, int64_t D, int64_t seg,
                      float* y, float* ckpt, cudaStream_t st) {
-  constexpr int W = 32 * kRgFwdV;
+  using C = DiagCfg<T>;
+  constexpr int W = C::RgFW, TB = C::RgFTB, S = C::RgFS;
+  constexpr size_t sm = RgFwdSmem<T, W, TB, S>::bytes;
+  CUtensorMap ma, mx;
+  if (int rc = tmap_rows<T>(&ma, a, batch * L, D, W, TB)) return rc;
+  if (int rc = tmap_rows<T>(&mx, x, batch * L, D, W, TB)) return rc;
+  auto k = rglru_fwd_kernel<T, W, TB, S>;
+  if (int rc = set_smem(k, sm)) return rc;
   dim3 grid((unsigned)((D + W - 1) / W), (unsigned)batch);
-  rglru_fwd_kernel<T, kRgFwdV, kRgFwdTW><<<grid, kThreads, 0, st>>>(
-      (const T*)a, (const T*)x, (int)L, D, (int)seg, y, ckpt);
+  k<<<grid, kThreads, sm, st>>>(ma, mx, (int)L, D, (int)seg, y, ckpt);
   return check_launch("rglru_fwd_kernel");
 }
 
@@ -699,21 +868,36 @@ template <typename T>
 int rglru_bwd_launch(const float* gy, const float* gf, const float* ckpt, const void* a, const void* x,
                      int64_t batch, int64_t L, int64_t D, int64_t seg, void* ga, void* gx, float* ws,
                      cudaStream_t st) {
-  constexpr int W = 32 * kRgBwdV, TB = kWarps * kRgBwdTW;
+  using C = DiagCfg<T>;
+  constexpr int W = C::RgBW, TB = C::RgBTB, S = C::RgBS;
+  constexpr size_t sm = RgBwdSmem<T, W, TB, S>::bytes;
+  CUtensorMap ma, mx, mg;
+  if (int rc = tmap_rows<T>(&ma, a, batch * L, D, W, TB)) return rc;
+  if (int rc = tmap_rows<T>(&mx, x, batch * L, D, W, TB)) return rc;
+  if (int rc = tmap_rows<float>(&mg, gy, batch * L, D, W, TB)) return rc;
+  auto k = rglru_bwd_kernel<T, W, TB, S>;
+  if (int rc = set_smem(k, sm)) return rc;
   dim3 grid((unsigned)((D + W - 1) / W), (unsigned)batch);
-  rglru_bwd_kernel<T, kRgBwdV, kRgBwdTW><<<grid, kThreads, 0, st>>>(
-      gy, gf, ckpt, (const T*)a, (const T*)x, (int)L, D, (int)seg, seg_group((int)seg, TB), (T*)ga,
-      (T*)gx, ws);
+  k<<<grid, kThreads, sm, st>>>(ma, mx, mg, gf, ckpt, (const T*)a, (const T*)x, (int)L, D, (int)seg,
+                                (T*)ga, (T*)gx, ws);
   return check_launch("rglru_bwd_kernel");
 }
 
 template <typename T>
 int rotlru_fwd_launch(const void* a, const void* cs, const void* sn, const void* x, int64_t batch,
                       int64_t L, int64_t Dp, int64_t seg, float* y, float* ckpt, cudaStream_t st) {
-  constexpr int W = 32 * kRotFwdV;
+  using C = DiagCfg<T>;
+  constexpr int W = C::RotFW, TB = C::RotFTB, S = C::RotFS;
+  constexpr size_t sm = RotFwdSmem<T, W, TB, S>::bytes;
+  CUtensorMap ma, mc, ms, mx;
+  if (int rc = tmap_rows<T>(&ma, a, batch * L, Dp, W, TB)) return rc;
+  if (int rc = tmap_rows<T>(&mc, cs, batch * L, Dp, W, TB)) return rc;
+  if (int rc = tmap_rows<T>(&ms, sn, batch * L, Dp, W, TB)) return rc;
+  if (int rc = tmap_rows<T>(&mx, x, batch * L, 2 * Dp, 2 * W, TB)) return rc;
+  auto k = rotlru_fwd_kernel<T, W, TB, S>;
+  if (int rc = set_smem(k, sm)) return rc;
   dim3 grid((unsigned)((Dp + W - 1) / W), (unsigned)batch);
-  rotlru_fwd_kernel<T, kRotFwdV, kRotFwdTW><<<grid, kThreads, 0, st>>>(
-      (const T*)a, (const T*)cs, (const T*)sn, (const T*)x, (int)L, Dp, (int)seg, y, ckpt);
+  k<<<grid, kThreads, sm, st>>>(ma, mc, ms, mx, (int)L, Dp, (int)seg, y, ckpt);
   return check_launch("rotlru_fwd_kernel");
 }
 
@@ -722,11 +906,20 @@ int rotlru_bwd_launch(const float* gy, const float* gf, const float* ckpt, const
                       const void* cs, const void* sn, const void* x, int64_t batch, int64_t L,
                       int64_t Dp, int64_t seg, void* ga, void* gcs, void* gsn, void* gx, float* ws,
                       cudaStream_t st) {
-  constexpr int W = 32 * kRotBwdV, TB = kWarps * kRotBwdTW;
+  using C = DiagCfg<T>;
+  constexpr int W = C::RotBW, TB = C::RotBTB, S = C::RotBS;
+  constexpr size_t sm = RotBwdSmem<T, W, TB, S>::bytes;
+  CUtensorMap ma, mc, ms, mx, mg;
+  if (int rc = tmap_rows<T>(&ma, a, batch * L, Dp, W, TB)) return rc;
+  if (int rc = tmap_rows<T>(&mc, cs, batch * L, Dp, W, TB)) return rc;
+  if (int rc = tmap_rows<T>(&ms, sn, batch * L, Dp, W, TB)) return rc;
+  if (int rc = tmap_rows<T>(&mx, x, batch * L, 2 * Dp, 2 * W, TB)) return rc;
+  if (int rc = tmap_rows<float>(&mg, gy, batch * L, 2 * Dp, 2 * W, TB)) return rc;
+  auto k = rotlru_bwd_kernel<T, W, TB, S>;
+  if (int rc = set_smem(k, sm)) return rc;
   dim3 grid((unsigned)((Dp + W - 1) / W), (unsigned)batch);
-  rotlru_bwd_kernel<T, kRotBwdV, kRotBwdTW><<<grid, kThreads, 0, st>>>(
-      gy, gf, ckpt, (const T*)a, (const T*)cs, (const T*)sn, (const T*)x, (int)L, Dp, (int)seg,
-      seg_group((int)seg, TB), (T*)ga, (T*)gcs, (T*)gsn, (T*)gx, ws);
+  k<<<grid, kThreads, sm, st>>>(ma, mc, ms, mx, mg, gf, ckpt, (const T*)a, (const T*)cs, (const T*)sn,
+                                (const T*)x, (int)L, Dp, (int)seg, (T*)ga, (T*)gcs, (T*)gsn, (T*)gx, ws);
   return check_launch("rotlru_bwd_kernel");
 }
 

@@ -45,6 +45,7 @@ size_t ssd_seq_bwd_ws_bytes(int64_t, int64_t, int64_t, int64_t, int64_t, int64_t
 size_t gla_seq_bwd_ws_bytes(int64_t, int64_t, int64_t, int64_t, int64_t);
 bool ssd_seq_supported(int64_t Dh, int64_t N);
 bool gla_seq_supported(int64_t Dh);
+int diag_device_error(bool clear);
 
 // ---- validation helpers -----------------------------------------------------
 static int check_seg(int64_t L, int64_t seg, int64_t lane_dim, const char* lane_name) {
@@ -118,6 +119,11 @@ int mr_abi_version(void) { return 1; }
 const char* mr_last_error(void) { return g_err; }
 
 uint64_t mr_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int mr_device_error_status(int clear) {
+  const int d = diag_device_error(clear != 0);
+  return d;
+}
 
 int mr_check_segment_shape(int64_t L, int64_t seg, int64_t lane_dim, const char* lane_name) {
   g_err[0] = 0;

@@ -1,0 +1,42 @@
+// TMA tensor maps (host) and tiled bulk-tensor copies (device).
+//
+// A tensor map describes a 2-D row-major view [rows, cols] of a global array
+// and the box (tile) one copy moves into shared memory. The driver's encoder
+// is fetched once through cudaGetDriverEntryPoint, so the library needs no
+// link-time dependency on libcuda. Loads only, never with cluster multicast.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace mr {
+
+// Encode a 2-D tiled map: inner (contiguous) extent `cols`, outer `rows`,
+// row pitch `row_bytes`, box [box_rows, box_cols], no swizzle unless given.
+// Out-of-bounds box elements read as zero. Returns MR_OK or an MR_E_* code.
+int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes,
+                 uint64_t cols, uint64_t rows, uint64_t row_bytes, uint32_t box_cols,
+                 uint32_t box_rows, CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE);
+
+template <typename T> struct TmapType;
+template <> struct TmapType<float> { static constexpr CUtensorMapDataType v = CU_TENSOR_MAP_DATA_TYPE_FLOAT32; };
+template <> struct TmapType<__nv_bfloat16> { static constexpr CUtensorMapDataType v = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16; };
+template <> struct TmapType<__half> { static constexpr CUtensorMapDataType v = CU_TENSOR_MAP_DATA_TYPE_FLOAT16; };
+
+// Tiled 2-D load of the box at (col x, row y) into shared memory, completing
+// on `bar`. x * element size must be a multiple of 16 bytes.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y),
+      "r"(static_cast<uint32_t>(__cvta_generic_to_shared(bar)))
+      : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+}  // namespace mr
