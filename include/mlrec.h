@@ -78,6 +78,13 @@ MR_API uint64_t mr_launch_count(void);
  * resets the word. For diagnostics and tests. */
 MR_API int mr_device_error_status(int clear);
 
+/* Diagnostic (no reference counterpart): one 128x128x128 bf16 tcgen05 tile
+ * per shared-memory operand form the chunked kernels use. A, Bk, Amn are
+ * [128,128] bf16, Bmn [128,64] bf16 (row-major); D1 = A*Bk^T [128,128],
+ * D2 = A*Bmn [128,64], D3 = Amn^T*Bmn [128,64], all f32. */
+MR_API int mr_selftest_umma(const void* A, const void* Bk, const void* Bmn, const void* Amn,
+                            float* D1, float* D2, float* D3, void* stream);
+
 /* Shape rule of the checkpoint/recompute pattern: seg > 0, L % seg == 0 and
  * lane_dim % 32 == 0 (mlx_recurrence/_chassis.py:92-115). lane_name names
  * lane_dim in the message. Host-only, launches nothing. */

@@ -46,6 +46,9 @@ size_t gla_seq_bwd_ws_bytes(int64_t, int64_t, int64_t, int64_t, int64_t);
 bool ssd_seq_supported(int64_t Dh, int64_t N);
 bool gla_seq_supported(int64_t Dh);
 int diag_device_error(bool clear);
+int selftest_device_error(bool clear);
+int umma_selftest_launch(const void*, const void*, const void*, const void*, float*, float*, float*,
+                         cudaStream_t);
 
 // ---- validation helpers -----------------------------------------------------
 static int check_seg(int64_t L, int64_t seg, int64_t lane_dim, const char* lane_name) {
@@ -121,8 +124,20 @@ const char* mr_last_error(void) { return g_err; }
 uint64_t mr_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 int mr_device_error_status(int clear) {
-  const int d = diag_device_error(clear != 0);
-  return d;
+  const int words[] = {diag_device_error(clear != 0), selftest_device_error(clear != 0)};
+  int r = 0;
+  for (int w : words) {
+    if (w < 0) return -1;
+    if (r == 0) r = w;
+  }
+  return r;
+}
+
+int mr_selftest_umma(const void* A, const void* Bk, const void* Bmn, const void* Amn, float* D1,
+                     float* D2, float* D3, void* stream) {
+  g_err[0] = 0;
+  MR_TRY(check_ptrs("mr_selftest_umma", {A, Bk, Bmn, Amn, D1, D2, D3}));
+  return umma_selftest_launch(A, Bk, Bmn, Amn, D1, D2, D3, (cudaStream_t)stream);
 }
 
 int mr_check_segment_shape(int64_t L, int64_t seg, int64_t lane_dim, const char* lane_name) {
