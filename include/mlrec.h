@@ -100,13 +100,23 @@ MR_API int mr_ssd_fwd(const void* u, const void* delta, const void* Bm, const vo
                int64_t batch, int64_t L, int64_t H, int64_t Dh, int64_t N, int64_t seg,
                float* y, float* h_ckpt, void* stream);
 
+/* Checkpoint spacing to pass to mr_ssd_fwd/mr_ssd_bwd for the fastest path
+ * when the caller only needs the segment rule L % seg == 0 and the final
+ * state: the tensor-core chunk length (128) when seg divides it and the
+ * chunked path applies (bf16/fp16, Dh = 64, N = 128, a_stride_n == 0,
+ * L % 128 == 0), else seg unchanged. Host-only. */
+MR_API int64_t mr_ssd_preferred_seg(int dtype, int64_t L, int64_t Dh, int64_t N, int64_t seg,
+                                    int64_t a_stride_n);
+
 /* Bytes of device workspace mr_ssd_bwd needs for these arguments. */
 MR_API size_t mr_ssd_bwd_workspace_bytes(int dtype, int64_t batch, int64_t L, int64_t H, int64_t Dh,
                                   int64_t N, int64_t seg, int64_t a_stride_n);
 
 /* grad_y [B,L,H,Dh] f32; grad_final [B,H,Dh,N] f32 or NULL;
  * grad_u/grad_delta/grad_B/grad_C in `dtype`; grad_A [H,N] f32 (summed over
- * the batch, ssd.py:305). */
+ * the batch, ssd.py:305). With a_stride_n == 0 (one rate per head) row h of
+ * grad_A holds d loss / d A_h divided evenly over its N entries, so that its
+ * sum over n is the derivative for the per-head rate. */
 MR_API int mr_ssd_bwd(const float* grad_y, const float* grad_final, const float* h_ckpt,
                const void* u, const void* delta, const void* Bm, const void* Cm,
                const float* A_neg, int64_t a_stride_h, int64_t a_stride_n, int dtype,

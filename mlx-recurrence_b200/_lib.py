@@ -42,6 +42,7 @@ SIGNATURES = {
     "mr_check_segment_shape": (_int, [_i64, _i64, _i64, ctypes.c_char_p]),
     "mr_ssd_fwd": (_int, [_p, _p, _p, _p, _p, _i64, _i64, _int, _i64, _i64, _i64, _i64, _i64, _i64,
                           _p, _p, _p]),
+    "mr_ssd_preferred_seg": (_i64, [_int, _i64, _i64, _i64, _i64, _i64]),
     "mr_ssd_bwd_workspace_bytes": (_sz, [_int, _i64, _i64, _i64, _i64, _i64, _i64, _i64]),
     "mr_ssd_bwd": (_int, [_p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _int, _i64, _i64, _i64, _i64,
                           _i64, _i64, _p, _p, _p, _p, _p, _p, _sz, _p]),

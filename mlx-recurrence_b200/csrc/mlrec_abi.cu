@@ -47,6 +47,13 @@ bool ssd_seq_supported(int64_t Dh, int64_t N);
 bool gla_seq_supported(int64_t Dh);
 int diag_device_error(bool clear);
 int selftest_device_error(bool clear);
+int ssdc_device_error(bool clear);
+bool ssd_chunk_supported(int dtype, int64_t L, int64_t Dh, int64_t N, int64_t seg, int64_t a_stride_n);
+bool ssd_chunk_bwd_supported(int dtype, int64_t L, int64_t Dh, int64_t N, int64_t seg, int64_t a_stride_n);
+int ssd_chunk_len();
+size_t ssd_chunk_bwd_ws_bytes(int64_t batch, int64_t H);
+template <typename T> int ssd_chunk_bwd_launch(const float*, const float*, const float*, const void*, const void*, const void*, const void*, const float*, int64_t, int64_t, int64_t, int64_t, int64_t, void*, void*, void*, void*, float*, float*, cudaStream_t);
+template <typename T> int ssd_chunk_fwd_launch(const void*, const void*, const void*, const void*, const float*, int64_t, int64_t, int64_t, int64_t, int64_t, float*, float*, cudaStream_t);
 int umma_selftest_launch(const void*, const void*, const void*, const void*, float*, float*, float*,
                          cudaStream_t);
 
@@ -124,7 +131,8 @@ const char* mr_last_error(void) { return g_err; }
 uint64_t mr_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 int mr_device_error_status(int clear) {
-  const int words[] = {diag_device_error(clear != 0), selftest_device_error(clear != 0)};
+  const int words[] = {diag_device_error(clear != 0), selftest_device_error(clear != 0),
+                       ssdc_device_error(clear != 0)};
   int r = 0;
   for (int w : words) {
     if (w < 0) return -1;
@@ -247,16 +255,27 @@ int mr_ssd_fwd(const void* u, const void* delta, const void* Bm, const void* Cm,
   MR_TRY(check_ptrs("mr_ssd_fwd", {u, delta, Bm, Cm, y, h_ckpt}));
   if (A_neg == nullptr) return set_error(MR_E_ALIGN, "mr_ssd_fwd: A_neg is NULL");
   cudaStream_t st = (cudaStream_t)stream;
+  if (ssd_chunk_supported(dtype, L, Dh, N, seg, a_stride_n)) {
+    if (dtype == MR_BF16)
+      return ssd_chunk_fwd_launch<__nv_bfloat16>(u, delta, Bm, Cm, A_neg, a_stride_h, batch, L, H, seg, y,
+                                                 h_ckpt, st);
+    return ssd_chunk_fwd_launch<__half>(u, delta, Bm, Cm, A_neg, a_stride_h, batch, L, H, seg, y, h_ckpt, st);
+  }
   MR_DTYPE_SWITCH(dtype, ssd_seq_fwd_launch<T>(u, delta, Bm, Cm, A_neg, a_stride_h, a_stride_n,
                                                batch, L, H, Dh, N, seg, y, h_ckpt, st));
 }
 
 size_t mr_ssd_bwd_workspace_bytes(int dtype, int64_t batch, int64_t L, int64_t H, int64_t Dh,
                                   int64_t N, int64_t seg, int64_t a_stride_n) {
-  (void)dtype;
-  (void)a_stride_n;
   if (batch <= 0 || L <= 0 || H <= 0 || Dh <= 0 || N <= 0 || seg <= 0) return 0;
+  if (ssd_chunk_bwd_supported(dtype, L, Dh, N, seg, a_stride_n)) return ssd_chunk_bwd_ws_bytes(batch, H);
   return ssd_seq_bwd_ws_bytes(batch, L, H, Dh, N, seg);
+}
+
+int64_t mr_ssd_preferred_seg(int dtype, int64_t L, int64_t Dh, int64_t N, int64_t seg, int64_t a_stride_n) {
+  const int64_t q = ssd_chunk_len();
+  if (seg > 0 && L % q == 0 && q % seg == 0 && ssd_chunk_bwd_supported(dtype, L, Dh, N, q, a_stride_n)) return q;
+  return seg;
 }
 
 int mr_ssd_bwd(const float* grad_y, const float* grad_final, const float* h_ckpt, const void* u,
@@ -271,12 +290,21 @@ int mr_ssd_bwd(const float* grad_y, const float* grad_final, const float* h_ckpt
   MR_TRY(check_opt_ptr("mr_ssd_bwd", grad_final));
   if (A_neg == nullptr || grad_A == nullptr)
     return set_error(MR_E_ALIGN, "mr_ssd_bwd: A_neg / grad_A is NULL");
-  const size_t need = ssd_seq_bwd_ws_bytes(batch, L, H, Dh, N, seg);
+  const bool chunk = ssd_chunk_bwd_supported(dtype, L, Dh, N, seg, a_stride_n);
+  const size_t need = chunk ? ssd_chunk_bwd_ws_bytes(batch, H) : ssd_seq_bwd_ws_bytes(batch, L, H, Dh, N, seg);
   if (workspace == nullptr || workspace_bytes < need)
     return set_error(MR_E_WORKSPACE, "mr_ssd_bwd: workspace of %zu bytes required, got %zu", need,
                      workspace_bytes);
   MR_TRY(check_opt_ptr("mr_ssd_bwd", workspace));
   cudaStream_t st = (cudaStream_t)stream;
+  if (chunk) {
+    if (dtype == MR_BF16)
+      return ssd_chunk_bwd_launch<__nv_bfloat16>(grad_y, grad_final, h_ckpt, u, delta, Bm, Cm, A_neg, a_stride_h,
+                                                 batch, L, H, seg, grad_u, grad_delta, grad_B, grad_C, grad_A,
+                                                 (float*)workspace, st);
+    return ssd_chunk_bwd_launch<__half>(grad_y, grad_final, h_ckpt, u, delta, Bm, Cm, A_neg, a_stride_h, batch, L,
+                                        H, seg, grad_u, grad_delta, grad_B, grad_C, grad_A, (float*)workspace, st);
+  }
   MR_DTYPE_SWITCH(dtype, ssd_seq_bwd_launch<T>(grad_y, grad_final, h_ckpt, u, delta, Bm, Cm, A_neg,
                                                a_stride_h, a_stride_n, batch, L, H, Dh, N, seg,
                                                grad_u, grad_delta, grad_B, grad_C, grad_A,

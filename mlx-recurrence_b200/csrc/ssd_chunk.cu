@@ -1,0 +1,928 @@
+// SSD (Mamba-2 head-wise selective scan) in chunked form on the tcgen05
+// tensor cores: the bf16/fp16 path for one decay rate per head.
+//
+// Reference: mlx_recurrence/ssd.py:54-135 (forward), ssd.py:382-394 (the
+// per-step definition). With a_t = exp(delta_t A_h), a chunk of Q = 128 steps
+// starting from state h0 [Dh, N] is, for Lam_t = sum_{r<=t} delta_r A_h
+// (cumulative within the chunk):
+//   y_t   = sum_{s<=t} exp(Lam_t - Lam_s) delta_s (C_t . B_s) u_s + exp(Lam_t) C_t h0^T
+//   h_end = exp(Lam_last) h0 + sum_s exp(Lam_last - Lam_s) delta_s u_s B_s^T
+// which is four tensor-core products per chunk (TMEM accumulators, f32):
+//   S    = C B^T            [t, s]   M=128 N=128 K=N     (A, B K-major)
+//   Y2   = C h0^T           [t, d]   M=128 N=64  K=N     (B = h0^T, MN-major)
+//   dH^T = B^T U~           [n, d]   M=128 N=64  K=Q     (A = B^T MN-major, B = U~ MN-major)
+//   Y1   = G U              [t, d]   M=128 N=64  K=Q     (G from S, K-major; U MN-major)
+// with U~_s = exp(Lam_last - Lam_s) delta_s u_s and
+// G[t, s] = S[t, s] exp(Lam_t - Lam_s) delta_s for s <= t (else 0).
+// Then y = Y1 + exp(Lam_t) Y2 and h <- exp(Lam_last) h + dH. Every exponent
+// is <= 0 (Lam decreases), so nothing overflows.
+//
+// One CTA owns one (batch, head) and walks its L/Q chunks in order. u, B and C
+// of the next chunk stream in by TMA (128B-swizzled boxes [128 steps x 64])
+// while the current chunk computes. The running state h stays in registers
+// in float32 (thread = state row n, 32 channels); its bf16 copy in shared
+// memory is the operand of the next chunk's Y2 product, and it is written to
+// h_ckpt in float32 at segment ends (seg a multiple of Q).
+#include "common.cuh"
+#include "tma.cuh"
+#include "tmap.cuh"
+#include "umma.cuh"
+
+namespace mr {
+
+namespace ssdc {
+constexpr int Q = 128;                 // chunk length (MMA M for t-rows)
+constexpr int DH = 64;                 // head dim (one 128-byte swizzle row)
+constexpr int NS = 128;                // state size N
+constexpr uint32_t TILE = 16384;       // [128 rows x 64 elements] 2-byte tile
+constexpr uint32_t STAGE = TILE * 5;   // u, B lo/hi, C lo/hi
+// small arrays (Lam, delta, warp sums, barriers, TMEM slot) first, then the
+// 1024-byte-aligned tiles
+constexpr size_t SMALL = (2 * Q + 8) * 4 + 6 * 8 + 16;
+constexpr size_t SMEM = SMALL + 1023 + 2 * STAGE + 2 * TILE + TILE + TILE;
+}  // namespace ssdc
+
+template <typename T> struct MmaFmt;
+template <> struct MmaFmt<__nv_bfloat16> { static constexpr int v = 1; };
+template <> struct MmaFmt<__half> { static constexpr int v = 0; };
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+  const T x = from_f<T>(a), y = from_f<T>(b);
+  return (uint32_t)(*reinterpret_cast<const uint16_t*>(&x)) |
+         ((uint32_t)(*reinterpret_cast<const uint16_t*>(&y)) << 16);
+}
+
+template <typename T>
+__device__ __forceinline__ void unpack8(const int4& v, float (&f)[8]) {
+  const T* p = reinterpret_cast<const T*>(&v);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) f[i] = to_f(p[i]);
+}
+
+template <typename T>
+__device__ __forceinline__ int4 pack8(const float* f) {
+  int4 r;
+  r.x = (int)pack2<T>(f[0], f[1]);
+  r.y = (int)pack2<T>(f[2], f[3]);
+  r.z = (int)pack2<T>(f[4], f[5]);
+  r.w = (int)pack2<T>(f[6], f[7]);
+  return r;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256, 1)
+ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_constant__ CUtensorMap tm_B,
+                     const __grid_constant__ CUtensorMap tm_C, const T* __restrict__ delta,
+                     const float* __restrict__ A, int64_t ash, int L, int H, int seg,
+                     float* __restrict__ y, float* __restrict__ ckpt) {
+  using namespace ssdc;
+  extern __shared__ unsigned char smem_raw[];
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem_raw);  // bc[2], u[2], mma
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 6);
+  float* sLam = reinterpret_cast<float*>(tslot + 4);  // [Q]
+  float* sDel = sLam + Q;                             // [Q]
+  float* sWarp = sDel + Q;                            // [8]
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sWarp + 8) + 1023) & ~uintptr_t(1023));
+  uint8_t* stg0 = sm;            // stage s: u | B lo | B hi | C lo | C hi
+  uint8_t* sG = sm + 2 * STAGE;  // G, two K-major tiles (s 0-63, 64-127)
+  uint8_t* sUt = sG + 2 * TILE;  // U~, MN-major [s][d]
+  uint8_t* sHt = sUt + TILE;     // h^T bf16, MN-major [n][d]
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int bh = blockIdx.x;
+  const int b = bh / H, h = bh % H;
+  const float Ah = A[(int64_t)h * ash];
+  const int nck = L / Q;
+  const int nseg = L / seg;
+  const int64_t row0 = (int64_t)b * L;
+  constexpr int fmt = MmaFmt<T>::v;
+  constexpr uint32_t idS = umma::idesc_f16(128, 128, fmt, 0, 0);
+  constexpr uint32_t idY = umma::idesc_f16(128, 64, fmt, 0, 1);
+  constexpr uint32_t idH = umma::idesc_f16(128, 64, fmt, 1, 1);
+
+  if (tid == 0) {
+    for (int i = 0; i < 5; ++i) mbar_init(&bar[i], 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    umma::tmem_alloc(tslot, 512);
+    umma::tmem_relinquish();
+  }
+  // h0 = 0 for the first chunk's Y2 product
+  for (int i = tid; i < (int)(TILE / 16); i += 256) reinterpret_cast<int4*>(sHt)[i] = make_int4(0, 0, 0, 0);
+  fence_proxy_async_smem();
+  __syncthreads();
+  umma::fence_after_sync();
+  const uint32_t tbase = *tslot;
+
+  // B and C of a chunk are free once its S/dH/Y2 products complete; u once Y1 completes.
+  auto issue_bc = [&](int c) {
+    const int st = c & 1;
+    uint8_t* s = stg0 + st * STAGE;
+    const int z = (int)(row0 + (int64_t)c * Q);
+    mbar_arrive_expect_tx(&bar[st], 4 * TILE);
+    tma_load_3d(s + TILE, &tm_B, 0, h, z, &bar[st]);
+    tma_load_3d(s + 2 * TILE, &tm_B, 64, h, z, &bar[st]);
+    tma_load_3d(s + 3 * TILE, &tm_C, 0, h, z, &bar[st]);
+    tma_load_3d(s + 4 * TILE, &tm_C, 64, h, z, &bar[st]);
+  };
+  auto issue_u = [&](int c) {
+    const int st = c & 1;
+    mbar_arrive_expect_tx(&bar[2 + st], TILE);
+    tma_load_3d(stg0 + st * STAGE, &tm_u, 0, h, (int)(row0 + (int64_t)c * Q), &bar[2 + st]);
+  };
+  if (tid == 0) {
+    for (int c = 0; c < 2 && c < nck; ++c) {
+      issue_u(c);
+      issue_bc(c);
+    }
+  }
+
+  const int q4 = warp & 3, jh = warp >> 2;  // TMEM lane quarter, column half
+  const int trow = 32 * q4 + lane;          // row t (or n) this thread owns
+  const uint32_t tl = tbase + ((uint32_t)(32 * q4) << 16);
+  float hreg[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) hreg[i] = 0.f;
+  float dnext = (tid < Q) ? to_f(delta[(row0 + tid) * H + h]) : 0.f;
+  uint32_t mph = 0;
+
+  // Prologue of chunk c: Lam (cumulative delta*A), delta, and U~ into shared memory.
+  auto prologue = [&](int c) {
+    constexpr int p = 0;
+    const float dcur = dnext;
+    if (tid < Q && c + 1 < nck) dnext = to_f(delta[(row0 + (int64_t)(c + 1) * Q + tid) * H + h]);
+    float lam = 0.f;
+    if (tid < Q) {
+      lam = dcur * Ah;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float n = __shfl_up_sync(0xffffffffu, lam, o);
+        if (lane >= o) lam += n;
+      }
+      if (lane == 31) sWarp[warp] = lam;
+      sDel[p * Q + tid] = dcur;
+    }
+    __syncthreads();
+    if (tid < Q) {
+      float off = 0.f;
+      for (int w = 0; w < warp; ++w) off += sWarp[w];
+      sLam[p * Q + tid] = lam + off;
+    }
+    __syncthreads();
+    const float lam_last = sLam[p * Q + Q - 1];
+    const int st = c & 1;
+    mbar_wait(&bar[2 + st], (uint32_t)(c >> 1) & 1u);
+    const uint8_t* sU = stg0 + st * STAGE;
+    const int s = tid >> 1, hf = tid & 1;
+    const float w = __expf(lam_last - sLam[p * Q + s]) * sDel[p * Q + s];
+#pragma unroll
+    for (int cc = 0; cc < 4; ++cc) {
+      const uint32_t off = umma::sw128_off(s, (hf * 4 + cc) * 8);
+      float f[8];
+      unpack8<T>(*reinterpret_cast<const int4*>(sU + off), f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) f[i] *= w;
+      *reinterpret_cast<int4*>(sUt + off) = pack8<T>(f);
+    }
+    fence_proxy_async_smem();
+  };
+
+  prologue(0);
+  for (int c = 0; c < nck; ++c) {
+    const int st = c & 1, p = 0;
+    uint8_t* sU = stg0 + st * STAGE;
+    uint8_t* sB = sU + TILE;
+    uint8_t* sC = sU + 3 * TILE;
+    const float* lamc = sLam + p * Q;
+    const float* delc = sDel + p * Q;
+    __syncthreads();  // U~, Lam of chunk c and h^T of chunk c-1 are in shared memory
+
+    // ---- S = C B^T, Y2 = C h0^T, dH^T = B^T U~
+    if (tid == 0) {
+      mbar_wait(&bar[st], (uint32_t)(c >> 1) & 1u);
+      umma::fence_after_sync();
+      const uint32_t aC = smem_u32(sC), aB = smem_u32(sB), aH = smem_u32(sHt), aUt = smem_u32(sUt);
+#pragma unroll
+      for (int k = 0; k < NS / 16; ++k) {
+        const uint32_t ko = (k >> 2) * TILE + (k & 3) * 32;
+        umma::mma_f16(tbase + 0, umma::sdesc_k(aC + ko), umma::sdesc_k(aB + ko), idS, k > 0);
+      }
+#pragma unroll
+      for (int k = 0; k < NS / 16; ++k) {
+        const uint32_t ko = (k >> 2) * TILE + (k & 3) * 32;
+        umma::mma_f16(tbase + 128, umma::sdesc_k(aC + ko), umma::sdesc_mn(aH + k * 2048, TILE), idY, k > 0);
+      }
+#pragma unroll
+      for (int k = 0; k < Q / 16; ++k)
+        umma::mma_f16(tbase + 192, umma::sdesc_mn(aB + k * 2048, TILE), umma::sdesc_mn(aUt + k * 2048, TILE),
+                      idH, k > 0);
+      umma::commit(&bar[4]);
+    }
+    mbar_wait(&bar[4], mph & 1u);
+    ++mph;
+    umma::fence_after_sync();
+
+    // ---- G[t, s] = S[t, s] exp(Lam_t - Lam_s) delta_s for s <= t
+    {
+      const int t = trow;
+      uint8_t* g = sG + jh * TILE;
+      if (64 * jh > t) {
+#pragma unroll
+        for (int ch = 0; ch < 8; ++ch)
+          *reinterpret_cast<int4*>(g + umma::sw128_off(t, ch * 8)) = make_int4(0, 0, 0, 0);
+      } else {
+        float v[64];
+#pragma unroll
+        for (int cb = 0; cb < 4; ++cb) umma::tmem_ld16(tl + 64 * jh + 16 * cb, *reinterpret_cast<float(*)[16]>(v + 16 * cb));
+        umma::tmem_wait_ld();
+        const float lt = lamc[t];
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          const int s = 64 * jh + i;
+          v[i] = (s <= t) ? v[i] * __expf(lt - lamc[s]) * delc[s] : 0.f;
+        }
+#pragma unroll
+        for (int ch = 0; ch < 8; ++ch) *reinterpret_cast<int4*>(g + umma::sw128_off(t, 8 * ch)) = pack8<T>(v + 8 * ch);
+      }
+      fence_proxy_async_smem();
+    }
+    umma::fence_before_sync();
+    __syncthreads();
+
+    // ---- Y1 = G U; B, C of this stage are free: stream chunk c+2's
+    if (tid == 0) {
+      umma::fence_after_sync();
+      const uint32_t aG = smem_u32(sG), aU = smem_u32(sU);
+#pragma unroll
+      for (int k = 0; k < Q / 16; ++k) {
+        const uint32_t ko = (k >> 2) * TILE + (k & 3) * 32;
+        umma::mma_f16(tbase + 256, umma::sdesc_k(aG + ko), umma::sdesc_mn(aU + k * 2048, TILE), idY, k > 0);
+      }
+      umma::commit(&bar[4]);
+      if (c + 2 < nck) issue_bc(c + 2);
+    }
+
+    // ---- state: h <- exp(Lam_last) h + dH (thread: row n = trow, 32 channels)
+    {
+      const int n = trow;
+      const float dec = __expf(lamc[Q - 1]);
+      float v[32];
+      umma::tmem_ld16(tl + 192 + 32 * jh, *reinterpret_cast<float(*)[16]>(v));
+      umma::tmem_ld16(tl + 192 + 32 * jh + 16, *reinterpret_cast<float(*)[16]>(v + 16));
+      umma::tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) hreg[i] = dec * hreg[i] + v[i];
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc)
+        *reinterpret_cast<int4*>(sHt + umma::sw128_off(n, 32 * jh + 8 * cc)) = pack8<T>(hreg + 8 * cc);
+      fence_proxy_async_smem();
+      if (((c + 1) * Q) % seg == 0) {
+        const int si = (c + 1) * Q / seg - 1;
+        float* dst = ckpt + (((int64_t)b * nseg + si) * H + h) * (int64_t)(NS * DH) + (int64_t)n * DH + 32 * jh;
+#pragma unroll
+        for (int i = 0; i < 32; i += 4)
+          __stcs(reinterpret_cast<float4*>(dst + i), make_float4(hreg[i], hreg[i + 1], hreg[i + 2], hreg[i + 3]));
+      }
+    }
+
+    // ---- next chunk's prologue overlaps the Y1 product (it rewrites Lam)
+    const float e_t = __expf(lamc[trow]);
+    __syncthreads();
+    if (c + 1 < nck) prologue(c + 1);
+
+    mbar_wait(&bar[4], mph & 1u);
+    ++mph;
+    umma::fence_after_sync();
+
+    // ---- y = Y1 + exp(Lam_t) Y2
+    {
+      const int t = trow;
+      const float e = e_t;
+      float* yr = y + ((row0 + (int64_t)c * Q + t) * H + h) * DH + 32 * jh;
+      float a[32], bb[32];
+      umma::tmem_ld16(tl + 256 + 32 * jh, *reinterpret_cast<float(*)[16]>(a));
+      umma::tmem_ld16(tl + 256 + 32 * jh + 16, *reinterpret_cast<float(*)[16]>(a + 16));
+      umma::tmem_ld16(tl + 128 + 32 * jh, *reinterpret_cast<float(*)[16]>(bb));
+      umma::tmem_ld16(tl + 128 + 32 * jh + 16, *reinterpret_cast<float(*)[16]>(bb + 16));
+      umma::tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 32; i += 4)
+        __stcs(reinterpret_cast<float4*>(yr + i), make_float4(a[i] + e * bb[i], a[i + 1] + e * bb[i + 1],
+                                                             a[i + 2] + e * bb[i + 2], a[i + 3] + e * bb[i + 3]));
+    }
+    umma::fence_before_sync();
+    // u of this stage is free once Y1 completed (waited above)
+    if (tid == 0 && c + 2 < nck) issue_u(c + 2);
+  }
+  __syncthreads();
+  if (warp == 0) umma::tmem_dealloc(tbase, 512);
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+
+// The tensor-core path: bf16/fp16 inputs, Dh = 64, N = 128, one decay rate
+// per head, L a multiple of the chunk. The forward writes checkpoints at any
+// multiple of the chunk; the backward needs one at every chunk start.
+bool ssd_chunk_supported(int dtype, int64_t L, int64_t Dh, int64_t N, int64_t seg, int64_t a_stride_n) {
+  return (dtype == MR_BF16 || dtype == MR_F16) && Dh == ssdc::DH && N == ssdc::NS && a_stride_n == 0 &&
+         L % ssdc::Q == 0 && seg % ssdc::Q == 0 && L <= (int64_t)INT32_MAX / 2;
+}
+bool ssd_chunk_bwd_supported(int dtype, int64_t L, int64_t Dh, int64_t N, int64_t seg, int64_t a_stride_n) {
+  return ssd_chunk_supported(dtype, L, Dh, N, seg, a_stride_n) && seg == ssdc::Q;
+}
+int ssd_chunk_len() { return ssdc::Q; }
+
+template <typename T>
+static int ssd_tmaps(const void* u, const void* Bm, const void* Cm, int64_t batch, int64_t L, int64_t H,
+                     CUtensorMap* mu, CUtensorMap* mB, CUtensorMap* mC) {
+  using namespace ssdc;
+  const auto dt = TmapType<T>::v;
+  const auto SW = CU_TENSOR_MAP_SWIZZLE_128B;
+  const uint64_t rows = (uint64_t)batch * L;
+  if (int rc = make_tmap_3d(mu, u, dt, 2, DH, H, rows, DH * 2, (uint64_t)H * DH * 2, 64, 1, Q, SW)) return rc;
+  if (int rc = make_tmap_3d(mB, Bm, dt, 2, NS, H, rows, NS * 2, (uint64_t)H * NS * 2, 64, 1, Q, SW)) return rc;
+  if (int rc = make_tmap_3d(mC, Cm, dt, 2, NS, H, rows, NS * 2, (uint64_t)H * NS * 2, 64, 1, Q, SW)) return rc;
+  return MR_OK;
+}
+
+template <typename T>
+int ssd_chunk_fwd_launch(const void* u, const void* delta, const void* Bm, const void* Cm, const float* A,
+                         int64_t ash, int64_t batch, int64_t L, int64_t H, int64_t seg, float* y,
+                         float* ckpt, cudaStream_t st) {
+  CUtensorMap mu, mB, mC;
+  if (int rc = ssd_tmaps<T>(u, Bm, Cm, batch, L, H, &mu, &mB, &mC)) return rc;
+  auto k = ssd_chunk_fwd_kernel<T>;
+  const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssdc::SMEM);
+  if (e != cudaSuccess) return set_error(MR_E_LAUNCH, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  k<<<(unsigned)(batch * H), 256, ssdc::SMEM, st>>>(mu, mB, mC, (const T*)delta, A, ash, (int)L, (int)H, (int)seg,
+                                                    y, ckpt);
+  return check_launch("ssd_chunk_fwd_kernel");
+}
+
+template int ssd_chunk_fwd_launch<__nv_bfloat16>(const void*, const void*, const void*, const void*,
+                                                 const float*, int64_t, int64_t, int64_t, int64_t, int64_t,
+                                                 float*, float*, cudaStream_t);
+template int ssd_chunk_fwd_launch<__half>(const void*, const void*, const void*, const void*, const float*,
+                                          int64_t, int64_t, int64_t, int64_t, int64_t, float*, float*,
+                                          cudaStream_t);
+
+int ssdc_device_error(bool clear) { return read_device_error(clear); }
+
+// ===========================================================================
+// Backward (reference: ssd.py:142-307, the VJP of ssd.py:382-394)
+// ===========================================================================
+//
+// Chunks are walked newest -> oldest. Psi is the adjoint flowing into the end
+// of the current chunk from later chunks (initially the final-state
+// cotangent), h0 the chunk's starting state (the previous checkpoint). With
+// E[s,t] = exp(Lam_s - Lam_t) for s >= t (else 0), w_t = exp(Lam_last - Lam_t)
+// delta_t and D_t = sum_{r<=t} delta_r (both within the chunk):
+//   S = C B^T, P = gy u^T                       [s, t]
+//   G' = S (.) E,  H1 = P (.) E (.) delta_t,     Z = S (.) H1
+//   r     = G'^T gy + diag(exp(Lam_last - Lam_t)) B Psi^T       [t, d]
+//   gu    = diag(delta) r
+//   gB    = H1^T C + diag(w) u Psi                               [t, n]
+//   gC    = H1 B + diag(exp(Lam_s)) gy h0                        [s, n]
+//   Psi  <- exp(Lam_last) Psi + (diag(exp(Lam)) gy)^T C          [d, n]
+//   dLam_t = rowsum_t Z - colsum_t Z + exp(Lam_t) gy_t.(C_t h0^T)
+//            - w_t u_t.(B_t Psi^T) + [t = last] <Psi, h_end>
+//   gdelta_t = A * sum_{t' >= t} dLam_t' + u_t . r_t
+//   dL/dA_h += sum_t dLam_t D_t
+// The tensor-core products per chunk, in three batches (TMEM columns):
+//   1: S [0,128)  P [128,256)  Y2 = C h0^T [256,320)  R2 = B Psi^T [320,384)
+//      dPsi^T = C^T (e^Lam gy) [384,448)
+//   2: S^T = B C^T [0,128)  P^T = u gy^T [128,256)  R1 = G'^T gy [256,320)
+//   3: gB1 = H1^T C [0,128)  gC1 = H1 B [128,256)  gB2 = u Psi [256,384)  gC2 = gy h0 [384,512)
+// gy enters P, P^T and R1 as bf16/fp16 hi + lo parts (two accumulated products).
+// colsum Z comes from the transposed products (thread t owns row t of S^T, P^T).
+
+namespace ssdb {
+constexpr int Q = 128, DH = 64, NS = 128;
+constexpr uint32_t TILE = 16384;
+// tiles: U, B lo/hi, C lo/hi, GY, GYt, PSI, H0, GP lo/hi, HH lo/hi
+constexpr int NTILE = 13;
+constexpr size_t SMALL = (5 * Q + 6 * Q + 64) * 4 + 4 * 8 + 16;
+constexpr size_t SMEM = SMALL + 1023 + NTILE * TILE;
+}  // namespace ssdb
+
+template <typename T>
+__global__ void __launch_bounds__(256, 1)
+ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_constant__ CUtensorMap tm_B,
+                     const __grid_constant__ CUtensorMap tm_C, const float* __restrict__ gy,
+                     const float* __restrict__ gfinal, const float* __restrict__ ckpt,
+                     const T* __restrict__ delta, const float* __restrict__ A, int64_t ash, int L, int H,
+                     int seg, T* __restrict__ gu, T* __restrict__ gdelta, T* __restrict__ gB,
+                     T* __restrict__ gC, float* __restrict__ gA_part) {
+  using namespace ssdb;
+  extern __shared__ unsigned char smem_raw[];
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem_raw);  // tma, mma
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 4);
+  float* sLam = reinterpret_cast<float*>(tslot + 4);  // Lam_t
+  float* sDel = sLam + Q;                             // delta_t
+  float* sW = sDel + Q;                               // w_t
+  float* sEL = sW + Q;                                // exp(Lam_t)
+  float* sD = sEL + Q;                                // D_t
+  float* sRow = sD + Q;                               // [2][Q] rowsum Z partials (by column half)
+  float* sCol = sRow + 2 * Q;                         // [2][Q]
+  float* sQ = sCol + 2 * Q;                           // [2][Q] gy.Y2 partials
+  float* sRed = sQ + 2 * Q;                           // 64 floats of reduction scratch
+  // m_t = u_t.R2_t and ur_t = u_t.r_t partials reuse sRow/sCol after use (see below)
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sRed + 64) + 1023) & ~uintptr_t(1023));
+  uint8_t* tU = sm;
+  uint8_t* tB = tU + TILE;        // 2 tiles
+  uint8_t* tC = tB + 2 * TILE;    // 2 tiles
+  uint8_t* tGY = tC + 2 * TILE;   // gy bf16 [s][d]
+  uint8_t* tGYt = tGY + TILE;     // exp(Lam_s) gy [s][d]
+  uint8_t* tPSI = tGYt + TILE;    // Psi^T bf16 [n][d]
+  uint8_t* tH0 = tPSI + TILE;     // h0^T bf16 [n][d]
+  uint8_t* tGP = tH0 + TILE;      // G' [s][t], 2 tiles (t halves)
+  uint8_t* tHH = tGP + 2 * TILE;  // H1 [s][t], 2 tiles
+  __shared__ float sM[2][Q];      // u_t . R2_t partials
+  __shared__ float sUR[2][Q];     // u_t . r_t partials
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int bh = blockIdx.x;
+  const int b = bh / H, h = bh % H;
+  const float Ah = A[(int64_t)h * ash];
+  const int nck = L / Q;
+  const int nseg = L / seg;
+  const int64_t row0 = (int64_t)b * L;
+  constexpr int fmt = MmaFmt<T>::v;
+  constexpr uint32_t id128KK = umma::idesc_f16(128, 128, fmt, 0, 0);
+  constexpr uint32_t id64KM = umma::idesc_f16(128, 64, fmt, 0, 1);
+  constexpr uint32_t id64MM = umma::idesc_f16(128, 64, fmt, 1, 1);
+  constexpr uint32_t id128MM = umma::idesc_f16(128, 128, fmt, 1, 1);
+  constexpr uint32_t id128KM = umma::idesc_f16(128, 128, fmt, 0, 1);
+
+  const int q4 = warp & 3, jh = warp >> 2;
+  const int row = 32 * q4 + lane;  // the row (s, t or n) this thread owns in TMEM
+  if (tid == 0) {
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    umma::tmem_alloc(tslot, 512);
+    umma::tmem_relinquish();
+  }
+  // Psi = dL/d(final state), thread (n = row, channels 32*jh..): gfinal is [B,H,Dh,N]
+  float psi[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i)
+    psi[i] = gfinal != nullptr ? gfinal[(((int64_t)b * H + h) * DH + 32 * jh + i) * NS + row] : 0.f;
+#pragma unroll
+  for (int cc = 0; cc < 4; ++cc)
+    *reinterpret_cast<int4*>(tPSI + umma::sw128_off(row, 32 * jh + 8 * cc)) = pack8<T>(psi + 8 * cc);
+  fence_proxy_async_smem();
+  __syncthreads();
+  umma::fence_after_sync();
+  const uint32_t tbase = *tslot;
+  const uint32_t tl = tbase + ((uint32_t)(32 * q4) << 16);
+
+  auto issue = [&](int c) {  // thread 0: u, B, C of chunk c
+    const int z = (int)(row0 + (int64_t)c * Q);
+    mbar_arrive_expect_tx(&bar[0], 5 * TILE);
+    tma_load_3d(tU, &tm_u, 0, h, z, &bar[0]);
+    tma_load_3d(tB, &tm_B, 0, h, z, &bar[0]);
+    tma_load_3d(tB + TILE, &tm_B, 64, h, z, &bar[0]);
+    tma_load_3d(tC, &tm_C, 0, h, z, &bar[0]);
+    tma_load_3d(tC + TILE, &tm_C, 64, h, z, &bar[0]);
+  };
+  if (tid == 0) issue(nck - 1);
+
+  // grad_y rows (thread: row s, channels 32*jh..) and delta of the first chunk processed
+  float gyr[32];
+  auto load_gy = [&](int c) {
+    const float* src = gy + ((row0 + (int64_t)c * Q + row) * H + h) * DH + 32 * jh;
+#pragma unroll
+    for (int i = 0; i < 32; i += 4) {
+      const float4 v = __ldcs(reinterpret_cast<const float4*>(src + i));
+      gyr[i] = v.x;
+      gyr[i + 1] = v.y;
+      gyr[i + 2] = v.z;
+      gyr[i + 3] = v.w;
+    }
+  };
+  load_gy(nck - 1);
+  float dnext = (tid < Q) ? to_f(delta[(row0 + (int64_t)(nck - 1) * Q + tid) * H + h]) : 0.f;
+  float gA_acc = 0.f;
+  uint32_t tph = 0, mph = 0;
+
+  auto block_sum = [&](float v) -> float {  // sum over all 256 threads
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    __syncthreads();
+    if (lane == 0) sRed[warp] = v;
+    __syncthreads();
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) s += sRed[w];
+    return s;
+  };
+
+  for (int c = nck - 1; c >= 0; --c) {
+    // ---- P0: Lam, D, w, exp(Lam); h0 (previous checkpoint); gy tiles
+    {
+      const float dcur = dnext;
+      if (tid < Q && c > 0) dnext = to_f(delta[(row0 + (int64_t)(c - 1) * Q + tid) * H + h]);
+      float lam = 0.f, dsum = 0.f;
+      if (tid < Q) {
+        lam = dcur * Ah;
+        dsum = dcur;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const float n1 = __shfl_up_sync(0xffffffffu, lam, o);
+          const float n2 = __shfl_up_sync(0xffffffffu, dsum, o);
+          if (lane >= o) {
+            lam += n1;
+            dsum += n2;
+          }
+        }
+        if (lane == 31) {
+          sRed[warp] = lam;
+          sRed[8 + warp] = dsum;
+        }
+        sDel[tid] = dcur;
+      }
+      __syncthreads();
+      if (tid < Q) {
+        float o1 = 0.f, o2 = 0.f;
+        for (int w = 0; w < warp; ++w) {
+          o1 += sRed[w];
+          o2 += sRed[8 + w];
+        }
+        sLam[tid] = lam + o1;
+        sD[tid] = dsum + o2;
+      }
+      __syncthreads();
+      if (tid < Q) {
+        sW[tid] = __expf(sLam[Q - 1] - sLam[tid]) * sDel[tid];
+        sEL[tid] = __expf(sLam[tid]);
+      }
+    }
+    float h0f[32];
+    if (c > 0) {
+      const float* src = ckpt + (((int64_t)b * nseg + (c * Q) / seg - 1) * H + h) * (int64_t)(NS * DH) +
+                         (int64_t)row * DH + 32 * jh;
+#pragma unroll
+      for (int i = 0; i < 32; i += 4) {
+        const float4 v = *reinterpret_cast<const float4*>(src + i);
+        h0f[i] = v.x;
+        h0f[i + 1] = v.y;
+        h0f[i + 2] = v.z;
+        h0f[i + 3] = v.w;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) h0f[i] = 0.f;
+    }
+    float psih0 = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) psih0 += psi[i] * h0f[i];
+#pragma unroll
+    for (int cc = 0; cc < 4; ++cc)
+      *reinterpret_cast<int4*>(tH0 + umma::sw128_off(row, 32 * jh + 8 * cc)) = pack8<T>(h0f + 8 * cc);
+    __syncthreads();  // sEL ready
+    {
+      // gy enters the S/P products as hi + lo 2-byte parts (P, P^T and R1 carry
+      // about 16 mantissa bits; dA/d-delta sum many of these terms)
+      const float el = sEL[row];
+      float t8[8], lo[8];
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        const uint32_t off = umma::sw128_off(row, 32 * jh + 8 * cc);
+        const int4 hi = pack8<T>(gyr + 8 * cc);
+        *reinterpret_cast<int4*>(tGY + off) = hi;
+        float hf[8];
+        unpack8<T>(hi, hf);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          t8[i] = el * gyr[8 * cc + i];
+          lo[i] = gyr[8 * cc + i] - hf[i];
+        }
+        *reinterpret_cast<int4*>(tGYt + off) = pack8<T>(t8);
+        *reinterpret_cast<int4*>(tGP + off) = pack8<T>(lo);  // gy lo part, read by batch 1 only
+      }
+    }
+    fence_proxy_async_smem();
+    const float psi_h0 = block_sum(psih0);  // includes a __syncthreads
+
+    // ---- batch 1: S, P, Y2, R2, dPsi^T
+    if (tid == 0) {
+      mbar_wait(&bar[0], tph & 1u);
+      ++tph;
+      umma::fence_after_sync();
+      const uint32_t aU = smem_u32(tU), aB = smem_u32(tB), aC = smem_u32(tC), aGY = smem_u32(tGY),
+                     aGYt = smem_u32(tGYt), aPSI = smem_u32(tPSI), aH0 = smem_u32(tH0);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const uint32_t ko = (k >> 2) * TILE + (k & 3) * 32;
+        umma::mma_f16(tbase + 0, umma::sdesc_k(aC + ko), umma::sdesc_k(aB + ko), id128KK, k > 0);
+        umma::mma_f16(tbase + 256, umma::sdesc_k(aC + ko), umma::sdesc_mn(aH0 + k * 2048, TILE), id64KM, k > 0);
+        umma::mma_f16(tbase + 320, umma::sdesc_k(aB + ko), umma::sdesc_mn(aPSI + k * 2048, TILE), id64KM, k > 0);
+        umma::mma_f16(tbase + 384, umma::sdesc_mn(aC + k * 2048, TILE), umma::sdesc_mn(aGYt + k * 2048, TILE),
+                      id64MM, k > 0);
+      }
+      const uint32_t aLo = smem_u32(tGP);
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        umma::mma_f16(tbase + 128, umma::sdesc_k(aGY + k * 32), umma::sdesc_k(aU + k * 32), id128KK, k > 0);
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        umma::mma_f16(tbase + 128, umma::sdesc_k(aLo + k * 32), umma::sdesc_k(aU + k * 32), id128KK, true);
+      umma::commit(&bar[1]);
+    }
+    mbar_wait(&bar[1], mph & 1u);
+    ++mph;
+    umma::fence_after_sync();
+
+    // gy lo part moves to the GYt tile (free now) for batch 2; G' takes its place
+#pragma unroll
+    for (int cc = 0; cc < 4; ++cc) {
+      const uint32_t off = umma::sw128_off(row, 32 * jh + 8 * cc);
+      *reinterpret_cast<int4*>(tGYt + off) = *reinterpret_cast<const int4*>(tGP + off);
+    }
+    __syncthreads();
+
+    // ---- epilogue 1 (thread: row s, t-half jh): G', H1, rowsum Z; gy.Y2; u.R2
+    {
+      const int s = row;
+      const float ls = sLam[s];
+      float rz = 0.f;
+      uint8_t* gp = tGP + jh * TILE;
+      uint8_t* hh = tHH + jh * TILE;
+      if (64 * jh > s) {
+#pragma unroll
+        for (int ch = 0; ch < 8; ++ch) {
+          *reinterpret_cast<int4*>(gp + umma::sw128_off(s, 8 * ch)) = make_int4(0, 0, 0, 0);
+          *reinterpret_cast<int4*>(hh + umma::sw128_off(s, 8 * ch)) = make_int4(0, 0, 0, 0);
+        }
+      } else {
+#pragma unroll
+        for (int cb = 0; cb < 4; ++cb) {
+          float sv[16], pv[16];
+          umma::tmem_ld16(tl + 64 * jh + 16 * cb, sv);
+          umma::tmem_ld16(tl + 128 + 64 * jh + 16 * cb, pv);
+          umma::tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int t = 64 * jh + 16 * cb + i;
+            const float e = (t <= s) ? __expf(ls - sLam[t]) : 0.f;
+            const float g = sv[i] * e;
+            const float h1 = pv[i] * e * sDel[t];
+            rz += sv[i] * h1;
+            sv[i] = g;
+            pv[i] = h1;
+          }
+          *reinterpret_cast<int4*>(gp + umma::sw128_off(s, 16 * cb)) = pack8<T>(sv);
+          *reinterpret_cast<int4*>(gp + umma::sw128_off(s, 16 * cb + 8)) = pack8<T>(sv + 8);
+          *reinterpret_cast<int4*>(hh + umma::sw128_off(s, 16 * cb)) = pack8<T>(pv);
+          *reinterpret_cast<int4*>(hh + umma::sw128_off(s, 16 * cb + 8)) = pack8<T>(pv + 8);
+        }
+      }
+      sRow[jh * Q + s] = rz;
+      // gy_s . Y2_s over this thread's 32 channels
+      float y2[32];
+      umma::tmem_ld16(tl + 256 + 32 * jh, *reinterpret_cast<float(*)[16]>(y2));
+      umma::tmem_ld16(tl + 256 + 32 * jh + 16, *reinterpret_cast<float(*)[16]>(y2 + 16));
+      float r2[32];
+      umma::tmem_ld16(tl + 320 + 32 * jh, *reinterpret_cast<float(*)[16]>(r2));
+      umma::tmem_ld16(tl + 320 + 32 * jh + 16, *reinterpret_cast<float(*)[16]>(r2 + 16));
+      umma::tmem_wait_ld();
+      float qa = 0.f, ma = 0.f;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) qa += gyr[i] * y2[i];
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        float f[8];
+        unpack8<T>(*reinterpret_cast<const int4*>(tU + umma::sw128_off(s, 32 * jh + 8 * cc)), f);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ma += f[i] * r2[8 * cc + i];
+      }
+      sQ[jh * Q + s] = qa;
+      sM[jh][s] = ma;
+      fence_proxy_async_smem();
+    }
+    umma::fence_before_sync();
+    __syncthreads();
+
+    // ---- batch 2: S^T, P^T, R1
+    if (tid == 0) {
+      umma::fence_after_sync();
+      const uint32_t aU = smem_u32(tU), aB = smem_u32(tB), aC = smem_u32(tC), aGY = smem_u32(tGY),
+                     aGP = smem_u32(tGP), aLo = smem_u32(tGYt);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const uint32_t ko = (k >> 2) * TILE + (k & 3) * 32;
+        umma::mma_f16(tbase + 0, umma::sdesc_k(aB + ko), umma::sdesc_k(aC + ko), id128KK, k > 0);
+        umma::mma_f16(tbase + 256, umma::sdesc_mn(aGP + k * 2048, TILE), umma::sdesc_mn(aGY + k * 2048, TILE),
+                      id64MM, k > 0);
+        umma::mma_f16(tbase + 256, umma::sdesc_mn(aGP + k * 2048, TILE), umma::sdesc_mn(aLo + k * 2048, TILE),
+                      id64MM, true);
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        umma::mma_f16(tbase + 128, umma::sdesc_k(aU + k * 32), umma::sdesc_k(aGY + k * 32), id128KK, k > 0);
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        umma::mma_f16(tbase + 128, umma::sdesc_k(aU + k * 32), umma::sdesc_k(aLo + k * 32), id128KK, true);
+      umma::commit(&bar[1]);
+    }
+    mbar_wait(&bar[1], mph & 1u);
+    ++mph;
+    umma::fence_after_sync();
+
+    // ---- epilogue 2 (thread: row t): colsum Z; r, grad_u, u.r; Psi update (row n)
+    {
+      const int t = row;
+      const float lt = sLam[t], dt = sDel[t];
+      float cz = 0.f;
+      if (64 * jh + 63 >= t) {
+#pragma unroll
+        for (int cb = 0; cb < 4; ++cb) {
+          float sv[16], pv[16];
+          umma::tmem_ld16(tl + 64 * jh + 16 * cb, sv);
+          umma::tmem_ld16(tl + 128 + 64 * jh + 16 * cb, pv);
+          umma::tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int s = 64 * jh + 16 * cb + i;
+            const float e = (s >= t) ? __expf(sLam[s] - lt) : 0.f;
+            cz += sv[i] * pv[i] * e;
+          }
+        }
+      }
+      sCol[jh * Q + t] = cz * dt;
+      float r1[32], r2[32], dp[32];
+      umma::tmem_ld16(tl + 256 + 32 * jh, *reinterpret_cast<float(*)[16]>(r1));
+      umma::tmem_ld16(tl + 256 + 32 * jh + 16, *reinterpret_cast<float(*)[16]>(r1 + 16));
+      umma::tmem_ld16(tl + 320 + 32 * jh, *reinterpret_cast<float(*)[16]>(r2));
+      umma::tmem_ld16(tl + 320 + 32 * jh + 16, *reinterpret_cast<float(*)[16]>(r2 + 16));
+      umma::tmem_ld16(tl + 384 + 32 * jh, *reinterpret_cast<float(*)[16]>(dp));
+      umma::tmem_ld16(tl + 384 + 32 * jh + 16, *reinterpret_cast<float(*)[16]>(dp + 16));
+      umma::tmem_wait_ld();
+      const float f2 = __expf(sLam[Q - 1] - lt);
+      const float dec = __expf(sLam[Q - 1]);
+      float ur = 0.f;
+      T* gup = gu + ((row0 + (int64_t)c * Q + t) * H + h) * DH + 32 * jh;
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        float f[8], o[8];
+        unpack8<T>(*reinterpret_cast<const int4*>(tU + umma::sw128_off(t, 32 * jh + 8 * cc)), f);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float rv = r1[8 * cc + i] + f2 * r2[8 * cc + i];
+          ur += f[i] * rv;
+          o[i] = dt * rv;
+        }
+        *reinterpret_cast<int4*>(gup + 8 * cc) = pack8<T>(o);
+      }
+      sUR[jh][t] = ur;
+      // Psi (row n = row) <- exp(Lam_last) Psi + dPsi; the bf16 copy is replaced after batch 3
+#pragma unroll
+      for (int i = 0; i < 32; ++i) psi[i] = dec * psi[i] + dp[i];
+    }
+    umma::fence_before_sync();
+    __syncthreads();
+
+    // ---- batch 3: gB1 = H1^T C, gC1 = H1 B, gB2 = u Psi(old), gC2 = gy h0
+    if (tid == 0) {
+      umma::fence_after_sync();
+      const uint32_t aU = smem_u32(tU), aB = smem_u32(tB), aC = smem_u32(tC), aGY = smem_u32(tGY),
+                     aPSI = smem_u32(tPSI), aH0 = smem_u32(tH0), aHH = smem_u32(tHH);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const uint32_t ko = (k >> 2) * TILE + (k & 3) * 32;
+        umma::mma_f16(tbase + 0, umma::sdesc_mn(aHH + k * 2048, TILE), umma::sdesc_mn(aC + k * 2048, TILE),
+                      id128MM, k > 0);
+        umma::mma_f16(tbase + 128, umma::sdesc_k(aHH + ko), umma::sdesc_mn(aB + k * 2048, TILE), id128KM, k > 0);
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        umma::mma_f16(tbase + 384, umma::sdesc_k(aGY + k * 32), umma::sdesc_k(aH0 + k * 32), id128KK, k > 0);
+        umma::mma_f16(tbase + 256, umma::sdesc_k(aU + k * 32), umma::sdesc_k(aPSI + k * 32), id128KK, k > 0);
+      }
+      umma::commit(&bar[1]);
+    }
+    // ---- grad_delta and grad_A while batch 3 runs (thread t < Q)
+    {
+      float wm = 0.f;
+      if (tid < Q) wm = sW[tid] * (sM[0][tid] + sM[1][tid]);
+      const float sum_wm = block_sum(wm);
+      float dl = 0.f;
+      if (tid < Q) {
+        const int t = tid;
+        dl = (sRow[t] + sRow[Q + t]) - (sCol[t] + sCol[Q + t]) + sEL[t] * (sQ[t] + sQ[Q + t]) - wm;
+        if (t == Q - 1) dl += sEL[Q - 1] * psi_h0 + sum_wm;
+      }
+      const float contrib = block_sum(tid < Q ? dl * sD[tid] : 0.f);
+      if (tid == 0) gA_acc += contrib;
+      // suffix sum of dLam over t (warps 0-3)
+      float suf = dl;
+      if (tid < Q) {
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const float n = __shfl_down_sync(0xffffffffu, suf, o);
+          if (lane + o < 32) suf += n;
+        }
+        if (lane == 0) sRed[16 + warp] = suf;
+      }
+      __syncthreads();
+      if (tid < Q) {
+        for (int w = warp + 1; w < 4; ++w) suf += sRed[16 + w];
+        const float g = Ah * suf + (sUR[0][tid] + sUR[1][tid]);
+        gdelta[(row0 + (int64_t)c * Q + tid) * H + h] = from_f<T>(g);
+      }
+    }
+    mbar_wait(&bar[1], mph & 1u);
+    ++mph;
+    umma::fence_after_sync();
+    // u, B, C of this chunk are no longer read: stream the previous chunk's
+    if (tid == 0 && c > 0) {
+      fence_proxy_async_smem();
+      issue(c - 1);
+    }
+    if (c > 0) load_gy(c - 1);
+
+    // ---- epilogue 3 (thread: row t for gB, row s for gC; 64 columns per half)
+    {
+      const int t = row;
+      const float wt = sW[t], et = sEL[t];
+      T* gbp = gB + ((row0 + (int64_t)c * Q + t) * H + h) * NS + 64 * jh;
+      T* gcp = gC + ((row0 + (int64_t)c * Q + t) * H + h) * NS + 64 * jh;
+#pragma unroll
+      for (int cb = 0; cb < 4; ++cb) {
+        float b1[16], b2[16], cv[16], c2[16];
+        umma::tmem_ld16(tl + 0 + 64 * jh + 16 * cb, b1);
+        umma::tmem_ld16(tl + 256 + 64 * jh + 16 * cb, b2);
+        umma::tmem_ld16(tl + 128 + 64 * jh + 16 * cb, cv);
+        umma::tmem_ld16(tl + 384 + 64 * jh + 16 * cb, c2);
+        umma::tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          b1[i] += wt * b2[i];
+          cv[i] += et * c2[i];
+        }
+        *reinterpret_cast<int4*>(gbp + 16 * cb) = pack8<T>(b1);
+        *reinterpret_cast<int4*>(gbp + 16 * cb + 8) = pack8<T>(b1 + 8);
+        *reinterpret_cast<int4*>(gcp + 16 * cb) = pack8<T>(cv);
+        *reinterpret_cast<int4*>(gcp + 16 * cb + 8) = pack8<T>(cv + 8);
+      }
+      // Psi's bf16 copy for the next chunk (its readers in batches 1 and 3 are done)
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc)
+        *reinterpret_cast<int4*>(tPSI + umma::sw128_off(row, 32 * jh + 8 * cc)) = pack8<T>(psi + 8 * cc);
+      fence_proxy_async_smem();
+    }
+    umma::fence_before_sync();
+    __syncthreads();
+  }
+  if (tid == 0) gA_part[bh] = gA_acc;
+  __syncthreads();
+  if (warp == 0) umma::tmem_dealloc(tbase, 512);
+}
+
+// grad_A[h, n] = (sum_b part[b, h]) / N: the per-head derivative spread over n
+__global__ void ssd_ga_head_kernel(const float* __restrict__ part, int B, int H, int N, float* __restrict__ gA) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= H * N) return;
+  const int h = i / N;
+  float s = 0.f;
+  for (int b = 0; b < B; ++b) s += part[b * H + h];
+  gA[i] = s / (float)N;
+}
+
+template <typename T>
+int ssd_chunk_bwd_launch(const float* gy, const float* gf, const float* ckpt, const void* u, const void* delta,
+                         const void* Bm, const void* Cm, const float* A, int64_t ash, int64_t batch, int64_t L,
+                         int64_t H, int64_t seg, void* gu, void* gd, void* gB, void* gC, float* gA,
+                         float* ws, cudaStream_t st) {
+  CUtensorMap mu, mB, mC;
+  if (int rc = ssd_tmaps<T>(u, Bm, Cm, batch, L, H, &mu, &mB, &mC)) return rc;
+  auto k = ssd_chunk_bwd_kernel<T>;
+  const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssdb::SMEM);
+  if (e != cudaSuccess) return set_error(MR_E_LAUNCH, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  k<<<(unsigned)(batch * H), 256, ssdb::SMEM, st>>>(mu, mB, mC, gy, gf, ckpt, (const T*)delta, A, ash, (int)L,
+                                                    (int)H, (int)seg, (T*)gu, (T*)gd, (T*)gB, (T*)gC, ws);
+  if (int rc = check_launch("ssd_chunk_bwd_kernel")) return rc;
+  const int HN = (int)(H * ssdb::NS);
+  ssd_ga_head_kernel<<<(HN + 255) / 256, 256, 0, st>>>(ws, (int)batch, (int)H, ssdb::NS, gA);
+  return check_launch("ssd_ga_head_kernel");
+}
+
+size_t ssd_chunk_bwd_ws_bytes(int64_t batch, int64_t H) { return (size_t)batch * H * sizeof(float); }
+
+template int ssd_chunk_bwd_launch<__nv_bfloat16>(const float*, const float*, const float*, const void*,
+                                                 const void*, const void*, const void*, const float*, int64_t,
+                                                 int64_t, int64_t, int64_t, int64_t, void*, void*, void*, void*,
+                                                 float*, float*, cudaStream_t);
+template int ssd_chunk_bwd_launch<__half>(const float*, const float*, const float*, const void*, const void*,
+                                          const void*, const void*, const float*, int64_t, int64_t, int64_t,
+                                          int64_t, int64_t, void*, void*, void*, void*, float*, float*,
+                                          cudaStream_t);
+
+}  // namespace mr

@@ -44,4 +44,23 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int
   return MR_OK;
 }
 
+int make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes,
+                 uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1, uint64_t s2, uint32_t b0,
+                 uint32_t b1, uint32_t b2, CUtensorMapSwizzle swizzle) {
+  EncodeTiledFn enc = encoder();
+  if (enc == nullptr) return set_error(MR_E_DEVICE, "cuTensorMapEncodeTiled is unavailable");
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) || (s1 & 15u) || (s2 & 15u) || ((b0 * elem_bytes) & 15u))
+    return set_error(MR_E_ALIGN, "tensor map: base, pitches and box row must be 16-byte multiples");
+  const cuuint64_t dims[3] = {d0, d1, d2};
+  const cuuint64_t strides[2] = {s1, s2};
+  const cuuint32_t box[3] = {b0, b1, b2};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = enc(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(MR_E_LAUNCH, "cuTensorMapEncodeTiled (3d) failed (%d)", (int)r);
+  return MR_OK;
+}
+
 }  // namespace mr

@@ -19,6 +19,12 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int
                  uint64_t cols, uint64_t rows, uint64_t row_bytes, uint32_t box_cols,
                  uint32_t box_rows, CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE);
 
+// 3-D tiled map over [d2, d1, d0] (d0 contiguous) with byte pitches s1, s2
+// for dims 1 and 2 and box [b2, b1, b0].
+int make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes,
+                 uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1, uint64_t s2, uint32_t b0,
+                 uint32_t b1, uint32_t b2, CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE);
+
 template <typename T> struct TmapType;
 template <> struct TmapType<float> { static constexpr CUtensorMapDataType v = CU_TENSOR_MAP_DATA_TYPE_FLOAT32; };
 template <> struct TmapType<__nv_bfloat16> { static constexpr CUtensorMapDataType v = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16; };
@@ -31,6 +37,16 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
           static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y),
+      "r"(static_cast<uint32_t>(__cvta_generic_to_shared(bar)))
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
+          static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z),
       "r"(static_cast<uint32_t>(__cvta_generic_to_shared(bar)))
       : "memory");
 }

@@ -58,14 +58,18 @@ class _SSDScan(torch.autograd.Function):
         dt = common_dtype(u, delta, B, C)
         u_, d_, B_, C_ = (prep(t, dt) for t in (u, delta, B, C))
         A32, ash, asn = _a_f32(A_neg)
+        code = _lib.DTYPE_CODE[dt]
+        # The checkpoints are internal (only the last one is returned, ssd.py:361/374):
+        # take the spacing of the fastest path for these shapes (same final state).
+        seg_i = int(_lib.load().mr_ssd_preferred_seg(code, L, Dh, N, seg, asn))
         y = torch.empty((Bt, L, H, Dh), dtype=torch.float32, device=dev)
-        ckpt = torch.empty((Bt, L // seg, H, N, Dh), dtype=torch.float32, device=dev)
+        ckpt = torch.empty((Bt, L // seg_i, H, N, Dh), dtype=torch.float32, device=dev)
         with torch.cuda.device(dev):
             _lib.call("mr_ssd_fwd", _lib.ptr(u_), _lib.ptr(d_), _lib.ptr(B_), _lib.ptr(C_),
-                      _lib.ptr(A32), ash, asn, _lib.DTYPE_CODE[dt], Bt, L, H, Dh, N, seg,
+                      _lib.ptr(A32), ash, asn, code, Bt, L, H, Dh, N, seg_i,
                       _lib.ptr(y), _lib.ptr(ckpt), _lib.stream_of(dev))
         ctx.save_for_backward(u_, d_, B_, C_, A32, ckpt)
-        ctx.meta = (seg, ash, asn, N)
+        ctx.meta = (seg_i, ash, asn, N)
         # last checkpoint [B, H, N, Dh] -> conceptual state [B, H, Dh, N] (ssd.py:373-374)
         final = ckpt[:, -1].transpose(-1, -2).contiguous()
         return y, final
@@ -81,6 +85,8 @@ class _SSDScan(torch.autograd.Function):
         gf = None if gfinal is None else gfinal.to(torch.float32).contiguous()
         gu, gd, gB, gC = (torch.empty_like(t) for t in (u_, d_, B_, C_))
         gA = torch.empty((H, N), dtype=torch.float32, device=dev)
+        # with one rate per head (asn == 0) row h of gA is d loss / d A_h spread
+        # evenly over n; autograd's expand-backward sums it back to the head
         with torch.cuda.device(dev):
             lib = _lib.load()
             nws = lib.mr_ssd_bwd_workspace_bytes(code, Bt, L, H, Dh, N, seg, asn)

@@ -158,3 +158,36 @@ def test_ssd_per_head_rate_view_matches_dense(mr, cuda_dev):
     y1 = mr.ssd_scan(*ts, Av)
     y2 = mr.ssd_scan(*ts, Ad)
     assert K.rel_err(y1.double().cpu().numpy(), y2.double().cpu().numpy()) < 1e-6
+
+
+@pytest.mark.parametrize("Bt,L,H,seg,dtype", [
+    (2, 256, 3, 32, torch.bfloat16),
+    (1, 384, 2, 128, torch.float16),
+    (1, 256, 2, 64, torch.bfloat16),
+])
+def test_ssd_tensor_core_path_through_api(mr, cuda_dev, Bt, L, H, seg, dtype):
+    """bf16/fp16, Dh=64, N=128, one decay rate per head (an [H] parameter
+    broadcast over N): the chunked tcgen05 path, forward and every gradient
+    (the [H] parameter's gradient for A) against the float64 oracle."""
+    rng = np.random.default_rng(L + H)
+    u = rng.standard_normal((Bt, L, H, 64))
+    delta = np.abs(rng.standard_normal((Bt, L, H))) * 0.1 + 0.01
+    Bm = rng.standard_normal((Bt, L, H, 128))
+    Cm = rng.standard_normal((Bt, L, H, 128))
+    A_h = -np.exp(rng.standard_normal(H) * 0.5)
+    ts = [torch.tensor(x, dtype=torch.float32).to(dtype).to(cuda_dev).requires_grad_(True) for x in (u, delta, Bm, Cm)]
+    A_t = torch.tensor(A_h, dtype=torch.float32, device=cuda_dev, requires_grad=True)
+    y, fin = mr.ssd_scan_with_state(*ts, A_t[:, None].expand(H, 128), seg=seg)
+    w = rng.standard_normal(tuple(y.shape))
+    wf = rng.standard_normal(tuple(fin.shape))
+    loss = (y * torch.tensor(w, dtype=torch.float32, device=cuda_dev)).sum() + \
+           (fin * torch.tensor(wf, dtype=torch.float32, device=cuda_dev)).sum()
+    grads = torch.autograd.grad(loss, ts + [A_t])
+    ins = [t.detach().double().cpu().numpy() for t in ts] + [np.repeat(A_h[:, None], 128, axis=1)]
+    yo, fo = K.oracle_fwd("ssd", ins)
+    ref = K.oracle_bwd("ssd", ins, w, wf)
+    assert K.rel_err(y.detach().double().cpu().numpy(), yo) < 2e-2
+    assert K.rel_err(fin.detach().double().cpu().numpy(), fo) < 2e-2
+    for name, g, r in zip(("u", "delta", "B", "C"), grads[:4], ref[:4]):
+        assert K.rel_err(g.double().cpu().numpy(), r) < 2e-2, name
+    assert K.rel_err(grads[4].double().cpu().numpy(), ref[4].sum(1)) < 2e-2, "A (per head)"
