@@ -124,6 +124,23 @@ MR_API int mr_ssd_bwd(const float* grad_y, const float* grad_final, const float*
                void* grad_u, void* grad_delta, void* grad_B, void* grad_C, float* grad_A,
                void* workspace, size_t workspace_bytes, void* stream);
 
+/* Allocation-free SSD backward. No counterpart in the reference: it exists
+ * for callers that cannot allocate device memory when the backward runs
+ * (inside a graph capture or an allocator callback, or embedders that only
+ * hand over pre-placed tensors). Same arguments and results as mr_ssd_bwd
+ * without the workspace; covers the tensor-core path only (bf16/f16, Dh=64,
+ * N=128, a_stride_n == 0, seg == 128, L % 128 == 0; else MR_E_SHAPE). Its
+ * scratch is a built-in 256 KiB device array per GPU (batch*H <= 65,536,
+ * else MR_E_WORKSPACE). The first call on a device looks up that array's
+ * address (make it before any stream capture); all calls on a device share
+ * the array, so calls that overlap on the GPU race. */
+MR_API int mr_ssd_bwd_noalloc(const float* grad_y, const float* grad_final, const float* h_ckpt,
+                              const void* u, const void* delta, const void* Bm, const void* Cm,
+                              const float* A_neg, int64_t a_stride_h, int64_t a_stride_n, int dtype,
+                              int64_t batch, int64_t L, int64_t H, int64_t Dh, int64_t N, int64_t seg,
+                              void* grad_u, void* grad_delta, void* grad_B, void* grad_C, float* grad_A,
+                              void* stream);
+
 /* ---------------------------------------------------------------- GLA ---
  * q,k,v [B,L,H,Dh], gates [B,L,H] in `dtype`; y [B,L,H,Dh] f32;
  * h_ckpt [B,L/seg,H,Dh(i),Dh(j)] f32 (gla.py:62). */

@@ -52,6 +52,9 @@ bool ssd_chunk_supported(int dtype, int64_t L, int64_t Dh, int64_t N, int64_t se
 bool ssd_chunk_bwd_supported(int dtype, int64_t L, int64_t Dh, int64_t N, int64_t seg, int64_t a_stride_n);
 int ssd_chunk_len();
 size_t ssd_chunk_bwd_ws_bytes(int64_t batch, int64_t H);
+int ssd_chunk_bwd_noalloc(int dtype, const float*, const float*, const float*, const void*, const void*,
+                          const void*, const void*, const float*, int64_t, int64_t, int64_t, int64_t, int64_t,
+                          void*, void*, void*, void*, float*, cudaStream_t);
 template <typename T> int ssd_chunk_bwd_launch(const float*, const float*, const float*, const void*, const void*, const void*, const void*, const float*, int64_t, int64_t, int64_t, int64_t, int64_t, void*, void*, void*, void*, float*, float*, cudaStream_t);
 template <typename T> int ssd_chunk_fwd_launch(const void*, const void*, const void*, const void*, const float*, int64_t, int64_t, int64_t, int64_t, int64_t, float*, float*, cudaStream_t);
 int umma_selftest_launch(const void*, const void*, const void*, const void*, float*, float*, float*,
@@ -309,6 +312,25 @@ int mr_ssd_bwd(const float* grad_y, const float* grad_final, const float* h_ckpt
                                                a_stride_h, a_stride_n, batch, L, H, Dh, N, seg,
                                                grad_u, grad_delta, grad_B, grad_C, grad_A,
                                                workspace, st));
+}
+
+int mr_ssd_bwd_noalloc(const float* grad_y, const float* grad_final, const float* h_ckpt, const void* u,
+                       const void* delta, const void* Bm, const void* Cm, const float* A_neg,
+                       int64_t a_stride_h, int64_t a_stride_n, int dtype, int64_t batch, int64_t L,
+                       int64_t H, int64_t Dh, int64_t N, int64_t seg, void* grad_u, void* grad_delta,
+                       void* grad_B, void* grad_C, float* grad_A, void* stream) {
+  g_err[0] = 0;
+  MR_TRY(ssd_common_checks("mr_ssd_bwd_noalloc", dtype, batch, L, H, Dh, N, seg));
+  MR_TRY(check_ptrs("mr_ssd_bwd_noalloc", {grad_y, h_ckpt, u, delta, Bm, Cm, grad_u, grad_delta, grad_B, grad_C}));
+  MR_TRY(check_opt_ptr("mr_ssd_bwd_noalloc", grad_final));
+  if (A_neg == nullptr || grad_A == nullptr)
+    return set_error(MR_E_ALIGN, "mr_ssd_bwd_noalloc: A_neg / grad_A is NULL");
+  if (!ssd_chunk_bwd_supported(dtype, L, Dh, N, seg, a_stride_n))
+    return set_error(MR_E_SHAPE,
+                     "mr_ssd_bwd_noalloc covers the tensor-core path only (bf16/f16, Dh=64, N=128, one rate "
+                     "per head, seg=128, L %% 128 == 0); use mr_ssd_bwd with a workspace otherwise");
+  return ssd_chunk_bwd_noalloc(dtype, grad_y, grad_final, h_ckpt, u, delta, Bm, Cm, A_neg, a_stride_h, batch,
+                               L, H, seg, grad_u, grad_delta, grad_B, grad_C, grad_A, (cudaStream_t)stream);
 }
 
 // --------------------------------------------------------------------- GLA ---

@@ -23,6 +23,8 @@
 // in float32 (thread = state row n, 32 channels); its bf16 copy in shared
 // memory is the operand of the next chunk's Y2 product, and it is written to
 // h_ckpt in float32 at segment ends (seg a multiple of Q).
+#include <mutex>
+
 #include "common.cuh"
 #include "tma.cuh"
 #include "tmap.cuh"
@@ -924,5 +926,69 @@ template int ssd_chunk_bwd_launch<__half>(const float*, const float*, const floa
                                           const void*, const void*, const float*, int64_t, int64_t, int64_t,
                                           int64_t, int64_t, void*, void*, void*, void*, float*, float*,
                                           cudaStream_t);
+
+
+// ===========================================================================
+// Allocation-free variant of the SSD backward (tensor-core path only)
+// ===========================================================================
+//
+// Some callers cannot allocate device memory at the moment they run the
+// backward: code running inside a CUDA-graph capture or a custom allocator's
+// callback, embedders that hand the library only pre-placed tensors, or
+// runtimes that forbid allocation on their hot path. For them this entry point
+// takes no workspace. Its only scratch - one float per (batch row, head), the
+// per-head partial derivatives for A - lives in the file-scope device array
+// below, which every GPU that loads the library holds until the process exits.
+//
+// Limits and behaviour:
+//   - batch * H <= kNoAllocMaxUnits (65,536), i.e. a 256 KiB array; larger
+//     problems are rejected with MR_E_WORKSPACE.
+//   - On the first call on a device (with that device current) the array's
+//     device address is looked up once and cached; make that first call
+//     before any stream capture on the device.
+//   - Every call on a device shares the array. Each call writes every entry it
+//     later reads, so nothing needs clearing between calls, but calls that
+//     overlap on the GPU (different streams, or concurrent graphs) race.
+
+constexpr int64_t kNoAllocMaxUnits = 65536;
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocMaxUnits];
+
+static int noalloc_scratch_ptr(float** out) {
+  constexpr int kMaxDev = 64;
+  static float* cached[kMaxDev] = {};
+  static std::mutex mu;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(MR_E_DEVICE, "cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDev) return set_error(MR_E_DEVICE, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (cached[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess)
+      return set_error(MR_E_DEVICE, "cudaGetSymbolAddress(scratch): %s", cudaGetErrorString(e));
+    cached[dev] = static_cast<float*>(p);
+  }
+  *out = cached[dev];
+  return MR_OK;
+}
+
+int ssd_chunk_bwd_noalloc(int dtype, const float* gy, const float* gf, const float* ckpt, const void* u,
+                          const void* delta, const void* Bm, const void* Cm, const float* A, int64_t ash,
+                          int64_t batch, int64_t L, int64_t H, int64_t seg, void* gu, void* gd, void* gB,
+                          void* gC, float* gA, cudaStream_t st) {
+  if (batch * H > kNoAllocMaxUnits)
+    return set_error(MR_E_WORKSPACE,
+                     "mr_ssd_bwd_noalloc: batch*H = %lld exceeds the built-in scratch of %lld (batch, head) "
+                     "entries; use mr_ssd_bwd with a workspace",
+                     (long long)(batch * H), (long long)kNoAllocMaxUnits);
+  float* scratch = nullptr;
+  if (int rc = noalloc_scratch_ptr(&scratch)) return rc;
+  if (dtype == MR_BF16)
+    return ssd_chunk_bwd_launch<__nv_bfloat16>(gy, gf, ckpt, u, delta, Bm, Cm, A, ash, batch, L, H, seg, gu, gd,
+                                               gB, gC, gA, scratch, st);
+  return ssd_chunk_bwd_launch<__half>(gy, gf, ckpt, u, delta, Bm, Cm, A, ash, batch, L, H, seg, gu, gd, gB, gC,
+                                      gA, scratch, st);
+}
 
 }  // namespace mr
