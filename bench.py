@@ -82,6 +82,20 @@ def algorithmic_bytes(cfg, batch):
     return inp + y, inp + y + inp
 
 
+# DRAM bytes (read + write) per launch measured by ncu on a B=4 instance of the
+# same configuration (profiles/ssd_chunk_c4.md), per batch row: the kernels'
+# traffic grows linearly with the (batch, head) units.
+_NCU_TRAFFIC_PER_BATCH_ROW = {
+    ("c4", "backward"): (2.440075e9 + 1.304630e9) / 4,
+    ("c4", "forward"): (1.349373e9 + 1.024133e9) / 4,
+}
+
+
+def _traffic(name, which, nb, cfg):
+    v = _NCU_TRAFFIC_PER_BATCH_ROW.get((name, which))
+    return None if v is None else v * nb
+
+
 # --------------------------------------------------------------------------- #
 # clocks sampled during the timed region
 # --------------------------------------------------------------------------- #
@@ -239,7 +253,9 @@ def run_ours(args):
             dist.barrier()
 
     name = args.config
-    cfg = W.CONFIGS[name]
+    cfg = dict(W.CONFIGS[name])
+    if args.batch:
+        cfg["B"] = args.batch
     b0, b1 = W.shard_batch(cfg["B"], rank, world)
     nb = b1 - b0
     ins = W.make_inputs(name, dev, seed=1000 + rank, batch=nb)
@@ -296,6 +312,30 @@ def run_ours(args):
     peak_mb = torch.cuda.max_memory_allocated(dev) / 2 ** 20
 
     # ---- timed: end to end from pinned host memory
+    e2e_ms = None
+    h2d = d2h = 0
+    if not args.no_e2e:
+        e2e_ms, h2d, d2h = _e2e(args, fn, ins, gy, dev, stream, barrier, ev)
+
+    # ---- max over ranks
+    t = torch.tensor([total_ms, e2e_ms or 0.0, statistics.mean(fwd_ms), statistics.mean(bwd_ms)],
+                     dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms, e2e_ms_max, f_ms, b_ms = t.tolist()
+    if e2e_ms is not None:
+        e2e_ms = e2e_ms_max
+    _report(args, rank, world, W, name, cfg, nb, total_ms, e2e_ms, f_ms, b_ms, h2d, d2h, peak_mb, launches, clk)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def _e2e(args, fn, ins, gy, dev, stream, barrier, ev):
+    """Same step through the public API with host buffers: per step, H2D copies
+    of every input from pinned memory, forward+backward, D2H of the last
+    step's outputs. Returns (ms for all steps, H2D bytes/step, D2H bytes/step)."""
+    import torch
     # A tensor broadcast along its last axis (SSD's per-head A_neg) travels as
     # its [.., 1] base and is re-expanded on the device, as a caller would.
     def compact(t):
@@ -340,15 +380,10 @@ def run_ours(args):
     e2e_e.record(stream)
     torch.cuda.synchronize()
     barrier()
-    e2e_ms = e2e_s.elapsed_time(e2e_e)
+    return e2e_s.elapsed_time(e2e_e), h2d, d2h
 
-    # ---- max over ranks
-    t = torch.tensor([total_ms, e2e_ms, statistics.mean(fwd_ms), statistics.mean(bwd_ms)],
-                     dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    total_ms, e2e_ms, f_ms, b_ms = t.tolist()
 
+def _report(args, rank, world, W, name, cfg, nb, total_ms, e2e_ms, f_ms, b_ms, h2d, d2h, peak_mb, launches, clk):
     if rank == 0:
         hbm, tc, peak_kind = _peaks()
         tok = W.tokens(cfg)  # whole job: all ranks together process the config
@@ -375,11 +410,12 @@ def run_ours(args):
             "bwd_ms": b_ms,
             "fwd_tokens_per_s": tok / (f_ms * 1e-3),
             "peak_mb": peak_mb,
-            "e2e": {"value": tok * args.steps / (e2e_ms * 1e-3), "unit": "tokens/s",
-                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "e2e": None if e2e_ms is None else {
+                "value": tok * args.steps / (e2e_ms * 1e-3), "unit": "tokens/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "roofline": {"bound": "hbm", "kernel": f"{cfg['kind']} {dom[0]}",
                          "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                         "frac": achieved / hbm, "traffic": None,
+                         "frac": achieved / hbm, "traffic": _traffic(name, dom[0], nb, cfg),
                          "algorithmic_bytes_per_launch": dom[1],
                          "peak_source": f"{peak_kind} hbm_gbs"},
             "gpu_launches": int(launches),
@@ -388,9 +424,6 @@ def run_ours(args):
         if world == 1 and not args.no_cpu_baseline:
             out["cpu_baseline"] = cpu_baseline(name)
         print(json.dumps(out), flush=True)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
 
 
 def run_reference(args):
@@ -445,6 +478,9 @@ def main():
     ap.add_argument("--config", default="c4", choices=["c0", "c1", "c2", "c3", "c4"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffer) timing")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="override the config's batch (a smaller instance, e.g. for profiler captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
