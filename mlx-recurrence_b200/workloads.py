@@ -3,8 +3,8 @@
 The reference measures on no public dataset; these generators draw inputs
 with the shapes and value distributions of its published configurations
 (from the reference's own test inputs and
-``docs/validation``). ``shard=(rank, world)`` returns one rank's slice of the
-independent units: a contiguous batch range when ``world`` divides B.
+``docs/validation``). A rank's shard is a contiguous batch range
+(``shard_batch``) generated with its own seed and ``batch=`` its size.
 """
 
 from __future__ import annotations
@@ -12,6 +12,8 @@ from __future__ import annotations
 import math
 
 import torch
+
+from .sharding import shard_batch  # noqa: F401  (re-exported for bench.py)
 
 CONFIGS = {
     "c0": dict(kind="ssd", B=3, L=512, H=12, Dh=64, N=16, seg=32, dtype=torch.float32),
@@ -32,14 +34,6 @@ DESCRIPTION = {
 
 def tokens(cfg):
     return cfg["B"] * cfg["L"]
-
-
-def shard_batch(B, rank, world):
-    """Contiguous batch range [b0, b1) of one rank."""
-    per = B // world
-    rem = B % world
-    b0 = rank * per + min(rank, rem)
-    return b0, b0 + per + (1 if rank < rem else 0)
 
 
 def make_inputs(name, device, seed=0, batch=None):
