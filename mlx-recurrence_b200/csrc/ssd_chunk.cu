@@ -40,7 +40,7 @@ constexpr uint32_t TILE = 16384;       // [128 rows x 64 elements] 2-byte tile
 constexpr uint32_t STAGE = TILE * 5;   // u, B lo/hi, C lo/hi
 // small arrays (Lam, delta, warp sums, barriers, TMEM slot) first, then the
 // 1024-byte-aligned tiles
-constexpr size_t SMALL = (2 * Q + 8) * 4 + 6 * 8 + 16;
+constexpr size_t SMALL = (3 * Q + 8) * 4 + 6 * 8 + 16;
 constexpr size_t SMEM = SMALL + 1023 + 2 * STAGE + 2 * TILE + TILE + TILE;
 }  // namespace ssdc
 
@@ -75,20 +75,21 @@ __device__ __forceinline__ int4 pack8(const float* f) {
 template <typename T>
 __global__ void __launch_bounds__(256, 1)
 ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_constant__ CUtensorMap tm_B,
-                     const __grid_constant__ CUtensorMap tm_C, const T* __restrict__ delta,
-                     const float* __restrict__ A, int64_t ash, int L, int H, int seg,
-                     float* __restrict__ y, float* __restrict__ ckpt) {
+                     const __grid_constant__ CUtensorMap tm_C, const __grid_constant__ CUtensorMap tm_y,
+                     const __grid_constant__ CUtensorMap tm_ck, const T* __restrict__ delta,
+                     const float* __restrict__ A, int64_t ash, int L, int H, int seg) {
   using namespace ssdc;
   extern __shared__ unsigned char smem_raw[];
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem_raw);  // bc[2], u[2], mma
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 6);
   float* sLam = reinterpret_cast<float*>(tslot + 4);  // [Q]
   float* sDel = sLam + Q;                             // [Q]
-  float* sWarp = sDel + Q;                            // [8]
+  float* sCF = sDel + Q;                              // [Q] column factors (see E1)
+  float* sWarp = sCF + Q;                             // [8]
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sWarp + 8) + 1023) & ~uintptr_t(1023));
   uint8_t* stg0 = sm;            // stage s: u | B lo | B hi | C lo | C hi
-  uint8_t* sG = sm + 2 * STAGE;  // G, two K-major tiles (s 0-63, 64-127)
-  uint8_t* sUt = sG + 2 * TILE;  // U~, MN-major [s][d]
+  uint8_t* sG = sm + 2 * STAGE;  // G, two K-major tiles (s 0-63, 64-127); then y staging
+  uint8_t* sUt = sG + 2 * TILE;  // U~, MN-major [s][d]; then checkpoint staging (n 0-63)
   uint8_t* sHt = sUt + TILE;     // h^T bf16, MN-major [n][d]
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -118,7 +119,8 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   umma::fence_after_sync();
   const uint32_t tbase = *tslot;
 
-  // B and C of a chunk are free once its S/dH/Y2 products complete; u once Y1 completes.
+  // B and C of a chunk are free once its S/dH/Y2 products complete; u once Y1
+  // completed and the checkpoint staged in its slot has been stored.
   auto issue_bc = [&](int c) {
     const int st = c & 1;
     uint8_t* s = stg0 + st * STAGE;
@@ -149,10 +151,12 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   for (int i = 0; i < 32; ++i) hreg[i] = 0.f;
   float dnext = (tid < Q) ? to_f(delta[(row0 + tid) * H + h]) : 0.f;
   uint32_t mph = 0;
+  bool safe = true;
 
-  // Prologue of chunk c: Lam (cumulative delta*A), delta, and U~ into shared memory.
-  auto prologue = [&](int c) {
-    constexpr int p = 0;
+  // Prologue of chunk c: Lam (cumulative delta*A), delta, the E1 column
+  // factors and U~ into shared memory. Returns whether every 16-step block's
+  // decay span is small enough for the factored exponentials of E1.
+  auto prologue = [&](int c) -> bool {
     const float dcur = dnext;
     if (tid < Q && c + 1 < nck) dnext = to_f(delta[(row0 + (int64_t)(c + 1) * Q + tid) * H + h]);
     float lam = 0.f;
@@ -164,21 +168,29 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
         if (lane >= o) lam += n;
       }
       if (lane == 31) sWarp[warp] = lam;
-      sDel[p * Q + tid] = dcur;
+      sDel[tid] = dcur;
     }
     __syncthreads();
     if (tid < Q) {
       float off = 0.f;
       for (int w = 0; w < warp; ++w) off += sWarp[w];
-      sLam[p * Q + tid] = lam + off;
+      sLam[tid] = lam + off;
     }
     __syncthreads();
-    const float lam_last = sLam[p * Q + Q - 1];
+    // column factor exp(Lam_{s0} - Lam_s) delta_s, s0 = start of s's 16-step block
+    bool wide = false;
+    if (tid < Q) {
+      const float span = sLam[tid & ~15] - sLam[tid];
+      sCF[tid] = __expf(span) * sDel[tid];
+      wide = span > 40.f;
+    }
+    const bool ok = !__syncthreads_or(wide);
+    const float lam_last = sLam[Q - 1];
     const int st = c & 1;
     mbar_wait(&bar[2 + st], (uint32_t)(c >> 1) & 1u);
     const uint8_t* sU = stg0 + st * STAGE;
     const int s = tid >> 1, hf = tid & 1;
-    const float w = __expf(lam_last - sLam[p * Q + s]) * sDel[p * Q + s];
+    const float w = __expf(lam_last - sLam[s]) * sDel[s];
 #pragma unroll
     for (int cc = 0; cc < 4; ++cc) {
       const uint32_t off = umma::sw128_off(s, (hf * 4 + cc) * 8);
@@ -189,16 +201,15 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
       *reinterpret_cast<int4*>(sUt + off) = pack8<T>(f);
     }
     fence_proxy_async_smem();
+    return ok;
   };
 
-  prologue(0);
+  safe = prologue(0);
   for (int c = 0; c < nck; ++c) {
-    const int st = c & 1, p = 0;
+    const int st = c & 1;
     uint8_t* sU = stg0 + st * STAGE;
     uint8_t* sB = sU + TILE;
     uint8_t* sC = sU + 3 * TILE;
-    const float* lamc = sLam + p * Q;
-    const float* delc = sDel + p * Q;
     __syncthreads();  // U~, Lam of chunk c and h^T of chunk c-1 are in shared memory
 
     // ---- S = C B^T, Y2 = C h0^T, dH^T = B^T U~
@@ -226,27 +237,39 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     ++mph;
     umma::fence_after_sync();
 
-    // ---- G[t, s] = S[t, s] exp(Lam_t - Lam_s) delta_s for s <= t
+    // ---- G[t, s] = S[t, s] exp(Lam_t - Lam_s) delta_s for s <= t.
+    // exp(Lam_t - Lam_s) = exp(Lam_t - Lam_s0) * exp(Lam_s0 - Lam_s) with s0 the
+    // start of s's 16-step block: 4 exponentials per thread instead of 64. When
+    // a block spans a decay above e^40 the exact per-element form is used.
     {
       const int t = trow;
+      const int tmax = 32 * q4 + 31;  // last row of this warp
       uint8_t* g = sG + jh * TILE;
-      if (64 * jh > t) {
+      const float lt = sLam[t];
 #pragma unroll
-        for (int ch = 0; ch < 8; ++ch)
-          *reinterpret_cast<int4*>(g + umma::sw128_off(t, ch * 8)) = make_int4(0, 0, 0, 0);
-      } else {
-        float v[64];
-#pragma unroll
-        for (int cb = 0; cb < 4; ++cb) umma::tmem_ld16(tl + 64 * jh + 16 * cb, *reinterpret_cast<float(*)[16]>(v + 16 * cb));
-        umma::tmem_wait_ld();
-        const float lt = lamc[t];
-#pragma unroll
-        for (int i = 0; i < 64; ++i) {
-          const int s = 64 * jh + i;
-          v[i] = (s <= t) ? v[i] * __expf(lt - lamc[s]) * delc[s] : 0.f;
+      for (int cb = 0; cb < 4; ++cb) {
+        const int s0 = 64 * jh + 16 * cb;
+        if (s0 > tmax) {  // above the diagonal for the whole warp
+          *reinterpret_cast<int4*>(g + umma::sw128_off(t, 16 * cb)) = make_int4(0, 0, 0, 0);
+          *reinterpret_cast<int4*>(g + umma::sw128_off(t, 16 * cb + 8)) = make_int4(0, 0, 0, 0);
+          continue;
         }
+        float v[16];
+        umma::tmem_ld16(tl + s0, v);
+        umma::tmem_wait_ld();
+        if (safe) {
+          const float rf = (t >= s0) ? __expf(lt - sLam[s0]) : 0.f;
 #pragma unroll
-        for (int ch = 0; ch < 8; ++ch) *reinterpret_cast<int4*>(g + umma::sw128_off(t, 8 * ch)) = pack8<T>(v + 8 * ch);
+          for (int i = 0; i < 16; ++i) v[i] = (s0 + i <= t) ? v[i] * rf * sCF[s0 + i] : 0.f;
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int s = s0 + i;
+            v[i] = (s <= t) ? v[i] * __expf(lt - sLam[s]) * sDel[s] : 0.f;
+          }
+        }
+        *reinterpret_cast<int4*>(g + umma::sw128_off(t, 16 * cb)) = pack8<T>(v);
+        *reinterpret_cast<int4*>(g + umma::sw128_off(t, 16 * cb + 8)) = pack8<T>(v + 8);
       }
       fence_proxy_async_smem();
     }
@@ -268,8 +291,7 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
 
     // ---- state: h <- exp(Lam_last) h + dH (thread: row n = trow, 32 channels)
     {
-      const int n = trow;
-      const float dec = __expf(lamc[Q - 1]);
+      const float dec = __expf(sLam[Q - 1]);
       float v[32];
       umma::tmem_ld16(tl + 192 + 32 * jh, *reinterpret_cast<float(*)[16]>(v));
       umma::tmem_ld16(tl + 192 + 32 * jh + 16, *reinterpret_cast<float(*)[16]>(v + 16));
@@ -278,46 +300,60 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
       for (int i = 0; i < 32; ++i) hreg[i] = dec * hreg[i] + v[i];
 #pragma unroll
       for (int cc = 0; cc < 4; ++cc)
-        *reinterpret_cast<int4*>(sHt + umma::sw128_off(n, 32 * jh + 8 * cc)) = pack8<T>(hreg + 8 * cc);
-      fence_proxy_async_smem();
-      if (((c + 1) * Q) % seg == 0) {
-        const int si = (c + 1) * Q / seg - 1;
-        float* dst = ckpt + (((int64_t)b * nseg + si) * H + h) * (int64_t)(NS * DH) + (int64_t)n * DH + 32 * jh;
-#pragma unroll
-        for (int i = 0; i < 32; i += 4)
-          __stcs(reinterpret_cast<float4*>(dst + i), make_float4(hreg[i], hreg[i + 1], hreg[i + 2], hreg[i + 3]));
-      }
+        *reinterpret_cast<int4*>(sHt + umma::sw128_off(trow, 32 * jh + 8 * cc)) = pack8<T>(hreg + 8 * cc);
     }
-
-    // ---- next chunk's prologue overlaps the Y1 product (it rewrites Lam)
-    const float e_t = __expf(lamc[trow]);
-    __syncthreads();
-    if (c + 1 < nck) prologue(c + 1);
+    const float e_t = __expf(sLam[trow]);
 
     mbar_wait(&bar[4], mph & 1u);
     ++mph;
     umma::fence_after_sync();
 
-    // ---- y = Y1 + exp(Lam_t) Y2
+    // ---- stage y = Y1 + exp(Lam_t) Y2 in sG, the checkpoint in U~ and u slots
     {
-      const int t = trow;
-      const float e = e_t;
-      float* yr = y + ((row0 + (int64_t)c * Q + t) * H + h) * DH + 32 * jh;
       float a[32], bb[32];
       umma::tmem_ld16(tl + 256 + 32 * jh, *reinterpret_cast<float(*)[16]>(a));
       umma::tmem_ld16(tl + 256 + 32 * jh + 16, *reinterpret_cast<float(*)[16]>(a + 16));
       umma::tmem_ld16(tl + 128 + 32 * jh, *reinterpret_cast<float(*)[16]>(bb));
       umma::tmem_ld16(tl + 128 + 32 * jh + 16, *reinterpret_cast<float(*)[16]>(bb + 16));
       umma::tmem_wait_ld();
+      uint8_t* yb = sG + jh * TILE;  // box [128 t][32 f32]
 #pragma unroll
       for (int i = 0; i < 32; i += 4)
-        __stcs(reinterpret_cast<float4*>(yr + i), make_float4(a[i] + e * bb[i], a[i + 1] + e * bb[i + 1],
-                                                             a[i + 2] + e * bb[i + 2], a[i + 3] + e * bb[i + 3]));
+        *reinterpret_cast<float4*>(yb + umma::sw128_off_f32(trow, i)) =
+            make_float4(a[i] + e_t * bb[i], a[i + 1] + e_t * bb[i + 1], a[i + 2] + e_t * bb[i + 2],
+                        a[i + 3] + e_t * bb[i + 3]);
     }
+    const bool ck = ((c + 1) * Q) % seg == 0;
+    if (ck) {
+      const int n = trow;
+      uint8_t* cb = (n < 64 ? sUt : sU) + jh * (TILE / 2);  // box [64 n][32 f32]
+#pragma unroll
+      for (int i = 0; i < 32; i += 4)
+        *reinterpret_cast<float4*>(cb + umma::sw128_off_f32(n & 63, i)) =
+            make_float4(hreg[i], hreg[i + 1], hreg[i + 2], hreg[i + 3]);
+    }
+    fence_proxy_async_smem();
     umma::fence_before_sync();
-    // u of this stage is free once Y1 completed (waited above)
-    if (tid == 0 && c + 2 < nck) issue_u(c + 2);
+    __syncthreads();
+    if (tid == 0) {
+      const int z = (int)(row0 + (int64_t)c * Q);
+      tma_store_3d(&tm_y, 0, h, z, sG);
+      tma_store_3d(&tm_y, 32, h, z, sG + TILE);
+      if (ck) {
+        const int zz = (int)(((int64_t)b * nseg + (c + 1) * Q / seg - 1) * H + h);
+        tma_store_3d(&tm_ck, 0, 0, zz, sUt);
+        tma_store_3d(&tm_ck, 32, 0, zz, sUt + TILE / 2);
+        tma_store_3d(&tm_ck, 0, 64, zz, sU);
+        tma_store_3d(&tm_ck, 32, 64, zz, sU + TILE / 2);
+      }
+      bulk_commit();
+      bulk_wait_read_all();  // staging slots reusable
+      if (c + 2 < nck) issue_u(c + 2);
+    }
+    __syncthreads();
+    if (c + 1 < nck) safe = prologue(c + 1);
   }
+  if (tid == 0) bulk_wait_all();
   __syncthreads();
   if (warp == 0) umma::tmem_dealloc(tbase, 512);
 }
@@ -355,13 +391,25 @@ template <typename T>
 int ssd_chunk_fwd_launch(const void* u, const void* delta, const void* Bm, const void* Cm, const float* A,
                          int64_t ash, int64_t batch, int64_t L, int64_t H, int64_t seg, float* y,
                          float* ckpt, cudaStream_t st) {
-  CUtensorMap mu, mB, mC;
+  CUtensorMap mu, mB, mC, my, mck;
   if (int rc = ssd_tmaps<T>(u, Bm, Cm, batch, L, H, &mu, &mB, &mC)) return rc;
+  {
+    using namespace ssdc;
+    const auto F32 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    const auto SW = CU_TENSOR_MAP_SWIZZLE_128B;
+    // y [B*L, H, Dh] f32, boxes [128 steps][32 channels]
+    if (int rc = make_tmap_3d(&my, y, F32, 4, DH, H, (uint64_t)batch * L, DH * 4, (uint64_t)H * DH * 4, 32, 1, Q, SW))
+      return rc;
+    // h_ckpt [B*nSeg*H, N, Dh] f32, boxes [64 states][32 channels]
+    if (int rc = make_tmap_3d(&mck, ckpt, F32, 4, DH, NS, (uint64_t)batch * (L / seg) * H, DH * 4,
+                              (uint64_t)NS * DH * 4, 32, 64, 1, SW))
+      return rc;
+  }
   auto k = ssd_chunk_fwd_kernel<T>;
   const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssdc::SMEM);
   if (e != cudaSuccess) return set_error(MR_E_LAUNCH, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-  k<<<(unsigned)(batch * H), 256, ssdc::SMEM, st>>>(mu, mB, mC, (const T*)delta, A, ash, (int)L, (int)H, (int)seg,
-                                                    y, ckpt);
+  k<<<(unsigned)(batch * H), 256, ssdc::SMEM, st>>>(mu, mB, mC, my, mck, (const T*)delta, A, ash, (int)L, (int)H,
+                                                    (int)seg);
   return check_launch("ssd_chunk_fwd_kernel");
 }
 

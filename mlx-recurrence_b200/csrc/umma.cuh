@@ -113,5 +113,12 @@ __device__ __forceinline__ uint32_t sw128_off(uint32_t row, uint32_t col) {
   return row * 128u + chunk * 16u + (col & 7) * 2u;
 }
 
+// Byte offset of float (row, col) in a 128B-swizzled tile of 32-float
+// (128-byte) rows: TMA's CU_TENSOR_MAP_SWIZZLE_128B layout for 4-byte data.
+__device__ __forceinline__ uint32_t sw128_off_f32(uint32_t row, uint32_t col) {
+  const uint32_t chunk = (col >> 2) ^ (row & 7);
+  return row * 128u + chunk * 16u + (col & 3) * 4u;
+}
+
 }  // namespace umma
 }  // namespace mr
