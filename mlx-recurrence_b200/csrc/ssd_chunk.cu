@@ -462,14 +462,14 @@ constexpr size_t SMEM = SMALL + 1023 + NTILE * TILE;
 template <typename T>
 __global__ void __launch_bounds__(256, 1)
 ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_constant__ CUtensorMap tm_B,
-                     const __grid_constant__ CUtensorMap tm_C, const float* __restrict__ gy,
-                     const float* __restrict__ gfinal, const float* __restrict__ ckpt,
-                     const T* __restrict__ delta, const float* __restrict__ A, int64_t ash, int L, int H,
-                     int seg, T* __restrict__ gu, T* __restrict__ gdelta, T* __restrict__ gB,
-                     T* __restrict__ gC, float* __restrict__ gA_part) {
+                     const __grid_constant__ CUtensorMap tm_C, const __grid_constant__ CUtensorMap tm_gu,
+                     const __grid_constant__ CUtensorMap tm_gB, const __grid_constant__ CUtensorMap tm_gC,
+                     const __grid_constant__ CUtensorMap tm_ck, const float* __restrict__ gy,
+                     const float* __restrict__ gfinal, const T* __restrict__ delta, const float* __restrict__ A,
+                     int64_t ash, int L, int H, int seg, T* __restrict__ gdelta, float* __restrict__ gA_part) {
   using namespace ssdb;
   extern __shared__ unsigned char smem_raw[];
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem_raw);  // tma, mma
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem_raw);  // tma(u,B,C), mma, ckpt
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 4);
   float* sLam = reinterpret_cast<float*>(tslot + 4);  // Lam_t
   float* sDel = sLam + Q;                             // delta_t
@@ -480,19 +480,20 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   float* sCol = sRow + 2 * Q;                         // [2][Q]
   float* sQ = sCol + 2 * Q;                           // [2][Q] gy.Y2 partials
   float* sRed = sQ + 2 * Q;                           // 64 floats of reduction scratch
-  // m_t = u_t.R2_t and ur_t = u_t.r_t partials reuse sRow/sCol after use (see below)
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sRed + 64) + 1023) & ~uintptr_t(1023));
   uint8_t* tU = sm;
   uint8_t* tB = tU + TILE;        // 2 tiles
   uint8_t* tC = tB + 2 * TILE;    // 2 tiles
   uint8_t* tGY = tC + 2 * TILE;   // gy bf16 [s][d]
-  uint8_t* tGYt = tGY + TILE;     // exp(Lam_s) gy [s][d]
+  uint8_t* tGYt = tGY + TILE;     // exp(Lam_s) gy [s][d]; gy lo part in batch 2; then grad_u staging
   uint8_t* tPSI = tGYt + TILE;    // Psi^T bf16 [n][d]
   uint8_t* tH0 = tPSI + TILE;     // h0^T bf16 [n][d]
-  uint8_t* tGP = tH0 + TILE;      // G' [s][t], 2 tiles (t halves)
-  uint8_t* tHH = tGP + 2 * TILE;  // H1 [s][t], 2 tiles
+  uint8_t* tGP = tH0 + TILE;      // G' [s][t], 2 tiles (t halves); then grad_B staging
+  uint8_t* tHH = tGP + 2 * TILE;  // H1 [s][t], 2 tiles; then grad_C staging; then h0 f32 prefetch
   __shared__ float sM[2][Q];      // u_t . R2_t partials
   __shared__ float sUR[2][Q];     // u_t . r_t partials
+  __shared__ float sCF1[Q];       // exp(Lam_t0 - Lam_t), t0 = start of t's 16-step block
+  __shared__ float sCF2[Q];       // exp(Lam_t - Lam_t0)
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bh = blockIdx.x;
@@ -510,9 +511,9 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
 
   const int q4 = warp & 3, jh = warp >> 2;
   const int row = 32 * q4 + lane;  // the row (s, t or n) this thread owns in TMEM
+  const int rmax = 32 * q4 + 31;   // last row of this warp
   if (tid == 0) {
-    mbar_init(&bar[0], 1);
-    mbar_init(&bar[1], 1);
+    for (int i = 0; i < 3; ++i) mbar_init(&bar[i], 1);
     fence_mbar_init();
   }
   if (warp == 0) {
@@ -542,7 +543,19 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     tma_load_3d(tC, &tm_C, 0, h, z, &bar[0]);
     tma_load_3d(tC + TILE, &tm_C, 64, h, z, &bar[0]);
   };
-  if (tid == 0) issue(nck - 1);
+  // h0 of chunk c (= checkpoint c-1, f32 [N][Dh]) into the HH tiles: boxes [64 n][32 d]
+  auto issue_h0 = [&](int c) {
+    const int zz = (int)(((int64_t)b * nseg + (c * Q) / seg - 1) * H + h);
+    mbar_arrive_expect_tx(&bar[2], 2 * TILE);
+    tma_load_3d(tHH, &tm_ck, 0, 0, zz, &bar[2]);
+    tma_load_3d(tHH + TILE / 2, &tm_ck, 32, 0, zz, &bar[2]);
+    tma_load_3d(tHH + TILE, &tm_ck, 0, 64, zz, &bar[2]);
+    tma_load_3d(tHH + TILE + TILE / 2, &tm_ck, 32, 64, zz, &bar[2]);
+  };
+  if (tid == 0) {
+    issue(nck - 1);
+    if (nck > 1) issue_h0(nck - 1);
+  }
 
   // grad_y rows (thread: row s, channels 32*jh..) and delta of the first chunk processed
   float gyr[32];
@@ -560,7 +573,7 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   load_gy(nck - 1);
   float dnext = (tid < Q) ? to_f(delta[(row0 + (int64_t)(nck - 1) * Q + tid) * H + h]) : 0.f;
   float gA_acc = 0.f;
-  uint32_t tph = 0, mph = 0;
+  uint32_t tph = 0, mph = 0, hph = 0;
 
   auto block_sum = [&](float v) -> float {  // sum over all 256 threads
 #pragma unroll
@@ -575,7 +588,8 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   };
 
   for (int c = nck - 1; c >= 0; --c) {
-    // ---- P0: Lam, D, w, exp(Lam); h0 (previous checkpoint); gy tiles
+    // ---- P0: Lam, D, w, exp(Lam), exponential factors; h0; gy tiles
+    bool safe;
     {
       const float dcur = dnext;
       if (tid < Q && c > 0) dnext = to_f(delta[(row0 + (int64_t)(c - 1) * Q + tid) * H + h]);
@@ -609,18 +623,25 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
         sD[tid] = dsum + o2;
       }
       __syncthreads();
+      bool wide = false;
       if (tid < Q) {
         sW[tid] = __expf(sLam[Q - 1] - sLam[tid]) * sDel[tid];
         sEL[tid] = __expf(sLam[tid]);
+        const float span = sLam[tid & ~15] - sLam[tid];
+        sCF1[tid] = __expf(span);
+        sCF2[tid] = __expf(-span);
+        wide = span > 40.f;
       }
+      safe = !__syncthreads_or(wide);  // also publishes sEL / sW / sCF
     }
     float h0f[32];
     if (c > 0) {
-      const float* src = ckpt + (((int64_t)b * nseg + (c * Q) / seg - 1) * H + h) * (int64_t)(NS * DH) +
-                         (int64_t)row * DH + 32 * jh;
+      mbar_wait(&bar[2], hph & 1u);
+      ++hph;
+      const uint8_t* hb = tHH + (row >= 64 ? TILE : 0) + jh * (TILE / 2);
 #pragma unroll
       for (int i = 0; i < 32; i += 4) {
-        const float4 v = *reinterpret_cast<const float4*>(src + i);
+        const float4 v = *reinterpret_cast<const float4*>(hb + umma::sw128_off_f32(row & 63, i));
         h0f[i] = v.x;
         h0f[i + 1] = v.y;
         h0f[i + 2] = v.z;
@@ -636,7 +657,6 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
 #pragma unroll
     for (int cc = 0; cc < 4; ++cc)
       *reinterpret_cast<int4*>(tH0 + umma::sw128_off(row, 32 * jh + 8 * cc)) = pack8<T>(h0f + 8 * cc);
-    __syncthreads();  // sEL ready
     {
       // gy enters the S/P products as hi + lo 2-byte parts (P, P^T and R1 carry
       // about 16 mantissa bits; dA/d-delta sum many of these terms)
@@ -667,7 +687,7 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
       ++tph;
       umma::fence_after_sync();
       const uint32_t aU = smem_u32(tU), aB = smem_u32(tB), aC = smem_u32(tC), aGY = smem_u32(tGY),
-                     aGYt = smem_u32(tGYt), aPSI = smem_u32(tPSI), aH0 = smem_u32(tH0);
+                     aGYt = smem_u32(tGYt), aPSI = smem_u32(tPSI), aH0 = smem_u32(tH0), aLo = smem_u32(tGP);
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
         const uint32_t ko = (k >> 2) * TILE + (k & 3) * 32;
@@ -677,7 +697,6 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
         umma::mma_f16(tbase + 384, umma::sdesc_mn(aC + k * 2048, TILE), umma::sdesc_mn(aGYt + k * 2048, TILE),
                       id64MM, k > 0);
       }
-      const uint32_t aLo = smem_u32(tGP);
 #pragma unroll
       for (int k = 0; k < 4; ++k)
         umma::mma_f16(tbase + 128, umma::sdesc_k(aGY + k * 32), umma::sdesc_k(aU + k * 32), id128KK, k > 0);
@@ -699,43 +718,45 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     __syncthreads();
 
     // ---- epilogue 1 (thread: row s, t-half jh): G', H1, rowsum Z; gy.Y2; u.R2
+    // exp(Lam_s - Lam_t) = exp(Lam_s - Lam_t0) * exp(Lam_t0 - Lam_t), t0 = block start
     {
       const int s = row;
       const float ls = sLam[s];
       float rz = 0.f;
       uint8_t* gp = tGP + jh * TILE;
       uint8_t* hh = tHH + jh * TILE;
-      if (64 * jh > s) {
 #pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {
-          *reinterpret_cast<int4*>(gp + umma::sw128_off(s, 8 * ch)) = make_int4(0, 0, 0, 0);
-          *reinterpret_cast<int4*>(hh + umma::sw128_off(s, 8 * ch)) = make_int4(0, 0, 0, 0);
+      for (int cb = 0; cb < 4; ++cb) {
+        const int t0 = 64 * jh + 16 * cb;
+        if (t0 > rmax) {
+          *reinterpret_cast<int4*>(gp + umma::sw128_off(s, 16 * cb)) = make_int4(0, 0, 0, 0);
+          *reinterpret_cast<int4*>(gp + umma::sw128_off(s, 16 * cb + 8)) = make_int4(0, 0, 0, 0);
+          *reinterpret_cast<int4*>(hh + umma::sw128_off(s, 16 * cb)) = make_int4(0, 0, 0, 0);
+          *reinterpret_cast<int4*>(hh + umma::sw128_off(s, 16 * cb + 8)) = make_int4(0, 0, 0, 0);
+          continue;
         }
-      } else {
+        float sv[16], pv[16];
+        umma::tmem_ld16(tl + t0, sv);
+        umma::tmem_ld16(tl + 128 + t0, pv);
+        umma::tmem_wait_ld();
+        const float rf = (safe && s >= t0) ? __expf(ls - sLam[t0]) : 0.f;
 #pragma unroll
-        for (int cb = 0; cb < 4; ++cb) {
-          float sv[16], pv[16];
-          umma::tmem_ld16(tl + 64 * jh + 16 * cb, sv);
-          umma::tmem_ld16(tl + 128 + 64 * jh + 16 * cb, pv);
-          umma::tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int t = 64 * jh + 16 * cb + i;
-            const float e = (t <= s) ? __expf(ls - sLam[t]) : 0.f;
-            const float g = sv[i] * e;
-            const float h1 = pv[i] * e * sDel[t];
-            rz += sv[i] * h1;
-            sv[i] = g;
-            pv[i] = h1;
-          }
-          *reinterpret_cast<int4*>(gp + umma::sw128_off(s, 16 * cb)) = pack8<T>(sv);
-          *reinterpret_cast<int4*>(gp + umma::sw128_off(s, 16 * cb + 8)) = pack8<T>(sv + 8);
-          *reinterpret_cast<int4*>(hh + umma::sw128_off(s, 16 * cb)) = pack8<T>(pv);
-          *reinterpret_cast<int4*>(hh + umma::sw128_off(s, 16 * cb + 8)) = pack8<T>(pv + 8);
+        for (int i = 0; i < 16; ++i) {
+          const int t = t0 + i;
+          const float e = (t <= s) ? (safe ? rf * sCF1[t] : __expf(ls - sLam[t])) : 0.f;
+          const float g = sv[i] * e;
+          const float h1 = pv[i] * e * sDel[t];
+          rz += sv[i] * h1;
+          sv[i] = g;
+          pv[i] = h1;
         }
+        *reinterpret_cast<int4*>(gp + umma::sw128_off(s, 16 * cb)) = pack8<T>(sv);
+        *reinterpret_cast<int4*>(gp + umma::sw128_off(s, 16 * cb + 8)) = pack8<T>(sv + 8);
+        *reinterpret_cast<int4*>(hh + umma::sw128_off(s, 16 * cb)) = pack8<T>(pv);
+        *reinterpret_cast<int4*>(hh + umma::sw128_off(s, 16 * cb + 8)) = pack8<T>(pv + 8);
       }
       sRow[jh * Q + s] = rz;
-      // gy_s . Y2_s over this thread's 32 channels
+      // gy_s . Y2_s over this thread's 32 channels; u_t . R2_t
       float y2[32];
       umma::tmem_ld16(tl + 256 + 32 * jh, *reinterpret_cast<float(*)[16]>(y2));
       umma::tmem_ld16(tl + 256 + 32 * jh + 16, *reinterpret_cast<float(*)[16]>(y2 + 16));
@@ -786,22 +807,26 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     ++mph;
     umma::fence_after_sync();
 
-    // ---- epilogue 2 (thread: row t): colsum Z; r, grad_u, u.r; Psi update (row n)
+    // ---- epilogue 2 (thread: row t): colsum Z; r, grad_u (staged in GYt), u.r; Psi update (row n)
     {
       const int t = row;
       const float lt = sLam[t], dt = sDel[t];
       float cz = 0.f;
-      if (64 * jh + 63 >= t) {
+      if (64 * jh + 63 >= 32 * q4) {
 #pragma unroll
         for (int cb = 0; cb < 4; ++cb) {
+          const int s0 = 64 * jh + 16 * cb;
+          if (s0 + 15 < 32 * q4) continue;  // the whole block is below every row of this warp
           float sv[16], pv[16];
-          umma::tmem_ld16(tl + 64 * jh + 16 * cb, sv);
-          umma::tmem_ld16(tl + 128 + 64 * jh + 16 * cb, pv);
+          umma::tmem_ld16(tl + s0, sv);
+          umma::tmem_ld16(tl + 128 + s0, pv);
           umma::tmem_wait_ld();
+          // exp(Lam_s - Lam_t) = exp(Lam_s0 - Lam_t) * exp(Lam_s - Lam_s0) for s >= t
+          const float rf = safe ? __expf(fminf(sLam[s0] - lt, 88.f)) : 0.f;
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            const int s = 64 * jh + 16 * cb + i;
-            const float e = (s >= t) ? __expf(sLam[s] - lt) : 0.f;
+            const int s = s0 + i;
+            const float e = (s >= t) ? (safe ? rf * sCF2[s] : __expf(sLam[s] - lt)) : 0.f;
             cz += sv[i] * pv[i] * e;
           }
         }
@@ -818,28 +843,29 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
       const float f2 = __expf(sLam[Q - 1] - lt);
       const float dec = __expf(sLam[Q - 1]);
       float ur = 0.f;
-      T* gup = gu + ((row0 + (int64_t)c * Q + t) * H + h) * DH + 32 * jh;
 #pragma unroll
       for (int cc = 0; cc < 4; ++cc) {
+        const uint32_t off = umma::sw128_off(t, 32 * jh + 8 * cc);
         float f[8], o[8];
-        unpack8<T>(*reinterpret_cast<const int4*>(tU + umma::sw128_off(t, 32 * jh + 8 * cc)), f);
+        unpack8<T>(*reinterpret_cast<const int4*>(tU + off), f);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const float rv = r1[8 * cc + i] + f2 * r2[8 * cc + i];
           ur += f[i] * rv;
           o[i] = dt * rv;
         }
-        *reinterpret_cast<int4*>(gup + 8 * cc) = pack8<T>(o);
+        *reinterpret_cast<int4*>(tGYt + off) = pack8<T>(o);  // grad_u staging (GYt free after batch 2)
       }
       sUR[jh][t] = ur;
       // Psi (row n = row) <- exp(Lam_last) Psi + dPsi; the bf16 copy is replaced after batch 3
 #pragma unroll
       for (int i = 0; i < 32; ++i) psi[i] = dec * psi[i] + dp[i];
+      fence_proxy_async_smem();
     }
     umma::fence_before_sync();
     __syncthreads();
 
-    // ---- batch 3: gB1 = H1^T C, gC1 = H1 B, gB2 = u Psi(old), gC2 = gy h0
+    // ---- batch 3: gB1 = H1^T C, gC1 = H1 B, gB2 = u Psi(old), gC2 = gy h0; store grad_u
     if (tid == 0) {
       umma::fence_after_sync();
       const uint32_t aU = smem_u32(tU), aB = smem_u32(tB), aC = smem_u32(tC), aGY = smem_u32(tGY),
@@ -857,6 +883,8 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
         umma::mma_f16(tbase + 256, umma::sdesc_k(aU + k * 32), umma::sdesc_k(aPSI + k * 32), id128KK, k > 0);
       }
       umma::commit(&bar[1]);
+      tma_store_3d(&tm_gu, 0, h, (int)(row0 + (int64_t)c * Q), tGYt);
+      bulk_commit();
     }
     // ---- grad_delta and grad_A while batch 3 runs (thread t < Q)
     {
@@ -898,12 +926,12 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     }
     if (c > 0) load_gy(c - 1);
 
-    // ---- epilogue 3 (thread: row t for gB, row s for gC; 64 columns per half)
+    // ---- epilogue 3: stage grad_B (row t) in GP, grad_C (row s) in HH; new Psi^T
     {
       const int t = row;
       const float wt = sW[t], et = sEL[t];
-      T* gbp = gB + ((row0 + (int64_t)c * Q + t) * H + h) * NS + 64 * jh;
-      T* gcp = gC + ((row0 + (int64_t)c * Q + t) * H + h) * NS + 64 * jh;
+      uint8_t* gbt = tGP + jh * TILE;
+      uint8_t* gct = tHH + jh * TILE;
 #pragma unroll
       for (int cb = 0; cb < 4; ++cb) {
         float b1[16], b2[16], cv[16], c2[16];
@@ -917,10 +945,10 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
           b1[i] += wt * b2[i];
           cv[i] += et * c2[i];
         }
-        *reinterpret_cast<int4*>(gbp + 16 * cb) = pack8<T>(b1);
-        *reinterpret_cast<int4*>(gbp + 16 * cb + 8) = pack8<T>(b1 + 8);
-        *reinterpret_cast<int4*>(gcp + 16 * cb) = pack8<T>(cv);
-        *reinterpret_cast<int4*>(gcp + 16 * cb + 8) = pack8<T>(cv + 8);
+        *reinterpret_cast<int4*>(gbt + umma::sw128_off(t, 16 * cb)) = pack8<T>(b1);
+        *reinterpret_cast<int4*>(gbt + umma::sw128_off(t, 16 * cb + 8)) = pack8<T>(b1 + 8);
+        *reinterpret_cast<int4*>(gct + umma::sw128_off(t, 16 * cb)) = pack8<T>(cv);
+        *reinterpret_cast<int4*>(gct + umma::sw128_off(t, 16 * cb + 8)) = pack8<T>(cv + 8);
       }
       // Psi's bf16 copy for the next chunk (its readers in batches 1 and 3 are done)
 #pragma unroll
@@ -930,8 +958,22 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     }
     umma::fence_before_sync();
     __syncthreads();
+    if (tid == 0) {
+      const int z = (int)(row0 + (int64_t)c * Q);
+      tma_store_3d(&tm_gB, 0, h, z, tGP);
+      tma_store_3d(&tm_gB, 64, h, z, tGP + TILE);
+      tma_store_3d(&tm_gC, 0, h, z, tHH);
+      tma_store_3d(&tm_gC, 64, h, z, tHH + TILE);
+      bulk_commit();
+      bulk_wait_read_all();  // GP, HH and GYt are reusable
+      if (c > 1) issue_h0(c - 1);
+    }
+    __syncthreads();
   }
-  if (tid == 0) gA_part[bh] = gA_acc;
+  if (tid == 0) {
+    gA_part[bh] = gA_acc;
+    bulk_wait_all();
+  }
   __syncthreads();
   if (warp == 0) umma::tmem_dealloc(tbase, 512);
 }
@@ -951,13 +993,22 @@ int ssd_chunk_bwd_launch(const float* gy, const float* gf, const float* ckpt, co
                          const void* Bm, const void* Cm, const float* A, int64_t ash, int64_t batch, int64_t L,
                          int64_t H, int64_t seg, void* gu, void* gd, void* gB, void* gC, float* gA,
                          float* ws, cudaStream_t st) {
-  CUtensorMap mu, mB, mC;
+  CUtensorMap mu, mB, mC, mgu, mgB, mgC, mck;
   if (int rc = ssd_tmaps<T>(u, Bm, Cm, batch, L, H, &mu, &mB, &mC)) return rc;
+  if (int rc = ssd_tmaps<T>(gu, gB, gC, batch, L, H, &mgu, &mgB, &mgC)) return rc;
+  {
+    using namespace ssdb;
+    // h_ckpt [B*nSeg*H, N, Dh] f32, boxes [64 states][32 channels]
+    if (int rc = make_tmap_3d(&mck, ckpt, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, DH, NS,
+                              (uint64_t)batch * (L / seg) * H, DH * 4, (uint64_t)NS * DH * 4, 32, 64, 1,
+                              CU_TENSOR_MAP_SWIZZLE_128B))
+      return rc;
+  }
   auto k = ssd_chunk_bwd_kernel<T>;
   const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssdb::SMEM);
   if (e != cudaSuccess) return set_error(MR_E_LAUNCH, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-  k<<<(unsigned)(batch * H), 256, ssdb::SMEM, st>>>(mu, mB, mC, gy, gf, ckpt, (const T*)delta, A, ash, (int)L,
-                                                    (int)H, (int)seg, (T*)gu, (T*)gd, (T*)gB, (T*)gC, ws);
+  k<<<(unsigned)(batch * H), 256, ssdb::SMEM, st>>>(mu, mB, mC, mgu, mgB, mgC, mck, gy, gf, (const T*)delta, A, ash,
+                                                    (int)L, (int)H, (int)seg, (T*)gd, ws);
   if (int rc = check_launch("ssd_chunk_bwd_kernel")) return rc;
   const int HN = (int)(H * ssdb::NS);
   ssd_ga_head_kernel<<<(HN + 255) / 256, 256, 0, st>>>(ws, (int)batch, (int)H, ssdb::NS, gA);
