@@ -20,7 +20,7 @@
 // One CTA owns one (batch, head) and walks its L/Q chunks in order. u, B and C
 // of the next chunk stream in by TMA (128B-swizzled boxes [128 steps x 64])
 // while the current chunk computes. The running state h stays in registers
-// in float32 (thread = state row n, 32 channels); its bf16 copy in shared
+// in float32 (thread = state row n, 16 channels); its bf16 copy in shared
 // memory is the operand of the next chunk's Y2 product, and it is written to
 // h_ckpt in float32 at segment ends (seg a multiple of Q).
 #include <mutex>
@@ -38,6 +38,8 @@ constexpr int DH = 64;                 // head dim (one 128-byte swizzle row)
 constexpr int NS = 128;                // state size N
 constexpr uint32_t TILE = 16384;       // [128 rows x 64 elements] 2-byte tile
 constexpr uint32_t STAGE = TILE * 5;   // u, B lo/hi, C lo/hi
+constexpr int NT = 512;                // threads: 16 warps
+constexpr int CH = 16;                 // state / y channels per thread
 // small arrays (Lam, delta, warp sums, barriers, TMEM slot) first, then the
 // 1024-byte-aligned tiles
 constexpr size_t SMALL = (3 * Q + 8) * 4 + 6 * 8 + 16;
@@ -53,6 +55,60 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
   const T x = from_f<T>(a), y = from_f<T>(b);
   return (uint32_t)(*reinterpret_cast<const uint16_t*>(&x)) |
          ((uint32_t)(*reinterpret_cast<const uint16_t*>(&y)) << 16);
+}
+
+// Streaming global loads pinned in program order. The proxy fences that hand
+// shared-memory tiles to the tensor cores wait for the issuing thread's
+// outstanding loads, so register prefetches are placed right after a fence;
+// as volatile asm the compiler cannot move them back above it.
+__device__ __forceinline__ float4 ld_pinned_f4(const float* p) {
+  float4 v;
+  asm volatile("ld.global.cs.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(p));
+  return v;
+}
+// raw 16-bit load: converted only where it is used, so the load does not stall here
+template <typename T>
+__device__ __forceinline__ unsigned short ld_pinned_u16(const T* p) {
+  unsigned short r;
+  asm volatile("ld.global.cs.u16 %0, [%1];" : "=h"(r) : "l"(p));
+  return r;
+}
+template <typename T>
+__device__ __forceinline__ float u16_to_f(unsigned short r) {
+  return to_f(*reinterpret_cast<const T*>(&r));
+}
+
+// Column sums of a warp's 32 x 16 block (lane = row, z = the lane's 16
+// columns), by a transposing butterfly: lanes 2c and 2c + 1 return the sum of
+// column c over all 32 lanes (16 shuffles instead of 16 full reductions).
+__device__ __forceinline__ float warp_colsum16(const float (&z)[16], int lane) {
+  float a8[8], a4[4], a2[2];
+  const bool b16 = lane & 16, b8 = lane & 8, b4 = lane & 4, b2 = lane & 2;
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    a8[i] = (b16 ? z[i + 8] : z[i]) + __shfl_xor_sync(0xffffffffu, b16 ? z[i] : z[i + 8], 16);
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    a4[i] = (b8 ? a8[i + 4] : a8[i]) + __shfl_xor_sync(0xffffffffu, b8 ? a8[i] : a8[i + 4], 8);
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+    a2[i] = (b4 ? a4[i + 2] : a4[i]) + __shfl_xor_sync(0xffffffffu, b4 ? a4[i] : a4[i + 2], 4);
+  const float a1 = (b2 ? a2[1] : a2[0]) + __shfl_xor_sync(0xffffffffu, b2 ? a2[0] : a2[1], 2);
+  return a1 + __shfl_xor_sync(0xffffffffu, a1, 1);
+}
+
+template <typename T>
+__device__ __forceinline__ uint2 pack4(const float4& f) {
+  return make_uint2(pack2<T>(f.x, f.y), pack2<T>(f.z, f.w));
+}
+
+template <typename T>
+__device__ __forceinline__ void unpack4(const uint2& v, float (&f)[4]) {
+  const T* p = reinterpret_cast<const T*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) f[i] = to_f(p[i]);
 }
 
 template <typename T>
@@ -73,7 +129,7 @@ __device__ __forceinline__ int4 pack8(const float* f) {
 }
 
 template <typename T>
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(ssdc::NT, 1)
 ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_constant__ CUtensorMap tm_B,
                      const __grid_constant__ CUtensorMap tm_C, const __grid_constant__ CUtensorMap tm_y,
                      const __grid_constant__ CUtensorMap tm_ck, const T* __restrict__ delta,
@@ -113,7 +169,7 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     umma::tmem_relinquish();
   }
   // h0 = 0 for the first chunk's Y2 product
-  for (int i = tid; i < (int)(TILE / 16); i += 256) reinterpret_cast<int4*>(sHt)[i] = make_int4(0, 0, 0, 0);
+  for (int i = tid; i < (int)(TILE / 16); i += NT) reinterpret_cast<int4*>(sHt)[i] = make_int4(0, 0, 0, 0);
   fence_proxy_async_smem();
   __syncthreads();
   umma::fence_after_sync();
@@ -143,13 +199,18 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     }
   }
 
-  const int q4 = warp & 3, jh = warp >> 2;  // TMEM lane quarter, column half
-  const int trow = 32 * q4 + lane;          // row t (or n) this thread owns
+  // warp w reads TMEM lanes 32*(w%4).. and owns column quarter w/4 of each
+  // row-wise epilogue: 32 of the 128 s-columns of G, 16 of the 64 channels
+  const int q4 = warp & 3, jq = warp >> 2;
+  const int trow = 32 * q4 + lane;  // row t (or n) this thread owns
+  const int ch0 = CH * jq;          // first channel of this thread
+  const int cq0 = 32 * jq;          // first s-column of this thread
+  const int ct0 = cq0 & 63;         // that column inside its 64-column G tile
   const uint32_t tl = tbase + ((uint32_t)(32 * q4) << 16);
-  float hreg[32];
+  float hreg[CH];
 #pragma unroll
-  for (int i = 0; i < 32; ++i) hreg[i] = 0.f;
-  float dnext = (tid < Q) ? to_f(delta[(row0 + tid) * H + h]) : 0.f;
+  for (int i = 0; i < CH; ++i) hreg[i] = 0.f;
+  unsigned short dnext = (tid < Q) ? ld_pinned_u16(delta + (row0 + tid) * H + h) : (unsigned short)0;
   uint32_t mph = 0;
   bool safe = true;
 
@@ -157,8 +218,7 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   // factors and U~ into shared memory. Returns whether every 16-step block's
   // decay span is small enough for the factored exponentials of E1.
   auto prologue = [&](int c) -> bool {
-    const float dcur = dnext;
-    if (tid < Q && c + 1 < nck) dnext = to_f(delta[(row0 + (int64_t)(c + 1) * Q + tid) * H + h]);
+    const float dcur = u16_to_f<T>(dnext);
     float lam = 0.f;
     if (tid < Q) {
       lam = dcur * Ah;
@@ -184,16 +244,22 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
       sCF[tid] = __expf(span) * sDel[tid];
       wide = span > 40.f;
     }
+    // the previous chunk's bulk stores must have read the y and checkpoint
+    // staging (G, U~ and u slots) before U~ and chunk c+1's u overwrite them
+    if (tid == 0 && c > 0) {
+      bulk_wait_read_all();
+      if (c + 1 < nck) issue_u(c + 1);
+    }
     const bool ok = !__syncthreads_or(wide);
     const float lam_last = sLam[Q - 1];
     const int st = c & 1;
     mbar_wait(&bar[2 + st], (uint32_t)(c >> 1) & 1u);
     const uint8_t* sU = stg0 + st * STAGE;
-    const int s = tid >> 1, hf = tid & 1;
+    const int s = tid >> 2, part = tid & 3;  // row s, channels 16*part..
     const float w = __expf(lam_last - sLam[s]) * sDel[s];
 #pragma unroll
-    for (int cc = 0; cc < 4; ++cc) {
-      const uint32_t off = umma::sw128_off(s, (hf * 4 + cc) * 8);
+    for (int cc = 0; cc < 2; ++cc) {
+      const uint32_t off = umma::sw128_off(s, part * 16 + cc * 8);
       float f[8];
       unpack8<T>(*reinterpret_cast<const int4*>(sU + off), f);
 #pragma unroll
@@ -201,6 +267,9 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
       *reinterpret_cast<int4*>(sUt + off) = pack8<T>(f);
     }
     fence_proxy_async_smem();
+    // the next chunk's delta (a proxy fence waits for outstanding loads, so
+    // it is issued after the fence)
+    if (tid < Q && c + 1 < nck) dnext = ld_pinned_u16(delta + (row0 + (int64_t)(c + 1) * Q + tid) * H + h);
     return ok;
   };
 
@@ -244,14 +313,15 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     {
       const int t = trow;
       const int tmax = 32 * q4 + 31;  // last row of this warp
-      uint8_t* g = sG + jh * TILE;
+      uint8_t* g = sG + (jq >> 1) * TILE;
       const float lt = sLam[t];
 #pragma unroll
-      for (int cb = 0; cb < 4; ++cb) {
-        const int s0 = 64 * jh + 16 * cb;
+      for (int cb = 0; cb < 2; ++cb) {
+        const int s0 = cq0 + 16 * cb;
+        const uint32_t o0 = umma::sw128_off(t, ct0 + 16 * cb), o1 = umma::sw128_off(t, ct0 + 16 * cb + 8);
         if (s0 > tmax) {  // above the diagonal for the whole warp
-          *reinterpret_cast<int4*>(g + umma::sw128_off(t, 16 * cb)) = make_int4(0, 0, 0, 0);
-          *reinterpret_cast<int4*>(g + umma::sw128_off(t, 16 * cb + 8)) = make_int4(0, 0, 0, 0);
+          *reinterpret_cast<int4*>(g + o0) = make_int4(0, 0, 0, 0);
+          *reinterpret_cast<int4*>(g + o1) = make_int4(0, 0, 0, 0);
           continue;
         }
         float v[16];
@@ -268,8 +338,8 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
             v[i] = (s <= t) ? v[i] * __expf(lt - sLam[s]) * sDel[s] : 0.f;
           }
         }
-        *reinterpret_cast<int4*>(g + umma::sw128_off(t, 16 * cb)) = pack8<T>(v);
-        *reinterpret_cast<int4*>(g + umma::sw128_off(t, 16 * cb + 8)) = pack8<T>(v + 8);
+        *reinterpret_cast<int4*>(g + o0) = pack8<T>(v);
+        *reinterpret_cast<int4*>(g + o1) = pack8<T>(v + 8);
       }
       fence_proxy_async_smem();
     }
@@ -289,18 +359,17 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
       if (c + 2 < nck) issue_bc(c + 2);
     }
 
-    // ---- state: h <- exp(Lam_last) h + dH (thread: row n = trow, 32 channels)
+    // ---- state: h <- exp(Lam_last) h + dH (thread: row n = trow, channels ch0..)
     {
       const float dec = __expf(sLam[Q - 1]);
-      float v[32];
-      umma::tmem_ld16(tl + 192 + 32 * jh, *reinterpret_cast<float(*)[16]>(v));
-      umma::tmem_ld16(tl + 192 + 32 * jh + 16, *reinterpret_cast<float(*)[16]>(v + 16));
+      float v[CH];
+      umma::tmem_ld16(tl + 192 + ch0, v);
       umma::tmem_wait_ld();
 #pragma unroll
-      for (int i = 0; i < 32; ++i) hreg[i] = dec * hreg[i] + v[i];
+      for (int i = 0; i < CH; ++i) hreg[i] = dec * hreg[i] + v[i];
 #pragma unroll
-      for (int cc = 0; cc < 4; ++cc)
-        *reinterpret_cast<int4*>(sHt + umma::sw128_off(trow, 32 * jh + 8 * cc)) = pack8<T>(hreg + 8 * cc);
+      for (int cc = 0; cc < CH / 8; ++cc)
+        *reinterpret_cast<int4*>(sHt + umma::sw128_off(trow, ch0 + 8 * cc)) = pack8<T>(hreg + 8 * cc);
     }
     const float e_t = __expf(sLam[trow]);
 
@@ -310,26 +379,24 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
 
     // ---- stage y = Y1 + exp(Lam_t) Y2 in sG, the checkpoint in U~ and u slots
     {
-      float a[32], bb[32];
-      umma::tmem_ld16(tl + 256 + 32 * jh, *reinterpret_cast<float(*)[16]>(a));
-      umma::tmem_ld16(tl + 256 + 32 * jh + 16, *reinterpret_cast<float(*)[16]>(a + 16));
-      umma::tmem_ld16(tl + 128 + 32 * jh, *reinterpret_cast<float(*)[16]>(bb));
-      umma::tmem_ld16(tl + 128 + 32 * jh + 16, *reinterpret_cast<float(*)[16]>(bb + 16));
+      float a[CH], bb[CH];
+      umma::tmem_ld16(tl + 256 + ch0, a);
+      umma::tmem_ld16(tl + 128 + ch0, bb);
       umma::tmem_wait_ld();
-      uint8_t* yb = sG + jh * TILE;  // box [128 t][32 f32]
+      uint8_t* yb = sG + (jq >> 1) * TILE;  // box [128 t][32 f32]
 #pragma unroll
-      for (int i = 0; i < 32; i += 4)
-        *reinterpret_cast<float4*>(yb + umma::sw128_off_f32(trow, i)) =
+      for (int i = 0; i < CH; i += 4)
+        *reinterpret_cast<float4*>(yb + umma::sw128_off_f32(trow, (ch0 & 31) + i)) =
             make_float4(a[i] + e_t * bb[i], a[i + 1] + e_t * bb[i + 1], a[i + 2] + e_t * bb[i + 2],
                         a[i + 3] + e_t * bb[i + 3]);
     }
     const bool ck = ((c + 1) * Q) % seg == 0;
     if (ck) {
       const int n = trow;
-      uint8_t* cb = (n < 64 ? sUt : sU) + jh * (TILE / 2);  // box [64 n][32 f32]
+      uint8_t* cb = (n < 64 ? sUt : sU) + (jq >> 1) * (TILE / 2);  // box [64 n][32 f32]
 #pragma unroll
-      for (int i = 0; i < 32; i += 4)
-        *reinterpret_cast<float4*>(cb + umma::sw128_off_f32(n & 63, i)) =
+      for (int i = 0; i < CH; i += 4)
+        *reinterpret_cast<float4*>(cb + umma::sw128_off_f32(n & 63, (ch0 & 31) + i)) =
             make_float4(hreg[i], hreg[i + 1], hreg[i + 2], hreg[i + 3]);
     }
     fence_proxy_async_smem();
@@ -346,11 +413,8 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
         tma_store_3d(&tm_ck, 0, 64, zz, sU);
         tma_store_3d(&tm_ck, 32, 64, zz, sU + TILE / 2);
       }
-      bulk_commit();
-      bulk_wait_read_all();  // staging slots reusable
-      if (c + 2 < nck) issue_u(c + 2);
+      bulk_commit();  // read back in the next prologue before the slots are reused
     }
-    __syncthreads();
     if (c + 1 < nck) safe = prologue(c + 1);
   }
   if (tid == 0) bulk_wait_all();
@@ -408,7 +472,7 @@ int ssd_chunk_fwd_launch(const void* u, const void* delta, const void* Bm, const
   auto k = ssd_chunk_fwd_kernel<T>;
   const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssdc::SMEM);
   if (e != cudaSuccess) return set_error(MR_E_LAUNCH, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-  k<<<(unsigned)(batch * H), 256, ssdc::SMEM, st>>>(mu, mB, mC, my, mck, (const T*)delta, A, ash, (int)L, (int)H,
+  k<<<(unsigned)(batch * H), ssdc::NT, ssdc::SMEM, st>>>(mu, mB, mC, my, mck, (const T*)delta, A, ash, (int)L, (int)H,
                                                     (int)seg);
   return check_launch("ssd_chunk_fwd_kernel");
 }
@@ -445,55 +509,67 @@ int ssdc_device_error(bool clear) { return read_device_error(clear); }
 // The tensor-core products per chunk, in three batches (TMEM columns):
 //   1: S [0,128)  P [128,256)  Y2 = C h0^T [256,320)  R2 = B Psi^T [320,384)
 //      dPsi^T = C^T (e^Lam gy) [384,448)
-//   2: S^T = B C^T [0,128)  P^T = u gy^T [128,256)  R1 = G'^T gy [256,320)
+//   2: R1 = G'^T gy [256,320)
 //   3: gB1 = H1^T C [0,128)  gC1 = H1 B [128,256)  gB2 = u Psi [256,384)  gC2 = gy h0 [384,512)
-// gy enters P, P^T and R1 as bf16/fp16 hi + lo parts (two accumulated products).
-// colsum Z comes from the transposed products (thread t owns row t of S^T, P^T).
+// gy enters P and R1 as bf16/fp16 hi + lo parts (two accumulated products).
+// rowsum Z and colsum Z are both taken from the f32 Z of epilogue 1 (the
+// diagonal terms, the largest, cancel exactly in rowsum - colsum); the column
+// sums by a transposing warp butterfly.
+//
+// 16 warps: warp w reads TMEM lanes 32*(w%4).. (its row quarter) and owns
+// column quarter w/4 of every row-wise epilogue (32 of 128 columns, or 16 of
+// the 64 channels), so four warps per SM sub-partition hide each other's TMEM,
+// shared-memory and global latencies.
 
 namespace ssdb {
 constexpr int Q = 128, DH = 64, NS = 128;
+constexpr int NT = 512;          // threads
+constexpr int CQ = 4;            // column quarters (warps per TMEM lane quarter)
+constexpr int CH = DH / CQ;      // channels per thread
 constexpr uint32_t TILE = 16384;
 // tiles: U, B lo/hi, C lo/hi, GY, GYt, PSI, H0, GP lo/hi, HH lo/hi
 constexpr int NTILE = 13;
-constexpr size_t SMALL = (5 * Q + 6 * Q + 64) * 4 + 4 * 8 + 16;
+// Lam, delta, w, exp(Lam), D, CF1, CF2; row/col/q/m/ur partials per column quarter; reduction scratch
+constexpr int NSMALLF = 7 * Q + 5 * CQ * Q + 64;
+constexpr size_t SMALL = NSMALLF * 4 + 4 * 8 + 16;
 constexpr size_t SMEM = SMALL + 1023 + NTILE * TILE;
 }  // namespace ssdb
 
 template <typename T>
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(ssdb::NT, 1)
 ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_constant__ CUtensorMap tm_B,
                      const __grid_constant__ CUtensorMap tm_C, const __grid_constant__ CUtensorMap tm_gu,
                      const __grid_constant__ CUtensorMap tm_gB, const __grid_constant__ CUtensorMap tm_gC,
-                     const __grid_constant__ CUtensorMap tm_ck, const float* __restrict__ gy,
+                     const float* __restrict__ ckpt, const float* __restrict__ gy,
                      const float* __restrict__ gfinal, const T* __restrict__ delta, const float* __restrict__ A,
                      int64_t ash, int L, int H, int seg, T* __restrict__ gdelta, float* __restrict__ gA_part) {
   using namespace ssdb;
   extern __shared__ unsigned char smem_raw[];
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem_raw);  // tma(u,B,C), mma, ckpt
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem_raw);  // tma(u,B,C), mma
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 4);
   float* sLam = reinterpret_cast<float*>(tslot + 4);  // Lam_t
   float* sDel = sLam + Q;                             // delta_t
   float* sW = sDel + Q;                               // w_t
   float* sEL = sW + Q;                                // exp(Lam_t)
   float* sD = sEL + Q;                                // D_t
-  float* sRow = sD + Q;                               // [2][Q] rowsum Z partials (by column half)
-  float* sCol = sRow + 2 * Q;                         // [2][Q]
-  float* sQ = sCol + 2 * Q;                           // [2][Q] gy.Y2 partials
-  float* sRed = sQ + 2 * Q;                           // 64 floats of reduction scratch
+  float* sCF1 = sD + Q;                               // exp(Lam_t0 - Lam_t), t0 = start of t's 16-step block
+  float* sCF2 = sCF1 + Q;                             // exp(Lam_t - Lam_t0)
+  float* sRow = sCF2 + Q;                             // [CQ][Q] rowsum Z partials (by column quarter)
+  float* sCol = sRow + CQ * Q;                        // [CQ][Q] colsum Z partials
+  float* sQ = sCol + CQ * Q;                          // [CQ][Q] gy.Y2 partials
+  float* sM = sQ + CQ * Q;                            // [CQ][Q] u_t . R2_t partials
+  float* sUR = sM + CQ * Q;                           // [CQ][Q] u_t . r_t partials
+  float* sRed = sUR + CQ * Q;                         // 64 floats of reduction scratch
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sRed + 64) + 1023) & ~uintptr_t(1023));
   uint8_t* tU = sm;
   uint8_t* tB = tU + TILE;        // 2 tiles
   uint8_t* tC = tB + 2 * TILE;    // 2 tiles
   uint8_t* tGY = tC + 2 * TILE;   // gy bf16 [s][d]
-  uint8_t* tGYt = tGY + TILE;     // exp(Lam_s) gy [s][d]; gy lo part in batch 2; then grad_u staging
+  uint8_t* tGYt = tGY + TILE;     // gy lo part [s][d] (batches 1, 2); then grad_u staging
   uint8_t* tPSI = tGYt + TILE;    // Psi^T bf16 [n][d]
   uint8_t* tH0 = tPSI + TILE;     // h0^T bf16 [n][d]
   uint8_t* tGP = tH0 + TILE;      // G' [s][t], 2 tiles (t halves); then grad_B staging
-  uint8_t* tHH = tGP + 2 * TILE;  // H1 [s][t], 2 tiles; then grad_C staging; then h0 f32 prefetch
-  __shared__ float sM[2][Q];      // u_t . R2_t partials
-  __shared__ float sUR[2][Q];     // u_t . r_t partials
-  __shared__ float sCF1[Q];       // exp(Lam_t0 - Lam_t), t0 = start of t's 16-step block
-  __shared__ float sCF2[Q];       // exp(Lam_t - Lam_t0)
+  uint8_t* tHH = tGP + 2 * TILE;  // exp(Lam_s) gy [s][d] (batch 1); H1 [s][t], 2 tiles; grad_C staging
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bh = blockIdx.x;
@@ -509,25 +585,28 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   constexpr uint32_t id128MM = umma::idesc_f16(128, 128, fmt, 1, 1);
   constexpr uint32_t id128KM = umma::idesc_f16(128, 128, fmt, 0, 1);
 
-  const int q4 = warp & 3, jh = warp >> 2;
+  const int q4 = warp & 3, jq = warp >> 2;
   const int row = 32 * q4 + lane;  // the row (s, t or n) this thread owns in TMEM
   const int rmax = 32 * q4 + 31;   // last row of this warp
+  const int ch0 = CH * jq;         // first channel (d) of this thread
+  const int cq0 = 32 * jq;         // first of this thread's 32 columns (t, s or n)
+  const int ct0 = cq0 & 63;        // that column inside its 64-column tile
   if (tid == 0) {
-    for (int i = 0; i < 3; ++i) mbar_init(&bar[i], 1);
+    for (int i = 0; i < 2; ++i) mbar_init(&bar[i], 1);
     fence_mbar_init();
   }
   if (warp == 0) {
     umma::tmem_alloc(tslot, 512);
     umma::tmem_relinquish();
   }
-  // Psi = dL/d(final state), thread (n = row, channels 32*jh..): gfinal is [B,H,Dh,N]
-  float psi[32];
+  // Psi = dL/d(final state), thread (n = row, channels ch0..): gfinal is [B,H,Dh,N]
+  float psi[CH];
 #pragma unroll
-  for (int i = 0; i < 32; ++i)
-    psi[i] = gfinal != nullptr ? gfinal[(((int64_t)b * H + h) * DH + 32 * jh + i) * NS + row] : 0.f;
+  for (int i = 0; i < CH; ++i)
+    psi[i] = gfinal != nullptr ? gfinal[(((int64_t)b * H + h) * DH + ch0 + i) * NS + row] : 0.f;
 #pragma unroll
-  for (int cc = 0; cc < 4; ++cc)
-    *reinterpret_cast<int4*>(tPSI + umma::sw128_off(row, 32 * jh + 8 * cc)) = pack8<T>(psi + 8 * cc);
+  for (int cc = 0; cc < CH / 8; ++cc)
+    *reinterpret_cast<int4*>(tPSI + umma::sw128_off(row, ch0 + 8 * cc)) = pack8<T>(psi + 8 * cc);
   fence_proxy_async_smem();
   __syncthreads();
   umma::fence_after_sync();
@@ -543,39 +622,34 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     tma_load_3d(tC, &tm_C, 0, h, z, &bar[0]);
     tma_load_3d(tC + TILE, &tm_C, 64, h, z, &bar[0]);
   };
-  // h0 of chunk c (= checkpoint c-1, f32 [N][Dh]) into the HH tiles: boxes [64 n][32 d]
-  auto issue_h0 = [&](int c) {
-    const int zz = (int)(((int64_t)b * nseg + (c * Q) / seg - 1) * H + h);
-    mbar_arrive_expect_tx(&bar[2], 2 * TILE);
-    tma_load_3d(tHH, &tm_ck, 0, 0, zz, &bar[2]);
-    tma_load_3d(tHH + TILE / 2, &tm_ck, 32, 0, zz, &bar[2]);
-    tma_load_3d(tHH + TILE, &tm_ck, 0, 64, zz, &bar[2]);
-    tma_load_3d(tHH + TILE + TILE / 2, &tm_ck, 32, 64, zz, &bar[2]);
-  };
-  if (tid == 0) {
-    issue(nck - 1);
-    if (nck > 1) issue_h0(nck - 1);
-  }
+  if (tid == 0) issue(nck - 1);
 
-  // grad_y rows (thread: row s, channels 32*jh..) and delta of the first chunk processed
-  float gyr[32];
+  // grad_y and h0 of a chunk are [128 rows][64 channels] f32 and enter the
+  // kernel through registers in a coalesced layout: thread i holds channels
+  // cd0..cd0+3 of rows cr0 + 32k, k = 0..3, so a warp's load covers two whole
+  // rows (a row-per-lane layout would touch 32 cache lines per instruction).
+  const int cd0 = 4 * (tid & 15), cr0 = tid >> 4;
+  float4 gyv[4];  // grad_y rows s
   auto load_gy = [&](int c) {
-    const float* src = gy + ((row0 + (int64_t)c * Q + row) * H + h) * DH + 32 * jh;
+    const float* src = gy + ((row0 + (int64_t)c * Q + cr0) * H + h) * DH + cd0;
 #pragma unroll
-    for (int i = 0; i < 32; i += 4) {
-      const float4 v = __ldcs(reinterpret_cast<const float4*>(src + i));
-      gyr[i] = v.x;
-      gyr[i + 1] = v.y;
-      gyr[i + 2] = v.z;
-      gyr[i + 3] = v.w;
-    }
+    for (int k = 0; k < 4; ++k) gyv[k] = ld_pinned_f4(src + (int64_t)32 * k * H * DH);
+  };
+  // h0 of chunk c > 0: the checkpoint at the end of the previous segment, [N][Dh] (rows n)
+  float4 h0v[4];
+  auto load_h0 = [&](int c) {
+    const int64_t kk = ((int64_t)b * nseg + (c * Q) / seg - 1) * H + h;
+    const float* src = ckpt + (kk * NS + cr0) * DH + cd0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) h0v[k] = ld_pinned_f4(src + 32 * k * DH);
   };
   load_gy(nck - 1);
-  float dnext = (tid < Q) ? to_f(delta[(row0 + (int64_t)(nck - 1) * Q + tid) * H + h]) : 0.f;
+  if (nck > 1) load_h0(nck - 1);
+  unsigned short dnext = (tid < Q) ? ld_pinned_u16(delta + (row0 + (int64_t)(nck - 1) * Q + tid) * H + h) : (unsigned short)0;
   float gA_acc = 0.f;
-  uint32_t tph = 0, mph = 0, hph = 0;
+  uint32_t tph = 0, mph = 0;
 
-  auto block_sum = [&](float v) -> float {  // sum over all 256 threads
+  auto block_sum = [&](float v) -> float {  // sum over all threads
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
     __syncthreads();
@@ -583,16 +657,16 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     __syncthreads();
     float s = 0.f;
 #pragma unroll
-    for (int w = 0; w < 8; ++w) s += sRed[w];
+    for (int w = 0; w < NT / 32; ++w) s += sRed[w];
     return s;
   };
+  auto sum4 = [&](const float* p, int i) { return (p[i] + p[Q + i]) + (p[2 * Q + i] + p[3 * Q + i]); };
 
   for (int c = nck - 1; c >= 0; --c) {
     // ---- P0: Lam, D, w, exp(Lam), exponential factors; h0; gy tiles
     bool safe;
     {
-      const float dcur = dnext;
-      if (tid < Q && c > 0) dnext = to_f(delta[(row0 + (int64_t)(c - 1) * Q + tid) * H + h]);
+      const float dcur = u16_to_f<T>(dnext);
       float lam = 0.f, dsum = 0.f;
       if (tid < Q) {
         lam = dcur * Ah;
@@ -607,8 +681,8 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
           }
         }
         if (lane == 31) {
-          sRed[warp] = lam;
-          sRed[8 + warp] = dsum;
+          sRed[16 + warp] = lam;
+          sRed[24 + warp] = dsum;
         }
         sDel[tid] = dcur;
       }
@@ -616,8 +690,8 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
       if (tid < Q) {
         float o1 = 0.f, o2 = 0.f;
         for (int w = 0; w < warp; ++w) {
-          o1 += sRed[w];
-          o2 += sRed[8 + w];
+          o1 += sRed[16 + w];
+          o2 += sRed[24 + w];
         }
         sLam[tid] = lam + o1;
         sD[tid] = dsum + o2;
@@ -632,51 +706,34 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
         sCF2[tid] = __expf(-span);
         wide = span > 40.f;
       }
+      // the previous chunk's bulk stores must have read GP, HH and GYt before
+      // they are rewritten below
+      if (tid == 0) bulk_wait_read_all();
       safe = !__syncthreads_or(wide);  // also publishes sEL / sW / sCF
     }
-    float h0f[32];
-    if (c > 0) {
-      mbar_wait(&bar[2], hph & 1u);
-      ++hph;
-      const uint8_t* hb = tHH + (row >= 64 ? TILE : 0) + jh * (TILE / 2);
-#pragma unroll
-      for (int i = 0; i < 32; i += 4) {
-        const float4 v = *reinterpret_cast<const float4*>(hb + umma::sw128_off_f32(row & 63, i));
-        h0f[i] = v.x;
-        h0f[i + 1] = v.y;
-        h0f[i + 2] = v.z;
-        h0f[i + 3] = v.w;
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 32; ++i) h0f[i] = 0.f;
-    }
+    // h0^T and the gy tiles from the coalesced registers (thread: rows cr0 + 32k,
+    // channels cd0..cd0+3). gy enters the S/P products as hi + lo 2-byte parts
+    // (P, P^T and R1 carry about 16 mantissa bits; dA/d-delta sum many of these
+    // terms); exp(Lam_s) gy, the dPsi operand, goes to HH until E1 writes H1.
+    // <Psi, h0> takes Psi's 2-byte copy (it weighs only the last step's dLam).
     float psih0 = 0.f;
 #pragma unroll
-    for (int i = 0; i < 32; ++i) psih0 += psi[i] * h0f[i];
-#pragma unroll
-    for (int cc = 0; cc < 4; ++cc)
-      *reinterpret_cast<int4*>(tH0 + umma::sw128_off(row, 32 * jh + 8 * cc)) = pack8<T>(h0f + 8 * cc);
-    {
-      // gy enters the S/P products as hi + lo 2-byte parts (P, P^T and R1 carry
-      // about 16 mantissa bits; dA/d-delta sum many of these terms)
-      const float el = sEL[row];
-      float t8[8], lo[8];
-#pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        const uint32_t off = umma::sw128_off(row, 32 * jh + 8 * cc);
-        const int4 hi = pack8<T>(gyr + 8 * cc);
-        *reinterpret_cast<int4*>(tGY + off) = hi;
-        float hf[8];
-        unpack8<T>(hi, hf);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          t8[i] = el * gyr[8 * cc + i];
-          lo[i] = gyr[8 * cc + i] - hf[i];
-        }
-        *reinterpret_cast<int4*>(tGYt + off) = pack8<T>(t8);
-        *reinterpret_cast<int4*>(tGP + off) = pack8<T>(lo);  // gy lo part, read by batch 1 only
-      }
+    for (int k = 0; k < 4; ++k) {
+      const int r = cr0 + 32 * k;
+      const uint32_t off = umma::sw128_off(r, cd0);
+      const float4 hv = c > 0 ? h0v[k] : make_float4(0.f, 0.f, 0.f, 0.f);
+      *reinterpret_cast<uint2*>(tH0 + off) = pack4<T>(hv);
+      float pf[4];
+      unpack4<T>(*reinterpret_cast<const uint2*>(tPSI + off), pf);
+      psih0 += pf[0] * hv.x + pf[1] * hv.y + pf[2] * hv.z + pf[3] * hv.w;
+      const float4 g = gyv[k];
+      const uint2 hi = pack4<T>(g);
+      float hf[4];
+      unpack4<T>(hi, hf);
+      const float el = sEL[r];
+      *reinterpret_cast<uint2*>(tGY + off) = hi;
+      *reinterpret_cast<uint2*>(tGYt + off) = pack4<T>(make_float4(g.x - hf[0], g.y - hf[1], g.z - hf[2], g.w - hf[3]));
+      *reinterpret_cast<uint2*>(tHH + off) = pack4<T>(make_float4(el * g.x, el * g.y, el * g.z, el * g.w));
     }
     fence_proxy_async_smem();
     const float psi_h0 = block_sum(psih0);  // includes a __syncthreads
@@ -687,14 +744,14 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
       ++tph;
       umma::fence_after_sync();
       const uint32_t aU = smem_u32(tU), aB = smem_u32(tB), aC = smem_u32(tC), aGY = smem_u32(tGY),
-                     aGYt = smem_u32(tGYt), aPSI = smem_u32(tPSI), aH0 = smem_u32(tH0), aLo = smem_u32(tGP);
+                     aEG = smem_u32(tHH), aPSI = smem_u32(tPSI), aH0 = smem_u32(tH0), aLo = smem_u32(tGYt);
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
         const uint32_t ko = (k >> 2) * TILE + (k & 3) * 32;
         umma::mma_f16(tbase + 0, umma::sdesc_k(aC + ko), umma::sdesc_k(aB + ko), id128KK, k > 0);
         umma::mma_f16(tbase + 256, umma::sdesc_k(aC + ko), umma::sdesc_mn(aH0 + k * 2048, TILE), id64KM, k > 0);
         umma::mma_f16(tbase + 320, umma::sdesc_k(aB + ko), umma::sdesc_mn(aPSI + k * 2048, TILE), id64KM, k > 0);
-        umma::mma_f16(tbase + 384, umma::sdesc_mn(aC + k * 2048, TILE), umma::sdesc_mn(aGYt + k * 2048, TILE),
+        umma::mma_f16(tbase + 384, umma::sdesc_mn(aC + k * 2048, TILE), umma::sdesc_mn(aEG + k * 2048, TILE),
                       id64MM, k > 0);
       }
 #pragma unroll
@@ -709,158 +766,150 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     ++mph;
     umma::fence_after_sync();
 
-    // gy lo part moves to the GYt tile (free now) for batch 2; G' takes its place
-#pragma unroll
-    for (int cc = 0; cc < 4; ++cc) {
-      const uint32_t off = umma::sw128_off(row, 32 * jh + 8 * cc);
-      *reinterpret_cast<int4*>(tGYt + off) = *reinterpret_cast<const int4*>(tGP + off);
-    }
-    __syncthreads();
-
-    // ---- epilogue 1 (thread: row s, t-half jh): G', H1, rowsum Z; gy.Y2; u.R2
+    // ---- epilogue 1 (thread: row s, t-columns cq0..cq0+31): G', H1, rowsum Z; gy.Y2; u.R2
     // exp(Lam_s - Lam_t) = exp(Lam_s - Lam_t0) * exp(Lam_t0 - Lam_t), t0 = block start
     {
       const int s = row;
-      const float ls = sLam[s];
-      float rz = 0.f;
-      uint8_t* gp = tGP + jh * TILE;
-      uint8_t* hh = tHH + jh * TILE;
-#pragma unroll
-      for (int cb = 0; cb < 4; ++cb) {
-        const int t0 = 64 * jh + 16 * cb;
-        if (t0 > rmax) {
-          *reinterpret_cast<int4*>(gp + umma::sw128_off(s, 16 * cb)) = make_int4(0, 0, 0, 0);
-          *reinterpret_cast<int4*>(gp + umma::sw128_off(s, 16 * cb + 8)) = make_int4(0, 0, 0, 0);
-          *reinterpret_cast<int4*>(hh + umma::sw128_off(s, 16 * cb)) = make_int4(0, 0, 0, 0);
-          *reinterpret_cast<int4*>(hh + umma::sw128_off(s, 16 * cb + 8)) = make_int4(0, 0, 0, 0);
-          continue;
-        }
-        float sv[16], pv[16];
-        umma::tmem_ld16(tl + t0, sv);
-        umma::tmem_ld16(tl + 128 + t0, pv);
-        umma::tmem_wait_ld();
-        const float rf = (safe && s >= t0) ? __expf(ls - sLam[t0]) : 0.f;
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int t = t0 + i;
-          const float e = (t <= s) ? (safe ? rf * sCF1[t] : __expf(ls - sLam[t])) : 0.f;
-          const float g = sv[i] * e;
-          const float h1 = pv[i] * e * sDel[t];
-          rz += sv[i] * h1;
-          sv[i] = g;
-          pv[i] = h1;
-        }
-        *reinterpret_cast<int4*>(gp + umma::sw128_off(s, 16 * cb)) = pack8<T>(sv);
-        *reinterpret_cast<int4*>(gp + umma::sw128_off(s, 16 * cb + 8)) = pack8<T>(sv + 8);
-        *reinterpret_cast<int4*>(hh + umma::sw128_off(s, 16 * cb)) = pack8<T>(pv);
-        *reinterpret_cast<int4*>(hh + umma::sw128_off(s, 16 * cb + 8)) = pack8<T>(pv + 8);
-      }
-      sRow[jh * Q + s] = rz;
-      // gy_s . Y2_s over this thread's 32 channels; u_t . R2_t
-      float y2[32];
-      umma::tmem_ld16(tl + 256 + 32 * jh, *reinterpret_cast<float(*)[16]>(y2));
-      umma::tmem_ld16(tl + 256 + 32 * jh + 16, *reinterpret_cast<float(*)[16]>(y2 + 16));
-      float r2[32];
-      umma::tmem_ld16(tl + 320 + 32 * jh, *reinterpret_cast<float(*)[16]>(r2));
-      umma::tmem_ld16(tl + 320 + 32 * jh + 16, *reinterpret_cast<float(*)[16]>(r2 + 16));
+      // gy_s . Y2_s (gy as its hi + lo parts) and u_s . R2_s over this thread's channels
+      float y2[CH], r2[CH];
+      umma::tmem_ld16(tl + 256 + ch0, y2);
+      umma::tmem_ld16(tl + 320 + ch0, r2);
       umma::tmem_wait_ld();
       float qa = 0.f, ma = 0.f;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) qa += gyr[i] * y2[i];
+      for (int cc = 0; cc < CH / 8; ++cc) {
+        const uint32_t off = umma::sw128_off(s, ch0 + 8 * cc);
+        float f[8], g[8];
+        unpack8<T>(*reinterpret_cast<const int4*>(tGY + off), f);
+        unpack8<T>(*reinterpret_cast<const int4*>(tGYt + off), g);
 #pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        float f[8];
-        unpack8<T>(*reinterpret_cast<const int4*>(tU + umma::sw128_off(s, 32 * jh + 8 * cc)), f);
+        for (int i = 0; i < 8; ++i) qa += (f[i] + g[i]) * y2[8 * cc + i];
+        unpack8<T>(*reinterpret_cast<const int4*>(tU + off), f);
 #pragma unroll
         for (int i = 0; i < 8; ++i) ma += f[i] * r2[8 * cc + i];
       }
-      sQ[jh * Q + s] = qa;
-      sM[jh][s] = ma;
+      sQ[jq * Q + s] = qa;
+      sM[jq * Q + s] = ma;
+
+      const float ls = sLam[s];
+      float rz = 0.f;
+      uint8_t* gp = tGP + (jq >> 1) * TILE;
+      uint8_t* hh = tHH + (jq >> 1) * TILE;
+      if (cq0 > rmax) {  // above the diagonal for every row of this warp
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          *reinterpret_cast<int4*>(gp + umma::sw128_off(s, ct0 + 8 * j)) = make_int4(0, 0, 0, 0);
+          *reinterpret_cast<int4*>(hh + umma::sw128_off(s, ct0 + 8 * j)) = make_int4(0, 0, 0, 0);
+        }
+        sCol[q4 * Q + cq0 + lane] = 0.f;
+      } else {
+#pragma unroll
+        for (int cb = 0; cb < 2; ++cb) {
+          const int t0 = cq0 + 16 * cb;
+          const uint32_t o0 = umma::sw128_off(s, ct0 + 16 * cb), o1 = umma::sw128_off(s, ct0 + 16 * cb + 8);
+          if (t0 > rmax) {
+            *reinterpret_cast<int4*>(gp + o0) = make_int4(0, 0, 0, 0);
+            *reinterpret_cast<int4*>(gp + o1) = make_int4(0, 0, 0, 0);
+            *reinterpret_cast<int4*>(hh + o0) = make_int4(0, 0, 0, 0);
+            *reinterpret_cast<int4*>(hh + o1) = make_int4(0, 0, 0, 0);
+            if ((lane & 1) == 0) sCol[q4 * Q + t0 + (lane >> 1)] = 0.f;
+            continue;
+          }
+          float sv[16], pv[16];
+          umma::tmem_ld16(tl + t0, sv);
+          umma::tmem_ld16(tl + 128 + t0, pv);
+          umma::tmem_wait_ld();
+          const float rf = (safe && s >= t0) ? __expf(ls - sLam[t0]) : 0.f;
+          float cf[16], dl[16];
+#pragma unroll
+          for (int i = 0; i < 16; i += 4) {
+            *reinterpret_cast<float4*>(cf + i) = *reinterpret_cast<const float4*>(sCF1 + t0 + i);
+            *reinterpret_cast<float4*>(dl + i) = *reinterpret_cast<const float4*>(sDel + t0 + i);
+          }
+          float z[16];  // Z[s, t] = S H1
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int t = t0 + i;
+            const float e = (t <= s) ? (safe ? rf * cf[i] : __expf(ls - sLam[t])) : 0.f;
+            const float g = sv[i] * e;
+            const float h1 = pv[i] * e * dl[i];
+            z[i] = sv[i] * h1;
+            rz += z[i];
+            sv[i] = g;
+            pv[i] = h1;
+          }
+          *reinterpret_cast<int4*>(gp + o0) = pack8<T>(sv);
+          *reinterpret_cast<int4*>(gp + o1) = pack8<T>(sv + 8);
+          *reinterpret_cast<int4*>(hh + o0) = pack8<T>(pv);
+          *reinterpret_cast<int4*>(hh + o1) = pack8<T>(pv + 8);
+          // colsum Z over this warp's 32 rows s (quarter q4), one partial per quarter
+          const float cz = warp_colsum16(z, lane);
+          if ((lane & 1) == 0) sCol[q4 * Q + t0 + (lane >> 1)] = cz;
+        }
+      }
+      sRow[jq * Q + s] = rz;
       fence_proxy_async_smem();
     }
     umma::fence_before_sync();
     __syncthreads();
 
-    // ---- batch 2: S^T, P^T, R1
+    // ---- batch 2: R1
     if (tid == 0) {
       umma::fence_after_sync();
-      const uint32_t aU = smem_u32(tU), aB = smem_u32(tB), aC = smem_u32(tC), aGY = smem_u32(tGY),
-                     aGP = smem_u32(tGP), aLo = smem_u32(tGYt);
+      const uint32_t aGY = smem_u32(tGY), aGP = smem_u32(tGP), aLo = smem_u32(tGYt);
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
-        const uint32_t ko = (k >> 2) * TILE + (k & 3) * 32;
-        umma::mma_f16(tbase + 0, umma::sdesc_k(aB + ko), umma::sdesc_k(aC + ko), id128KK, k > 0);
         umma::mma_f16(tbase + 256, umma::sdesc_mn(aGP + k * 2048, TILE), umma::sdesc_mn(aGY + k * 2048, TILE),
                       id64MM, k > 0);
         umma::mma_f16(tbase + 256, umma::sdesc_mn(aGP + k * 2048, TILE), umma::sdesc_mn(aLo + k * 2048, TILE),
                       id64MM, true);
       }
-#pragma unroll
-      for (int k = 0; k < 4; ++k)
-        umma::mma_f16(tbase + 128, umma::sdesc_k(aU + k * 32), umma::sdesc_k(aGY + k * 32), id128KK, k > 0);
-#pragma unroll
-      for (int k = 0; k < 4; ++k)
-        umma::mma_f16(tbase + 128, umma::sdesc_k(aU + k * 32), umma::sdesc_k(aLo + k * 32), id128KK, true);
       umma::commit(&bar[1]);
     }
     mbar_wait(&bar[1], mph & 1u);
     ++mph;
     umma::fence_after_sync();
 
-    // ---- epilogue 2 (thread: row t): colsum Z; r, grad_u (staged in GYt), u.r; Psi update (row n)
+    // ---- epilogue 2 (thread: row t, channels ch0..): r, grad_u (staged in GYt), u.r; Psi update (row n)
     {
       const int t = row;
       const float lt = sLam[t], dt = sDel[t];
-      float cz = 0.f;
-      if (64 * jh + 63 >= 32 * q4) {
+      {
+        float r1[CH], r2[CH], dp[CH];
+        umma::tmem_ld16(tl + 256 + ch0, r1);
+        umma::tmem_ld16(tl + 320 + ch0, r2);
+        umma::tmem_ld16(tl + 384 + ch0, dp);
+        umma::tmem_wait_ld();
+        const float f2 = __expf(sLam[Q - 1] - lt);
+        const float dec = __expf(sLam[Q - 1]);
+        float ur = 0.f;
 #pragma unroll
-        for (int cb = 0; cb < 4; ++cb) {
-          const int s0 = 64 * jh + 16 * cb;
-          if (s0 + 15 < 32 * q4) continue;  // the whole block is below every row of this warp
-          float sv[16], pv[16];
-          umma::tmem_ld16(tl + s0, sv);
-          umma::tmem_ld16(tl + 128 + s0, pv);
-          umma::tmem_wait_ld();
-          // exp(Lam_s - Lam_t) = exp(Lam_s0 - Lam_t) * exp(Lam_s - Lam_s0) for s >= t
-          const float rf = safe ? __expf(fminf(sLam[s0] - lt, 88.f)) : 0.f;
+        for (int cc = 0; cc < CH / 8; ++cc) {
+          const uint32_t off = umma::sw128_off(t, ch0 + 8 * cc);
+          float f[8], o[8];
+          unpack8<T>(*reinterpret_cast<const int4*>(tU + off), f);
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int s = s0 + i;
-            const float e = (s >= t) ? (safe ? rf * sCF2[s] : __expf(sLam[s] - lt)) : 0.f;
-            cz += sv[i] * pv[i] * e;
+          for (int i = 0; i < 8; ++i) {
+            const float rv = r1[8 * cc + i] + f2 * r2[8 * cc + i];
+            ur += f[i] * rv;
+            o[i] = dt * rv;
           }
+          *reinterpret_cast<int4*>(tGYt + off) = pack8<T>(o);  // grad_u staging (GYt free after batch 2)
         }
+        sUR[jq * Q + t] = ur;
+        // Psi (row n = row) <- exp(Lam_last) Psi + dPsi; the bf16 copy is replaced after batch 3
+#pragma unroll
+        for (int i = 0; i < CH; ++i) psi[i] = dec * psi[i] + dp[i];
       }
-      sCol[jh * Q + t] = cz * dt;
-      float r1[32], r2[32], dp[32];
-      umma::tmem_ld16(tl + 256 + 32 * jh, *reinterpret_cast<float(*)[16]>(r1));
-      umma::tmem_ld16(tl + 256 + 32 * jh + 16, *reinterpret_cast<float(*)[16]>(r1 + 16));
-      umma::tmem_ld16(tl + 320 + 32 * jh, *reinterpret_cast<float(*)[16]>(r2));
-      umma::tmem_ld16(tl + 320 + 32 * jh + 16, *reinterpret_cast<float(*)[16]>(r2 + 16));
-      umma::tmem_ld16(tl + 384 + 32 * jh, *reinterpret_cast<float(*)[16]>(dp));
-      umma::tmem_ld16(tl + 384 + 32 * jh + 16, *reinterpret_cast<float(*)[16]>(dp + 16));
-      umma::tmem_wait_ld();
-      const float f2 = __expf(sLam[Q - 1] - lt);
-      const float dec = __expf(sLam[Q - 1]);
-      float ur = 0.f;
-#pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        const uint32_t off = umma::sw128_off(t, 32 * jh + 8 * cc);
-        float f[8], o[8];
-        unpack8<T>(*reinterpret_cast<const int4*>(tU + off), f);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float rv = r1[8 * cc + i] + f2 * r2[8 * cc + i];
-          ur += f[i] * rv;
-          o[i] = dt * rv;
-        }
-        *reinterpret_cast<int4*>(tGYt + off) = pack8<T>(o);  // grad_u staging (GYt free after batch 2)
-      }
-      sUR[jh][t] = ur;
-      // Psi (row n = row) <- exp(Lam_last) Psi + dPsi; the bf16 copy is replaced after batch 3
-#pragma unroll
-      for (int i = 0; i < 32; ++i) psi[i] = dec * psi[i] + dp[i];
       fence_proxy_async_smem();
+      // The next chunk's register operands. A proxy fence waits for the thread's
+      // outstanding loads, so they are issued after this one and have batch 3 and
+      // epilogue 3 to arrive.
+      if (c > 0) {
+        load_gy(c - 1);
+        if (tid < Q) dnext = ld_pinned_u16(delta + (row0 + (int64_t)(c - 1) * Q + tid) * H + h);
+      }
+      if (c > 1) load_h0(c - 1);
     }
     umma::fence_before_sync();
     __syncthreads();
@@ -889,12 +938,12 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     // ---- grad_delta and grad_A while batch 3 runs (thread t < Q)
     {
       float wm = 0.f;
-      if (tid < Q) wm = sW[tid] * (sM[0][tid] + sM[1][tid]);
+      if (tid < Q) wm = sW[tid] * sum4(sM, tid);
       const float sum_wm = block_sum(wm);
       float dl = 0.f;
       if (tid < Q) {
         const int t = tid;
-        dl = (sRow[t] + sRow[Q + t]) - (sCol[t] + sCol[Q + t]) + sEL[t] * (sQ[t] + sQ[Q + t]) - wm;
+        dl = sum4(sRow, t) - sum4(sCol, t) + sEL[t] * sum4(sQ, t) - wm;
         if (t == Q - 1) dl += sEL[Q - 1] * psi_h0 + sum_wm;
       }
       const float contrib = block_sum(tid < Q ? dl * sD[tid] : 0.f);
@@ -907,12 +956,12 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
           const float n = __shfl_down_sync(0xffffffffu, suf, o);
           if (lane + o < 32) suf += n;
         }
-        if (lane == 0) sRed[16 + warp] = suf;
+        if (lane == 0) sRed[32 + warp] = suf;
       }
       __syncthreads();
       if (tid < Q) {
-        for (int w = warp + 1; w < 4; ++w) suf += sRed[16 + w];
-        const float g = Ah * suf + (sUR[0][tid] + sUR[1][tid]);
+        for (int w = warp + 1; w < 4; ++w) suf += sRed[32 + w];
+        const float g = Ah * suf + sum4(sUR, tid);
         gdelta[(row0 + (int64_t)c * Q + tid) * H + h] = from_f<T>(g);
       }
     }
@@ -924,51 +973,49 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
       fence_proxy_async_smem();
       issue(c - 1);
     }
-    if (c > 0) load_gy(c - 1);
 
-    // ---- epilogue 3: stage grad_B (row t) in GP, grad_C (row s) in HH; new Psi^T
+    // ---- epilogue 3: stage grad_B (row t) in GP, grad_C (row s) in HH (columns n = cq0..); new Psi^T
     {
       const int t = row;
       const float wt = sW[t], et = sEL[t];
-      uint8_t* gbt = tGP + jh * TILE;
-      uint8_t* gct = tHH + jh * TILE;
+      uint8_t* gbt = tGP + (jq >> 1) * TILE;
+      uint8_t* gct = tHH + (jq >> 1) * TILE;
 #pragma unroll
-      for (int cb = 0; cb < 4; ++cb) {
-        float b1[16], b2[16], cv[16], c2[16];
-        umma::tmem_ld16(tl + 0 + 64 * jh + 16 * cb, b1);
-        umma::tmem_ld16(tl + 256 + 64 * jh + 16 * cb, b2);
-        umma::tmem_ld16(tl + 128 + 64 * jh + 16 * cb, cv);
-        umma::tmem_ld16(tl + 384 + 64 * jh + 16 * cb, c2);
+      for (int cb = 0; cb < 2; ++cb) {
+        const int col = cq0 + 16 * cb;
+        const uint32_t o0 = umma::sw128_off(t, ct0 + 16 * cb), o1 = umma::sw128_off(t, ct0 + 16 * cb + 8);
+        float v1[16], v2[16];
+        umma::tmem_ld16(tl + 0 + col, v1);  // gB1 + w_t gB2
+        umma::tmem_ld16(tl + 256 + col, v2);
         umma::tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          b1[i] += wt * b2[i];
-          cv[i] += et * c2[i];
-        }
-        *reinterpret_cast<int4*>(gbt + umma::sw128_off(t, 16 * cb)) = pack8<T>(b1);
-        *reinterpret_cast<int4*>(gbt + umma::sw128_off(t, 16 * cb + 8)) = pack8<T>(b1 + 8);
-        *reinterpret_cast<int4*>(gct + umma::sw128_off(t, 16 * cb)) = pack8<T>(cv);
-        *reinterpret_cast<int4*>(gct + umma::sw128_off(t, 16 * cb + 8)) = pack8<T>(cv + 8);
+        for (int i = 0; i < 16; ++i) v1[i] += wt * v2[i];
+        *reinterpret_cast<int4*>(gbt + o0) = pack8<T>(v1);
+        *reinterpret_cast<int4*>(gbt + o1) = pack8<T>(v1 + 8);
+        umma::tmem_ld16(tl + 128 + col, v1);  // gC1 + exp(Lam_s) gC2
+        umma::tmem_ld16(tl + 384 + col, v2);
+        umma::tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v1[i] += et * v2[i];
+        *reinterpret_cast<int4*>(gct + o0) = pack8<T>(v1);
+        *reinterpret_cast<int4*>(gct + o1) = pack8<T>(v1 + 8);
       }
       // Psi's bf16 copy for the next chunk (its readers in batches 1 and 3 are done)
 #pragma unroll
-      for (int cc = 0; cc < 4; ++cc)
-        *reinterpret_cast<int4*>(tPSI + umma::sw128_off(row, 32 * jh + 8 * cc)) = pack8<T>(psi + 8 * cc);
+      for (int cc = 0; cc < CH / 8; ++cc)
+        *reinterpret_cast<int4*>(tPSI + umma::sw128_off(row, ch0 + 8 * cc)) = pack8<T>(psi + 8 * cc);
       fence_proxy_async_smem();
     }
     umma::fence_before_sync();
     __syncthreads();
-    if (tid == 0) {
+    if (tid == 0) {  // read back by the next chunk's P0 (bulk_wait_read_all) before reuse
       const int z = (int)(row0 + (int64_t)c * Q);
       tma_store_3d(&tm_gB, 0, h, z, tGP);
       tma_store_3d(&tm_gB, 64, h, z, tGP + TILE);
       tma_store_3d(&tm_gC, 0, h, z, tHH);
       tma_store_3d(&tm_gC, 64, h, z, tHH + TILE);
       bulk_commit();
-      bulk_wait_read_all();  // GP, HH and GYt are reusable
-      if (c > 1) issue_h0(c - 1);
     }
-    __syncthreads();
   }
   if (tid == 0) {
     gA_part[bh] = gA_acc;
@@ -993,22 +1040,14 @@ int ssd_chunk_bwd_launch(const float* gy, const float* gf, const float* ckpt, co
                          const void* Bm, const void* Cm, const float* A, int64_t ash, int64_t batch, int64_t L,
                          int64_t H, int64_t seg, void* gu, void* gd, void* gB, void* gC, float* gA,
                          float* ws, cudaStream_t st) {
-  CUtensorMap mu, mB, mC, mgu, mgB, mgC, mck;
+  CUtensorMap mu, mB, mC, mgu, mgB, mgC;
   if (int rc = ssd_tmaps<T>(u, Bm, Cm, batch, L, H, &mu, &mB, &mC)) return rc;
   if (int rc = ssd_tmaps<T>(gu, gB, gC, batch, L, H, &mgu, &mgB, &mgC)) return rc;
-  {
-    using namespace ssdb;
-    // h_ckpt [B*nSeg*H, N, Dh] f32, boxes [64 states][32 channels]
-    if (int rc = make_tmap_3d(&mck, ckpt, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, DH, NS,
-                              (uint64_t)batch * (L / seg) * H, DH * 4, (uint64_t)NS * DH * 4, 32, 64, 1,
-                              CU_TENSOR_MAP_SWIZZLE_128B))
-      return rc;
-  }
   auto k = ssd_chunk_bwd_kernel<T>;
   const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssdb::SMEM);
   if (e != cudaSuccess) return set_error(MR_E_LAUNCH, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-  k<<<(unsigned)(batch * H), 256, ssdb::SMEM, st>>>(mu, mB, mC, mgu, mgB, mgC, mck, gy, gf, (const T*)delta, A, ash,
-                                                    (int)L, (int)H, (int)seg, (T*)gd, ws);
+  k<<<(unsigned)(batch * H), ssdb::NT, ssdb::SMEM, st>>>(mu, mB, mC, mgu, mgB, mgC, ckpt, gy, gf, (const T*)delta, A,
+                                                         ash, (int)L, (int)H, (int)seg, (T*)gd, ws);
   if (int rc = check_launch("ssd_chunk_bwd_kernel")) return rc;
   const int HN = (int)(H * ssdb::NS);
   ssd_ga_head_kernel<<<(HN + 255) / 256, 256, 0, st>>>(ws, (int)batch, (int)H, ssdb::NS, gA);
