@@ -68,6 +68,11 @@ __device__ __forceinline__ float4 ld_pinned_f4(const float* p) {
                : "l"(p));
   return v;
 }
+// barrier over the first `nthreads` threads of named barrier `id` (1..15; 0 is __syncthreads)
+__device__ __forceinline__ void named_barrier_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
 // raw 16-bit load: converted only where it is used, so the load does not stall here
 template <typename T>
 __device__ __forceinline__ unsigned short ld_pinned_u16(const T* p) {
@@ -529,9 +534,11 @@ constexpr int CH = DH / CQ;      // channels per thread
 constexpr uint32_t TILE = 16384;
 // tiles: U, B lo/hi, C lo/hi, GY, GYt, PSI, H0, GP lo/hi, HH lo/hi
 constexpr int NTILE = 13;
-// Lam, delta, w, exp(Lam), D, CF1, CF2; row/col/q/m/ur partials per column quarter; reduction scratch
-constexpr int NSMALLF = 7 * Q + 5 * CQ * Q + 64;
-constexpr size_t SMALL = NSMALLF * 4 + 4 * 8 + 16;
+// per-chunk scalars (Lam, delta, w, exp(Lam), D, CF1) in two buffers; row/col/q/m/ur
+// partials per column quarter; reduction scratch
+constexpr int NSC = 6;
+constexpr int NSMALLF = 2 * NSC * Q + 5 * CQ * Q + 64;
+constexpr size_t SMALL = NSMALLF * 4 + 4 * 8 + 16 + 16;
 constexpr size_t SMEM = SMALL + 1023 + NTILE * TILE;
 }  // namespace ssdb
 
@@ -547,19 +554,17 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   extern __shared__ unsigned char smem_raw[];
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem_raw);  // tma(u,B,C), mma
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 4);
-  float* sLam = reinterpret_cast<float*>(tslot + 4);  // Lam_t
-  float* sDel = sLam + Q;                             // delta_t
-  float* sW = sDel + Q;                               // w_t
-  float* sEL = sW + Q;                                // exp(Lam_t)
-  float* sD = sEL + Q;                                // D_t
-  float* sCF1 = sD + Q;                               // exp(Lam_t0 - Lam_t), t0 = start of t's 16-step block
-  float* sCF2 = sCF1 + Q;                             // exp(Lam_t - Lam_t0)
-  float* sRow = sCF2 + Q;                             // [CQ][Q] rowsum Z partials (by column quarter)
+  int* sWide = reinterpret_cast<int*>(tslot + 4);     // [2] a 16-step block spans a decay above e^40
+  // [2][NSC][Q] per-chunk scalars, buffer c & 1 for chunk c: Lam_t, delta_t, w_t,
+  // exp(Lam_t), D_t, exp(Lam_t0 - Lam_t) (t0 = start of t's 16-step block)
+  float* sSc = reinterpret_cast<float*>(sWide + 4);
+  float* sRow = sSc + 2 * NSC * Q;                    // [CQ][Q] rowsum Z partials (by row quarter)
   float* sCol = sRow + CQ * Q;                        // [CQ][Q] colsum Z partials
   float* sQ = sCol + CQ * Q;                          // [CQ][Q] gy.Y2 partials
   float* sM = sQ + CQ * Q;                            // [CQ][Q] u_t . R2_t partials
   float* sUR = sM + CQ * Q;                           // [CQ][Q] u_t . r_t partials
   float* sRed = sUR + CQ * Q;                         // 64 floats of reduction scratch
+  // sRed: [0,12) grad_delta warp sums, [16,24) scalar scan, [32,48) <Psi, h0> warp partials
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sRed + 64) + 1023) & ~uintptr_t(1023));
   uint8_t* tU = sm;
   uint8_t* tB = tU + TILE;        // 2 tiles
@@ -626,14 +631,18 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
 
   // grad_y and h0 of a chunk are [128 rows][64 channels] f32 and enter the
   // kernel through registers in a coalesced layout: thread i holds channels
-  // cd0..cd0+3 of rows cr0 + 32k, k = 0..3, so a warp's load covers two whole
-  // rows (a row-per-lane layout would touch 32 cache lines per instruction).
-  const int cd0 = 4 * (tid & 15), cr0 = tid >> 4;
+  // cd0..cd0+7 of rows cr0 + 64k, k = 0..1 (float4 v[2k + j] = channels
+  // cd0 + 4j..), so eight lanes cover a whole row (a row-per-lane layout
+  // would touch 32 cache lines per instruction) and the tiles are written
+  // with 16-byte stores.
+  const int cd0 = 8 * (tid & 7), cr0 = tid >> 3;
   float4 gyv[4];  // grad_y rows s
   auto load_gy = [&](int c) {
     const float* src = gy + ((row0 + (int64_t)c * Q + cr0) * H + h) * DH + cd0;
 #pragma unroll
-    for (int k = 0; k < 4; ++k) gyv[k] = ld_pinned_f4(src + (int64_t)32 * k * H * DH);
+    for (int k = 0; k < 2; ++k)
+#pragma unroll
+      for (int j = 0; j < 2; ++j) gyv[2 * k + j] = ld_pinned_f4(src + (int64_t)64 * k * H * DH + 4 * j);
   };
   // h0 of chunk c > 0: the checkpoint at the end of the previous segment, [N][Dh] (rows n)
   float4 h0v[4];
@@ -641,105 +650,110 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     const int64_t kk = ((int64_t)b * nseg + (c * Q) / seg - 1) * H + h;
     const float* src = ckpt + (kk * NS + cr0) * DH + cd0;
 #pragma unroll
-    for (int k = 0; k < 4; ++k) h0v[k] = ld_pinned_f4(src + 32 * k * DH);
+    for (int k = 0; k < 2; ++k)
+#pragma unroll
+      for (int j = 0; j < 2; ++j) h0v[2 * k + j] = ld_pinned_f4(src + 64 * k * DH + 4 * j);
   };
   load_gy(nck - 1);
   if (nck > 1) load_h0(nck - 1);
-  unsigned short dnext = (tid < Q) ? ld_pinned_u16(delta + (row0 + (int64_t)(nck - 1) * Q + tid) * H + h) : (unsigned short)0;
   float gA_acc = 0.f;
   uint32_t tph = 0, mph = 0;
 
-  auto block_sum = [&](float v) -> float {  // sum over all threads
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    __syncthreads();
-    if (lane == 0) sRed[warp] = v;
-    __syncthreads();
-    float s = 0.f;
-#pragma unroll
-    for (int w = 0; w < NT / 32; ++w) s += sRed[w];
-    return s;
-  };
   auto sum4 = [&](const float* p, int i) { return (p[i] + p[Q + i]) + (p[2 * Q + i] + p[3 * Q + i]); };
+  // A chunk's scalars from its delta (raw bits), by the 128 threads of one
+  // named barrier group (t = index in the group) into buffer buf.
+  auto chunk_scalars = [&](unsigned short dbits, int t, int buf, int barid) {
+    float* sl = sSc + buf * NSC * Q;
+    const float dcur = u16_to_f<T>(dbits);
+    float lam = dcur * Ah, dsum = dcur;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float n1 = __shfl_up_sync(0xffffffffu, lam, o);
+      const float n2 = __shfl_up_sync(0xffffffffu, dsum, o);
+      if (lane >= o) {
+        lam += n1;
+        dsum += n2;
+      }
+    }
+    const int w = t >> 5;
+    if (lane == 31) {
+      sRed[16 + w] = lam;
+      sRed[20 + w] = dsum;
+    }
+    if (t == 0) sWide[buf] = 0;
+    named_barrier_sync(barid, 128);
+    for (int v = 0; v < w; ++v) {
+      lam += sRed[16 + v];
+      dsum += sRed[20 + v];
+    }
+    sl[t] = lam;
+    sl[Q + t] = dcur;
+    sl[4 * Q + t] = dsum;
+    named_barrier_sync(barid, 128);
+    sl[2 * Q + t] = __expf(sl[Q - 1] - lam) * dcur;
+    sl[3 * Q + t] = __expf(lam);
+    const float span = sl[t & ~15] - lam;
+    sl[5 * Q + t] = __expf(span);
+    if (__any_sync(0xffffffffu, span > 40.f) && lane == 0) sWide[buf] = 1;
+  };
+  // the first chunk processed (the last one)
+  unsigned short dnext = 0;
+  if (warp < 4) {
+    dnext = ld_pinned_u16(delta + (row0 + (int64_t)(nck - 1) * Q + tid) * H + h);
+    chunk_scalars(dnext, tid, (nck - 1) & 1, 1);
+  }
 
   for (int c = nck - 1; c >= 0; --c) {
-    // ---- P0: Lam, D, w, exp(Lam), exponential factors; h0; gy tiles
-    bool safe;
-    {
-      const float dcur = u16_to_f<T>(dnext);
-      float lam = 0.f, dsum = 0.f;
-      if (tid < Q) {
-        lam = dcur * Ah;
-        dsum = dcur;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const float n1 = __shfl_up_sync(0xffffffffu, lam, o);
-          const float n2 = __shfl_up_sync(0xffffffffu, dsum, o);
-          if (lane >= o) {
-            lam += n1;
-            dsum += n2;
-          }
-        }
-        if (lane == 31) {
-          sRed[16 + warp] = lam;
-          sRed[24 + warp] = dsum;
-        }
-        sDel[tid] = dcur;
-      }
-      __syncthreads();
-      if (tid < Q) {
-        float o1 = 0.f, o2 = 0.f;
-        for (int w = 0; w < warp; ++w) {
-          o1 += sRed[16 + w];
-          o2 += sRed[24 + w];
-        }
-        sLam[tid] = lam + o1;
-        sD[tid] = dsum + o2;
-      }
-      __syncthreads();
-      bool wide = false;
-      if (tid < Q) {
-        sW[tid] = __expf(sLam[Q - 1] - sLam[tid]) * sDel[tid];
-        sEL[tid] = __expf(sLam[tid]);
-        const float span = sLam[tid & ~15] - sLam[tid];
-        sCF1[tid] = __expf(span);
-        sCF2[tid] = __expf(-span);
-        wide = span > 40.f;
-      }
-      // the previous chunk's bulk stores must have read GP, HH and GYt before
-      // they are rewritten below
-      if (tid == 0) bulk_wait_read_all();
-      safe = !__syncthreads_or(wide);  // also publishes sEL / sW / sCF
-    }
-    // h0^T and the gy tiles from the coalesced registers (thread: rows cr0 + 32k,
-    // channels cd0..cd0+3). gy enters the S/P products as hi + lo 2-byte parts
-    // (P, P^T and R1 carry about 16 mantissa bits; dA/d-delta sum many of these
-    // terms); exp(Lam_s) gy, the dPsi operand, goes to HH until E1 writes H1.
-    // <Psi, h0> takes Psi's 2-byte copy (it weighs only the last step's dLam).
+    // ---- P0: h0 and gy tiles (the chunk's scalars were computed during the previous chunk)
+    float* sLam = sSc + (c & 1) * NSC * Q;
+    float* sDel = sLam + Q;
+    float* sW = sDel + Q;
+    float* sEL = sW + Q;
+    float* sD = sEL + Q;
+    float* sCF1 = sD + Q;
+    // the previous chunk's grad_u and grad_C bulk stores must have read GYt and
+    // HH before they are rewritten below (grad_B's, from GP, may still run:
+    // the batch-1 issuer waits for it, E1 rewrites GP)
+    if (tid == 0) bulk_wait_read<1>();
+    __syncthreads();
+    const bool safe = sWide[c & 1] == 0;
     float psih0 = 0.f;
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const int r = cr0 + 32 * k;
+    for (int k = 0; k < 2; ++k) {
+      const int r = cr0 + 64 * k;
       const uint32_t off = umma::sw128_off(r, cd0);
-      const float4 hv = c > 0 ? h0v[k] : make_float4(0.f, 0.f, 0.f, 0.f);
-      *reinterpret_cast<uint2*>(tH0 + off) = pack4<T>(hv);
-      float pf[4];
-      unpack4<T>(*reinterpret_cast<const uint2*>(tPSI + off), pf);
-      psih0 += pf[0] * hv.x + pf[1] * hv.y + pf[2] * hv.z + pf[3] * hv.w;
-      const float4 g = gyv[k];
-      const uint2 hi = pack4<T>(g);
-      float hf[4];
-      unpack4<T>(hi, hf);
+      float hv[8], g[8], hf[8], t8[8];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const float4 a = c > 0 ? h0v[2 * k + j] : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float4 v = gyv[2 * k + j];
+        hv[4 * j] = a.x, hv[4 * j + 1] = a.y, hv[4 * j + 2] = a.z, hv[4 * j + 3] = a.w;
+        g[4 * j] = v.x, g[4 * j + 1] = v.y, g[4 * j + 2] = v.z, g[4 * j + 3] = v.w;
+      }
+      *reinterpret_cast<int4*>(tH0 + off) = pack8<T>(hv);
+      unpack8<T>(*reinterpret_cast<const int4*>(tPSI + off), hf);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) psih0 += hf[i] * hv[i];
+      const int4 hi = pack8<T>(g);
+      *reinterpret_cast<int4*>(tGY + off) = hi;
+      unpack8<T>(hi, hf);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) t8[i] = g[i] - hf[i];
+      *reinterpret_cast<int4*>(tGYt + off) = pack8<T>(t8);
       const float el = sEL[r];
-      *reinterpret_cast<uint2*>(tGY + off) = hi;
-      *reinterpret_cast<uint2*>(tGYt + off) = pack4<T>(make_float4(g.x - hf[0], g.y - hf[1], g.z - hf[2], g.w - hf[3]));
-      *reinterpret_cast<uint2*>(tHH + off) = pack4<T>(make_float4(el * g.x, el * g.y, el * g.z, el * g.w));
+#pragma unroll
+      for (int i = 0; i < 8; ++i) t8[i] = el * g[i];
+      *reinterpret_cast<int4*>(tHH + off) = pack8<T>(t8);
     }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) psih0 += __shfl_xor_sync(0xffffffffu, psih0, o);
+    if (lane == 0) sRed[32 + warp] = psih0;
     fence_proxy_async_smem();
-    const float psi_h0 = block_sum(psih0);  // includes a __syncthreads
+    __syncthreads();
 
     // ---- batch 1: S, P, Y2, R2, dPsi^T
     if (tid == 0) {
+      bulk_wait_read<0>();
       mbar_wait(&bar[0], tph & 1u);
       ++tph;
       umma::fence_after_sync();
@@ -907,7 +921,7 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
       // epilogue 3 to arrive.
       if (c > 0) {
         load_gy(c - 1);
-        if (tid < Q) dnext = ld_pinned_u16(delta + (row0 + (int64_t)(c - 1) * Q + tid) * H + h);
+        if (warp >= 4 && warp < 8) dnext = ld_pinned_u16(delta + (row0 + (int64_t)(c - 1) * Q + tid - 128) * H + h);
       }
       if (c > 1) load_h0(c - 1);
     }
@@ -935,35 +949,46 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
       tma_store_3d(&tm_gu, 0, h, (int)(row0 + (int64_t)c * Q), tGYt);
       bulk_commit();
     }
-    // ---- grad_delta and grad_A while batch 3 runs (thread t < Q)
-    {
-      float wm = 0.f;
-      if (tid < Q) wm = sW[tid] * sum4(sM, tid);
-      const float sum_wm = block_sum(wm);
-      float dl = 0.f;
-      if (tid < Q) {
-        const int t = tid;
-        dl = sum4(sRow, t) - sum4(sCol, t) + sEL[t] * sum4(sQ, t) - wm;
-        if (t == Q - 1) dl += sEL[Q - 1] * psi_h0 + sum_wm;
-      }
-      const float contrib = block_sum(tid < Q ? dl * sD[tid] : 0.f);
-      if (tid == 0) gA_acc += contrib;
-      // suffix sum of dLam over t (warps 0-3)
-      float suf = dl;
-      if (tid < Q) {
+    // ---- while batch 3 runs: grad_delta and grad_A (warps 0-3, thread t), and the
+    //      previous chunk's scalars (warps 4-7)
+    // dLam_t = x_t + [t = last] lastv with x_t = rowsum Z - colsum Z + exp(Lam_t) q_t - w_t m_t,
+    // lastv = exp(Lam_last) <Psi, h0> + sum_t w_t m_t; grad_delta_t = A sum_{t' >= t} dLam_t' + u_t.r_t
+    if (warp < 4) {
+      const int t = tid;
+      const float wm = sW[t] * sum4(sM, t);
+      const float x = sum4(sRow, t) - sum4(sCol, t) + sEL[t] * sum4(sQ, t) - wm;
+      float suf = x, swm = wm, sxd = x * sD[t];
 #pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const float n = __shfl_down_sync(0xffffffffu, suf, o);
-          if (lane + o < 32) suf += n;
-        }
-        if (lane == 0) sRed[32 + warp] = suf;
+      for (int o = 1; o < 32; o <<= 1) {
+        const float n = __shfl_down_sync(0xffffffffu, suf, o);
+        if (lane + o < 32) suf += n;
       }
-      __syncthreads();
-      if (tid < Q) {
-        for (int w = warp + 1; w < 4; ++w) suf += sRed[32 + w];
-        const float g = Ah * suf + sum4(sUR, tid);
-        gdelta[(row0 + (int64_t)c * Q + tid) * H + h] = from_f<T>(g);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        swm += __shfl_xor_sync(0xffffffffu, swm, o);
+        sxd += __shfl_xor_sync(0xffffffffu, sxd, o);
       }
+      if (lane == 0) {
+        sRed[warp] = suf;  // the warp's total of x
+        sRed[4 + warp] = swm;
+        sRed[8 + warp] = sxd;
+      }
+      named_barrier_sync(1, 128);
+      float sum_wm = 0.f, sum_xd = 0.f, later = 0.f, psi_h0 = 0.f;
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {
+        sum_wm += sRed[4 + v];
+        sum_xd += sRed[8 + v];
+        if (v > warp) later += sRed[v];
+      }
+#pragma unroll
+      for (int v = 0; v < NT / 32; ++v) psi_h0 += sRed[32 + v];
+      const float lastv = sEL[Q - 1] * psi_h0 + sum_wm;
+      if (t == 0) gA_acc += sum_xd + lastv * sD[Q - 1];
+      const float g = Ah * (suf + later + lastv) + sum4(sUR, t);
+      gdelta[(row0 + (int64_t)c * Q + t) * H + h] = from_f<T>(g);
+    } else if (warp < 8 && c > 0) {
+      chunk_scalars(dnext, tid - 128, (c - 1) & 1, 2);
     }
     mbar_wait(&bar[1], mph & 1u);
     ++mph;
@@ -1010,10 +1035,11 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     __syncthreads();
     if (tid == 0) {  // read back by the next chunk's P0 (bulk_wait_read_all) before reuse
       const int z = (int)(row0 + (int64_t)c * Q);
-      tma_store_3d(&tm_gB, 0, h, z, tGP);
-      tma_store_3d(&tm_gB, 64, h, z, tGP + TILE);
       tma_store_3d(&tm_gC, 0, h, z, tHH);
       tma_store_3d(&tm_gC, 64, h, z, tHH + TILE);
+      bulk_commit();
+      tma_store_3d(&tm_gB, 0, h, z, tGP);
+      tma_store_3d(&tm_gB, 64, h, z, tGP + TILE);
       bulk_commit();
     }
   }
