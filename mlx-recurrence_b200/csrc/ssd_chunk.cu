@@ -552,7 +552,7 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
                      int64_t ash, int L, int H, int seg, T* __restrict__ gdelta, float* __restrict__ gA_part) {
   using namespace ssdb;
   extern __shared__ unsigned char smem_raw[];
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem_raw);  // tma(u,B,C), mma
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem_raw);  // tma(u,B,C), mma, mma (batch 1 second group)
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 4);
   int* sWide = reinterpret_cast<int*>(tslot + 4);     // [2] a 16-step block spans a decay above e^40
   // [2][NSC][Q] per-chunk scalars, buffer c & 1 for chunk c: Lam_t, delta_t, w_t,
@@ -597,7 +597,7 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   const int cq0 = 32 * jq;         // first of this thread's 32 columns (t, s or n)
   const int ct0 = cq0 & 63;        // that column inside its 64-column tile
   if (tid == 0) {
-    for (int i = 0; i < 2; ++i) mbar_init(&bar[i], 1);
+    for (int i = 0; i < 3; ++i) mbar_init(&bar[i], 1);
     fence_mbar_init();
   }
   if (warp == 0) {
@@ -657,7 +657,7 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   load_gy(nck - 1);
   if (nck > 1) load_h0(nck - 1);
   float gA_acc = 0.f;
-  uint32_t tph = 0, mph = 0;
+  uint32_t tph = 0, mph = 0, mph2 = 0;
 
   auto sum4 = [&](const float* p, int i) { return (p[i] + p[Q + i]) + (p[2 * Q + i] + p[3 * Q + i]); };
   // A chunk's scalars from its delta (raw bits), by the 128 threads of one
@@ -751,7 +751,8 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     fence_proxy_async_smem();
     __syncthreads();
 
-    // ---- batch 1: S, P, Y2, R2, dPsi^T
+    // ---- batch 1, in two commit groups: dPsi^T, S, P (dPsi^T first: it reads the HH
+    //      tile that epilogue 1 rewrites), then Y2, R2
     if (tid == 0) {
       bulk_wait_read<0>();
       mbar_wait(&bar[0], tph & 1u);
@@ -760,13 +761,13 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
       const uint32_t aU = smem_u32(tU), aB = smem_u32(tB), aC = smem_u32(tC), aGY = smem_u32(tGY),
                      aEG = smem_u32(tHH), aPSI = smem_u32(tPSI), aH0 = smem_u32(tH0), aLo = smem_u32(tGYt);
 #pragma unroll
+      for (int k = 0; k < 8; ++k)
+        umma::mma_f16(tbase + 384, umma::sdesc_mn(aC + k * 2048, TILE), umma::sdesc_mn(aEG + k * 2048, TILE),
+                      id64MM, k > 0);
+#pragma unroll
       for (int k = 0; k < 8; ++k) {
         const uint32_t ko = (k >> 2) * TILE + (k & 3) * 32;
         umma::mma_f16(tbase + 0, umma::sdesc_k(aC + ko), umma::sdesc_k(aB + ko), id128KK, k > 0);
-        umma::mma_f16(tbase + 256, umma::sdesc_k(aC + ko), umma::sdesc_mn(aH0 + k * 2048, TILE), id64KM, k > 0);
-        umma::mma_f16(tbase + 320, umma::sdesc_k(aB + ko), umma::sdesc_mn(aPSI + k * 2048, TILE), id64KM, k > 0);
-        umma::mma_f16(tbase + 384, umma::sdesc_mn(aC + k * 2048, TILE), umma::sdesc_mn(aEG + k * 2048, TILE),
-                      id64MM, k > 0);
       }
 #pragma unroll
       for (int k = 0; k < 4; ++k)
@@ -775,36 +776,23 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
       for (int k = 0; k < 4; ++k)
         umma::mma_f16(tbase + 128, umma::sdesc_k(aLo + k * 32), umma::sdesc_k(aU + k * 32), id128KK, true);
       umma::commit(&bar[1]);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const uint32_t ko = (k >> 2) * TILE + (k & 3) * 32;
+        umma::mma_f16(tbase + 256, umma::sdesc_k(aC + ko), umma::sdesc_mn(aH0 + k * 2048, TILE), id64KM, k > 0);
+        umma::mma_f16(tbase + 320, umma::sdesc_k(aB + ko), umma::sdesc_mn(aPSI + k * 2048, TILE), id64KM, k > 0);
+      }
+      umma::commit(&bar[2]);
     }
     mbar_wait(&bar[1], mph & 1u);
     ++mph;
     umma::fence_after_sync();
 
-    // ---- epilogue 1 (thread: row s, t-columns cq0..cq0+31): G', H1, rowsum Z; gy.Y2; u.R2
+    // ---- epilogue 1 (thread: row s, t-columns cq0..cq0+31): G', H1, rowsum Z; then gy.Y2,
+    //      u.R2 and the Psi update (row n, channels ch0..)
     // exp(Lam_s - Lam_t) = exp(Lam_s - Lam_t0) * exp(Lam_t0 - Lam_t), t0 = block start
     {
       const int s = row;
-      // gy_s . Y2_s (gy as its hi + lo parts) and u_s . R2_s over this thread's channels
-      float y2[CH], r2[CH];
-      umma::tmem_ld16(tl + 256 + ch0, y2);
-      umma::tmem_ld16(tl + 320 + ch0, r2);
-      umma::tmem_wait_ld();
-      float qa = 0.f, ma = 0.f;
-#pragma unroll
-      for (int cc = 0; cc < CH / 8; ++cc) {
-        const uint32_t off = umma::sw128_off(s, ch0 + 8 * cc);
-        float f[8], g[8];
-        unpack8<T>(*reinterpret_cast<const int4*>(tGY + off), f);
-        unpack8<T>(*reinterpret_cast<const int4*>(tGYt + off), g);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) qa += (f[i] + g[i]) * y2[8 * cc + i];
-        unpack8<T>(*reinterpret_cast<const int4*>(tU + off), f);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) ma += f[i] * r2[8 * cc + i];
-      }
-      sQ[jq * Q + s] = qa;
-      sM[jq * Q + s] = ma;
-
       const float ls = sLam[s];
       float rz = 0.f;
       uint8_t* gp = tGP + (jq >> 1) * TILE;
@@ -863,6 +851,36 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
       }
       sRow[jq * Q + s] = rz;
       fence_proxy_async_smem();
+
+      mbar_wait(&bar[2], mph2 & 1u);
+      ++mph2;
+      umma::fence_after_sync();
+      // gy_s . Y2_s (gy as its hi + lo parts) and u_s . R2_s over this thread's channels
+      float y2[CH], r2[CH];
+      umma::tmem_ld16(tl + 256 + ch0, y2);
+      umma::tmem_ld16(tl + 320 + ch0, r2);
+      umma::tmem_wait_ld();
+      float qa = 0.f, ma = 0.f;
+#pragma unroll
+      for (int cc = 0; cc < CH / 8; ++cc) {
+        const uint32_t off = umma::sw128_off(s, ch0 + 8 * cc);
+        float f[8], g[8];
+        unpack8<T>(*reinterpret_cast<const int4*>(tGY + off), f);
+        unpack8<T>(*reinterpret_cast<const int4*>(tGYt + off), g);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) qa += (f[i] + g[i]) * y2[8 * cc + i];
+        unpack8<T>(*reinterpret_cast<const int4*>(tU + off), f);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ma += f[i] * r2[8 * cc + i];
+      }
+      sQ[jq * Q + s] = qa;
+      sM[jq * Q + s] = ma;
+      // Psi (row n = row) <- exp(Lam_last) Psi + dPsi; the 2-byte copy is replaced after batch 3
+      umma::tmem_ld16(tl + 384 + ch0, y2);
+      umma::tmem_wait_ld();
+      const float dec = __expf(sLam[Q - 1]);
+#pragma unroll
+      for (int i = 0; i < CH; ++i) psi[i] = dec * psi[i] + y2[i];
     }
     umma::fence_before_sync();
     __syncthreads();
@@ -880,22 +898,28 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
       }
       umma::commit(&bar[1]);
     }
+    // The next chunk's register operands, while batch 2 runs. A proxy fence waits
+    // for the thread's outstanding loads, so they are issued right after one,
+    // with batch 2 and epilogue 2 to arrive before the next.
+    if (c > 0) {
+      load_gy(c - 1);
+      if (warp >= 4 && warp < 8) dnext = ld_pinned_u16(delta + (row0 + (int64_t)(c - 1) * Q + tid - 128) * H + h);
+    }
+    if (c > 1) load_h0(c - 1);
     mbar_wait(&bar[1], mph & 1u);
     ++mph;
     umma::fence_after_sync();
 
-    // ---- epilogue 2 (thread: row t, channels ch0..): r, grad_u (staged in GYt), u.r; Psi update (row n)
+    // ---- epilogue 2 (thread: row t, channels ch0..): r, grad_u (staged in GYt), u.r
     {
       const int t = row;
       const float lt = sLam[t], dt = sDel[t];
       {
-        float r1[CH], r2[CH], dp[CH];
+        float r1[CH], r2[CH];
         umma::tmem_ld16(tl + 256 + ch0, r1);
         umma::tmem_ld16(tl + 320 + ch0, r2);
-        umma::tmem_ld16(tl + 384 + ch0, dp);
         umma::tmem_wait_ld();
         const float f2 = __expf(sLam[Q - 1] - lt);
-        const float dec = __expf(sLam[Q - 1]);
         float ur = 0.f;
 #pragma unroll
         for (int cc = 0; cc < CH / 8; ++cc) {
@@ -911,19 +935,8 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
           *reinterpret_cast<int4*>(tGYt + off) = pack8<T>(o);  // grad_u staging (GYt free after batch 2)
         }
         sUR[jq * Q + t] = ur;
-        // Psi (row n = row) <- exp(Lam_last) Psi + dPsi; the bf16 copy is replaced after batch 3
-#pragma unroll
-        for (int i = 0; i < CH; ++i) psi[i] = dec * psi[i] + dp[i];
       }
       fence_proxy_async_smem();
-      // The next chunk's register operands. A proxy fence waits for the thread's
-      // outstanding loads, so they are issued after this one and have batch 3 and
-      // epilogue 3 to arrive.
-      if (c > 0) {
-        load_gy(c - 1);
-        if (warp >= 4 && warp < 8) dnext = ld_pinned_u16(delta + (row0 + (int64_t)(c - 1) * Q + tid - 128) * H + h);
-      }
-      if (c > 1) load_h0(c - 1);
     }
     umma::fence_before_sync();
     __syncthreads();
