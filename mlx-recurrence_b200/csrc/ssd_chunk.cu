@@ -631,18 +631,15 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
 
   // grad_y and h0 of a chunk are [128 rows][64 channels] f32 and enter the
   // kernel through registers in a coalesced layout: thread i holds channels
-  // cd0..cd0+7 of rows cr0 + 64k, k = 0..1 (float4 v[2k + j] = channels
-  // cd0 + 4j..), so eight lanes cover a whole row (a row-per-lane layout
-  // would touch 32 cache lines per instruction) and the tiles are written
-  // with 16-byte stores.
-  const int cd0 = 8 * (tid & 7), cr0 = tid >> 3;
+  // cd0..cd0+3 of rows cr0 + 32k, k = 0..3, so a warp's load covers two whole
+  // rows, four cache lines (a row-per-lane layout would touch 32 lines per
+  // instruction).
+  const int cd0 = 4 * (tid & 15), cr0 = tid >> 4;
   float4 gyv[4];  // grad_y rows s
   auto load_gy = [&](int c) {
     const float* src = gy + ((row0 + (int64_t)c * Q + cr0) * H + h) * DH + cd0;
 #pragma unroll
-    for (int k = 0; k < 2; ++k)
-#pragma unroll
-      for (int j = 0; j < 2; ++j) gyv[2 * k + j] = ld_pinned_f4(src + (int64_t)64 * k * H * DH + 4 * j);
+    for (int k = 0; k < 4; ++k) gyv[k] = ld_pinned_f4(src + (int64_t)32 * k * H * DH);
   };
   // h0 of chunk c > 0: the checkpoint at the end of the previous segment, [N][Dh] (rows n)
   float4 h0v[4];
@@ -650,9 +647,7 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     const int64_t kk = ((int64_t)b * nseg + (c * Q) / seg - 1) * H + h;
     const float* src = ckpt + (kk * NS + cr0) * DH + cd0;
 #pragma unroll
-    for (int k = 0; k < 2; ++k)
-#pragma unroll
-      for (int j = 0; j < 2; ++j) h0v[2 * k + j] = ld_pinned_f4(src + 64 * k * DH + 4 * j);
+    for (int k = 0; k < 4; ++k) h0v[k] = ld_pinned_f4(src + 32 * k * DH);
   };
   load_gy(nck - 1);
   if (nck > 1) load_h0(nck - 1);
@@ -719,31 +714,22 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     const bool safe = sWide[c & 1] == 0;
     float psih0 = 0.f;
 #pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      const int r = cr0 + 64 * k;
+    for (int k = 0; k < 4; ++k) {
+      const int r = cr0 + 32 * k;
       const uint32_t off = umma::sw128_off(r, cd0);
-      float hv[8], g[8], hf[8], t8[8];
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const float4 a = c > 0 ? h0v[2 * k + j] : make_float4(0.f, 0.f, 0.f, 0.f);
-        const float4 v = gyv[2 * k + j];
-        hv[4 * j] = a.x, hv[4 * j + 1] = a.y, hv[4 * j + 2] = a.z, hv[4 * j + 3] = a.w;
-        g[4 * j] = v.x, g[4 * j + 1] = v.y, g[4 * j + 2] = v.z, g[4 * j + 3] = v.w;
-      }
-      *reinterpret_cast<int4*>(tH0 + off) = pack8<T>(hv);
-      unpack8<T>(*reinterpret_cast<const int4*>(tPSI + off), hf);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) psih0 += hf[i] * hv[i];
-      const int4 hi = pack8<T>(g);
-      *reinterpret_cast<int4*>(tGY + off) = hi;
-      unpack8<T>(hi, hf);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) t8[i] = g[i] - hf[i];
-      *reinterpret_cast<int4*>(tGYt + off) = pack8<T>(t8);
+      const float4 hv = c > 0 ? h0v[k] : make_float4(0.f, 0.f, 0.f, 0.f);
+      *reinterpret_cast<uint2*>(tH0 + off) = pack4<T>(hv);
+      float pf[4];
+      unpack4<T>(*reinterpret_cast<const uint2*>(tPSI + off), pf);
+      psih0 += pf[0] * hv.x + pf[1] * hv.y + pf[2] * hv.z + pf[3] * hv.w;
+      const float4 g = gyv[k];
+      const uint2 hi = pack4<T>(g);
+      float hf[4];
+      unpack4<T>(hi, hf);
       const float el = sEL[r];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) t8[i] = el * g[i];
-      *reinterpret_cast<int4*>(tHH + off) = pack8<T>(t8);
+      *reinterpret_cast<uint2*>(tGY + off) = hi;
+      *reinterpret_cast<uint2*>(tGYt + off) = pack4<T>(make_float4(g.x - hf[0], g.y - hf[1], g.z - hf[2], g.w - hf[3]));
+      *reinterpret_cast<uint2*>(tHH + off) = pack4<T>(make_float4(el * g.x, el * g.y, el * g.z, el * g.w));
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) psih0 += __shfl_xor_sync(0xffffffffu, psih0, o);
@@ -898,14 +884,14 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
       }
       umma::commit(&bar[1]);
     }
-    // The next chunk's register operands, while batch 2 runs. A proxy fence waits
-    // for the thread's outstanding loads, so they are issued right after one,
-    // with batch 2 and epilogue 2 to arrive before the next.
+    // The next chunk's register operands: grad_y here, while batch 2 runs, h0
+    // after epilogue 2 (an SM keeps a limited number of load bytes in flight).
+    // A proxy fence waits for the thread's outstanding loads, so each group is
+    // issued right after one, with a batch and an epilogue to arrive before the next.
     if (c > 0) {
       load_gy(c - 1);
       if (warp >= 4 && warp < 8) dnext = ld_pinned_u16(delta + (row0 + (int64_t)(c - 1) * Q + tid - 128) * H + h);
     }
-    if (c > 1) load_h0(c - 1);
     mbar_wait(&bar[1], mph & 1u);
     ++mph;
     umma::fence_after_sync();
@@ -937,6 +923,7 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
         sUR[jq * Q + t] = ur;
       }
       fence_proxy_async_smem();
+      if (c > 1) load_h0(c - 1);
     }
     umma::fence_before_sync();
     __syncthreads();
