@@ -143,10 +143,20 @@ MR_API int mr_ssd_bwd_noalloc(const float* grad_y, const float* grad_final, cons
 
 /* ---------------------------------------------------------------- GLA ---
  * q,k,v [B,L,H,Dh], gates [B,L,H] in `dtype`; y [B,L,H,Dh] f32;
- * h_ckpt [B,L/seg,H,Dh(i),Dh(j)] f32 (gla.py:62). */
+ * h_ckpt [B,L/seg,H,Dh(i),Dh(j)] f32 (gla.py:62).
+ * bf16/fp16 with Dh = 64, L % 128 == 0 and seg % 128 == 0 run on the tensor
+ * cores (chunks of 128 steps); units (batch row, head) with a gate outside
+ * [1e-3, 1] are then recomputed step by step, so every input gets the
+ * per-step result. */
 MR_API int mr_gla_fwd(const void* q, const void* k, const void* v, const void* gates, int dtype,
                int64_t batch, int64_t L, int64_t H, int64_t Dh, int64_t seg,
                float* y, float* h_ckpt, void* stream);
+
+/* Checkpoint spacing for the fastest GLA path when the caller only needs the
+ * segment rule and the final state: 128 when seg divides it and the
+ * tensor-core path applies (bf16/fp16, Dh = 64, L % 128 == 0), else seg.
+ * No reference counterpart (the reference always checkpoints at seg). Host-only. */
+MR_API int64_t mr_gla_preferred_seg(int dtype, int64_t L, int64_t Dh, int64_t seg);
 
 MR_API size_t mr_gla_bwd_workspace_bytes(int dtype, int64_t batch, int64_t L, int64_t H, int64_t Dh,
                                   int64_t seg);

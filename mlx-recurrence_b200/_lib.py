@@ -49,6 +49,7 @@ SIGNATURES = {
     "mr_ssd_bwd_noalloc": (_int, [_p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _int, _i64, _i64, _i64, _i64,
                                   _i64, _i64, _p, _p, _p, _p, _p, _p]),
     "mr_gla_fwd": (_int, [_p, _p, _p, _p, _int, _i64, _i64, _i64, _i64, _i64, _p, _p, _p]),
+    "mr_gla_preferred_seg": (_i64, [_int, _i64, _i64, _i64]),
     "mr_gla_bwd_workspace_bytes": (_sz, [_int, _i64, _i64, _i64, _i64, _i64]),
     "mr_gla_bwd": (_int, [_p, _p, _p, _p, _p, _p, _p, _int, _i64, _i64, _i64, _i64, _i64, _p, _p, _p,
                           _p, _p, _sz, _p]),

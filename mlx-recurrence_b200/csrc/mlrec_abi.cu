@@ -37,8 +37,12 @@ template <typename T> int rotlru_fwd_launch(const void*, const void*, const void
 template <typename T> int rotlru_bwd_launch(const float*, const float*, const float*, const void*, const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, void*, void*, void*, void*, float*, cudaStream_t);
 template <typename T> int ssd_seq_fwd_launch(const void*, const void*, const void*, const void*, const float*, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, float*, float*, cudaStream_t);
 template <typename T> int ssd_seq_bwd_launch(const float*, const float*, const float*, const void*, const void*, const void*, const void*, const float*, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, void*, void*, void*, void*, float*, void*, cudaStream_t);
-template <typename T> int gla_seq_fwd_launch(const void*, const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, int64_t, float*, float*, cudaStream_t);
-template <typename T> int gla_seq_bwd_launch(const float*, const float*, const float*, const void*, const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, int64_t, void*, void*, void*, void*, void*, cudaStream_t);
+template <typename T> int gla_seq_fwd_launch(const void*, const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, int64_t, float*, float*, cudaStream_t, int);
+template <typename T> int gla_seq_bwd_launch(const float*, const float*, const float*, const void*, const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, int64_t, void*, void*, void*, void*, void*, cudaStream_t, int);
+template <typename T> int gla_chunk_fwd_launch(const void*, const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, float*, float*, cudaStream_t);
+template <typename T> int gla_chunk_bwd_launch(const float*, const float*, const float*, const void*, const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, void*, void*, void*, void*, cudaStream_t);
+bool gla_chunk_supported(int dtype, int64_t L, int64_t Dh, int64_t seg);
+size_t gla_fallback_ws_bytes(int64_t, int64_t, int64_t, int64_t, int64_t);
 size_t rglru_bwd_ws_bytes(int64_t, int64_t, int64_t, int64_t);
 size_t rotlru_bwd_ws_bytes(int64_t, int64_t, int64_t, int64_t);
 size_t ssd_seq_bwd_ws_bytes(int64_t, int64_t, int64_t, int64_t, int64_t, int64_t);
@@ -354,13 +358,34 @@ int mr_gla_fwd(const void* q, const void* k, const void* v, const void* gates, i
   MR_TRY(gla_common_checks("mr_gla_fwd", dtype, batch, L, H, Dh, seg));
   MR_TRY(check_ptrs("mr_gla_fwd", {q, k, v, gates, y, h_ckpt}));
   cudaStream_t st = (cudaStream_t)stream;
-  MR_DTYPE_SWITCH(dtype, gla_seq_fwd_launch<T>(q, k, v, gates, batch, L, H, Dh, seg, y, h_ckpt, st));
+  if (gla_chunk_supported(dtype, L, Dh, seg)) {
+    // tensor-core chunks for every unit, then the per-step kernel redoes the
+    // units with a gate outside [1e-3, 1]
+    if (dtype == MR_BF16) {
+      MR_TRY(gla_chunk_fwd_launch<__nv_bfloat16>(q, k, v, gates, batch, L, H, seg, y, h_ckpt, st));
+      return gla_seq_fwd_launch<__nv_bfloat16>(q, k, v, gates, batch, L, H, Dh, seg, y, h_ckpt, st, 1);
+    }
+    MR_TRY(gla_chunk_fwd_launch<__half>(q, k, v, gates, batch, L, H, seg, y, h_ckpt, st));
+    return gla_seq_fwd_launch<__half>(q, k, v, gates, batch, L, H, Dh, seg, y, h_ckpt, st, 1);
+  }
+  MR_DTYPE_SWITCH(dtype, gla_seq_fwd_launch<T>(q, k, v, gates, batch, L, H, Dh, seg, y, h_ckpt, st, 0));
+}
+
+int64_t mr_gla_preferred_seg(int dtype, int64_t L, int64_t Dh, int64_t seg) {
+  const int64_t q = ssd_chunk_len();
+  if (seg > 0 && L % q == 0 && q % seg == 0 && gla_chunk_supported(dtype, L, Dh, q)) return q;
+  return seg;
+}
+
+// the backward's tensor-core path needs a checkpoint at every chunk start
+static bool gla_chunk_bwd(int dtype, int64_t L, int64_t Dh, int64_t seg) {
+  return gla_chunk_supported(dtype, L, Dh, seg) && seg == ssd_chunk_len();
 }
 
 size_t mr_gla_bwd_workspace_bytes(int dtype, int64_t batch, int64_t L, int64_t H, int64_t Dh,
                                   int64_t seg) {
-  (void)dtype;
   if (batch <= 0 || L <= 0 || H <= 0 || Dh <= 0 || seg <= 0) return 0;
+  if (gla_chunk_bwd(dtype, L, Dh, seg)) return gla_fallback_ws_bytes(batch, L, H, Dh, seg);
   return gla_seq_bwd_ws_bytes(batch, L, H, Dh, seg);
 }
 
@@ -373,15 +398,30 @@ int mr_gla_bwd(const float* grad_y, const float* grad_final, const float* h_ckpt
   MR_TRY(gla_common_checks("mr_gla_bwd", dtype, batch, L, H, Dh, seg));
   MR_TRY(check_ptrs("mr_gla_bwd", {grad_y, h_ckpt, q, k, v, gates, grad_q, grad_k, grad_v, grad_gates}));
   MR_TRY(check_opt_ptr("mr_gla_bwd", grad_final));
-  const size_t need = gla_seq_bwd_ws_bytes(batch, L, H, Dh, seg);
+  const bool chunk = gla_chunk_bwd(dtype, L, Dh, seg);
+  const size_t need = chunk ? gla_fallback_ws_bytes(batch, L, H, Dh, seg) : gla_seq_bwd_ws_bytes(batch, L, H, Dh, seg);
   if (workspace == nullptr || workspace_bytes < need)
     return set_error(MR_E_WORKSPACE, "mr_gla_bwd: workspace of %zu bytes required, got %zu", need,
                      workspace_bytes);
   MR_TRY(check_opt_ptr("mr_gla_bwd", workspace));
   cudaStream_t st = (cudaStream_t)stream;
+  if (chunk) {
+    // tensor-core chunks for every unit, then the per-step kernel redoes the
+    // units with a gate outside [1e-3, 1] (workspace: its scratch slots)
+    if (dtype == MR_BF16) {
+      MR_TRY(gla_chunk_bwd_launch<__nv_bfloat16>(grad_y, grad_final, h_ckpt, q, k, v, gates, batch, L, H, seg,
+                                                 grad_q, grad_k, grad_v, grad_gates, st));
+      return gla_seq_bwd_launch<__nv_bfloat16>(grad_y, grad_final, h_ckpt, q, k, v, gates, batch, L, H, Dh, seg,
+                                               grad_q, grad_k, grad_v, grad_gates, workspace, st, 1);
+    }
+    MR_TRY(gla_chunk_bwd_launch<__half>(grad_y, grad_final, h_ckpt, q, k, v, gates, batch, L, H, seg, grad_q,
+                                        grad_k, grad_v, grad_gates, st));
+    return gla_seq_bwd_launch<__half>(grad_y, grad_final, h_ckpt, q, k, v, gates, batch, L, H, Dh, seg, grad_q,
+                                      grad_k, grad_v, grad_gates, workspace, st, 1);
+  }
   MR_DTYPE_SWITCH(dtype, gla_seq_bwd_launch<T>(grad_y, grad_final, h_ckpt, q, k, v, gates, batch, L,
                                                H, Dh, seg, grad_q, grad_k, grad_v, grad_gates,
-                                               workspace, st));
+                                               workspace, st, 0));
 }
 
 }  // extern "C"

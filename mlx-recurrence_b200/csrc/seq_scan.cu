@@ -270,15 +270,28 @@ __global__ void sum_over_batch_kernel(const float* __restrict__ part, int64_t ba
 // GLA
 // ============================================================================
 
+// Gates the tensor-core GLA path computes to within tolerance (its chunk
+// algebra works in log g and divides by g for the gate gradient). Units with
+// any other gate are recomputed here after the chunk kernel ("only_bad").
+__device__ __forceinline__ bool gla_gate_ok(float g) { return g >= 1e-3f && g <= 1.f; }
+
+template <typename T>
+__device__ bool gla_unit_has_bad_gate(const T* __restrict__ gates, int64_t b, int h, int L, int H) {
+  bool bad = false;
+  for (int t = threadIdx.x; t < L; t += blockDim.x) bad |= !gla_gate_ok(to_f(gates[(b * L + t) * H + h]));
+  return __syncthreads_or(bad) != 0;
+}
+
 template <typename T, int R, int IK>
 __global__ void __launch_bounds__(kSeqThreads)
 gla_seq_fwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
                    const T* __restrict__ gates, int L, int H, int Dh, int seg,
-                   float* __restrict__ y, float* __restrict__ ckpt) {
+                   float* __restrict__ y, float* __restrict__ ckpt, int only_bad) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t b = blockIdx.x / H;
   const int h = blockIdx.x % H;
   const int nseg = L / seg;
+  if (only_bad && !gla_unit_has_bad_gate(gates, b, h, L, H)) return;
   float S[IK][R];
 #pragma unroll
   for (int i = 0; i < IK; ++i)
@@ -324,18 +337,22 @@ gla_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfina
                    const float* __restrict__ ckpt, const T* __restrict__ q,
                    const T* __restrict__ k, const T* __restrict__ v, const T* __restrict__ gates,
                    int L, int H, int Dh, int seg, T* __restrict__ gq, T* __restrict__ gk,
-                   T* __restrict__ gv, T* __restrict__ gg, float* __restrict__ scratch) {
+                   T* __restrict__ gv, T* __restrict__ gg, float* __restrict__ scratch, int units,
+                   int only_bad) {
   constexpr int NP = 32 * IK;
   __shared__ float pQ[kTS][8][NP];
   __shared__ float pK[kTS][8][NP];
   __shared__ float pg[kTS][8];
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int64_t b = blockIdx.x / H;
-  const int h = blockIdx.x % H;
   const int nseg = L / seg;
   constexpr int E = R * IK;
+  // one scratch slot per CTA; a CTA walks units blockIdx.x, + gridDim.x, ...
   float* scr = scratch + (int64_t)blockIdx.x * (seg + 1) * E * kSeqThreads + tid;
+  for (int unit = blockIdx.x; unit < units; unit += gridDim.x) {
+  const int64_t b = unit / H;
+  const int h = unit % H;
+  if (only_bad && !gla_unit_has_bad_gate(gates, b, h, L, H)) continue;
 
   float adj[IK][R];
 #pragma unroll
@@ -444,6 +461,8 @@ gla_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfina
       }
     }
   }
+  __syncthreads();  // the slot's scratch is reused by the next unit
+  }
 }
 
 // ============================================================================
@@ -464,6 +483,13 @@ size_t ssd_seq_bwd_ws_bytes(int64_t batch, int64_t L, int64_t H, int64_t Dh, int
 size_t gla_seq_bwd_ws_bytes(int64_t batch, int64_t L, int64_t H, int64_t Dh, int64_t seg) {
   const int64_t R = Dh / 8, IK = Dh / 32;
   return (size_t)batch * H * (seg + 1) * R * IK * kSeqThreads * sizeof(float);
+}
+// scratch slots of the GLA fallback after the tensor-core backward (units with
+// out-of-range gates, walked by this many CTAs)
+constexpr int64_t kGlaFallbackSlots = 16;
+size_t gla_fallback_ws_bytes(int64_t batch, int64_t L, int64_t H, int64_t Dh, int64_t seg) {
+  const int64_t slots = batch * H < kGlaFallbackSlots ? batch * H : kGlaFallbackSlots;
+  return gla_seq_bwd_ws_bytes(slots, L, 1, Dh, seg);
 }
 
 bool ssd_seq_supported(int64_t Dh, int64_t N) {
@@ -544,35 +570,41 @@ int ssd_seq_bwd_launch(const float* gy, const float* gf, const float* ckpt, cons
   return check_launch("sum_over_batch_kernel");
 }
 
+// only_bad: recompute just the units with a gate outside the tensor-core
+// path's range (gla_gate_ok), after that path has written every unit.
 template <typename T>
 int gla_seq_fwd_launch(const void* q, const void* k, const void* v, const void* g, int64_t batch,
                        int64_t L, int64_t H, int64_t Dh, int64_t seg, float* y, float* ckpt,
-                       cudaStream_t st) {
+                       cudaStream_t st, int only_bad) {
   dim3 grid((unsigned)(batch * H));
   const T *q_ = (const T*)q, *k_ = (const T*)k, *v_ = (const T*)v, *g_ = (const T*)g;
+  const int L_ = (int)L, H_ = (int)H, s_ = (int)seg;
   switch ((int)Dh) {
-    case 32: gla_seq_fwd_kernel<T, 4, 1><<<grid, kSeqThreads, 0, st>>>(q_, k_, v_, g_, (int)L, (int)H, 32, (int)seg, y, ckpt); break;
-    case 64: gla_seq_fwd_kernel<T, 8, 2><<<grid, kSeqThreads, 0, st>>>(q_, k_, v_, g_, (int)L, (int)H, 64, (int)seg, y, ckpt); break;
-    case 96: gla_seq_fwd_kernel<T, 12, 3><<<grid, kSeqThreads, 0, st>>>(q_, k_, v_, g_, (int)L, (int)H, 96, (int)seg, y, ckpt); break;
-    default: gla_seq_fwd_kernel<T, 16, 4><<<grid, kSeqThreads, 0, st>>>(q_, k_, v_, g_, (int)L, (int)H, 128, (int)seg, y, ckpt); break;
+    case 32: gla_seq_fwd_kernel<T, 4, 1><<<grid, kSeqThreads, 0, st>>>(q_, k_, v_, g_, L_, H_, 32, s_, y, ckpt, only_bad); break;
+    case 64: gla_seq_fwd_kernel<T, 8, 2><<<grid, kSeqThreads, 0, st>>>(q_, k_, v_, g_, L_, H_, 64, s_, y, ckpt, only_bad); break;
+    case 96: gla_seq_fwd_kernel<T, 12, 3><<<grid, kSeqThreads, 0, st>>>(q_, k_, v_, g_, L_, H_, 96, s_, y, ckpt, only_bad); break;
+    default: gla_seq_fwd_kernel<T, 16, 4><<<grid, kSeqThreads, 0, st>>>(q_, k_, v_, g_, L_, H_, 128, s_, y, ckpt, only_bad); break;
   }
   return check_launch("gla_seq_fwd_kernel");
 }
 
+// ws: gla_seq_bwd_ws_bytes (every unit) or, with only_bad, gla_fallback_ws_bytes
 template <typename T>
 int gla_seq_bwd_launch(const float* gy, const float* gf, const float* ckpt, const void* q,
                        const void* k, const void* v, const void* g, int64_t batch, int64_t L,
                        int64_t H, int64_t Dh, int64_t seg, void* gq, void* gk, void* gv, void* gg,
-                       void* ws, cudaStream_t st) {
-  dim3 grid((unsigned)(batch * H));
+                       void* ws, cudaStream_t st, int only_bad) {
+  const int64_t units = batch * H;
+  dim3 grid((unsigned)(only_bad ? (units < kGlaFallbackSlots ? units : kGlaFallbackSlots) : units));
   const T *q_ = (const T*)q, *k_ = (const T*)k, *v_ = (const T*)v, *g_ = (const T*)g;
   T *gq_ = (T*)gq, *gk_ = (T*)gk, *gv_ = (T*)gv, *gg_ = (T*)gg;
   float* scr = (float*)ws;
+  const int L_ = (int)L, H_ = (int)H, s_ = (int)seg, u_ = (int)units;
   switch ((int)Dh) {
-    case 32: gla_seq_bwd_kernel<T, 4, 1><<<grid, kSeqThreads, 0, st>>>(gy, gf, ckpt, q_, k_, v_, g_, (int)L, (int)H, 32, (int)seg, gq_, gk_, gv_, gg_, scr); break;
-    case 64: gla_seq_bwd_kernel<T, 8, 2><<<grid, kSeqThreads, 0, st>>>(gy, gf, ckpt, q_, k_, v_, g_, (int)L, (int)H, 64, (int)seg, gq_, gk_, gv_, gg_, scr); break;
-    case 96: gla_seq_bwd_kernel<T, 12, 3><<<grid, kSeqThreads, 0, st>>>(gy, gf, ckpt, q_, k_, v_, g_, (int)L, (int)H, 96, (int)seg, gq_, gk_, gv_, gg_, scr); break;
-    default: gla_seq_bwd_kernel<T, 16, 4><<<grid, kSeqThreads, 0, st>>>(gy, gf, ckpt, q_, k_, v_, g_, (int)L, (int)H, 128, (int)seg, gq_, gk_, gv_, gg_, scr); break;
+    case 32: gla_seq_bwd_kernel<T, 4, 1><<<grid, kSeqThreads, 0, st>>>(gy, gf, ckpt, q_, k_, v_, g_, L_, H_, 32, s_, gq_, gk_, gv_, gg_, scr, u_, only_bad); break;
+    case 64: gla_seq_bwd_kernel<T, 8, 2><<<grid, kSeqThreads, 0, st>>>(gy, gf, ckpt, q_, k_, v_, g_, L_, H_, 64, s_, gq_, gk_, gv_, gg_, scr, u_, only_bad); break;
+    case 96: gla_seq_bwd_kernel<T, 12, 3><<<grid, kSeqThreads, 0, st>>>(gy, gf, ckpt, q_, k_, v_, g_, L_, H_, 96, s_, gq_, gk_, gv_, gg_, scr, u_, only_bad); break;
+    default: gla_seq_bwd_kernel<T, 16, 4><<<grid, kSeqThreads, 0, st>>>(gy, gf, ckpt, q_, k_, v_, g_, L_, H_, 128, s_, gq_, gk_, gv_, gg_, scr, u_, only_bad); break;
   }
   return check_launch("gla_seq_bwd_kernel");
 }
@@ -587,11 +619,11 @@ int gla_seq_bwd_launch(const float* gy, const float* gf, const float* ckpt, cons
                                      void*, void*, void*, void*, float*, void*, cudaStream_t);    \
   template int gla_seq_fwd_launch<T>(const void*, const void*, const void*, const void*, int64_t,  \
                                      int64_t, int64_t, int64_t, int64_t, float*, float*,           \
-                                     cudaStream_t);                                                \
+                                     cudaStream_t, int);                                           \
   template int gla_seq_bwd_launch<T>(const float*, const float*, const float*, const void*,        \
                                      const void*, const void*, const void*, int64_t, int64_t,      \
                                      int64_t, int64_t, int64_t, void*, void*, void*, void*, void*, \
-                                     cudaStream_t);
+                                     cudaStream_t, int);
 MR_INST(float)
 MR_INST(__nv_bfloat16)
 MR_INST(__half)

@@ -32,18 +32,36 @@
 
 namespace mr {
 
+// The two recurrences on this path. SSD (Mamba-2): state [Dh, N = 128],
+// a_t = exp(delta_t A_h), input delta_t u_t B_t^T, output h C_t. GLA: state
+// [Dk = 64, Dv = 64] with a_t = g_t (the gate), input k_t v_t^T, output
+// q_t^T h; it is the SSD chunk algebra with N = 64, delta = 1, per-step log
+// decay log g_t and (u, B, C) = (v, k, q) - GLA's h[i][j] is SSD's h^T.
+struct SsdRec {
+  static constexpr bool kGla = false;
+  static constexpr int NS = 128;
+};
+struct GlaRec {
+  static constexpr bool kGla = true;
+  static constexpr int NS = 64;
+};
+
 namespace ssdc {
 constexpr int Q = 128;                 // chunk length (MMA M for t-rows)
 constexpr int DH = 64;                 // head dim (one 128-byte swizzle row)
-constexpr int NS = 128;                // state size N
 constexpr uint32_t TILE = 16384;       // [128 rows x 64 elements] 2-byte tile
-constexpr uint32_t STAGE = TILE * 5;   // u, B lo/hi, C lo/hi
 constexpr int NT = 512;                // threads: 16 warps
 constexpr int CH = 16;                 // state / y channels per thread
 // small arrays (Lam, delta, warp sums, barriers, TMEM slot) first, then the
 // 1024-byte-aligned tiles
 constexpr size_t SMALL = (3 * Q + 8) * 4 + 6 * 8 + 16;
-constexpr size_t SMEM = SMALL + 1023 + 2 * STAGE + 2 * TILE + TILE + TILE;
+template <typename V> struct Cfg {
+  static constexpr int NS = V::NS;                     // state size N (B, C width)
+  static constexpr int NB = NS / 64;                   // 64-wide tiles of B and C
+  static constexpr uint32_t STAGE = TILE * (1 + 2 * NB);  // u, B, C
+  // stages, G (2), U~, h^T; GLA adds a zero tile that pads the M = 64 product B^T U~
+  static constexpr size_t SMEM = SMALL + 1023 + 2 * STAGE + 4 * TILE + (V::kGla ? TILE : 0);
+};
 }  // namespace ssdc
 
 template <typename T> struct MmaFmt;
@@ -133,13 +151,26 @@ __device__ __forceinline__ int4 pack8(const float* f) {
   return r;
 }
 
-template <typename T>
+// decay input of step t: delta_t (SSD, log decay delta_t A_h) or the gate g_t
+// (GLA, log decay log g_t; a gate <= 0 or NaN is clamped to e^-80 - such units
+// are recomputed by the sequential kernels, see gla_gate_ok)
+template <typename V>
+__device__ __forceinline__ float step_log_decay(float x, float Ah) {
+  if constexpr (V::kGla)
+    return fmaxf(logf(x), -80.f);
+  else
+    return x * Ah;
+}
+
+template <typename T, typename V>
 __global__ void __launch_bounds__(ssdc::NT, 1)
 ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_constant__ CUtensorMap tm_B,
                      const __grid_constant__ CUtensorMap tm_C, const __grid_constant__ CUtensorMap tm_y,
                      const __grid_constant__ CUtensorMap tm_ck, const T* __restrict__ delta,
                      const float* __restrict__ A, int64_t ash, int L, int H, int seg) {
   using namespace ssdc;
+  constexpr int NS = Cfg<V>::NS, NB = Cfg<V>::NB;
+  constexpr uint32_t STAGE = Cfg<V>::STAGE;
   extern __shared__ unsigned char smem_raw[];
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem_raw);  // bc[2], u[2], mma
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 6);
@@ -148,15 +179,16 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   float* sCF = sDel + Q;                              // [Q] column factors (see E1)
   float* sWarp = sCF + Q;                             // [8]
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sWarp + 8) + 1023) & ~uintptr_t(1023));
-  uint8_t* stg0 = sm;            // stage s: u | B lo | B hi | C lo | C hi
+  uint8_t* stg0 = sm;            // stage s: u | B (NB tiles) | C (NB tiles)
   uint8_t* sG = sm + 2 * STAGE;  // G, two K-major tiles (s 0-63, 64-127); then y staging
   uint8_t* sUt = sG + 2 * TILE;  // U~, MN-major [s][d]; then checkpoint staging (n 0-63)
   uint8_t* sHt = sUt + TILE;     // h^T bf16, MN-major [n][d]
+  uint8_t* sZero = sHt + TILE;   // GLA: zeros, the n = 64..127 half of B^T in B^T U~
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bh = blockIdx.x;
   const int b = bh / H, h = bh % H;
-  const float Ah = A[(int64_t)h * ash];
+  const float Ah = V::kGla ? 0.f : A[(int64_t)h * ash];
   const int nck = L / Q;
   const int nseg = L / seg;
   const int64_t row0 = (int64_t)b * L;
@@ -175,6 +207,8 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   }
   // h0 = 0 for the first chunk's Y2 product
   for (int i = tid; i < (int)(TILE / 16); i += NT) reinterpret_cast<int4*>(sHt)[i] = make_int4(0, 0, 0, 0);
+  if constexpr (V::kGla)
+    for (int i = tid; i < (int)(TILE / 16); i += NT) reinterpret_cast<int4*>(sZero)[i] = make_int4(0, 0, 0, 0);
   fence_proxy_async_smem();
   __syncthreads();
   umma::fence_after_sync();
@@ -186,11 +220,12 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     const int st = c & 1;
     uint8_t* s = stg0 + st * STAGE;
     const int z = (int)(row0 + (int64_t)c * Q);
-    mbar_arrive_expect_tx(&bar[st], 4 * TILE);
-    tma_load_3d(s + TILE, &tm_B, 0, h, z, &bar[st]);
-    tma_load_3d(s + 2 * TILE, &tm_B, 64, h, z, &bar[st]);
-    tma_load_3d(s + 3 * TILE, &tm_C, 0, h, z, &bar[st]);
-    tma_load_3d(s + 4 * TILE, &tm_C, 64, h, z, &bar[st]);
+    mbar_arrive_expect_tx(&bar[st], 2 * NB * TILE);
+#pragma unroll
+    for (int j = 0; j < NB; ++j) {
+      tma_load_3d(s + (1 + j) * TILE, &tm_B, 64 * j, h, z, &bar[st]);
+      tma_load_3d(s + (1 + NB + j) * TILE, &tm_C, 64 * j, h, z, &bar[st]);
+    }
   };
   auto issue_u = [&](int c) {
     const int st = c & 1;
@@ -226,14 +261,14 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     const float dcur = u16_to_f<T>(dnext);
     float lam = 0.f;
     if (tid < Q) {
-      lam = dcur * Ah;
+      lam = step_log_decay<V>(dcur, Ah);
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         const float n = __shfl_up_sync(0xffffffffu, lam, o);
         if (lane >= o) lam += n;
       }
       if (lane == 31) sWarp[warp] = lam;
-      sDel[tid] = dcur;
+      sDel[tid] = V::kGla ? 1.f : dcur;
     }
     __syncthreads();
     if (tid < Q) {
@@ -283,7 +318,7 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     const int st = c & 1;
     uint8_t* sU = stg0 + st * STAGE;
     uint8_t* sB = sU + TILE;
-    uint8_t* sC = sU + 3 * TILE;
+    uint8_t* sC = sU + (1 + NB) * TILE;
     __syncthreads();  // U~, Lam of chunk c and h^T of chunk c-1 are in shared memory
 
     // ---- S = C B^T, Y2 = C h0^T, dH^T = B^T U~
@@ -301,9 +336,12 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
         const uint32_t ko = (k >> 2) * TILE + (k & 3) * 32;
         umma::mma_f16(tbase + 128, umma::sdesc_k(aC + ko), umma::sdesc_mn(aH + k * 2048, TILE), idY, k > 0);
       }
+      // B^T as an MN-major A operand of M = 128 state rows: its second 64-row
+      // block is B's second tile (SSD) or the zero tile (GLA, N = 64)
+      const uint32_t lboB = V::kGla ? smem_u32(sZero) - aB : TILE;
 #pragma unroll
       for (int k = 0; k < Q / 16; ++k)
-        umma::mma_f16(tbase + 192, umma::sdesc_mn(aB + k * 2048, TILE), umma::sdesc_mn(aUt + k * 2048, TILE),
+        umma::mma_f16(tbase + 192, umma::sdesc_mn(aB + k * 2048, lboB), umma::sdesc_mn(aUt + k * 2048, TILE),
                       idH, k > 0);
       umma::commit(&bar[4]);
     }
@@ -396,7 +434,7 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
                         a[i + 3] + e_t * bb[i + 3]);
     }
     const bool ck = ((c + 1) * Q) % seg == 0;
-    if (ck) {
+    if (ck && trow < NS) {
       const int n = trow;
       uint8_t* cb = (n < 64 ? sUt : sU) + (jq >> 1) * (TILE / 2);  // box [64 n][32 f32]
 #pragma unroll
@@ -415,8 +453,10 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
         const int zz = (int)(((int64_t)b * nseg + (c + 1) * Q / seg - 1) * H + h);
         tma_store_3d(&tm_ck, 0, 0, zz, sUt);
         tma_store_3d(&tm_ck, 32, 0, zz, sUt + TILE / 2);
-        tma_store_3d(&tm_ck, 0, 64, zz, sU);
-        tma_store_3d(&tm_ck, 32, 64, zz, sU + TILE / 2);
+        if constexpr (NS > 64) {
+          tma_store_3d(&tm_ck, 0, 64, zz, sU);
+          tma_store_3d(&tm_ck, 32, 64, zz, sU + TILE / 2);
+        }
       }
       bulk_commit();  // read back in the next prologue before the slots are reused
     }
@@ -435,15 +475,21 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
 // per head, L a multiple of the chunk. The forward writes checkpoints at any
 // multiple of the chunk; the backward needs one at every chunk start.
 bool ssd_chunk_supported(int dtype, int64_t L, int64_t Dh, int64_t N, int64_t seg, int64_t a_stride_n) {
-  return (dtype == MR_BF16 || dtype == MR_F16) && Dh == ssdc::DH && N == ssdc::NS && a_stride_n == 0 &&
+  return (dtype == MR_BF16 || dtype == MR_F16) && Dh == ssdc::DH && N == SsdRec::NS && a_stride_n == 0 &&
          L % ssdc::Q == 0 && seg % ssdc::Q == 0 && L <= (int64_t)INT32_MAX / 2;
+}
+// GLA on the tensor cores: bf16/fp16, Dh = 64 (state 64 x 64), L a multiple
+// of the chunk, checkpoints at chunk multiples.
+bool gla_chunk_supported(int dtype, int64_t L, int64_t Dh, int64_t seg) {
+  return (dtype == MR_BF16 || dtype == MR_F16) && Dh == ssdc::DH && L % ssdc::Q == 0 && seg % ssdc::Q == 0 &&
+         L <= (int64_t)INT32_MAX / 2;
 }
 bool ssd_chunk_bwd_supported(int dtype, int64_t L, int64_t Dh, int64_t N, int64_t seg, int64_t a_stride_n) {
   return ssd_chunk_supported(dtype, L, Dh, N, seg, a_stride_n) && seg == ssdc::Q;
 }
 int ssd_chunk_len() { return ssdc::Q; }
 
-template <typename T>
+template <typename T, int NS = SsdRec::NS>
 static int ssd_tmaps(const void* u, const void* Bm, const void* Cm, int64_t batch, int64_t L, int64_t H,
                      CUtensorMap* mu, CUtensorMap* mB, CUtensorMap* mC) {
   using namespace ssdc;
@@ -456,12 +502,14 @@ static int ssd_tmaps(const void* u, const void* Bm, const void* Cm, int64_t batc
   return MR_OK;
 }
 
-template <typename T>
-int ssd_chunk_fwd_launch(const void* u, const void* delta, const void* Bm, const void* Cm, const float* A,
-                         int64_t ash, int64_t batch, int64_t L, int64_t H, int64_t seg, float* y,
-                         float* ckpt, cudaStream_t st) {
+template <typename T, typename V>
+static int chunk_fwd_launch(const void* u, const void* delta, const void* Bm, const void* Cm, const float* A,
+                            int64_t ash, int64_t batch, int64_t L, int64_t H, int64_t seg, float* y,
+                            float* ckpt, cudaStream_t st) {
+  constexpr int NS = V::NS;
+  constexpr size_t SMEM = ssdc::Cfg<V>::SMEM;
   CUtensorMap mu, mB, mC, my, mck;
-  if (int rc = ssd_tmaps<T>(u, Bm, Cm, batch, L, H, &mu, &mB, &mC)) return rc;
+  if (int rc = ssd_tmaps<T, NS>(u, Bm, Cm, batch, L, H, &mu, &mB, &mC)) return rc;
   {
     using namespace ssdc;
     const auto F32 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
@@ -474,12 +522,27 @@ int ssd_chunk_fwd_launch(const void* u, const void* delta, const void* Bm, const
                               (uint64_t)NS * DH * 4, 32, 64, 1, SW))
       return rc;
   }
-  auto k = ssd_chunk_fwd_kernel<T>;
-  const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssdc::SMEM);
+  auto k = ssd_chunk_fwd_kernel<T, V>;
+  const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM);
   if (e != cudaSuccess) return set_error(MR_E_LAUNCH, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-  k<<<(unsigned)(batch * H), ssdc::NT, ssdc::SMEM, st>>>(mu, mB, mC, my, mck, (const T*)delta, A, ash, (int)L, (int)H,
-                                                    (int)seg);
-  return check_launch("ssd_chunk_fwd_kernel");
+  k<<<(unsigned)(batch * H), ssdc::NT, SMEM, st>>>(mu, mB, mC, my, mck, (const T*)delta, A, ash, (int)L, (int)H,
+                                                   (int)seg);
+  return check_launch(V::kGla ? "gla_chunk_fwd_kernel" : "ssd_chunk_fwd_kernel");
+}
+
+template <typename T>
+int ssd_chunk_fwd_launch(const void* u, const void* delta, const void* Bm, const void* Cm, const float* A,
+                         int64_t ash, int64_t batch, int64_t L, int64_t H, int64_t seg, float* y,
+                         float* ckpt, cudaStream_t st) {
+  return chunk_fwd_launch<T, SsdRec>(u, delta, Bm, Cm, A, ash, batch, L, H, seg, y, ckpt, st);
+}
+
+// GLA forward: (u, B, C, decay input) = (v, k, q, gates); y and the
+// checkpoints [B, L/seg, H, Dk, Dv] as the sequential kernel writes them.
+template <typename T>
+int gla_chunk_fwd_launch(const void* q, const void* k, const void* v, const void* gates, int64_t batch,
+                         int64_t L, int64_t H, int64_t seg, float* y, float* ckpt, cudaStream_t st) {
+  return chunk_fwd_launch<T, GlaRec>(v, gates, k, q, nullptr, 0, batch, L, H, seg, y, ckpt, st);
 }
 
 template int ssd_chunk_fwd_launch<__nv_bfloat16>(const void*, const void*, const void*, const void*,
@@ -488,6 +551,10 @@ template int ssd_chunk_fwd_launch<__nv_bfloat16>(const void*, const void*, const
 template int ssd_chunk_fwd_launch<__half>(const void*, const void*, const void*, const void*, const float*,
                                           int64_t, int64_t, int64_t, int64_t, int64_t, float*, float*,
                                           cudaStream_t);
+template int gla_chunk_fwd_launch<__nv_bfloat16>(const void*, const void*, const void*, const void*, int64_t,
+                                                 int64_t, int64_t, int64_t, float*, float*, cudaStream_t);
+template int gla_chunk_fwd_launch<__half>(const void*, const void*, const void*, const void*, int64_t, int64_t,
+                                          int64_t, int64_t, float*, float*, cudaStream_t);
 
 int ssdc_device_error(bool clear) { return read_device_error(clear); }
 
@@ -527,22 +594,26 @@ int ssdc_device_error(bool clear) { return read_device_error(clear); }
 // shared-memory and global latencies.
 
 namespace ssdb {
-constexpr int Q = 128, DH = 64, NS = 128;
+constexpr int Q = 128, DH = 64;
 constexpr int NT = 512;          // threads
 constexpr int CQ = 4;            // column quarters (warps per TMEM lane quarter)
 constexpr int CH = DH / CQ;      // channels per thread
 constexpr uint32_t TILE = 16384;
-// tiles: U, B lo/hi, C lo/hi, GY, GYt, PSI, H0, GP lo/hi, HH lo/hi
-constexpr int NTILE = 13;
-// per-chunk scalars (Lam, delta, w, exp(Lam), D, CF1) in two buffers; row/col/q/m/ur
-// partials per column quarter; reduction scratch
+// per-chunk scalars (Lam, delta, w, exp(Lam), D or the gate, CF1) in two buffers;
+// row/col/q/m/ur partials per column quarter; reduction scratch
 constexpr int NSC = 6;
 constexpr int NSMALLF = 2 * NSC * Q + 5 * CQ * Q + 64;
 constexpr size_t SMALL = NSMALLF * 4 + 4 * 8 + 16 + 16;
-constexpr size_t SMEM = SMALL + 1023 + NTILE * TILE;
+template <typename V> struct Cfg {
+  static constexpr int NS = V::NS;
+  static constexpr int NB = NS / 64;  // 64-wide tiles of B and C
+  // tiles: U, B, C, GY, GYt, PSI, H0, GP (2), HH (2); GLA adds a zero tile (M = 64 padding)
+  static constexpr int NTILE = 9 + 2 * NB + (V::kGla ? 1 : 0);
+  static constexpr size_t SMEM = SMALL + 1023 + NTILE * TILE;
+};
 }  // namespace ssdb
 
-template <typename T>
+template <typename T, typename V>
 __global__ void __launch_bounds__(ssdb::NT, 1)
 ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_constant__ CUtensorMap tm_B,
                      const __grid_constant__ CUtensorMap tm_C, const __grid_constant__ CUtensorMap tm_gu,
@@ -551,6 +622,8 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
                      const float* __restrict__ gfinal, const T* __restrict__ delta, const float* __restrict__ A,
                      int64_t ash, int L, int H, int seg, T* __restrict__ gdelta, float* __restrict__ gA_part) {
   using namespace ssdb;
+  constexpr int NS = Cfg<V>::NS, NB = Cfg<V>::NB;
+  constexpr int NCT = NS / CQ;  // state columns n per thread in epilogue 3 (16-column blocks: NCT / 16)
   extern __shared__ unsigned char smem_raw[];
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem_raw);  // tma(u,B,C), mma, mma (batch 1 second group)
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 4);
@@ -567,19 +640,20 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   // sRed: [0,12) grad_delta warp sums, [16,24) scalar scan, [32,48) <Psi, h0> warp partials
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sRed + 64) + 1023) & ~uintptr_t(1023));
   uint8_t* tU = sm;
-  uint8_t* tB = tU + TILE;        // 2 tiles
-  uint8_t* tC = tB + 2 * TILE;    // 2 tiles
-  uint8_t* tGY = tC + 2 * TILE;   // gy bf16 [s][d]
+  uint8_t* tB = tU + TILE;        // NB tiles
+  uint8_t* tC = tB + NB * TILE;   // NB tiles
+  uint8_t* tGY = tC + NB * TILE;  // gy bf16 [s][d]
   uint8_t* tGYt = tGY + TILE;     // gy lo part [s][d] (batches 1, 2); then grad_u staging
   uint8_t* tPSI = tGYt + TILE;    // Psi^T bf16 [n][d]
   uint8_t* tH0 = tPSI + TILE;     // h0^T bf16 [n][d]
   uint8_t* tGP = tH0 + TILE;      // G' [s][t], 2 tiles (t halves); then grad_B staging
   uint8_t* tHH = tGP + 2 * TILE;  // exp(Lam_s) gy [s][d] (batch 1); H1 [s][t], 2 tiles; grad_C staging
+  uint8_t* tZero = tHH + 2 * TILE;  // GLA: zeros, the n = 64..127 half of C^T in dPsi^T
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bh = blockIdx.x;
   const int b = bh / H, h = bh % H;
-  const float Ah = A[(int64_t)h * ash];
+  const float Ah = V::kGla ? 0.f : A[(int64_t)h * ash];
   const int nck = L / Q;
   const int nseg = L / seg;
   const int64_t row0 = (int64_t)b * L;
@@ -587,8 +661,9 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   constexpr uint32_t id128KK = umma::idesc_f16(128, 128, fmt, 0, 0);
   constexpr uint32_t id64KM = umma::idesc_f16(128, 64, fmt, 0, 1);
   constexpr uint32_t id64MM = umma::idesc_f16(128, 64, fmt, 1, 1);
-  constexpr uint32_t id128MM = umma::idesc_f16(128, 128, fmt, 1, 1);
-  constexpr uint32_t id128KM = umma::idesc_f16(128, 128, fmt, 0, 1);
+  constexpr uint32_t idNMM = umma::idesc_f16(128, NS, fmt, 1, 1);  // batch 3 products, N = state size
+  constexpr uint32_t idNKM = umma::idesc_f16(128, NS, fmt, 0, 1);
+  constexpr uint32_t idNKK = umma::idesc_f16(128, NS, fmt, 0, 0);
 
   const int q4 = warp & 3, jq = warp >> 2;
   const int row = 32 * q4 + lane;  // the row (s, t or n) this thread owns in TMEM
@@ -605,10 +680,18 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     umma::tmem_relinquish();
   }
   // Psi = dL/d(final state), thread (n = row, channels ch0..): gfinal is [B,H,Dh,N]
+  // (SSD) or [B,H,Dk,Dv] = [.., n, d] (GLA)
   float psi[CH];
 #pragma unroll
-  for (int i = 0; i < CH; ++i)
-    psi[i] = gfinal != nullptr ? gfinal[(((int64_t)b * H + h) * DH + ch0 + i) * NS + row] : 0.f;
+  for (int i = 0; i < CH; ++i) {
+    const int64_t bh64 = (int64_t)b * H + h;
+    if constexpr (V::kGla)
+      psi[i] = (gfinal != nullptr && row < NS) ? gfinal[(bh64 * NS + row) * DH + ch0 + i] : 0.f;
+    else
+      psi[i] = gfinal != nullptr ? gfinal[(bh64 * DH + ch0 + i) * NS + row] : 0.f;
+  }
+  if constexpr (V::kGla)
+    for (int i = tid; i < (int)(TILE / 16); i += NT) reinterpret_cast<int4*>(tZero)[i] = make_int4(0, 0, 0, 0);
 #pragma unroll
   for (int cc = 0; cc < CH / 8; ++cc)
     *reinterpret_cast<int4*>(tPSI + umma::sw128_off(row, ch0 + 8 * cc)) = pack8<T>(psi + 8 * cc);
@@ -620,12 +703,13 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
 
   auto issue = [&](int c) {  // thread 0: u, B, C of chunk c
     const int z = (int)(row0 + (int64_t)c * Q);
-    mbar_arrive_expect_tx(&bar[0], 5 * TILE);
+    mbar_arrive_expect_tx(&bar[0], (1 + 2 * NB) * TILE);
     tma_load_3d(tU, &tm_u, 0, h, z, &bar[0]);
-    tma_load_3d(tB, &tm_B, 0, h, z, &bar[0]);
-    tma_load_3d(tB + TILE, &tm_B, 64, h, z, &bar[0]);
-    tma_load_3d(tC, &tm_C, 0, h, z, &bar[0]);
-    tma_load_3d(tC + TILE, &tm_C, 64, h, z, &bar[0]);
+#pragma unroll
+    for (int j = 0; j < NB; ++j) {
+      tma_load_3d(tB + j * TILE, &tm_B, 64 * j, h, z, &bar[0]);
+      tma_load_3d(tC + j * TILE, &tm_C, 64 * j, h, z, &bar[0]);
+    }
   };
   if (tid == 0) issue(nck - 1);
 
@@ -647,7 +731,7 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     const int64_t kk = ((int64_t)b * nseg + (c * Q) / seg - 1) * H + h;
     const float* src = ckpt + (kk * NS + cr0) * DH + cd0;
 #pragma unroll
-    for (int k = 0; k < 4; ++k) h0v[k] = ld_pinned_f4(src + 32 * k * DH);
+    for (int k = 0; k < NS / 32; ++k) h0v[k] = ld_pinned_f4(src + 32 * k * DH);
   };
   load_gy(nck - 1);
   if (nck > 1) load_h0(nck - 1);
@@ -659,8 +743,8 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   // named barrier group (t = index in the group) into buffer buf.
   auto chunk_scalars = [&](unsigned short dbits, int t, int buf, int barid) {
     float* sl = sSc + buf * NSC * Q;
-    const float dcur = u16_to_f<T>(dbits);
-    float lam = dcur * Ah, dsum = dcur;
+    const float dcur = u16_to_f<T>(dbits);  // delta_t (SSD) or the gate g_t (GLA)
+    float lam = step_log_decay<V>(dcur, Ah), dsum = dcur;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const float n1 = __shfl_up_sync(0xffffffffu, lam, o);
@@ -682,10 +766,10 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
       dsum += sRed[20 + v];
     }
     sl[t] = lam;
-    sl[Q + t] = dcur;
-    sl[4 * Q + t] = dsum;
+    sl[Q + t] = V::kGla ? 1.f : dcur;      // delta (1 for GLA)
+    sl[4 * Q + t] = V::kGla ? dcur : dsum;  // D_t for dL/dA (SSD) or the gate (GLA)
     named_barrier_sync(barid, 128);
-    sl[2 * Q + t] = __expf(sl[Q - 1] - lam) * dcur;
+    sl[2 * Q + t] = __expf(sl[Q - 1] - lam) * (V::kGla ? 1.f : dcur);
     sl[3 * Q + t] = __expf(lam);
     const float span = sl[t & ~15] - lam;
     sl[5 * Q + t] = __expf(span);
@@ -717,7 +801,7 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     for (int k = 0; k < 4; ++k) {
       const int r = cr0 + 32 * k;
       const uint32_t off = umma::sw128_off(r, cd0);
-      const float4 hv = c > 0 ? h0v[k] : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4 hv = (c > 0 && r < NS) ? h0v[k < NS / 32 ? k : 0] : make_float4(0.f, 0.f, 0.f, 0.f);
       *reinterpret_cast<uint2*>(tH0 + off) = pack4<T>(hv);
       float pf[4];
       unpack4<T>(*reinterpret_cast<const uint2*>(tPSI + off), pf);
@@ -746,12 +830,15 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
       umma::fence_after_sync();
       const uint32_t aU = smem_u32(tU), aB = smem_u32(tB), aC = smem_u32(tC), aGY = smem_u32(tGY),
                      aEG = smem_u32(tHH), aPSI = smem_u32(tPSI), aH0 = smem_u32(tH0), aLo = smem_u32(tGYt);
+      // C^T as an MN-major A operand of M = 128 state rows: its second 64-row block is
+      // C's second tile (SSD) or the zero tile (GLA, N = 64)
+      const uint32_t lboC = V::kGla ? smem_u32(tZero) - aC : TILE;
 #pragma unroll
       for (int k = 0; k < 8; ++k)
-        umma::mma_f16(tbase + 384, umma::sdesc_mn(aC + k * 2048, TILE), umma::sdesc_mn(aEG + k * 2048, TILE),
+        umma::mma_f16(tbase + 384, umma::sdesc_mn(aC + k * 2048, lboC), umma::sdesc_mn(aEG + k * 2048, TILE),
                       id64MM, k > 0);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
+      for (int k = 0; k < NS / 16; ++k) {
         const uint32_t ko = (k >> 2) * TILE + (k & 3) * 32;
         umma::mma_f16(tbase + 0, umma::sdesc_k(aC + ko), umma::sdesc_k(aB + ko), id128KK, k > 0);
       }
@@ -763,7 +850,7 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
         umma::mma_f16(tbase + 128, umma::sdesc_k(aLo + k * 32), umma::sdesc_k(aU + k * 32), id128KK, true);
       umma::commit(&bar[1]);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
+      for (int k = 0; k < NS / 16; ++k) {
         const uint32_t ko = (k >> 2) * TILE + (k & 3) * 32;
         umma::mma_f16(tbase + 256, umma::sdesc_k(aC + ko), umma::sdesc_mn(aH0 + k * 2048, TILE), id64KM, k > 0);
         umma::mma_f16(tbase + 320, umma::sdesc_k(aB + ko), umma::sdesc_mn(aPSI + k * 2048, TILE), id64KM, k > 0);
@@ -928,7 +1015,8 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     umma::fence_before_sync();
     __syncthreads();
 
-    // ---- batch 3: gB1 = H1^T C, gC1 = H1 B, gB2 = u Psi(old), gC2 = gy h0; store grad_u
+    // ---- batch 3: gB1 = H1^T C, gC1 = H1 B, gB2 = u Psi(old), gC2 = gy h0 at columns 0, N, 2N, 3N;
+    //      store grad_u
     if (tid == 0) {
       umma::fence_after_sync();
       const uint32_t aU = smem_u32(tU), aB = smem_u32(tB), aC = smem_u32(tC), aGY = smem_u32(tGY),
@@ -937,13 +1025,13 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
       for (int k = 0; k < 8; ++k) {
         const uint32_t ko = (k >> 2) * TILE + (k & 3) * 32;
         umma::mma_f16(tbase + 0, umma::sdesc_mn(aHH + k * 2048, TILE), umma::sdesc_mn(aC + k * 2048, TILE),
-                      id128MM, k > 0);
-        umma::mma_f16(tbase + 128, umma::sdesc_k(aHH + ko), umma::sdesc_mn(aB + k * 2048, TILE), id128KM, k > 0);
+                      idNMM, k > 0);
+        umma::mma_f16(tbase + NS, umma::sdesc_k(aHH + ko), umma::sdesc_mn(aB + k * 2048, TILE), idNKM, k > 0);
       }
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        umma::mma_f16(tbase + 384, umma::sdesc_k(aGY + k * 32), umma::sdesc_k(aH0 + k * 32), id128KK, k > 0);
-        umma::mma_f16(tbase + 256, umma::sdesc_k(aU + k * 32), umma::sdesc_k(aPSI + k * 32), id128KK, k > 0);
+        umma::mma_f16(tbase + 3 * NS, umma::sdesc_k(aGY + k * 32), umma::sdesc_k(aH0 + k * 32), idNKK, k > 0);
+        umma::mma_f16(tbase + 2 * NS, umma::sdesc_k(aU + k * 32), umma::sdesc_k(aPSI + k * 32), idNKK, k > 0);
       }
       umma::commit(&bar[1]);
       tma_store_3d(&tm_gu, 0, h, (int)(row0 + (int64_t)c * Q), tGYt);
@@ -984,8 +1072,14 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
 #pragma unroll
       for (int v = 0; v < NT / 32; ++v) psi_h0 += sRed[32 + v];
       const float lastv = sEL[Q - 1] * psi_h0 + sum_wm;
-      if (t == 0) gA_acc += sum_xd + lastv * sD[Q - 1];
-      const float g = Ah * (suf + later + lastv) + sum4(sUR, t);
+      const float dlam = suf + later + lastv;  // dL/d(log decay of step t)
+      float g;
+      if constexpr (V::kGla) {
+        g = dlam / sD[t];  // dL/dg_t = dL/dlog(g_t) / g_t (sD holds the gate)
+      } else {
+        if (t == 0) gA_acc += sum_xd + lastv * sD[Q - 1];
+        g = Ah * dlam + sum4(sUR, t);
+      }
       gdelta[(row0 + (int64_t)c * Q + t) * H + h] = from_f<T>(g);
     } else if (warp < 8 && c > 0) {
       chunk_scalars(dnext, tid - 128, (c - 1) & 1, 2);
@@ -999,26 +1093,28 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
       issue(c - 1);
     }
 
-    // ---- epilogue 3: stage grad_B (row t) in GP, grad_C (row s) in HH (columns n = cq0..); new Psi^T
+    // ---- epilogue 3: stage grad_B (row t) in GP, grad_C (row s) in HH (columns n = NCT * jq..);
+    //      new Psi^T
     {
       const int t = row;
       const float wt = sW[t], et = sEL[t];
-      uint8_t* gbt = tGP + (jq >> 1) * TILE;
-      uint8_t* gct = tHH + (jq >> 1) * TILE;
+      const int nc0 = NCT * jq;  // first state column of this thread
+      uint8_t* gbt = tGP + (nc0 >> 6) * TILE;
+      uint8_t* gct = tHH + (nc0 >> 6) * TILE;
 #pragma unroll
-      for (int cb = 0; cb < 2; ++cb) {
-        const int col = cq0 + 16 * cb;
-        const uint32_t o0 = umma::sw128_off(t, ct0 + 16 * cb), o1 = umma::sw128_off(t, ct0 + 16 * cb + 8);
+      for (int cb = 0; cb < NCT / 16; ++cb) {
+        const int col = nc0 + 16 * cb;
+        const uint32_t o0 = umma::sw128_off(t, (col & 63)), o1 = umma::sw128_off(t, (col & 63) + 8);
         float v1[16], v2[16];
         umma::tmem_ld16(tl + 0 + col, v1);  // gB1 + w_t gB2
-        umma::tmem_ld16(tl + 256 + col, v2);
+        umma::tmem_ld16(tl + 2 * NS + col, v2);
         umma::tmem_wait_ld();
 #pragma unroll
         for (int i = 0; i < 16; ++i) v1[i] += wt * v2[i];
         *reinterpret_cast<int4*>(gbt + o0) = pack8<T>(v1);
         *reinterpret_cast<int4*>(gbt + o1) = pack8<T>(v1 + 8);
-        umma::tmem_ld16(tl + 128 + col, v1);  // gC1 + exp(Lam_s) gC2
-        umma::tmem_ld16(tl + 384 + col, v2);
+        umma::tmem_ld16(tl + NS + col, v1);  // gC1 + exp(Lam_s) gC2
+        umma::tmem_ld16(tl + 3 * NS + col, v2);
         umma::tmem_wait_ld();
 #pragma unroll
         for (int i = 0; i < 16; ++i) v1[i] += et * v2[i];
@@ -1035,16 +1131,16 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     __syncthreads();
     if (tid == 0) {  // read back by the next chunk's P0 (bulk_wait_read_all) before reuse
       const int z = (int)(row0 + (int64_t)c * Q);
-      tma_store_3d(&tm_gC, 0, h, z, tHH);
-      tma_store_3d(&tm_gC, 64, h, z, tHH + TILE);
+#pragma unroll
+      for (int j = 0; j < NB; ++j) tma_store_3d(&tm_gC, 64 * j, h, z, tHH + j * TILE);
       bulk_commit();
-      tma_store_3d(&tm_gB, 0, h, z, tGP);
-      tma_store_3d(&tm_gB, 64, h, z, tGP + TILE);
+#pragma unroll
+      for (int j = 0; j < NB; ++j) tma_store_3d(&tm_gB, 64 * j, h, z, tGP + j * TILE);
       bulk_commit();
     }
   }
   if (tid == 0) {
-    gA_part[bh] = gA_acc;
+    if constexpr (!V::kGla) gA_part[bh] = gA_acc;
     bulk_wait_all();
   }
   __syncthreads();
@@ -1061,23 +1157,44 @@ __global__ void ssd_ga_head_kernel(const float* __restrict__ part, int B, int H,
   gA[i] = s / (float)N;
 }
 
+template <typename T, typename V>
+static int chunk_bwd_launch(const float* gy, const float* gf, const float* ckpt, const void* u, const void* delta,
+                            const void* Bm, const void* Cm, const float* A, int64_t ash, int64_t batch, int64_t L,
+                            int64_t H, int64_t seg, void* gu, void* gd, void* gB, void* gC, float* ws,
+                            cudaStream_t st) {
+  constexpr size_t SMEM = ssdb::Cfg<V>::SMEM;
+  CUtensorMap mu, mB, mC, mgu, mgB, mgC;
+  if (int rc = ssd_tmaps<T, V::NS>(u, Bm, Cm, batch, L, H, &mu, &mB, &mC)) return rc;
+  if (int rc = ssd_tmaps<T, V::NS>(gu, gB, gC, batch, L, H, &mgu, &mgB, &mgC)) return rc;
+  auto k = ssd_chunk_bwd_kernel<T, V>;
+  const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM);
+  if (e != cudaSuccess) return set_error(MR_E_LAUNCH, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  k<<<(unsigned)(batch * H), ssdb::NT, SMEM, st>>>(mu, mB, mC, mgu, mgB, mgC, ckpt, gy, gf, (const T*)delta, A, ash,
+                                                   (int)L, (int)H, (int)seg, (T*)gd, ws);
+  return check_launch(V::kGla ? "gla_chunk_bwd_kernel" : "ssd_chunk_bwd_kernel");
+}
+
 template <typename T>
 int ssd_chunk_bwd_launch(const float* gy, const float* gf, const float* ckpt, const void* u, const void* delta,
                          const void* Bm, const void* Cm, const float* A, int64_t ash, int64_t batch, int64_t L,
                          int64_t H, int64_t seg, void* gu, void* gd, void* gB, void* gC, float* gA,
                          float* ws, cudaStream_t st) {
-  CUtensorMap mu, mB, mC, mgu, mgB, mgC;
-  if (int rc = ssd_tmaps<T>(u, Bm, Cm, batch, L, H, &mu, &mB, &mC)) return rc;
-  if (int rc = ssd_tmaps<T>(gu, gB, gC, batch, L, H, &mgu, &mgB, &mgC)) return rc;
-  auto k = ssd_chunk_bwd_kernel<T>;
-  const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssdb::SMEM);
-  if (e != cudaSuccess) return set_error(MR_E_LAUNCH, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-  k<<<(unsigned)(batch * H), ssdb::NT, ssdb::SMEM, st>>>(mu, mB, mC, mgu, mgB, mgC, ckpt, gy, gf, (const T*)delta, A,
-                                                         ash, (int)L, (int)H, (int)seg, (T*)gd, ws);
-  if (int rc = check_launch("ssd_chunk_bwd_kernel")) return rc;
-  const int HN = (int)(H * ssdb::NS);
-  ssd_ga_head_kernel<<<(HN + 255) / 256, 256, 0, st>>>(ws, (int)batch, (int)H, ssdb::NS, gA);
+  if (int rc = chunk_bwd_launch<T, SsdRec>(gy, gf, ckpt, u, delta, Bm, Cm, A, ash, batch, L, H, seg, gu, gd, gB,
+                                           gC, ws, st))
+    return rc;
+  const int HN = (int)(H * SsdRec::NS);
+  ssd_ga_head_kernel<<<(HN + 255) / 256, 256, 0, st>>>(ws, (int)batch, (int)H, SsdRec::NS, gA);
   return check_launch("ssd_ga_head_kernel");
+}
+
+// GLA backward on the tensor cores: grads (q, k, v, gates) = (gC, gB, gu, gdelta)
+// of the SSD algebra with (u, B, C) = (v, k, q); checkpoints at every chunk.
+template <typename T>
+int gla_chunk_bwd_launch(const float* gy, const float* gf, const float* ckpt, const void* q, const void* k,
+                         const void* v, const void* gates, int64_t batch, int64_t L, int64_t H, int64_t seg,
+                         void* gq, void* gk, void* gv, void* gg, cudaStream_t st) {
+  return chunk_bwd_launch<T, GlaRec>(gy, gf, ckpt, v, gates, k, q, nullptr, 0, batch, L, H, seg, gv, gg, gk, gq,
+                                     nullptr, st);
 }
 
 size_t ssd_chunk_bwd_ws_bytes(int64_t batch, int64_t H) { return (size_t)batch * H * sizeof(float); }
@@ -1090,6 +1207,12 @@ template int ssd_chunk_bwd_launch<__half>(const float*, const float*, const floa
                                           const void*, const void*, const float*, int64_t, int64_t, int64_t,
                                           int64_t, int64_t, void*, void*, void*, void*, float*, float*,
                                           cudaStream_t);
+template int gla_chunk_bwd_launch<__nv_bfloat16>(const float*, const float*, const float*, const void*,
+                                                 const void*, const void*, const void*, int64_t, int64_t,
+                                                 int64_t, int64_t, void*, void*, void*, void*, cudaStream_t);
+template int gla_chunk_bwd_launch<__half>(const float*, const float*, const float*, const void*, const void*,
+                                          const void*, const void*, int64_t, int64_t, int64_t, int64_t, void*,
+                                          void*, void*, void*, cudaStream_t);
 
 
 // ===========================================================================

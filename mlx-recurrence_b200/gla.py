@@ -40,14 +40,18 @@ class _GLAScan(torch.autograd.Function):
         dev = _lib.require_cuda(q, k, v, gates)
         dt = common_dtype(q, k, v, gates)
         q_, k_, v_, g_ = (prep(t, dt) for t in (q, k, v, gates))
+        code = _lib.DTYPE_CODE[dt]
+        # The checkpoints are internal (only the last one is returned, gla.py:329):
+        # take the spacing of the fastest path for these shapes (same final state).
+        seg_i = int(_lib.load().mr_gla_preferred_seg(code, L, Dh, seg))
         y = torch.empty((Bt, L, H, Dh), dtype=torch.float32, device=dev)
-        ckpt = torch.empty((Bt, L // seg, H, Dh, Dh), dtype=torch.float32, device=dev)
+        ckpt = torch.empty((Bt, L // seg_i, H, Dh, Dh), dtype=torch.float32, device=dev)
         with torch.cuda.device(dev):
             _lib.call("mr_gla_fwd", _lib.ptr(q_), _lib.ptr(k_), _lib.ptr(v_), _lib.ptr(g_),
-                      _lib.DTYPE_CODE[dt], Bt, L, H, Dh, seg, _lib.ptr(y), _lib.ptr(ckpt),
+                      code, Bt, L, H, Dh, seg_i, _lib.ptr(y), _lib.ptr(ckpt),
                       _lib.stream_of(dev))
         ctx.save_for_backward(q_, k_, v_, g_, ckpt)
-        ctx.seg = seg
+        ctx.seg = seg_i
         return y, ckpt[:, -1].clone()
 
     @staticmethod

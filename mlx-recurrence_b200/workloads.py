@@ -21,6 +21,8 @@ CONFIGS = {
     "c2": dict(kind="rglru", B=8, L=4096, D=2560, seg=32, dtype=torch.bfloat16),
     "c3": dict(kind="rotlru", B=16, L=8192, Dp=1024, seg=32, dtype=torch.bfloat16),
     "c4": dict(kind="ssd", B=32, L=16384, H=32, Dh=64, N=128, seg=32, dtype=torch.bfloat16),
+    # the GLA shape of the target (SSD/GLA fwd+bwd at B=32, L=16384, H=32, Dh=64)
+    "c5": dict(kind="gla", B=32, L=16384, H=32, Dh=64, seg=32, dtype=torch.bfloat16),
 }
 
 DESCRIPTION = {
@@ -29,6 +31,7 @@ DESCRIPTION = {
     "c2": "rglru_scan bf16 B=8 L=4096 D=2560 seg=32",
     "c3": "rotlru_scan bf16 B=16 L=8192 D=2048 seg=32",
     "c4": "ssd_scan bf16 B=32 L=16384 H=32 Dh=64 N=128 seg=32",
+    "c5": "gla_scan bf16 B=32 L=16384 H=32 Dh=64 seg=32",
 }
 
 
