@@ -350,118 +350,118 @@ gla_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfina
   // one scratch slot per CTA; a CTA walks units blockIdx.x, + gridDim.x, ...
   float* scr = scratch + (int64_t)blockIdx.x * (seg + 1) * E * kSeqThreads + tid;
   for (int unit = blockIdx.x; unit < units; unit += gridDim.x) {
-  const int64_t b = unit / H;
-  const int h = unit % H;
-  if (only_bad && !gla_unit_has_bad_gate(gates, b, h, L, H)) continue;
+    const int64_t b = unit / H;
+    const int h = unit % H;
+    if (only_bad && !gla_unit_has_bad_gate(gates, b, h, L, H)) continue;
 
-  float adj[IK][R];
+    float adj[IK][R];
 #pragma unroll
-  for (int i = 0; i < IK; ++i)
+    for (int i = 0; i < IK; ++i)
 #pragma unroll
-    for (int r = 0; r < R; ++r)
-      adj[i][r] = gfinal != nullptr
-                      ? gfinal[((b * H + h) * Dh + lane + 32 * i) * (int64_t)Dh + warp + 8 * r]
-                      : 0.f;
+      for (int r = 0; r < R; ++r)
+        adj[i][r] = gfinal != nullptr
+                        ? gfinal[((b * H + h) * Dh + lane + 32 * i) * (int64_t)Dh + warp + 8 * r]
+                        : 0.f;
 
-  for (int s = nseg - 1; s >= 0; --s) {
-    {
-      float S[IK][R];
-      const float* ck = ckpt + ((b * nseg + (s - 1)) * H + h) * (int64_t)Dh * Dh;
+    for (int s = nseg - 1; s >= 0; --s) {
+      {
+        float S[IK][R];
+        const float* ck = ckpt + ((b * nseg + (s - 1)) * H + h) * (int64_t)Dh * Dh;
 #pragma unroll
-      for (int i = 0; i < IK; ++i)
+        for (int i = 0; i < IK; ++i)
 #pragma unroll
-        for (int r = 0; r < R; ++r) {
-          S[i][r] = s > 0 ? ck[(int64_t)(lane + 32 * i) * Dh + warp + 8 * r] : 0.f;
-          scr[(int64_t)(i * R + r) * kSeqThreads] = S[i][r];
-        }
-      for (int tl = 0; tl < seg; ++tl) {
-        const int64_t row = (b * L + (int64_t)s * seg + tl) * H + h;
-        const float g = to_f(gates[row]);
-        float ki[IK];
+          for (int r = 0; r < R; ++r) {
+            S[i][r] = s > 0 ? ck[(int64_t)(lane + 32 * i) * Dh + warp + 8 * r] : 0.f;
+            scr[(int64_t)(i * R + r) * kSeqThreads] = S[i][r];
+          }
+        for (int tl = 0; tl < seg; ++tl) {
+          const int64_t row = (b * L + (int64_t)s * seg + tl) * H + h;
+          const float g = to_f(gates[row]);
+          float ki[IK];
 #pragma unroll
-        for (int i = 0; i < IK; ++i) ki[i] = to_f(k[row * Dh + lane + 32 * i]);
-        float* sp = scr + (int64_t)(tl + 1) * E * kSeqThreads;
+          for (int i = 0; i < IK; ++i) ki[i] = to_f(k[row * Dh + lane + 32 * i]);
+          float* sp = scr + (int64_t)(tl + 1) * E * kSeqThreads;
 #pragma unroll
-        for (int r = 0; r < R; ++r) {
-          const float vj = to_f(v[row * Dh + warp + 8 * r]);
+          for (int r = 0; r < R; ++r) {
+            const float vj = to_f(v[row * Dh + warp + 8 * r]);
 #pragma unroll
-          for (int i = 0; i < IK; ++i) {
-            S[i][r] = g * S[i][r] + ki[i] * vj;
-            sp[(int64_t)(i * R + r) * kSeqThreads] = S[i][r];
+            for (int i = 0; i < IK; ++i) {
+              S[i][r] = g * S[i][r] + ki[i] * vj;
+              sp[(int64_t)(i * R + r) * kSeqThreads] = S[i][r];
+            }
           }
         }
       }
-    }
 
-    for (int tl = seg - 1; tl >= 0; --tl) {
-      const int slot = (seg - 1 - tl) % kTS;
-      const int64_t t = (int64_t)s * seg + tl;
-      const int64_t row = (b * L + t) * H + h;
-      const float g = to_f(gates[row]);
-      float ki[IK], qi[IK];
-#pragma unroll
-      for (int i = 0; i < IK; ++i) {
-        ki[i] = to_f(k[row * Dh + lane + 32 * i]);
-        qi[i] = to_f(q[row * Dh + lane + 32 * i]);
-      }
-      const float* sc = scr + (int64_t)(tl + 1) * E * kSeqThreads;
-      const float* sprev = scr + (int64_t)tl * E * kSeqThreads;
-      float ggs = 0.f, pq[IK], pk[IK];
-#pragma unroll
-      for (int i = 0; i < IK; ++i) pq[i] = pk[i] = 0.f;
-#pragma unroll
-      for (int r = 0; r < R; ++r) {
-        const int j = warp + 8 * r;
-        const float vj = to_f(v[row * Dh + j]);
-        const float go = gy[row * Dh + j];
-        float gv_r = 0.f;
+      for (int tl = seg - 1; tl >= 0; --tl) {
+        const int slot = (seg - 1 - tl) % kTS;
+        const int64_t t = (int64_t)s * seg + tl;
+        const int64_t row = (b * L + t) * H + h;
+        const float g = to_f(gates[row]);
+        float ki[IK], qi[IK];
 #pragma unroll
         for (int i = 0; i < IK; ++i) {
-          const float hc = sc[(int64_t)(i * R + r) * kSeqThreads];
-          const float hp = sprev[(int64_t)(i * R + r) * kSeqThreads];
-          const float ad = adj[i][r] + qi[i] * go;  // gla.py:213
-          gv_r += ad * ki[i];
-          ggs += ad * hp;
-          pq[i] += go * hc;
-          pk[i] += ad * vj;
-          adj[i][r] = ad * g;
+          ki[i] = to_f(k[row * Dh + lane + 32 * i]);
+          qi[i] = to_f(q[row * Dh + lane + 32 * i]);
         }
-        gv_r = warp_sum(gv_r);
-        if (lane == 0) gv[row * Dh + j] = from_f<T>(gv_r);
-      }
-      ggs = warp_sum(ggs);
-      if (lane == 0) pg[slot][warp] = ggs;
+        const float* sc = scr + (int64_t)(tl + 1) * E * kSeqThreads;
+        const float* sprev = scr + (int64_t)tl * E * kSeqThreads;
+        float ggs = 0.f, pq[IK], pk[IK];
 #pragma unroll
-      for (int i = 0; i < IK; ++i) {
-        pQ[slot][warp][lane + 32 * i] = pq[i];
-        pK[slot][warp][lane + 32 * i] = pk[i];
-      }
-      if (slot == kTS - 1 || tl == 0) {
-        __syncthreads();
-        const int nsl = slot + 1;
-        for (int idx = tid; idx < nsl * Dh; idx += kSeqThreads) {
-          const int sl = idx / Dh, i = idx % Dh;
-          float sq = 0.f, sk = 0.f;
+        for (int i = 0; i < IK; ++i) pq[i] = pk[i] = 0.f;
 #pragma unroll
-          for (int w = 0; w < 8; ++w) {
-            sq += pQ[sl][w][i];
-            sk += pK[sl][w][i];
+        for (int r = 0; r < R; ++r) {
+          const int j = warp + 8 * r;
+          const float vj = to_f(v[row * Dh + j]);
+          const float go = gy[row * Dh + j];
+          float gv_r = 0.f;
+#pragma unroll
+          for (int i = 0; i < IK; ++i) {
+            const float hc = sc[(int64_t)(i * R + r) * kSeqThreads];
+            const float hp = sprev[(int64_t)(i * R + r) * kSeqThreads];
+            const float ad = adj[i][r] + qi[i] * go;  // gla.py:213
+            gv_r += ad * ki[i];
+            ggs += ad * hp;
+            pq[i] += go * hc;
+            pk[i] += ad * vj;
+            adj[i][r] = ad * g;
           }
-          const int64_t rr = (b * L + t + (slot - sl)) * H + h;
-          gq[rr * Dh + i] = from_f<T>(sq);
-          gk[rr * Dh + i] = from_f<T>(sk);
+          gv_r = warp_sum(gv_r);
+          if (lane == 0) gv[row * Dh + j] = from_f<T>(gv_r);
         }
-        if (tid < nsl) {
-          float sd = 0.f;
+        ggs = warp_sum(ggs);
+        if (lane == 0) pg[slot][warp] = ggs;
 #pragma unroll
-          for (int w = 0; w < 8; ++w) sd += pg[tid][w];
-          gg[(b * L + t + (slot - tid)) * H + h] = from_f<T>(sd);
+        for (int i = 0; i < IK; ++i) {
+          pQ[slot][warp][lane + 32 * i] = pq[i];
+          pK[slot][warp][lane + 32 * i] = pk[i];
         }
-        __syncthreads();
+        if (slot == kTS - 1 || tl == 0) {
+          __syncthreads();
+          const int nsl = slot + 1;
+          for (int idx = tid; idx < nsl * Dh; idx += kSeqThreads) {
+            const int sl = idx / Dh, i = idx % Dh;
+            float sq = 0.f, sk = 0.f;
+#pragma unroll
+            for (int w = 0; w < 8; ++w) {
+              sq += pQ[sl][w][i];
+              sk += pK[sl][w][i];
+            }
+            const int64_t rr = (b * L + t + (slot - sl)) * H + h;
+            gq[rr * Dh + i] = from_f<T>(sq);
+            gk[rr * Dh + i] = from_f<T>(sk);
+          }
+          if (tid < nsl) {
+            float sd = 0.f;
+#pragma unroll
+            for (int w = 0; w < 8; ++w) sd += pg[tid][w];
+            gg[(b * L + t + (slot - tid)) * H + h] = from_f<T>(sd);
+          }
+          __syncthreads();
+        }
       }
     }
-  }
-  __syncthreads();  // the slot's scratch is reused by the next unit
+    __syncthreads();  // the slot's scratch is reused by the next unit
   }
 }
 
