@@ -2,6 +2,8 @@
 // loads/stores of V consecutive elements, and the launch-error plumbing.
 #pragma once
 
+#include <type_traits>
+
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -58,8 +60,17 @@ __device__ __forceinline__ Vec<T, V> ld_stream(const T* p) {
 template <typename T, int V>
 __device__ __forceinline__ void st_vec(T* p, const float (&f)[V]) {
   Vec<T, V> r;
+  if constexpr (V % 2 == 0 && std::is_same_v<T, __nv_bfloat16>) {
+    // pairs by the packed conversion (one instruction per pair, off the XU pipe)
 #pragma unroll
-  for (int i = 0; i < V; ++i) r.v[i] = from_f<T>(f[i]);
+    for (int i = 0; i < V; i += 2) *reinterpret_cast<__nv_bfloat162*>(&r.v[i]) = __floats2bfloat162_rn(f[i], f[i + 1]);
+  } else if constexpr (V % 2 == 0 && std::is_same_v<T, __half>) {
+#pragma unroll
+    for (int i = 0; i < V; i += 2) *reinterpret_cast<__half2*>(&r.v[i]) = __floats2half2_rn(f[i], f[i + 1]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < V; ++i) r.v[i] = from_f<T>(f[i]);
+  }
   *reinterpret_cast<Vec<T, V>*>(p) = r;
 }
 

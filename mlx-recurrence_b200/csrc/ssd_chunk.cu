@@ -68,11 +68,17 @@ template <typename T> struct MmaFmt;
 template <> struct MmaFmt<__nv_bfloat16> { static constexpr int v = 1; };
 template <> struct MmaFmt<__half> { static constexpr int v = 0; };
 
-template <typename T>
-__device__ __forceinline__ uint32_t pack2(float a, float b) {
-  const T x = from_f<T>(a), y = from_f<T>(b);
-  return (uint32_t)(*reinterpret_cast<const uint16_t*>(&x)) |
-         ((uint32_t)(*reinterpret_cast<const uint16_t*>(&y)) << 16);
+// two floats -> one 32-bit word of 2-byte values (a in the low half), round to
+// nearest even, by the packed conversion (one instruction for the pair; the
+// scalar conversions of each value run on the slower XU pipe)
+template <typename T> __device__ __forceinline__ uint32_t pack2(float a, float b);
+template <> __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+template <> __device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
+  const __half2 v = __floats2half2_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&v);
 }
 
 // Streaming global loads pinned in program order. The proxy fences that hand
