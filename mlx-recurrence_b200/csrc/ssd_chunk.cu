@@ -378,8 +378,17 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
         umma::tmem_wait_ld();
         if (safe) {
           const float rf = (t >= s0) ? __expf(lt - sLam[s0]) : 0.f;
+          float cf[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) v[i] = (s0 + i <= t) ? v[i] * rf * sCF[s0 + i] : 0.f;
+          for (int i = 0; i < 16; i += 4)
+            *reinterpret_cast<float4*>(cf + i) = *reinterpret_cast<const float4*>(sCF + s0 + i);
+          if (s0 + 15 <= tmax - 31) {  // wholly below the diagonal for this warp: no mask
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] *= rf * cf[i];
+          } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] = (s0 + i <= t) ? v[i] * rf * cf[i] : 0.f;
+          }
         } else {
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
@@ -900,23 +909,39 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
           umma::tmem_ld16(tl + t0, sv);
           umma::tmem_ld16(tl + 128 + t0, pv);
           umma::tmem_wait_ld();
-          const float rf = (safe && s >= t0) ? __expf(ls - sLam[t0]) : 0.f;
-          float cf[16], dl[16];
+          // E[s, t] (0 above the diagonal); blocks wholly below it skip the mask
+          float e[16];
+          if (safe) {
+            const float rf = (s >= t0) ? __expf(ls - sLam[t0]) : 0.f;
 #pragma unroll
-          for (int i = 0; i < 16; i += 4) {
-            *reinterpret_cast<float4*>(cf + i) = *reinterpret_cast<const float4*>(sCF1 + t0 + i);
-            *reinterpret_cast<float4*>(dl + i) = *reinterpret_cast<const float4*>(sDel + t0 + i);
+            for (int i = 0; i < 16; i += 4)
+              *reinterpret_cast<float4*>(e + i) = *reinterpret_cast<const float4*>(sCF1 + t0 + i);
+            if (t0 + 15 <= rmax - 31) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i) e[i] *= rf;
+            } else {
+#pragma unroll
+              for (int i = 0; i < 16; ++i) e[i] = (t0 + i <= s) ? e[i] * rf : 0.f;
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) e[i] = (t0 + i <= s) ? __expf(ls - sLam[t0 + i]) : 0.f;
+          }
+          if constexpr (!V::kGla) {  // H1 carries delta_t (1 for GLA)
+            float dl[16];
+#pragma unroll
+            for (int i = 0; i < 16; i += 4)
+              *reinterpret_cast<float4*>(dl + i) = *reinterpret_cast<const float4*>(sDel + t0 + i);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) pv[i] *= dl[i];
           }
           float z[16];  // Z[s, t] = S H1
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            const int t = t0 + i;
-            const float e = (t <= s) ? (safe ? rf * cf[i] : __expf(ls - sLam[t])) : 0.f;
-            const float g = sv[i] * e;
-            const float h1 = pv[i] * e * dl[i];
+            const float h1 = pv[i] * e[i];
             z[i] = sv[i] * h1;
             rz += z[i];
-            sv[i] = g;
+            sv[i] *= e[i];
             pv[i] = h1;
           }
           *reinterpret_cast<int4*>(gp + o0) = pack8<T>(sv);
