@@ -805,9 +805,9 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     float* sEL = sW + Q;
     float* sD = sEL + Q;
     float* sCF1 = sD + Q;
-    // the previous chunk's grad_u and grad_C bulk stores must have read GYt and
-    // HH before they are rewritten below (grad_B's, from GP, may still run:
-    // the batch-1 issuer waits for it, E1 rewrites GP)
+    // the previous chunk's grad_u store and grad_C's first box must have read GYt
+    // and HH tile 0 before they are rewritten below (the rest of grad_C and
+    // grad_B may still run: the batch-1 issuer waits for them, E1 rewrites GP, HH)
     if (tid == 0) bulk_wait_read<1>();
     __syncthreads();
     const bool safe = sWide[c & 1] == 0;
@@ -1040,6 +1040,12 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
         }
         sUR[jq * Q + t] = ur;
       }
+      // fold epilogue 1's four partials of one array per thread into its slot 0
+      // (rowsum Z, colsum Z, gy.Y2, u.R2 for jq = 0..3), shortening grad_delta
+      {
+        float* arr = jq == 0 ? sRow : jq == 1 ? sCol : jq == 2 ? sQ : sM;
+        arr[t] = sum4(arr, t);
+      }
       fence_proxy_async_smem();
       if (c > 1) load_h0(c - 1);
     }
@@ -1074,8 +1080,8 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     // lastv = exp(Lam_last) <Psi, h0> + sum_t w_t m_t; grad_delta_t = A sum_{t' >= t} dLam_t' + u_t.r_t
     if (warp < 4) {
       const int t = tid;
-      const float wm = sW[t] * sum4(sM, t);
-      const float x = sum4(sRow, t) - sum4(sCol, t) + sEL[t] * sum4(sQ, t) - wm;
+      const float wm = sW[t] * sM[t];
+      const float x = sRow[t] - sCol[t] + sEL[t] * sQ[t] - wm;
       float suf = x, swm = wm, sxd = x * sD[t];
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -1162,9 +1168,11 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     __syncthreads();
     if (tid == 0) {  // read back by the next chunk's P0 (bulk_wait_read_all) before reuse
       const int z = (int)(row0 + (int64_t)c * Q);
-#pragma unroll
-      for (int j = 0; j < NB; ++j) tma_store_3d(&tm_gC, 64 * j, h, z, tHH + j * TILE);
+      // groups: grad_C's first box (HH tile 0, rewritten first, by P0), then the rest
+      tma_store_3d(&tm_gC, 0, h, z, tHH);
       bulk_commit();
+#pragma unroll
+      for (int j = 1; j < NB; ++j) tma_store_3d(&tm_gC, 64 * j, h, z, tHH + j * TILE);
 #pragma unroll
       for (int j = 0; j < NB; ++j) tma_store_3d(&tm_gB, 64 * j, h, z, tGP + j * TILE);
       bulk_commit();
