@@ -282,6 +282,15 @@ __device__ bool gla_unit_has_bad_gate(const T* __restrict__ gates, int64_t b, in
   return __syncthreads_or(bad) != 0;
 }
 
+// flags[unit] = unit (b * H + h) holds a gate outside the tensor-core range; one CTA per unit
+template <typename T>
+__global__ void __launch_bounds__(kSeqThreads)
+gla_bad_units_kernel(const T* __restrict__ gates, int L, int H, int* __restrict__ flags) {
+  const int unit = blockIdx.x;
+  const bool bad = gla_unit_has_bad_gate(gates, unit / H, unit % H, L, H);
+  if (threadIdx.x == 0) flags[unit] = bad ? 1 : 0;
+}
+
 template <typename T, int R, int IK>
 __global__ void __launch_bounds__(kSeqThreads)
 gla_seq_fwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
@@ -338,7 +347,7 @@ gla_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfina
                    const T* __restrict__ k, const T* __restrict__ v, const T* __restrict__ gates,
                    int L, int H, int Dh, int seg, T* __restrict__ gq, T* __restrict__ gk,
                    T* __restrict__ gv, T* __restrict__ gg, float* __restrict__ scratch, int units,
-                   int only_bad) {
+                   const int* __restrict__ only_flags) {
   constexpr int NP = 32 * IK;
   __shared__ float pQ[kTS][8][NP];
   __shared__ float pK[kTS][8][NP];
@@ -352,7 +361,7 @@ gla_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfina
   for (int unit = blockIdx.x; unit < units; unit += gridDim.x) {
     const int64_t b = unit / H;
     const int h = unit % H;
-    if (only_bad && !gla_unit_has_bad_gate(gates, b, h, L, H)) continue;
+    if (only_flags != nullptr && only_flags[unit] == 0) continue;
 
     float adj[IK][R];
 #pragma unroll
@@ -487,9 +496,11 @@ size_t gla_seq_bwd_ws_bytes(int64_t batch, int64_t L, int64_t H, int64_t Dh, int
 // scratch slots of the GLA fallback after the tensor-core backward (units with
 // out-of-range gates, walked by this many CTAs)
 constexpr int64_t kGlaFallbackSlots = 16;
+// layout: the slots' scratch, then one int flag per unit (256-byte aligned)
 size_t gla_fallback_ws_bytes(int64_t batch, int64_t L, int64_t H, int64_t Dh, int64_t seg) {
   const int64_t slots = batch * H < kGlaFallbackSlots ? batch * H : kGlaFallbackSlots;
-  return gla_seq_bwd_ws_bytes(slots, L, 1, Dh, seg);
+  const size_t scr = (gla_seq_bwd_ws_bytes(slots, L, 1, Dh, seg) + 255) / 256 * 256;
+  return scr + (size_t)batch * H * sizeof(int);
 }
 
 bool ssd_seq_supported(int64_t Dh, int64_t N) {
@@ -595,16 +606,24 @@ int gla_seq_bwd_launch(const float* gy, const float* gf, const float* ckpt, cons
                        int64_t H, int64_t Dh, int64_t seg, void* gq, void* gk, void* gv, void* gg,
                        void* ws, cudaStream_t st, int only_bad) {
   const int64_t units = batch * H;
-  dim3 grid((unsigned)(only_bad ? (units < kGlaFallbackSlots ? units : kGlaFallbackSlots) : units));
   const T *q_ = (const T*)q, *k_ = (const T*)k, *v_ = (const T*)v, *g_ = (const T*)g;
   T *gq_ = (T*)gq, *gk_ = (T*)gk, *gv_ = (T*)gv, *gg_ = (T*)gg;
   float* scr = (float*)ws;
   const int L_ = (int)L, H_ = (int)H, s_ = (int)seg, u_ = (int)units;
+  const int* flags = nullptr;
+  if (only_bad) {  // flag the units first (one CTA each), then walk them with a few slots
+    const int64_t slots = units < kGlaFallbackSlots ? units : kGlaFallbackSlots;
+    int* f = (int*)((char*)ws + (gla_seq_bwd_ws_bytes(slots, L, 1, Dh, seg) + 255) / 256 * 256);
+    gla_bad_units_kernel<T><<<(unsigned)units, kSeqThreads, 0, st>>>(g_, L_, H_, f);
+    if (int rc = check_launch("gla_bad_units_kernel")) return rc;
+    flags = f;
+  }
+  dim3 grid((unsigned)(only_bad ? (units < kGlaFallbackSlots ? units : kGlaFallbackSlots) : units));
   switch ((int)Dh) {
-    case 32: gla_seq_bwd_kernel<T, 4, 1><<<grid, kSeqThreads, 0, st>>>(gy, gf, ckpt, q_, k_, v_, g_, L_, H_, 32, s_, gq_, gk_, gv_, gg_, scr, u_, only_bad); break;
-    case 64: gla_seq_bwd_kernel<T, 8, 2><<<grid, kSeqThreads, 0, st>>>(gy, gf, ckpt, q_, k_, v_, g_, L_, H_, 64, s_, gq_, gk_, gv_, gg_, scr, u_, only_bad); break;
-    case 96: gla_seq_bwd_kernel<T, 12, 3><<<grid, kSeqThreads, 0, st>>>(gy, gf, ckpt, q_, k_, v_, g_, L_, H_, 96, s_, gq_, gk_, gv_, gg_, scr, u_, only_bad); break;
-    default: gla_seq_bwd_kernel<T, 16, 4><<<grid, kSeqThreads, 0, st>>>(gy, gf, ckpt, q_, k_, v_, g_, L_, H_, 128, s_, gq_, gk_, gv_, gg_, scr, u_, only_bad); break;
+    case 32: gla_seq_bwd_kernel<T, 4, 1><<<grid, kSeqThreads, 0, st>>>(gy, gf, ckpt, q_, k_, v_, g_, L_, H_, 32, s_, gq_, gk_, gv_, gg_, scr, u_, flags); break;
+    case 64: gla_seq_bwd_kernel<T, 8, 2><<<grid, kSeqThreads, 0, st>>>(gy, gf, ckpt, q_, k_, v_, g_, L_, H_, 64, s_, gq_, gk_, gv_, gg_, scr, u_, flags); break;
+    case 96: gla_seq_bwd_kernel<T, 12, 3><<<grid, kSeqThreads, 0, st>>>(gy, gf, ckpt, q_, k_, v_, g_, L_, H_, 96, s_, gq_, gk_, gv_, gg_, scr, u_, flags); break;
+    default: gla_seq_bwd_kernel<T, 16, 4><<<grid, kSeqThreads, 0, st>>>(gy, gf, ckpt, q_, k_, v_, g_, L_, H_, 128, s_, gq_, gk_, gv_, gg_, scr, u_, flags); break;
   }
   return check_launch("gla_seq_bwd_kernel");
 }
