@@ -82,12 +82,14 @@ def algorithmic_bytes(cfg, batch):
     return inp + y, inp + y + inp
 
 
-# DRAM bytes (read + write) per launch measured by ncu on a B=4 instance of the
-# same configuration (profiles/ssd_chunk_c4.md), per batch row: the kernels'
-# traffic grows linearly with the (batch, head) units.
+# DRAM bytes (read + write) per launch measured by ncu on a B=2 instance of the
+# same configuration (profiles/ssd_chunk_c4.md, profiles/gla_chunk_c5.md), per
+# batch row: the kernels' traffic grows linearly with the (batch, head) units.
 _NCU_TRAFFIC_PER_BATCH_ROW = {
-    ("c4", "backward"): (2.440075e9 + 1.304630e9) / 4,
-    ("c4", "forward"): (1.349373e9 + 1.024133e9) / 4,
+    ("c4", "backward"): (1.214505e9 + 0.630143e9) / 2,
+    ("c4", "forward"): (0.674436e9 + 0.495007e9) / 2,
+    ("c5", "backward"): (0.810017e9 + 0.364701e9) / 2,
+    ("c5", "forward"): (0.407027e9 + 0.358031e9) / 2,
 }
 
 
