@@ -1,6 +1,6 @@
 // Asynchronous-copy helpers for sm_100a: shared-memory mbarriers, 1-D bulk
-// copies global -> shared through the TMA unit (cp.async.bulk, no cluster
-// multicast anywhere), and bounded waits.
+// copies global -> shared through the TMA unit (cp.async.bulk, each CTA
+// fetching its own data), and bounded waits.
 //
 // Every wait is bounded: after kSpinLimit polls it records an error code in
 // this translation unit's device word g_device_error (read through

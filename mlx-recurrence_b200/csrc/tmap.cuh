@@ -3,7 +3,8 @@
 // A tensor map describes a 2-D row-major view [rows, cols] of a global array
 // and the box (tile) one copy moves into shared memory. The driver's encoder
 // is fetched once through cudaGetDriverEntryPoint, so the library needs no
-// link-time dependency on libcuda. Loads only, never with cluster multicast.
+// link-time dependency on libcuda. Every CTA loads its own tiles from this
+// GPU's memory; no copy is shared across the CTAs of a cluster.
 #pragma once
 
 #include <cuda.h>
