@@ -352,7 +352,8 @@ def _e2e(args, fn, ins, gy, dev, stream, barrier, ev):
     host_gy = gy.to("cpu").pin_memory()
     dev_ins = [torch.empty_like(h, device=dev) for h in host_ins]
     dev_gy = torch.empty_like(gy)
-    y_probe = fn(*leaves)
+    with torch.no_grad():
+        y_probe = fn(*(t.detach() for t in ins))  # only for the result's shape and dtype
     res_host = torch.empty(y_probe[:, -1].shape, dtype=y_probe.dtype, pin_memory=True)
     del y_probe
     h2d = sum(t.numel() * t.element_size() for t in host_ins) + host_gy.numel() * 4
