@@ -52,15 +52,19 @@ constexpr int DH = 64;                 // head dim (one 128-byte swizzle row)
 constexpr uint32_t TILE = 16384;       // [128 rows x 64 elements] 2-byte tile
 constexpr int NT = 512;                // threads: 16 warps
 constexpr int CH = 16;                 // state / y channels per thread
-// small arrays (Lam, delta, warp sums, barriers, TMEM slot) first, then the
-// 1024-byte-aligned tiles
-constexpr size_t SMALL = (3 * Q + 8) * 4 + 6 * 8 + 16;
+// small arrays (barriers, TMEM slot, two buffers of per-chunk scalars, scan
+// scratch) in the first SMALL_PAD bytes, then the tiles. The dynamic shared
+// memory base is 1024-byte aligned (no static shared memory; checked at kernel
+// entry), so the tiles start on a 128B-swizzle atom without slack.
+constexpr size_t SMALL = 6 * 8 + 16 + 2 * (2 * Q * 4 + Q * 2) + 8 * 4;
+constexpr size_t SMALL_PAD = 3072;
+static_assert(SMALL <= SMALL_PAD, "forward scalar arrays overflow their region");
 template <typename V> struct Cfg {
   static constexpr int NS = V::NS;                     // state size N (B, C width)
   static constexpr int NB = NS / 64;                   // 64-wide tiles of B and C
   static constexpr uint32_t STAGE = TILE * (1 + 2 * NB);  // u, B, C
   // stages, G (2), U~, h^T; GLA adds a zero tile that pads the M = 64 product B^T U~
-  static constexpr size_t SMEM = SMALL + 1023 + 2 * STAGE + 4 * TILE + (V::kGla ? TILE : 0);
+  static constexpr size_t SMEM = SMALL_PAD + 2 * STAGE + 4 * TILE + (V::kGla ? TILE : 0);
 };
 }  // namespace ssdc
 
@@ -178,13 +182,20 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   constexpr int NS = Cfg<V>::NS, NB = Cfg<V>::NB;
   constexpr uint32_t STAGE = Cfg<V>::STAGE;
   extern __shared__ unsigned char smem_raw[];
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem_raw);  // bc[2], u[2], mma
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem_raw);  // bc[2], u[2], mma (S, then Y1), mma (Y2, dH)
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 6);
-  float* sLam = reinterpret_cast<float*>(tslot + 4);  // [Q]
-  float* sDel = sLam + Q;                             // [Q]
-  float* sCF = sDel + Q;                              // [Q] column factors (see E1)
-  float* sWarp = sCF + Q;                             // [8]
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sWarp + 8) + 1023) & ~uintptr_t(1023));
+  int* sWide = reinterpret_cast<int*>(tslot + 2);  // [2] a 16-step block spans a decay above e^40
+  // [2][2][Q] f32 per-chunk scalars, buffer c & 1 for chunk c: Lam_t (cumulative
+  // log decay), the E1 column factor exp(Lam_s0 - Lam_s) delta_s; [2][Q] raw
+  // 2-byte delta_t (SSD)
+  float* sSc = reinterpret_cast<float*>(tslot + 4);
+  unsigned short* sDr = reinterpret_cast<unsigned short*>(sSc + 4 * Q);
+  float* sWarp = reinterpret_cast<float*>(sDr + 2 * Q);  // [8] scan scratch
+  uint8_t* sm = smem_raw + SMALL_PAD;
+  if ((smem_u32(smem_raw) & 1023u) != 0) {  // the tiles' 1024-byte alignment (see SMALL_PAD)
+    if (threadIdx.x == 0) atomicCAS(&g_device_error, 0, 2);
+    return;
+  }
   uint8_t* stg0 = sm;            // stage s: u | B (NB tiles) | C (NB tiles)
   uint8_t* sG = sm + 2 * STAGE;  // G, two K-major tiles (s 0-63, 64-127); then y staging
   uint8_t* sUt = sG + 2 * TILE;  // U~, MN-major [s][d]; then checkpoint staging (n 0-63)
@@ -204,7 +215,7 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   constexpr uint32_t idH = umma::idesc_f16(128, 64, fmt, 1, 1);
 
   if (tid == 0) {
-    for (int i = 0; i < 5; ++i) mbar_init(&bar[i], 1);
+    for (int i = 0; i < 6; ++i) mbar_init(&bar[i], 1);
     fence_mbar_init();
   }
   if (warp == 0) {
@@ -220,7 +231,7 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   umma::fence_after_sync();
   const uint32_t tbase = *tslot;
 
-  // B and C of a chunk are free once its S/dH/Y2 products complete; u once Y1
+  // B and C of a chunk are free once its S/Y2/dH products complete; u once Y1
   // completed and the checkpoint staged in its slot has been stored.
   auto issue_bc = [&](int c) {
     const int st = c & 1;
@@ -256,53 +267,58 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   float hreg[CH];
 #pragma unroll
   for (int i = 0; i < CH; ++i) hreg[i] = 0.f;
-  unsigned short dnext = (tid < Q) ? ld_pinned_u16(delta + (row0 + tid) * H + h) : (unsigned short)0;
-  uint32_t mph = 0;
-  bool safe = true;
+  uint32_t mph = 0, mph2 = 0;
 
-  // Prologue of chunk c: Lam (cumulative delta*A), delta, the E1 column
-  // factors and U~ into shared memory. Returns whether every 16-step block's
-  // decay span is small enough for the factored exponentials of E1.
-  auto prologue = [&](int c) -> bool {
+  // The next chunk's scalars are computed during E1 by four warps whose G
+  // columns lie wholly above the diagonal (warps 4, 8, 9, 12: no E1 work),
+  // synchronised on named barrier 1; step t = 32 * group position + lane.
+  const int spos = warp == 4 ? 0 : warp == 8 ? 1 : warp == 9 ? 2 : warp == 12 ? 3 : -1;
+  const int sst = 32 * spos + lane;
+  unsigned short dnext = 0;  // raw delta / gate of step sst of the next chunk to scan
+  auto chunk_scalars = [&](int buf) {
+    float* sl = sSc + buf * 2 * Q;
     const float dcur = u16_to_f<T>(dnext);
-    float lam = 0.f;
-    if (tid < Q) {
-      lam = step_log_decay<V>(dcur, Ah);
+    float lam = step_log_decay<V>(dcur, Ah);
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const float n = __shfl_up_sync(0xffffffffu, lam, o);
-        if (lane >= o) lam += n;
-      }
-      if (lane == 31) sWarp[warp] = lam;
-      sDel[tid] = V::kGla ? 1.f : dcur;
+    for (int o = 1; o < 32; o <<= 1) {
+      const float n = __shfl_up_sync(0xffffffffu, lam, o);
+      if (lane >= o) lam += n;
     }
-    __syncthreads();
-    if (tid < Q) {
-      float off = 0.f;
-      for (int w = 0; w < warp; ++w) off += sWarp[w];
-      sLam[tid] = lam + off;
-    }
-    __syncthreads();
+    if (lane == 31) sWarp[spos] = lam;
+    if (sst == 0) sWide[buf] = 0;
+    named_barrier_sync(1, 128);
+    for (int v = 0; v < spos; ++v) lam += sWarp[v];
+    const float dl = V::kGla ? 1.f : dcur;
+    sl[sst] = lam;
+    sDr[buf * Q + sst] = dnext;
+    named_barrier_sync(1, 128);
     // column factor exp(Lam_{s0} - Lam_s) delta_s, s0 = start of s's 16-step block
-    bool wide = false;
-    if (tid < Q) {
-      const float span = sLam[tid & ~15] - sLam[tid];
-      sCF[tid] = __expf(span) * sDel[tid];
-      wide = span > 40.f;
-    }
-    // the previous chunk's bulk stores must have read the y and checkpoint
-    // staging (G, U~ and u slots) before U~ and chunk c+1's u overwrite them
+    const float span = sl[sst & ~15] - lam;
+    sl[Q + sst] = __expf(span) * dl;
+    if (__any_sync(0xffffffffu, span > 40.f) && lane == 0) sWide[buf] = 1;
+  };
+  if (spos >= 0) {
+    dnext = ld_pinned_u16(delta + (row0 + sst) * H + h);
+    chunk_scalars(0);
+    if (nck > 1) dnext = ld_pinned_u16(delta + (row0 + (int64_t)Q + sst) * H + h);
+  }
+  __syncthreads();
+
+  // Prologue of chunk c: U~ = exp(Lam_last - Lam_s) delta_s u_s into shared
+  // memory, once the previous chunk's checkpoint stores have read its slots.
+  auto prologue = [&](int c) {
     if (tid == 0 && c > 0) {
-      bulk_wait_read_all();
+      bulk_wait_read<1>();  // the checkpoint group (U~ and u slots); y's may still run
       if (c + 1 < nck) issue_u(c + 1);
     }
-    const bool ok = !__syncthreads_or(wide);
+    __syncthreads();
+    const float* sLam = sSc + (c & 1) * 2 * Q;
     const float lam_last = sLam[Q - 1];
     const int st = c & 1;
     mbar_wait(&bar[2 + st], (uint32_t)(c >> 1) & 1u);
     const uint8_t* sU = stg0 + st * STAGE;
     const int s = tid >> 2, part = tid & 3;  // row s, channels 16*part..
-    const float w = __expf(lam_last - sLam[s]) * sDel[s];
+    const float w = __expf(lam_last - sLam[s]) * (V::kGla ? 1.f : u16_to_f<T>(sDr[(c & 1) * Q + s]));
 #pragma unroll
     for (int cc = 0; cc < 2; ++cc) {
       const uint32_t off = umma::sw128_off(s, part * 16 + cc * 8);
@@ -313,22 +329,23 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
       *reinterpret_cast<int4*>(sUt + off) = pack8<T>(f);
     }
     fence_proxy_async_smem();
-    // the next chunk's delta (a proxy fence waits for outstanding loads, so
-    // it is issued after the fence)
-    if (tid < Q && c + 1 < nck) dnext = ld_pinned_u16(delta + (row0 + (int64_t)(c + 1) * Q + tid) * H + h);
-    return ok;
   };
 
-  safe = prologue(0);
+  prologue(0);
   for (int c = 0; c < nck; ++c) {
     const int st = c & 1;
     uint8_t* sU = stg0 + st * STAGE;
     uint8_t* sB = sU + TILE;
     uint8_t* sC = sU + (1 + NB) * TILE;
-    __syncthreads();  // U~, Lam of chunk c and h^T of chunk c-1 are in shared memory
+    const float* sLam = sSc + st * 2 * Q;
+    const float* sCF = sLam + Q;
+    const unsigned short* sDel = sDr + st * Q;  // raw delta (SSD)
+    __syncthreads();  // U~ and the scalars of chunk c and h^T of chunk c-1 are in shared memory
+    const bool safe = sWide[st] == 0;
 
-    // ---- S = C B^T, Y2 = C h0^T, dH^T = B^T U~
+    // ---- S = C B^T (commit 1), then Y2 = C h0^T, dH^T = B^T U~ (commit 2)
     if (tid == 0) {
+      bulk_wait_read<0>();  // the previous chunk's y stores have read G's tiles (E1 rewrites them)
       mbar_wait(&bar[st], (uint32_t)(c >> 1) & 1u);
       umma::fence_after_sync();
       const uint32_t aC = smem_u32(sC), aB = smem_u32(sB), aH = smem_u32(sHt), aUt = smem_u32(sUt);
@@ -337,6 +354,7 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
         const uint32_t ko = (k >> 2) * TILE + (k & 3) * 32;
         umma::mma_f16(tbase + 0, umma::sdesc_k(aC + ko), umma::sdesc_k(aB + ko), idS, k > 0);
       }
+      umma::commit(&bar[4]);
 #pragma unroll
       for (int k = 0; k < NS / 16; ++k) {
         const uint32_t ko = (k >> 2) * TILE + (k & 3) * 32;
@@ -349,7 +367,7 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
       for (int k = 0; k < Q / 16; ++k)
         umma::mma_f16(tbase + 192, umma::sdesc_mn(aB + k * 2048, lboB), umma::sdesc_mn(aUt + k * 2048, TILE),
                       idH, k > 0);
-      umma::commit(&bar[4]);
+      umma::commit(&bar[5]);
     }
     mbar_wait(&bar[4], mph & 1u);
     ++mph;
@@ -393,18 +411,24 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const int s = s0 + i;
-            v[i] = (s <= t) ? v[i] * __expf(lt - sLam[s]) * sDel[s] : 0.f;
+            const float dl = V::kGla ? 1.f : u16_to_f<T>(sDel[s]);
+            v[i] = (s <= t) ? v[i] * __expf(lt - sLam[s]) * dl : 0.f;
           }
         }
         *reinterpret_cast<int4*>(g + o0) = pack8<T>(v);
         *reinterpret_cast<int4*>(g + o1) = pack8<T>(v + 8);
       }
       fence_proxy_async_smem();
+      // the scalar warps (no G work) prepare the next chunk's scalars meanwhile
+      if (spos >= 0 && c + 1 < nck) {
+        chunk_scalars((c + 1) & 1);
+        if (c + 2 < nck) dnext = ld_pinned_u16(delta + (row0 + (int64_t)(c + 2) * Q + sst) * H + h);
+      }
     }
     umma::fence_before_sync();
     __syncthreads();
 
-    // ---- Y1 = G U; B, C of this stage are free: stream chunk c+2's
+    // ---- Y1 = G U
     if (tid == 0) {
       umma::fence_after_sync();
       const uint32_t aG = smem_u32(sG), aU = smem_u32(sU);
@@ -414,8 +438,12 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
         umma::mma_f16(tbase + 256, umma::sdesc_k(aG + ko), umma::sdesc_mn(aU + k * 2048, TILE), idY, k > 0);
       }
       umma::commit(&bar[4]);
-      if (c + 2 < nck) issue_bc(c + 2);
     }
+    mbar_wait(&bar[5], mph2 & 1u);  // Y2 and dH
+    ++mph2;
+    umma::fence_after_sync();
+    // B, C of this stage are no longer read: stream chunk c+2's (a thread other than the MMA issuer)
+    if (tid == 32 && c + 2 < nck) issue_bc(c + 2);
 
     // ---- state: h <- exp(Lam_last) h + dH (thread: row n = trow, channels ch0..)
     {
@@ -461,9 +489,9 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     umma::fence_before_sync();
     __syncthreads();
     if (tid == 0) {
+      // two bulk groups: the checkpoint (U~ and u slots, needed first by the next
+      // prologue; empty without a checkpoint), then y (G's tiles, needed by E1)
       const int z = (int)(row0 + (int64_t)c * Q);
-      tma_store_3d(&tm_y, 0, h, z, sG);
-      tma_store_3d(&tm_y, 32, h, z, sG + TILE);
       if (ck) {
         const int zz = (int)(((int64_t)b * nseg + (c + 1) * Q / seg - 1) * H + h);
         tma_store_3d(&tm_ck, 0, 0, zz, sUt);
@@ -473,9 +501,12 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
           tma_store_3d(&tm_ck, 32, 64, zz, sU + TILE / 2);
         }
       }
-      bulk_commit();  // read back in the next prologue before the slots are reused
+      bulk_commit();
+      tma_store_3d(&tm_y, 0, h, z, sG);
+      tma_store_3d(&tm_y, 32, h, z, sG + TILE);
+      bulk_commit();
     }
-    if (c + 1 < nck) safe = prologue(c + 1);
+    if (c + 1 < nck) prologue(c + 1);
   }
   if (tid == 0) bulk_wait_all();
   __syncthreads();
