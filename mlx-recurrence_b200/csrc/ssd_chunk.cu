@@ -1039,7 +1039,7 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     // issued right after one, with a batch and an epilogue to arrive before the next.
     if (c > 0) {
       load_gy(c - 1);
-      if (warp >= 4 && warp < 8) dnext = ld_pinned_u16(delta + (row0 + (int64_t)(c - 1) * Q + tid - 128) * H + h);
+      if (warp >= 8 && warp < 12) dnext = ld_pinned_u16(delta + (row0 + (int64_t)(c - 1) * Q + tid - 256) * H + h);
     }
     mbar_wait(&bar[1], mph & 1u);
     ++mph;
@@ -1105,12 +1105,12 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
       tma_store_3d(&tm_gu, 0, h, (int)(row0 + (int64_t)c * Q), tGYt);
       bulk_commit();
     }
-    // ---- while batch 3 runs: grad_delta and grad_A (warps 0-3, thread t), and the
-    //      previous chunk's scalars (warps 4-7)
+    // ---- while batch 3 runs: grad_delta and grad_A (warps 4-7, thread t; warp 0 issues the
+    //      MMAs), and the previous chunk's scalars (warps 8-11)
     // dLam_t = x_t + [t = last] lastv with x_t = rowsum Z - colsum Z + exp(Lam_t) q_t - w_t m_t,
     // lastv = exp(Lam_last) <Psi, h0> + sum_t w_t m_t; grad_delta_t = A sum_{t' >= t} dLam_t' + u_t.r_t
-    if (warp < 4) {
-      const int t = tid;
+    if (warp >= 4 && warp < 8) {
+      const int t = tid - 128, gw = warp - 4;
       const float wm = sW[t] * sM[t];
       const float x = sRow[t] - sCol[t] + sEL[t] * sQ[t] - wm;
       float suf = x, swm = wm, sxd = x * sD[t];
@@ -1125,9 +1125,9 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
         sxd += __shfl_xor_sync(0xffffffffu, sxd, o);
       }
       if (lane == 0) {
-        sRed[warp] = suf;  // the warp's total of x
-        sRed[4 + warp] = swm;
-        sRed[8 + warp] = sxd;
+        sRed[gw] = suf;  // the warp's total of x
+        sRed[4 + gw] = swm;
+        sRed[8 + gw] = sxd;
       }
       named_barrier_sync(1, 128);
       float sum_wm = 0.f, sum_xd = 0.f, later = 0.f, psi_h0 = 0.f;
@@ -1135,7 +1135,7 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
       for (int v = 0; v < 4; ++v) {
         sum_wm += sRed[4 + v];
         sum_xd += sRed[8 + v];
-        if (v > warp) later += sRed[v];
+        if (v > gw) later += sRed[v];
       }
 #pragma unroll
       for (int v = 0; v < NT / 32; ++v) psi_h0 += sRed[32 + v];
@@ -1149,8 +1149,8 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
         g = Ah * dlam + sum4(sUR, t);
       }
       gdelta[(row0 + (int64_t)c * Q + t) * H + h] = from_f<T>(g);
-    } else if (warp < 8 && c > 0) {
-      chunk_scalars(dnext, tid - 128, (c - 1) & 1, 2);
+    } else if (warp >= 8 && warp < 12 && c > 0) {
+      chunk_scalars(dnext, tid - 256, (c - 1) & 1, 2);
     }
     mbar_wait(&bar[1], mph & 1u);
     ++mph;
@@ -1209,10 +1209,9 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
       bulk_commit();
     }
   }
-  if (tid == 0) {
-    if constexpr (!V::kGla) gA_part[bh] = gA_acc;
-    bulk_wait_all();
-  }
+  if constexpr (!V::kGla)
+    if (tid == 128) gA_part[bh] = gA_acc;  // step t = 0 of the grad_delta warps
+  if (tid == 0) bulk_wait_all();
   __syncthreads();
   if (warp == 0) umma::tmem_dealloc(tbase, 512);
 }
