@@ -198,7 +198,7 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   }
   uint8_t* stg0 = sm;            // stage s: u | B (NB tiles) | C (NB tiles)
   uint8_t* sG = sm + 2 * STAGE;  // G, two K-major tiles (s 0-63, 64-127); then y staging
-  uint8_t* sUt = sG + 2 * TILE;  // U~, MN-major [s][d]; then checkpoint staging (n 0-63)
+  uint8_t* sUt = sG + 2 * TILE;  // U~, MN-major [s][d]
   uint8_t* sHt = sUt + TILE;     // h^T bf16, MN-major [n][d]
   uint8_t* sZero = sHt + TILE;   // GLA: zeros, the n = 64..127 half of B^T in B^T U~
 
@@ -231,8 +231,9 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   umma::fence_after_sync();
   const uint32_t tbase = *tslot;
 
-  // B and C of a chunk are free once its S/Y2/dH products complete; u once Y1
-  // completed and the checkpoint staged in its slot has been stored.
+  // A stage (u, B, C of one chunk) is reloaded once the chunk's products have
+  // completed and the checkpoint staged in its u slot (and B's first tile for
+  // SSD) has been stored.
   auto issue_bc = [&](int c) {
     const int st = c & 1;
     uint8_t* s = stg0 + st * STAGE;
@@ -304,13 +305,8 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   }
   __syncthreads();
 
-  // Prologue of chunk c: U~ = exp(Lam_last - Lam_s) delta_s u_s into shared
-  // memory, once the previous chunk's checkpoint stores have read its slots.
+  // Prologue of chunk c: U~ = exp(Lam_last - Lam_s) delta_s u_s into shared memory.
   auto prologue = [&](int c) {
-    if (tid == 0 && c > 0) {
-      bulk_wait_read<1>();  // the checkpoint group (U~ and u slots); y's may still run
-      if (c + 1 < nck) issue_u(c + 1);
-    }
     __syncthreads();
     const float* sLam = sSc + (c & 1) * 2 * Q;
     const float lam_last = sLam[Q - 1];
@@ -345,7 +341,13 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
 
     // ---- S = C B^T (commit 1), then Y2 = C h0^T, dH^T = B^T U~ (commit 2)
     if (tid == 0) {
-      bulk_wait_read<0>();  // the previous chunk's y stores have read G's tiles (E1 rewrites them)
+      // the previous chunk's y and checkpoint stores have read G's tiles (E1 rewrites
+      // them) and their stage, which then streams in chunk c+1
+      bulk_wait_read<0>();
+      if (c > 0 && c + 1 < nck) {
+        issue_u(c + 1);
+        issue_bc(c + 1);
+      }
       mbar_wait(&bar[st], (uint32_t)(c >> 1) & 1u);
       umma::fence_after_sync();
       const uint32_t aC = smem_u32(sC), aB = smem_u32(sB), aH = smem_u32(sHt), aUt = smem_u32(sUt);
@@ -442,8 +444,6 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     mbar_wait(&bar[5], mph2 & 1u);  // Y2 and dH
     ++mph2;
     umma::fence_after_sync();
-    // B, C of this stage are no longer read: stream chunk c+2's (a thread other than the MMA issuer)
-    if (tid == 32 && c + 2 < nck) issue_bc(c + 2);
 
     // ---- state: h <- exp(Lam_last) h + dH (thread: row n = trow, channels ch0..)
     {
@@ -463,7 +463,8 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     ++mph;
     umma::fence_after_sync();
 
-    // ---- stage y = Y1 + exp(Lam_t) Y2 in sG, the checkpoint in U~ and u slots
+    // ---- stage y = Y1 + exp(Lam_t) Y2 in sG, the checkpoint in this stage's u slot
+    //      (states n >= 64) and first B tile (n < 64; GLA: the u slot)
     {
       float a[CH], bb[CH];
       umma::tmem_ld16(tl + 256 + ch0, a);
@@ -477,9 +478,10 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
                         a[i + 3] + e_t * bb[i + 3]);
     }
     const bool ck = ((c + 1) * Q) % seg == 0;
+    uint8_t* sCk0 = V::kGla ? sU : sB;  // checkpoint states 0-63
     if (ck && trow < NS) {
       const int n = trow;
-      uint8_t* cb = (n < 64 ? sUt : sU) + (jq >> 1) * (TILE / 2);  // box [64 n][32 f32]
+      uint8_t* cb = (n < 64 ? sCk0 : sU) + (jq >> 1) * (TILE / 2);  // box [64 n][32 f32]
 #pragma unroll
       for (int i = 0; i < CH; i += 4)
         *reinterpret_cast<float4*>(cb + umma::sw128_off_f32(n & 63, (ch0 & 31) + i)) =
@@ -488,20 +490,17 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     fence_proxy_async_smem();
     umma::fence_before_sync();
     __syncthreads();
-    if (tid == 0) {
-      // two bulk groups: the checkpoint (U~ and u slots, needed first by the next
-      // prologue; empty without a checkpoint), then y (G's tiles, needed by E1)
+    if (tid == 0) {  // drained before the next chunk's MMAs (bulk_wait_read<0> there)
       const int z = (int)(row0 + (int64_t)c * Q);
       if (ck) {
         const int zz = (int)(((int64_t)b * nseg + (c + 1) * Q / seg - 1) * H + h);
-        tma_store_3d(&tm_ck, 0, 0, zz, sUt);
-        tma_store_3d(&tm_ck, 32, 0, zz, sUt + TILE / 2);
+        tma_store_3d(&tm_ck, 0, 0, zz, sCk0);
+        tma_store_3d(&tm_ck, 32, 0, zz, sCk0 + TILE / 2);
         if constexpr (NS > 64) {
           tma_store_3d(&tm_ck, 0, 64, zz, sU);
           tma_store_3d(&tm_ck, 32, 64, zz, sU + TILE / 2);
         }
       }
-      bulk_commit();
       tma_store_3d(&tm_y, 0, h, z, sG);
       tma_store_3d(&tm_y, 32, h, z, sG + TILE);
       bulk_commit();
