@@ -445,7 +445,6 @@ rotlru_fwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
   const int64_t D = 2 * Dp;
   const int nseg = L / seg;
   const int nblk = (L + TB - 1) / TB;
-  const int64_t pbase = b * (int64_t)L * Dp + p0;
   const int64_t xbase = b * (int64_t)L * D + 2 * p0;
 
   if (threadIdx.x == 0) {
@@ -809,13 +808,14 @@ rotlru_bwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
 // ============================================================================
 
 // Tile shapes (channels per CTA W, steps per block TB, pipeline stages S),
-// chosen so three (forward) or two (backward) CTAs fit an SM and S-1 blocks
-// stay in flight per CTA.
+// from a sweep on B200 at c2/c3 (bf16): one channel per lane with long blocks
+// for RG-LRU (more CTAs, shorter per-thread chains in phase 1), 64-pair tiles
+// for the rotLRU forward, 32-pair tiles of 64 steps for its backward.
 template <typename T> struct DiagCfg {
-  static constexpr int RgFW = 64, RgFTB = 64, RgFS = sizeof(T) == 4 ? 2 : 4;
-  static constexpr int RgBW = 64, RgBTB = 32, RgBS = sizeof(T) == 4 ? 2 : 3;
-  static constexpr int RotFW = 64, RotFTB = 32, RotFS = sizeof(T) == 4 ? 2 : 4;
-  static constexpr int RotBW = 64, RotBTB = 32, RotBS = 2;
+  static constexpr int RgFW = 32, RgFTB = 128, RgFS = sizeof(T) == 4 ? 2 : 4;
+  static constexpr int RgBW = 32, RgBTB = 128, RgBS = 2;
+  static constexpr int RotFW = 64, RotFTB = 64, RotFS = sizeof(T) == 4 ? 2 : 4;
+  static constexpr int RotBW = 32, RotBTB = 64, RotBS = 2;
 };
 
 template <typename K>
