@@ -652,8 +652,9 @@ constexpr size_t SMALL = NSMALLF * 4 + 4 * 8 + 16 + 16;
 template <typename V> struct Cfg {
   static constexpr int NS = V::NS;
   static constexpr int NB = NS / 64;  // 64-wide tiles of B and C
-  // tiles: U, B, C, GY, GYt, PSI, H0, GP (2), HH (2); GLA adds a zero tile (M = 64 padding)
-  static constexpr int NTILE = 9 + 2 * NB + (V::kGla ? 1 : 0);
+  // tiles: U, B, C, GY, GYt, PSI, H0, GP (2), HH (2); GLA adds a zero tile (M = 64
+  // padding) and its own tile for exp(Lam) gy (SSD stages it in HH, drained first)
+  static constexpr int NTILE = 9 + 2 * NB + (V::kGla ? 2 : 0);
   static constexpr size_t SMEM = SMALL + 1023 + NTILE * TILE;
 };
 }  // namespace ssdb
@@ -692,8 +693,9 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   uint8_t* tPSI = tGYt + TILE;    // Psi^T bf16 [n][d]
   uint8_t* tH0 = tPSI + TILE;     // h0^T bf16 [n][d]
   uint8_t* tGP = tH0 + TILE;      // G' [s][t], 2 tiles (t halves); then grad_B staging
-  uint8_t* tHH = tGP + 2 * TILE;  // exp(Lam_s) gy [s][d] (batch 1); H1 [s][t], 2 tiles; grad_C staging
+  uint8_t* tHH = tGP + 2 * TILE;  // (SSD: exp(Lam_s) gy, batch 1); H1 [s][t], 2 tiles; grad_C staging
   uint8_t* tZero = tHH + 2 * TILE;  // GLA: zeros, the n = 64..127 half of C^T in dPsi^T
+  uint8_t* tEG = V::kGla ? tZero + TILE : tHH;  // exp(Lam_s) gy [s][d], the dPsi operand (batch 1)
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bh = blockIdx.x;
@@ -835,10 +837,15 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     float* sEL = sW + Q;
     float* sD = sEL + Q;
     float* sCF1 = sD + Q;
-    // the previous chunk's grad_u store and grad_C's first box must have read GYt
-    // and HH tile 0 before they are rewritten below (the rest of grad_C and
-    // grad_B may still run: the batch-1 issuer waits for them, E1 rewrites GP, HH)
-    if (tid == 0) bulk_wait_read<1>();
+    // the previous chunk's grad_u store and (SSD, exp(Lam) gy staged in HH) grad_C's
+    // first box must have read GYt and HH tile 0 before they are rewritten below (the
+    // rest may still run: the batch-1 issuer waits for it, E1 rewrites GP, HH)
+    if (tid == 0) {
+      if constexpr (V::kGla)
+        bulk_wait_read<2>();
+      else
+        bulk_wait_read<1>();
+    }
     __syncthreads();
     const bool safe = sWide[c & 1] == 0;
     float psih0 = 0.f;
@@ -858,7 +865,7 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
       const float el = sEL[r];
       *reinterpret_cast<uint2*>(tGY + off) = hi;
       *reinterpret_cast<uint2*>(tGYt + off) = pack4<T>(make_float4(g.x - hf[0], g.y - hf[1], g.z - hf[2], g.w - hf[3]));
-      *reinterpret_cast<uint2*>(tHH + off) = pack4<T>(make_float4(el * g.x, el * g.y, el * g.z, el * g.w));
+      *reinterpret_cast<uint2*>(tEG + off) = pack4<T>(make_float4(el * g.x, el * g.y, el * g.z, el * g.w));
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) psih0 += __shfl_xor_sync(0xffffffffu, psih0, o);
@@ -874,7 +881,7 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
       ++tph;
       umma::fence_after_sync();
       const uint32_t aU = smem_u32(tU), aB = smem_u32(tB), aC = smem_u32(tC), aGY = smem_u32(tGY),
-                     aEG = smem_u32(tHH), aPSI = smem_u32(tPSI), aH0 = smem_u32(tH0), aLo = smem_u32(tGYt);
+                     aEG = smem_u32(tEG), aPSI = smem_u32(tPSI), aH0 = smem_u32(tH0), aLo = smem_u32(tGYt);
       // C^T as an MN-major A operand of M = 128 state rows: its second 64-row block is
       // C's second tile (SSD) or the zero tile (GLA, N = 64)
       const uint32_t lboC = V::kGla ? smem_u32(tZero) - aC : TILE;
