@@ -102,11 +102,12 @@ __device__ __forceinline__ void named_barrier_sync(int id, int nthreads) {
 }
 
 // raw 16-bit load: converted only where it is used, so the load does not stall here
+// (into a 32-bit register: a 16-bit one can force a widening move, which waits for the load)
 template <typename T>
 __device__ __forceinline__ unsigned short ld_pinned_u16(const T* p) {
-  unsigned short r;
-  asm volatile("ld.global.cs.u16 %0, [%1];" : "=h"(r) : "l"(p));
-  return r;
+  uint32_t r;
+  asm volatile("ld.global.cs.u16 %0, [%1];" : "=r"(r) : "l"(p));
+  return (unsigned short)r;
 }
 template <typename T>
 __device__ __forceinline__ float u16_to_f(unsigned short r) {
@@ -626,8 +627,13 @@ int ssdc_device_error(bool clear) { return read_device_error(clear); }
 // The tensor-core products per chunk, in three batches (TMEM columns):
 //   1: S [0,128)  P [128,256)  Y2 = C h0^T [256,320)  R2 = B Psi^T [320,384)
 //      dPsi^T = C^T (e^Lam gy) [384,448)
-//   2: R1 = G'^T gy [256,320)
-//   3: gB1 = H1^T C [0,128)  gC1 = H1 B [128,256)  gB2 = u Psi [256,384)  gC2 = gy h0 [384,512)
+//   2: R1 = G'^T [gy_hi | gy_lo] [384,512) (one N = 128 product of the two halves)
+//   3: gB1 = H1^T C [0,N)  gC1 = H1 B [N,2N)  gB2 = u Psi [2N,3N)  gC2 = gy h0 [3N,4N)
+// Batch 3 is issued with batch 2 where its columns are free then (GLA, N = 64:
+// all of it; SSD, N = 128: gB1 and gC1, the rest once epilogue 2 has read R1, R2),
+// so it runs under epilogue 2. An N = 64 product reads its operands from shared
+// memory at 2/3 of the tensor rate (48 cycles per 128x64x16 step against 64 for
+// 128x128x16), hence R1's two halves as one N = 128 product.
 // gy enters P and R1 as bf16/fp16 hi + lo parts (two accumulated products).
 // rowsum Z and colsum Z are both taken from the f32 Z of epilogue 1 (the
 // diagonal terms, the largest, cancel exactly in rowsum - colsum); the column
@@ -648,14 +654,16 @@ constexpr uint32_t TILE = 16384;
 // row/col/q/m/ur partials per column quarter; reduction scratch
 constexpr int NSC = 6;
 constexpr int NSMALLF = 2 * NSC * Q + 5 * CQ * Q + 64;
-constexpr size_t SMALL = NSMALLF * 4 + 4 * 8 + 16 + 16;
+constexpr int DT_BYTES = Q * 8 * 2;  // TMA box of delta: [128 steps][8 heads]
+constexpr size_t SMALL = 128 + DT_BYTES + NSMALLF * 4;  // barriers etc. in the first 128 bytes
+constexpr size_t SMALL_PAD = (SMALL + 1023) / 1024 * 1024;  // the tiles start 1024-aligned
 template <typename V> struct Cfg {
   static constexpr int NS = V::NS;
   static constexpr int NB = NS / 64;  // 64-wide tiles of B and C
   // tiles: U, B, C, GY, GYt, PSI, H0, GP (2), HH (2); GLA adds a zero tile (M = 64
   // padding) and its own tile for exp(Lam) gy (SSD stages it in HH, drained first)
   static constexpr int NTILE = 9 + 2 * NB + (V::kGla ? 2 : 0);
-  static constexpr size_t SMEM = SMALL + 1023 + NTILE * TILE;
+  static constexpr size_t SMEM = SMALL_PAD + NTILE * TILE;
 };
 }  // namespace ssdb
 
@@ -665,26 +673,34 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
                      const __grid_constant__ CUtensorMap tm_C, const __grid_constant__ CUtensorMap tm_gu,
                      const __grid_constant__ CUtensorMap tm_gB, const __grid_constant__ CUtensorMap tm_gC,
                      const float* __restrict__ ckpt, const float* __restrict__ gy,
-                     const float* __restrict__ gfinal, const T* __restrict__ delta, const float* __restrict__ A,
-                     int64_t ash, int L, int H, int seg, T* __restrict__ gdelta, float* __restrict__ gA_part) {
+                     const __grid_constant__ CUtensorMap tm_d, int dmap, const float* __restrict__ gfinal,
+                     const T* __restrict__ delta, const float* __restrict__ A, int64_t ash, int L, int H, int seg,
+                     T* __restrict__ gdelta, float* __restrict__ gA_part) {
   using namespace ssdb;
   constexpr int NS = Cfg<V>::NS, NB = Cfg<V>::NB;
   constexpr int NCT = NS / CQ;  // state columns n per thread in epilogue 3 (16-column blocks: NCT / 16)
-  extern __shared__ unsigned char smem_raw[];
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem_raw);  // tma(u,B,C), mma, mma (batch 1 second group)
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  if ((smem_u32(smem_raw) & 1023u) != 0) {  // the tiles' 1024-byte alignment (SMALL_PAD)
+    if (threadIdx.x == 0) atomicCAS(&g_device_error, 0, 2);
+    return;
+  }
+  // barriers: tma(u,B,C), mma, mma (batch 1 second group), tma(delta)
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem_raw);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 4);
   int* sWide = reinterpret_cast<int*>(tslot + 4);     // [2] a 16-step block spans a decay above e^40
+  // [Q][8] delta of heads h & ~7.. (a TMA destination: 128-byte aligned)
+  unsigned short* sDt = reinterpret_cast<unsigned short*>(smem_raw + 128);
   // [2][NSC][Q] per-chunk scalars, buffer c & 1 for chunk c: Lam_t, delta_t, w_t,
   // exp(Lam_t), D_t, exp(Lam_t0 - Lam_t) (t0 = start of t's 16-step block)
-  float* sSc = reinterpret_cast<float*>(sWide + 4);
+  float* sSc = reinterpret_cast<float*>(sDt + Q * 8);
   float* sRow = sSc + 2 * NSC * Q;                    // [CQ][Q] rowsum Z partials (by row quarter)
   float* sCol = sRow + CQ * Q;                        // [CQ][Q] colsum Z partials
   float* sQ = sCol + CQ * Q;                          // [CQ][Q] gy.Y2 partials
   float* sM = sQ + CQ * Q;                            // [CQ][Q] u_t . R2_t partials
   float* sUR = sM + CQ * Q;                           // [CQ][Q] u_t . r_t partials
   float* sRed = sUR + CQ * Q;                         // 64 floats of reduction scratch
-  // sRed: [0,12) grad_delta warp sums, [16,24) scalar scan, [32,48) <Psi, h0> warp partials
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sRed + 64) + 1023) & ~uintptr_t(1023));
+  // sRed: [0,12) grad_delta warp sums, [32,48) <Psi, h0> warp partials
+  uint8_t* sm = smem_raw + SMALL_PAD;
   uint8_t* tU = sm;
   uint8_t* tB = tU + TILE;        // NB tiles
   uint8_t* tC = tB + NB * TILE;   // NB tiles
@@ -706,6 +722,7 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   const int64_t row0 = (int64_t)b * L;
   constexpr int fmt = MmaFmt<T>::v;
   constexpr uint32_t id128KK = umma::idesc_f16(128, 128, fmt, 0, 0);
+  constexpr uint32_t id128MM = umma::idesc_f16(128, 128, fmt, 1, 1);
   constexpr uint32_t id64KM = umma::idesc_f16(128, 64, fmt, 0, 1);
   constexpr uint32_t id64MM = umma::idesc_f16(128, 64, fmt, 1, 1);
   constexpr uint32_t idNMM = umma::idesc_f16(128, NS, fmt, 1, 1);  // batch 3 products, N = state size
@@ -719,7 +736,7 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   const int cq0 = 32 * jq;         // first of this thread's 32 columns (t, s or n)
   const int ct0 = cq0 & 63;        // that column inside its 64-column tile
   if (tid == 0) {
-    for (int i = 0; i < 3; ++i) mbar_init(&bar[i], 1);
+    for (int i = 0; i < 4; ++i) mbar_init(&bar[i], 1);
     fence_mbar_init();
   }
   if (warp == 0) {
@@ -786,48 +803,104 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   uint32_t tph = 0, mph = 0, mph2 = 0;
 
   auto sum4 = [&](const float* p, int i) { return (p[i] + p[Q + i]) + (p[2 * Q + i] + p[3 * Q + i]); };
-  // A chunk's scalars from its delta (raw bits), by the 128 threads of one
-  // named barrier group (t = index in the group) into buffer buf.
-  auto chunk_scalars = [&](unsigned short dbits, int t, int buf, int barid) {
+  // A chunk's scalars from its delta, by one warp (lane l: steps 4l..4l+3)
+  // into buffer buf. The delta of a chunk arrives by TMA a chunk ahead (its
+  // box: 128 steps of the 8 heads h & ~7..); where the layout does not allow
+  // that box (H % 8 != 0 or a misaligned pointer) the warp loads it directly.
+  constexpr int kScalarWarp = 8;
+  uint32_t dph = 0;
+  auto issue_delta = [&](int c) {  // thread 0
+    mbar_arrive_expect_tx(&bar[3], DT_BYTES);
+    tma_load_2d(sDt, &tm_d, h & ~7, (int)(row0 + (int64_t)c * Q), &bar[3]);
+  };
+  auto delta_bits = [&](int c) {  // the scalar warp: raw delta of steps 4 * lane + 0..3, two per word
+    uint32_t v[4];
+    if (dmap) {
+      mbar_wait(&bar[3], dph & 1u);
+      ++dph;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) v[i] = sDt[(4 * lane + i) * 8 + (h & 7)];
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) v[i] = ld_pinned_u16(delta + (row0 + (int64_t)c * Q + 4 * lane + i) * H + h);
+    }
+    return make_uint2(v[0] | (v[1] << 16), v[2] | (v[3] << 16));
+  };
+  auto chunk_scalars = [&](uint2 raw, int buf) {
     float* sl = sSc + buf * NSC * Q;
-    const float dcur = u16_to_f<T>(dbits);  // delta_t (SSD) or the gate g_t (GLA)
-    float lam = step_log_decay<V>(dcur, Ah), dsum = dcur;
+    float dc[4], lam[4], ds[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t wbits = i < 2 ? raw.x : raw.y;
+      dc[i] = u16_to_f<T>((unsigned short)(wbits >> (16 * (i & 1))));  // delta_t (SSD) or the gate g_t (GLA)
+      lam[i] = step_log_decay<V>(dc[i], Ah) + (i > 0 ? lam[i - 1] : 0.f);
+      ds[i] = dc[i] + (i > 0 ? ds[i - 1] : 0.f);
+    }
+    float lt = lam[3], dt = ds[3];  // inclusive scan of the lanes' totals
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const float n1 = __shfl_up_sync(0xffffffffu, lam, o);
-      const float n2 = __shfl_up_sync(0xffffffffu, dsum, o);
+      const float n1 = __shfl_up_sync(0xffffffffu, lt, o);
+      const float n2 = __shfl_up_sync(0xffffffffu, dt, o);
       if (lane >= o) {
-        lam += n1;
-        dsum += n2;
+        lt += n1;
+        dt += n2;
       }
     }
-    const int w = t >> 5;
-    if (lane == 31) {
-      sRed[16 + w] = lam;
-      sRed[20 + w] = dsum;
+    float lx = __shfl_up_sync(0xffffffffu, lt, 1), dx = __shfl_up_sync(0xffffffffu, dt, 1);
+    if (lane == 0) lx = dx = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      lam[i] += lx;
+      ds[i] += dx;
     }
-    if (t == 0) sWide[buf] = 0;
-    named_barrier_sync(barid, 128);
-    for (int v = 0; v < w; ++v) {
-      lam += sRed[16 + v];
-      dsum += sRed[20 + v];
+    const float lam_last = __shfl_sync(0xffffffffu, lam[3], 31);
+    const float lam_blk = __shfl_sync(0xffffffffu, lam[0], lane & ~3);  // Lam at the 16-step block start
+    float w[4], el[4], cf[4];
+    bool wide = false;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      w[i] = __expf(lam_last - lam[i]) * (V::kGla ? 1.f : dc[i]);
+      el[i] = __expf(lam[i]);
+      const float span = lam_blk - lam[i];
+      cf[i] = __expf(span);
+      wide |= span > 40.f;
     }
-    sl[t] = lam;
-    sl[Q + t] = V::kGla ? 1.f : dcur;      // delta (1 for GLA)
-    sl[4 * Q + t] = V::kGla ? dcur : dsum;  // D_t for dL/dA (SSD) or the gate (GLA)
-    named_barrier_sync(barid, 128);
-    sl[2 * Q + t] = __expf(sl[Q - 1] - lam) * (V::kGla ? 1.f : dcur);
-    sl[3 * Q + t] = __expf(lam);
-    const float span = sl[t & ~15] - lam;
-    sl[5 * Q + t] = __expf(span);
-    if (__any_sync(0xffffffffu, span > 40.f) && lane == 0) sWide[buf] = 1;
+    float4* sl4 = reinterpret_cast<float4*>(sl) + lane;
+    sl4[0] = make_float4(lam[0], lam[1], lam[2], lam[3]);
+    sl4[Q / 4] = V::kGla ? make_float4(1.f, 1.f, 1.f, 1.f) : make_float4(dc[0], dc[1], dc[2], dc[3]);  // delta
+    sl4[2 * Q / 4] = make_float4(w[0], w[1], w[2], w[3]);
+    sl4[3 * Q / 4] = make_float4(el[0], el[1], el[2], el[3]);
+    // D_t for dL/dA (SSD) or the gate (GLA)
+    sl4[4 * Q / 4] = V::kGla ? make_float4(dc[0], dc[1], dc[2], dc[3]) : make_float4(ds[0], ds[1], ds[2], ds[3]);
+    sl4[5 * Q / 4] = make_float4(cf[0], cf[1], cf[2], cf[3]);
+    const bool any_wide = __any_sync(0xffffffffu, wide);
+    if (lane == 0) sWide[buf] = any_wide ? 1 : 0;
   };
-  // the first chunk processed (the last one)
-  unsigned short dnext = 0;
-  if (warp < 4) {
-    dnext = ld_pinned_u16(delta + (row0 + (int64_t)(nck - 1) * Q + tid) * H + h);
-    chunk_scalars(dnext, tid, (nck - 1) & 1, 1);
-  }
+  // batch 3 (thread 0): gB1 = H1^T C and gC1 = H1 B at columns 0 and N, then
+  // gB2 = u Psi(old) and gC2 = gy h0 at columns 2N and 3N
+  auto batch3_h1 = [&]() {
+    const uint32_t aB = smem_u32(tB), aC = smem_u32(tC), aHH = smem_u32(tHH);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const uint32_t ko = (k >> 2) * TILE + (k & 3) * 32;
+      umma::mma_f16(tbase + 0, umma::sdesc_mn(aHH + k * 2048, TILE), umma::sdesc_mn(aC + k * 2048, TILE), idNMM,
+                    k > 0);
+      umma::mma_f16(tbase + NS, umma::sdesc_k(aHH + ko), umma::sdesc_mn(aB + k * 2048, TILE), idNKM, k > 0);
+    }
+  };
+  auto batch3_state = [&]() {
+    const uint32_t aU = smem_u32(tU), aGY = smem_u32(tGY), aPSI = smem_u32(tPSI), aH0 = smem_u32(tH0);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      umma::mma_f16(tbase + 3 * NS, umma::sdesc_k(aGY + k * 32), umma::sdesc_k(aH0 + k * 32), idNKK, k > 0);
+      umma::mma_f16(tbase + 2 * NS, umma::sdesc_k(aU + k * 32), umma::sdesc_k(aPSI + k * 32), idNKK, k > 0);
+    }
+  };
+  // the first chunk processed (the last one); chunk nck-2's delta follows
+  if (dmap && tid == 0) issue_delta(nck - 1);
+  if (warp == kScalarWarp) chunk_scalars(delta_bits(nck - 1), (nck - 1) & 1);
+  __syncthreads();
+  if (dmap && tid == 0 && nck > 1) issue_delta(nck - 2);
 
   for (int c = nck - 1; c >= 0; --c) {
     // ---- P0: h0 and gy tiles (the chunk's scalars were computed during the previous chunk)
@@ -1026,38 +1099,45 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     umma::fence_before_sync();
     __syncthreads();
 
-    // ---- batch 2: R1
+    // ---- batch 2: R1 = G'^T [gy_hi | gy_lo] (the lo tile is the second 64-wide N block),
+    //      then batch 3 as far as its columns are free
     if (tid == 0) {
       umma::fence_after_sync();
-      const uint32_t aGY = smem_u32(tGY), aGP = smem_u32(tGP), aLo = smem_u32(tGYt);
+      const uint32_t aGY = smem_u32(tGY), aGP = smem_u32(tGP);
+      const uint32_t lboGY = smem_u32(tGYt) - aGY;
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        umma::mma_f16(tbase + 256, umma::sdesc_mn(aGP + k * 2048, TILE), umma::sdesc_mn(aGY + k * 2048, TILE),
-                      id64MM, k > 0);
-        umma::mma_f16(tbase + 256, umma::sdesc_mn(aGP + k * 2048, TILE), umma::sdesc_mn(aLo + k * 2048, TILE),
-                      id64MM, true);
-      }
+      for (int k = 0; k < 8; ++k)
+        umma::mma_f16(tbase + 384, umma::sdesc_mn(aGP + k * 2048, TILE), umma::sdesc_mn(aGY + k * 2048, lboGY),
+                      id128MM, k > 0);
       umma::commit(&bar[1]);
+      batch3_h1();
+      if constexpr (V::kGla) {
+        batch3_state();
+        umma::commit(&bar[2]);
+      }
     }
     // The next chunk's register operands: grad_y here, while batch 2 runs, h0
     // after epilogue 2 (an SM keeps a limited number of load bytes in flight).
     // A proxy fence waits for the thread's outstanding loads, so each group is
     // issued right after one, with a batch and an epilogue to arrive before the next.
-    if (c > 0) {
-      load_gy(c - 1);
-      if (warp >= 8 && warp < 12) dnext = ld_pinned_u16(delta + (row0 + (int64_t)(c - 1) * Q + tid - 256) * H + h);
-    }
+    if (c > 0) load_gy(c - 1);
+    // the previous chunk's scalars (its delta arrived during the chunk before)
+    if (warp == kScalarWarp && c > 0) chunk_scalars(delta_bits(c - 1), (c - 1) & 1);
     mbar_wait(&bar[1], mph & 1u);
     ++mph;
     umma::fence_after_sync();
 
-    // ---- epilogue 2 (thread: row t, channels ch0..): r, grad_u (staged in GYt), u.r
+    // ---- epilogue 2 (thread: row t, channels ch0..): r, grad_u (staged in GYt), u.r (SSD)
     {
       const int t = row;
       const float lt = sLam[t], dt = sDel[t];
       {
         float r1[CH], r2[CH];
-        umma::tmem_ld16(tl + 256 + ch0, r1);
+        umma::tmem_ld16(tl + 384 + ch0, r1);
+        umma::tmem_ld16(tl + 448 + ch0, r2);
+        umma::tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < CH; ++i) r1[i] += r2[i];
         umma::tmem_ld16(tl + 320 + ch0, r2);
         umma::tmem_wait_ld();
         const float f2 = __expf(sLam[Q - 1] - lt);
@@ -1066,16 +1146,16 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
         for (int cc = 0; cc < CH / 8; ++cc) {
           const uint32_t off = umma::sw128_off(t, ch0 + 8 * cc);
           float f[8], o[8];
-          unpack8<T>(*reinterpret_cast<const int4*>(tU + off), f);
+          if constexpr (!V::kGla) unpack8<T>(*reinterpret_cast<const int4*>(tU + off), f);
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             const float rv = r1[8 * cc + i] + f2 * r2[8 * cc + i];
-            ur += f[i] * rv;
-            o[i] = dt * rv;
+            if constexpr (!V::kGla) ur += f[i] * rv;
+            o[i] = V::kGla ? rv : dt * rv;
           }
           *reinterpret_cast<int4*>(tGYt + off) = pack8<T>(o);  // grad_u staging (GYt free after batch 2)
         }
-        sUR[jq * Q + t] = ur;
+        if constexpr (!V::kGla) sUR[jq * Q + t] = ur;
       }
       // fold epilogue 1's four partials of one array per thread into its slot 0
       // (rowsum Z, colsum Z, gy.Y2, u.R2 for jq = 0..3), shortening grad_delta
@@ -1089,30 +1169,18 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     umma::fence_before_sync();
     __syncthreads();
 
-    // ---- batch 3: gB1 = H1^T C, gC1 = H1 B, gB2 = u Psi(old), gC2 = gy h0 at columns 0, N, 2N, 3N;
-    //      store grad_u
+    // ---- SSD: the rest of batch 3 (R1, R2 are read); store grad_u
     if (tid == 0) {
       umma::fence_after_sync();
-      const uint32_t aU = smem_u32(tU), aB = smem_u32(tB), aC = smem_u32(tC), aGY = smem_u32(tGY),
-                     aPSI = smem_u32(tPSI), aH0 = smem_u32(tH0), aHH = smem_u32(tHH);
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const uint32_t ko = (k >> 2) * TILE + (k & 3) * 32;
-        umma::mma_f16(tbase + 0, umma::sdesc_mn(aHH + k * 2048, TILE), umma::sdesc_mn(aC + k * 2048, TILE),
-                      idNMM, k > 0);
-        umma::mma_f16(tbase + NS, umma::sdesc_k(aHH + ko), umma::sdesc_mn(aB + k * 2048, TILE), idNKM, k > 0);
+      if constexpr (!V::kGla) {
+        batch3_state();
+        umma::commit(&bar[2]);
       }
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        umma::mma_f16(tbase + 3 * NS, umma::sdesc_k(aGY + k * 32), umma::sdesc_k(aH0 + k * 32), idNKK, k > 0);
-        umma::mma_f16(tbase + 2 * NS, umma::sdesc_k(aU + k * 32), umma::sdesc_k(aPSI + k * 32), idNKK, k > 0);
-      }
-      umma::commit(&bar[1]);
       tma_store_3d(&tm_gu, 0, h, (int)(row0 + (int64_t)c * Q), tGYt);
       bulk_commit();
+      if (dmap && c > 1) issue_delta(c - 2);  // the scalar warp has read chunk c-1's box
     }
-    // ---- while batch 3 runs: grad_delta and grad_A (warps 4-7, thread t; warp 0 issues the
-    //      MMAs), and the previous chunk's scalars (warps 8-11)
+    // ---- while batch 3 completes: grad_delta and grad_A (warps 4-7, thread t)
     // dLam_t = x_t + [t = last] lastv with x_t = rowsum Z - colsum Z + exp(Lam_t) q_t - w_t m_t,
     // lastv = exp(Lam_last) <Psi, h0> + sum_t w_t m_t; grad_delta_t = A sum_{t' >= t} dLam_t' + u_t.r_t
     if (warp >= 4 && warp < 8) {
@@ -1155,11 +1223,9 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
         g = Ah * dlam + sum4(sUR, t);
       }
       gdelta[(row0 + (int64_t)c * Q + t) * H + h] = from_f<T>(g);
-    } else if (warp >= 8 && warp < 12 && c > 0) {
-      chunk_scalars(dnext, tid - 256, (c - 1) & 1, 2);
     }
-    mbar_wait(&bar[1], mph & 1u);
-    ++mph;
+    mbar_wait(&bar[2], mph2 & 1u);
+    ++mph2;
     umma::fence_after_sync();
     // u, B, C of this chunk are no longer read: stream the previous chunk's
     if (tid == 0 && c > 0) {
@@ -1238,14 +1304,21 @@ static int chunk_bwd_launch(const float* gy, const float* gf, const float* ckpt,
                             int64_t H, int64_t seg, void* gu, void* gd, void* gB, void* gC, float* ws,
                             cudaStream_t st) {
   constexpr size_t SMEM = ssdb::Cfg<V>::SMEM;
-  CUtensorMap mu, mB, mC, mgu, mgB, mgC;
+  CUtensorMap mu, mB, mC, mgu, mgB, mgC, md;
   if (int rc = ssd_tmaps<T, V::NS>(u, Bm, Cm, batch, L, H, &mu, &mB, &mC)) return rc;
   if (int rc = ssd_tmaps<T, V::NS>(gu, gB, gC, batch, L, H, &mgu, &mgB, &mgC)) return rc;
+  // delta [B*L, H] in boxes of 128 steps x 8 heads (16 bytes), where the row pitch and base allow
+  const int dmap = (H % 8 == 0 && (reinterpret_cast<uintptr_t>(delta) & 15) == 0) ? 1 : 0;
+  memset(&md, 0, sizeof(md));
+  if (dmap)
+    if (int rc = make_tmap_2d(&md, delta, TmapType<T>::v, 2, (uint64_t)H, (uint64_t)batch * L, (uint64_t)H * 2, 8,
+                              ssdb::Q))
+      return rc;
   auto k = ssd_chunk_bwd_kernel<T, V>;
   const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM);
   if (e != cudaSuccess) return set_error(MR_E_LAUNCH, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-  k<<<(unsigned)(batch * H), ssdb::NT, SMEM, st>>>(mu, mB, mC, mgu, mgB, mgC, ckpt, gy, gf, (const T*)delta, A, ash,
-                                                   (int)L, (int)H, (int)seg, (T*)gd, ws);
+  k<<<(unsigned)(batch * H), ssdb::NT, SMEM, st>>>(mu, mB, mC, mgu, mgB, mgC, ckpt, gy, md, dmap, gf,
+                                                   (const T*)delta, A, ash, (int)L, (int)H, (int)seg, (T*)gd, ws);
   return check_launch(V::kGla ? "gla_chunk_bwd_kernel" : "ssd_chunk_bwd_kernel");
 }
 

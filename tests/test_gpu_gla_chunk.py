@@ -88,6 +88,7 @@ def test_gla_chunk_forward_matches_oracle(cuda_dev, Bt, L, H, gates, dtype):
     (2, 512, 3, "sigmoid", True, torch.bfloat16),
     (1, 384, 2, "strong", False, torch.bfloat16),
     (1, 256, 2, "sigmoid", True, torch.float16),
+    (1, 256, 16, "sigmoid", True, torch.bfloat16),  # H % 8 == 0: the gates arrive by TMA
 ])
 def test_gla_chunk_backward_matches_oracle(cuda_dev, Bt, L, H, gates, with_final, dtype):
     """Every gradient of <y, gy> + <final, g_final>."""

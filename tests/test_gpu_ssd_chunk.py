@@ -72,6 +72,7 @@ def test_chunk_forward_matches_oracle(cuda_dev, Bt, L, H, seg, dt_scale, dtype):
     (2, 512, 3, 0.1, True, torch.bfloat16),
     (1, 384, 2, 2.0, False, torch.bfloat16),
     (1, 256, 2, 0.1, True, torch.float16),
+    (1, 256, 16, 0.1, True, torch.bfloat16),  # H % 8 == 0: delta arrives by TMA
 ])
 def test_chunk_backward_matches_oracle(cuda_dev, Bt, L, H, dt_scale, with_final, dtype):
     """Every gradient of <y, gy> + <final, g_final>; grad_A as the per-head
