@@ -807,7 +807,7 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   // into buffer buf. The delta of a chunk arrives by TMA a chunk ahead (its
   // box: 128 steps of the 8 heads h & ~7..); where the layout does not allow
   // that box (H % 8 != 0 or a misaligned pointer) the warp loads it directly.
-  constexpr int kScalarWarp = 8;
+  constexpr int kScalarWarp = 9;  // off sub-partition 0, whose thread 0 blocks while it issues the MMAs
   uint32_t dph = 0;
   auto issue_delta = [&](int c) {  // thread 0
     mbar_arrive_expect_tx(&bar[3], DT_BYTES);
@@ -946,8 +946,9 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     fence_proxy_async_smem();
     __syncthreads();
 
-    // ---- batch 1, in two commit groups: dPsi^T, S, P (dPsi^T first: it reads the HH
-    //      tile that epilogue 1 rewrites), then Y2, R2
+    // ---- batch 1, in two commit groups: epilogue 1 starts on the first. SSD: dPsi^T, S, P
+    //      (dPsi^T first: it reads exp(Lam) gy staged in the HH tile that epilogue 1
+    //      rewrites), then Y2, R2; GLA (exp(Lam) gy in its own tile): S, P, then dPsi^T, Y2, R2
     if (tid == 0) {
       bulk_wait_read<0>();
       mbar_wait(&bar[0], tph & 1u);
@@ -955,13 +956,16 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
       umma::fence_after_sync();
       const uint32_t aU = smem_u32(tU), aB = smem_u32(tB), aC = smem_u32(tC), aGY = smem_u32(tGY),
                      aEG = smem_u32(tEG), aPSI = smem_u32(tPSI), aH0 = smem_u32(tH0), aLo = smem_u32(tGYt);
-      // C^T as an MN-major A operand of M = 128 state rows: its second 64-row block is
-      // C's second tile (SSD) or the zero tile (GLA, N = 64)
-      const uint32_t lboC = V::kGla ? smem_u32(tZero) - aC : TILE;
+      auto mma_dpsi = [&]() {
+        // C^T as an MN-major A operand of M = 128 state rows: its second 64-row block is
+        // C's second tile (SSD) or the zero tile (GLA, N = 64)
+        const uint32_t lboC = V::kGla ? smem_u32(tZero) - aC : TILE;
 #pragma unroll
-      for (int k = 0; k < 8; ++k)
-        umma::mma_f16(tbase + 384, umma::sdesc_mn(aC + k * 2048, lboC), umma::sdesc_mn(aEG + k * 2048, TILE),
-                      id64MM, k > 0);
+        for (int k = 0; k < 8; ++k)
+          umma::mma_f16(tbase + 384, umma::sdesc_mn(aC + k * 2048, lboC), umma::sdesc_mn(aEG + k * 2048, TILE),
+                        id64MM, k > 0);
+      };
+      if constexpr (!V::kGla) mma_dpsi();
 #pragma unroll
       for (int k = 0; k < NS / 16; ++k) {
         const uint32_t ko = (k >> 2) * TILE + (k & 3) * 32;
@@ -974,6 +978,7 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
       for (int k = 0; k < 4; ++k)
         umma::mma_f16(tbase + 128, umma::sdesc_k(aLo + k * 32), umma::sdesc_k(aU + k * 32), id128KK, true);
       umma::commit(&bar[1]);
+      if constexpr (V::kGla) mma_dpsi();
 #pragma unroll
       for (int k = 0; k < NS / 16; ++k) {
         const uint32_t ko = (k >> 2) * TILE + (k & 3) * 32;
