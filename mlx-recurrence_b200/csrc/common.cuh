@@ -25,6 +25,16 @@ template <> __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float
 }
 template <> __device__ __forceinline__ __half from_f<__half>(float v) { return __float2half_rn(v); }
 
+// ---- GLA gate range of the tensor-core path ----------------------------------
+// Gates the chunked GLA kernels compute to within tolerance (their algebra works
+// in log g and divides by g for the gate gradient). A unit (batch row, head) with
+// any other gate is marked by the chunk kernel with a NaN in its first output
+// element (y[b, 0, h, 0] forward, grad_gates[b, 0, h] backward) and recomputed
+// by the per-step kernels, which recompute every marked unit (a NaN there for any
+// other reason is recomputed to the same value).
+__device__ __forceinline__ bool gla_gate_in_range(float g) { return g >= 1e-3f && g <= 1.f; }
+constexpr unsigned kMarkNaN = 0x7fc00000u;
+
 // ---- V consecutive elements as one vector access ----------------------------
 // Raw storage of V elements of T (V*sizeof(T) bytes: 2..16), loaded/stored as
 // a single aligned vector instruction.

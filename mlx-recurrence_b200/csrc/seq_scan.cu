@@ -270,37 +270,19 @@ __global__ void sum_over_batch_kernel(const float* __restrict__ part, int64_t ba
 // GLA
 // ============================================================================
 
-// Gates the tensor-core GLA path computes to within tolerance (its chunk
-// algebra works in log g and divides by g for the gate gradient). Units with
-// any other gate are recomputed here after the chunk kernel ("only_bad").
-__device__ __forceinline__ bool gla_gate_ok(float g) { return g >= 1e-3f && g <= 1.f; }
-
-template <typename T>
-__device__ bool gla_unit_has_bad_gate(const T* __restrict__ gates, int64_t b, int h, int L, int H) {
-  bool bad = false;
-  for (int t = threadIdx.x; t < L; t += blockDim.x) bad |= !gla_gate_ok(to_f(gates[(b * L + t) * H + h]));
-  return __syncthreads_or(bad) != 0;
-}
-
-// flags[unit] = unit (b * H + h) holds a gate outside the tensor-core range; one CTA per unit
-template <typename T>
-__global__ void __launch_bounds__(kSeqThreads)
-gla_bad_units_kernel(const T* __restrict__ gates, int L, int H, int* __restrict__ flags) {
-  const int unit = blockIdx.x;
-  const bool bad = gla_unit_has_bad_gate(gates, unit / H, unit % H, L, H);
-  if (threadIdx.x == 0) flags[unit] = bad ? 1 : 0;
-}
+// After the tensor-core GLA path ("only_marked"), these kernels recompute the
+// units it marked (a gate outside gla_gate_in_range; common.cuh).
 
 template <typename T, int R, int IK>
 __global__ void __launch_bounds__(kSeqThreads)
 gla_seq_fwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
                    const T* __restrict__ gates, int L, int H, int Dh, int seg,
-                   float* __restrict__ y, float* __restrict__ ckpt, int only_bad) {
+                   float* __restrict__ y, float* __restrict__ ckpt, int only_marked) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t b = blockIdx.x / H;
   const int h = blockIdx.x % H;
   const int nseg = L / seg;
-  if (only_bad && !gla_unit_has_bad_gate(gates, b, h, L, H)) return;
+  if (only_marked && !isnan(y[(b * L * H + h) * Dh])) return;
   float S[IK][R];
 #pragma unroll
   for (int i = 0; i < IK; ++i)
@@ -347,7 +329,7 @@ gla_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfina
                    const T* __restrict__ k, const T* __restrict__ v, const T* __restrict__ gates,
                    int L, int H, int Dh, int seg, T* __restrict__ gq, T* __restrict__ gk,
                    T* __restrict__ gv, T* __restrict__ gg, float* __restrict__ scratch, int units,
-                   const int* __restrict__ only_flags) {
+                   int only_marked) {
   constexpr int NP = 32 * IK;
   __shared__ float pQ[kTS][8][NP];
   __shared__ float pK[kTS][8][NP];
@@ -361,7 +343,7 @@ gla_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfina
   for (int unit = blockIdx.x; unit < units; unit += gridDim.x) {
     const int64_t b = unit / H;
     const int h = unit % H;
-    if (only_flags != nullptr && only_flags[unit] == 0) continue;
+    if (only_marked && !isnan(to_f(gg[b * L * H + h]))) continue;
 
     float adj[IK][R];
 #pragma unroll
@@ -496,11 +478,10 @@ size_t gla_seq_bwd_ws_bytes(int64_t batch, int64_t L, int64_t H, int64_t Dh, int
 // scratch slots of the GLA fallback after the tensor-core backward (units with
 // out-of-range gates, walked by this many CTAs)
 constexpr int64_t kGlaFallbackSlots = 16;
-// layout: the slots' scratch, then one int flag per unit (256-byte aligned)
+// the scratch of kGlaFallbackSlots units walked in turn
 size_t gla_fallback_ws_bytes(int64_t batch, int64_t L, int64_t H, int64_t Dh, int64_t seg) {
   const int64_t slots = batch * H < kGlaFallbackSlots ? batch * H : kGlaFallbackSlots;
-  const size_t scr = (gla_seq_bwd_ws_bytes(slots, L, 1, Dh, seg) + 255) / 256 * 256;
-  return scr + (size_t)batch * H * sizeof(int);
+  return gla_seq_bwd_ws_bytes(slots, L, 1, Dh, seg);
 }
 
 bool ssd_seq_supported(int64_t Dh, int64_t N) {
@@ -581,8 +562,8 @@ int ssd_seq_bwd_launch(const float* gy, const float* gf, const float* ckpt, cons
   return check_launch("sum_over_batch_kernel");
 }
 
-// only_bad: recompute just the units with a gate outside the tensor-core
-// path's range (gla_gate_ok), after that path has written every unit.
+// only_bad: recompute just the units the tensor-core path marked (a gate
+// outside gla_gate_in_range), after that path has written every unit.
 template <typename T>
 int gla_seq_fwd_launch(const void* q, const void* k, const void* v, const void* g, int64_t batch,
                        int64_t L, int64_t H, int64_t Dh, int64_t seg, float* y, float* ckpt,
@@ -610,14 +591,8 @@ int gla_seq_bwd_launch(const float* gy, const float* gf, const float* ckpt, cons
   T *gq_ = (T*)gq, *gk_ = (T*)gk, *gv_ = (T*)gv, *gg_ = (T*)gg;
   float* scr = (float*)ws;
   const int L_ = (int)L, H_ = (int)H, s_ = (int)seg, u_ = (int)units;
-  const int* flags = nullptr;
-  if (only_bad) {  // flag the units first (one CTA each), then walk them with a few slots
-    const int64_t slots = units < kGlaFallbackSlots ? units : kGlaFallbackSlots;
-    int* f = (int*)((char*)ws + (gla_seq_bwd_ws_bytes(slots, L, 1, Dh, seg) + 255) / 256 * 256);
-    gla_bad_units_kernel<T><<<(unsigned)units, kSeqThreads, 0, st>>>(g_, L_, H_, f);
-    if (int rc = check_launch("gla_bad_units_kernel")) return rc;
-    flags = f;
-  }
+  // only_bad: a few CTAs walk the units and recompute the marked ones
+  const int flags = only_bad ? 1 : 0;
   dim3 grid((unsigned)(only_bad ? (units < kGlaFallbackSlots ? units : kGlaFallbackSlots) : units));
   switch ((int)Dh) {
     case 32: gla_seq_bwd_kernel<T, 4, 1><<<grid, kSeqThreads, 0, st>>>(gy, gf, ckpt, q_, k_, v_, g_, L_, H_, 32, s_, gq_, gk_, gv_, gg_, scr, u_, flags); break;

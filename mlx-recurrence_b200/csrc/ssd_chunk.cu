@@ -164,7 +164,7 @@ __device__ __forceinline__ int4 pack8(const float* f) {
 
 // decay input of step t: delta_t (SSD, log decay delta_t A_h) or the gate g_t
 // (GLA, log decay log g_t; a gate <= 0 or NaN is clamped to e^-80 - such units
-// are recomputed by the sequential kernels, see gla_gate_ok)
+// are marked for the per-step kernels, see gla_gate_in_range)
 template <typename V>
 __device__ __forceinline__ float step_log_decay(float x, float Ah) {
   if constexpr (V::kGla)
@@ -178,7 +178,7 @@ __global__ void __launch_bounds__(ssdc::NT, 1)
 ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_constant__ CUtensorMap tm_B,
                      const __grid_constant__ CUtensorMap tm_C, const __grid_constant__ CUtensorMap tm_y,
                      const __grid_constant__ CUtensorMap tm_ck, const T* __restrict__ delta,
-                     const float* __restrict__ A, int64_t ash, int L, int H, int seg) {
+                     const float* __restrict__ A, int64_t ash, int L, int H, int seg, float* __restrict__ y) {
   using namespace ssdc;
   constexpr int NS = Cfg<V>::NS, NB = Cfg<V>::NB;
   constexpr uint32_t STAGE = Cfg<V>::STAGE;
@@ -192,6 +192,7 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   float* sSc = reinterpret_cast<float*>(tslot + 4);
   unsigned short* sDr = reinterpret_cast<unsigned short*>(sSc + 4 * Q);
   float* sWarp = reinterpret_cast<float*>(sDr + 2 * Q);  // [8] scan scratch
+  int* sMark = reinterpret_cast<int*>(sWarp + 7);         // GLA: a gate outside the tensor-core range
   uint8_t* sm = smem_raw + SMALL_PAD;
   if ((smem_u32(smem_raw) & 1023u) != 0) {  // the tiles' 1024-byte alignment (see SMALL_PAD)
     if (threadIdx.x == 0) atomicCAS(&g_device_error, 0, 2);
@@ -218,6 +219,7 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   if (tid == 0) {
     for (int i = 0; i < 6; ++i) mbar_init(&bar[i], 1);
     fence_mbar_init();
+    *sMark = 0;
   }
   if (warp == 0) {
     umma::tmem_alloc(tslot, 512);
@@ -281,6 +283,8 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     float* sl = sSc + buf * 2 * Q;
     const float dcur = u16_to_f<T>(dnext);
     float lam = step_log_decay<V>(dcur, Ah);
+    if constexpr (V::kGla)
+      if (__any_sync(0xffffffffu, !gla_gate_in_range(dcur)) && lane == 0) *sMark = 1;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const float n = __shfl_up_sync(0xffffffffu, lam, o);
@@ -510,6 +514,8 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   }
   if (tid == 0) bulk_wait_all();
   __syncthreads();
+  if constexpr (V::kGla)  // mark the unit for the per-step kernel (its y has landed)
+    if (tid == 0 && *sMark) y[((int64_t)b * L * H + h) * DH] = __uint_as_float(kMarkNaN);
   if (warp == 0) umma::tmem_dealloc(tbase, 512);
 }
 
@@ -572,7 +578,7 @@ static int chunk_fwd_launch(const void* u, const void* delta, const void* Bm, co
   const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM);
   if (e != cudaSuccess) return set_error(MR_E_LAUNCH, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
   k<<<(unsigned)(batch * H), ssdc::NT, SMEM, st>>>(mu, mB, mC, my, mck, (const T*)delta, A, ash, (int)L, (int)H,
-                                                   (int)seg);
+                                                   (int)seg, y);
   return check_launch(V::kGla ? "gla_chunk_fwd_kernel" : "ssd_chunk_fwd_kernel");
 }
 
@@ -737,6 +743,7 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   const int ct0 = cq0 & 63;        // that column inside its 64-column tile
   if (tid == 0) {
     for (int i = 0; i < 4; ++i) mbar_init(&bar[i], 1);
+    sWide[2] = 0;  // GLA: a gate outside the tensor-core range
     fence_mbar_init();
   }
   if (warp == 0) {
@@ -835,6 +842,11 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
       dc[i] = u16_to_f<T>((unsigned short)(wbits >> (16 * (i & 1))));  // delta_t (SSD) or the gate g_t (GLA)
       lam[i] = step_log_decay<V>(dc[i], Ah) + (i > 0 ? lam[i - 1] : 0.f);
       ds[i] = dc[i] + (i > 0 ? ds[i - 1] : 0.f);
+    }
+    if constexpr (V::kGla) {
+      const bool out = !gla_gate_in_range(dc[0]) || !gla_gate_in_range(dc[1]) || !gla_gate_in_range(dc[2]) ||
+                       !gla_gate_in_range(dc[3]);
+      if (__any_sync(0xffffffffu, out) && lane == 0) sWide[2] = 1;
     }
     float lt = lam[3], dt = ds[3];  // inclusive scan of the lanes' totals
 #pragma unroll
@@ -1290,6 +1302,8 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     if (tid == 128) gA_part[bh] = gA_acc;  // step t = 0 of the grad_delta warps
   if (tid == 0) bulk_wait_all();
   __syncthreads();
+  if constexpr (V::kGla)  // mark the unit for the per-step kernel
+    if (tid == 0 && sWide[2]) gdelta[row0 * H + h] = from_f<T>(__uint_as_float(kMarkNaN));
   if (warp == 0) umma::tmem_dealloc(tbase, 512);
 }
 

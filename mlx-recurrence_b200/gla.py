@@ -35,6 +35,8 @@ def _validate(q, k, v, gates):
 class _GLAScan(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, gates, seg):
+        # an unused output's cotangent arrives as None (no zero tensor is made)
+        ctx.set_materialize_grads(False)
         Bt, L, H, Dh = _validate(q, k, v, gates)
         check_segment_shape(L, seg, Dh, "Dh")  # gla.py:287
         dev = _lib.require_cuda(q, k, v, gates)

@@ -23,6 +23,8 @@ from ._chassis import DEFAULT_SEG, check_segment_shape, common_dtype, grad_out, 
 class _RGLRUScan(torch.autograd.Function):
     @staticmethod
     def forward(ctx, a, x, seg):
+        # an unused output's cotangent arrives as None (no zero tensor is made)
+        ctx.set_materialize_grads(False)
         if a.dim() != 3 or x.shape != a.shape:
             raise ValueError(f"a and x must both be [B, L, D], got {tuple(a.shape)} and {tuple(x.shape)}")
         Bt, L, D = a.shape

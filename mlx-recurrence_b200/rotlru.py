@@ -38,6 +38,8 @@ def _validate(a, cs, sn, x):
 class _RotLRUScan(torch.autograd.Function):
     @staticmethod
     def forward(ctx, a, cs, sn, x, seg):
+        # an unused output's cotangent arrives as None (no zero tensor is made)
+        ctx.set_materialize_grads(False)
         Bt, L, Dp = _validate(a, cs, sn, x)
         check_segment_shape(L, seg, x.shape[2], "D")  # rotlru.py:565
         dev = _lib.require_cuda(a, cs, sn, x)

@@ -52,6 +52,8 @@ def _a_f32(A_neg):
 class _SSDScan(torch.autograd.Function):
     @staticmethod
     def forward(ctx, u, delta, B, C, A_neg, seg):
+        # an unused output's cotangent arrives as None (no zero tensor is made)
+        ctx.set_materialize_grads(False)
         Bt, L, H, Dh, N = _validate(u, delta, B, C, A_neg)
         check_segment_shape(L, seg, Dh, "Dh")  # ssd.py:328
         dev = _lib.require_cuda(u, delta, B, C, A_neg)
