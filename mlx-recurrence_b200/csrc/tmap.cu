@@ -24,6 +24,15 @@ static EncodeTiledFn encoder() {
   return fn;
 }
 
+// The encoder checks the address against the calling thread's current context.
+// A thread that has made no CUDA runtime call yet (an autograd worker thread
+// that only reused cached allocations, say) has none: bind its current device's
+// primary context (the runtime does so on cudaSetDevice) and encode again.
+static bool bind_current_device() {
+  int d = 0;
+  return cudaGetDevice(&d) == cudaSuccess && cudaSetDevice(d) == cudaSuccess;
+}
+
 int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes,
                  uint64_t cols, uint64_t rows, uint64_t row_bytes, uint32_t box_cols,
                  uint32_t box_rows, CUtensorMapSwizzle swizzle) {
@@ -35,9 +44,12 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int
   const cuuint64_t strides[1] = {row_bytes};
   const cuuint32_t box[2] = {box_cols, box_rows};
   const cuuint32_t estr[2] = {1, 1};
-  const CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
-                         CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  auto encode = [&] {
+    return enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  };
+  CUresult r = encode();
+  if (r == CUDA_ERROR_INVALID_CONTEXT && bind_current_device()) r = encode();
   if (r != CUDA_SUCCESS)
     return set_error(MR_E_LAUNCH, "cuTensorMapEncodeTiled failed (%d): dims %llu x %llu, box %u x %u",
                      (int)r, (unsigned long long)cols, (unsigned long long)rows, box_cols, box_rows);
@@ -55,9 +67,12 @@ int make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int
   const cuuint64_t strides[2] = {s1, s2};
   const cuuint32_t box[3] = {b0, b1, b2};
   const cuuint32_t estr[3] = {1, 1, 1};
-  const CUresult r = enc(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr,
-                         CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  auto encode = [&] {
+    return enc(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  };
+  CUresult r = encode();
+  if (r == CUDA_ERROR_INVALID_CONTEXT && bind_current_device()) r = encode();
   if (r != CUDA_SUCCESS)
     return set_error(MR_E_LAUNCH, "cuTensorMapEncodeTiled (3d) failed (%d)", (int)r);
   return MR_OK;
