@@ -82,14 +82,19 @@ def algorithmic_bytes(cfg, batch):
     return inp + y, inp + y + inp
 
 
-# DRAM bytes (read + write) per launch measured by ncu on a B=2 instance of the
-# same configuration (profiles/ssd_chunk_c4.md, profiles/gla_chunk_c5.md), per
-# batch row: the kernels' traffic grows linearly with the (batch, head) units.
+# DRAM bytes (read + write) per launch measured by ncu, per batch row: the
+# kernels' traffic grows linearly with the independent units. Chunk kernels
+# (c4, c5) from a B=2 instance of the same configuration, diagonal scans (c2,
+# c3) from the full configuration.
 _NCU_TRAFFIC_PER_BATCH_ROW = {
-    ("c4", "backward"): (1.214505e9 + 0.630143e9) / 2,
-    ("c4", "forward"): (0.674436e9 + 0.495007e9) / 2,
-    ("c5", "backward"): (0.810017e9 + 0.364701e9) / 2,
-    ("c5", "forward"): (0.407027e9 + 0.358031e9) / 2,
+    ("c4", "backward"): (1.208137e9 + 0.629970e9) / 2,
+    ("c4", "forward"): (0.677076e9 + 0.496836e9) / 2,
+    ("c5", "backward"): (0.806439e9 + 0.363859e9) / 2,
+    ("c5", "forward"): (0.407030e9 + 0.357562e9) / 2,
+    ("c2", "backward"): (674.370e6 + 309.851e6) / 8,
+    ("c2", "forward"): (336.269e6 + 298.693e6) / 8,
+    ("c3", "backward"): (2.516725e9 + 1.315607e9) / 16,
+    ("c3", "forward"): (1.342216e9 + 1.059618e9) / 16,
 }
 
 
