@@ -201,6 +201,50 @@ MR_API int mr_rotlru_bwd(const float* grad_y, const float* grad_final, const flo
                   void* grad_a, void* grad_cs, void* grad_sn, void* grad_x,
                   void* workspace, size_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------------ initial state ---
+ * No counterpart in the reference, which starts every scan from a zero state
+ * and cannot resume from a returned final state (ssd.py:365-375). These
+ * variants take the same arguments as the entry points above plus
+ *   h0       the initial state, float32, in the final state's layout
+ *            ([B,H,Dh,N] SSD, [B,H,Dh,Dh] GLA, [B,D] RG-LRU, [B,2Dp] rotLRU),
+ *            or NULL for zero; forward and backward must get the same h0;
+ *   grad_h0  (backward) the gradient of the loss w.r.t. h0, float32, same
+ *            layout, or NULL when not wanted.
+ * Passing the final state of one call as h0 of the next continues the scan
+ * (chunked prefill). The plain entry points equal these with NULLs. */
+MR_API int mr_ssd_fwd_h0(const void* u, const void* delta, const void* Bm, const void* Cm, const float* A_neg,
+                         int64_t a_stride_h, int64_t a_stride_n, int dtype, int64_t batch, int64_t L, int64_t H,
+                         int64_t Dh, int64_t N, int64_t seg, float* y, float* h_ckpt, const float* h0,
+                         void* stream);
+MR_API int mr_ssd_bwd_h0(const float* grad_y, const float* grad_final, const float* h_ckpt, const void* u,
+                         const void* delta, const void* Bm, const void* Cm, const float* A_neg,
+                         int64_t a_stride_h, int64_t a_stride_n, int dtype, int64_t batch, int64_t L, int64_t H,
+                         int64_t Dh, int64_t N, int64_t seg, void* grad_u, void* grad_delta, void* grad_B,
+                         void* grad_C, float* grad_A, void* workspace, size_t workspace_bytes, const float* h0,
+                         float* grad_h0, void* stream);
+MR_API int mr_gla_fwd_h0(const void* q, const void* k, const void* v, const void* gates, int dtype,
+                         int64_t batch, int64_t L, int64_t H, int64_t Dh, int64_t seg, float* y, float* h_ckpt,
+                         const float* h0, void* stream);
+MR_API int mr_gla_bwd_h0(const float* grad_y, const float* grad_final, const float* h_ckpt, const void* q,
+                         const void* k, const void* v, const void* gates, int dtype, int64_t batch, int64_t L,
+                         int64_t H, int64_t Dh, int64_t seg, void* grad_q, void* grad_k, void* grad_v,
+                         void* grad_gates, void* workspace, size_t workspace_bytes, const float* h0,
+                         float* grad_h0, void* stream);
+MR_API int mr_rglru_fwd_h0(const void* a, const void* x, int dtype, int64_t batch, int64_t L, int64_t D,
+                           int64_t seg, float* y, float* h_ckpt, const float* h0, void* stream);
+MR_API int mr_rglru_bwd_h0(const float* grad_y, const float* grad_final, const float* h_ckpt, const void* a,
+                           const void* x, int dtype, int64_t batch, int64_t L, int64_t D, int64_t seg,
+                           void* grad_a, void* grad_x, void* workspace, size_t workspace_bytes,
+                           const float* h0, float* grad_h0, void* stream);
+MR_API int mr_rotlru_fwd_h0(const void* a, const void* cs, const void* sn, const void* x, int dtype,
+                            int64_t batch, int64_t L, int64_t Dp, int64_t seg, float* y, float* h_ckpt,
+                            const float* h0, void* stream);
+MR_API int mr_rotlru_bwd_h0(const float* grad_y, const float* grad_final, const float* h_ckpt, const void* a,
+                            const void* cs, const void* sn, const void* x, int dtype, int64_t batch, int64_t L,
+                            int64_t Dp, int64_t seg, void* grad_a, void* grad_cs, void* grad_sn, void* grad_x,
+                            void* workspace, size_t workspace_bytes, const float* h0, float* grad_h0,
+                            void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -68,6 +68,21 @@ def prep(t, dtype):
     return t.contiguous()
 
 
+def prep_h0(h0, shape, device):
+    """Initial state as float32 contiguous on ``device`` (None stays None).
+
+    ``shape`` is the final state's shape: a returned final state can be passed
+    back as ``h0`` to continue a scan (no counterpart in the reference, which
+    always starts from zero, ``ssd.py:365-375``)."""
+    if h0 is None:
+        return None
+    if tuple(h0.shape) != tuple(shape):
+        raise ValueError(f"h0 must have the final state's shape {tuple(shape)}, got {tuple(h0.shape)}")
+    if h0.device != device:
+        raise ValueError(f"h0 must be on {device}, got {h0.device}")
+    return h0.to(torch.float32).contiguous()
+
+
 def grad_out(g, shape, device):
     """fp32 contiguous cotangent (zeros when autograd passes None)."""
     if g is None:

@@ -60,6 +60,20 @@ SIGNATURES = {
     "mr_rotlru_bwd_workspace_bytes": (_sz, [_int, _i64, _i64, _i64, _i64]),
     "mr_rotlru_bwd": (_int, [_p, _p, _p, _p, _p, _p, _p, _int, _i64, _i64, _i64, _i64, _p, _p, _p, _p,
                              _p, _sz, _p]),
+    # initial-state variants: (h0) before the stream (forward), (h0, grad_h0) backward
+    "mr_ssd_fwd_h0": (_int, [_p, _p, _p, _p, _p, _i64, _i64, _int, _i64, _i64, _i64, _i64, _i64, _i64,
+                             _p, _p, _p, _p]),
+    "mr_ssd_bwd_h0": (_int, [_p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _int, _i64, _i64, _i64, _i64,
+                             _i64, _i64, _p, _p, _p, _p, _p, _p, _sz, _p, _p, _p]),
+    "mr_gla_fwd_h0": (_int, [_p, _p, _p, _p, _int, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _p]),
+    "mr_gla_bwd_h0": (_int, [_p, _p, _p, _p, _p, _p, _p, _int, _i64, _i64, _i64, _i64, _i64, _p, _p, _p,
+                             _p, _p, _sz, _p, _p, _p]),
+    "mr_rglru_fwd_h0": (_int, [_p, _p, _int, _i64, _i64, _i64, _i64, _p, _p, _p, _p]),
+    "mr_rglru_bwd_h0": (_int, [_p, _p, _p, _p, _p, _int, _i64, _i64, _i64, _i64, _p, _p, _p, _sz, _p, _p,
+                               _p]),
+    "mr_rotlru_fwd_h0": (_int, [_p, _p, _p, _p, _int, _i64, _i64, _i64, _i64, _p, _p, _p, _p]),
+    "mr_rotlru_bwd_h0": (_int, [_p, _p, _p, _p, _p, _p, _p, _int, _i64, _i64, _i64, _i64, _p, _p, _p, _p,
+                                _p, _sz, _p, _p, _p]),
 }
 
 _lib = None

@@ -84,10 +84,11 @@ struct RgFwdSmem {
   static constexpr size_t bytes = (size_t)2 * S * TB * W * sizeof(T) + 2 * 2 * kWarps * W * 4 + S * 8;
 };
 
-template <typename T, int W, int TB, int S>
+template <typename T, int W, int TB, int S, bool kH0>
 __global__ void __launch_bounds__(kThreads, 3)
 rglru_fwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_x,
-                 int L, int64_t D, int seg, float* __restrict__ y, float* __restrict__ ckpt) {
+                 int L, int64_t D, int seg, float* __restrict__ y, float* __restrict__ ckpt,
+                 const float* __restrict__ h0) {
   constexpr int V = W / 32, TW = TB / kWarps;
   extern __shared__ __align__(128) unsigned char smem[];
   T* sa = reinterpret_cast<T*>(smem);
@@ -121,9 +122,9 @@ rglru_fwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
   if (threadIdx.x == 0)
     for (int k = 0; k < S - 1 && k < nblk; ++k) issue(k);
 
-  float carry[V];
+  float carry[V];  // the state before the block: h0 [B, D] or zero
 #pragma unroll
-  for (int v = 0; v < V; ++v) carry[v] = 0.f;
+  for (int v = 0; v < V; ++v) carry[v] = (kH0 && act) ? h0[b * D + c0 + cl + v] : 0.f;
 
   for (int blk = 0; blk < nblk; ++blk) {
     const int s = blk % S;
@@ -213,13 +214,13 @@ struct RgBwdSmem {
       (size_t)S * TB * W * (2 * sizeof(T) + 4) + 4 * 2 * kWarps * W * 4 + S * 8;
 };
 
-template <typename T, int W, int TB, int S>
+template <typename T, int W, int TB, int S, bool kH0>
 __global__ void __launch_bounds__(kThreads, 3)
 rglru_bwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_x,
                  const __grid_constant__ CUtensorMap tm_g, const float* __restrict__ gfinal,
                  const float* __restrict__ ckpt, const T* __restrict__ a, const T* __restrict__ x,
                  int L, int64_t D, int seg, T* __restrict__ ga, T* __restrict__ gx,
-                 float* __restrict__ ws) {
+                 float* __restrict__ ws, const float* __restrict__ h0, float* __restrict__ gh0) {
   constexpr int V = W / 32, TW = TB / kWarps;
   extern __shared__ __align__(128) unsigned char smem[];
   T* sa = reinterpret_cast<T*>(smem);
@@ -279,7 +280,8 @@ rglru_bwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
       float cur[V];
 #pragma unroll
       for (int v = 0; v < V; ++v)
-        cur[v] = (sidx > 0 && act) ? ckpt[(b * nseg + sidx - 1) * D + c0 + cl + v] : 0.f;
+        cur[v] = !act ? 0.f : sidx > 0 ? ckpt[(b * nseg + sidx - 1) * D + c0 + cl + v]
+                 : kH0 ? h0[b * D + c0 + cl + v] : 0.f;
       for (int jj = 0; jj + 1 < bm.nsub; ++jj, ++it) {
         const int buf = it & 1;
         const int t0 = s0 + jj * TB + warp * TW;
@@ -341,7 +343,8 @@ rglru_bwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
       if (j > 0)
         hs[v] = act ? wsb[(int64_t)j * W + v] : 0.f;
       else
-        hs[v] = (tb0 > 0 && act) ? ckpt[(b * nseg + tb0 / seg - 1) * D + c0 + cl + v] : 0.f;
+        hs[v] = !act ? 0.f : tb0 > 0 ? ckpt[(b * nseg + tb0 / seg - 1) * D + c0 + cl + v]
+                : kH0 ? h0[b * D + c0 + cl + v] : 0.f;
     }
 
 #pragma unroll
@@ -410,6 +413,10 @@ rglru_bwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
       }
     }
   }
+  // the reverse carry past step 0 is the gradient of the initial state
+  if (kH0 && gh0 != nullptr && act)
+#pragma unroll
+    for (int v = 0; v < V; ++v) gh0[b * D + c0 + cl + v] = cr[v];
 }
 
 // ============================================================================
@@ -421,11 +428,12 @@ struct RotFwdSmem {
   static constexpr size_t bytes = (size_t)S * TB * W * 5 * sizeof(T) + 2 * 2 * kWarps * W * 8 + S * 8;
 };
 
-template <typename T, int W, int TB, int S>
+template <typename T, int W, int TB, int S, bool kH0>
 __global__ void __launch_bounds__(kThreads, 2)
 rotlru_fwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_c,
                   const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_x,
-                  int L, int64_t Dp, int seg, float* __restrict__ y, float* __restrict__ ckpt) {
+                  int L, int64_t Dp, int seg, float* __restrict__ y, float* __restrict__ ckpt,
+                  const float* __restrict__ h0) {
   constexpr int V = W / 32, TW = TB / kWarps;
   extern __shared__ __align__(128) unsigned char smem[];
   T* sa = reinterpret_cast<T*>(smem);
@@ -464,9 +472,11 @@ rotlru_fwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
   if (threadIdx.x == 0)
     for (int k = 0; k < S - 1 && k < nblk; ++k) issue(k);
 
-  cf carry[V];
+  cf carry[V];  // the state before the block: h0 [B, 2Dp] (pairs) or zero
 #pragma unroll
-  for (int v = 0; v < V; ++v) carry[v] = {0.f, 0.f};
+  for (int v = 0; v < V; ++v)
+    carry[v] = (kH0 && act) ? cf{h0[b * D + 2 * (p0 + pl + v)], h0[b * D + 2 * (p0 + pl + v) + 1]}
+                            : cf{0.f, 0.f};
 
   for (int blk = 0; blk < nblk; ++blk) {
     const int s = blk % S;
@@ -563,7 +573,7 @@ struct RotBwdSmem {
       (size_t)S * TB * W * (5 * sizeof(T) + 8) + 4 * 2 * kWarps * W * 8 + S * 8;
 };
 
-template <typename T, int W, int TB, int S>
+template <typename T, int W, int TB, int S, bool kH0>
 __global__ void __launch_bounds__(kThreads, 2)
 rotlru_bwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_c,
                   const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_x,
@@ -571,7 +581,7 @@ rotlru_bwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
                   const float* __restrict__ ckpt, const T* __restrict__ a, const T* __restrict__ cs,
                   const T* __restrict__ sn, const T* __restrict__ x, int L, int64_t Dp, int seg,
                   T* __restrict__ ga, T* __restrict__ gcs, T* __restrict__ gsn, T* __restrict__ gx,
-                  float* __restrict__ ws) {
+                  float* __restrict__ ws, const float* __restrict__ h0, float* __restrict__ gh0) {
   constexpr int V = W / 32, TW = TB / kWarps;
   extern __shared__ __align__(128) unsigned char smem[];
   T* sa = reinterpret_cast<T*>(smem);
@@ -638,12 +648,9 @@ rotlru_bwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
       cf cur[V];
 #pragma unroll
       for (int v = 0; v < V; ++v) {
-        if (sidx > 0 && act) {
-          const float* ck = ckpt + (b * nseg + sidx - 1) * D + 2 * (p0 + pl + v);
-          cur[v] = {ck[0], ck[1]};
-        } else {
-          cur[v] = {0.f, 0.f};
-        }
+        const float* ck = sidx > 0 ? ckpt + (b * nseg + sidx - 1) * D + 2 * (p0 + pl + v)
+                          : kH0 ? h0 + b * D + 2 * (p0 + pl + v) : nullptr;
+        cur[v] = (act && ck != nullptr) ? cf{ck[0], ck[1]} : cf{0.f, 0.f};
       }
       for (int jj = 0; jj + 1 < bm.nsub; ++jj, ++it) {
         const int buf = it & 1;
@@ -714,11 +721,10 @@ rotlru_bwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
     for (int v = 0; v < V; ++v) {
       if (j > 0) {
         hs[v] = act ? cf{wsb[(int64_t)j * 2 * W + 2 * v], wsb[(int64_t)j * 2 * W + 2 * v + 1]} : cf{0.f, 0.f};
-      } else if (tb0 > 0 && act) {
-        const float* ck = ckpt + (b * nseg + tb0 / seg - 1) * D + 2 * (p0 + pl + v);
-        hs[v] = {ck[0], ck[1]};
       } else {
-        hs[v] = {0.f, 0.f};
+        const float* ck = tb0 > 0 ? ckpt + (b * nseg + tb0 / seg - 1) * D + 2 * (p0 + pl + v)
+                          : kH0 ? h0 + b * D + 2 * (p0 + pl + v) : nullptr;
+        hs[v] = (act && ck != nullptr) ? cf{ck[0], ck[1]} : cf{0.f, 0.f};
       }
     }
 
@@ -801,6 +807,13 @@ rotlru_bwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
       }
     }
   }
+  // the reverse carry past step 0 is the gradient of the initial state
+  if (kH0 && gh0 != nullptr && act)
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      gh0[b * D + 2 * (p0 + pl + v)] = cr[v].r;
+      gh0[b * D + 2 * (p0 + pl + v) + 1] = cr[v].i;
+    }
 }
 
 // ============================================================================
@@ -850,24 +863,25 @@ static int tmap_rows(CUtensorMap* m, const void* base, int64_t rows, int64_t col
 
 template <typename T>
 int rglru_fwd_launch(const void* a, const void* x, int64_t batch, int64_t L, int64_t D, int64_t seg,
-                     float* y, float* ckpt, cudaStream_t st) {
+                     float* y, float* ckpt, const float* h0, cudaStream_t st) {
   using C = DiagCfg<T>;
   constexpr int W = C::RgFW, TB = C::RgFTB, S = C::RgFS;
   constexpr size_t sm = RgFwdSmem<T, W, TB, S>::bytes;
   CUtensorMap ma, mx;
   if (int rc = tmap_rows<T>(&ma, a, batch * L, D, W, TB)) return rc;
   if (int rc = tmap_rows<T>(&mx, x, batch * L, D, W, TB)) return rc;
-  auto k = rglru_fwd_kernel<T, W, TB, S>;
+  // an initial state selects its own instantiation (the common case's code stays as it was)
+  auto k = h0 != nullptr ? rglru_fwd_kernel<T, W, TB, S, true> : rglru_fwd_kernel<T, W, TB, S, false>;
   if (int rc = set_smem(k, sm)) return rc;
   dim3 grid((unsigned)((D + W - 1) / W), (unsigned)batch);
-  k<<<grid, kThreads, sm, st>>>(ma, mx, (int)L, D, (int)seg, y, ckpt);
+  k<<<grid, kThreads, sm, st>>>(ma, mx, (int)L, D, (int)seg, y, ckpt, h0);
   return check_launch("rglru_fwd_kernel");
 }
 
 template <typename T>
 int rglru_bwd_launch(const float* gy, const float* gf, const float* ckpt, const void* a, const void* x,
                      int64_t batch, int64_t L, int64_t D, int64_t seg, void* ga, void* gx, float* ws,
-                     cudaStream_t st) {
+                     const float* h0, float* gh0, cudaStream_t st) {
   using C = DiagCfg<T>;
   constexpr int W = C::RgBW, TB = C::RgBTB, S = C::RgBS;
   constexpr size_t sm = RgBwdSmem<T, W, TB, S>::bytes;
@@ -875,17 +889,18 @@ int rglru_bwd_launch(const float* gy, const float* gf, const float* ckpt, const 
   if (int rc = tmap_rows<T>(&ma, a, batch * L, D, W, TB)) return rc;
   if (int rc = tmap_rows<T>(&mx, x, batch * L, D, W, TB)) return rc;
   if (int rc = tmap_rows<float>(&mg, gy, batch * L, D, W, TB)) return rc;
-  auto k = rglru_bwd_kernel<T, W, TB, S>;
+  auto k = h0 != nullptr ? rglru_bwd_kernel<T, W, TB, S, true> : rglru_bwd_kernel<T, W, TB, S, false>;
   if (int rc = set_smem(k, sm)) return rc;
   dim3 grid((unsigned)((D + W - 1) / W), (unsigned)batch);
   k<<<grid, kThreads, sm, st>>>(ma, mx, mg, gf, ckpt, (const T*)a, (const T*)x, (int)L, D, (int)seg,
-                                (T*)ga, (T*)gx, ws);
+                                (T*)ga, (T*)gx, ws, h0, gh0);
   return check_launch("rglru_bwd_kernel");
 }
 
 template <typename T>
 int rotlru_fwd_launch(const void* a, const void* cs, const void* sn, const void* x, int64_t batch,
-                      int64_t L, int64_t Dp, int64_t seg, float* y, float* ckpt, cudaStream_t st) {
+                      int64_t L, int64_t Dp, int64_t seg, float* y, float* ckpt, const float* h0,
+                      cudaStream_t st) {
   using C = DiagCfg<T>;
   constexpr int W = C::RotFW, TB = C::RotFTB, S = C::RotFS;
   constexpr size_t sm = RotFwdSmem<T, W, TB, S>::bytes;
@@ -894,10 +909,10 @@ int rotlru_fwd_launch(const void* a, const void* cs, const void* sn, const void*
   if (int rc = tmap_rows<T>(&mc, cs, batch * L, Dp, W, TB)) return rc;
   if (int rc = tmap_rows<T>(&ms, sn, batch * L, Dp, W, TB)) return rc;
   if (int rc = tmap_rows<T>(&mx, x, batch * L, 2 * Dp, 2 * W, TB)) return rc;
-  auto k = rotlru_fwd_kernel<T, W, TB, S>;
+  auto k = h0 != nullptr ? rotlru_fwd_kernel<T, W, TB, S, true> : rotlru_fwd_kernel<T, W, TB, S, false>;
   if (int rc = set_smem(k, sm)) return rc;
   dim3 grid((unsigned)((Dp + W - 1) / W), (unsigned)batch);
-  k<<<grid, kThreads, sm, st>>>(ma, mc, ms, mx, (int)L, Dp, (int)seg, y, ckpt);
+  k<<<grid, kThreads, sm, st>>>(ma, mc, ms, mx, (int)L, Dp, (int)seg, y, ckpt, h0);
   return check_launch("rotlru_fwd_kernel");
 }
 
@@ -905,7 +920,7 @@ template <typename T>
 int rotlru_bwd_launch(const float* gy, const float* gf, const float* ckpt, const void* a,
                       const void* cs, const void* sn, const void* x, int64_t batch, int64_t L,
                       int64_t Dp, int64_t seg, void* ga, void* gcs, void* gsn, void* gx, float* ws,
-                      cudaStream_t st) {
+                      const float* h0, float* gh0, cudaStream_t st) {
   using C = DiagCfg<T>;
   constexpr int W = C::RotBW, TB = C::RotBTB, S = C::RotBS;
   constexpr size_t sm = RotBwdSmem<T, W, TB, S>::bytes;
@@ -915,26 +930,28 @@ int rotlru_bwd_launch(const float* gy, const float* gf, const float* ckpt, const
   if (int rc = tmap_rows<T>(&ms, sn, batch * L, Dp, W, TB)) return rc;
   if (int rc = tmap_rows<T>(&mx, x, batch * L, 2 * Dp, 2 * W, TB)) return rc;
   if (int rc = tmap_rows<float>(&mg, gy, batch * L, 2 * Dp, 2 * W, TB)) return rc;
-  auto k = rotlru_bwd_kernel<T, W, TB, S>;
+  auto k = h0 != nullptr ? rotlru_bwd_kernel<T, W, TB, S, true> : rotlru_bwd_kernel<T, W, TB, S, false>;
   if (int rc = set_smem(k, sm)) return rc;
   dim3 grid((unsigned)((Dp + W - 1) / W), (unsigned)batch);
   k<<<grid, kThreads, sm, st>>>(ma, mc, ms, mx, mg, gf, ckpt, (const T*)a, (const T*)cs, (const T*)sn,
-                                (const T*)x, (int)L, Dp, (int)seg, (T*)ga, (T*)gcs, (T*)gsn, (T*)gx, ws);
+                                (const T*)x, (int)L, Dp, (int)seg, (T*)ga, (T*)gcs, (T*)gsn, (T*)gx, ws, h0,
+                                gh0);
   return check_launch("rotlru_bwd_kernel");
 }
 
 #define MR_INST(T)                                                                                  \
   template int rglru_fwd_launch<T>(const void*, const void*, int64_t, int64_t, int64_t, int64_t,    \
-                                   float*, float*, cudaStream_t);                                  \
+                                   float*, float*, const float*, cudaStream_t);                    \
   template int rglru_bwd_launch<T>(const float*, const float*, const float*, const void*,          \
                                    const void*, int64_t, int64_t, int64_t, int64_t, void*, void*,  \
-                                   float*, cudaStream_t);                                          \
+                                   float*, const float*, float*, cudaStream_t);                    \
   template int rotlru_fwd_launch<T>(const void*, const void*, const void*, const void*, int64_t,   \
-                                    int64_t, int64_t, int64_t, float*, float*, cudaStream_t);      \
+                                    int64_t, int64_t, int64_t, float*, float*, const float*,       \
+                                    cudaStream_t);                                                 \
   template int rotlru_bwd_launch<T>(const float*, const float*, const float*, const void*,         \
                                     const void*, const void*, const void*, int64_t, int64_t,       \
                                     int64_t, int64_t, void*, void*, void*, void*, float*,          \
-                                    cudaStream_t);
+                                    const float*, float*, cudaStream_t);
 MR_INST(float)
 MR_INST(__nv_bfloat16)
 MR_INST(__half)

@@ -31,16 +31,17 @@ int check_launch(const char* what) {
 }
 
 // ---- launchers defined in the kernel translation units ----------------------
-template <typename T> int rglru_fwd_launch(const void*, const void*, int64_t, int64_t, int64_t, int64_t, float*, float*, cudaStream_t);
-template <typename T> int rglru_bwd_launch(const float*, const float*, const float*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, void*, void*, float*, cudaStream_t);
-template <typename T> int rotlru_fwd_launch(const void*, const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, float*, float*, cudaStream_t);
-template <typename T> int rotlru_bwd_launch(const float*, const float*, const float*, const void*, const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, void*, void*, void*, void*, float*, cudaStream_t);
-template <typename T> int ssd_seq_fwd_launch(const void*, const void*, const void*, const void*, const float*, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, float*, float*, cudaStream_t);
-template <typename T> int ssd_seq_bwd_launch(const float*, const float*, const float*, const void*, const void*, const void*, const void*, const float*, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, void*, void*, void*, void*, float*, void*, cudaStream_t);
-template <typename T> int gla_seq_fwd_launch(const void*, const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, int64_t, float*, float*, cudaStream_t, int);
-template <typename T> int gla_seq_bwd_launch(const float*, const float*, const float*, const void*, const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, int64_t, void*, void*, void*, void*, void*, cudaStream_t, int);
-template <typename T> int gla_chunk_fwd_launch(const void*, const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, float*, float*, cudaStream_t);
-template <typename T> int gla_chunk_bwd_launch(const float*, const float*, const float*, const void*, const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, void*, void*, void*, void*, cudaStream_t);
+// (h0: initial state or NULL; gh0: its gradient or NULL; both in the final state's layout)
+template <typename T> int rglru_fwd_launch(const void*, const void*, int64_t, int64_t, int64_t, int64_t, float*, float*, const float*, cudaStream_t);
+template <typename T> int rglru_bwd_launch(const float*, const float*, const float*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, void*, void*, float*, const float*, float*, cudaStream_t);
+template <typename T> int rotlru_fwd_launch(const void*, const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, float*, float*, const float*, cudaStream_t);
+template <typename T> int rotlru_bwd_launch(const float*, const float*, const float*, const void*, const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, void*, void*, void*, void*, float*, const float*, float*, cudaStream_t);
+template <typename T> int ssd_seq_fwd_launch(const void*, const void*, const void*, const void*, const float*, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, float*, float*, const float*, cudaStream_t);
+template <typename T> int ssd_seq_bwd_launch(const float*, const float*, const float*, const void*, const void*, const void*, const void*, const float*, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, void*, void*, void*, void*, float*, void*, const float*, float*, cudaStream_t);
+template <typename T> int gla_seq_fwd_launch(const void*, const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, int64_t, float*, float*, const float*, cudaStream_t, int);
+template <typename T> int gla_seq_bwd_launch(const float*, const float*, const float*, const void*, const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, int64_t, void*, void*, void*, void*, void*, const float*, float*, cudaStream_t, int);
+template <typename T> int gla_chunk_fwd_launch(const void*, const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, float*, float*, const float*, cudaStream_t);
+template <typename T> int gla_chunk_bwd_launch(const float*, const float*, const float*, const void*, const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, void*, void*, void*, void*, const float*, float*, cudaStream_t);
 bool gla_chunk_supported(int dtype, int64_t L, int64_t Dh, int64_t seg);
 size_t gla_fallback_ws_bytes(int64_t, int64_t, int64_t, int64_t, int64_t);
 size_t rglru_bwd_ws_bytes(int64_t, int64_t, int64_t, int64_t);
@@ -59,8 +60,8 @@ size_t ssd_chunk_bwd_ws_bytes(int64_t batch, int64_t H);
 int ssd_chunk_bwd_noalloc(int dtype, const float*, const float*, const float*, const void*, const void*,
                           const void*, const void*, const float*, int64_t, int64_t, int64_t, int64_t, int64_t,
                           void*, void*, void*, void*, float*, cudaStream_t);
-template <typename T> int ssd_chunk_bwd_launch(const float*, const float*, const float*, const void*, const void*, const void*, const void*, const float*, int64_t, int64_t, int64_t, int64_t, int64_t, void*, void*, void*, void*, float*, float*, cudaStream_t);
-template <typename T> int ssd_chunk_fwd_launch(const void*, const void*, const void*, const void*, const float*, int64_t, int64_t, int64_t, int64_t, int64_t, float*, float*, cudaStream_t);
+template <typename T> int ssd_chunk_bwd_launch(const float*, const float*, const float*, const void*, const void*, const void*, const void*, const float*, int64_t, int64_t, int64_t, int64_t, int64_t, void*, void*, void*, void*, float*, float*, const float*, float*, cudaStream_t);
+template <typename T> int ssd_chunk_fwd_launch(const void*, const void*, const void*, const void*, const float*, int64_t, int64_t, int64_t, int64_t, int64_t, float*, float*, const float*, cudaStream_t);
 int umma_selftest_launch(const void*, const void*, const void*, const void*, float*, float*, float*,
                          cudaStream_t);
 
@@ -131,7 +132,7 @@ using namespace mr;
 
 extern "C" {
 
-int mr_abi_version(void) { return 1; }
+int mr_abi_version(void) { return 2; }  // 2: the _h0 (initial state) entry points
 
 const char* mr_last_error(void) { return g_err; }
 
@@ -163,13 +164,19 @@ int mr_check_segment_shape(int64_t L, int64_t seg, int64_t lane_dim, const char*
 // ------------------------------------------------------------------ RG-LRU ---
 int mr_rglru_fwd(const void* a, const void* x, int dtype, int64_t batch, int64_t L, int64_t D,
                  int64_t seg, float* y, float* h_ckpt, void* stream) {
+  return mr_rglru_fwd_h0(a, x, dtype, batch, L, D, seg, y, h_ckpt, nullptr, stream);
+}
+
+int mr_rglru_fwd_h0(const void* a, const void* x, int dtype, int64_t batch, int64_t L, int64_t D,
+                    int64_t seg, float* y, float* h_ckpt, const float* h0, void* stream) {
   g_err[0] = 0;
   MR_TRY(check_dims("mr_rglru_fwd", batch, L, D));
   MR_TRY(check_seg(L, seg, D, "D"));
   MR_TRY(check_dtype(dtype));
   MR_TRY(check_ptrs("mr_rglru_fwd", {a, x, y, h_ckpt}));
   cudaStream_t st = (cudaStream_t)stream;
-  MR_DTYPE_SWITCH(dtype, rglru_fwd_launch<T>(a, x, batch, L, D, seg, y, h_ckpt, st));
+  MR_TRY(check_opt_ptr("mr_rglru_fwd", h0));
+  MR_DTYPE_SWITCH(dtype, rglru_fwd_launch<T>(a, x, batch, L, D, seg, y, h_ckpt, h0, st));
 }
 
 size_t mr_rglru_bwd_workspace_bytes(int dtype, int64_t batch, int64_t L, int64_t D, int64_t seg) {
@@ -182,6 +189,14 @@ int mr_rglru_bwd(const float* grad_y, const float* grad_final, const float* h_ck
                     const void* a, const void* x, int dtype, int64_t batch, int64_t L, int64_t D,
                     int64_t seg, void* grad_a, void* grad_x, void* workspace,
                     size_t workspace_bytes, void* stream) {
+  return mr_rglru_bwd_h0(grad_y, grad_final, h_ckpt, a, x, dtype, batch, L, D, seg, grad_a, grad_x, workspace,
+                         workspace_bytes, nullptr, nullptr, stream);
+}
+
+int mr_rglru_bwd_h0(const float* grad_y, const float* grad_final, const float* h_ckpt, const void* a,
+                    const void* x, int dtype, int64_t batch, int64_t L, int64_t D, int64_t seg, void* grad_a,
+                    void* grad_x, void* workspace, size_t workspace_bytes, const float* h0, float* grad_h0,
+                    void* stream) {
   g_err[0] = 0;
   MR_TRY(check_dims("mr_rglru_bwd", batch, L, D));
   MR_TRY(check_seg(L, seg, D, "D"));
@@ -193,22 +208,31 @@ int mr_rglru_bwd(const float* grad_y, const float* grad_final, const float* h_ck
     return set_error(MR_E_WORKSPACE, "mr_rglru_bwd: workspace of %zu bytes required, got %zu",
                      need, workspace_bytes);
   MR_TRY(check_opt_ptr("mr_rglru_bwd", workspace));
+  MR_TRY(check_opt_ptr("mr_rglru_bwd", h0));
+  MR_TRY(check_opt_ptr("mr_rglru_bwd", grad_h0));
   cudaStream_t st = (cudaStream_t)stream;
   MR_DTYPE_SWITCH(dtype, rglru_bwd_launch<T>(grad_y, grad_final, h_ckpt, a, x, batch, L, D, seg,
-                                             grad_a, grad_x, (float*)workspace, st));
+                                             grad_a, grad_x, (float*)workspace, h0, grad_h0, st));
 }
 
 // ------------------------------------------------------------------ rotLRU ---
 int mr_rotlru_fwd(const void* a, const void* cs, const void* sn, const void* x, int dtype,
                   int64_t batch, int64_t L, int64_t Dp, int64_t seg, float* y, float* h_ckpt,
                   void* stream) {
+  return mr_rotlru_fwd_h0(a, cs, sn, x, dtype, batch, L, Dp, seg, y, h_ckpt, nullptr, stream);
+}
+
+int mr_rotlru_fwd_h0(const void* a, const void* cs, const void* sn, const void* x, int dtype, int64_t batch,
+                     int64_t L, int64_t Dp, int64_t seg, float* y, float* h_ckpt, const float* h0,
+                     void* stream) {
   g_err[0] = 0;
   MR_TRY(check_dims("mr_rotlru_fwd", batch, L, Dp));
   MR_TRY(check_seg(L, seg, 2 * Dp, "D"));
   MR_TRY(check_dtype(dtype));
   MR_TRY(check_ptrs("mr_rotlru_fwd", {a, cs, sn, x, y, h_ckpt}));
   cudaStream_t st = (cudaStream_t)stream;
-  MR_DTYPE_SWITCH(dtype, rotlru_fwd_launch<T>(a, cs, sn, x, batch, L, Dp, seg, y, h_ckpt, st));
+  MR_TRY(check_opt_ptr("mr_rotlru_fwd", h0));
+  MR_DTYPE_SWITCH(dtype, rotlru_fwd_launch<T>(a, cs, sn, x, batch, L, Dp, seg, y, h_ckpt, h0, st));
 }
 
 size_t mr_rotlru_bwd_workspace_bytes(int dtype, int64_t batch, int64_t L, int64_t Dp, int64_t seg) {
@@ -222,6 +246,15 @@ int mr_rotlru_bwd(const float* grad_y, const float* grad_final, const float* h_c
                      int64_t batch, int64_t L, int64_t Dp, int64_t seg, void* grad_a,
                      void* grad_cs, void* grad_sn, void* grad_x, void* workspace,
                      size_t workspace_bytes, void* stream) {
+  return mr_rotlru_bwd_h0(grad_y, grad_final, h_ckpt, a, cs, sn, x, dtype, batch, L, Dp, seg, grad_a, grad_cs,
+                          grad_sn, grad_x, workspace, workspace_bytes, nullptr, nullptr, stream);
+}
+
+int mr_rotlru_bwd_h0(const float* grad_y, const float* grad_final, const float* h_ckpt, const void* a,
+                     const void* cs, const void* sn, const void* x, int dtype, int64_t batch, int64_t L,
+                     int64_t Dp, int64_t seg, void* grad_a, void* grad_cs, void* grad_sn, void* grad_x,
+                     void* workspace, size_t workspace_bytes, const float* h0, float* grad_h0,
+                     void* stream) {
   g_err[0] = 0;
   MR_TRY(check_dims("mr_rotlru_bwd", batch, L, Dp));
   MR_TRY(check_seg(L, seg, 2 * Dp, "D"));
@@ -233,10 +266,12 @@ int mr_rotlru_bwd(const float* grad_y, const float* grad_final, const float* h_c
     return set_error(MR_E_WORKSPACE, "mr_rotlru_bwd: workspace of %zu bytes required, got %zu",
                      need, workspace_bytes);
   MR_TRY(check_opt_ptr("mr_rotlru_bwd", workspace));
+  MR_TRY(check_opt_ptr("mr_rotlru_bwd", h0));
+  MR_TRY(check_opt_ptr("mr_rotlru_bwd", grad_h0));
   cudaStream_t st = (cudaStream_t)stream;
   MR_DTYPE_SWITCH(dtype, rotlru_bwd_launch<T>(grad_y, grad_final, h_ckpt, a, cs, sn, x, batch, L,
                                               Dp, seg, grad_a, grad_cs, grad_sn, grad_x,
-                                              (float*)workspace, st));
+                                              (float*)workspace, h0, grad_h0, st));
 }
 
 // --------------------------------------------------------------------- SSD ---
@@ -257,19 +292,28 @@ int mr_ssd_fwd(const void* u, const void* delta, const void* Bm, const void* Cm,
                int64_t a_stride_h, int64_t a_stride_n, int dtype, int64_t batch, int64_t L,
                int64_t H, int64_t Dh, int64_t N, int64_t seg, float* y, float* h_ckpt,
                void* stream) {
+  return mr_ssd_fwd_h0(u, delta, Bm, Cm, A_neg, a_stride_h, a_stride_n, dtype, batch, L, H, Dh, N, seg, y, h_ckpt,
+                       nullptr, stream);
+}
+
+int mr_ssd_fwd_h0(const void* u, const void* delta, const void* Bm, const void* Cm, const float* A_neg,
+                  int64_t a_stride_h, int64_t a_stride_n, int dtype, int64_t batch, int64_t L, int64_t H,
+                  int64_t Dh, int64_t N, int64_t seg, float* y, float* h_ckpt, const float* h0, void* stream) {
   g_err[0] = 0;
   MR_TRY(ssd_common_checks("mr_ssd_fwd", dtype, batch, L, H, Dh, N, seg));
   MR_TRY(check_ptrs("mr_ssd_fwd", {u, delta, Bm, Cm, y, h_ckpt}));
   if (A_neg == nullptr) return set_error(MR_E_ALIGN, "mr_ssd_fwd: A_neg is NULL");
+  MR_TRY(check_opt_ptr("mr_ssd_fwd", h0));
   cudaStream_t st = (cudaStream_t)stream;
   if (ssd_chunk_supported(dtype, L, Dh, N, seg, a_stride_n)) {
     if (dtype == MR_BF16)
       return ssd_chunk_fwd_launch<__nv_bfloat16>(u, delta, Bm, Cm, A_neg, a_stride_h, batch, L, H, seg, y,
-                                                 h_ckpt, st);
-    return ssd_chunk_fwd_launch<__half>(u, delta, Bm, Cm, A_neg, a_stride_h, batch, L, H, seg, y, h_ckpt, st);
+                                                 h_ckpt, h0, st);
+    return ssd_chunk_fwd_launch<__half>(u, delta, Bm, Cm, A_neg, a_stride_h, batch, L, H, seg, y, h_ckpt, h0,
+                                        st);
   }
   MR_DTYPE_SWITCH(dtype, ssd_seq_fwd_launch<T>(u, delta, Bm, Cm, A_neg, a_stride_h, a_stride_n,
-                                               batch, L, H, Dh, N, seg, y, h_ckpt, st));
+                                               batch, L, H, Dh, N, seg, y, h_ckpt, h0, st));
 }
 
 size_t mr_ssd_bwd_workspace_bytes(int dtype, int64_t batch, int64_t L, int64_t H, int64_t Dh,
@@ -291,6 +335,16 @@ int mr_ssd_bwd(const float* grad_y, const float* grad_final, const float* h_ckpt
                int64_t H, int64_t Dh, int64_t N, int64_t seg, void* grad_u, void* grad_delta,
                void* grad_B, void* grad_C, float* grad_A, void* workspace,
                size_t workspace_bytes, void* stream) {
+  return mr_ssd_bwd_h0(grad_y, grad_final, h_ckpt, u, delta, Bm, Cm, A_neg, a_stride_h, a_stride_n, dtype, batch,
+                       L, H, Dh, N, seg, grad_u, grad_delta, grad_B, grad_C, grad_A, workspace, workspace_bytes,
+                       nullptr, nullptr, stream);
+}
+
+int mr_ssd_bwd_h0(const float* grad_y, const float* grad_final, const float* h_ckpt, const void* u,
+                  const void* delta, const void* Bm, const void* Cm, const float* A_neg, int64_t a_stride_h,
+                  int64_t a_stride_n, int dtype, int64_t batch, int64_t L, int64_t H, int64_t Dh, int64_t N,
+                  int64_t seg, void* grad_u, void* grad_delta, void* grad_B, void* grad_C, float* grad_A,
+                  void* workspace, size_t workspace_bytes, const float* h0, float* grad_h0, void* stream) {
   g_err[0] = 0;
   MR_TRY(ssd_common_checks("mr_ssd_bwd", dtype, batch, L, H, Dh, N, seg));
   MR_TRY(check_ptrs("mr_ssd_bwd", {grad_y, h_ckpt, u, delta, Bm, Cm, grad_u, grad_delta, grad_B, grad_C}));
@@ -303,19 +357,22 @@ int mr_ssd_bwd(const float* grad_y, const float* grad_final, const float* h_ckpt
     return set_error(MR_E_WORKSPACE, "mr_ssd_bwd: workspace of %zu bytes required, got %zu", need,
                      workspace_bytes);
   MR_TRY(check_opt_ptr("mr_ssd_bwd", workspace));
+  MR_TRY(check_opt_ptr("mr_ssd_bwd", h0));
+  MR_TRY(check_opt_ptr("mr_ssd_bwd", grad_h0));
   cudaStream_t st = (cudaStream_t)stream;
   if (chunk) {
     if (dtype == MR_BF16)
       return ssd_chunk_bwd_launch<__nv_bfloat16>(grad_y, grad_final, h_ckpt, u, delta, Bm, Cm, A_neg, a_stride_h,
                                                  batch, L, H, seg, grad_u, grad_delta, grad_B, grad_C, grad_A,
-                                                 (float*)workspace, st);
+                                                 (float*)workspace, h0, grad_h0, st);
     return ssd_chunk_bwd_launch<__half>(grad_y, grad_final, h_ckpt, u, delta, Bm, Cm, A_neg, a_stride_h, batch, L,
-                                        H, seg, grad_u, grad_delta, grad_B, grad_C, grad_A, (float*)workspace, st);
+                                        H, seg, grad_u, grad_delta, grad_B, grad_C, grad_A, (float*)workspace, h0,
+                                        grad_h0, st);
   }
   MR_DTYPE_SWITCH(dtype, ssd_seq_bwd_launch<T>(grad_y, grad_final, h_ckpt, u, delta, Bm, Cm, A_neg,
                                                a_stride_h, a_stride_n, batch, L, H, Dh, N, seg,
                                                grad_u, grad_delta, grad_B, grad_C, grad_A,
-                                               workspace, st));
+                                               workspace, h0, grad_h0, st));
 }
 
 int mr_ssd_bwd_noalloc(const float* grad_y, const float* grad_final, const float* h_ckpt, const void* u,
@@ -354,21 +411,28 @@ static int gla_common_checks(const char* what, int dtype, int64_t batch, int64_t
 int mr_gla_fwd(const void* q, const void* k, const void* v, const void* gates, int dtype,
                int64_t batch, int64_t L, int64_t H, int64_t Dh, int64_t seg, float* y,
                float* h_ckpt, void* stream) {
+  return mr_gla_fwd_h0(q, k, v, gates, dtype, batch, L, H, Dh, seg, y, h_ckpt, nullptr, stream);
+}
+
+int mr_gla_fwd_h0(const void* q, const void* k, const void* v, const void* gates, int dtype, int64_t batch,
+                  int64_t L, int64_t H, int64_t Dh, int64_t seg, float* y, float* h_ckpt, const float* h0,
+                  void* stream) {
   g_err[0] = 0;
   MR_TRY(gla_common_checks("mr_gla_fwd", dtype, batch, L, H, Dh, seg));
   MR_TRY(check_ptrs("mr_gla_fwd", {q, k, v, gates, y, h_ckpt}));
+  MR_TRY(check_opt_ptr("mr_gla_fwd", h0));
   cudaStream_t st = (cudaStream_t)stream;
   if (gla_chunk_supported(dtype, L, Dh, seg)) {
     // tensor-core chunks for every unit, then the per-step kernel redoes the
     // units with a gate outside [1e-3, 1]
     if (dtype == MR_BF16) {
-      MR_TRY(gla_chunk_fwd_launch<__nv_bfloat16>(q, k, v, gates, batch, L, H, seg, y, h_ckpt, st));
-      return gla_seq_fwd_launch<__nv_bfloat16>(q, k, v, gates, batch, L, H, Dh, seg, y, h_ckpt, st, 1);
+      MR_TRY(gla_chunk_fwd_launch<__nv_bfloat16>(q, k, v, gates, batch, L, H, seg, y, h_ckpt, h0, st));
+      return gla_seq_fwd_launch<__nv_bfloat16>(q, k, v, gates, batch, L, H, Dh, seg, y, h_ckpt, h0, st, 1);
     }
-    MR_TRY(gla_chunk_fwd_launch<__half>(q, k, v, gates, batch, L, H, seg, y, h_ckpt, st));
-    return gla_seq_fwd_launch<__half>(q, k, v, gates, batch, L, H, Dh, seg, y, h_ckpt, st, 1);
+    MR_TRY(gla_chunk_fwd_launch<__half>(q, k, v, gates, batch, L, H, seg, y, h_ckpt, h0, st));
+    return gla_seq_fwd_launch<__half>(q, k, v, gates, batch, L, H, Dh, seg, y, h_ckpt, h0, st, 1);
   }
-  MR_DTYPE_SWITCH(dtype, gla_seq_fwd_launch<T>(q, k, v, gates, batch, L, H, Dh, seg, y, h_ckpt, st, 0));
+  MR_DTYPE_SWITCH(dtype, gla_seq_fwd_launch<T>(q, k, v, gates, batch, L, H, Dh, seg, y, h_ckpt, h0, st, 0));
 }
 
 int64_t mr_gla_preferred_seg(int dtype, int64_t L, int64_t Dh, int64_t seg) {
@@ -394,6 +458,14 @@ int mr_gla_bwd(const float* grad_y, const float* grad_final, const float* h_ckpt
                int64_t L, int64_t H, int64_t Dh, int64_t seg, void* grad_q, void* grad_k,
                void* grad_v, void* grad_gates, void* workspace, size_t workspace_bytes,
                void* stream) {
+  return mr_gla_bwd_h0(grad_y, grad_final, h_ckpt, q, k, v, gates, dtype, batch, L, H, Dh, seg, grad_q, grad_k,
+                       grad_v, grad_gates, workspace, workspace_bytes, nullptr, nullptr, stream);
+}
+
+int mr_gla_bwd_h0(const float* grad_y, const float* grad_final, const float* h_ckpt, const void* q, const void* k,
+                  const void* v, const void* gates, int dtype, int64_t batch, int64_t L, int64_t H, int64_t Dh,
+                  int64_t seg, void* grad_q, void* grad_k, void* grad_v, void* grad_gates, void* workspace,
+                  size_t workspace_bytes, const float* h0, float* grad_h0, void* stream) {
   g_err[0] = 0;
   MR_TRY(gla_common_checks("mr_gla_bwd", dtype, batch, L, H, Dh, seg));
   MR_TRY(check_ptrs("mr_gla_bwd", {grad_y, h_ckpt, q, k, v, gates, grad_q, grad_k, grad_v, grad_gates}));
@@ -404,24 +476,26 @@ int mr_gla_bwd(const float* grad_y, const float* grad_final, const float* h_ckpt
     return set_error(MR_E_WORKSPACE, "mr_gla_bwd: workspace of %zu bytes required, got %zu", need,
                      workspace_bytes);
   MR_TRY(check_opt_ptr("mr_gla_bwd", workspace));
+  MR_TRY(check_opt_ptr("mr_gla_bwd", h0));
+  MR_TRY(check_opt_ptr("mr_gla_bwd", grad_h0));
   cudaStream_t st = (cudaStream_t)stream;
   if (chunk) {
     // tensor-core chunks for every unit, then the per-step kernel redoes the
     // units with a gate outside [1e-3, 1] (workspace: its scratch slots)
     if (dtype == MR_BF16) {
       MR_TRY(gla_chunk_bwd_launch<__nv_bfloat16>(grad_y, grad_final, h_ckpt, q, k, v, gates, batch, L, H, seg,
-                                                 grad_q, grad_k, grad_v, grad_gates, st));
+                                                 grad_q, grad_k, grad_v, grad_gates, h0, grad_h0, st));
       return gla_seq_bwd_launch<__nv_bfloat16>(grad_y, grad_final, h_ckpt, q, k, v, gates, batch, L, H, Dh, seg,
-                                               grad_q, grad_k, grad_v, grad_gates, workspace, st, 1);
+                                               grad_q, grad_k, grad_v, grad_gates, workspace, h0, grad_h0, st, 1);
     }
     MR_TRY(gla_chunk_bwd_launch<__half>(grad_y, grad_final, h_ckpt, q, k, v, gates, batch, L, H, seg, grad_q,
-                                        grad_k, grad_v, grad_gates, st));
+                                        grad_k, grad_v, grad_gates, h0, grad_h0, st));
     return gla_seq_bwd_launch<__half>(grad_y, grad_final, h_ckpt, q, k, v, gates, batch, L, H, Dh, seg, grad_q,
-                                      grad_k, grad_v, grad_gates, workspace, st, 1);
+                                      grad_k, grad_v, grad_gates, workspace, h0, grad_h0, st, 1);
   }
   MR_DTYPE_SWITCH(dtype, gla_seq_bwd_launch<T>(grad_y, grad_final, h_ckpt, q, k, v, gates, batch, L,
                                                H, Dh, seg, grad_q, grad_k, grad_v, grad_gates,
-                                               workspace, st, 0));
+                                               workspace, h0, grad_h0, st, 0));
 }
 
 }  // extern "C"

@@ -36,7 +36,7 @@ __global__ void __launch_bounds__(kSeqThreads)
 ssd_seq_fwd_kernel(const T* __restrict__ u, const T* __restrict__ delta, const T* __restrict__ Bm,
                    const T* __restrict__ Cm, const float* __restrict__ A, int64_t ash, int64_t asn,
                    int L, int H, int Dh, int N, int seg, float* __restrict__ y,
-                   float* __restrict__ ckpt) {
+                   float* __restrict__ ckpt, const float* __restrict__ h0) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t b = blockIdx.x / H;
   const int h = blockIdx.x % H;
@@ -48,11 +48,15 @@ ssd_seq_fwd_kernel(const T* __restrict__ u, const T* __restrict__ delta, const T
     const int n = lane + 32 * k;
     An[k] = n < N ? A[h * ash + n * asn] : 0.f;
   }
+  // initial state h0 [B,H,Dh,N] (the final-state layout) or zero
   float st[R][NK];
 #pragma unroll
   for (int r = 0; r < R; ++r)
 #pragma unroll
-    for (int k = 0; k < NK; ++k) st[r][k] = 0.f;
+    for (int k = 0; k < NK; ++k) {
+      const int n = lane + 32 * k;
+      st[r][k] = (h0 != nullptr && n < N) ? h0[((b * H + h) * Dh + warp + 8 * r) * (int64_t)N + n] : 0.f;
+    }
 
   for (int t = 0; t < L; ++t) {
     const int64_t row = (b * L + t) * H + h;
@@ -100,7 +104,8 @@ ssd_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfina
                    const T* __restrict__ delta, const T* __restrict__ Bm, const T* __restrict__ Cm,
                    const float* __restrict__ A, int64_t ash, int64_t asn, int L, int H, int Dh,
                    int N, int seg, T* __restrict__ gu, T* __restrict__ gdelta, T* __restrict__ gB,
-                   T* __restrict__ gC, float* __restrict__ gA_part, float* __restrict__ scratch) {
+                   T* __restrict__ gC, float* __restrict__ gA_part, float* __restrict__ scratch,
+                   const float* __restrict__ h0, float* __restrict__ gh0) {
   constexpr int NP = 32 * NK;
   __shared__ float pB[kTS][8][NP];
   __shared__ float pC[kTS][8][NP];
@@ -141,7 +146,11 @@ ssd_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfina
 #pragma unroll
         for (int k = 0; k < NK; ++k) {
           const int n = lane + 32 * k;
-          st[r][k] = (s > 0 && n < N) ? ck[(int64_t)n * Dh + warp + 8 * r] : 0.f;
+          const int d = warp + 8 * r;
+          st[r][k] = n >= N                ? 0.f
+                     : s > 0               ? ck[(int64_t)n * Dh + d]
+                     : h0 != nullptr       ? h0[((b * H + h) * Dh + d) * (int64_t)N + n]
+                                           : 0.f;
           scr[(int64_t)(r * NK + k) * kSeqThreads] = st[r][k];
         }
       for (int tl = 0; tl < seg; ++tl) {
@@ -243,6 +252,15 @@ ssd_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfina
     }
   }
 
+  // gradient of the initial state: the adjoint carried past step 0
+  if (gh0 != nullptr)
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int k = 0; k < NK; ++k) {
+        const int n = lane + 32 * k;
+        if (n < N) gh0[((b * H + h) * Dh + warp + 8 * r) * (int64_t)N + n] = adj[r][k];
+      }
   // grad_A partial for this (b, h): sum over rows (in-thread) and warps
   __syncthreads();
 #pragma unroll
@@ -277,17 +295,20 @@ template <typename T, int R, int IK>
 __global__ void __launch_bounds__(kSeqThreads)
 gla_seq_fwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
                    const T* __restrict__ gates, int L, int H, int Dh, int seg,
-                   float* __restrict__ y, float* __restrict__ ckpt, int only_marked) {
+                   float* __restrict__ y, float* __restrict__ ckpt, int only_marked,
+                   const float* __restrict__ h0) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t b = blockIdx.x / H;
   const int h = blockIdx.x % H;
   const int nseg = L / seg;
   if (only_marked && !isnan(y[(b * L * H + h) * Dh])) return;
+  // initial state h0 [B,H,Dh(i),Dh(j)] (the final-state layout) or zero
   float S[IK][R];
 #pragma unroll
   for (int i = 0; i < IK; ++i)
 #pragma unroll
-    for (int r = 0; r < R; ++r) S[i][r] = 0.f;
+    for (int r = 0; r < R; ++r)
+      S[i][r] = h0 != nullptr ? h0[((b * H + h) * Dh + lane + 32 * i) * (int64_t)Dh + warp + 8 * r] : 0.f;
 
   for (int t = 0; t < L; ++t) {
     const int64_t row = (b * L + t) * H + h;
@@ -329,7 +350,7 @@ gla_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfina
                    const T* __restrict__ k, const T* __restrict__ v, const T* __restrict__ gates,
                    int L, int H, int Dh, int seg, T* __restrict__ gq, T* __restrict__ gk,
                    T* __restrict__ gv, T* __restrict__ gg, float* __restrict__ scratch, int units,
-                   int only_marked) {
+                   int only_marked, const float* __restrict__ h0, float* __restrict__ gh0) {
   constexpr int NP = 32 * IK;
   __shared__ float pQ[kTS][8][NP];
   __shared__ float pK[kTS][8][NP];
@@ -362,7 +383,8 @@ gla_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfina
         for (int i = 0; i < IK; ++i)
 #pragma unroll
           for (int r = 0; r < R; ++r) {
-            S[i][r] = s > 0 ? ck[(int64_t)(lane + 32 * i) * Dh + warp + 8 * r] : 0.f;
+            const int64_t e = (int64_t)(lane + 32 * i) * Dh + warp + 8 * r;
+            S[i][r] = s > 0 ? ck[e] : h0 != nullptr ? h0[(b * H + h) * (int64_t)Dh * Dh + e] : 0.f;
             scr[(int64_t)(i * R + r) * kSeqThreads] = S[i][r];
           }
         for (int tl = 0; tl < seg; ++tl) {
@@ -452,6 +474,13 @@ gla_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfina
         }
       }
     }
+    // gradient of the initial state: the adjoint carried past step 0
+    if (gh0 != nullptr)
+#pragma unroll
+      for (int i = 0; i < IK; ++i)
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+          gh0[((b * H + h) * Dh + lane + 32 * i) * (int64_t)Dh + warp + 8 * r] = adj[i][r];
     __syncthreads();  // the slot's scratch is reused by the next unit
   }
 }
@@ -503,23 +532,24 @@ bool gla_seq_supported(int64_t Dh) { return Dh == 32 || Dh == 64 || Dh == 96 || 
 template <typename T, int R>
 static void ssd_fwd_nk(int nk, dim3 g, cudaStream_t st, const T* u, const T* dl, const T* Bm,
                        const T* Cm, const float* A, int64_t ash, int64_t asn, int L, int H, int Dh,
-                       int N, int seg, float* y, float* ck) {
+                       int N, int seg, float* y, float* ck, const float* h0) {
   if (nk == 1)
-    ssd_seq_fwd_kernel<T, R, 1><<<g, kSeqThreads, 0, st>>>(u, dl, Bm, Cm, A, ash, asn, L, H, Dh, N, seg, y, ck);
+    ssd_seq_fwd_kernel<T, R, 1><<<g, kSeqThreads, 0, st>>>(u, dl, Bm, Cm, A, ash, asn, L, H, Dh, N, seg, y, ck, h0);
   else if (nk == 2)
-    ssd_seq_fwd_kernel<T, R, 2><<<g, kSeqThreads, 0, st>>>(u, dl, Bm, Cm, A, ash, asn, L, H, Dh, N, seg, y, ck);
+    ssd_seq_fwd_kernel<T, R, 2><<<g, kSeqThreads, 0, st>>>(u, dl, Bm, Cm, A, ash, asn, L, H, Dh, N, seg, y, ck, h0);
   else
-    ssd_seq_fwd_kernel<T, R, 4><<<g, kSeqThreads, 0, st>>>(u, dl, Bm, Cm, A, ash, asn, L, H, Dh, N, seg, y, ck);
+    ssd_seq_fwd_kernel<T, R, 4><<<g, kSeqThreads, 0, st>>>(u, dl, Bm, Cm, A, ash, asn, L, H, Dh, N, seg, y, ck, h0);
 }
 
 template <typename T>
 int ssd_seq_fwd_launch(const void* u, const void* delta, const void* Bm, const void* Cm,
                        const float* A, int64_t ash, int64_t asn, int64_t batch, int64_t L, int64_t H,
-                       int64_t Dh, int64_t N, int64_t seg, float* y, float* ckpt, cudaStream_t st) {
+                       int64_t Dh, int64_t N, int64_t seg, float* y, float* ckpt, const float* h0,
+                       cudaStream_t st) {
   dim3 g((unsigned)(batch * H));
 #define MR_CALL(R_, NK_)                                                                       \
   ssd_fwd_nk<T, R_>(NK_, g, st, (const T*)u, (const T*)delta, (const T*)Bm, (const T*)Cm, A, ash, \
-                    asn, (int)L, (int)H, (int)Dh, (int)N, (int)seg, y, ckpt)
+                    asn, (int)L, (int)H, (int)Dh, (int)N, (int)seg, y, ckpt, h0)
   MR_SSD_DISPATCH(Dh, N, MR_CALL);
 #undef MR_CALL
   return check_launch("ssd_seq_fwd_kernel");
@@ -529,13 +559,13 @@ template <typename T, int R>
 static void ssd_bwd_nk(int nk, dim3 g, cudaStream_t st, const float* gy, const float* gf,
                        const float* ck, const T* u, const T* dl, const T* Bm, const T* Cm,
                        const float* A, int64_t ash, int64_t asn, int L, int H, int Dh, int N, int seg,
-                       T* gu, T* gd, T* gB, T* gC, float* gAp, float* scr) {
+                       T* gu, T* gd, T* gB, T* gC, float* gAp, float* scr, const float* h0, float* gh0) {
   if (nk == 1)
-    ssd_seq_bwd_kernel<T, R, 1><<<g, kSeqThreads, 0, st>>>(gy, gf, ck, u, dl, Bm, Cm, A, ash, asn, L, H, Dh, N, seg, gu, gd, gB, gC, gAp, scr);
+    ssd_seq_bwd_kernel<T, R, 1><<<g, kSeqThreads, 0, st>>>(gy, gf, ck, u, dl, Bm, Cm, A, ash, asn, L, H, Dh, N, seg, gu, gd, gB, gC, gAp, scr, h0, gh0);
   else if (nk == 2)
-    ssd_seq_bwd_kernel<T, R, 2><<<g, kSeqThreads, 0, st>>>(gy, gf, ck, u, dl, Bm, Cm, A, ash, asn, L, H, Dh, N, seg, gu, gd, gB, gC, gAp, scr);
+    ssd_seq_bwd_kernel<T, R, 2><<<g, kSeqThreads, 0, st>>>(gy, gf, ck, u, dl, Bm, Cm, A, ash, asn, L, H, Dh, N, seg, gu, gd, gB, gC, gAp, scr, h0, gh0);
   else
-    ssd_seq_bwd_kernel<T, R, 4><<<g, kSeqThreads, 0, st>>>(gy, gf, ck, u, dl, Bm, Cm, A, ash, asn, L, H, Dh, N, seg, gu, gd, gB, gC, gAp, scr);
+    ssd_seq_bwd_kernel<T, R, 4><<<g, kSeqThreads, 0, st>>>(gy, gf, ck, u, dl, Bm, Cm, A, ash, asn, L, H, Dh, N, seg, gu, gd, gB, gC, gAp, scr, h0, gh0);
 }
 
 template <typename T>
@@ -543,7 +573,7 @@ int ssd_seq_bwd_launch(const float* gy, const float* gf, const float* ckpt, cons
                        const void* delta, const void* Bm, const void* Cm, const float* A,
                        int64_t ash, int64_t asn, int64_t batch, int64_t L, int64_t H, int64_t Dh,
                        int64_t N, int64_t seg, void* gu, void* gd, void* gB, void* gC, float* gA,
-                       void* ws, cudaStream_t st) {
+                       void* ws, const float* h0, float* gh0, cudaStream_t st) {
   const int64_t R = Dh / 8, NK = nk_of(N);
   const size_t scr_bytes = (size_t)batch * H * (seg + 1) * R * NK * kSeqThreads * sizeof(float);
   float* scr = (float*)ws;
@@ -552,7 +582,7 @@ int ssd_seq_bwd_launch(const float* gy, const float* gf, const float* ckpt, cons
 #define MR_CALL(R_, NK_)                                                                        \
   ssd_bwd_nk<T, R_>(NK_, g, st, gy, gf, ckpt, (const T*)u, (const T*)delta, (const T*)Bm,         \
                     (const T*)Cm, A, ash, asn, (int)L, (int)H, (int)Dh, (int)N, (int)seg, (T*)gu,  \
-                    (T*)gd, (T*)gB, (T*)gC, gAp, scr)
+                    (T*)gd, (T*)gB, (T*)gC, gAp, scr, h0, gh0)
   MR_SSD_DISPATCH(Dh, N, MR_CALL);
 #undef MR_CALL
   int rc = check_launch("ssd_seq_bwd_kernel");
@@ -567,15 +597,15 @@ int ssd_seq_bwd_launch(const float* gy, const float* gf, const float* ckpt, cons
 template <typename T>
 int gla_seq_fwd_launch(const void* q, const void* k, const void* v, const void* g, int64_t batch,
                        int64_t L, int64_t H, int64_t Dh, int64_t seg, float* y, float* ckpt,
-                       cudaStream_t st, int only_bad) {
+                       const float* h0, cudaStream_t st, int only_bad) {
   dim3 grid((unsigned)(batch * H));
   const T *q_ = (const T*)q, *k_ = (const T*)k, *v_ = (const T*)v, *g_ = (const T*)g;
   const int L_ = (int)L, H_ = (int)H, s_ = (int)seg;
   switch ((int)Dh) {
-    case 32: gla_seq_fwd_kernel<T, 4, 1><<<grid, kSeqThreads, 0, st>>>(q_, k_, v_, g_, L_, H_, 32, s_, y, ckpt, only_bad); break;
-    case 64: gla_seq_fwd_kernel<T, 8, 2><<<grid, kSeqThreads, 0, st>>>(q_, k_, v_, g_, L_, H_, 64, s_, y, ckpt, only_bad); break;
-    case 96: gla_seq_fwd_kernel<T, 12, 3><<<grid, kSeqThreads, 0, st>>>(q_, k_, v_, g_, L_, H_, 96, s_, y, ckpt, only_bad); break;
-    default: gla_seq_fwd_kernel<T, 16, 4><<<grid, kSeqThreads, 0, st>>>(q_, k_, v_, g_, L_, H_, 128, s_, y, ckpt, only_bad); break;
+    case 32: gla_seq_fwd_kernel<T, 4, 1><<<grid, kSeqThreads, 0, st>>>(q_, k_, v_, g_, L_, H_, 32, s_, y, ckpt, only_bad, h0); break;
+    case 64: gla_seq_fwd_kernel<T, 8, 2><<<grid, kSeqThreads, 0, st>>>(q_, k_, v_, g_, L_, H_, 64, s_, y, ckpt, only_bad, h0); break;
+    case 96: gla_seq_fwd_kernel<T, 12, 3><<<grid, kSeqThreads, 0, st>>>(q_, k_, v_, g_, L_, H_, 96, s_, y, ckpt, only_bad, h0); break;
+    default: gla_seq_fwd_kernel<T, 16, 4><<<grid, kSeqThreads, 0, st>>>(q_, k_, v_, g_, L_, H_, 128, s_, y, ckpt, only_bad, h0); break;
   }
   return check_launch("gla_seq_fwd_kernel");
 }
@@ -585,7 +615,7 @@ template <typename T>
 int gla_seq_bwd_launch(const float* gy, const float* gf, const float* ckpt, const void* q,
                        const void* k, const void* v, const void* g, int64_t batch, int64_t L,
                        int64_t H, int64_t Dh, int64_t seg, void* gq, void* gk, void* gv, void* gg,
-                       void* ws, cudaStream_t st, int only_bad) {
+                       void* ws, const float* h0, float* gh0, cudaStream_t st, int only_bad) {
   const int64_t units = batch * H;
   const T *q_ = (const T*)q, *k_ = (const T*)k, *v_ = (const T*)v, *g_ = (const T*)g;
   T *gq_ = (T*)gq, *gk_ = (T*)gk, *gv_ = (T*)gv, *gg_ = (T*)gg;
@@ -595,10 +625,10 @@ int gla_seq_bwd_launch(const float* gy, const float* gf, const float* ckpt, cons
   const int flags = only_bad ? 1 : 0;
   dim3 grid((unsigned)(only_bad ? (units < kGlaFallbackSlots ? units : kGlaFallbackSlots) : units));
   switch ((int)Dh) {
-    case 32: gla_seq_bwd_kernel<T, 4, 1><<<grid, kSeqThreads, 0, st>>>(gy, gf, ckpt, q_, k_, v_, g_, L_, H_, 32, s_, gq_, gk_, gv_, gg_, scr, u_, flags); break;
-    case 64: gla_seq_bwd_kernel<T, 8, 2><<<grid, kSeqThreads, 0, st>>>(gy, gf, ckpt, q_, k_, v_, g_, L_, H_, 64, s_, gq_, gk_, gv_, gg_, scr, u_, flags); break;
-    case 96: gla_seq_bwd_kernel<T, 12, 3><<<grid, kSeqThreads, 0, st>>>(gy, gf, ckpt, q_, k_, v_, g_, L_, H_, 96, s_, gq_, gk_, gv_, gg_, scr, u_, flags); break;
-    default: gla_seq_bwd_kernel<T, 16, 4><<<grid, kSeqThreads, 0, st>>>(gy, gf, ckpt, q_, k_, v_, g_, L_, H_, 128, s_, gq_, gk_, gv_, gg_, scr, u_, flags); break;
+    case 32: gla_seq_bwd_kernel<T, 4, 1><<<grid, kSeqThreads, 0, st>>>(gy, gf, ckpt, q_, k_, v_, g_, L_, H_, 32, s_, gq_, gk_, gv_, gg_, scr, u_, flags, h0, gh0); break;
+    case 64: gla_seq_bwd_kernel<T, 8, 2><<<grid, kSeqThreads, 0, st>>>(gy, gf, ckpt, q_, k_, v_, g_, L_, H_, 64, s_, gq_, gk_, gv_, gg_, scr, u_, flags, h0, gh0); break;
+    case 96: gla_seq_bwd_kernel<T, 12, 3><<<grid, kSeqThreads, 0, st>>>(gy, gf, ckpt, q_, k_, v_, g_, L_, H_, 96, s_, gq_, gk_, gv_, gg_, scr, u_, flags, h0, gh0); break;
+    default: gla_seq_bwd_kernel<T, 16, 4><<<grid, kSeqThreads, 0, st>>>(gy, gf, ckpt, q_, k_, v_, g_, L_, H_, 128, s_, gq_, gk_, gv_, gg_, scr, u_, flags, h0, gh0); break;
   }
   return check_launch("gla_seq_bwd_kernel");
 }
@@ -606,18 +636,20 @@ int gla_seq_bwd_launch(const float* gy, const float* gf, const float* ckpt, cons
 #define MR_INST(T)                                                                                  \
   template int ssd_seq_fwd_launch<T>(const void*, const void*, const void*, const void*,           \
                                      const float*, int64_t, int64_t, int64_t, int64_t, int64_t,   \
-                                     int64_t, int64_t, int64_t, float*, float*, cudaStream_t);    \
+                                     int64_t, int64_t, int64_t, float*, float*, const float*,     \
+                                     cudaStream_t);                                                \
   template int ssd_seq_bwd_launch<T>(const float*, const float*, const float*, const void*,        \
                                      const void*, const void*, const void*, const float*, int64_t, \
                                      int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, \
-                                     void*, void*, void*, void*, float*, void*, cudaStream_t);    \
+                                     void*, void*, void*, void*, float*, void*, const float*,      \
+                                     float*, cudaStream_t);                                        \
   template int gla_seq_fwd_launch<T>(const void*, const void*, const void*, const void*, int64_t,  \
                                      int64_t, int64_t, int64_t, int64_t, float*, float*,           \
-                                     cudaStream_t, int);                                           \
+                                     const float*, cudaStream_t, int);                             \
   template int gla_seq_bwd_launch<T>(const float*, const float*, const float*, const void*,        \
                                      const void*, const void*, const void*, int64_t, int64_t,      \
                                      int64_t, int64_t, int64_t, void*, void*, void*, void*, void*, \
-                                     cudaStream_t, int);
+                                     const float*, float*, cudaStream_t, int);
 MR_INST(float)
 MR_INST(__nv_bfloat16)
 MR_INST(__half)

@@ -173,12 +173,15 @@ __device__ __forceinline__ float step_log_decay(float x, float Ah) {
     return x * Ah;
 }
 
-template <typename T, typename V>
+// kH0: an initial state is given (a separate instantiation, so the common case's
+// code is untouched by it)
+template <typename T, typename V, bool kH0>
 __global__ void __launch_bounds__(ssdc::NT, 1)
 ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_constant__ CUtensorMap tm_B,
                      const __grid_constant__ CUtensorMap tm_C, const __grid_constant__ CUtensorMap tm_y,
                      const __grid_constant__ CUtensorMap tm_ck, const T* __restrict__ delta,
-                     const float* __restrict__ A, int64_t ash, int L, int H, int seg, float* __restrict__ y) {
+                     const float* __restrict__ A, int64_t ash, int L, int H, int seg, float* __restrict__ y,
+                     const float* __restrict__ h0) {
   using namespace ssdc;
   constexpr int NS = Cfg<V>::NS, NB = Cfg<V>::NB;
   constexpr uint32_t STAGE = Cfg<V>::STAGE;
@@ -225,7 +228,7 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     umma::tmem_alloc(tslot, 512);
     umma::tmem_relinquish();
   }
-  // h0 = 0 for the first chunk's Y2 product
+  // h^T = 0 for the first chunk's Y2 product (rewritten below from an initial state)
   for (int i = tid; i < (int)(TILE / 16); i += NT) reinterpret_cast<int4*>(sHt)[i] = make_int4(0, 0, 0, 0);
   if constexpr (V::kGla)
     for (int i = tid; i < (int)(TILE / 16); i += NT) reinterpret_cast<int4*>(sZero)[i] = make_int4(0, 0, 0, 0);
@@ -268,9 +271,28 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   const int cq0 = 32 * jq;          // first s-column of this thread
   const int ct0 = cq0 & 63;         // that column inside its 64-column G tile
   const uint32_t tl = tbase + ((uint32_t)(32 * q4) << 16);
+  // the state (row n = trow, channels ch0..): the initial state h0 or zero. h0 has the final
+  // state's layout, [B,H,Dh,N] (SSD, element (d, n)) or [B,H,Dk,Dv] (GLA, element (n, d)).
   float hreg[CH];
 #pragma unroll
   for (int i = 0; i < CH; ++i) hreg[i] = 0.f;
+  if constexpr (kH0) {
+    const int64_t bh = (int64_t)b * H + h;
+#pragma unroll
+    for (int i = 0; i < CH; ++i) {
+      if (trow >= NS)
+        hreg[i] = 0.f;
+      else if constexpr (V::kGla)
+        hreg[i] = h0[(bh * NS + trow) * DH + ch0 + i];
+      else
+        hreg[i] = h0[(bh * DH + ch0 + i) * NS + trow];
+    }
+    // its 2-byte copy for chunk 0's Y2 (these threads cover the tile)
+#pragma unroll
+    for (int cc = 0; cc < CH / 8; ++cc)
+      *reinterpret_cast<int4*>(sHt + umma::sw128_off(trow, ch0 + 8 * cc)) = pack8<T>(hreg + 8 * cc);
+    fence_proxy_async_smem();
+  }
   uint32_t mph = 0, mph2 = 0;
 
   // The next chunk's scalars are computed during E1 by four warps whose G
@@ -557,7 +579,7 @@ static int ssd_tmaps(const void* u, const void* Bm, const void* Cm, int64_t batc
 template <typename T, typename V>
 static int chunk_fwd_launch(const void* u, const void* delta, const void* Bm, const void* Cm, const float* A,
                             int64_t ash, int64_t batch, int64_t L, int64_t H, int64_t seg, float* y,
-                            float* ckpt, cudaStream_t st) {
+                            float* ckpt, const float* h0, cudaStream_t st) {
   constexpr int NS = V::NS;
   constexpr size_t SMEM = ssdc::Cfg<V>::SMEM;
   CUtensorMap mu, mB, mC, my, mck;
@@ -574,39 +596,41 @@ static int chunk_fwd_launch(const void* u, const void* delta, const void* Bm, co
                               (uint64_t)NS * DH * 4, 32, 64, 1, SW))
       return rc;
   }
-  auto k = ssd_chunk_fwd_kernel<T, V>;
+  auto k = h0 != nullptr ? ssd_chunk_fwd_kernel<T, V, true> : ssd_chunk_fwd_kernel<T, V, false>;
   const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM);
   if (e != cudaSuccess) return set_error(MR_E_LAUNCH, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
   k<<<(unsigned)(batch * H), ssdc::NT, SMEM, st>>>(mu, mB, mC, my, mck, (const T*)delta, A, ash, (int)L, (int)H,
-                                                   (int)seg, y);
+                                                   (int)seg, y, h0);
   return check_launch(V::kGla ? "gla_chunk_fwd_kernel" : "ssd_chunk_fwd_kernel");
 }
 
 template <typename T>
 int ssd_chunk_fwd_launch(const void* u, const void* delta, const void* Bm, const void* Cm, const float* A,
                          int64_t ash, int64_t batch, int64_t L, int64_t H, int64_t seg, float* y,
-                         float* ckpt, cudaStream_t st) {
-  return chunk_fwd_launch<T, SsdRec>(u, delta, Bm, Cm, A, ash, batch, L, H, seg, y, ckpt, st);
+                         float* ckpt, const float* h0, cudaStream_t st) {
+  return chunk_fwd_launch<T, SsdRec>(u, delta, Bm, Cm, A, ash, batch, L, H, seg, y, ckpt, h0, st);
 }
 
 // GLA forward: (u, B, C, decay input) = (v, k, q, gates); y and the
 // checkpoints [B, L/seg, H, Dk, Dv] as the sequential kernel writes them.
 template <typename T>
 int gla_chunk_fwd_launch(const void* q, const void* k, const void* v, const void* gates, int64_t batch,
-                         int64_t L, int64_t H, int64_t seg, float* y, float* ckpt, cudaStream_t st) {
-  return chunk_fwd_launch<T, GlaRec>(v, gates, k, q, nullptr, 0, batch, L, H, seg, y, ckpt, st);
+                         int64_t L, int64_t H, int64_t seg, float* y, float* ckpt, const float* h0,
+                         cudaStream_t st) {
+  return chunk_fwd_launch<T, GlaRec>(v, gates, k, q, nullptr, 0, batch, L, H, seg, y, ckpt, h0, st);
 }
 
 template int ssd_chunk_fwd_launch<__nv_bfloat16>(const void*, const void*, const void*, const void*,
                                                  const float*, int64_t, int64_t, int64_t, int64_t, int64_t,
-                                                 float*, float*, cudaStream_t);
+                                                 float*, float*, const float*, cudaStream_t);
 template int ssd_chunk_fwd_launch<__half>(const void*, const void*, const void*, const void*, const float*,
                                           int64_t, int64_t, int64_t, int64_t, int64_t, float*, float*,
-                                          cudaStream_t);
+                                          const float*, cudaStream_t);
 template int gla_chunk_fwd_launch<__nv_bfloat16>(const void*, const void*, const void*, const void*, int64_t,
-                                                 int64_t, int64_t, int64_t, float*, float*, cudaStream_t);
+                                                 int64_t, int64_t, int64_t, float*, float*, const float*,
+                                                 cudaStream_t);
 template int gla_chunk_fwd_launch<__half>(const void*, const void*, const void*, const void*, int64_t, int64_t,
-                                          int64_t, int64_t, float*, float*, cudaStream_t);
+                                          int64_t, int64_t, float*, float*, const float*, cudaStream_t);
 
 int ssdc_device_error(bool clear) { return read_device_error(clear); }
 
@@ -673,7 +697,8 @@ template <typename V> struct Cfg {
 };
 }  // namespace ssdb
 
-template <typename T, typename V>
+// kH0: an initial state is given (a separate instantiation, as in the forward)
+template <typename T, typename V, bool kH0>
 __global__ void __launch_bounds__(ssdb::NT, 1)
 ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_constant__ CUtensorMap tm_B,
                      const __grid_constant__ CUtensorMap tm_C, const __grid_constant__ CUtensorMap tm_gu,
@@ -681,7 +706,8 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
                      const float* __restrict__ ckpt, const float* __restrict__ gy,
                      const __grid_constant__ CUtensorMap tm_d, int dmap, const float* __restrict__ gfinal,
                      const T* __restrict__ delta, const float* __restrict__ A, int64_t ash, int L, int H, int seg,
-                     T* __restrict__ gdelta, float* __restrict__ gA_part) {
+                     T* __restrict__ gdelta, float* __restrict__ gA_part, const float* __restrict__ h0,
+                     float* __restrict__ gh0) {
   using namespace ssdb;
   constexpr int NS = Cfg<V>::NS, NB = Cfg<V>::NB;
   constexpr int NCT = NS / CQ;  // state columns n per thread in epilogue 3 (16-column blocks: NCT / 16)
@@ -796,16 +822,32 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
 #pragma unroll
     for (int k = 0; k < 4; ++k) gyv[k] = ld_pinned_f4(src + (int64_t)32 * k * H * DH);
   };
-  // h0 of chunk c > 0: the checkpoint at the end of the previous segment, [N][Dh] (rows n)
+  // h0 of chunk c > 0: the checkpoint at the end of the previous segment, [N][Dh] (rows n);
+  // of chunk 0: the initial state h0 (the final state's layout: [B,H,Dh,N] for SSD, element
+  // (d, n), or [B,H,Dk,Dv] for GLA, element (n, d)), when given
   float4 h0v[4];
+  constexpr bool has_h0 = kH0;
   auto load_h0 = [&](int c) {
-    const int64_t kk = ((int64_t)b * nseg + (c * Q) / seg - 1) * H + h;
-    const float* src = ckpt + (kk * NS + cr0) * DH + cd0;
+    if (c > 0) {
+      const int64_t kk = ((int64_t)b * nseg + (c * Q) / seg - 1) * H + h;
+      const float* src = ckpt + (kk * NS + cr0) * DH + cd0;
 #pragma unroll
-    for (int k = 0; k < NS / 32; ++k) h0v[k] = ld_pinned_f4(src + 32 * k * DH);
+      for (int k = 0; k < NS / 32; ++k) h0v[k] = ld_pinned_f4(src + 32 * k * DH);
+    } else {
+      const int64_t bh = (int64_t)b * H + h;
+#pragma unroll
+      for (int k = 0; k < NS / 32; ++k) {
+        const int n = cr0 + 32 * k;
+        float e[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          e[i] = V::kGla ? h0[(bh * NS + n) * DH + cd0 + i] : h0[(bh * DH + cd0 + i) * NS + n];
+        h0v[k] = make_float4(e[0], e[1], e[2], e[3]);
+      }
+    }
   };
   load_gy(nck - 1);
-  if (nck > 1) load_h0(nck - 1);
+  if (nck > 1 || has_h0) load_h0(nck - 1);
   float gA_acc = 0.f;
   uint32_t tph = 0, mph = 0, mph2 = 0;
 
@@ -938,7 +980,7 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     for (int k = 0; k < 4; ++k) {
       const int r = cr0 + 32 * k;
       const uint32_t off = umma::sw128_off(r, cd0);
-      const float4 hv = (c > 0 && r < NS) ? h0v[k < NS / 32 ? k : 0] : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4 hv = ((c > 0 || has_h0) && r < NS) ? h0v[k < NS / 32 ? k : 0] : make_float4(0.f, 0.f, 0.f, 0.f);
       *reinterpret_cast<uint2*>(tH0 + off) = pack4<T>(hv);
       float pf[4];
       unpack4<T>(*reinterpret_cast<const uint2*>(tPSI + off), pf);
@@ -1181,7 +1223,7 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
         arr[t] = sum4(arr, t);
       }
       fence_proxy_async_smem();
-      if (c > 1) load_h0(c - 1);
+      if (c > 1 || (c == 1 && has_h0)) load_h0(c - 1);
     }
     umma::fence_before_sync();
     __syncthreads();
@@ -1304,6 +1346,17 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   __syncthreads();
   if constexpr (V::kGla)  // mark the unit for the per-step kernel
     if (tid == 0 && sWide[2]) gdelta[row0 * H + h] = from_f<T>(__uint_as_float(kMarkNaN));
+  // the adjoint carried past chunk 0 is the gradient of the initial state
+  if (kH0 && gh0 != nullptr && row < NS) {
+    const int64_t bh = (int64_t)b * H + h;
+#pragma unroll
+    for (int i = 0; i < CH; ++i) {
+      if constexpr (V::kGla)
+        gh0[(bh * NS + row) * DH + ch0 + i] = psi[i];
+      else
+        gh0[(bh * DH + ch0 + i) * NS + row] = psi[i];
+    }
+  }
   if (warp == 0) umma::tmem_dealloc(tbase, 512);
 }
 
@@ -1321,7 +1374,7 @@ template <typename T, typename V>
 static int chunk_bwd_launch(const float* gy, const float* gf, const float* ckpt, const void* u, const void* delta,
                             const void* Bm, const void* Cm, const float* A, int64_t ash, int64_t batch, int64_t L,
                             int64_t H, int64_t seg, void* gu, void* gd, void* gB, void* gC, float* ws,
-                            cudaStream_t st) {
+                            const float* h0, float* gh0, cudaStream_t st) {
   constexpr size_t SMEM = ssdb::Cfg<V>::SMEM;
   CUtensorMap mu, mB, mC, mgu, mgB, mgC, md;
   if (int rc = ssd_tmaps<T, V::NS>(u, Bm, Cm, batch, L, H, &mu, &mB, &mC)) return rc;
@@ -1333,11 +1386,12 @@ static int chunk_bwd_launch(const float* gy, const float* gf, const float* ckpt,
     if (int rc = make_tmap_2d(&md, delta, TmapType<T>::v, 2, (uint64_t)H, (uint64_t)batch * L, (uint64_t)H * 2, 8,
                               ssdb::Q))
       return rc;
-  auto k = ssd_chunk_bwd_kernel<T, V>;
+  auto k = h0 != nullptr ? ssd_chunk_bwd_kernel<T, V, true> : ssd_chunk_bwd_kernel<T, V, false>;
   const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM);
   if (e != cudaSuccess) return set_error(MR_E_LAUNCH, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
   k<<<(unsigned)(batch * H), ssdb::NT, SMEM, st>>>(mu, mB, mC, mgu, mgB, mgC, ckpt, gy, md, dmap, gf,
-                                                   (const T*)delta, A, ash, (int)L, (int)H, (int)seg, (T*)gd, ws);
+                                                   (const T*)delta, A, ash, (int)L, (int)H, (int)seg, (T*)gd, ws,
+                                                   h0, gh0);
   return check_launch(V::kGla ? "gla_chunk_bwd_kernel" : "ssd_chunk_bwd_kernel");
 }
 
@@ -1345,9 +1399,9 @@ template <typename T>
 int ssd_chunk_bwd_launch(const float* gy, const float* gf, const float* ckpt, const void* u, const void* delta,
                          const void* Bm, const void* Cm, const float* A, int64_t ash, int64_t batch, int64_t L,
                          int64_t H, int64_t seg, void* gu, void* gd, void* gB, void* gC, float* gA,
-                         float* ws, cudaStream_t st) {
+                         float* ws, const float* h0, float* gh0, cudaStream_t st) {
   if (int rc = chunk_bwd_launch<T, SsdRec>(gy, gf, ckpt, u, delta, Bm, Cm, A, ash, batch, L, H, seg, gu, gd, gB,
-                                           gC, ws, st))
+                                           gC, ws, h0, gh0, st))
     return rc;
   const int HN = (int)(H * SsdRec::NS);
   ssd_ga_head_kernel<<<(HN + 255) / 256, 256, 0, st>>>(ws, (int)batch, (int)H, SsdRec::NS, gA);
@@ -1359,9 +1413,9 @@ int ssd_chunk_bwd_launch(const float* gy, const float* gf, const float* ckpt, co
 template <typename T>
 int gla_chunk_bwd_launch(const float* gy, const float* gf, const float* ckpt, const void* q, const void* k,
                          const void* v, const void* gates, int64_t batch, int64_t L, int64_t H, int64_t seg,
-                         void* gq, void* gk, void* gv, void* gg, cudaStream_t st) {
+                         void* gq, void* gk, void* gv, void* gg, const float* h0, float* gh0, cudaStream_t st) {
   return chunk_bwd_launch<T, GlaRec>(gy, gf, ckpt, v, gates, k, q, nullptr, 0, batch, L, H, seg, gv, gg, gk, gq,
-                                     nullptr, st);
+                                     nullptr, h0, gh0, st);
 }
 
 size_t ssd_chunk_bwd_ws_bytes(int64_t batch, int64_t H) { return (size_t)batch * H * sizeof(float); }
@@ -1369,17 +1423,18 @@ size_t ssd_chunk_bwd_ws_bytes(int64_t batch, int64_t H) { return (size_t)batch *
 template int ssd_chunk_bwd_launch<__nv_bfloat16>(const float*, const float*, const float*, const void*,
                                                  const void*, const void*, const void*, const float*, int64_t,
                                                  int64_t, int64_t, int64_t, int64_t, void*, void*, void*, void*,
-                                                 float*, float*, cudaStream_t);
+                                                 float*, float*, const float*, float*, cudaStream_t);
 template int ssd_chunk_bwd_launch<__half>(const float*, const float*, const float*, const void*, const void*,
                                           const void*, const void*, const float*, int64_t, int64_t, int64_t,
                                           int64_t, int64_t, void*, void*, void*, void*, float*, float*,
-                                          cudaStream_t);
+                                          const float*, float*, cudaStream_t);
 template int gla_chunk_bwd_launch<__nv_bfloat16>(const float*, const float*, const float*, const void*,
                                                  const void*, const void*, const void*, int64_t, int64_t,
-                                                 int64_t, int64_t, void*, void*, void*, void*, cudaStream_t);
+                                                 int64_t, int64_t, void*, void*, void*, void*, const float*,
+                                                 float*, cudaStream_t);
 template int gla_chunk_bwd_launch<__half>(const float*, const float*, const float*, const void*, const void*,
                                           const void*, const void*, int64_t, int64_t, int64_t, int64_t, void*,
-                                          void*, void*, void*, cudaStream_t);
+                                          void*, void*, void*, const float*, float*, cudaStream_t);
 
 
 // ===========================================================================
@@ -1440,9 +1495,9 @@ int ssd_chunk_bwd_noalloc(int dtype, const float* gy, const float* gf, const flo
   if (int rc = noalloc_scratch_ptr(&scratch)) return rc;
   if (dtype == MR_BF16)
     return ssd_chunk_bwd_launch<__nv_bfloat16>(gy, gf, ckpt, u, delta, Bm, Cm, A, ash, batch, L, H, seg, gu, gd,
-                                               gB, gC, gA, scratch, st);
+                                               gB, gC, gA, scratch, nullptr, nullptr, st);
   return ssd_chunk_bwd_launch<__half>(gy, gf, ckpt, u, delta, Bm, Cm, A, ash, batch, L, H, seg, gu, gd, gB, gC,
-                                      gA, scratch, st);
+                                      gA, scratch, nullptr, nullptr, st);
 }
 
 }  // namespace mr

@@ -17,7 +17,7 @@ from __future__ import annotations
 import torch
 
 from . import _lib
-from ._chassis import DEFAULT_SEG, check_segment_shape, common_dtype, grad_out, prep
+from ._chassis import DEFAULT_SEG, check_segment_shape, common_dtype, grad_out, prep, prep_h0
 
 
 def _validate(q, k, v, gates):
@@ -34,7 +34,7 @@ def _validate(q, k, v, gates):
 
 class _GLAScan(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, q, k, v, gates, seg):
+    def forward(ctx, q, k, v, gates, seg, h0):
         # an unused output's cotangent arrives as None (no zero tensor is made)
         ctx.set_materialize_grads(False)
         Bt, L, H, Dh = _validate(q, k, v, gates)
@@ -43,64 +43,69 @@ class _GLAScan(torch.autograd.Function):
         dt = common_dtype(q, k, v, gates)
         q_, k_, v_, g_ = (prep(t, dt) for t in (q, k, v, gates))
         code = _lib.DTYPE_CODE[dt]
+        h0_ = prep_h0(h0, (Bt, H, Dh, Dh), dev)
         # The checkpoints are internal (only the last one is returned, gla.py:329):
         # take the spacing of the fastest path for these shapes (same final state).
         seg_i = int(_lib.load().mr_gla_preferred_seg(code, L, Dh, seg))
         y = torch.empty((Bt, L, H, Dh), dtype=torch.float32, device=dev)
         ckpt = torch.empty((Bt, L // seg_i, H, Dh, Dh), dtype=torch.float32, device=dev)
         with torch.cuda.device(dev):
-            _lib.call("mr_gla_fwd", _lib.ptr(q_), _lib.ptr(k_), _lib.ptr(v_), _lib.ptr(g_),
-                      code, Bt, L, H, Dh, seg_i, _lib.ptr(y), _lib.ptr(ckpt),
+            _lib.call("mr_gla_fwd_h0", _lib.ptr(q_), _lib.ptr(k_), _lib.ptr(v_), _lib.ptr(g_),
+                      code, Bt, L, H, Dh, seg_i, _lib.ptr(y), _lib.ptr(ckpt), _lib.ptr(h0_),
                       _lib.stream_of(dev))
-        ctx.save_for_backward(q_, k_, v_, g_, ckpt)
+        ctx.save_for_backward(q_, k_, v_, g_, ckpt, h0_)
         ctx.seg = seg_i
         return y, ckpt[:, -1].clone()
 
     @staticmethod
     def backward(ctx, gy, gfinal):
-        q_, k_, v_, g_, ckpt = ctx.saved_tensors
+        q_, k_, v_, g_, ckpt, h0_ = ctx.saved_tensors
         Bt, L, H, Dh = q_.shape
         dev = q_.device
         code = _lib.DTYPE_CODE[q_.dtype]
         gy = grad_out(gy, (Bt, L, H, Dh), dev)
         gf = None if gfinal is None else gfinal.to(torch.float32).contiguous()
         gq, gk, gv, gg = (torch.empty_like(t) for t in (q_, k_, v_, g_))
+        gh0 = torch.empty_like(h0_) if (h0_ is not None and ctx.needs_input_grad[5]) else None
         with torch.cuda.device(dev):
             lib = _lib.load()
             nws = lib.mr_gla_bwd_workspace_bytes(code, Bt, L, H, Dh, ctx.seg)
             ws = torch.empty(max(nws, 16), dtype=torch.uint8, device=dev)
-            _lib.call("mr_gla_bwd", _lib.ptr(gy), _lib.ptr(gf), _lib.ptr(ckpt), _lib.ptr(q_),
+            _lib.call("mr_gla_bwd_h0", _lib.ptr(gy), _lib.ptr(gf), _lib.ptr(ckpt), _lib.ptr(q_),
                       _lib.ptr(k_), _lib.ptr(v_), _lib.ptr(g_), code, Bt, L, H, Dh, ctx.seg,
                       _lib.ptr(gq), _lib.ptr(gk), _lib.ptr(gv), _lib.ptr(gg), _lib.ptr(ws),
-                      ws.numel(), _lib.stream_of(dev))
-        return gq, gk, gv, gg, None
+                      ws.numel(), _lib.ptr(h0_), _lib.ptr(gh0), _lib.stream_of(dev))
+        return gq, gk, gv, gg, None, gh0
 
 
-def gla_scan(q, k, v, gates, seg=DEFAULT_SEG):
+def gla_scan(q, k, v, gates, seg=DEFAULT_SEG, h0=None):
     """Gated linear attention recurrence (``gla.py:301-318``).
 
     Args:
         q, k, v: [B, L, H, Dh] (q pre-scaled / post-RoPE)
         gates:   [B, L, H] scalar forget gate per head
         seg:     checkpoint segment length (L % seg == 0; default 32)
+        h0:      optional initial state [B, H, Dh, Dh] (the final state's layout;
+                 differentiable). Not in the reference, which starts from zero.
 
     Returns:
         y:       [B, L, H, Dh] float32
     """
-    y, _ = _GLAScan.apply(q, k, v, gates, seg)
+    y, _ = _GLAScan.apply(q, k, v, gates, seg, h0)
     return y
 
 
-def gla_scan_with_state(q, k, v, gates, seg=DEFAULT_SEG):
-    """GLA scan that also returns the final state ``[B, H, Dh, Dh]`` (``gla.py:321-329``)."""
-    return _GLAScan.apply(q, k, v, gates, seg)
+def gla_scan_with_state(q, k, v, gates, seg=DEFAULT_SEG, h0=None):
+    """GLA scan that also returns the final state ``[B, H, Dh, Dh]`` (``gla.py:321-329``).
+    Passing it back as ``h0`` continues the scan (chunked prefill)."""
+    return _GLAScan.apply(q, k, v, gates, seg, h0)
 
 
-def gla_scan_reference(q, k, v, gates):
+def gla_scan_reference(q, k, v, gates, h0=None):
     """Per-step torch loop (``gla.py:336-346``). Differentiable, any device."""
     Bt, L, H, Dh = q.shape
     ft = torch.promote_types(q.dtype, torch.float32)
-    h = torch.zeros((Bt, H, Dh, Dh), dtype=ft, device=q.device)
+    h = torch.zeros((Bt, H, Dh, Dh), dtype=ft, device=q.device) if h0 is None else h0.to(ft)
     ys = []
     for t in range(L):
         g = gates[:, t, :, None, None]

@@ -17,12 +17,12 @@ from __future__ import annotations
 import torch
 
 from . import _lib
-from ._chassis import DEFAULT_SEG, check_segment_shape, common_dtype, grad_out, prep
+from ._chassis import DEFAULT_SEG, check_segment_shape, common_dtype, grad_out, prep, prep_h0
 
 
 class _RGLRUScan(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, a, x, seg):
+    def forward(ctx, a, x, seg, h0):
         # an unused output's cotangent arrives as None (no zero tensor is made)
         ctx.set_materialize_grads(False)
         if a.dim() != 3 or x.shape != a.shape:
@@ -32,18 +32,19 @@ class _RGLRUScan(torch.autograd.Function):
         dev = _lib.require_cuda(a, x)
         dt = common_dtype(a, x)
         a_, x_ = prep(a, dt), prep(x, dt)
+        h0_ = prep_h0(h0, (Bt, D), dev)
         y = torch.empty((Bt, L, D), dtype=torch.float32, device=dev)
         ckpt = torch.empty((Bt, L // seg, D), dtype=torch.float32, device=dev)
         with torch.cuda.device(dev):
-            _lib.call("mr_rglru_fwd", _lib.ptr(a_), _lib.ptr(x_), _lib.DTYPE_CODE[dt], Bt, L, D, seg,
-                      _lib.ptr(y), _lib.ptr(ckpt), _lib.stream_of(dev))
-        ctx.save_for_backward(a_, x_, ckpt)
+            _lib.call("mr_rglru_fwd_h0", _lib.ptr(a_), _lib.ptr(x_), _lib.DTYPE_CODE[dt], Bt, L, D, seg,
+                      _lib.ptr(y), _lib.ptr(ckpt), _lib.ptr(h0_), _lib.stream_of(dev))
+        ctx.save_for_backward(a_, x_, ckpt, h0_)
         ctx.seg = seg
         return y, ckpt[:, -1].clone()
 
     @staticmethod
     def backward(ctx, gy, gfinal):
-        a_, x_, ckpt = ctx.saved_tensors
+        a_, x_, ckpt, h0_ = ctx.saved_tensors
         Bt, L, D = a_.shape
         dev = a_.device
         dt = a_.dtype
@@ -51,24 +52,27 @@ class _RGLRUScan(torch.autograd.Function):
         gf = None if gfinal is None else gfinal.to(torch.float32).contiguous()
         ga = torch.empty_like(a_)
         gx = torch.empty_like(x_)
+        gh0 = torch.empty_like(h0_) if (h0_ is not None and ctx.needs_input_grad[3]) else None
         code = _lib.DTYPE_CODE[dt]
         with torch.cuda.device(dev):
             lib = _lib.load()
             nws = lib.mr_rglru_bwd_workspace_bytes(code, Bt, L, D, ctx.seg)
             ws = torch.empty(max(nws, 1), dtype=torch.uint8, device=dev) if nws else None
-            _lib.call("mr_rglru_bwd", _lib.ptr(gy), _lib.ptr(gf), _lib.ptr(ckpt), _lib.ptr(a_),
+            _lib.call("mr_rglru_bwd_h0", _lib.ptr(gy), _lib.ptr(gf), _lib.ptr(ckpt), _lib.ptr(a_),
                       _lib.ptr(x_), code, Bt, L, D, ctx.seg, _lib.ptr(ga), _lib.ptr(gx), _lib.ptr(ws),
-                      nws, _lib.stream_of(dev))
-        return ga, gx, None
+                      nws, _lib.ptr(h0_), _lib.ptr(gh0), _lib.stream_of(dev))
+        return ga, gx, None, gh0
 
 
-def rglru_scan(a, x, seg=DEFAULT_SEG):
+def rglru_scan(a, x, seg=DEFAULT_SEG, h0=None):
     """RG-LRU diagonal linear scan (``rglru.py:234-256``).
 
     Args:
         a:   [B, L, D] per-channel recurrent gate (any real value).
         x:   [B, L, D] the already-gated input.
         seg: checkpoint segment length (L % seg == 0; default 32).
+        h0:  optional initial state [B, D] (float32 state; differentiable).
+             Not in the reference, which starts from zero.
 
     Returns:
         y:   [B, L, D] float32, ``y_t = h_t``.
@@ -77,19 +81,21 @@ def rglru_scan(a, x, seg=DEFAULT_SEG):
     and fp16 inputs are widened on read and their gradients are returned in
     the input dtype.
     """
-    y, _ = _RGLRUScan.apply(a, x, seg)
+    y, _ = _RGLRUScan.apply(a, x, seg, h0)
     return y
 
 
-def rglru_scan_with_state(a, x, seg=DEFAULT_SEG):
-    """RG-LRU scan that also returns the final state [B, D] (``rglru.py:259-267``)."""
-    return _RGLRUScan.apply(a, x, seg)
+def rglru_scan_with_state(a, x, seg=DEFAULT_SEG, h0=None):
+    """RG-LRU scan that also returns the final state [B, D] (``rglru.py:259-267``).
+    Passing it back as ``h0`` continues the scan (chunked prefill)."""
+    return _RGLRUScan.apply(a, x, seg, h0)
 
 
-def rglru_scan_reference(a, x):
+def rglru_scan_reference(a, x, h0=None):
     """Per-step torch loop (``rglru.py:274-282``). Differentiable, any device."""
     Bt, L, D = a.shape
-    h = torch.zeros((Bt, D), dtype=torch.promote_types(a.dtype, torch.float32), device=a.device)
+    ft = torch.promote_types(a.dtype, torch.float32)
+    h = torch.zeros((Bt, D), dtype=ft, device=a.device) if h0 is None else h0.to(ft)
     ys = []
     for t in range(L):
         h = a[:, t, :] * h + x[:, t, :]

@@ -18,7 +18,7 @@ from __future__ import annotations
 import torch
 
 from . import _lib
-from ._chassis import DEFAULT_SEG, check_segment_shape, common_dtype, grad_out, prep
+from ._chassis import DEFAULT_SEG, check_segment_shape, common_dtype, grad_out, prep, prep_h0
 
 
 def _validate(a, cs, sn, x):
@@ -37,7 +37,7 @@ def _validate(a, cs, sn, x):
 
 class _RotLRUScan(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, a, cs, sn, x, seg):
+    def forward(ctx, a, cs, sn, x, seg, h0):
         # an unused output's cotangent arrives as None (no zero tensor is made)
         ctx.set_materialize_grads(False)
         Bt, L, Dp = _validate(a, cs, sn, x)
@@ -46,37 +46,39 @@ class _RotLRUScan(torch.autograd.Function):
         dt = common_dtype(a, cs, sn, x)
         a_, c_, s_, x_ = (prep(t, dt) for t in (a, cs, sn, x))
         D = 2 * Dp
+        h0_ = prep_h0(h0, (Bt, D), dev)
         y = torch.empty((Bt, L, D), dtype=torch.float32, device=dev)
         ckpt = torch.empty((Bt, L // seg, D), dtype=torch.float32, device=dev)
         with torch.cuda.device(dev):
-            _lib.call("mr_rotlru_fwd", _lib.ptr(a_), _lib.ptr(c_), _lib.ptr(s_), _lib.ptr(x_),
-                      _lib.DTYPE_CODE[dt], Bt, L, Dp, seg, _lib.ptr(y), _lib.ptr(ckpt),
+            _lib.call("mr_rotlru_fwd_h0", _lib.ptr(a_), _lib.ptr(c_), _lib.ptr(s_), _lib.ptr(x_),
+                      _lib.DTYPE_CODE[dt], Bt, L, Dp, seg, _lib.ptr(y), _lib.ptr(ckpt), _lib.ptr(h0_),
                       _lib.stream_of(dev))
-        ctx.save_for_backward(a_, c_, s_, x_, ckpt)
+        ctx.save_for_backward(a_, c_, s_, x_, ckpt, h0_)
         ctx.seg = seg
         return y, ckpt[:, -1].clone()
 
     @staticmethod
     def backward(ctx, gy, gfinal):
-        a_, c_, s_, x_, ckpt = ctx.saved_tensors
+        a_, c_, s_, x_, ckpt, h0_ = ctx.saved_tensors
         Bt, L, Dp = a_.shape
         dev = a_.device
         code = _lib.DTYPE_CODE[a_.dtype]
         gy = grad_out(gy, (Bt, L, 2 * Dp), dev)
         gf = None if gfinal is None else gfinal.to(torch.float32).contiguous()
         ga, gc, gs, gx = (torch.empty_like(t) for t in (a_, c_, s_, x_))
+        gh0 = torch.empty_like(h0_) if (h0_ is not None and ctx.needs_input_grad[5]) else None
         with torch.cuda.device(dev):
             lib = _lib.load()
             nws = lib.mr_rotlru_bwd_workspace_bytes(code, Bt, L, Dp, ctx.seg)
             ws = torch.empty(nws, dtype=torch.uint8, device=dev) if nws else None
-            _lib.call("mr_rotlru_bwd", _lib.ptr(gy), _lib.ptr(gf), _lib.ptr(ckpt), _lib.ptr(a_),
+            _lib.call("mr_rotlru_bwd_h0", _lib.ptr(gy), _lib.ptr(gf), _lib.ptr(ckpt), _lib.ptr(a_),
                       _lib.ptr(c_), _lib.ptr(s_), _lib.ptr(x_), code, Bt, L, Dp, ctx.seg,
                       _lib.ptr(ga), _lib.ptr(gc), _lib.ptr(gs), _lib.ptr(gx), _lib.ptr(ws), nws,
-                      _lib.stream_of(dev))
-        return ga, gc, gs, gx, None
+                      _lib.ptr(h0_), _lib.ptr(gh0), _lib.stream_of(dev))
+        return ga, gc, gs, gx, None, gh0
 
 
-def rotlru_scan(a, cs, sn, x, seg=DEFAULT_SEG):
+def rotlru_scan(a, cs, sn, x, seg=DEFAULT_SEG, h0=None):
     """Rotational LRU pair-diagonal scan (``rotlru.py:297-320``).
 
     Args:
@@ -85,28 +87,35 @@ def rotlru_scan(a, cs, sn, x, seg=DEFAULT_SEG):
         sn:  [B, L, Dp] sin(theta_t).
         x:   [B, L, D]  drive, D = 2*Dp, pairs interleaved (u, w).
         seg: checkpoint segment length (L % seg == 0; default 32).
+        h0:  optional initial state [B, D] (pairs interleaved; differentiable).
+             Not in the reference, which starts from zero.
 
     Returns:
         y:   [B, L, D] float32.
 
     ``D`` must be a multiple of 32. Gradients flow to all four inputs.
     """
-    y, _ = _RotLRUScan.apply(a, cs, sn, x, seg)
+    y, _ = _RotLRUScan.apply(a, cs, sn, x, seg, h0)
     return y
 
 
-def rotlru_scan_with_state(a, cs, sn, x, seg=DEFAULT_SEG):
-    """Rotational LRU scan that also returns the final state [B, D] (``rotlru.py:323-331``)."""
-    return _RotLRUScan.apply(a, cs, sn, x, seg)
+def rotlru_scan_with_state(a, cs, sn, x, seg=DEFAULT_SEG, h0=None):
+    """Rotational LRU scan that also returns the final state [B, D] (``rotlru.py:323-331``).
+    Passing it back as ``h0`` continues the scan (chunked prefill)."""
+    return _RotLRUScan.apply(a, cs, sn, x, seg, h0)
 
 
-def rotlru_scan_reference(a, cs, sn, x):
+def rotlru_scan_reference(a, cs, sn, x, h0=None):
     """Per-step torch loop (``rotlru.py:338-351``). Differentiable, any device."""
     Bt, L, Dp = _validate(a, cs, sn, x)
     xp = x.reshape(Bt, L, Dp, 2)
     ft = torch.promote_types(a.dtype, torch.float32)
-    u = torch.zeros((Bt, Dp), dtype=ft, device=a.device)
-    w = torch.zeros((Bt, Dp), dtype=ft, device=a.device)
+    if h0 is None:
+        u = torch.zeros((Bt, Dp), dtype=ft, device=a.device)
+        w = torch.zeros((Bt, Dp), dtype=ft, device=a.device)
+    else:
+        hp = h0.to(ft).reshape(Bt, Dp, 2)
+        u, w = hp[..., 0], hp[..., 1]
     ys = []
     for t in range(L):
         at, c, s = a[:, t, :], cs[:, t, :], sn[:, t, :]

@@ -21,7 +21,7 @@ from __future__ import annotations
 import torch
 
 from . import _lib
-from ._chassis import DEFAULT_SEG, check_segment_shape, common_dtype, grad_out, prep
+from ._chassis import DEFAULT_SEG, check_segment_shape, common_dtype, grad_out, prep, prep_h0
 
 
 def _validate(u, delta, B, C, A_neg):
@@ -51,7 +51,7 @@ def _a_f32(A_neg):
 
 class _SSDScan(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, u, delta, B, C, A_neg, seg):
+    def forward(ctx, u, delta, B, C, A_neg, seg, h0):
         # an unused output's cotangent arrives as None (no zero tensor is made)
         ctx.set_materialize_grads(False)
         Bt, L, H, Dh, N = _validate(u, delta, B, C, A_neg)
@@ -60,6 +60,7 @@ class _SSDScan(torch.autograd.Function):
         dt = common_dtype(u, delta, B, C)
         u_, d_, B_, C_ = (prep(t, dt) for t in (u, delta, B, C))
         A32, ash, asn = _a_f32(A_neg)
+        h0_ = prep_h0(h0, (Bt, H, Dh, N), dev)
         code = _lib.DTYPE_CODE[dt]
         # The checkpoints are internal (only the last one is returned, ssd.py:361/374):
         # take the spacing of the fastest path for these shapes (same final state).
@@ -67,10 +68,10 @@ class _SSDScan(torch.autograd.Function):
         y = torch.empty((Bt, L, H, Dh), dtype=torch.float32, device=dev)
         ckpt = torch.empty((Bt, L // seg_i, H, N, Dh), dtype=torch.float32, device=dev)
         with torch.cuda.device(dev):
-            _lib.call("mr_ssd_fwd", _lib.ptr(u_), _lib.ptr(d_), _lib.ptr(B_), _lib.ptr(C_),
+            _lib.call("mr_ssd_fwd_h0", _lib.ptr(u_), _lib.ptr(d_), _lib.ptr(B_), _lib.ptr(C_),
                       _lib.ptr(A32), ash, asn, code, Bt, L, H, Dh, N, seg_i,
-                      _lib.ptr(y), _lib.ptr(ckpt), _lib.stream_of(dev))
-        ctx.save_for_backward(u_, d_, B_, C_, A32, ckpt)
+                      _lib.ptr(y), _lib.ptr(ckpt), _lib.ptr(h0_), _lib.stream_of(dev))
+        ctx.save_for_backward(u_, d_, B_, C_, A32, ckpt, h0_)
         ctx.meta = (seg_i, ash, asn, N)
         # last checkpoint [B, H, N, Dh] -> conceptual state [B, H, Dh, N] (ssd.py:373-374)
         final = ckpt[:, -1].transpose(-1, -2).contiguous()
@@ -78,7 +79,7 @@ class _SSDScan(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, gy, gfinal):
-        u_, d_, B_, C_, A32, ckpt = ctx.saved_tensors
+        u_, d_, B_, C_, A32, ckpt, h0_ = ctx.saved_tensors
         seg, ash, asn, N = ctx.meta
         Bt, L, H, Dh = u_.shape
         dev = u_.device
@@ -87,20 +88,22 @@ class _SSDScan(torch.autograd.Function):
         gf = None if gfinal is None else gfinal.to(torch.float32).contiguous()
         gu, gd, gB, gC = (torch.empty_like(t) for t in (u_, d_, B_, C_))
         gA = torch.empty((H, N), dtype=torch.float32, device=dev)
+        gh0 = torch.empty_like(h0_) if (h0_ is not None and ctx.needs_input_grad[6]) else None
         # with one rate per head (asn == 0) row h of gA is d loss / d A_h spread
         # evenly over n; autograd's expand-backward sums it back to the head
         with torch.cuda.device(dev):
             lib = _lib.load()
             nws = lib.mr_ssd_bwd_workspace_bytes(code, Bt, L, H, Dh, N, seg, asn)
             ws = torch.empty(max(nws, 16), dtype=torch.uint8, device=dev)
-            _lib.call("mr_ssd_bwd", _lib.ptr(gy), _lib.ptr(gf), _lib.ptr(ckpt), _lib.ptr(u_),
+            _lib.call("mr_ssd_bwd_h0", _lib.ptr(gy), _lib.ptr(gf), _lib.ptr(ckpt), _lib.ptr(u_),
                       _lib.ptr(d_), _lib.ptr(B_), _lib.ptr(C_), _lib.ptr(A32), ash, asn, code, Bt, L,
                       H, Dh, N, seg, _lib.ptr(gu), _lib.ptr(gd), _lib.ptr(gB), _lib.ptr(gC),
-                      _lib.ptr(gA), _lib.ptr(ws), ws.numel(), _lib.stream_of(dev))
-        return gu, gd, gB, gC, gA, None
+                      _lib.ptr(gA), _lib.ptr(ws), ws.numel(), _lib.ptr(h0_), _lib.ptr(gh0),
+                      _lib.stream_of(dev))
+        return gu, gd, gB, gC, gA, None, gh0
 
 
-def ssd_scan(u, delta, B, C, A_neg, seg=DEFAULT_SEG):
+def ssd_scan(u, delta, B, C, A_neg, seg=DEFAULT_SEG, h0=None):
     """Head-wise SSD (Mamba-2) selective scan (``ssd.py:344-362``).
 
     Args:
@@ -110,25 +113,28 @@ def ssd_scan(u, delta, B, C, A_neg, seg=DEFAULT_SEG):
         C:      [B, L, H, N]  output projection
         A_neg:  [H, N]        decay rates (negative)
         seg:    checkpoint segment length (L % seg == 0; default 32)
+        h0:     optional initial state [B, H, Dh, N] (the final state's layout;
+                differentiable). Not in the reference, which starts from zero.
 
     Returns:
         y:      [B, L, H, Dh] float32
     """
-    y, _ = _SSDScan.apply(u, delta, B, C, A_neg, seg)
+    y, _ = _SSDScan.apply(u, delta, B, C, A_neg, seg, h0)
     return y
 
 
-def ssd_scan_with_state(u, delta, B, C, A_neg, seg=DEFAULT_SEG):
-    """SSD scan that also returns the final state ``[B, H, Dh, N]`` (``ssd.py:365-375``)."""
-    return _SSDScan.apply(u, delta, B, C, A_neg, seg)
+def ssd_scan_with_state(u, delta, B, C, A_neg, seg=DEFAULT_SEG, h0=None):
+    """SSD scan that also returns the final state ``[B, H, Dh, N]`` (``ssd.py:365-375``).
+    Passing it back as ``h0`` continues the scan (chunked prefill)."""
+    return _SSDScan.apply(u, delta, B, C, A_neg, seg, h0)
 
 
-def ssd_scan_reference(u, delta, B, C, A_neg):
+def ssd_scan_reference(u, delta, B, C, A_neg, h0=None):
     """Per-step torch loop (``ssd.py:382-394``). Differentiable, any device."""
     Bt, L, H, Dh = u.shape
     N = A_neg.shape[-1]
     ft = torch.promote_types(u.dtype, torch.float32)
-    h = torch.zeros((Bt, H, Dh, N), dtype=ft, device=u.device)
+    h = torch.zeros((Bt, H, Dh, N), dtype=ft, device=u.device) if h0 is None else h0.to(ft)
     ys = []
     for t in range(L):
         dt = delta[:, t, :, None, None]
