@@ -245,6 +245,29 @@ MR_API int mr_rotlru_bwd_h0(const float* grad_y, const float* grad_final, const 
                             void* workspace, size_t workspace_bytes, const float* h0, float* grad_h0,
                             void* stream);
 
+/* -------------------------------------------------------- decode steps ---
+ * No counterpart in the reference (a decode step there is a scan of length 1,
+ * one Metal dispatch per call). One time step of the recurrence for a batch of
+ * sequences: `state` (float32, the final state's layout, as above) is advanced
+ * in place and y receives the step's output (float32). Inputs are one token's
+ * slices in `dtype`:
+ *   SSD:    u [B,H,Dh], delta [B,H], Bm/Cm [B,H,N], A_neg as in mr_ssd_fwd
+ *           (N <= 128); y [B,H,Dh]
+ *   GLA:    q,k,v [B,H,Dh], gates [B,H] (Dh <= 128); y [B,H,Dh]
+ *   RG-LRU: a, x [B,D]; y [B,D]
+ *   rotLRU: a, cs, sn [B,Dp], x [B,2Dp]; y [B,2Dp]
+ * The update is one step of the reference's pure loops (ssd.py:382-394,
+ * gla.py:336-346, rglru.py:274-282, rotlru.py:338-351). */
+MR_API int mr_ssd_step(const void* u, const void* delta, const void* Bm, const void* Cm, const float* A_neg,
+                       int64_t a_stride_h, int64_t a_stride_n, int dtype, int64_t batch, int64_t H, int64_t Dh,
+                       int64_t N, float* state, float* y, void* stream);
+MR_API int mr_gla_step(const void* q, const void* k, const void* v, const void* gates, int dtype, int64_t batch,
+                       int64_t H, int64_t Dh, float* state, float* y, void* stream);
+MR_API int mr_rglru_step(const void* a, const void* x, int dtype, int64_t batch, int64_t D, float* state,
+                         float* y, void* stream);
+MR_API int mr_rotlru_step(const void* a, const void* cs, const void* sn, const void* x, int dtype,
+                          int64_t batch, int64_t Dp, float* state, float* y, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -8,6 +8,9 @@ torch.autograd.Functions over a C-ABI library of sm_100a CUDA kernels
     rglru   - RG-LRU diagonal recurrence
     rotlru  - rotational LRU (complex-diagonal over interleaved pairs)
 
+Beyond the reference: an optional initial state ``h0=`` on every scan
+(chunked prefill) and one-token decode steps ``*_step`` on a state cache.
+
 Import with ``importlib.import_module("mlx-recurrence_b200")`` (the directory
 name carries a hyphen); after that the package is also registered as
 ``mlx_recurrence_b200``.
@@ -16,10 +19,10 @@ name carries a hyphen); after that the package is also registered as
 import sys as _sys
 
 from ._chassis import DEFAULT_SEG, check_segment_shape, get_or_build_kernel, parity_check
-from .gla import gla_scan, gla_scan_reference, gla_scan_with_state
-from .rglru import rglru_scan, rglru_scan_reference, rglru_scan_with_state
-from .rotlru import rotlru_scan, rotlru_scan_reference, rotlru_scan_with_state
-from .ssd import ssd_scan, ssd_scan_reference, ssd_scan_with_state
+from .gla import gla_scan, gla_scan_reference, gla_scan_with_state, gla_step
+from .rglru import rglru_scan, rglru_scan_reference, rglru_scan_with_state, rglru_step
+from .rotlru import rotlru_scan, rotlru_scan_reference, rotlru_scan_with_state, rotlru_step
+from .ssd import ssd_scan, ssd_scan_reference, ssd_scan_with_state, ssd_step
 
 __all__ = [
     "ssd_scan",
@@ -34,6 +37,11 @@ __all__ = [
     "rotlru_scan",
     "rotlru_scan_with_state",
     "rotlru_scan_reference",
+    # one-token decode steps on a float32 state cache (not in the reference)
+    "ssd_step",
+    "gla_step",
+    "rglru_step",
+    "rotlru_step",
     "DEFAULT_SEG",
     "get_or_build_kernel",
     "check_segment_shape",

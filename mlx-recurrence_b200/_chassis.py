@@ -83,6 +83,16 @@ def prep_h0(h0, shape, device):
     return h0.to(torch.float32).contiguous()
 
 
+def step_state(state, shape, device):
+    """The decode-step state cache: float32, contiguous, on ``device``, in the
+    final state's ``shape`` (it is advanced in place, so it is not copied)."""
+    if tuple(state.shape) != tuple(shape):
+        raise ValueError(f"state must have the final state's shape {tuple(shape)}, got {tuple(state.shape)}")
+    if state.dtype != torch.float32 or not state.is_contiguous() or state.device != device:
+        raise ValueError("state must be a contiguous float32 tensor on the inputs' device (updated in place)")
+    return state
+
+
 def grad_out(g, shape, device):
     """fp32 contiguous cotangent (zeros when autograd passes None)."""
     if g is None:

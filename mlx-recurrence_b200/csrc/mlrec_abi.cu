@@ -62,6 +62,10 @@ int ssd_chunk_bwd_noalloc(int dtype, const float*, const float*, const float*, c
                           void*, void*, void*, void*, float*, cudaStream_t);
 template <typename T> int ssd_chunk_bwd_launch(const float*, const float*, const float*, const void*, const void*, const void*, const void*, const float*, int64_t, int64_t, int64_t, int64_t, int64_t, void*, void*, void*, void*, float*, float*, const float*, float*, cudaStream_t);
 template <typename T> int ssd_chunk_fwd_launch(const void*, const void*, const void*, const void*, const float*, int64_t, int64_t, int64_t, int64_t, int64_t, float*, float*, const float*, cudaStream_t);
+template <typename T> int ssd_step_launch(const void*, const void*, const void*, const void*, const float*, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, float*, float*, cudaStream_t);
+template <typename T> int gla_step_launch(const void*, const void*, const void*, const void*, int64_t, int64_t, int64_t, float*, float*, cudaStream_t);
+template <typename T> int rglru_step_launch(const void*, const void*, int64_t, int64_t, float*, float*, cudaStream_t);
+template <typename T> int rotlru_step_launch(const void*, const void*, const void*, const void*, int64_t, int64_t, float*, float*, cudaStream_t);
 int umma_selftest_launch(const void*, const void*, const void*, const void*, float*, float*, float*,
                          cudaStream_t);
 
@@ -132,7 +136,7 @@ using namespace mr;
 
 extern "C" {
 
-int mr_abi_version(void) { return 2; }  // 2: the _h0 (initial state) entry points
+int mr_abi_version(void) { return 3; }  // 2: the _h0 (initial state) entry points; 3: the decode steps
 
 const char* mr_last_error(void) { return g_err; }
 
@@ -496,6 +500,60 @@ int mr_gla_bwd_h0(const float* grad_y, const float* grad_final, const float* h_c
   MR_DTYPE_SWITCH(dtype, gla_seq_bwd_launch<T>(grad_y, grad_final, h_ckpt, q, k, v, gates, batch, L,
                                                H, Dh, seg, grad_q, grad_k, grad_v, grad_gates,
                                                workspace, h0, grad_h0, st, 0));
+}
+
+// ------------------------------------------------------------ decode steps ---
+static int step_dims(const char* what, std::initializer_list<int64_t> dims) {
+  for (int64_t d : dims)
+    if (d <= 0) return set_error(MR_E_SHAPE, "%s: every dimension must be positive", what);
+  return MR_OK;
+}
+
+int mr_ssd_step(const void* u, const void* delta, const void* Bm, const void* Cm, const float* A_neg,
+                int64_t a_stride_h, int64_t a_stride_n, int dtype, int64_t batch, int64_t H, int64_t Dh,
+                int64_t N, float* state, float* y, void* stream) {
+  g_err[0] = 0;
+  MR_TRY(step_dims("mr_ssd_step", {batch, H, Dh, N}));
+  if (N > 128) return set_error(MR_E_SHAPE, "mr_ssd_step: N <= 128 supported, got N=%lld", (long long)N);
+  if (batch * H > (int64_t)INT32_MAX) return set_error(MR_E_SHAPE, "mr_ssd_step: batch*H too large");
+  MR_TRY(check_dtype(dtype));
+  MR_TRY(check_ptrs("mr_ssd_step", {u, delta, Bm, Cm, state, y}));
+  if (A_neg == nullptr) return set_error(MR_E_ALIGN, "mr_ssd_step: A_neg is NULL");
+  cudaStream_t st = (cudaStream_t)stream;
+  MR_DTYPE_SWITCH(dtype, ssd_step_launch<T>(u, delta, Bm, Cm, A_neg, a_stride_h, a_stride_n, batch, H, Dh, N,
+                                            state, y, st));
+}
+
+int mr_gla_step(const void* q, const void* k, const void* v, const void* gates, int dtype, int64_t batch,
+                int64_t H, int64_t Dh, float* state, float* y, void* stream) {
+  g_err[0] = 0;
+  MR_TRY(step_dims("mr_gla_step", {batch, H, Dh}));
+  if (Dh > 128) return set_error(MR_E_SHAPE, "mr_gla_step: Dh <= 128 supported, got Dh=%lld", (long long)Dh);
+  if (batch * H > (int64_t)INT32_MAX) return set_error(MR_E_SHAPE, "mr_gla_step: batch*H too large");
+  MR_TRY(check_dtype(dtype));
+  MR_TRY(check_ptrs("mr_gla_step", {q, k, v, gates, state, y}));
+  cudaStream_t st = (cudaStream_t)stream;
+  MR_DTYPE_SWITCH(dtype, gla_step_launch<T>(q, k, v, gates, batch, H, Dh, state, y, st));
+}
+
+int mr_rglru_step(const void* a, const void* x, int dtype, int64_t batch, int64_t D, float* state, float* y,
+                  void* stream) {
+  g_err[0] = 0;
+  MR_TRY(step_dims("mr_rglru_step", {batch, D}));
+  MR_TRY(check_dtype(dtype));
+  MR_TRY(check_ptrs("mr_rglru_step", {a, x, state, y}));
+  cudaStream_t st = (cudaStream_t)stream;
+  MR_DTYPE_SWITCH(dtype, rglru_step_launch<T>(a, x, batch, D, state, y, st));
+}
+
+int mr_rotlru_step(const void* a, const void* cs, const void* sn, const void* x, int dtype, int64_t batch,
+                   int64_t Dp, float* state, float* y, void* stream) {
+  g_err[0] = 0;
+  MR_TRY(step_dims("mr_rotlru_step", {batch, Dp}));
+  MR_TRY(check_dtype(dtype));
+  MR_TRY(check_ptrs("mr_rotlru_step", {a, cs, sn, x, state, y}));
+  cudaStream_t st = (cudaStream_t)stream;
+  MR_DTYPE_SWITCH(dtype, rotlru_step_launch<T>(a, cs, sn, x, batch, Dp, state, y, st));
 }
 
 }  // extern "C"

@@ -17,7 +17,7 @@ from __future__ import annotations
 import torch
 
 from . import _lib
-from ._chassis import DEFAULT_SEG, check_segment_shape, common_dtype, grad_out, prep, prep_h0
+from ._chassis import DEFAULT_SEG, check_segment_shape, common_dtype, grad_out, prep, prep_h0, step_state
 
 
 def _validate(q, k, v, gates):
@@ -113,3 +113,25 @@ def gla_scan_reference(q, k, v, gates, h0=None):
         h = g * h + kv
         ys.append(torch.sum(q[:, t, :, :, None] * h, dim=-2))
     return torch.stack(ys, dim=1)
+
+
+def gla_step(q, k, v, gates, state):
+    """One decode step (no counterpart in the reference): advances ``state``
+    [B, H, Dh, Dh] (float32, the final state's layout) in place by one step of
+    ``gla.py:336-346`` and returns y [B, H, Dh] float32. ``q``, ``k``, ``v``
+    [B, H, Dh], ``gates`` [B, H]. Not differentiable."""
+    if q.dim() != 3 or k.shape != q.shape or v.shape != q.shape:
+        raise ValueError(f"q, k, v must all be [B, H, Dh], got {tuple(q.shape)}, {tuple(k.shape)}, "
+                         f"{tuple(v.shape)}")
+    Bt, H, Dh = q.shape
+    if tuple(gates.shape) != (Bt, H):
+        raise ValueError(f"gates must be [B, H] = [{Bt}, {H}], got {tuple(gates.shape)}")
+    dev = _lib.require_cuda(q, k, v, gates, state)
+    state = step_state(state, (Bt, H, Dh, Dh), dev)
+    dt = common_dtype(q, k, v, gates)
+    q_, k_, v_, g_ = (prep(t.detach(), dt) for t in (q, k, v, gates))
+    y = torch.empty((Bt, H, Dh), dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        _lib.call("mr_gla_step", _lib.ptr(q_), _lib.ptr(k_), _lib.ptr(v_), _lib.ptr(g_), _lib.DTYPE_CODE[dt],
+                  Bt, H, Dh, _lib.ptr(state), _lib.ptr(y), _lib.stream_of(dev))
+    return y

@@ -17,7 +17,7 @@ from __future__ import annotations
 import torch
 
 from . import _lib
-from ._chassis import DEFAULT_SEG, check_segment_shape, common_dtype, grad_out, prep, prep_h0
+from ._chassis import DEFAULT_SEG, check_segment_shape, common_dtype, grad_out, prep, prep_h0, step_state
 
 
 class _RGLRUScan(torch.autograd.Function):
@@ -101,3 +101,21 @@ def rglru_scan_reference(a, x, h0=None):
         h = a[:, t, :] * h + x[:, t, :]
         ys.append(h)
     return torch.stack(ys, dim=1)
+
+
+def rglru_step(a, x, state):
+    """One decode step (no counterpart in the reference): ``state`` [B, D]
+    (float32) <- a * state + x in place (``rglru.py:274-282``); returns the new
+    state as y [B, D] float32. ``a``, ``x`` [B, D]. Not differentiable."""
+    if a.dim() != 2 or x.shape != a.shape:
+        raise ValueError(f"a and x must both be [B, D], got {tuple(a.shape)} and {tuple(x.shape)}")
+    Bt, D = a.shape
+    dev = _lib.require_cuda(a, x, state)
+    state = step_state(state, (Bt, D), dev)
+    dt = common_dtype(a, x)
+    a_, x_ = prep(a.detach(), dt), prep(x.detach(), dt)
+    y = torch.empty((Bt, D), dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        _lib.call("mr_rglru_step", _lib.ptr(a_), _lib.ptr(x_), _lib.DTYPE_CODE[dt], Bt, D, _lib.ptr(state),
+                  _lib.ptr(y), _lib.stream_of(dev))
+    return y

@@ -18,7 +18,7 @@ from __future__ import annotations
 import torch
 
 from . import _lib
-from ._chassis import DEFAULT_SEG, check_segment_shape, common_dtype, grad_out, prep, prep_h0
+from ._chassis import DEFAULT_SEG, check_segment_shape, common_dtype, grad_out, prep, prep_h0, step_state
 
 
 def _validate(a, cs, sn, x):
@@ -124,3 +124,25 @@ def rotlru_scan_reference(a, cs, sn, x, h0=None):
         u, w = un, wn
         ys.append(torch.stack([u, w], dim=-1).reshape(Bt, 2 * Dp))
     return torch.stack(ys, dim=1)
+
+
+def rotlru_step(a, cs, sn, x, state):
+    """One decode step (no counterpart in the reference): advances ``state``
+    [B, 2Dp] (float32, pairs interleaved) in place by one step of
+    ``rotlru.py:338-351`` and returns the new state as y [B, 2Dp] float32.
+    ``a``, ``cs``, ``sn`` [B, Dp], ``x`` [B, 2Dp]. Not differentiable."""
+    if a.dim() != 2 or cs.shape != a.shape or sn.shape != a.shape:
+        raise ValueError(f"a/cs/sn must all be [B, Dp], got {tuple(a.shape)}, {tuple(cs.shape)}, "
+                         f"{tuple(sn.shape)}")
+    Bt, Dp = a.shape
+    if tuple(x.shape) != (Bt, 2 * Dp):
+        raise ValueError(f"x must be [B, 2*Dp] = [{Bt}, {2 * Dp}], got {tuple(x.shape)}")
+    dev = _lib.require_cuda(a, cs, sn, x, state)
+    state = step_state(state, (Bt, 2 * Dp), dev)
+    dt = common_dtype(a, cs, sn, x)
+    a_, c_, s_, x_ = (prep(t.detach(), dt) for t in (a, cs, sn, x))
+    y = torch.empty((Bt, 2 * Dp), dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        _lib.call("mr_rotlru_step", _lib.ptr(a_), _lib.ptr(c_), _lib.ptr(s_), _lib.ptr(x_), _lib.DTYPE_CODE[dt],
+                  Bt, Dp, _lib.ptr(state), _lib.ptr(y), _lib.stream_of(dev))
+    return y

@@ -21,7 +21,7 @@ from __future__ import annotations
 import torch
 
 from . import _lib
-from ._chassis import DEFAULT_SEG, check_segment_shape, common_dtype, grad_out, prep, prep_h0
+from ._chassis import DEFAULT_SEG, check_segment_shape, common_dtype, grad_out, prep, prep_h0, step_state
 
 
 def _validate(u, delta, B, C, A_neg):
@@ -143,3 +143,32 @@ def ssd_scan_reference(u, delta, B, C, A_neg, h0=None):
         h = decay * h + inp
         ys.append(torch.sum(h * C[:, t, :, None, :], dim=-1))
     return torch.stack(ys, dim=1)
+
+
+def ssd_step(u, delta, B, C, A_neg, state):
+    """One decode step (no counterpart in the reference, where a step is a scan
+    of length 1): advances ``state`` [B, H, Dh, N] (float32, the final state's
+    layout) in place by one step of ``ssd.py:382-394`` and returns y [B, H, Dh]
+    float32. ``u`` [B, H, Dh], ``delta`` [B, H], ``B``/``C`` [B, H, N], ``A_neg``
+    [H, N]. Not differentiable."""
+    if u.dim() != 3:
+        raise ValueError(f"u must be [B, H, Dh], got shape {tuple(u.shape)}")
+    Bt, H, Dh = u.shape
+    if A_neg.dim() != 2 or A_neg.shape[0] != H:
+        raise ValueError(f"A_neg must be [H, N] = [{H}, N], got {tuple(A_neg.shape)}")
+    N = A_neg.shape[1]
+    if tuple(delta.shape) != (Bt, H):
+        raise ValueError(f"delta must be [B, H] = [{Bt}, {H}], got {tuple(delta.shape)}")
+    for name, t in (("B", B), ("C", C)):
+        if tuple(t.shape) != (Bt, H, N):
+            raise ValueError(f"{name} must be [B, H, N] = [{Bt}, {H}, {N}], got {tuple(t.shape)}")
+    dev = _lib.require_cuda(u, delta, B, C, A_neg, state)
+    state = step_state(state, (Bt, H, Dh, N), dev)
+    dt = common_dtype(u, delta, B, C)
+    u_, d_, B_, C_ = (prep(t.detach(), dt) for t in (u, delta, B, C))
+    A32, ash, asn = _a_f32(A_neg.detach())
+    y = torch.empty((Bt, H, Dh), dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        _lib.call("mr_ssd_step", _lib.ptr(u_), _lib.ptr(d_), _lib.ptr(B_), _lib.ptr(C_), _lib.ptr(A32), ash,
+                  asn, _lib.DTYPE_CODE[dt], Bt, H, Dh, N, _lib.ptr(state), _lib.ptr(y), _lib.stream_of(dev))
+    return y
