@@ -75,6 +75,9 @@ def algorithmic_bytes(cfg, batch):
     elif k == "rglru":
         inp = B * L * cfg["D"] * 2 * es
         y = B * L * cfg["D"] * 4
+    elif k == "rglru_gated":  # x, r, i (lam: one value per channel)
+        inp = B * L * cfg["D"] * 3 * es
+        y = B * L * cfg["D"] * 4
     else:
         Dp = cfg["Dp"]
         inp = B * L * Dp * 5 * es
@@ -199,7 +202,7 @@ def cpu_sample(name):
         ins = [t[:, :, :hs] if t.dim() >= 3 else t[:hs] for t in ins]
         frac = hs / (cfg["B"] * cfg["H"])
         desc = f"1 batch row x {hs} of {cfg['H']} heads (full L), scaled by units"
-    elif k in ("rglru", "rotlru") and cfg["B"] > 1 and cfg["B"] * cfg["L"] > 2 ** 15:
+    elif k in ("rglru", "rglru_gated", "rotlru") and cfg["B"] > 1 and cfg["B"] * cfg["L"] > 2 ** 15:
         nb = 1
         ins = W.make_inputs(name, "cpu", seed=1000, batch=nb)
         frac = nb / cfg["B"]
@@ -215,6 +218,15 @@ def cpu_sample(name):
     return ins, gy, frac, desc
 
 
+def _cpu_run(c_oracle, W, cfg, ins, gy):
+    """One forward+backward of the C restatement; for the gated RG-LRU the
+    reference's host-side gating (rglru.py:8-27) runs first, in numpy."""
+    if cfg["kind"] == "rglru_gated":
+        a, b = W.gated_to_plain(*ins)
+        return c_oracle.run("rglru", [a, b], cfg["seg"], gy=gy)
+    return c_oracle.run(cfg["kind"], ins, cfg["seg"], gy=gy)
+
+
 def cpu_baseline(name, reps=1):
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import c_oracle  # float32 C restatement (test infrastructure)
@@ -222,11 +234,11 @@ def cpu_baseline(name, reps=1):
     cfg = W.CONFIGS[name]
     ins, gy, frac, desc = cpu_sample(name)
     c_oracle.lib()
-    c_oracle.run(cfg["kind"], ins, cfg["seg"], gy=gy)  # warm-up
+    _cpu_run(c_oracle, W, cfg, ins, gy)  # warm-up
     times = []
     for _ in range(reps):
         t0 = time.perf_counter()
-        c_oracle.run(cfg["kind"], ins, cfg["seg"], gy=gy)
+        _cpu_run(c_oracle, W, cfg, ins, gy)
         times.append(time.perf_counter() - t0)
     t = statistics.median(times)
     tok = W.tokens(cfg) * frac
@@ -446,10 +458,10 @@ def run_reference(args):
     ins, gy, frac, desc = cpu_sample(name)
     c_oracle.lib()
     for _ in range(args.warmup):
-        c_oracle.run(cfg["kind"], ins, cfg["seg"], gy=gy)
+        _cpu_run(c_oracle, W, cfg, ins, gy)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        c_oracle.run(cfg["kind"], ins, cfg["seg"], gy=gy)
+        _cpu_run(c_oracle, W, cfg, ins, gy)
     dt = time.perf_counter() - t0
     tok = W.tokens(cfg) * frac
     v = tok * args.steps / dt
@@ -483,7 +495,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--config", default="c4", choices=["c0", "c1", "c2", "c3", "c4", "c5"])
+    ap.add_argument("--config", default="c4", choices=["c0", "c1", "c2", "c3", "c4", "c5", "c2g"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffer) timing")

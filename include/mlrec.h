@@ -245,6 +245,25 @@ MR_API int mr_rotlru_bwd_h0(const float* grad_y, const float* grad_final, const 
                             void* workspace, size_t workspace_bytes, const float* h0, float* grad_h0,
                             void* stream);
 
+/* ------------------------------------------------------ gated RG-LRU ---
+ * The RG-LRU scan with its input gating folded in (no counterpart in the
+ * reference, which leaves the gating to MLX host code, rglru.py:8-27, and
+ * takes a, b through HBM): inputs x, r (activated recurrence gate), i
+ * (activated input gate) [B,L,D] in `dtype` and lam [D] float32;
+ *   a_t = sigmoid(lam)^(c r_t),  b_t = sqrt(1 - a_t^2) i_t x_t,
+ *   h_t = a_t h_{t-1} + b_t,     y_t = h_t.
+ * y, h_ckpt, h0 as in mr_rglru_fwd(_h0). The backward returns the gradients of
+ * x, r, i (in `dtype`) and of lam (float32 [D], summed over batch and time). */
+MR_API int mr_rglru_gated_fwd(const void* x, const void* r, const void* i, const float* lam, float c, int dtype,
+                              int64_t batch, int64_t L, int64_t D, int64_t seg, float* y, float* h_ckpt,
+                              const float* h0, void* stream);
+MR_API size_t mr_rglru_gated_bwd_workspace_bytes(int dtype, int64_t batch, int64_t L, int64_t D, int64_t seg);
+MR_API int mr_rglru_gated_bwd(const float* grad_y, const float* grad_final, const float* h_ckpt, const void* x,
+                              const void* r, const void* i, const float* lam, float c, int dtype, int64_t batch,
+                              int64_t L, int64_t D, int64_t seg, void* grad_x, void* grad_r, void* grad_i,
+                              float* grad_lam, void* workspace, size_t workspace_bytes, const float* h0,
+                              float* grad_h0, void* stream);
+
 /* -------------------------------------------------------- decode steps ---
  * No counterpart in the reference (a decode step there is a scan of length 1,
  * one Metal dispatch per call). One time step of the recurrence for a batch of

@@ -9,7 +9,8 @@ torch.autograd.Functions over a C-ABI library of sm_100a CUDA kernels
     rotlru  - rotational LRU (complex-diagonal over interleaved pairs)
 
 Beyond the reference: an optional initial state ``h0=`` on every scan
-(chunked prefill) and one-token decode steps ``*_step`` on a state cache.
+(chunked prefill), one-token decode steps ``*_step`` on a state cache, and
+``rglru_scan_gated`` with the RG-LRU input gating inside the kernels.
 
 Import with ``importlib.import_module("mlx-recurrence_b200")`` (the directory
 name carries a hyphen); after that the package is also registered as
@@ -20,7 +21,8 @@ import sys as _sys
 
 from ._chassis import DEFAULT_SEG, check_segment_shape, get_or_build_kernel, parity_check
 from .gla import gla_scan, gla_scan_reference, gla_scan_with_state, gla_step
-from .rglru import rglru_scan, rglru_scan_reference, rglru_scan_with_state, rglru_step
+from .rglru import (rglru_scan, rglru_scan_gated, rglru_scan_gated_with_state, rglru_scan_reference,
+                    rglru_scan_with_state, rglru_step)
 from .rotlru import rotlru_scan, rotlru_scan_reference, rotlru_scan_with_state, rotlru_step
 from .ssd import ssd_scan, ssd_scan_reference, ssd_scan_with_state, ssd_step
 
@@ -37,6 +39,9 @@ __all__ = [
     "rotlru_scan",
     "rotlru_scan_with_state",
     "rotlru_scan_reference",
+    # the RG-LRU scan with its input gating in the kernels (not in the reference)
+    "rglru_scan_gated",
+    "rglru_scan_gated_with_state",
     # one-token decode steps on a float32 state cache (not in the reference)
     "ssd_step",
     "gla_step",

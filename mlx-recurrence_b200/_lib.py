@@ -74,6 +74,11 @@ SIGNATURES = {
     "mr_rotlru_fwd_h0": (_int, [_p, _p, _p, _p, _int, _i64, _i64, _i64, _i64, _p, _p, _p, _p]),
     "mr_rotlru_bwd_h0": (_int, [_p, _p, _p, _p, _p, _p, _p, _int, _i64, _i64, _i64, _i64, _p, _p, _p, _p,
                                 _p, _sz, _p, _p, _p]),
+    # the RG-LRU scan with its input gating folded in
+    "mr_rglru_gated_fwd": (_int, [_p, _p, _p, _p, ctypes.c_float, _int, _i64, _i64, _i64, _i64, _p, _p, _p, _p]),
+    "mr_rglru_gated_bwd_workspace_bytes": (_sz, [_int, _i64, _i64, _i64, _i64]),
+    "mr_rglru_gated_bwd": (_int, [_p, _p, _p, _p, _p, _p, _p, ctypes.c_float, _int, _i64, _i64, _i64, _i64, _p,
+                                  _p, _p, _p, _p, _sz, _p, _p, _p]),
     # one-token decode steps (state advanced in place)
     "mr_ssd_step": (_int, [_p, _p, _p, _p, _p, _i64, _i64, _int, _i64, _i64, _i64, _i64, _p, _p, _p]),
     "mr_gla_step": (_int, [_p, _p, _p, _p, _int, _i64, _i64, _i64, _p, _p, _p]),

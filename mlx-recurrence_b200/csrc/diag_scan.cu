@@ -79,21 +79,43 @@ struct BlockMap {
 // RG-LRU forward
 // ============================================================================
 
-template <typename T, int W, int TB, int S>
-struct RgFwdSmem {
-  static constexpr size_t bytes = (size_t)2 * S * TB * W * sizeof(T) + 2 * 2 * kWarps * W * 4 + S * 8;
+// Input gating folded into the RG-LRU kernels (kG): the stored inputs are x,
+// r, i (three tiles) and a per-channel Lambda, and the scan's gate and input
+// are formed on load, a_t = sigmoid(Lambda)^(c r_t), b_t = sqrt(1 - a_t^2) i_t x_t
+// (the prologue the reference leaves to MLX host code, rglru.py:8-27; with r
+// the activated recurrence gate this is Griffin's exp(-c softplus(-Lambda) r_t)).
+struct RgGate {
+  const float* lam;  // [D] Lambda
+  float c;           // the gate exponent scale
 };
 
-template <typename T, int W, int TB, int S, bool kH0>
+// log sigmoid(x), stable for either sign
+__device__ __forceinline__ float log_sigmoid(float x) { return x >= 0.f ? -log1pf(expf(-x)) : x - log1pf(expf(x)); }
+
+// a = exp(z) (z = c r log sigmoid(Lambda) <= 0) and s = sqrt(1 - a^2), with
+// 1 - a^2 = (1 - a)(1 + a) and 1 - a = -expm1(z): no cancellation as a -> 1
+__device__ __forceinline__ void rg_gate(float z, float& a, float& s) {
+  a = expf(z);
+  s = sqrtf(fmaxf(-expm1f(z) * (1.f + a), 0.f));
+}
+
+template <typename T, int W, int TB, int S, int NIN>
+struct RgFwdSmem {
+  static constexpr size_t bytes = (size_t)NIN * S * TB * W * sizeof(T) + 2 * 2 * kWarps * W * 4 + S * 8;
+};
+
+template <typename T, int W, int TB, int S, bool kH0, bool kG>
 __global__ void __launch_bounds__(kThreads, 3)
 rglru_fwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_x,
-                 int L, int64_t D, int seg, float* __restrict__ y, float* __restrict__ ckpt,
-                 const float* __restrict__ h0) {
-  constexpr int V = W / 32, TW = TB / kWarps;
+                 const __grid_constant__ CUtensorMap tm_i, RgGate gate, int L, int64_t D, int seg,
+                 float* __restrict__ y, float* __restrict__ ckpt, const float* __restrict__ h0) {
+  // kG: tm_a, tm_x, tm_i map x, r, i; else a and x (tm_i unused)
+  constexpr int V = W / 32, TW = TB / kWarps, NIN = kG ? 3 : 2;
   extern __shared__ __align__(128) unsigned char smem[];
   T* sa = reinterpret_cast<T*>(smem);
   T* sx = sa + S * TB * W;
-  float* sA = reinterpret_cast<float*>(sx + S * TB * W);
+  T* si = sx + S * TB * W;  // kG only
+  float* sA = reinterpret_cast<float*>(sa + NIN * S * TB * W);
   float* sH = sA + 2 * kWarps * W;
   uint64_t* bar = reinterpret_cast<uint64_t*>(sH + 2 * kWarps * W);
 
@@ -115,9 +137,10 @@ rglru_fwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
 
   auto issue = [&](int blk) {  // one thread: a [TB x W] box per input
     const int s = blk % S, row = (int)(b * L) + blk * TB;
-    mbar_arrive_expect_tx(&bar[s], 2u * TB * W * sizeof(T));
+    mbar_arrive_expect_tx(&bar[s], (uint32_t)NIN * TB * W * sizeof(T));
     tma_load_2d(sa + s * TB * W, &tm_a, (int)c0, row, &bar[s]);
     tma_load_2d(sx + s * TB * W, &tm_x, (int)c0, row, &bar[s]);
+    if constexpr (kG) tma_load_2d(si + s * TB * W, &tm_i, (int)c0, row, &bar[s]);
   };
   if (threadIdx.x == 0)
     for (int k = 0; k < S - 1 && k < nblk; ++k) issue(k);
@@ -125,6 +148,9 @@ rglru_fwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
   float carry[V];  // the state before the block: h0 [B, D] or zero
 #pragma unroll
   for (int v = 0; v < V; ++v) carry[v] = (kH0 && act) ? h0[b * D + c0 + cl + v] : 0.f;
+  float cl2[V];  // kG: c log sigmoid(Lambda) of the lane's channels
+#pragma unroll
+  for (int v = 0; v < V; ++v) cl2[v] = (kG && act) ? gate.c * log_sigmoid(gate.lam[c0 + cl + v]) : 0.f;
 
   for (int blk = 0; blk < nblk; ++blk) {
     const int s = blk % S;
@@ -141,10 +167,21 @@ rglru_fwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
       const bool ok = t0 + i < L;
       const Vec<T, V> va = ld_vec<T, V>(ra + i * W);
       const Vec<T, V> vx = ld_vec<T, V>(rx + i * W);
+      if constexpr (kG) {  // (va, vx, vi) = (x, r, i)
+        const Vec<T, V> vi = ld_vec<T, V>(si + (s * TB + r0) * W + cl + i * W);
 #pragma unroll
-      for (int v = 0; v < V; ++v) {
-        fa[i][v] = ok ? to_f(va.v[v]) : 1.f;
-        fx[i][v] = ok ? to_f(vx.v[v]) : 0.f;
+        for (int v = 0; v < V; ++v) {
+          float av, sv;
+          rg_gate(cl2[v] * to_f(vx.v[v]), av, sv);
+          fa[i][v] = ok ? av : 1.f;
+          fx[i][v] = ok ? sv * to_f(vi.v[v]) * to_f(va.v[v]) : 0.f;
+        }
+      } else {
+#pragma unroll
+        for (int v = 0; v < V; ++v) {
+          fa[i][v] = ok ? to_f(va.v[v]) : 1.f;
+          fx[i][v] = ok ? to_f(vx.v[v]) : 0.f;
+        }
       }
     }
 #pragma unroll
@@ -208,24 +245,29 @@ rglru_fwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
 // RG-LRU backward
 // ============================================================================
 
-template <typename T, int W, int TB, int S>
+template <typename T, int W, int TB, int S, int NIN>
 struct RgBwdSmem {
   static constexpr size_t bytes =
-      (size_t)S * TB * W * (2 * sizeof(T) + 4) + 4 * 2 * kWarps * W * 4 + S * 8;
+      (size_t)S * TB * W * (NIN * sizeof(T) + 4) + 4 * 2 * kWarps * W * 4 + S * 8;
 };
 
-template <typename T, int W, int TB, int S, bool kH0>
-__global__ void __launch_bounds__(kThreads, 3)
+// kG: the inputs (a, x, ig) are (x, r, i) and the gradients (ga, gx, gi) are those
+// of (x, r, i); glam_part [B, D] receives each batch row's d loss / d Lambda.
+template <typename T, int W, int TB, int S, bool kH0, bool kG>
+__global__ void __launch_bounds__(kThreads, kG ? 2 : 3)  // gated: 2 CTAs per SM by shared memory anyway
 rglru_bwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_x,
-                 const __grid_constant__ CUtensorMap tm_g, const float* __restrict__ gfinal,
-                 const float* __restrict__ ckpt, const T* __restrict__ a, const T* __restrict__ x,
-                 int L, int64_t D, int seg, T* __restrict__ ga, T* __restrict__ gx,
-                 float* __restrict__ ws, const float* __restrict__ h0, float* __restrict__ gh0) {
-  constexpr int V = W / 32, TW = TB / kWarps;
+                 const __grid_constant__ CUtensorMap tm_g, const __grid_constant__ CUtensorMap tm_i,
+                 RgGate gate, const float* __restrict__ gfinal, const float* __restrict__ ckpt,
+                 const T* __restrict__ a, const T* __restrict__ x, const T* __restrict__ ig, int L, int64_t D,
+                 int seg, T* __restrict__ ga, T* __restrict__ gx, T* __restrict__ gi,
+                 float* __restrict__ glam_part, float* __restrict__ ws, const float* __restrict__ h0,
+                 float* __restrict__ gh0) {
+  constexpr int V = W / 32, TW = TB / kWarps, NIN = kG ? 3 : 2;
   extern __shared__ __align__(128) unsigned char smem[];
   T* sa = reinterpret_cast<T*>(smem);
   T* sx = sa + S * TB * W;
-  float* sg = reinterpret_cast<float*>(sx + S * TB * W);
+  T* si = sx + S * TB * W;  // kG only
+  float* sg = reinterpret_cast<float*>(sa + NIN * S * TB * W);
   float* sA = sg + S * TB * W;
   float* sH = sA + 2 * kWarps * W;
   float* sR = sH + 2 * kWarps * W;
@@ -255,9 +297,10 @@ rglru_bwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
     int t0, nt, j;
     bm.range(bm.nq - 1 - p, t0, nt, j);
     const int row = (int)(b * L) + t0;
-    mbar_arrive_expect_tx(&bar[s], (uint32_t)TB * W * (2u * sizeof(T) + 4u));
+    mbar_arrive_expect_tx(&bar[s], (uint32_t)TB * W * (NIN * (uint32_t)sizeof(T) + 4u));
     tma_load_2d(sa + s * TB * W, &tm_a, (int)c0, row, &bar[s]);
     tma_load_2d(sx + s * TB * W, &tm_x, (int)c0, row, &bar[s]);
+    if constexpr (kG) tma_load_2d(si + s * TB * W, &tm_i, (int)c0, row, &bar[s]);
     tma_load_2d(sg + s * TB * W, &tm_g, (int)c0, row, &bar[s]);
   };
   if (threadIdx.x == 0)
@@ -266,6 +309,21 @@ rglru_bwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
   float cr[V];
 #pragma unroll
   for (int v = 0; v < V; ++v) cr[v] = (gfinal != nullptr && act) ? gfinal[b * D + c0 + cl + v] : 0.f;
+  // kG: c log sigmoid(Lambda), c (1 - sigmoid(Lambda)) and the d loss / d Lambda sum of the lane
+  float cl2[V], klam[V], glam[V];
+#pragma unroll
+  for (int v = 0; v < V; ++v) {
+    const float lm = (kG && act) ? gate.lam[c0 + cl + v] : 0.f;
+    cl2[v] = kG ? gate.c * log_sigmoid(lm) : 0.f;
+    klam[v] = kG ? gate.c / (1.f + expf(lm)) : 0.f;  // c (1 - sigmoid(Lambda)) = c sigmoid(-Lambda)
+    glam[v] = 0.f;
+  }
+  // kG: the scan's gate and input from (x, r, i) at global offset o of the lane's channel v
+  auto gated_ab = [&](int64_t o, int v, float& av, float& bv) {
+    float sv;
+    rg_gate(cl2[v] * to_f(x[o]), av, sv);
+    bv = sv * to_f(ig[o]) * to_f(a[o]);
+  };
   int it = 0;  // exchange-buffer parity
 
   for (int p = 0; p < bm.nq; ++p) {
@@ -292,8 +350,15 @@ rglru_bwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
 #pragma unroll
           for (int i = 0; i < TW; ++i) {
             if (act && t0 + i < tend) {
-              const float av = to_f(a[gbase + (int64_t)(t0 + i) * D + cl + v]);
-              H = av * H + to_f(x[gbase + (int64_t)(t0 + i) * D + cl + v]);
+              const int64_t o = gbase + (int64_t)(t0 + i) * D + cl + v;
+              float av, bv;
+              if constexpr (kG) {
+                gated_ab(o, v, av, bv);
+              } else {
+                av = to_f(a[o]);
+                bv = to_f(x[o]);
+              }
+              H = av * H + bv;
               A = av * A;
             }
           }
@@ -323,6 +388,7 @@ rglru_bwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
     const T* rx = sx + (s * TB + r0) * W + cl;
     const float* rg = sg + (s * TB + r0) * W + cl;
 
+    const T* ri = si + (s * TB + r0) * W + cl;  // kG: i
     float fa[TW][V], fx[TW][V], fg[TW][V];
 #pragma unroll
     for (int i = 0; i < TW; ++i) {
@@ -330,11 +396,23 @@ rglru_bwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
       const Vec<T, V> va = ld_vec<T, V>(ra + i * W);
       const Vec<T, V> vx = ld_vec<T, V>(rx + i * W);
       const Vec<float, V> vg = ld_vec<float, V>(rg + i * W);
+      if constexpr (kG) {  // (va, vx, vi) = (x, r, i)
+        const Vec<T, V> vi = ld_vec<T, V>(ri + i * W);
 #pragma unroll
-      for (int v = 0; v < V; ++v) {
-        fa[i][v] = ok ? to_f(va.v[v]) : 1.f;
-        fx[i][v] = ok ? to_f(vx.v[v]) : 0.f;
-        fg[i][v] = ok ? vg.v[v] : 0.f;
+        for (int v = 0; v < V; ++v) {
+          float av, sv;
+          rg_gate(cl2[v] * to_f(vx.v[v]), av, sv);
+          fa[i][v] = ok ? av : 1.f;
+          fx[i][v] = ok ? sv * to_f(vi.v[v]) * to_f(va.v[v]) : 0.f;
+          fg[i][v] = ok ? vg.v[v] : 0.f;
+        }
+      } else {
+#pragma unroll
+        for (int v = 0; v < V; ++v) {
+          fa[i][v] = ok ? to_f(va.v[v]) : 1.f;
+          fx[i][v] = ok ? to_f(vx.v[v]) : 0.f;
+          fg[i][v] = ok ? vg.v[v] : 0.f;
+        }
       }
     }
     float hs[V];
@@ -406,12 +484,48 @@ rglru_bwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
         o_a[v] = adj * hp[i][v];
         crin[v] = adj * fa[i][v];
       }
-      if (act && t < tend) {
+      if constexpr (kG) {
+        // chain through b = sqrt(1 - a^2) i x and a = exp(c log sigmoid(Lambda) r):
+        // grads of x, r, i and the Lambda sum (out of range steps have adj = 0)
+        const Vec<T, V> vxx = ld_vec<T, V>(ra + i * W), vr = ld_vec<T, V>(rx + i * W), vi = ld_vec<T, V>(ri + i * W);
+        float o_gx[V], o_gr[V], o_gi[V];
+#pragma unroll
+        for (int v = 0; v < V; ++v) {
+          const float xx = to_f(vxx.v[v]), rr = to_f(vr.v[v]), ii = to_f(vi.v[v]);
+          float av, sg_;
+          rg_gate(cl2[v] * rr, av, sg_);
+          o_gx[v] = o_x[v] * sg_ * ii;
+          o_gi[v] = o_x[v] * sg_ * xx;
+          const float gat = o_a[v] - (sg_ > 0.f ? o_x[v] * ii * xx * av / sg_ : 0.f);
+          o_gr[v] = gat * cl2[v] * av;
+          if (t < tend) glam[v] += gat * rr * av * klam[v];
+        }
+        if (act && t < tend) {
+          const int64_t o = gbase + (int64_t)t * D + cl;
+          st_vec<T, V>(ga + o, o_gx);
+          st_vec<T, V>(gx + o, o_gr);
+          st_vec<T, V>(gi + o, o_gi);
+        }
+      } else if (act && t < tend) {
         const int64_t o = gbase + (int64_t)t * D + cl;
         st_vec<T, V>(gx + o, o_x);
         st_vec<T, V>(ga + o, o_a);
       }
     }
+  }
+  if constexpr (kG) {  // the CTA's d loss / d Lambda: a sum over its warps' steps
+    __syncthreads();
+#pragma unroll
+    for (int v = 0; v < V; ++v) sA[warp * W + cl + v] = glam[v];
+    __syncthreads();
+    if (warp == 0 && act)
+#pragma unroll
+      for (int v = 0; v < V; ++v) {
+        float acc = 0.f;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) acc += sA[w * W + cl + v];
+        glam_part[b * D + c0 + cl + v] = acc;
+      }
   }
   // the reverse carry past step 0 is the gradient of the initial state
   if (kH0 && gh0 != nullptr && act)
@@ -861,40 +975,94 @@ static int tmap_rows(CUtensorMap* m, const void* base, int64_t rows, int64_t col
                       (uint64_t)cols * sizeof(T), (uint32_t)W, (uint32_t)TB);
 }
 
+// kG: (a, x, ig) are (x, r, i) with the gate in `gate`; else ig is unused
+template <typename T, bool kG>
+static int rglru_fwd_any(const void* a, const void* x, const void* ig, RgGate gate, int64_t batch, int64_t L,
+                         int64_t D, int64_t seg, float* y, float* ckpt, const float* h0, cudaStream_t st) {
+  using C = DiagCfg<T>;
+  // three input tiles per stage when gated: one stage fewer keeps three CTAs per SM (bf16)
+  constexpr int W = C::RgFW, TB = C::RgFTB, S = kG && C::RgFS > 3 ? 3 : C::RgFS;
+  constexpr size_t sm = RgFwdSmem<T, W, TB, S, kG ? 3 : 2>::bytes;
+  CUtensorMap ma, mx, mi;
+  if (int rc = tmap_rows<T>(&ma, a, batch * L, D, W, TB)) return rc;
+  if (int rc = tmap_rows<T>(&mx, x, batch * L, D, W, TB)) return rc;
+  if (int rc = tmap_rows<T>(&mi, kG ? ig : a, batch * L, D, W, TB)) return rc;
+  // an initial state selects its own instantiation (the common case's code stays as it was)
+  auto k = h0 != nullptr ? rglru_fwd_kernel<T, W, TB, S, true, kG> : rglru_fwd_kernel<T, W, TB, S, false, kG>;
+  if (int rc = set_smem(k, sm)) return rc;
+  dim3 grid((unsigned)((D + W - 1) / W), (unsigned)batch);
+  k<<<grid, kThreads, sm, st>>>(ma, mx, mi, gate, (int)L, D, (int)seg, y, ckpt, h0);
+  return check_launch("rglru_fwd_kernel");
+}
+
 template <typename T>
 int rglru_fwd_launch(const void* a, const void* x, int64_t batch, int64_t L, int64_t D, int64_t seg,
                      float* y, float* ckpt, const float* h0, cudaStream_t st) {
+  return rglru_fwd_any<T, false>(a, x, nullptr, RgGate{nullptr, 0.f}, batch, L, D, seg, y, ckpt, h0, st);
+}
+
+template <typename T>
+int rglru_gated_fwd_launch(const void* x, const void* r, const void* i, const float* lam, float c, int64_t batch,
+                           int64_t L, int64_t D, int64_t seg, float* y, float* ckpt, const float* h0,
+                           cudaStream_t st) {
+  return rglru_fwd_any<T, true>(x, r, i, RgGate{lam, c}, batch, L, D, seg, y, ckpt, h0, st);
+}
+
+// d loss / d Lambda [D] = sum over batch rows of the per-row partials [B, D]
+__global__ void lambda_sum_kernel(const float* __restrict__ part, int64_t batch, int64_t D,
+                                  float* __restrict__ glam) {
+  const int64_t d = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (d >= D) return;
+  float acc = 0.f;
+  for (int64_t b = 0; b < batch; ++b) acc += part[b * D + d];
+  glam[d] = acc;
+}
+
+template <typename T, bool kG>
+static int rglru_bwd_any(const float* gy, const float* gf, const float* ckpt, const void* a, const void* x,
+                         const void* ig, RgGate gate, int64_t batch, int64_t L, int64_t D, int64_t seg, void* ga,
+                         void* gx, void* gi, float* glam_part, float* ws, const float* h0, float* gh0,
+                         cudaStream_t st) {
   using C = DiagCfg<T>;
-  constexpr int W = C::RgFW, TB = C::RgFTB, S = C::RgFS;
-  constexpr size_t sm = RgFwdSmem<T, W, TB, S>::bytes;
-  CUtensorMap ma, mx;
+  constexpr int W = C::RgBW, TB = C::RgBTB, S = C::RgBS;
+  constexpr size_t sm = RgBwdSmem<T, W, TB, S, kG ? 3 : 2>::bytes;
+  CUtensorMap ma, mx, mg, mi;
   if (int rc = tmap_rows<T>(&ma, a, batch * L, D, W, TB)) return rc;
   if (int rc = tmap_rows<T>(&mx, x, batch * L, D, W, TB)) return rc;
-  // an initial state selects its own instantiation (the common case's code stays as it was)
-  auto k = h0 != nullptr ? rglru_fwd_kernel<T, W, TB, S, true> : rglru_fwd_kernel<T, W, TB, S, false>;
+  if (int rc = tmap_rows<float>(&mg, gy, batch * L, D, W, TB)) return rc;
+  if (int rc = tmap_rows<T>(&mi, kG ? ig : a, batch * L, D, W, TB)) return rc;
+  auto k = h0 != nullptr ? rglru_bwd_kernel<T, W, TB, S, true, kG> : rglru_bwd_kernel<T, W, TB, S, false, kG>;
   if (int rc = set_smem(k, sm)) return rc;
   dim3 grid((unsigned)((D + W - 1) / W), (unsigned)batch);
-  k<<<grid, kThreads, sm, st>>>(ma, mx, (int)L, D, (int)seg, y, ckpt, h0);
-  return check_launch("rglru_fwd_kernel");
+  k<<<grid, kThreads, sm, st>>>(ma, mx, mg, mi, gate, gf, ckpt, (const T*)a, (const T*)x, (const T*)ig, (int)L, D,
+                                (int)seg, (T*)ga, (T*)gx, (T*)gi, glam_part, ws, h0, gh0);
+  return check_launch("rglru_bwd_kernel");
 }
 
 template <typename T>
 int rglru_bwd_launch(const float* gy, const float* gf, const float* ckpt, const void* a, const void* x,
                      int64_t batch, int64_t L, int64_t D, int64_t seg, void* ga, void* gx, float* ws,
                      const float* h0, float* gh0, cudaStream_t st) {
-  using C = DiagCfg<T>;
-  constexpr int W = C::RgBW, TB = C::RgBTB, S = C::RgBS;
-  constexpr size_t sm = RgBwdSmem<T, W, TB, S>::bytes;
-  CUtensorMap ma, mx, mg;
-  if (int rc = tmap_rows<T>(&ma, a, batch * L, D, W, TB)) return rc;
-  if (int rc = tmap_rows<T>(&mx, x, batch * L, D, W, TB)) return rc;
-  if (int rc = tmap_rows<float>(&mg, gy, batch * L, D, W, TB)) return rc;
-  auto k = h0 != nullptr ? rglru_bwd_kernel<T, W, TB, S, true> : rglru_bwd_kernel<T, W, TB, S, false>;
-  if (int rc = set_smem(k, sm)) return rc;
-  dim3 grid((unsigned)((D + W - 1) / W), (unsigned)batch);
-  k<<<grid, kThreads, sm, st>>>(ma, mx, mg, gf, ckpt, (const T*)a, (const T*)x, (int)L, D, (int)seg,
-                                (T*)ga, (T*)gx, ws, h0, gh0);
-  return check_launch("rglru_bwd_kernel");
+  return rglru_bwd_any<T, false>(gy, gf, ckpt, a, x, nullptr, RgGate{nullptr, 0.f}, batch, L, D, seg, ga, gx,
+                                 nullptr, nullptr, ws, h0, gh0, st);
+}
+
+// workspace: the plain backward's (long segments), then the [B, D] Lambda partials
+size_t rglru_gated_bwd_ws_bytes(int64_t batch, int64_t L, int64_t D, int64_t seg) {
+  return (rglru_bwd_ws_bytes(batch, L, D, seg) + 255) / 256 * 256 + (size_t)batch * D * sizeof(float);
+}
+
+template <typename T>
+int rglru_gated_bwd_launch(const float* gy, const float* gf, const float* ckpt, const void* x, const void* r,
+                           const void* i, const float* lam, float c, int64_t batch, int64_t L, int64_t D,
+                           int64_t seg, void* gx, void* gr, void* gi, float* glam, void* ws, const float* h0,
+                           float* gh0, cudaStream_t st) {
+  float* part = (float*)((char*)ws + (rglru_bwd_ws_bytes(batch, L, D, seg) + 255) / 256 * 256);
+  if (int rc = rglru_bwd_any<T, true>(gy, gf, ckpt, x, r, i, RgGate{lam, c}, batch, L, D, seg, gx, gr, gi, part,
+                                      (float*)ws, h0, gh0, st))
+    return rc;
+  lambda_sum_kernel<<<(unsigned)((D + 255) / 256), 256, 0, st>>>(part, batch, D, glam);
+  return check_launch("lambda_sum_kernel");
 }
 
 template <typename T>
@@ -948,6 +1116,13 @@ int rotlru_bwd_launch(const float* gy, const float* gf, const float* ckpt, const
   template int rotlru_fwd_launch<T>(const void*, const void*, const void*, const void*, int64_t,   \
                                     int64_t, int64_t, int64_t, float*, float*, const float*,       \
                                     cudaStream_t);                                                 \
+  template int rglru_gated_fwd_launch<T>(const void*, const void*, const void*, const float*, float, \
+                                         int64_t, int64_t, int64_t, int64_t, float*, float*,       \
+                                         const float*, cudaStream_t);                              \
+  template int rglru_gated_bwd_launch<T>(const float*, const float*, const float*, const void*,     \
+                                         const void*, const void*, const float*, float, int64_t,   \
+                                         int64_t, int64_t, int64_t, void*, void*, void*, float*,   \
+                                         void*, const float*, float*, cudaStream_t);               \
   template int rotlru_bwd_launch<T>(const float*, const float*, const float*, const void*,         \
                                     const void*, const void*, const void*, int64_t, int64_t,       \
                                     int64_t, int64_t, void*, void*, void*, void*, float*,          \

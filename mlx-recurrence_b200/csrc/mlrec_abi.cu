@@ -66,6 +66,9 @@ template <typename T> int ssd_step_launch(const void*, const void*, const void*,
 template <typename T> int gla_step_launch(const void*, const void*, const void*, const void*, int64_t, int64_t, int64_t, float*, float*, cudaStream_t);
 template <typename T> int rglru_step_launch(const void*, const void*, int64_t, int64_t, float*, float*, cudaStream_t);
 template <typename T> int rotlru_step_launch(const void*, const void*, const void*, const void*, int64_t, int64_t, float*, float*, cudaStream_t);
+template <typename T> int rglru_gated_fwd_launch(const void*, const void*, const void*, const float*, float, int64_t, int64_t, int64_t, int64_t, float*, float*, const float*, cudaStream_t);
+template <typename T> int rglru_gated_bwd_launch(const float*, const float*, const float*, const void*, const void*, const void*, const float*, float, int64_t, int64_t, int64_t, int64_t, void*, void*, void*, float*, void*, const float*, float*, cudaStream_t);
+size_t rglru_gated_bwd_ws_bytes(int64_t, int64_t, int64_t, int64_t);
 int umma_selftest_launch(const void*, const void*, const void*, const void*, float*, float*, float*,
                          cudaStream_t);
 
@@ -136,7 +139,8 @@ using namespace mr;
 
 extern "C" {
 
-int mr_abi_version(void) { return 3; }  // 2: the _h0 (initial state) entry points; 3: the decode steps
+// 2: the _h0 (initial state) entry points; 3: the decode steps; 4: the gated RG-LRU scan
+int mr_abi_version(void) { return 4; }
 
 const char* mr_last_error(void) { return g_err; }
 
@@ -217,6 +221,47 @@ int mr_rglru_bwd_h0(const float* grad_y, const float* grad_final, const float* h
   cudaStream_t st = (cudaStream_t)stream;
   MR_DTYPE_SWITCH(dtype, rglru_bwd_launch<T>(grad_y, grad_final, h_ckpt, a, x, batch, L, D, seg,
                                              grad_a, grad_x, (float*)workspace, h0, grad_h0, st));
+}
+
+int mr_rglru_gated_fwd(const void* x, const void* r, const void* i, const float* lam, float c, int dtype,
+                       int64_t batch, int64_t L, int64_t D, int64_t seg, float* y, float* h_ckpt, const float* h0,
+                       void* stream) {
+  g_err[0] = 0;
+  MR_TRY(check_dims("mr_rglru_gated_fwd", batch, L, D));
+  MR_TRY(check_seg(L, seg, D, "D"));
+  MR_TRY(check_dtype(dtype));
+  MR_TRY(check_ptrs("mr_rglru_gated_fwd", {x, r, i, lam, y, h_ckpt}));
+  MR_TRY(check_opt_ptr("mr_rglru_gated_fwd", h0));
+  cudaStream_t st = (cudaStream_t)stream;
+  MR_DTYPE_SWITCH(dtype, rglru_gated_fwd_launch<T>(x, r, i, lam, c, batch, L, D, seg, y, h_ckpt, h0, st));
+}
+
+size_t mr_rglru_gated_bwd_workspace_bytes(int dtype, int64_t batch, int64_t L, int64_t D, int64_t seg) {
+  (void)dtype;
+  if (batch <= 0 || L <= 0 || D <= 0 || seg <= 0) return 0;
+  return rglru_gated_bwd_ws_bytes(batch, L, D, seg);
+}
+
+int mr_rglru_gated_bwd(const float* grad_y, const float* grad_final, const float* h_ckpt, const void* x,
+                       const void* r, const void* i, const float* lam, float c, int dtype, int64_t batch, int64_t L,
+                       int64_t D, int64_t seg, void* grad_x, void* grad_r, void* grad_i, float* grad_lam,
+                       void* workspace, size_t workspace_bytes, const float* h0, float* grad_h0, void* stream) {
+  g_err[0] = 0;
+  MR_TRY(check_dims("mr_rglru_gated_bwd", batch, L, D));
+  MR_TRY(check_seg(L, seg, D, "D"));
+  MR_TRY(check_dtype(dtype));
+  MR_TRY(check_ptrs("mr_rglru_gated_bwd", {grad_y, h_ckpt, x, r, i, lam, grad_x, grad_r, grad_i, grad_lam}));
+  MR_TRY(check_opt_ptr("mr_rglru_gated_bwd", grad_final));
+  MR_TRY(check_opt_ptr("mr_rglru_gated_bwd", h0));
+  MR_TRY(check_opt_ptr("mr_rglru_gated_bwd", grad_h0));
+  const size_t need = rglru_gated_bwd_ws_bytes(batch, L, D, seg);
+  if (workspace == nullptr || workspace_bytes < need)
+    return set_error(MR_E_WORKSPACE, "mr_rglru_gated_bwd: workspace of %zu bytes required, got %zu", need,
+                     workspace_bytes);
+  MR_TRY(check_opt_ptr("mr_rglru_gated_bwd", workspace));
+  cudaStream_t st = (cudaStream_t)stream;
+  MR_DTYPE_SWITCH(dtype, rglru_gated_bwd_launch<T>(grad_y, grad_final, h_ckpt, x, r, i, lam, c, batch, L, D, seg,
+                                                   grad_x, grad_r, grad_i, grad_lam, workspace, h0, grad_h0, st));
 }
 
 // ------------------------------------------------------------------ rotLRU ---

@@ -119,3 +119,80 @@ def rglru_step(a, x, state):
         _lib.call("mr_rglru_step", _lib.ptr(a_), _lib.ptr(x_), _lib.DTYPE_CODE[dt], Bt, D, _lib.ptr(state),
                   _lib.ptr(y), _lib.stream_of(dev))
     return y
+
+
+class _RGLRUGatedScan(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, r, i, lam, c, seg, h0):
+        ctx.set_materialize_grads(False)
+        if x.dim() != 3 or r.shape != x.shape or i.shape != x.shape:
+            raise ValueError(f"x, r, i must all be [B, L, D], got {tuple(x.shape)}, {tuple(r.shape)}, "
+                             f"{tuple(i.shape)}")
+        Bt, L, D = x.shape
+        if tuple(lam.shape) != (D,):
+            raise ValueError(f"lam must be [D] = [{D}], got {tuple(lam.shape)}")
+        check_segment_shape(L, seg, D, "D")
+        dev = _lib.require_cuda(x, r, i, lam)
+        dt = common_dtype(x, r, i)
+        x_, r_, i_ = (prep(t, dt) for t in (x, r, i))
+        lam_ = lam.detach().to(torch.float32).contiguous()
+        h0_ = prep_h0(h0, (Bt, D), dev)
+        y = torch.empty((Bt, L, D), dtype=torch.float32, device=dev)
+        ckpt = torch.empty((Bt, L // seg, D), dtype=torch.float32, device=dev)
+        with torch.cuda.device(dev):
+            _lib.call("mr_rglru_gated_fwd", _lib.ptr(x_), _lib.ptr(r_), _lib.ptr(i_), _lib.ptr(lam_), float(c),
+                      _lib.DTYPE_CODE[dt], Bt, L, D, seg, _lib.ptr(y), _lib.ptr(ckpt), _lib.ptr(h0_),
+                      _lib.stream_of(dev))
+        ctx.save_for_backward(x_, r_, i_, lam_, ckpt, h0_)
+        ctx.seg, ctx.c = seg, float(c)
+        return y, ckpt[:, -1].clone()
+
+    @staticmethod
+    def backward(ctx, gy, gfinal):
+        x_, r_, i_, lam_, ckpt, h0_ = ctx.saved_tensors
+        Bt, L, D = x_.shape
+        dev = x_.device
+        code = _lib.DTYPE_CODE[x_.dtype]
+        gy = grad_out(gy, (Bt, L, D), dev)
+        gf = None if gfinal is None else gfinal.to(torch.float32).contiguous()
+        gx, gr, gi = (torch.empty_like(t) for t in (x_, r_, i_))
+        glam = torch.empty_like(lam_)
+        gh0 = torch.empty_like(h0_) if (h0_ is not None and ctx.needs_input_grad[6]) else None
+        with torch.cuda.device(dev):
+            lib = _lib.load()
+            nws = lib.mr_rglru_gated_bwd_workspace_bytes(code, Bt, L, D, ctx.seg)
+            ws = torch.empty(max(nws, 16), dtype=torch.uint8, device=dev)
+            _lib.call("mr_rglru_gated_bwd", _lib.ptr(gy), _lib.ptr(gf), _lib.ptr(ckpt), _lib.ptr(x_), _lib.ptr(r_),
+                      _lib.ptr(i_), _lib.ptr(lam_), ctx.c, code, Bt, L, D, ctx.seg, _lib.ptr(gx), _lib.ptr(gr),
+                      _lib.ptr(gi), _lib.ptr(glam), _lib.ptr(ws), ws.numel(), _lib.ptr(h0_), _lib.ptr(gh0),
+                      _lib.stream_of(dev))
+        return gx, gr, gi, glam, None, None, gh0
+
+
+def rglru_scan_gated(x, r, i, lam, c=8.0, seg=DEFAULT_SEG, h0=None):
+    """RG-LRU with its input gating folded into the scan kernels.
+
+    The reference computes the gate and the gated input in MLX host code ahead
+    of the scan (``rglru.py:8-27``) and passes ``a`` and ``b`` through memory;
+    here they are formed as the kernels load x, r and i:
+
+        a_t = sigmoid(lam)^(c r_t),  b_t = sqrt(1 - a_t^2) i_t x_t,  h_t = a_t h_{t-1} + b_t
+
+    Args:
+        x:   [B, L, D] input.
+        r:   [B, L, D] activated recurrence gate (in [0, 1]).
+        i:   [B, L, D] activated input gate.
+        lam: [D] per-channel Lambda (float32 state of the gate).
+        c:   gate exponent scale (8 in Griffin).
+        seg, h0: as in :func:`rglru_scan`.
+
+    Returns:
+        y:   [B, L, D] float32. Differentiable in x, r, i, lam and h0.
+    """
+    y, _ = _RGLRUGatedScan.apply(x, r, i, lam, c, seg, h0)
+    return y
+
+
+def rglru_scan_gated_with_state(x, r, i, lam, c=8.0, seg=DEFAULT_SEG, h0=None):
+    """:func:`rglru_scan_gated` that also returns the final state [B, D]."""
+    return _RGLRUGatedScan.apply(x, r, i, lam, c, seg, h0)

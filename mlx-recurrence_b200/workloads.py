@@ -23,6 +23,8 @@ CONFIGS = {
     "c4": dict(kind="ssd", B=32, L=16384, H=32, Dh=64, N=128, seg=32, dtype=torch.bfloat16),
     # the GLA shape of the target (SSD/GLA fwd+bwd at B=32, L=16384, H=32, Dh=64)
     "c5": dict(kind="gla", B=32, L=16384, H=32, Dh=64, seg=32, dtype=torch.bfloat16),
+    # c2 with the RG-LRU input gating inside the kernels (x, r, i, lam in; c = 8)
+    "c2g": dict(kind="rglru_gated", B=8, L=4096, D=2560, seg=32, dtype=torch.bfloat16),
 }
 
 DESCRIPTION = {
@@ -32,7 +34,10 @@ DESCRIPTION = {
     "c3": "rotlru_scan bf16 B=16 L=8192 D=2048 seg=32",
     "c4": "ssd_scan bf16 B=32 L=16384 H=32 Dh=64 N=128 seg=32",
     "c5": "gla_scan bf16 B=32 L=16384 H=32 Dh=64 seg=32",
+    "c2g": "rglru_scan_gated bf16 B=8 L=4096 D=2560 seg=32 (gating in the kernels, c=8)",
 }
+
+GATE_C = 8.0  # the RG-LRU gate exponent scale of c2 / c2g
 
 
 def tokens(cfg):
@@ -69,13 +74,15 @@ def make_inputs(name, device, seed=0, batch=None):
         v = torch.randn((B, L, H, Dh), **f32) * s
         g_ = torch.sigmoid(torch.randn((B, L, H), **f32) + 2.0)
         return tuple(t.to(dt) for t in (q, k, v, g_))
-    if cfg["kind"] == "rglru":
+    if cfg["kind"] in ("rglru", "rglru_gated"):
         D = cfg["D"]
         x = torch.randn((B, L, D), **f32)
         r = torch.sigmoid(torch.randn((B, L, D), **f32))
         i = torch.sigmoid(torch.randn((B, L, D), **f32))
         lam = torch.rand((D,), **f32) * (6.9 - 2.2) + 2.2
-        a = torch.sigmoid(lam) ** (8.0 * r)
+        if cfg["kind"] == "rglru_gated":
+            return (x.to(dt), r.to(dt), i.to(dt), lam)
+        a = torch.sigmoid(lam) ** (GATE_C * r)
         b = torch.sqrt(1.0 - a * a) * (i * x)
         return (a.to(dt), b.to(dt))
     if cfg["kind"] == "rotlru":
@@ -92,7 +99,7 @@ def output_shape(name, batch=None):
     B = cfg["B"] if batch is None else batch
     if cfg["kind"] in ("ssd", "gla"):
         return (B, cfg["L"], cfg["H"], cfg["Dh"])
-    if cfg["kind"] == "rglru":
+    if cfg["kind"] in ("rglru", "rglru_gated"):
         return (B, cfg["L"], cfg["D"])
     return (B, cfg["L"], 2 * cfg["Dp"])
 
@@ -100,5 +107,17 @@ def output_shape(name, batch=None):
 def scan_fn(pkg, name):
     kind = CONFIGS[name]["kind"]
     seg = CONFIGS[name]["seg"]
+    if kind == "rglru_gated":
+        return lambda *xs: pkg.rglru_scan_gated(*xs, GATE_C, seg=seg)
     f = getattr(pkg, f"{kind}_scan")
     return lambda *xs: f(*xs, seg=seg)
+
+
+def gated_to_plain(x, r, i, lam):
+    """numpy (x, r, i, lam) of c2g -> the (a, b) the plain RG-LRU scan takes
+    (the host-side prologue of rglru.py:8-27), for the CPU baselines."""
+    import numpy as np
+    ls = -np.logaddexp(0.0, -lam)
+    a = np.exp(GATE_C * r * ls)
+    b = np.sqrt(np.maximum(1.0 - a * a, 0.0)) * i * x
+    return a.astype(np.float32), b.astype(np.float32)

@@ -139,3 +139,33 @@ def test_h0_gradient_matches_finite_difference(kind):
         fd[i] = (np.sum(fwd(*ins, h0=hp.reshape(fshape))[0] * w) -
                  np.sum(fwd(*ins, h0=hm.reshape(fshape))[0] * w)) / (2 * eps)
     np.testing.assert_allclose(np.asarray(gh0).reshape(-1), fd, rtol=1e-6, atol=1e-8)
+
+
+def test_rglru_gated_gradients_match_finite_difference():
+    """The gated RG-LRU oracle (input gating ahead of the scan, rglru.py:8-27):
+    every gradient against central differences of <y, w> + <final, wf>."""
+    rng = np.random.default_rng(9)
+    Bt, T, D, c = 2, 5, 3, 8.0
+    x = rng.standard_normal((Bt, T, D))
+    r = rng.uniform(0.1, 0.9, (Bt, T, D))
+    i = rng.uniform(0.1, 0.9, (Bt, T, D))
+    lam = rng.uniform(2.2, 6.9, D)
+    h0 = rng.standard_normal((Bt, D))
+    w = rng.standard_normal((Bt, T, D))
+    wf = rng.standard_normal((Bt, D))
+
+    def loss(x_, r_, i_, lam_, h0_):
+        y, f = R.rglru_gated_forward(x_, r_, i_, lam_, c, h0=h0_)
+        return np.sum(y * w) + np.sum(f * wf)
+
+    grads = R.rglru_gated_backward(x, r, i, lam, c, w, wf, h0=h0)
+    args = [x, r, i, lam, h0]
+    eps = 1e-6
+    for k, g in enumerate(grads):
+        fd = np.zeros(args[k].size)
+        for j in range(args[k].size):
+            p, m = [a.copy() for a in args], [a.copy() for a in args]
+            p[k].reshape(-1)[j] += eps
+            m[k].reshape(-1)[j] -= eps
+            fd[j] = (loss(*p) - loss(*m)) / (2 * eps)
+        np.testing.assert_allclose(np.asarray(g).reshape(-1), fd, rtol=1e-5, atol=1e-7)
