@@ -92,11 +92,12 @@ struct RgGate {
 // log sigmoid(x), stable for either sign
 __device__ __forceinline__ float log_sigmoid(float x) { return x >= 0.f ? -log1pf(expf(-x)) : x - log1pf(expf(x)); }
 
-// a = exp(z) (z = c r log sigmoid(Lambda) <= 0) and s = sqrt(1 - a^2), with
-// 1 - a^2 = (1 - a)(1 + a) and 1 - a = -expm1(z): no cancellation as a -> 1
+// a = exp(z) (z = c r log sigmoid(Lambda) <= 0) and s = sqrt(1 - a^2) from one
+// e = expm1(z): a = 1 + e, 1 - a^2 = -e (2 + e), no cancellation as a -> 1
 __device__ __forceinline__ void rg_gate(float z, float& a, float& s) {
-  a = expf(z);
-  s = sqrtf(fmaxf(-expm1f(z) * (1.f + a), 0.f));
+  const float e = expm1f(z);
+  a = 1.f + e;
+  s = sqrtf(fmaxf(-e * (2.f + e), 0.f));
 }
 
 template <typename T, int W, int TB, int S, int NIN>
@@ -390,6 +391,7 @@ rglru_bwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
 
     const T* ri = si + (s * TB + r0) * W + cl;  // kG: i
     float fa[TW][V], fx[TW][V], fg[TW][V];
+    float fsg[kG ? TW : 1][V];  // kG: sqrt(1 - a^2) of each step
 #pragma unroll
     for (int i = 0; i < TW; ++i) {
       const bool ok = t0 + i < tend;
@@ -405,6 +407,7 @@ rglru_bwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
           fa[i][v] = ok ? av : 1.f;
           fx[i][v] = ok ? sv * to_f(vi.v[v]) * to_f(va.v[v]) : 0.f;
           fg[i][v] = ok ? vg.v[v] : 0.f;
+          fsg[i][v] = sv;
         }
       } else {
 #pragma unroll
@@ -492,8 +495,7 @@ rglru_bwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
 #pragma unroll
         for (int v = 0; v < V; ++v) {
           const float xx = to_f(vxx.v[v]), rr = to_f(vr.v[v]), ii = to_f(vi.v[v]);
-          float av, sg_;
-          rg_gate(cl2[v] * rr, av, sg_);
+          const float av = fa[i][v], sg_ = fsg[i][v];
           o_gx[v] = o_x[v] * sg_ * ii;
           o_gi[v] = o_x[v] * sg_ * xx;
           const float gat = o_a[v] - (sg_ > 0.f ? o_x[v] * ii * xx * av / sg_ : 0.f);
