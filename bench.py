@@ -78,6 +78,10 @@ def algorithmic_bytes(cfg, batch):
     elif k == "rglru_gated":  # x, r, i (lam: one value per channel)
         inp = B * L * cfg["D"] * 3 * es
         y = B * L * cfg["D"] * 4
+    elif k == "rotlru_angle":  # a, theta, x (two values per pair)
+        Dp = cfg["Dp"]
+        inp = B * L * Dp * 4 * es
+        y = B * L * 2 * Dp * 4
     else:
         Dp = cfg["Dp"]
         inp = B * L * Dp * 5 * es
@@ -202,7 +206,7 @@ def cpu_sample(name):
         ins = [t[:, :, :hs] if t.dim() >= 3 else t[:hs] for t in ins]
         frac = hs / (cfg["B"] * cfg["H"])
         desc = f"1 batch row x {hs} of {cfg['H']} heads (full L), scaled by units"
-    elif k in ("rglru", "rglru_gated", "rotlru") and cfg["B"] > 1 and cfg["B"] * cfg["L"] > 2 ** 15:
+    elif k in ("rglru", "rglru_gated", "rotlru", "rotlru_angle") and cfg["B"] > 1 and cfg["B"] * cfg["L"] > 2 ** 15:
         nb = 1
         ins = W.make_inputs(name, "cpu", seed=1000, batch=nb)
         frac = nb / cfg["B"]
@@ -213,17 +217,20 @@ def cpu_sample(name):
         desc = "full config"
     ins = [t.float().contiguous().numpy() for t in ins]
     g = torch.Generator().manual_seed(7)
-    yshape = ins[0].shape if k != "rotlru" else ins[3].shape
+    yshape = ins[3].shape if k == "rotlru" else ins[2].shape if k == "rotlru_angle" else ins[0].shape
     gy = torch.randn(yshape, generator=g).numpy()
     return ins, gy, frac, desc
 
 
 def _cpu_run(c_oracle, W, cfg, ins, gy):
     """One forward+backward of the C restatement; for the gated RG-LRU the
-    reference's host-side gating (rglru.py:8-27) runs first, in numpy."""
+    reference's host-side gating (rglru.py:8-27), for the rotLRU angle input
+    its host-side cos/sin (rotlru.py:18-22), runs first, in numpy."""
     if cfg["kind"] == "rglru_gated":
         a, b = W.gated_to_plain(*ins)
         return c_oracle.run("rglru", [a, b], cfg["seg"], gy=gy)
+    if cfg["kind"] == "rotlru_angle":
+        return c_oracle.run("rotlru", list(W.angle_to_plain(*ins)), cfg["seg"], gy=gy)
     return c_oracle.run(cfg["kind"], ins, cfg["seg"], gy=gy)
 
 
@@ -495,7 +502,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--config", default="c4", choices=["c0", "c1", "c2", "c3", "c4", "c5", "c2g"])
+    ap.add_argument("--config", default="c4", choices=["c0", "c1", "c2", "c3", "c4", "c5", "c2g", "c3a"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffer) timing")

@@ -245,6 +245,24 @@ MR_API int mr_rotlru_bwd_h0(const float* grad_y, const float* grad_final, const 
                             void* workspace, size_t workspace_bytes, const float* h0, float* grad_h0,
                             void* stream);
 
+/* ------------------------------------------------- rotLRU, angle input ---
+ * The rotLRU scan taking the rotation angle theta [B,L,Dp] in place of cs, sn
+ * (no counterpart in the reference, which forms cos and sin in MLX host code
+ * and passes both through HBM, rotlru.py:18-22): the kernels form
+ * cos(theta), sin(theta) in float32 as they load each tile, so the scan reads
+ * four streams instead of five and the backward writes grad_theta =
+ * cos(theta) grad_sn - sin(theta) grad_cs directly. Everything else (layout,
+ * h_ckpt, h0, workspace size from mr_rotlru_bwd_workspace_bytes) is as in
+ * mr_rotlru_fwd_h0 / mr_rotlru_bwd_h0; h0 and grad_h0 may be NULL. */
+MR_API int mr_rotlru_angle_fwd(const void* a, const void* theta, const void* x, int dtype, int64_t batch,
+                               int64_t L, int64_t Dp, int64_t seg, float* y, float* h_ckpt, const float* h0,
+                               void* stream);
+MR_API int mr_rotlru_angle_bwd(const float* grad_y, const float* grad_final, const float* h_ckpt, const void* a,
+                               const void* theta, const void* x, int dtype, int64_t batch, int64_t L,
+                               int64_t Dp, int64_t seg, void* grad_a, void* grad_theta, void* grad_x,
+                               void* workspace, size_t workspace_bytes, const float* h0, float* grad_h0,
+                               void* stream);
+
 /* ------------------------------------------------------ gated RG-LRU ---
  * The RG-LRU scan with its input gating folded in (no counterpart in the
  * reference, which leaves the gating to MLX host code, rglru.py:8-27, and

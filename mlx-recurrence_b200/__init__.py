@@ -23,7 +23,8 @@ from ._chassis import DEFAULT_SEG, check_segment_shape, get_or_build_kernel, par
 from .gla import gla_scan, gla_scan_reference, gla_scan_with_state, gla_step
 from .rglru import (rglru_scan, rglru_scan_gated, rglru_scan_gated_with_state, rglru_scan_reference,
                     rglru_scan_with_state, rglru_step)
-from .rotlru import rotlru_scan, rotlru_scan_reference, rotlru_scan_with_state, rotlru_step
+from .rotlru import (rotlru_scan, rotlru_scan_angle, rotlru_scan_angle_with_state, rotlru_scan_reference,
+                     rotlru_scan_with_state, rotlru_step)
 from .ssd import ssd_scan, ssd_scan_reference, ssd_scan_with_state, ssd_step
 
 __all__ = [
@@ -39,6 +40,8 @@ __all__ = [
     "rotlru_scan",
     "rotlru_scan_with_state",
     "rotlru_scan_reference",
+    "rotlru_scan_angle",
+    "rotlru_scan_angle_with_state",
     # the RG-LRU scan with its input gating in the kernels (not in the reference)
     "rglru_scan_gated",
     "rglru_scan_gated_with_state",

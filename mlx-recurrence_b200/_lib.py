@@ -79,6 +79,10 @@ SIGNATURES = {
     "mr_rglru_gated_bwd_workspace_bytes": (_sz, [_int, _i64, _i64, _i64, _i64]),
     "mr_rglru_gated_bwd": (_int, [_p, _p, _p, _p, _p, _p, _p, ctypes.c_float, _int, _i64, _i64, _i64, _i64, _p,
                                   _p, _p, _p, _p, _sz, _p, _p, _p]),
+    # the rotLRU scan taking the rotation angle (cos, sin formed in the kernels)
+    "mr_rotlru_angle_fwd": (_int, [_p, _p, _p, _int, _i64, _i64, _i64, _i64, _p, _p, _p, _p]),
+    "mr_rotlru_angle_bwd": (_int, [_p, _p, _p, _p, _p, _p, _int, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _sz,
+                                   _p, _p, _p]),
     # one-token decode steps (state advanced in place)
     "mr_ssd_step": (_int, [_p, _p, _p, _p, _p, _i64, _i64, _int, _i64, _i64, _i64, _i64, _p, _p, _p]),
     "mr_gla_step": (_int, [_p, _p, _p, _p, _int, _i64, _i64, _i64, _p, _p, _p]),

@@ -539,12 +539,63 @@ rglru_bwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant
 // rotLRU forward (pairs interleaved in x / y; rotlru.py:80-146)
 // ============================================================================
 
-template <typename T, int W, int TB, int S>
+// cos and sin of an angle for the rotLRU angle input. Cody-Waite reduction
+// (Cody & Waite, "Software Manual for the Elementary Functions", 1980): k =
+// rint(t 2/pi), r = t - k pi/2 with pi/2 split in two floats (hi = pi/2
+// rounded to float, lo = the float nearest pi/2 - hi) and fused multiply-adds,
+// so r is exact to a few float ulps for |t| < 2^17 pi/2; then the Taylor series
+// of sin r to r^9 and cos r to r^10 on |r| <= pi/4 (truncation below 2e-9), and
+// the quadrant k mod 4 picks and signs the pair. About 20 instructions with no
+// taken branch, small enough to unroll across a tile (the library's sincosf
+// carries a long path for huge arguments that bloats an unrolled loop);
+// arguments beyond the reduction's range, and non-finite ones, go to sincosf
+// out of line.
+__device__ __noinline__ float2 rot_sincos_wide(float t) {
+  float sv, cv;
+  sincosf(t, &sv, &cv);
+  return make_float2(sv, cv);
+}
+
+__device__ __forceinline__ void rot_sincos(float t, float& sv, float& cv) {
+  constexpr float kTwoOverPi = (float)(2.0 / 3.14159265358979323846);
+  constexpr float kHalfPiHi = (float)(3.14159265358979323846 / 2.0);
+  constexpr float kHalfPiLo = (float)(3.14159265358979323846 / 2.0 - (double)kHalfPiHi);
+  if (!(fabsf(t) < 205887.4f)) {  // 2^17 pi/2; NaN takes this branch too
+    const float2 w = rot_sincos_wide(t);
+    sv = w.x, cv = w.y;
+    return;
+  }
+  const float k = rintf(t * kTwoOverPi);
+  float r = fmaf(-k, kHalfPiHi, t);
+  r = fmaf(-k, kHalfPiLo, r);
+  const float r2 = r * r;
+  float ps = (float)(1.0 / 362880.0);
+  ps = fmaf(ps, r2, (float)(-1.0 / 5040.0));
+  ps = fmaf(ps, r2, (float)(1.0 / 120.0));
+  ps = fmaf(ps, r2, (float)(-1.0 / 6.0));
+  const float sr = fmaf(ps * r2, r, r);
+  float pc = (float)(-1.0 / 3628800.0);
+  pc = fmaf(pc, r2, (float)(1.0 / 40320.0));
+  pc = fmaf(pc, r2, (float)(-1.0 / 720.0));
+  pc = fmaf(pc, r2, (float)(1.0 / 24.0));
+  pc = fmaf(pc, r2, -0.5f);
+  const float cr = fmaf(pc, r2, 1.f);
+  const int q = __float2int_rn(k);
+  const float a = (q & 1) ? cr : sr, b = (q & 1) ? sr : cr;
+  sv = (q & 2) ? -a : a;
+  cv = ((q + 1) & 2) ? -b : b;
+}
+
+// kTh: the rotation comes as its angle theta (one tile, in the cs slot) and the
+// kernels form cos and sin on load; the reference takes cos and sin from host
+// code (rotlru.py:18-22). NT: input tiles per stage (5 units of T: a, cs, sn, x;
+// 4 with the angle).
+template <typename T, int W, int TB, int S, int NT = 5>
 struct RotFwdSmem {
-  static constexpr size_t bytes = (size_t)S * TB * W * 5 * sizeof(T) + 2 * 2 * kWarps * W * 8 + S * 8;
+  static constexpr size_t bytes = (size_t)S * TB * W * NT * sizeof(T) + 2 * 2 * kWarps * W * 8 + S * 8;
 };
 
-template <typename T, int W, int TB, int S, bool kH0>
+template <typename T, int W, int TB, int S, bool kH0, bool kTh>
 __global__ void __launch_bounds__(kThreads, 2)
 rotlru_fwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_c,
                   const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_x,
@@ -553,8 +604,8 @@ rotlru_fwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
   constexpr int V = W / 32, TW = TB / kWarps;
   extern __shared__ __align__(128) unsigned char smem[];
   T* sa = reinterpret_cast<T*>(smem);
-  T* sc = sa + S * TB * W;
-  T* ss = sc + S * TB * W;
+  T* sc = sa + S * TB * W;                     // cs, or theta (kTh)
+  T* ss = sc + (kTh ? 0 : S * TB * W);         // sn (kTh: unused)
   T* sx = ss + S * TB * W;  // [S][TB][2W]
   cf* sZ = reinterpret_cast<cf*>(sx + S * TB * 2 * W);
   cf* sH = sZ + 2 * kWarps * W;
@@ -579,10 +630,10 @@ rotlru_fwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
 
   auto issue = [&](int blk) {  // one thread: [TB x W] boxes of a, cs, sn; [TB x 2W] of x
     const int s = blk % S, row = (int)(b * L) + blk * TB;
-    mbar_arrive_expect_tx(&bar[s], (uint32_t)TB * W * 5u * sizeof(T));
+    mbar_arrive_expect_tx(&bar[s], (uint32_t)TB * W * (kTh ? 4u : 5u) * sizeof(T));
     tma_load_2d(sa + s * TB * W, &tm_a, (int)p0, row, &bar[s]);
     tma_load_2d(sc + s * TB * W, &tm_c, (int)p0, row, &bar[s]);
-    tma_load_2d(ss + s * TB * W, &tm_s, (int)p0, row, &bar[s]);
+    if constexpr (!kTh) tma_load_2d(ss + s * TB * W, &tm_s, (int)p0, row, &bar[s]);
     tma_load_2d(sx + s * TB * 2 * W, &tm_x, (int)(2 * p0), row, &bar[s]);
   };
   if (threadIdx.x == 0)
@@ -613,9 +664,14 @@ rotlru_fwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
       const Vec<T, 2 * V> vx = ld_vec<T, 2 * V>(sx + row * 2 * W + 2 * pl);
 #pragma unroll
       for (int v = 0; v < V; ++v) {
+        float cv, sv;
+        if constexpr (kTh)
+          rot_sincos(to_f(vc.v[v]), sv, cv);
+        else
+          cv = to_f(vc.v[v]), sv = to_f(vs.v[v]);
         fa[i][v] = ok ? to_f(va.v[v]) : 1.f;
-        fc[i][v] = ok ? to_f(vc.v[v]) : 1.f;
-        fs[i][v] = ok ? to_f(vs.v[v]) : 0.f;
+        fc[i][v] = ok ? cv : 1.f;
+        fs[i][v] = ok ? sv : 0.f;
         fx[i][v] = ok ? cf{to_f(vx.v[2 * v]), to_f(vx.v[2 * v + 1])} : cf{0.f, 0.f};
       }
     }
@@ -683,13 +739,14 @@ rotlru_fwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
 // rotLRU backward (rotlru.py:153-266)
 // ============================================================================
 
-template <typename T, int W, int TB, int S>
+template <typename T, int W, int TB, int S, int NT = 5>
 struct RotBwdSmem {
   static constexpr size_t bytes =
-      (size_t)S * TB * W * (5 * sizeof(T) + 8) + 4 * 2 * kWarps * W * 8 + S * 8;
+      (size_t)S * TB * W * (NT * sizeof(T) + 8) + 4 * 2 * kWarps * W * 8 + S * 8;
 };
 
-template <typename T, int W, int TB, int S, bool kH0>
+// kTh: cs holds theta and gcs receives d loss / d theta (sn, gsn unused)
+template <typename T, int W, int TB, int S, bool kH0, bool kTh>
 __global__ void __launch_bounds__(kThreads, 2)
 rotlru_bwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_c,
                   const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_x,
@@ -701,8 +758,8 @@ rotlru_bwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
   constexpr int V = W / 32, TW = TB / kWarps;
   extern __shared__ __align__(128) unsigned char smem[];
   T* sa = reinterpret_cast<T*>(smem);
-  T* sc = sa + S * TB * W;
-  T* ss = sc + S * TB * W;
+  T* sc = sa + S * TB * W;                                  // cs, or theta (kTh)
+  T* ss = sc + (kTh ? 0 : S * TB * W);                      // sn (kTh: unused)
   T* sx = ss + S * TB * W;                                  // [S][TB][2W]
   float* sg = reinterpret_cast<float*>(sx + S * TB * 2 * W);  // [S][TB][2W]
   cf* sZ = reinterpret_cast<cf*>(sg + S * TB * 2 * W);
@@ -735,10 +792,10 @@ rotlru_bwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
     int t0, nt, j;
     bm.range(bm.nq - 1 - p, t0, nt, j);
     const int row = (int)(b * L) + t0;
-    mbar_arrive_expect_tx(&bar[s], (uint32_t)TB * W * (5u * sizeof(T) + 8u));
+    mbar_arrive_expect_tx(&bar[s], (uint32_t)TB * W * ((kTh ? 4u : 5u) * sizeof(T) + 8u));
     tma_load_2d(sa + s * TB * W, &tm_a, (int)p0, row, &bar[s]);
     tma_load_2d(sc + s * TB * W, &tm_c, (int)p0, row, &bar[s]);
-    tma_load_2d(ss + s * TB * W, &tm_s, (int)p0, row, &bar[s]);
+    if constexpr (!kTh) tma_load_2d(ss + s * TB * W, &tm_s, (int)p0, row, &bar[s]);
     tma_load_2d(sx + s * TB * 2 * W, &tm_x, (int)(2 * p0), row, &bar[s]);
     tma_load_2d(sg + s * TB * 2 * W, &tm_g, (int)(2 * p0), row, &bar[s]);
   };
@@ -781,7 +838,12 @@ rotlru_bwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
               const int64_t o = pbase + (int64_t)(t0 + i) * Dp + pl + v;
               const int64_t ox = xbase + (int64_t)(t0 + i) * D + 2 * (pl + v);
               const float av = to_f(a[o]);
-              const cf z = {av * to_f(cs[o]), av * to_f(sn[o])};
+              float cv, sv;
+              if constexpr (kTh)
+                rot_sincos(to_f(cs[o]), sv, cv);
+              else
+                cv = to_f(cs[o]), sv = to_f(sn[o]);
+              const cf z = {av * cv, av * sv};
               H = cfma(z, H, {to_f(x[ox]), to_f(x[ox + 1])});
               Z = cmul(z, Z);
             }
@@ -825,9 +887,14 @@ rotlru_bwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
       const Vec<float, 2 * V> vg = ld_vec<float, 2 * V>(sg + row * 2 * W + 2 * pl);
 #pragma unroll
       for (int v = 0; v < V; ++v) {
+        float cv, sv;
+        if constexpr (kTh)
+          rot_sincos(to_f(vc.v[v]), sv, cv);
+        else
+          cv = to_f(vc.v[v]), sv = to_f(vs.v[v]);
         fa[i][v] = ok ? to_f(va.v[v]) : 1.f;
-        fc[i][v] = ok ? to_f(vc.v[v]) : 1.f;
-        fs[i][v] = ok ? to_f(vs.v[v]) : 0.f;
+        fc[i][v] = ok ? cv : 1.f;
+        fs[i][v] = ok ? sv : 0.f;
         fx[i][v] = ok ? cf{to_f(vx.v[2 * v]), to_f(vx.v[2 * v + 1])} : cf{0.f, 0.f};
         fg[i][v] = ok ? cf{vg.v[2 * v], vg.v[2 * v + 1]} : cf{0.f, 0.f};
       }
@@ -912,13 +979,14 @@ rotlru_bwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
         o_a[v] = aU * ru + aW * rw;
         o_c[v] = av * (aU * up + aW * wp);
         o_s[v] = av * (aW * up - aU * wp);
+        if constexpr (kTh) o_c[v] = c * o_s[v] - sv * o_c[v];  // d/dtheta = cos d/dsn - sin d/dcs
         crin[v] = {av * (c * aU + sv * aW), av * (-sv * aU + c * aW)};
       }
       if (act && t < tend) {
         const int64_t o = pbase + (int64_t)t * Dp + pl;
         st_vec<T, V>(ga + o, o_a);
         st_vec<T, V>(gcs + o, o_c);
-        st_vec<T, V>(gsn + o, o_s);
+        if constexpr (!kTh) st_vec<T, V>(gsn + o, o_s);
         st_vec<T, 2 * V>(gx + xbase + (int64_t)t * D + 2 * pl, o_x);
       }
     }
@@ -939,11 +1007,15 @@ rotlru_bwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
 // Tile shapes (channels per CTA W, steps per block TB, pipeline stages S),
 // from a sweep on B200 at c2/c3 (bf16): one channel per lane with long blocks
 // for RG-LRU (more CTAs, shorter per-thread chains in phase 1), 64-pair tiles
-// for the rotLRU forward, 32-pair tiles of 64 steps for its backward.
+// for the rotLRU forward, 32-pair tiles of 64 steps for its backward. The
+// rotLRU forward with the angle input takes three stages (112 KB of shared
+// memory, two CTAs per SM): its cos/sin work wants the second CTA's warps to
+// overlap it (0.71 -> 0.55 ms at c3, against 0.63 with 32-pair tiles).
 template <typename T> struct DiagCfg {
   static constexpr int RgFW = 32, RgFTB = 128, RgFS = sizeof(T) == 4 ? 2 : 4;
   static constexpr int RgBW = 32, RgBTB = 128, RgBS = 2;
   static constexpr int RotFW = 64, RotFTB = 64, RotFS = sizeof(T) == 4 ? 2 : 4;
+  static constexpr int RotAFW = 64, RotAFTB = 64, RotAFS = sizeof(T) == 4 ? 2 : 3;  // angle input
   static constexpr int RotBW = 32, RotBTB = 64, RotBS = 2;
 };
 
@@ -1067,19 +1139,19 @@ int rglru_gated_bwd_launch(const float* gy, const float* gf, const float* ckpt, 
   return check_launch("lambda_sum_kernel");
 }
 
-template <typename T>
-int rotlru_fwd_launch(const void* a, const void* cs, const void* sn, const void* x, int64_t batch,
-                      int64_t L, int64_t Dp, int64_t seg, float* y, float* ckpt, const float* h0,
-                      cudaStream_t st) {
+// sn == nullptr: cs holds the angle theta (the kernels form cos and sin)
+template <typename T, bool kTh>
+int rotlru_fwd_any(const void* a, const void* cs, const void* sn, const void* x, int64_t batch, int64_t L,
+                   int64_t Dp, int64_t seg, float* y, float* ckpt, const float* h0, cudaStream_t st) {
   using C = DiagCfg<T>;
-  constexpr int W = C::RotFW, TB = C::RotFTB, S = C::RotFS;
-  constexpr size_t sm = RotFwdSmem<T, W, TB, S>::bytes;
+  constexpr int W = kTh ? C::RotAFW : C::RotFW, TB = kTh ? C::RotAFTB : C::RotFTB, S = kTh ? C::RotAFS : C::RotFS;
+  constexpr size_t sm = RotFwdSmem<T, W, TB, S, kTh ? 4 : 5>::bytes;
   CUtensorMap ma, mc, ms, mx;
   if (int rc = tmap_rows<T>(&ma, a, batch * L, Dp, W, TB)) return rc;
   if (int rc = tmap_rows<T>(&mc, cs, batch * L, Dp, W, TB)) return rc;
-  if (int rc = tmap_rows<T>(&ms, sn, batch * L, Dp, W, TB)) return rc;
+  if (int rc = tmap_rows<T>(&ms, kTh ? cs : sn, batch * L, Dp, W, TB)) return rc;
   if (int rc = tmap_rows<T>(&mx, x, batch * L, 2 * Dp, 2 * W, TB)) return rc;
-  auto k = h0 != nullptr ? rotlru_fwd_kernel<T, W, TB, S, true> : rotlru_fwd_kernel<T, W, TB, S, false>;
+  auto k = h0 != nullptr ? rotlru_fwd_kernel<T, W, TB, S, true, kTh> : rotlru_fwd_kernel<T, W, TB, S, false, kTh>;
   if (int rc = set_smem(k, sm)) return rc;
   dim3 grid((unsigned)((Dp + W - 1) / W), (unsigned)batch);
   k<<<grid, kThreads, sm, st>>>(ma, mc, ms, mx, (int)L, Dp, (int)seg, y, ckpt, h0);
@@ -1087,26 +1159,55 @@ int rotlru_fwd_launch(const void* a, const void* cs, const void* sn, const void*
 }
 
 template <typename T>
-int rotlru_bwd_launch(const float* gy, const float* gf, const float* ckpt, const void* a,
-                      const void* cs, const void* sn, const void* x, int64_t batch, int64_t L,
-                      int64_t Dp, int64_t seg, void* ga, void* gcs, void* gsn, void* gx, float* ws,
-                      const float* h0, float* gh0, cudaStream_t st) {
+int rotlru_fwd_launch(const void* a, const void* cs, const void* sn, const void* x, int64_t batch,
+                      int64_t L, int64_t Dp, int64_t seg, float* y, float* ckpt, const float* h0,
+                      cudaStream_t st) {
+  return rotlru_fwd_any<T, false>(a, cs, sn, x, batch, L, Dp, seg, y, ckpt, h0, st);
+}
+
+template <typename T>
+int rotlru_angle_fwd_launch(const void* a, const void* theta, const void* x, int64_t batch, int64_t L, int64_t Dp,
+                            int64_t seg, float* y, float* ckpt, const float* h0, cudaStream_t st) {
+  return rotlru_fwd_any<T, true>(a, theta, nullptr, x, batch, L, Dp, seg, y, ckpt, h0, st);
+}
+
+// sn == nullptr: cs holds theta and gcs receives its gradient (gsn unused)
+template <typename T, bool kTh>
+int rotlru_bwd_any(const float* gy, const float* gf, const float* ckpt, const void* a, const void* cs,
+                   const void* sn, const void* x, int64_t batch, int64_t L, int64_t Dp, int64_t seg, void* ga,
+                   void* gcs, void* gsn, void* gx, float* ws, const float* h0, float* gh0, cudaStream_t st) {
   using C = DiagCfg<T>;
-  constexpr int W = C::RotBW, TB = C::RotBTB, S = C::RotBS;
-  constexpr size_t sm = RotBwdSmem<T, W, TB, S>::bytes;
+  constexpr int W = C::RotBW, TB = C::RotBTB, S = C::RotBS;  // the angle input shares the workspace layout
+  constexpr size_t sm = RotBwdSmem<T, W, TB, S, kTh ? 4 : 5>::bytes;
   CUtensorMap ma, mc, ms, mx, mg;
   if (int rc = tmap_rows<T>(&ma, a, batch * L, Dp, W, TB)) return rc;
   if (int rc = tmap_rows<T>(&mc, cs, batch * L, Dp, W, TB)) return rc;
-  if (int rc = tmap_rows<T>(&ms, sn, batch * L, Dp, W, TB)) return rc;
+  if (int rc = tmap_rows<T>(&ms, kTh ? cs : sn, batch * L, Dp, W, TB)) return rc;
   if (int rc = tmap_rows<T>(&mx, x, batch * L, 2 * Dp, 2 * W, TB)) return rc;
   if (int rc = tmap_rows<float>(&mg, gy, batch * L, 2 * Dp, 2 * W, TB)) return rc;
-  auto k = h0 != nullptr ? rotlru_bwd_kernel<T, W, TB, S, true> : rotlru_bwd_kernel<T, W, TB, S, false>;
+  auto k = h0 != nullptr ? rotlru_bwd_kernel<T, W, TB, S, true, kTh> : rotlru_bwd_kernel<T, W, TB, S, false, kTh>;
   if (int rc = set_smem(k, sm)) return rc;
   dim3 grid((unsigned)((Dp + W - 1) / W), (unsigned)batch);
   k<<<grid, kThreads, sm, st>>>(ma, mc, ms, mx, mg, gf, ckpt, (const T*)a, (const T*)cs, (const T*)sn,
                                 (const T*)x, (int)L, Dp, (int)seg, (T*)ga, (T*)gcs, (T*)gsn, (T*)gx, ws, h0,
                                 gh0);
   return check_launch("rotlru_bwd_kernel");
+}
+
+template <typename T>
+int rotlru_bwd_launch(const float* gy, const float* gf, const float* ckpt, const void* a,
+                      const void* cs, const void* sn, const void* x, int64_t batch, int64_t L,
+                      int64_t Dp, int64_t seg, void* ga, void* gcs, void* gsn, void* gx, float* ws,
+                      const float* h0, float* gh0, cudaStream_t st) {
+  return rotlru_bwd_any<T, false>(gy, gf, ckpt, a, cs, sn, x, batch, L, Dp, seg, ga, gcs, gsn, gx, ws, h0, gh0, st);
+}
+
+template <typename T>
+int rotlru_angle_bwd_launch(const float* gy, const float* gf, const float* ckpt, const void* a, const void* theta,
+                            const void* x, int64_t batch, int64_t L, int64_t Dp, int64_t seg, void* ga,
+                            void* gtheta, void* gx, float* ws, const float* h0, float* gh0, cudaStream_t st) {
+  return rotlru_bwd_any<T, true>(gy, gf, ckpt, a, theta, nullptr, x, batch, L, Dp, seg, ga, gtheta, nullptr, gx,
+                                 ws, h0, gh0, st);
 }
 
 #define MR_INST(T)                                                                                  \
@@ -1128,7 +1229,14 @@ int rotlru_bwd_launch(const float* gy, const float* gf, const float* ckpt, const
   template int rotlru_bwd_launch<T>(const float*, const float*, const float*, const void*,         \
                                     const void*, const void*, const void*, int64_t, int64_t,       \
                                     int64_t, int64_t, void*, void*, void*, void*, float*,          \
-                                    const float*, float*, cudaStream_t);
+                                    const float*, float*, cudaStream_t);                           \
+  template int rotlru_angle_fwd_launch<T>(const void*, const void*, const void*, int64_t, int64_t, \
+                                          int64_t, int64_t, float*, float*, const float*,          \
+                                          cudaStream_t);                                           \
+  template int rotlru_angle_bwd_launch<T>(const float*, const float*, const float*, const void*,   \
+                                          const void*, const void*, int64_t, int64_t, int64_t,     \
+                                          int64_t, void*, void*, void*, float*, const float*,      \
+                                          float*, cudaStream_t);
 MR_INST(float)
 MR_INST(__nv_bfloat16)
 MR_INST(__half)

@@ -69,6 +69,8 @@ template <typename T> int rotlru_step_launch(const void*, const void*, const voi
 template <typename T> int rglru_gated_fwd_launch(const void*, const void*, const void*, const float*, float, int64_t, int64_t, int64_t, int64_t, float*, float*, const float*, cudaStream_t);
 template <typename T> int rglru_gated_bwd_launch(const float*, const float*, const float*, const void*, const void*, const void*, const float*, float, int64_t, int64_t, int64_t, int64_t, void*, void*, void*, float*, void*, const float*, float*, cudaStream_t);
 size_t rglru_gated_bwd_ws_bytes(int64_t, int64_t, int64_t, int64_t);
+template <typename T> int rotlru_angle_fwd_launch(const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, float*, float*, const float*, cudaStream_t);
+template <typename T> int rotlru_angle_bwd_launch(const float*, const float*, const float*, const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, void*, void*, void*, float*, const float*, float*, cudaStream_t);
 int umma_selftest_launch(const void*, const void*, const void*, const void*, float*, float*, float*,
                          cudaStream_t);
 
@@ -140,7 +142,7 @@ using namespace mr;
 extern "C" {
 
 // 2: the _h0 (initial state) entry points; 3: the decode steps; 4: the gated RG-LRU scan
-int mr_abi_version(void) { return 4; }
+int mr_abi_version(void) { return 5; }
 
 const char* mr_last_error(void) { return g_err; }
 
@@ -321,6 +323,41 @@ int mr_rotlru_bwd_h0(const float* grad_y, const float* grad_final, const float* 
   MR_DTYPE_SWITCH(dtype, rotlru_bwd_launch<T>(grad_y, grad_final, h_ckpt, a, cs, sn, x, batch, L,
                                               Dp, seg, grad_a, grad_cs, grad_sn, grad_x,
                                               (float*)workspace, h0, grad_h0, st));
+}
+
+int mr_rotlru_angle_fwd(const void* a, const void* theta, const void* x, int dtype, int64_t batch, int64_t L,
+                        int64_t Dp, int64_t seg, float* y, float* h_ckpt, const float* h0, void* stream) {
+  g_err[0] = 0;
+  MR_TRY(check_dims("mr_rotlru_angle_fwd", batch, L, Dp));
+  MR_TRY(check_seg(L, seg, 2 * Dp, "D"));
+  MR_TRY(check_dtype(dtype));
+  MR_TRY(check_ptrs("mr_rotlru_angle_fwd", {a, theta, x, y, h_ckpt}));
+  MR_TRY(check_opt_ptr("mr_rotlru_angle_fwd", h0));
+  cudaStream_t st = (cudaStream_t)stream;
+  MR_DTYPE_SWITCH(dtype, rotlru_angle_fwd_launch<T>(a, theta, x, batch, L, Dp, seg, y, h_ckpt, h0, st));
+}
+
+int mr_rotlru_angle_bwd(const float* grad_y, const float* grad_final, const float* h_ckpt, const void* a,
+                        const void* theta, const void* x, int dtype, int64_t batch, int64_t L, int64_t Dp,
+                        int64_t seg, void* grad_a, void* grad_theta, void* grad_x, void* workspace,
+                        size_t workspace_bytes, const float* h0, float* grad_h0, void* stream) {
+  g_err[0] = 0;
+  MR_TRY(check_dims("mr_rotlru_angle_bwd", batch, L, Dp));
+  MR_TRY(check_seg(L, seg, 2 * Dp, "D"));
+  MR_TRY(check_dtype(dtype));
+  MR_TRY(check_ptrs("mr_rotlru_angle_bwd", {grad_y, h_ckpt, a, theta, x, grad_a, grad_theta, grad_x}));
+  MR_TRY(check_opt_ptr("mr_rotlru_angle_bwd", grad_final));
+  const size_t need = rotlru_bwd_ws_bytes(batch, L, Dp, seg);
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need))
+    return set_error(MR_E_WORKSPACE, "mr_rotlru_angle_bwd: workspace of %zu bytes required, got %zu", need,
+                     workspace_bytes);
+  MR_TRY(check_opt_ptr("mr_rotlru_angle_bwd", workspace));
+  MR_TRY(check_opt_ptr("mr_rotlru_angle_bwd", h0));
+  MR_TRY(check_opt_ptr("mr_rotlru_angle_bwd", grad_h0));
+  cudaStream_t st = (cudaStream_t)stream;
+  MR_DTYPE_SWITCH(dtype, rotlru_angle_bwd_launch<T>(grad_y, grad_final, h_ckpt, a, theta, x, batch, L, Dp, seg,
+                                                    grad_a, grad_theta, grad_x, (float*)workspace, h0, grad_h0,
+                                                    st));
 }
 
 // --------------------------------------------------------------------- SSD ---

@@ -5,7 +5,7 @@ meaning, validation messages and shape rules, backed by the sm_100a kernels
 in ``csrc/diag_scan.cu``. Pairs are interleaved in the channel axis
 (``x[..., 2p]`` is u, ``x[..., 2p+1]`` is w); ``a``, ``cs = cos(theta)`` and
 ``sn = sin(theta)`` are per pair. The kernels are range-agnostic: ``a`` may be
-negative and ``(cs, sn)`` need not be normalised (``rotlru.py:18-24``).
+negative and ``(cs, sn)`` need not be normalised (``rotlru.py:18-22``).
 
 VJP (``rotlru.py:35-40``): ``adj_t = gy_t + a_{t+1} M_{t+1}^T adj_{t+1}``,
 ``grad_x = adj``, ``grad_a = adj . (M h_{t-1})``,
@@ -103,6 +103,76 @@ def rotlru_scan_with_state(a, cs, sn, x, seg=DEFAULT_SEG, h0=None):
     """Rotational LRU scan that also returns the final state [B, D] (``rotlru.py:323-331``).
     Passing it back as ``h0`` continues the scan (chunked prefill)."""
     return _RotLRUScan.apply(a, cs, sn, x, seg, h0)
+
+
+class _RotLRUAngleScan(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, a, theta, x, seg, h0):
+        ctx.set_materialize_grads(False)
+        if a.dim() == 3 and theta.shape != a.shape:
+            raise ValueError(f"a/theta shapes must match, got {tuple(a.shape)}, {tuple(theta.shape)}")
+        Bt, L, Dp = _validate(a, theta, theta, x)
+        check_segment_shape(L, seg, x.shape[2], "D")
+        dev = _lib.require_cuda(a, theta, x)
+        dt = common_dtype(a, theta, x)
+        a_, t_, x_ = (prep(t, dt) for t in (a, theta, x))
+        D = 2 * Dp
+        h0_ = prep_h0(h0, (Bt, D), dev)
+        y = torch.empty((Bt, L, D), dtype=torch.float32, device=dev)
+        ckpt = torch.empty((Bt, L // seg, D), dtype=torch.float32, device=dev)
+        with torch.cuda.device(dev):
+            _lib.call("mr_rotlru_angle_fwd", _lib.ptr(a_), _lib.ptr(t_), _lib.ptr(x_), _lib.DTYPE_CODE[dt], Bt,
+                      L, Dp, seg, _lib.ptr(y), _lib.ptr(ckpt), _lib.ptr(h0_), _lib.stream_of(dev))
+        ctx.save_for_backward(a_, t_, x_, ckpt, h0_)
+        ctx.seg = seg
+        return y, ckpt[:, -1].clone()
+
+    @staticmethod
+    def backward(ctx, gy, gfinal):
+        a_, t_, x_, ckpt, h0_ = ctx.saved_tensors
+        Bt, L, Dp = a_.shape
+        dev = a_.device
+        code = _lib.DTYPE_CODE[a_.dtype]
+        gy = grad_out(gy, (Bt, L, 2 * Dp), dev)
+        gf = None if gfinal is None else gfinal.to(torch.float32).contiguous()
+        ga, gt, gx = (torch.empty_like(t) for t in (a_, t_, x_))
+        gh0 = torch.empty_like(h0_) if (h0_ is not None and ctx.needs_input_grad[4]) else None
+        with torch.cuda.device(dev):
+            lib = _lib.load()
+            nws = lib.mr_rotlru_bwd_workspace_bytes(code, Bt, L, Dp, ctx.seg)
+            ws = torch.empty(nws, dtype=torch.uint8, device=dev) if nws else None
+            _lib.call("mr_rotlru_angle_bwd", _lib.ptr(gy), _lib.ptr(gf), _lib.ptr(ckpt), _lib.ptr(a_),
+                      _lib.ptr(t_), _lib.ptr(x_), code, Bt, L, Dp, ctx.seg, _lib.ptr(ga), _lib.ptr(gt),
+                      _lib.ptr(gx), _lib.ptr(ws), nws, _lib.ptr(h0_), _lib.ptr(gh0), _lib.stream_of(dev))
+        return ga, gt, gx, None, gh0
+
+
+def rotlru_scan_angle(a, theta, x, seg=DEFAULT_SEG, h0=None):
+    """The rotLRU scan taking the rotation angle itself (no counterpart in the
+    reference, whose callers form ``cs = cos(theta)``, ``sn = sin(theta)`` in
+    host code and pass both, ``rotlru.py:18-22``). Equal to
+    ``rotlru_scan(a, cos(theta), sin(theta), x)``; the kernels form cos and sin
+    in float32 as they load each tile, so the scan reads four streams instead of
+    five and no cs/sn tensors (or their gradients) are materialised.
+
+    Args:
+        a:     [B, L, Dp] per-pair magnitude gate.
+        theta: [B, L, Dp] rotation angle (radians).
+        x:     [B, L, D]  drive, D = 2*Dp, pairs interleaved (u, w).
+        seg:   checkpoint segment length (L % seg == 0).
+        h0:    optional initial state [B, D] (differentiable).
+
+    Returns:
+        y: [B, L, D] float32. Gradients flow to a, theta, x (and h0):
+        ``grad_theta = cos(theta) grad_sn - sin(theta) grad_cs``.
+    """
+    y, _ = _RotLRUAngleScan.apply(a, theta, x, seg, h0)
+    return y
+
+
+def rotlru_scan_angle_with_state(a, theta, x, seg=DEFAULT_SEG, h0=None):
+    """:func:`rotlru_scan_angle` that also returns the final state [B, D]."""
+    return _RotLRUAngleScan.apply(a, theta, x, seg, h0)
 
 
 def rotlru_scan_reference(a, cs, sn, x, h0=None):

@@ -25,6 +25,8 @@ CONFIGS = {
     "c5": dict(kind="gla", B=32, L=16384, H=32, Dh=64, seg=32, dtype=torch.bfloat16),
     # c2 with the RG-LRU input gating inside the kernels (x, r, i, lam in; c = 8)
     "c2g": dict(kind="rglru_gated", B=8, L=4096, D=2560, seg=32, dtype=torch.bfloat16),
+    # c3 with the rotation angle in place of cos/sin (cos, sin formed in the kernels)
+    "c3a": dict(kind="rotlru_angle", B=16, L=8192, Dp=1024, seg=32, dtype=torch.bfloat16),
 }
 
 DESCRIPTION = {
@@ -35,6 +37,7 @@ DESCRIPTION = {
     "c4": "ssd_scan bf16 B=32 L=16384 H=32 Dh=64 N=128 seg=32",
     "c5": "gla_scan bf16 B=32 L=16384 H=32 Dh=64 seg=32",
     "c2g": "rglru_scan_gated bf16 B=8 L=4096 D=2560 seg=32 (gating in the kernels, c=8)",
+    "c3a": "rotlru_scan_angle bf16 B=16 L=8192 D=2048 seg=32 (cos, sin formed in the kernels)",
 }
 
 GATE_C = 8.0  # the RG-LRU gate exponent scale of c2 / c2g
@@ -85,11 +88,13 @@ def make_inputs(name, device, seed=0, batch=None):
         a = torch.sigmoid(lam) ** (GATE_C * r)
         b = torch.sqrt(1.0 - a * a) * (i * x)
         return (a.to(dt), b.to(dt))
-    if cfg["kind"] == "rotlru":
+    if cfg["kind"] in ("rotlru", "rotlru_angle"):
         Dp = cfg["Dp"]
         x = torch.randn((B, L, 2 * Dp), **f32)
         a = torch.sigmoid(torch.randn((B, L, Dp), **f32) + 3.0)
         th = (torch.rand((B, L, Dp), **f32) * 2.0 - 1.0) * (math.pi / 16)
+        if cfg["kind"] == "rotlru_angle":
+            return (a.to(dt), th.to(dt), x.to(dt))
         return (a.to(dt), torch.cos(th).to(dt), torch.sin(th).to(dt), x.to(dt))
     raise KeyError(name)
 
@@ -109,6 +114,8 @@ def scan_fn(pkg, name):
     seg = CONFIGS[name]["seg"]
     if kind == "rglru_gated":
         return lambda *xs: pkg.rglru_scan_gated(*xs, GATE_C, seg=seg)
+    if kind == "rotlru_angle":
+        return lambda *xs: pkg.rotlru_scan_angle(*xs, seg=seg)
     f = getattr(pkg, f"{kind}_scan")
     return lambda *xs: f(*xs, seg=seg)
 
@@ -121,3 +128,10 @@ def gated_to_plain(x, r, i, lam):
     a = np.exp(GATE_C * r * ls)
     b = np.sqrt(np.maximum(1.0 - a * a, 0.0)) * i * x
     return a.astype(np.float32), b.astype(np.float32)
+
+
+def angle_to_plain(a, theta, x):
+    """numpy (a, theta, x) of c3a -> the (a, cs, sn, x) the plain rotLRU scan
+    takes (the host-side cos/sin of rotlru.py:18-22), for the CPU baselines."""
+    import numpy as np
+    return a, np.cos(theta).astype(np.float32), np.sin(theta).astype(np.float32), x

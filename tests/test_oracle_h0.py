@@ -169,3 +169,32 @@ def test_rglru_gated_gradients_match_finite_difference():
             m[k].reshape(-1)[j] -= eps
             fd[j] = (loss(*p) - loss(*m)) / (2 * eps)
         np.testing.assert_allclose(np.asarray(g).reshape(-1), fd, rtol=1e-5, atol=1e-7)
+
+
+def test_rotlru_angle_gradients_match_finite_difference():
+    """The rotLRU angle oracle (cs = cos theta, sn = sin theta ahead of the
+    scan, rotlru.py:18-22): every gradient against central differences."""
+    rng = np.random.default_rng(13)
+    Bt, T, Dp = 2, 5, 2
+    a = rng.uniform(-1.0, 1.0, (Bt, T, Dp))
+    th = rng.uniform(-3.0, 3.0, (Bt, T, Dp))
+    x = rng.standard_normal((Bt, T, 2 * Dp))
+    h0 = rng.standard_normal((Bt, 2 * Dp))
+    w = rng.standard_normal((Bt, T, 2 * Dp))
+    wf = rng.standard_normal((Bt, 2 * Dp))
+
+    def loss(a_, th_, x_, h0_):
+        y, f = R.rotlru_angle_forward(a_, th_, x_, h0=h0_)
+        return np.sum(y * w) + np.sum(f * wf)
+
+    grads = R.rotlru_angle_backward(a, th, x, w, wf, h0=h0)
+    args = [a, th, x, h0]
+    eps = 1e-6
+    for k, g in enumerate(grads):
+        fd = np.zeros(args[k].size)
+        for j in range(args[k].size):
+            p, m = [v.copy() for v in args], [v.copy() for v in args]
+            p[k].reshape(-1)[j] += eps
+            m[k].reshape(-1)[j] -= eps
+            fd[j] = (loss(*p) - loss(*m)) / (2 * eps)
+        np.testing.assert_allclose(np.asarray(g).reshape(-1), fd, rtol=1e-5, atol=1e-7)
