@@ -245,6 +245,30 @@ MR_API int mr_rotlru_bwd_h0(const float* grad_y, const float* grad_final, const 
                             void* workspace, size_t workspace_bytes, const float* h0, float* grad_h0,
                             void* stream);
 
+/* ------------------------------------------------------ Gated DeltaNet ---
+ * A recurrence the reference carries as a design only
+ * (docs/DESIGN_gated_deltanet.md), built from its pinned recurrence
+ * (section 1, R1''/R2') and adjoint (section 4): per (batch row, head) a state
+ * S [Dh(i), Dh(j)] with
+ *   S_t = alpha_t (I - beta_t k_t k_t^T) S_{t-1} + beta_t k_t v_t^T,
+ *   y_t = S_t^T q_t.
+ * q, k, v [B,L,H,Dh] (q, k L2-normalised by the caller) and alpha, beta [B,L,H]
+ * (already activated: alpha in (0,1], beta in (0,1) for a contraction) in
+ * `dtype`; y [B,L,H,Dh] float32; h_ckpt [B, L/seg, H, Dh, Dh] float32 (the state
+ * after each segment, i-major; the last is the final state); h0 / grad_h0
+ * [B,H,Dh,Dh] float32 or NULL. Dh must be 32 or 64 and L a multiple of seg.
+ * The backward writes grad_q, grad_k, grad_v, grad_alpha, grad_beta in
+ * `dtype` and needs mr_gdn_bwd_workspace_bytes of device scratch. */
+MR_API int mr_gdn_fwd(const void* q, const void* k, const void* v, const void* alpha, const void* beta, int dtype,
+                      int64_t batch, int64_t L, int64_t H, int64_t Dh, int64_t seg, float* y, float* h_ckpt,
+                      const float* h0, void* stream);
+MR_API size_t mr_gdn_bwd_workspace_bytes(int dtype, int64_t batch, int64_t L, int64_t H, int64_t Dh, int64_t seg);
+MR_API int mr_gdn_bwd(const float* grad_y, const float* grad_final, const float* h_ckpt, const void* q,
+                      const void* k, const void* v, const void* alpha, const void* beta, int dtype, int64_t batch,
+                      int64_t L, int64_t H, int64_t Dh, int64_t seg, void* grad_q, void* grad_k, void* grad_v,
+                      void* grad_alpha, void* grad_beta, void* workspace, size_t workspace_bytes, const float* h0,
+                      float* grad_h0, void* stream);
+
 /* ------------------------------------------------- rotLRU, angle input ---
  * The rotLRU scan taking the rotation angle theta [B,L,Dp] in place of cs, sn
  * (no counterpart in the reference, which forms cos and sin in MLX host code

@@ -9,8 +9,11 @@ torch.autograd.Functions over a C-ABI library of sm_100a CUDA kernels
     rotlru  - rotational LRU (complex-diagonal over interleaved pairs)
 
 Beyond the reference: an optional initial state ``h0=`` on every scan
-(chunked prefill), one-token decode steps ``*_step`` on a state cache, and
-``rglru_scan_gated`` with the RG-LRU input gating inside the kernels.
+(chunked prefill), one-token decode steps ``*_step`` on a state cache,
+``rglru_scan_gated`` with the RG-LRU input gating inside the kernels,
+``rotlru_scan_angle`` taking the rotation angle, and
+``gated_deltanet_scan``, the recurrence the reference carries as a design
+(``docs/DESIGN_gated_deltanet.md``).
 
 Import with ``importlib.import_module("mlx-recurrence_b200")`` (the directory
 name carries a hyphen); after that the package is also registered as
@@ -20,6 +23,7 @@ name carries a hyphen); after that the package is also registered as
 import sys as _sys
 
 from ._chassis import DEFAULT_SEG, check_segment_shape, get_or_build_kernel, parity_check
+from .gdn import gated_deltanet_scan, gated_deltanet_scan_reference, gated_deltanet_scan_with_state
 from .gla import gla_scan, gla_scan_reference, gla_scan_with_state, gla_step
 from .rglru import (rglru_scan, rglru_scan_gated, rglru_scan_gated_with_state, rglru_scan_reference,
                     rglru_scan_with_state, rglru_step)
@@ -45,6 +49,10 @@ __all__ = [
     # the RG-LRU scan with its input gating in the kernels (not in the reference)
     "rglru_scan_gated",
     "rglru_scan_gated_with_state",
+    # Gated DeltaNet (a design only in the reference)
+    "gated_deltanet_scan",
+    "gated_deltanet_scan_with_state",
+    "gated_deltanet_scan_reference",
     # one-token decode steps on a float32 state cache (not in the reference)
     "ssd_step",
     "gla_step",

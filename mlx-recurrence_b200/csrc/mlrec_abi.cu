@@ -69,6 +69,9 @@ template <typename T> int rotlru_step_launch(const void*, const void*, const voi
 template <typename T> int rglru_gated_fwd_launch(const void*, const void*, const void*, const float*, float, int64_t, int64_t, int64_t, int64_t, float*, float*, const float*, cudaStream_t);
 template <typename T> int rglru_gated_bwd_launch(const float*, const float*, const float*, const void*, const void*, const void*, const float*, float, int64_t, int64_t, int64_t, int64_t, void*, void*, void*, float*, void*, const float*, float*, cudaStream_t);
 size_t rglru_gated_bwd_ws_bytes(int64_t, int64_t, int64_t, int64_t);
+template <typename T> int gdn_fwd_launch(const void*, const void*, const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, int64_t, float*, float*, const float*, cudaStream_t);
+template <typename T> int gdn_bwd_launch(const float*, const float*, const float*, const void*, const void*, const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, int64_t, void*, void*, void*, void*, void*, void*, const float*, float*, cudaStream_t);
+size_t gdn_bwd_ws_bytes(int64_t, int64_t, int64_t, int64_t, int64_t);
 template <typename T> int rotlru_angle_fwd_launch(const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, float*, float*, const float*, cudaStream_t);
 template <typename T> int rotlru_angle_bwd_launch(const float*, const float*, const float*, const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, void*, void*, void*, float*, const float*, float*, cudaStream_t);
 int umma_selftest_launch(const void*, const void*, const void*, const void*, float*, float*, float*,
@@ -142,7 +145,7 @@ using namespace mr;
 extern "C" {
 
 // 2: the _h0 (initial state) entry points; 3: the decode steps; 4: the gated RG-LRU scan
-int mr_abi_version(void) { return 5; }
+int mr_abi_version(void) { return 6; }
 
 const char* mr_last_error(void) { return g_err; }
 
@@ -358,6 +361,56 @@ int mr_rotlru_angle_bwd(const float* grad_y, const float* grad_final, const floa
   MR_DTYPE_SWITCH(dtype, rotlru_angle_bwd_launch<T>(grad_y, grad_final, h_ckpt, a, theta, x, batch, L, Dp, seg,
                                                     grad_a, grad_theta, grad_x, (float*)workspace, h0, grad_h0,
                                                     st));
+}
+
+// ---------------------------------------------------------- Gated DeltaNet ---
+static int gdn_common_checks(const char* what, int dtype, int64_t batch, int64_t L, int64_t H, int64_t Dh,
+                             int64_t seg) {
+  MR_TRY(check_dims(what, batch, L, H));
+  if (Dh != 32 && Dh != 64)
+    return set_error(MR_E_SHAPE, "%s: Dh=%lld is not supported (32 or 64)", what, (long long)Dh);
+  MR_TRY(check_seg(L, seg, Dh, "Dh"));
+  if (batch * H > (int64_t)INT32_MAX) return set_error(MR_E_SHAPE, "%s: batch*H too large", what);
+  return check_dtype(dtype);
+}
+
+int mr_gdn_fwd(const void* q, const void* k, const void* v, const void* alpha, const void* beta, int dtype,
+               int64_t batch, int64_t L, int64_t H, int64_t Dh, int64_t seg, float* y, float* h_ckpt,
+               const float* h0, void* stream) {
+  g_err[0] = 0;
+  MR_TRY(gdn_common_checks("mr_gdn_fwd", dtype, batch, L, H, Dh, seg));
+  MR_TRY(check_ptrs("mr_gdn_fwd", {q, k, v, alpha, beta, y, h_ckpt}));
+  MR_TRY(check_opt_ptr("mr_gdn_fwd", h0));
+  cudaStream_t st = (cudaStream_t)stream;
+  MR_DTYPE_SWITCH(dtype, gdn_fwd_launch<T>(q, k, v, alpha, beta, batch, L, H, Dh, seg, y, h_ckpt, h0, st));
+}
+
+size_t mr_gdn_bwd_workspace_bytes(int dtype, int64_t batch, int64_t L, int64_t H, int64_t Dh, int64_t seg) {
+  (void)dtype;
+  if (batch <= 0 || L <= 0 || H <= 0 || Dh <= 0 || seg <= 0) return 0;
+  return gdn_bwd_ws_bytes(batch, L, H, Dh, seg);
+}
+
+int mr_gdn_bwd(const float* grad_y, const float* grad_final, const float* h_ckpt, const void* q, const void* k,
+               const void* v, const void* alpha, const void* beta, int dtype, int64_t batch, int64_t L, int64_t H,
+               int64_t Dh, int64_t seg, void* grad_q, void* grad_k, void* grad_v, void* grad_alpha,
+               void* grad_beta, void* workspace, size_t workspace_bytes, const float* h0, float* grad_h0,
+               void* stream) {
+  g_err[0] = 0;
+  MR_TRY(gdn_common_checks("mr_gdn_bwd", dtype, batch, L, H, Dh, seg));
+  MR_TRY(check_ptrs("mr_gdn_bwd", {grad_y, h_ckpt, q, k, v, alpha, beta, grad_q, grad_k, grad_v, grad_alpha,
+                                   grad_beta, workspace}));
+  MR_TRY(check_opt_ptr("mr_gdn_bwd", grad_final));
+  MR_TRY(check_opt_ptr("mr_gdn_bwd", h0));
+  MR_TRY(check_opt_ptr("mr_gdn_bwd", grad_h0));
+  const size_t need = gdn_bwd_ws_bytes(batch, L, H, Dh, seg);
+  if (workspace_bytes < need)
+    return set_error(MR_E_WORKSPACE, "mr_gdn_bwd: workspace of %zu bytes required, got %zu", need,
+                     workspace_bytes);
+  cudaStream_t st = (cudaStream_t)stream;
+  MR_DTYPE_SWITCH(dtype, gdn_bwd_launch<T>(grad_y, grad_final, h_ckpt, q, k, v, alpha, beta, batch, L, H, Dh, seg,
+                                           grad_q, grad_k, grad_v, grad_alpha, grad_beta, workspace, h0, grad_h0,
+                                           st));
 }
 
 // --------------------------------------------------------------------- SSD ---
