@@ -23,13 +23,15 @@
 // (grad_q = S_t go, grad_k = G w + S_{t-1} gp) go through shared memory once
 // per step.
 //
-// Backward: per segment (newest first), phase A replays the forward from the
-// segment's checkpoint, storing w_t and p_t per step and a sub-checkpoint of
-// S every kGdnK steps in a per-CTA scratch (short-lived, L2-resident); phase B
-// walks the sub-blocks newest first, replays the kGdnK states S_{t-1} of the
-// sub-block from its sub-checkpoint into thread-private shared-memory slots
-// (with the stored w, two operations per element and step), and runs the
-// adjoint step (docs/DESIGN_gated_deltanet.md:334-401):
+// The forward also keeps w_t and p_t per step ([B,L,H,2,Dh] float32, the size of
+// two outputs), so the backward never repeats the dot products: per segment
+// (newest first), phase A replays the states from the segment's checkpoint with
+// the stored w (S <- alpha S + k w^T, two operations per element and step) and
+// keeps a sub-checkpoint of S every kGdnK steps in a per-CTA scratch
+// (short-lived, L2-resident); phase B walks the sub-blocks newest first,
+// replays the kGdnK states S_{t-1} of the sub-block from its sub-checkpoint into
+// thread-private shared-memory slots, and runs the adjoint step
+// (docs/DESIGN_gated_deltanet.md:334-401):
 //   G += q go^T;  d = G^T k;  gp = -alpha beta d
 //   grad_q = S_t go,  grad_k = G w + S_{t-1} gp,  grad_v = beta d
 //   grad_alpha = <G, S_{t-1}> - beta d.p,  grad_beta = d.(v - alpha p)
@@ -77,6 +79,48 @@ __device__ __forceinline__ void gdn_update(float (&S)[R], const float (&kr)[R], 
   for (int r = 0; r < R; ++r) S[r] = fmaf(a, S[r], __fmul_rn(kr[r], w));
 }
 
+// 16-byte asynchronous global -> shared copies (each thread waits for its own
+// groups; the block barrier after the wait publishes them)
+__device__ __forceinline__ void gdn_cp16(void* smem, const void* gmem) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem));
+}
+__device__ __forceinline__ void gdn_cp_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void gdn_cp_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
+
+// rows of TS steps of NV (<= 3) [B,L,H,DH] tensors of one (b, h) into shared
+// [NV][TS][DH] (steps past L are not copied)
+template <typename T, int DH, int TS, int NV, int NT>
+__device__ __forceinline__ void gdn_stage_rows(T* dst, const T* s0, const T* s1, const T* s2, int64_t b, int h,
+                                               int L, int H, int t0) {
+  constexpr int CH = DH * (int)sizeof(T) / 16;  // 16-byte chunks per row
+  constexpr int VN = 16 / (int)sizeof(T);
+  for (int c = threadIdx.x; c < NV * TS * CH; c += NT) {
+    const int which = c / (TS * CH), rem = c % (TS * CH), tt = rem / CH, ch = rem % CH;
+    const int t = t0 + tt;
+    const T* src = which == 0 ? s0 : which == 1 ? s1 : s2;
+    if (t < L) gdn_cp16(dst + (which * TS + tt) * DH + ch * VN, src + ((b * L + t) * H + h) * DH + ch * VN);
+  }
+}
+
+// 4 consecutive elements of T (shared memory) as floats
+template <typename T>
+__device__ __forceinline__ float4 gdn_ld4(const T* p) {
+  const Vec<T, 4> x = ld_vec<T, 4>(p);
+  return make_float4(to_f(x.v[0]), to_f(x.v[1]), to_f(x.v[2]), to_f(x.v[3]));
+}
+
+// R consecutive floats (shared memory, 16-byte aligned)
+template <int R>
+__device__ __forceinline__ void gdn_ld_f32(const float* p, float (&f)[R]) {
+#pragma unroll
+  for (int c = 0; c < R / 4; ++c) {
+    const float4 x = *reinterpret_cast<const float4*>(p + 4 * c);
+    f[4 * c] = x.x, f[4 * c + 1] = x.y, f[4 * c + 2] = x.z, f[4 * c + 3] = x.w;
+  }
+}
+
 template <int R>
 __device__ __forceinline__ float gdn_dot(const float (&x)[R], const float (&y)[R]) {
   float acc = 0.f;
@@ -85,75 +129,159 @@ __device__ __forceinline__ float gdn_dot(const float (&x)[R], const float (&y)[R
   return acc;
 }
 
+constexpr int kGdnTS = 16;  // steps per staged block of the forward and the backward's replay
+
 template <typename T, int DH, bool kH0>
 __global__ void __launch_bounds__(DH * 4)
 gdn_fwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
                const T* __restrict__ alpha, const T* __restrict__ beta, int L, int H, int seg,
-               float* __restrict__ y, float* __restrict__ ckpt, const float* __restrict__ h0) {
-  constexpr int R = DH / 4;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+               float* __restrict__ y, float* __restrict__ ckpt, float* __restrict__ wp,
+               const float* __restrict__ h0) {
+  constexpr int R = DH / 4, NT = DH * 4, TS = kGdnTS;
+  static_assert(TS * (DH / 4) == NT, "the conversion pass gives each thread 4 elements of each row");
+  // staged inputs: k, q, v rows as copied [2 buffers][3][TS][DH] of T, as floats
+  // [3][TS][DH], k.q per step [TS], alpha and beta [2][2][TS]
+  __shared__ __align__(16) T srow[2][3 * TS * DH];
+  __shared__ __align__(16) float sf[3 * TS * DH];
+  __shared__ float skq[TS];
+  __shared__ float sab[2][2][TS];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 3, j = warp * 8 + (lane & 7), i0 = g * R;
   const int64_t b = blockIdx.x / H;
   const int h = blockIdx.x % H;
-  const int nseg = L / seg;
+  const int nseg = L / seg, nblk = (L + TS - 1) / TS;
   const int64_t sbase = ((b * H + h) * DH + i0) * (int64_t)DH + j;  // element (i0, j) of [B,H,DH,DH]
   float S[R];
 #pragma unroll
   for (int r = 0; r < R; ++r) S[r] = kH0 ? h0[sbase + r * DH] : 0.f;
 
-  for (int t = 0; t < L; ++t) {
-    const int64_t row = (b * L + t) * H + h;
-    float kr[R], qr[R];
-    gdn_load_rows<T, R>(k + row * DH + i0, kr);
-    gdn_load_rows<T, R>(q + row * DH + i0, qr);
-    const float vj = to_f(v[row * DH + j]);
-    const float a = to_f(alpha[row]), bt = to_f(beta[row]);
-    const float p = gdn_group_sum(gdn_dot(kr, S));
-    const float sq = gdn_group_sum(gdn_dot(qr, S));
-    const float kq = gdn_group_sum(gdn_dot(kr, qr));
-    const float w = bt * fmaf(-a, p, vj);
-    if (g == 0) y[row * DH + j] = fmaf(a, sq, kq * w);
-    gdn_update(S, kr, a, w);
-    if ((t + 1) % seg == 0) {
-      float* c = ckpt + ((b * nseg + (t + 1) / seg - 1) * H + h) * (int64_t)DH * DH + (int64_t)i0 * DH + j;
-#pragma unroll
-      for (int r = 0; r < R; ++r) c[r * DH] = S[r];
+  // alpha, beta of a block: thread tid < 2*TS holds one value until it is stored
+  auto load_ab = [&](int blk) {
+    const int t = blk * TS + (tid % TS);
+    return (tid < 2 * TS && t < L) ? to_f((tid < TS ? alpha : beta)[(b * L + t) * H + h]) : 0.f;
+  };
+  gdn_stage_rows<T, DH, TS, 3, NT>(srow[0], k, q, v, b, h, L, H, 0);
+  gdn_cp_commit();
+  float ab = load_ab(0);
+  if (tid < 2 * TS) sab[0][tid / TS][tid % TS] = ab;
+
+  for (int blk = 0; blk < nblk; ++blk) {
+    const int buf = blk & 1;
+    if (blk + 1 < nblk) {
+      gdn_stage_rows<T, DH, TS, 3, NT>(srow[buf ^ 1], k, q, v, b, h, L, H, (blk + 1) * TS);
+      ab = load_ab(blk + 1);
     }
+    gdn_cp_commit();
+    gdn_cp_wait<1>();
+    __syncthreads();
+    {  // one pass per block: rows to floats (4 elements of k, q, v per thread) and k.q per step
+      const int tt = tid / (DH / 4), c4 = (tid % (DH / 4)) * 4;
+      const T* src = srow[buf] + tt * DH + c4;
+      const float4 kk = gdn_ld4(src), qq = gdn_ld4(src + TS * DH), vv = gdn_ld4(src + 2 * TS * DH);
+      float* dst = sf + tt * DH + c4;
+      *reinterpret_cast<float4*>(dst) = kk;
+      *reinterpret_cast<float4*>(dst + TS * DH) = qq;
+      *reinterpret_cast<float4*>(dst + 2 * TS * DH) = vv;
+      float part = fmaf(kk.x, qq.x, fmaf(kk.y, qq.y, fmaf(kk.z, qq.z, kk.w * qq.w)));
+#pragma unroll
+      for (int o = 1; o < DH / 4; o <<= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+      if (c4 == 0) skq[tt] = part;
+    }
+    __syncthreads();
+    const float* fk = sf;
+    const float* fq = sf + TS * DH;
+    const float* fv = sf + 2 * TS * DH;
+    const int nt = min(TS, L - blk * TS);
+    for (int tt = 0; tt < nt; ++tt) {
+      const int t = blk * TS + tt;
+      float kr[R], qr[R];
+      gdn_ld_f32<R>(fk + tt * DH + i0, kr);
+      gdn_ld_f32<R>(fq + tt * DH + i0, qr);
+      const float vj = fv[tt * DH + j];
+      const float a = sab[buf][0][tt], bt = sab[buf][1][tt];
+      const float p = gdn_group_sum(gdn_dot(kr, S));
+      const float sqv = gdn_group_sum(gdn_dot(qr, S));
+      const float kq = skq[tt];
+      const float w = bt * fmaf(-a, p, vj);
+      if (g == 0) {
+        const int64_t row = (b * L + t) * H + h;
+        y[row * DH + j] = fmaf(a, sqv, kq * w);
+        if (wp != nullptr) {
+          wp[row * 2 * DH + j] = w;
+          wp[(row * 2 + 1) * DH + j] = p;
+        }
+      }
+      gdn_update(S, kr, a, w);
+      if ((t + 1) % seg == 0) {
+        float* c = ckpt + ((b * nseg + (t + 1) / seg - 1) * H + h) * (int64_t)DH * DH + (int64_t)i0 * DH + j;
+#pragma unroll
+        for (int r = 0; r < R; ++r) c[r * DH] = S[r];
+      }
+    }
+    if (blk + 1 < nblk && tid < 2 * TS) sab[buf ^ 1][tid / TS][tid % TS] = ab;
+    __syncthreads();  // the next block's copies go into this buffer
   }
 }
 
-template <int DH>
+// Shared memory of the backward (bytes): thread-private state slots [K][R][NT],
+// the reduction buffer [2][DH(j)][DH + 4 (i)], the per-warp scalars, and the
+// staged inputs, phase A's ([2][alpha][TS], [2][w][TS][DH] float, [2 buffers][k][TS][DH] of T)
+// and phase B's ([2][go, w, p][K][DH] float, [2][alpha, beta][K], the
+// current sub-block's q, k, v as floats [3][K][DH] and w.go [K], [2][q, k, v][K][DH]
+// of T) sharing one region.
+template <typename T, int DH>
 struct GdnBwdSmem {
-  static constexpr int NT = DH * 4;
-  static constexpr size_t slots = (size_t)kGdnK * DH * DH;  // [K][R][NT], thread-private
-  static constexpr size_t red = (size_t)2 * DH * (DH + 4);  // [2][DH(j)][DH + 4 (i)]
-  static constexpr size_t bytes = (slots + red + 2 * (NT / 32)) * sizeof(float);
+  static constexpr int NT = DH * 4, K = kGdnK, TS = kGdnTS;
+  static constexpr size_t slots = (size_t)K * DH * DH * 4;
+  static constexpr size_t red = (size_t)2 * DH * (DH + 4) * 4;
+  static constexpr size_t rsc = 2 * (NT / 32) * 4 < 16 ? 16 : 2 * (NT / 32) * 4;
+  static constexpr size_t a_ab = (size_t)2 * TS * 4, a_w = (size_t)2 * TS * DH * 4;
+  static constexpr size_t a_rows = (size_t)2 * TS * DH * sizeof(T);
+  static constexpr size_t b_f32 = (size_t)2 * 3 * K * DH * 4, b_ab = (size_t)2 * 2 * K * 4;
+  static constexpr size_t b_cvt = (size_t)3 * K * DH * 4, b_wgo = 16;
+  static constexpr size_t b_rows = (size_t)2 * 3 * K * DH * sizeof(T);
+  static constexpr size_t stage_a = a_ab + a_w + a_rows, stage_b = b_f32 + b_ab + b_cvt + b_wgo + b_rows;
+  static constexpr size_t stage = stage_a > stage_b ? stage_a : stage_b;
+  static constexpr size_t bytes = slots + red + rsc + stage;
 };
 
-// per-CTA scratch: sub-checkpoints [ceil(seg/K)][R][NT], then w and p [seg][DH]
+// per-CTA scratch: sub-checkpoints [ceil(seg/K)][R][NT]
 __host__ __device__ __forceinline__ int64_t gdn_scratch_floats(int64_t Dh, int64_t seg) {
-  return (seg + kGdnK - 1) / kGdnK * Dh * Dh + 2 * seg * Dh;
+  return (seg + kGdnK - 1) / kGdnK * Dh * Dh;
 }
 
 template <typename T, int DH, bool kH0>
 __global__ void __launch_bounds__(DH * 4, DH == 64 ? 2 : 4)
 gdn_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfinal, const float* __restrict__ ckpt,
-               const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
+               const float* __restrict__ wp, const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
                const T* __restrict__ alpha, const T* __restrict__ beta, int L, int H, int seg, int units,
                T* __restrict__ gq, T* __restrict__ gk, T* __restrict__ gv, T* __restrict__ galpha,
                T* __restrict__ gbeta, float* __restrict__ ws, const float* __restrict__ h0,
                float* __restrict__ gh0) {
-  constexpr int R = DH / 4, NT = DH * 4, NW = NT / 32, K = kGdnK, RS = DH + 4;
+  using SM = GdnBwdSmem<T, DH>;
+  constexpr int R = DH / 4, NT = DH * 4, NW = NT / 32, K = kGdnK, TS = kGdnTS, RS = DH + 4;
+  constexpr int CHF = DH * 4 / 16;  // 16-byte chunks of a float row
   extern __shared__ float4 gdn_smem[];
-  float* slots = reinterpret_cast<float*>(gdn_smem);
-  float* red = slots + K * DH * DH;
-  float* rsc = red + 2 * DH * RS;
+  unsigned char* base = reinterpret_cast<unsigned char*>(gdn_smem);
+  float* slots = reinterpret_cast<float*>(base);
+  float* red = reinterpret_cast<float*>(base + SM::slots);
+  float* rsc = reinterpret_cast<float*>(base + SM::slots + SM::red);
+  unsigned char* stg = base + SM::slots + SM::red + SM::rsc;
+  // phase A staging
+  float* a_ab = reinterpret_cast<float*>(stg);                 // [2][TS]: alpha
+  float* a_w = reinterpret_cast<float*>(stg + SM::a_ab);       // [2][TS][DH]: w
+  T* a_rows = reinterpret_cast<T*>(stg + SM::a_ab + SM::a_w);  // [2][TS][DH]: k
+  // phase B staging
+  float* b_f32 = reinterpret_cast<float*>(stg);                // [2][3][K][DH]
+  float* b_ab = reinterpret_cast<float*>(stg + SM::b_f32);     // [2][2][K]
+  float* b_cvt = reinterpret_cast<float*>(stg + SM::b_f32 + SM::b_ab);  // [3][K][DH]: q, k, v
+  float* b_wgo = b_cvt + 3 * K * DH;                                   // [K]
+  T* b_rows = reinterpret_cast<T*>(stg + SM::b_f32 + SM::b_ab + SM::b_cvt + SM::b_wgo);  // [2][3][K][DH]
+
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 3, j = warp * 8 + (lane & 7), i0 = g * R;
-  const int nseg = L / seg, nsb = (seg + K - 1) / K;
+  const int nseg = L / seg, nsb = (seg + K - 1) / K, nblk = (seg + TS - 1) / TS;
   float* sub = ws + (int64_t)blockIdx.x * gdn_scratch_floats(DH, seg);
-  float* vw = sub + (int64_t)nsb * DH * DH;  // [seg][DH]
-  float* vp = vw + (int64_t)seg * DH;        // [seg][DH]
   // role in the reduction over j: vector (0 grad_q, 1 grad_k), quad of rows, column phase
   const int rv = tid / (NT / 2), rq = (tid % (NT / 2)) / 8, rj = tid & 7;
 
@@ -166,38 +294,109 @@ gdn_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfinal, c
     for (int r = 0; r < R; ++r) G[r] = gfinal != nullptr ? gfinal[sbase + r * DH] : 0.f;
 
     for (int s = nseg - 1; s >= 0; --s) {
-      const int64_t t0 = (int64_t)s * seg;
-      // ---- phase A: replay the segment, keep w, p and every K-th state
+      const int t0 = s * seg;
+      // alpha / beta of NS steps from step tl0 of the segment (thread tid < 2*NS holds one)
+      auto load_ab = [&](int tl0, int NS) {
+        const int tl = tl0 + tid % NS;
+        return (tid < 2 * NS && tl < seg) ? to_f((tid < NS ? alpha : beta)[(b * L + t0 + tl) * H + h]) : 0.f;
+      };
+      // ---- phase A: replay the segment's states with the stored w, keep every K-th
       {
         float S[R];
         const float* src = s > 0 ? ckpt + ((b * nseg + s - 1) * H + h) * (int64_t)DH * DH + (int64_t)i0 * DH + j
                            : kH0 ? h0 + sbase : nullptr;
 #pragma unroll
         for (int r = 0; r < R; ++r) S[r] = src != nullptr ? src[r * DH] : 0.f;
-        for (int tl = 0; tl < seg; ++tl) {
-          if (tl % K == 0) {
-            float* d = sub + (int64_t)(tl / K) * DH * DH + tid;
+        // k rows (T) and w rows (float) of TS steps from step tl0 of the segment into buffer bb
+        auto stage_a = [&](int tl0, int bb) {
+          gdn_stage_rows<T, DH, TS, 1, NT>(a_rows + bb * TS * DH, k, k, k, b, h, L, H, t0 + tl0);
+          for (int c = tid; c < TS * CHF; c += NT) {
+            const int tt = c / CHF, ch = c % CHF, tl = tl0 + tt;
+            if (tl < seg) gdn_cp16(a_w + (bb * TS + tt) * DH + ch * 4, wp + ((b * L + t0 + tl) * H + h) * 2 * DH + ch * 4);
+          }
+        };
+        stage_a(0, 0);
+        gdn_cp_commit();
+        float ab = load_ab(0, TS);
+        if (tid < TS) a_ab[tid] = ab;
+        for (int blk = 0; blk < nblk; ++blk) {
+          const int buf = blk & 1;
+          if (blk + 1 < nblk) {
+            stage_a((blk + 1) * TS, buf ^ 1);
+            ab = load_ab((blk + 1) * TS, TS);
+          }
+          gdn_cp_commit();
+          gdn_cp_wait<1>();
+          __syncthreads();
+          const T* sk = a_rows + buf * TS * DH;
+          const float* sw = a_w + buf * TS * DH;
+          const float* sa = a_ab + buf * TS;
+          const int nt = min(TS, seg - blk * TS);
+          for (int tt = 0; tt < nt; ++tt) {
+            const int tl = blk * TS + tt;
+            if (tl % K == 0) {
+              float* d = sub + (int64_t)(tl / K) * DH * DH + tid;
 #pragma unroll
-            for (int r = 0; r < R; ++r) d[r * NT] = S[r];
+              for (int r = 0; r < R; ++r) d[r * NT] = S[r];
+            }
+            float kr[R];
+            gdn_load_rows<T, R>(sk + tt * DH + i0, kr);
+            gdn_update(S, kr, sa[tt], sw[tt * DH + j]);
           }
-          const int64_t row = (b * L + t0 + tl) * H + h;
-          float kr[R];
-          gdn_load_rows<T, R>(k + row * DH + i0, kr);
-          const float vj = to_f(v[row * DH + j]);
-          const float a = to_f(alpha[row]), bt = to_f(beta[row]);
-          const float p = gdn_group_sum(gdn_dot(kr, S));
-          const float w = bt * fmaf(-a, p, vj);
-          if (g == 0) {
-            vw[tl * DH + j] = w;
-            vp[tl * DH + j] = p;
-          }
-          gdn_update(S, kr, a, w);
+          if (blk + 1 < nblk && tid < TS) a_ab[(buf ^ 1) * TS + tid] = ab;
+          __syncthreads();  // this buffer is refilled next; sub-checkpoints visible to the block
         }
       }
-      __syncthreads();  // w, p of the segment visible to the column's four row groups
 
-      // ---- phase B: sub-blocks newest first
+      // ---- phase B: sub-blocks newest first, their inputs staged one sub-block ahead
+      auto stage_b = [&](int sb, int bb) {
+        gdn_stage_rows<T, DH, K, 3, NT>(b_rows + bb * 3 * K * DH, q, k, v, b, h, L, H, t0 + sb * K);
+        float* dst = b_f32 + bb * 3 * K * DH;
+        for (int c = tid; c < 3 * K * CHF; c += NT) {
+          const int which = c / (K * CHF), rem = c % (K * CHF), tt = rem / CHF, ch = rem % CHF;
+          const int tl = sb * K + tt;
+          if (tl < seg) {
+            const int64_t row = (b * L + t0 + tl) * H + h;
+            const float* src = which == 0 ? gy + row * DH : wp + (row * 2 + (which - 1)) * DH;
+            gdn_cp16(dst + (which * K + tt) * DH + ch * 4, src + ch * 4);
+          }
+        }
+      };
+      stage_b(nsb - 1, 0);
+      gdn_cp_commit();
+      float ab = load_ab((nsb - 1) * K, K);
+      if (tid < 2 * K) b_ab[tid] = ab;
       for (int sb = nsb - 1; sb >= 0; --sb) {
+        const int bb = (nsb - 1 - sb) & 1;
+        if (sb > 0) {
+          stage_b(sb - 1, bb ^ 1);
+          ab = load_ab((sb - 1) * K, K);
+        }
+        gdn_cp_commit();
+        gdn_cp_wait<1>();
+        __syncthreads();
+        const float* fgo = b_f32 + bb * 3 * K * DH;
+        const float* fw = fgo + K * DH;
+        const float* fp = fw + K * DH;
+        const float* fab = b_ab + bb * 2 * K;
+        if (tid < K * DH / 4) {  // the sub-block's q, k, v rows as floats, and w.go per step
+          const int m = tid / (DH / 4), c4 = (tid % (DH / 4)) * 4;
+          const T* src = b_rows + bb * 3 * K * DH + m * DH + c4;
+          float* dst = b_cvt + m * DH + c4;
+          *reinterpret_cast<float4*>(dst) = gdn_ld4(src);
+          *reinterpret_cast<float4*>(dst + K * DH) = gdn_ld4(src + K * DH);
+          *reinterpret_cast<float4*>(dst + 2 * K * DH) = gdn_ld4(src + 2 * K * DH);
+          const float4 ww = *reinterpret_cast<const float4*>(fw + m * DH + c4);
+          const float4 gg = *reinterpret_cast<const float4*>(fgo + m * DH + c4);
+          float part = fmaf(ww.x, gg.x, fmaf(ww.y, gg.y, fmaf(ww.z, gg.z, ww.w * gg.w)));
+#pragma unroll
+          for (int o = 1; o < DH / 4; o <<= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+          if (c4 == 0) b_wgo[m] = part;
+        }
+        __syncthreads();
+        const float* rq_ = b_cvt;            // q rows
+        const float* rk_ = b_cvt + K * DH;   // k rows
+        const float* rv_ = b_cvt + 2 * K * DH;  // v rows
         const int tb = sb * K, nk = min(K, seg - tb);
         {
           float cur[R];
@@ -207,38 +406,35 @@ gdn_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfinal, c
             cur[r] = src[r * NT];
             slots[r * NT + tid] = cur[r];
           }
-#pragma unroll
-          for (int m = 1; m < K; ++m) {
-            if (m < nk) {
-              const int tl = tb + m - 1;
-              const int64_t row = (b * L + t0 + tl) * H + h;
+#pragma unroll 1
+          for (int m = 1; m < nk; ++m) {
+            {
               float kr[R];
-              gdn_load_rows<T, R>(k + row * DH + i0, kr);
-              gdn_update(cur, kr, to_f(alpha[row]), vw[tl * DH + j]);
+              gdn_ld_f32<R>(rk_ + (m - 1) * DH + i0, kr);
+              gdn_update(cur, kr, fab[m - 1], fw[(m - 1) * DH + j]);
 #pragma unroll
               for (int r = 0; r < R; ++r) slots[(m * R + r) * NT + tid] = cur[r];
             }
           }
         }
-#pragma unroll
-        for (int m = K - 1; m >= 0; --m) {
-          if (m < nk) {
-            const int tl = tb + m;
-            const int64_t row = (b * L + t0 + tl) * H + h;
+#pragma unroll 1
+        for (int m = nk - 1; m >= 0; --m) {
+          {
+            const int64_t row = (b * L + t0 + tb + m) * H + h;
             float kr[R], Sp[R];
-            gdn_load_rows<T, R>(k + row * DH + i0, kr);
-            const float go = gy[row * DH + j];
+            gdn_ld_f32<R>(rk_ + m * DH + i0, kr);
+            const float go = fgo[m * DH + j];
             {
               float qr[R];
-              gdn_load_rows<T, R>(q + row * DH + i0, qr);
+              gdn_ld_f32<R>(rq_ + m * DH + i0, qr);
 #pragma unroll
               for (int r = 0; r < R; ++r) G[r] = fmaf(qr[r], go, G[r]);  // output seed (B0)
             }
 #pragma unroll
             for (int r = 0; r < R; ++r) Sp[r] = slots[(m * R + r) * NT + tid];
-            const float vj = to_f(v[row * DH + j]);
-            const float a = to_f(alpha[row]), bt = to_f(beta[row]);
-            const float w = vw[tl * DH + j], p = vp[tl * DH + j];
+            const float vj = rv_[m * DH + j];
+            const float a = fab[m], bt = fab[K + m];
+            const float w = fw[m * DH + j], p = fp[m * DH + j];
             const float d = gdn_group_sum(gdn_dot(kr, G));
             const float gp = -a * bt * d;
             float gaP = gdn_dot(G, Sp), gbP = 0.f;
@@ -247,7 +443,8 @@ gdn_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfinal, c
               gbP = d * fmaf(-a, p, vj);
               gv[row * DH + j] = from_f<T>(bt * d);
             }
-            // this column's terms of grad_q (S_t go) and grad_k (G w + S_{t-1} gp)
+            // this column's terms of grad_q and grad_k (G w + S_{t-1} gp); grad_q =
+            // S_t go = alpha S_{t-1} go + k (w.go), the last term added by the reducer
             float* rw = red + (int64_t)j * RS + i0;
 #pragma unroll
             for (int c = 0; c < R / 4; ++c) {
@@ -257,7 +454,7 @@ gdn_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfinal, c
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
                 const int r = 4 * c + e;
-                p1[e] = fmaf(a, Sp[r], kr[r] * w) * go;
+                p1[e] = Sp[r] * go;
                 p2[e] = fmaf(G[r], w, Sp[r] * gp);
               }
               *reinterpret_cast<float4*>(rw + 4 * c) = r1;
@@ -288,7 +485,15 @@ gdn_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfinal, c
                 acc.w += __shfl_xor_sync(0xffffffffu, acc.w, o);
               }
               if (rj == 0) {
-                const float out[4] = {acc.x, acc.y, acc.z, acc.w};
+                float out[4] = {acc.x, acc.y, acc.z, acc.w};
+                if (rv == 0) {  // grad_q = alpha (S_{t-1} go) + k (w.go)
+                  const float4 kk = *reinterpret_cast<const float4*>(rk_ + m * DH + 4 * rq);
+                  const float wg = b_wgo[m];
+                  out[0] = fmaf(a, out[0], kk.x * wg);
+                  out[1] = fmaf(a, out[1], kk.y * wg);
+                  out[2] = fmaf(a, out[2], kk.z * wg);
+                  out[3] = fmaf(a, out[3], kk.w * wg);
+                }
                 st_vec<T, 4>((rv == 0 ? gq : gk) + row * DH + 4 * rq, out);
               }
               if (tid == 0) {
@@ -305,6 +510,8 @@ gdn_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfinal, c
             __syncthreads();
           }
         }
+        if (sb > 0 && tid < 2 * K) b_ab[(bb ^ 1) * 2 * K + tid] = ab;
+        __syncthreads();  // the staged buffer is refilled next
       }
     }
     // the adjoint carried past step 0 is the gradient of the initial state
@@ -327,20 +534,20 @@ static int gdn_set_smem(Kern kernel, size_t bytes) {
 
 template <typename T, int DH>
 static int gdn_fwd_dh(const T* q, const T* k, const T* v, const T* al, const T* be, int64_t batch, int64_t L,
-                      int64_t H, int64_t seg, float* y, float* ckpt, const float* h0, cudaStream_t st) {
+                      int64_t H, int64_t seg, float* y, float* ckpt, float* wp, const float* h0, cudaStream_t st) {
   const dim3 grid((unsigned)(batch * H));
   auto kern = h0 != nullptr ? gdn_fwd_kernel<T, DH, true> : gdn_fwd_kernel<T, DH, false>;
-  kern<<<grid, DH * 4, 0, st>>>(q, k, v, al, be, (int)L, (int)H, (int)seg, y, ckpt, h0);
+  kern<<<grid, DH * 4, 0, st>>>(q, k, v, al, be, (int)L, (int)H, (int)seg, y, ckpt, wp, h0);
   return check_launch("gdn_fwd_kernel");
 }
 
 template <typename T>
 int gdn_fwd_launch(const void* q, const void* k, const void* v, const void* alpha, const void* beta, int64_t batch,
-                   int64_t L, int64_t H, int64_t Dh, int64_t seg, float* y, float* ckpt, const float* h0,
-                   cudaStream_t st) {
+                   int64_t L, int64_t H, int64_t Dh, int64_t seg, float* y, float* ckpt, float* wp,
+                   const float* h0, cudaStream_t st) {
   const T *q_ = (const T*)q, *k_ = (const T*)k, *v_ = (const T*)v, *a_ = (const T*)alpha, *b_ = (const T*)beta;
-  if (Dh == 32) return gdn_fwd_dh<T, 32>(q_, k_, v_, a_, b_, batch, L, H, seg, y, ckpt, h0, st);
-  return gdn_fwd_dh<T, 64>(q_, k_, v_, a_, b_, batch, L, H, seg, y, ckpt, h0, st);
+  if (Dh == 32) return gdn_fwd_dh<T, 32>(q_, k_, v_, a_, b_, batch, L, H, seg, y, ckpt, wp, h0, st);
+  return gdn_fwd_dh<T, 64>(q_, k_, v_, a_, b_, batch, L, H, seg, y, ckpt, wp, h0, st);
 }
 
 static int64_t gdn_bwd_grid(int64_t batch, int64_t H) {
@@ -354,36 +561,38 @@ size_t gdn_bwd_ws_bytes(int64_t batch, int64_t L, int64_t H, int64_t Dh, int64_t
 }
 
 template <typename T, int DH>
-static int gdn_bwd_dh(const float* gy, const float* gf, const float* ckpt, const T* q, const T* k, const T* v,
+static int gdn_bwd_dh(const float* gy, const float* gf, const float* ckpt, const float* wp, const T* q, const T* k, const T* v,
                       const T* al, const T* be, int64_t batch, int64_t L, int64_t H, int64_t seg, T* gq, T* gk,
                       T* gv, T* ga, T* gb, float* ws, const float* h0, float* gh0, cudaStream_t st) {
-  constexpr size_t sm = GdnBwdSmem<DH>::bytes;
+  constexpr size_t sm = GdnBwdSmem<T, DH>::bytes;
   auto kern = h0 != nullptr ? gdn_bwd_kernel<T, DH, true> : gdn_bwd_kernel<T, DH, false>;
   if (int rc = gdn_set_smem(kern, sm)) return rc;
   const dim3 grid((unsigned)gdn_bwd_grid(batch, H));
-  kern<<<grid, DH * 4, sm, st>>>(gy, gf, ckpt, q, k, v, al, be, (int)L, (int)H, (int)seg, (int)(batch * H), gq, gk,
+  kern<<<grid, DH * 4, sm, st>>>(gy, gf, ckpt, wp, q, k, v, al, be, (int)L, (int)H, (int)seg, (int)(batch * H), gq, gk,
                                  gv, ga, gb, ws, h0, gh0);
   return check_launch("gdn_bwd_kernel");
 }
 
 template <typename T>
-int gdn_bwd_launch(const float* gy, const float* gf, const float* ckpt, const void* q, const void* k, const void* v,
+int gdn_bwd_launch(const float* gy, const float* gf, const float* ckpt, const float* wp, const void* q, const void* k, const void* v,
                    const void* alpha, const void* beta, int64_t batch, int64_t L, int64_t H, int64_t Dh, int64_t seg,
                    void* gq, void* gk, void* gv, void* galpha, void* gbeta, void* ws, const float* h0, float* gh0,
                    cudaStream_t st) {
   const T *q_ = (const T*)q, *k_ = (const T*)k, *v_ = (const T*)v, *a_ = (const T*)alpha, *b_ = (const T*)beta;
   T *gq_ = (T*)gq, *gk_ = (T*)gk, *gv_ = (T*)gv, *ga_ = (T*)galpha, *gb_ = (T*)gbeta;
   if (Dh == 32)
-    return gdn_bwd_dh<T, 32>(gy, gf, ckpt, q_, k_, v_, a_, b_, batch, L, H, seg, gq_, gk_, gv_, ga_, gb_,
+    return gdn_bwd_dh<T, 32>(gy, gf, ckpt, wp, q_, k_, v_, a_, b_, batch, L, H, seg, gq_, gk_, gv_, ga_, gb_,
                              (float*)ws, h0, gh0, st);
-  return gdn_bwd_dh<T, 64>(gy, gf, ckpt, q_, k_, v_, a_, b_, batch, L, H, seg, gq_, gk_, gv_, ga_, gb_, (float*)ws,
+  return gdn_bwd_dh<T, 64>(gy, gf, ckpt, wp, q_, k_, v_, a_, b_, batch, L, H, seg, gq_, gk_, gv_, ga_, gb_, (float*)ws,
                            h0, gh0, st);
 }
 
 #define MR_INST(T)                                                                                              \
   template int gdn_fwd_launch<T>(const void*, const void*, const void*, const void*, const void*, int64_t,     \
-                                 int64_t, int64_t, int64_t, int64_t, float*, float*, const float*, cudaStream_t); \
-  template int gdn_bwd_launch<T>(const float*, const float*, const float*, const void*, const void*,           \
+                                 int64_t, int64_t, int64_t, int64_t, float*, float*, float*, const float*,     \
+                                 cudaStream_t);                                                               \
+  template int gdn_bwd_launch<T>(const float*, const float*, const float*, const float*, const void*,          \
+                                 const void*,                                                                 \
                                  const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t,    \
                                  int64_t, void*, void*, void*, void*, void*, void*, const float*, float*,      \
                                  cudaStream_t);

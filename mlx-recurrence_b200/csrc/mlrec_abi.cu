@@ -69,8 +69,8 @@ template <typename T> int rotlru_step_launch(const void*, const void*, const voi
 template <typename T> int rglru_gated_fwd_launch(const void*, const void*, const void*, const float*, float, int64_t, int64_t, int64_t, int64_t, float*, float*, const float*, cudaStream_t);
 template <typename T> int rglru_gated_bwd_launch(const float*, const float*, const float*, const void*, const void*, const void*, const float*, float, int64_t, int64_t, int64_t, int64_t, void*, void*, void*, float*, void*, const float*, float*, cudaStream_t);
 size_t rglru_gated_bwd_ws_bytes(int64_t, int64_t, int64_t, int64_t);
-template <typename T> int gdn_fwd_launch(const void*, const void*, const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, int64_t, float*, float*, const float*, cudaStream_t);
-template <typename T> int gdn_bwd_launch(const float*, const float*, const float*, const void*, const void*, const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, int64_t, void*, void*, void*, void*, void*, void*, const float*, float*, cudaStream_t);
+template <typename T> int gdn_fwd_launch(const void*, const void*, const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, int64_t, float*, float*, float*, const float*, cudaStream_t);
+template <typename T> int gdn_bwd_launch(const float*, const float*, const float*, const float*, const void*, const void*, const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, int64_t, void*, void*, void*, void*, void*, void*, const float*, float*, cudaStream_t);
 size_t gdn_bwd_ws_bytes(int64_t, int64_t, int64_t, int64_t, int64_t);
 template <typename T> int rotlru_angle_fwd_launch(const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, float*, float*, const float*, cudaStream_t);
 template <typename T> int rotlru_angle_bwd_launch(const float*, const float*, const float*, const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, void*, void*, void*, float*, const float*, float*, cudaStream_t);
@@ -376,13 +376,15 @@ static int gdn_common_checks(const char* what, int dtype, int64_t batch, int64_t
 
 int mr_gdn_fwd(const void* q, const void* k, const void* v, const void* alpha, const void* beta, int dtype,
                int64_t batch, int64_t L, int64_t H, int64_t Dh, int64_t seg, float* y, float* h_ckpt,
-               const float* h0, void* stream) {
+               float* step_cache, const float* h0, void* stream) {
   g_err[0] = 0;
   MR_TRY(gdn_common_checks("mr_gdn_fwd", dtype, batch, L, H, Dh, seg));
   MR_TRY(check_ptrs("mr_gdn_fwd", {q, k, v, alpha, beta, y, h_ckpt}));
+  MR_TRY(check_opt_ptr("mr_gdn_fwd", step_cache));
   MR_TRY(check_opt_ptr("mr_gdn_fwd", h0));
   cudaStream_t st = (cudaStream_t)stream;
-  MR_DTYPE_SWITCH(dtype, gdn_fwd_launch<T>(q, k, v, alpha, beta, batch, L, H, Dh, seg, y, h_ckpt, h0, st));
+  MR_DTYPE_SWITCH(dtype, gdn_fwd_launch<T>(q, k, v, alpha, beta, batch, L, H, Dh, seg, y, h_ckpt, step_cache, h0,
+                                           st));
 }
 
 size_t mr_gdn_bwd_workspace_bytes(int dtype, int64_t batch, int64_t L, int64_t H, int64_t Dh, int64_t seg) {
@@ -391,15 +393,16 @@ size_t mr_gdn_bwd_workspace_bytes(int dtype, int64_t batch, int64_t L, int64_t H
   return gdn_bwd_ws_bytes(batch, L, H, Dh, seg);
 }
 
-int mr_gdn_bwd(const float* grad_y, const float* grad_final, const float* h_ckpt, const void* q, const void* k,
+int mr_gdn_bwd(const float* grad_y, const float* grad_final, const float* h_ckpt, const float* step_cache,
+               const void* q, const void* k,
                const void* v, const void* alpha, const void* beta, int dtype, int64_t batch, int64_t L, int64_t H,
                int64_t Dh, int64_t seg, void* grad_q, void* grad_k, void* grad_v, void* grad_alpha,
                void* grad_beta, void* workspace, size_t workspace_bytes, const float* h0, float* grad_h0,
                void* stream) {
   g_err[0] = 0;
   MR_TRY(gdn_common_checks("mr_gdn_bwd", dtype, batch, L, H, Dh, seg));
-  MR_TRY(check_ptrs("mr_gdn_bwd", {grad_y, h_ckpt, q, k, v, alpha, beta, grad_q, grad_k, grad_v, grad_alpha,
-                                   grad_beta, workspace}));
+  MR_TRY(check_ptrs("mr_gdn_bwd", {grad_y, h_ckpt, step_cache, q, k, v, alpha, beta, grad_q, grad_k, grad_v,
+                                   grad_alpha, grad_beta, workspace}));
   MR_TRY(check_opt_ptr("mr_gdn_bwd", grad_final));
   MR_TRY(check_opt_ptr("mr_gdn_bwd", h0));
   MR_TRY(check_opt_ptr("mr_gdn_bwd", grad_h0));
@@ -408,7 +411,7 @@ int mr_gdn_bwd(const float* grad_y, const float* grad_final, const float* h_ckpt
     return set_error(MR_E_WORKSPACE, "mr_gdn_bwd: workspace of %zu bytes required, got %zu", need,
                      workspace_bytes);
   cudaStream_t st = (cudaStream_t)stream;
-  MR_DTYPE_SWITCH(dtype, gdn_bwd_launch<T>(grad_y, grad_final, h_ckpt, q, k, v, alpha, beta, batch, L, H, Dh, seg,
+  MR_DTYPE_SWITCH(dtype, gdn_bwd_launch<T>(grad_y, grad_final, h_ckpt, step_cache, q, k, v, alpha, beta, batch, L, H, Dh, seg,
                                            grad_q, grad_k, grad_v, grad_alpha, grad_beta, workspace, h0, grad_h0,
                                            st));
 }

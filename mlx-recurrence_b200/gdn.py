@@ -53,16 +53,20 @@ class _GDNScan(torch.autograd.Function):
         h0_ = prep_h0(h0, (Bt, H, Dh, Dh), dev)
         y = torch.empty((Bt, L, H, Dh), dtype=torch.float32, device=dev)
         ckpt = torch.empty((Bt, L // seg, H, Dh, Dh), dtype=torch.float32, device=dev)
+        # w and p of every step, kept for the backward only when a gradient is wanted
+        cache = (torch.empty((Bt, L, H, 2, Dh), dtype=torch.float32, device=dev)
+                 if any(ctx.needs_input_grad) else None)
         with torch.cuda.device(dev):
             _lib.call("mr_gdn_fwd", _lib.ptr(q_), _lib.ptr(k_), _lib.ptr(v_), _lib.ptr(a_), _lib.ptr(b_), code,
-                      Bt, L, H, Dh, seg, _lib.ptr(y), _lib.ptr(ckpt), _lib.ptr(h0_), _lib.stream_of(dev))
-        ctx.save_for_backward(q_, k_, v_, a_, b_, ckpt, h0_)
+                      Bt, L, H, Dh, seg, _lib.ptr(y), _lib.ptr(ckpt), _lib.ptr(cache), _lib.ptr(h0_),
+                      _lib.stream_of(dev))
+        ctx.save_for_backward(q_, k_, v_, a_, b_, ckpt, cache, h0_)
         ctx.seg = seg
         return y, ckpt[:, -1].clone()
 
     @staticmethod
     def backward(ctx, gy, gfinal):
-        q_, k_, v_, a_, b_, ckpt, h0_ = ctx.saved_tensors
+        q_, k_, v_, a_, b_, ckpt, cache, h0_ = ctx.saved_tensors
         Bt, L, H, Dh = q_.shape
         dev = q_.device
         code = _lib.DTYPE_CODE[q_.dtype]
@@ -74,10 +78,10 @@ class _GDNScan(torch.autograd.Function):
             lib = _lib.load()
             nws = lib.mr_gdn_bwd_workspace_bytes(code, Bt, L, H, Dh, ctx.seg)
             ws = torch.empty(max(nws, 16), dtype=torch.uint8, device=dev)
-            _lib.call("mr_gdn_bwd", _lib.ptr(gy), _lib.ptr(gf), _lib.ptr(ckpt), _lib.ptr(q_), _lib.ptr(k_),
-                      _lib.ptr(v_), _lib.ptr(a_), _lib.ptr(b_), code, Bt, L, H, Dh, ctx.seg, _lib.ptr(gq),
-                      _lib.ptr(gk), _lib.ptr(gv), _lib.ptr(ga), _lib.ptr(gb), _lib.ptr(ws), ws.numel(),
-                      _lib.ptr(h0_), _lib.ptr(gh0), _lib.stream_of(dev))
+            _lib.call("mr_gdn_bwd", _lib.ptr(gy), _lib.ptr(gf), _lib.ptr(ckpt), _lib.ptr(cache), _lib.ptr(q_),
+                      _lib.ptr(k_), _lib.ptr(v_), _lib.ptr(a_), _lib.ptr(b_), code, Bt, L, H, Dh, ctx.seg,
+                      _lib.ptr(gq), _lib.ptr(gk), _lib.ptr(gv), _lib.ptr(ga), _lib.ptr(gb), _lib.ptr(ws),
+                      ws.numel(), _lib.ptr(h0_), _lib.ptr(gh0), _lib.stream_of(dev))
         return gq, gk, gv, ga, gb, None, gh0
 
 
