@@ -72,6 +72,10 @@ def algorithmic_bytes(cfg, batch):
         H, Dh = cfg["H"], cfg["Dh"]
         inp = B * L * H * (3 * Dh + 1) * es
         y = B * L * H * Dh * 4
+    elif k == "gdn":  # q, k, v and alpha, beta per head
+        H, Dh = cfg["H"], cfg["Dh"]
+        inp = B * L * H * (3 * Dh + 2) * es
+        y = B * L * H * Dh * 4
     elif k == "rglru":
         inp = B * L * cfg["D"] * 2 * es
         y = B * L * cfg["D"] * 4
@@ -200,7 +204,7 @@ def cpu_sample(name):
     cfg = W.CONFIGS[name]
     k = cfg["kind"]
     threads = os.cpu_count() or 1
-    if k in ("ssd", "gla") and cfg["B"] * cfg["H"] > 2 * threads and cfg["L"] * cfg["Dh"] > 2 ** 18:
+    if k in ("ssd", "gla", "gdn") and cfg["B"] * cfg["H"] > 2 * threads and cfg["L"] * cfg["Dh"] > 2 ** 18:
         hs = min(cfg["H"], max(1, threads))
         ins = W.make_inputs(name, "cpu", seed=1000, batch=1)
         ins = [t[:, :, :hs] if t.dim() >= 3 else t[:hs] for t in ins]
@@ -445,6 +449,8 @@ def _report(args, rank, world, W, name, cfg, nb, total_ms, e2e_ms, f_ms, b_ms, h
                          "frac": achieved / hbm, "traffic": _traffic(name, dom[0], nb, cfg),
                          "algorithmic_bytes_per_launch": dom[1],
                          "peak_source": f"{peak_kind} hbm_gbs"},
+            **({"note": "per-step delta-rule recurrence: bound by FP32 issue and per-step latency on the "
+                        "CUDA cores, not by HBM"} if cfg["kind"] == "gdn" else {}),
             "gpu_launches": int(launches),
             "clocks": clk.summary(),
         }
@@ -502,7 +508,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--config", default="c4", choices=["c0", "c1", "c2", "c3", "c4", "c5", "c2g", "c3a"])
+    ap.add_argument("--config", default="c4", choices=["c0", "c1", "c2", "c3", "c4", "c5", "c2g", "c3a", "c6"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffer) timing")

@@ -27,6 +27,8 @@ CONFIGS = {
     "c2g": dict(kind="rglru_gated", B=8, L=4096, D=2560, seg=32, dtype=torch.bfloat16),
     # c3 with the rotation angle in place of cos/sin (cos, sin formed in the kernels)
     "c3a": dict(kind="rotlru_angle", B=16, L=8192, Dp=1024, seg=32, dtype=torch.bfloat16),
+    # Gated DeltaNet (a design only in the reference) at the unit count of c5
+    "c6": dict(kind="gdn", B=32, L=2048, H=32, Dh=64, seg=64, dtype=torch.bfloat16),
 }
 
 DESCRIPTION = {
@@ -38,6 +40,7 @@ DESCRIPTION = {
     "c5": "gla_scan bf16 B=32 L=16384 H=32 Dh=64 seg=32",
     "c2g": "rglru_scan_gated bf16 B=8 L=4096 D=2560 seg=32 (gating in the kernels, c=8)",
     "c3a": "rotlru_scan_angle bf16 B=16 L=8192 D=2048 seg=32 (cos, sin formed in the kernels)",
+    "c6": "gated_deltanet_scan bf16 B=32 L=2048 H=32 Dh=64 seg=64",
 }
 
 GATE_C = 8.0  # the RG-LRU gate exponent scale of c2 / c2g
@@ -77,6 +80,14 @@ def make_inputs(name, device, seed=0, batch=None):
         v = torch.randn((B, L, H, Dh), **f32) * s
         g_ = torch.sigmoid(torch.randn((B, L, H), **f32) + 2.0)
         return tuple(t.to(dt) for t in (q, k, v, g_))
+    if cfg["kind"] == "gdn":
+        H, Dh = cfg["H"], cfg["Dh"]
+        q = torch.nn.functional.normalize(torch.randn((B, L, H, Dh), **f32), dim=-1)
+        k = torch.nn.functional.normalize(torch.randn((B, L, H, Dh), **f32), dim=-1)
+        v = torch.randn((B, L, H, Dh), **f32)
+        alpha = torch.exp(-torch.nn.functional.softplus(torch.randn((B, L, H), **f32) - 3.0))
+        beta = torch.sigmoid(torch.randn((B, L, H), **f32))
+        return tuple(t.to(dt) for t in (q, k, v, alpha, beta))
     if cfg["kind"] in ("rglru", "rglru_gated"):
         D = cfg["D"]
         x = torch.randn((B, L, D), **f32)
@@ -102,7 +113,7 @@ def make_inputs(name, device, seed=0, batch=None):
 def output_shape(name, batch=None):
     cfg = CONFIGS[name]
     B = cfg["B"] if batch is None else batch
-    if cfg["kind"] in ("ssd", "gla"):
+    if cfg["kind"] in ("ssd", "gla", "gdn"):
         return (B, cfg["L"], cfg["H"], cfg["Dh"])
     if cfg["kind"] in ("rglru", "rglru_gated"):
         return (B, cfg["L"], cfg["D"])
@@ -116,6 +127,8 @@ def scan_fn(pkg, name):
         return lambda *xs: pkg.rglru_scan_gated(*xs, GATE_C, seg=seg)
     if kind == "rotlru_angle":
         return lambda *xs: pkg.rotlru_scan_angle(*xs, seg=seg)
+    if kind == "gdn":
+        return lambda *xs: pkg.gated_deltanet_scan(*xs, seg=seg)
     f = getattr(pkg, f"{kind}_scan")
     return lambda *xs: f(*xs, seg=seg)
 

@@ -107,5 +107,23 @@ def rotlru(a, cs, sn, x, seg, gy=None, g_final=None):
     return out
 
 
+def gdn(q, k, v, alpha, beta, seg, gy=None, g_final=None):
+    q, k, v, alpha, beta = map(_f, (q, k, v, alpha, beta))
+    Bt, L, H, Dh = q.shape
+    y = np.empty_like(q)
+    ck = np.empty((Bt, L // seg, H, Dh, Dh), np.float32)
+    lib().orc_gdn_fwd(*map(_p, (q, k, v, alpha, beta)), *_i(Bt, L, H, Dh, seg), _p(y), _p(ck))
+    out = {"y": y, "final": ck[:, -1].copy()}
+    if gy is not None:
+        gy = _f(gy)
+        gf = None if g_final is None else _f(g_final)
+        grads = [np.empty_like(t) for t in (q, k, v, alpha, beta)]
+        lib().orc_gdn_bwd(_p(gy), _p(gf), _p(ck), *map(_p, (q, k, v, alpha, beta)), *_i(Bt, L, H, Dh, seg),
+                          *map(_p, grads))
+        out["grads"] = grads
+    return out
+
+
 def run(kind, ins, seg, gy=None, g_final=None):
-    return {"ssd": ssd, "gla": gla, "rglru": rglru, "rotlru": rotlru}[kind](*ins, seg, gy=gy, g_final=g_final)
+    fns = {"ssd": ssd, "gla": gla, "rglru": rglru, "rotlru": rotlru, "gdn": gdn}
+    return fns[kind](*ins, seg, gy=gy, g_final=g_final)

@@ -10,6 +10,8 @@
  *   GLA    forward gla.py:78-100,  backward gla.py:158-235
  *   RG-LRU forward rglru.py:88-100, backward rglru.py:147-180
  *   rotLRU forward rotlru.py:383-405, backward rotlru.py:456-518
+ *   Gated DeltaNet (a design only in the reference) docs/DESIGN_gated_deltanet.md
+ *          sections 1 and 4
  * One OpenMP task per independent unit ((b,h) for SSD/GLA, b for the
  * diagonal scans, whose channels are looped inside). Cross-lane simd_sum
  * reductions become plain loops over the lane axis. The state at every
@@ -346,5 +348,110 @@ void orc_rotlru_bwd(const float* gy, const float* gfinal, const float* ckpt, con
     }
     free(adj);
     free(hs);
+  }
+}
+
+/* ------------------------------------------------------- Gated DeltaNet -- */
+/* The reference carries this recurrence as a design only
+ * (docs/DESIGN_gated_deltanet.md): S_t = alpha (I - beta k k^T) S_{t-1} +
+ * beta k v^T, o_t = S_t^T q (section 1, R1''/R2'), S[i][j] with i the key axis;
+ * the adjoint of its section 4. Checkpoint + recompute as the other scans. */
+static void gdn_advance(float* S, const float* kr, const float* vr, float a, float bt, i64 Dh, float* p,
+                        float* w) {
+  for (i64 j = 0; j < Dh; ++j) p[j] = 0.f;
+  for (i64 i = 0; i < Dh; ++i)
+    for (i64 j = 0; j < Dh; ++j) p[j] += kr[i] * S[i * Dh + j];
+  for (i64 j = 0; j < Dh; ++j) w[j] = bt * (vr[j] - a * p[j]);
+  for (i64 i = 0; i < Dh; ++i)
+    for (i64 j = 0; j < Dh; ++j) S[i * Dh + j] = a * S[i * Dh + j] + kr[i] * w[j];
+}
+
+void orc_gdn_fwd(const float* q, const float* k, const float* v, const float* alpha, const float* beta, i64 Bt,
+                 i64 L, i64 H, i64 Dh, i64 seg, float* y, float* ckpt) {
+  const i64 nseg = L / seg;
+#pragma omp parallel for schedule(dynamic, 1)
+  for (i64 bh = 0; bh < Bt * H; ++bh) {
+    const i64 b = bh / H, h = bh % H;
+    float* S = (float*)calloc((size_t)(Dh * Dh + 2 * Dh), sizeof(float));
+    float *p = S + Dh * Dh, *w = p + Dh;
+    for (i64 t = 0; t < L; ++t) {
+      const i64 row = (b * L + t) * H + h;
+      gdn_advance(S, k + row * Dh, v + row * Dh, alpha[row], beta[row], Dh, p, w);
+      float* yr = y + row * Dh;
+      for (i64 j = 0; j < Dh; ++j) yr[j] = 0.f;
+      for (i64 i = 0; i < Dh; ++i)
+        for (i64 j = 0; j < Dh; ++j) yr[j] += q[row * Dh + i] * S[i * Dh + j];
+      if ((t + 1) % seg == 0)
+        memcpy(ckpt + ((b * nseg + t / seg) * H + h) * Dh * Dh, S, (size_t)(Dh * Dh) * sizeof(float));
+    }
+    free(S);
+  }
+}
+
+void orc_gdn_bwd(const float* gy, const float* gfinal, const float* ckpt, const float* q, const float* k,
+                 const float* v, const float* alpha, const float* beta, i64 Bt, i64 L, i64 H, i64 Dh, i64 seg,
+                 float* gq, float* gk, float* gv, float* ga, float* gb) {
+  const i64 nseg = L / seg;
+#pragma omp parallel for schedule(dynamic, 1)
+  for (i64 bh = 0; bh < Bt * H; ++bh) {
+    const i64 b = bh / H, h = bh % H;
+    const i64 S2 = Dh * Dh;
+    float* G = (float*)calloc((size_t)S2, sizeof(float));
+    float* scr = (float*)malloc((size_t)((seg + 1) * S2 + 4 * Dh) * sizeof(float));
+    float *p = scr + (seg + 1) * S2, *w = p + Dh, *d = w + Dh, *tmp = d + Dh;
+    if (gfinal)
+      for (i64 i = 0; i < S2; ++i) G[i] = gfinal[bh * S2 + i];
+    for (i64 s = nseg - 1; s >= 0; --s) {
+      if (s > 0)
+        memcpy(scr, ckpt + ((b * nseg + s - 1) * H + h) * S2, (size_t)S2 * sizeof(float));
+      else
+        memset(scr, 0, (size_t)S2 * sizeof(float));
+      for (i64 tl = 0; tl < seg; ++tl) {
+        const i64 row = (b * L + s * seg + tl) * H + h;
+        memcpy(scr + (tl + 1) * S2, scr + tl * S2, (size_t)S2 * sizeof(float));
+        gdn_advance(scr + (tl + 1) * S2, k + row * Dh, v + row * Dh, alpha[row], beta[row], Dh, p, w);
+      }
+      for (i64 tl = seg - 1; tl >= 0; --tl) {
+        const i64 row = (b * L + s * seg + tl) * H + h;
+        const float a = alpha[row], bt = beta[row];
+        const float* Sp = scr + tl * S2;
+        const float* St = scr + (tl + 1) * S2;
+        const float *qr = q + row * Dh, *kr = k + row * Dh, *vr = v + row * Dh, *go = gy + row * Dh;
+        for (i64 j = 0; j < Dh; ++j) p[j] = 0.f;
+        for (i64 i = 0; i < Dh; ++i)
+          for (i64 j = 0; j < Dh; ++j) p[j] += kr[i] * Sp[i * Dh + j];
+        for (i64 j = 0; j < Dh; ++j) w[j] = bt * (vr[j] - a * p[j]);
+        for (i64 i = 0; i < Dh; ++i)
+          for (i64 j = 0; j < Dh; ++j) G[i * Dh + j] += qr[i] * go[j];
+        for (i64 j = 0; j < Dh; ++j) d[j] = 0.f;
+        for (i64 i = 0; i < Dh; ++i)
+          for (i64 j = 0; j < Dh; ++j) d[j] += kr[i] * G[i * Dh + j];
+        float gas = 0.f, gbs = 0.f;
+        for (i64 i = 0; i < Dh; ++i) {
+          float sq = 0.f, sk = 0.f, sd = 0.f;
+          for (i64 j = 0; j < Dh; ++j) {
+            const i64 e = i * Dh + j;
+            sq += St[e] * go[j];
+            sk += G[e] * w[j];
+            sd += Sp[e] * d[j];
+            gas += G[e] * Sp[e];
+          }
+          gq[row * Dh + i] = sq;
+          tmp[i] = sk - a * bt * sd;
+        }
+        for (i64 i = 0; i < Dh; ++i) gk[row * Dh + i] = tmp[i];
+        for (i64 j = 0; j < Dh; ++j) {
+          gv[row * Dh + j] = bt * d[j];
+          gas -= bt * d[j] * p[j];
+          gbs += d[j] * (vr[j] - a * p[j]);
+        }
+        ga[row] = gas;
+        gb[row] = gbs;
+        for (i64 i = 0; i < Dh; ++i)
+          for (i64 j = 0; j < Dh; ++j) G[i * Dh + j] = a * G[i * Dh + j] - a * bt * kr[i] * d[j];
+      }
+    }
+    free(G);
+    free(scr);
   }
 }

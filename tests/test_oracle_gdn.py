@@ -93,3 +93,20 @@ def test_gdn_shape_rules(bad):
     al = torch.zeros(1, 32, 3 if bad == "alpha" else 2)
     with pytest.raises(ValueError, match="Dh=48 is not supported" if bad == "dh" else "alpha must be"):
         mr.gated_deltanet_scan(q, q, q, al, torch.zeros(1, 32, 2))
+
+
+def test_c_oracle_gdn_matches_numpy_oracle():
+    """The float32 C restatement (the timed CPU baseline of the Gated DeltaNet
+    bench configuration) against the float64 oracle, with a final-state cotangent."""
+    import c_oracle
+    rng = np.random.default_rng(13)
+    Bt, T, H, Dh, seg = 2, 48, 2, 8, 16
+    ins = [np.asarray(x, np.float32).astype(np.float64) for x in _inputs(rng, Bt, T, H, Dh)]
+    y, f = R.gdn_forward(*ins)
+    w, wf = rng.standard_normal(y.shape), rng.standard_normal(f.shape)
+    ref = R.gdn_backward(*ins, w, wf)
+    out = c_oracle.run("gdn", ins, seg, gy=w, g_final=wf)
+    assert R.rel_err(out["y"], y) < 1e-5
+    assert R.rel_err(out["final"], f) < 1e-5
+    for g, r in zip(out["grads"], ref):
+        assert R.rel_err(g, r) < 1e-5
