@@ -121,6 +121,38 @@ __device__ __forceinline__ void gdn_ld_f32(const float* p, float (&f)[R]) {
   }
 }
 
+// Sum over a warp's 8 columns (lanes jl = lane & 7) of each lane's R values
+// (rows g R .. g R + R - 1, g = lane >> 3) through the warp's transpose buffer
+// wb (8 rows of 4R + 4 floats); out[DH] (shared) receives the warp's sums.
+template <int R>
+__device__ __forceinline__ void gdn_warp_colsum(float* wb, const float (&x)[R], float* out) {
+  constexpr int RS = 4 * R + 4, E = R / 8;  // buffer row stride; rows summed per lane
+  static_assert(E == 1 || E == 2, "R must be 8 or 16");
+  const int lane = threadIdx.x & 31, g = lane >> 3, jl = lane & 7;
+  float* dst = wb + jl * RS + g * R;
+#pragma unroll
+  for (int c = 0; c < R / 4; ++c)
+    *reinterpret_cast<float4*>(dst + 4 * c) = make_float4(x[4 * c], x[4 * c + 1], x[4 * c + 2], x[4 * c + 3]);
+  __syncwarp();
+  const float* src = wb + g * R + E * jl;
+  if constexpr (E == 2) {
+    float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int jj = 0; jj < 8; ++jj) {
+      const float2 v = *reinterpret_cast<const float2*>(src + jj * RS);
+      acc.x += v.x, acc.y += v.y;
+    }
+    __syncwarp();  // the buffer is written again next
+    *reinterpret_cast<float2*>(out + g * R + E * jl) = acc;
+  } else {
+    float acc = 0.f;
+#pragma unroll
+    for (int jj = 0; jj < 8; ++jj) acc += src[jj * RS];
+    __syncwarp();
+    out[g * R + jl] = acc;
+  }
+}
+
 template <int R>
 __device__ __forceinline__ float gdn_dot(const float (&x)[R], const float (&y)[R]) {
   float acc = 0.f;
@@ -233,8 +265,9 @@ template <typename T, int DH>
 struct GdnBwdSmem {
   static constexpr int NT = DH * 4, K = kGdnK, TS = kGdnTS;
   static constexpr size_t slots = (size_t)K * DH * DH * 4;
-  static constexpr size_t red = (size_t)2 * DH * (DH + 4) * 4;
-  static constexpr size_t rsc = 2 * (NT / 32) * 4 < 16 ? 16 : 2 * (NT / 32) * 4;
+  static constexpr size_t red = (size_t)(NT / 32) * 8 * (DH + 4) * 4;  // per-warp transpose buffers
+  static constexpr size_t part = (size_t)K * (NT / 32) * 2 * DH * 4;   // [K][NW][2][DH] partial sums
+  static constexpr size_t rsc = ((size_t)K * (NT / 32) * 2 * 4 + 15) / 16 * 16;  // [K][NW][2] scalars
   static constexpr size_t a_ab = (size_t)2 * TS * 4, a_w = (size_t)2 * TS * DH * 4;
   static constexpr size_t a_rows = (size_t)2 * TS * DH * sizeof(T);
   static constexpr size_t b_f32 = (size_t)2 * 3 * K * DH * 4, b_ab = (size_t)2 * 2 * K * 4;
@@ -242,7 +275,7 @@ struct GdnBwdSmem {
   static constexpr size_t b_rows = (size_t)2 * 3 * K * DH * sizeof(T);
   static constexpr size_t stage_a = a_ab + a_w + a_rows, stage_b = b_f32 + b_ab + b_cvt + b_wgo + b_rows;
   static constexpr size_t stage = stage_a > stage_b ? stage_a : stage_b;
-  static constexpr size_t bytes = slots + red + rsc + stage;
+  static constexpr size_t bytes = slots + red + part + rsc + stage;
 };
 
 // per-CTA scratch: sub-checkpoints [ceil(seg/K)][R][NT]
@@ -264,9 +297,9 @@ gdn_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfinal, c
   extern __shared__ float4 gdn_smem[];
   unsigned char* base = reinterpret_cast<unsigned char*>(gdn_smem);
   float* slots = reinterpret_cast<float*>(base);
-  float* red = reinterpret_cast<float*>(base + SM::slots);
-  float* rsc = reinterpret_cast<float*>(base + SM::slots + SM::red);
-  unsigned char* stg = base + SM::slots + SM::red + SM::rsc;
+  float* ppart = reinterpret_cast<float*>(base + SM::slots + SM::red);
+  float* psc = reinterpret_cast<float*>(base + SM::slots + SM::red + SM::part);
+  unsigned char* stg = base + SM::slots + SM::red + SM::part + SM::rsc;
   // phase A staging
   float* a_ab = reinterpret_cast<float*>(stg);                 // [2][TS]: alpha
   float* a_w = reinterpret_cast<float*>(stg + SM::a_ab);       // [2][TS][DH]: w
@@ -281,9 +314,8 @@ gdn_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfinal, c
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 3, j = warp * 8 + (lane & 7), i0 = g * R;
   const int nseg = L / seg, nsb = (seg + K - 1) / K, nblk = (seg + TS - 1) / TS;
+  float* wbuf = reinterpret_cast<float*>(base + SM::slots) + warp * 8 * RS;  // this warp's transpose buffer
   float* sub = ws + (int64_t)blockIdx.x * gdn_scratch_floats(DH, seg);
-  // role in the reduction over j: vector (0 grad_q, 1 grad_k), quad of rows, column phase
-  const int rv = tid / (NT / 2), rq = (tid % (NT / 2)) / 8, rj = tid & 7;
 
   for (int unit = blockIdx.x; unit < units; unit += gridDim.x) {
     const int64_t b = unit / H;
@@ -443,71 +475,62 @@ gdn_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfinal, c
               gbP = d * fmaf(-a, p, vj);
               gv[row * DH + j] = from_f<T>(bt * d);
             }
-            // this column's terms of grad_q and grad_k (G w + S_{t-1} gp); grad_q =
-            // S_t go = alpha S_{t-1} go + k (w.go), the last term added by the reducer
-            float* rw = red + (int64_t)j * RS + i0;
+            // this column's terms of grad_q and grad_k (G w + S_{t-1} gp), summed over the
+            // warp's 8 columns through its transpose buffer; grad_q = S_t go = alpha
+            // S_{t-1} go + k (w.go), alpha and the last term applied by the sub-block's reducer
+            {
+              float r1[R], r2[R];
 #pragma unroll
-            for (int c = 0; c < R / 4; ++c) {
-              float4 r1, r2;
-              float* p1 = &r1.x;
-              float* p2 = &r2.x;
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const int r = 4 * c + e;
-                p1[e] = Sp[r] * go;
-                p2[e] = fmaf(G[r], w, Sp[r] * gp);
+              for (int r = 0; r < R; ++r) {
+                r1[r] = Sp[r] * go;
+                r2[r] = fmaf(G[r], w, Sp[r] * gp);
               }
-              *reinterpret_cast<float4*>(rw + 4 * c) = r1;
-              *reinterpret_cast<float4*>(rw + DH * RS + 4 * c) = r2;
+              float* pw = ppart + ((m * NW + warp) * 2) * DH;
+              gdn_warp_colsum<R>(wbuf, r1, pw);
+              gdn_warp_colsum<R>(wbuf, r2, pw + DH);
             }
 #pragma unroll
             for (int r = 0; r < R; ++r) G[r] = fmaf(a, G[r], kr[r] * gp);  // adjoint to t-1 (Bp')
-            gaP = gdn_warp_sum(gaP);
-            gbP = gdn_warp_sum(gbP);
+            // the scalar gradients of alpha and beta: over the row groups, then the warp's columns
+            gaP = gdn_group_sum(gaP);
+#pragma unroll
+            for (int o = 1; o < 8; o <<= 1) {
+              gaP += __shfl_xor_sync(0xffffffffu, gaP, o);
+              gbP += __shfl_xor_sync(0xffffffffu, gbP, o);
+            }
             if (lane == 0) {
-              rsc[warp] = gaP;
-              rsc[NW + warp] = gbP;
+              psc[(m * NW + warp) * 2] = gaP;
+              psc[(m * NW + warp) * 2 + 1] = gbP;
             }
-            __syncthreads();
-            {
-              float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-              const float* rr = red + (int64_t)rv * DH * RS + 4 * rq;
+          }
+        }
+        __syncthreads();  // the sub-block's per-warp partial sums are complete
+        {  // reduce them over the warps: one float pair of grad_q or grad_k per thread
+          const int m = tid / (NT / K), rem = tid % (NT / K), vq = rem / (DH / 2), i2 = (rem % (DH / 2)) * 2;
+          if (m < nk) {
+            float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
-              for (int jj = rj; jj < DH; jj += 8) {
-                const float4 x = *reinterpret_cast<const float4*>(rr + jj * RS);
-                acc.x += x.x, acc.y += x.y, acc.z += x.z, acc.w += x.w;
-              }
-#pragma unroll
-              for (int o = 1; o < 8; o <<= 1) {
-                acc.x += __shfl_xor_sync(0xffffffffu, acc.x, o);
-                acc.y += __shfl_xor_sync(0xffffffffu, acc.y, o);
-                acc.z += __shfl_xor_sync(0xffffffffu, acc.z, o);
-                acc.w += __shfl_xor_sync(0xffffffffu, acc.w, o);
-              }
-              if (rj == 0) {
-                float out[4] = {acc.x, acc.y, acc.z, acc.w};
-                if (rv == 0) {  // grad_q = alpha (S_{t-1} go) + k (w.go)
-                  const float4 kk = *reinterpret_cast<const float4*>(rk_ + m * DH + 4 * rq);
-                  const float wg = b_wgo[m];
-                  out[0] = fmaf(a, out[0], kk.x * wg);
-                  out[1] = fmaf(a, out[1], kk.y * wg);
-                  out[2] = fmaf(a, out[2], kk.z * wg);
-                  out[3] = fmaf(a, out[3], kk.w * wg);
-                }
-                st_vec<T, 4>((rv == 0 ? gq : gk) + row * DH + 4 * rq, out);
-              }
-              if (tid == 0) {
-                float sa = 0.f, sbeta = 0.f;
-#pragma unroll
-                for (int w2 = 0; w2 < NW; ++w2) {
-                  sa += rsc[w2];
-                  sbeta += rsc[NW + w2];
-                }
-                galpha[row] = from_f<T>(sa);
-                gbeta[row] = from_f<T>(sbeta);
-              }
+            for (int w2 = 0; w2 < NW; ++w2) {
+              const float2 x = *reinterpret_cast<const float2*>(ppart + ((m * NW + w2) * 2 + vq) * DH + i2);
+              acc.x += x.x, acc.y += x.y;
             }
-            __syncthreads();
+            float out[2] = {acc.x, acc.y};
+            const float a = fab[m];
+            if (vq == 0) {  // grad_q = alpha (S_{t-1} go) + k (w.go)
+              const float wg = b_wgo[m];
+              out[0] = fmaf(a, out[0], rk_[m * DH + i2] * wg);
+              out[1] = fmaf(a, out[1], rk_[m * DH + i2 + 1] * wg);
+            }
+            const int64_t row = (b * L + t0 + tb + m) * H + h;
+            st_vec<T, 2>((vq == 0 ? gq : gk) + row * DH + i2, out);
+          }
+          if (tid < 2 * nk) {
+            const int mm = tid >> 1, which = tid & 1;
+            float sum = 0.f;
+#pragma unroll
+            for (int w2 = 0; w2 < NW; ++w2) sum += psc[(mm * NW + w2) * 2 + which];
+            const int64_t row = (b * L + t0 + tb + mm) * H + h;
+            (which == 0 ? galpha : gbeta)[row] = from_f<T>(sum);
           }
         }
         if (sb > 0 && tid < 2 * K) b_ab[(bb ^ 1) * 2 * K + tid] = ab;
