@@ -255,8 +255,9 @@ gdn_fwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
   }
 }
 
-// Shared memory of the backward (bytes): thread-private state slots [K][R][NT],
-// the reduction buffer [2][DH(j)][DH + 4 (i)], the per-warp scalars, and the
+// Shared memory of the backward (bytes): thread-private state slots
+// [K][R/4][NT] float4, one transpose buffer per warp [8][DH + 4], the per-warp
+// column sums of the sub-block [K][NW][2][DH] and its scalars [K][NW][2], and the
 // staged inputs, phase A's ([2][alpha][TS], [2][w][TS][DH] float, [2 buffers][k][TS][DH] of T)
 // and phase B's ([2][go, w, p][K][DH] float, [2][alpha, beta][K], the
 // current sub-block's q, k, v as floats [3][K][DH] and w.go [K], [2][q, k, v][K][DH]
@@ -264,7 +265,7 @@ gdn_fwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
 template <typename T, int DH>
 struct GdnBwdSmem {
   static constexpr int NT = DH * 4, K = kGdnK, TS = kGdnTS;
-  static constexpr size_t slots = (size_t)K * DH * DH * 4;
+  static constexpr size_t slots = (size_t)K * DH * DH * 4;  // [K][R/4][NT] float4, thread-private
   static constexpr size_t red = (size_t)(NT / 32) * 8 * (DH + 4) * 4;  // per-warp transpose buffers
   static constexpr size_t part = (size_t)K * (NT / 32) * 2 * DH * 4;   // [K][NW][2][DH] partial sums
   static constexpr size_t rsc = ((size_t)K * (NT / 32) * 2 * 4 + 15) / 16 * 16;  // [K][NW][2] scalars
@@ -278,7 +279,7 @@ struct GdnBwdSmem {
   static constexpr size_t bytes = slots + red + part + rsc + stage;
 };
 
-// per-CTA scratch: sub-checkpoints [ceil(seg/K)][R][NT]
+// per-CTA scratch: sub-checkpoints [ceil(seg/K)][R/4][NT] of float4
 __host__ __device__ __forceinline__ int64_t gdn_scratch_floats(int64_t Dh, int64_t seg) {
   return (seg + kGdnK - 1) / kGdnK * Dh * Dh;
 }
@@ -296,7 +297,7 @@ gdn_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfinal, c
   constexpr int CHF = DH * 4 / 16;  // 16-byte chunks of a float row
   extern __shared__ float4 gdn_smem[];
   unsigned char* base = reinterpret_cast<unsigned char*>(gdn_smem);
-  float* slots = reinterpret_cast<float*>(base);
+  float4* slots4 = reinterpret_cast<float4*>(base);  // [K][R/4][NT]
   float* ppart = reinterpret_cast<float*>(base + SM::slots + SM::red);
   float* psc = reinterpret_cast<float*>(base + SM::slots + SM::red + SM::part);
   unsigned char* stg = base + SM::slots + SM::red + SM::part + SM::rsc;
@@ -367,9 +368,9 @@ gdn_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfinal, c
           for (int tt = 0; tt < nt; ++tt) {
             const int tl = blk * TS + tt;
             if (tl % K == 0) {
-              float* d = sub + (int64_t)(tl / K) * DH * DH + tid;
+              float4* d = reinterpret_cast<float4*>(sub + (int64_t)(tl / K) * DH * DH) + tid;
 #pragma unroll
-              for (int r = 0; r < R; ++r) d[r * NT] = S[r];
+              for (int c = 0; c < R / 4; ++c) d[c * NT] = make_float4(S[4 * c], S[4 * c + 1], S[4 * c + 2], S[4 * c + 3]);
             }
             float kr[R];
             gdn_load_rows<T, R>(sk + tt * DH + i0, kr);
@@ -432,21 +433,21 @@ gdn_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfinal, c
         const int tb = sb * K, nk = min(K, seg - tb);
         {
           float cur[R];
-          const float* src = sub + (int64_t)sb * DH * DH + tid;
+          const float4* src = reinterpret_cast<const float4*>(sub + (int64_t)sb * DH * DH) + tid;
 #pragma unroll
-          for (int r = 0; r < R; ++r) {
-            cur[r] = src[r * NT];
-            slots[r * NT + tid] = cur[r];
+          for (int c = 0; c < R / 4; ++c) {
+            const float4 x = src[c * NT];
+            cur[4 * c] = x.x, cur[4 * c + 1] = x.y, cur[4 * c + 2] = x.z, cur[4 * c + 3] = x.w;
+            slots4[c * NT + tid] = x;
           }
 #pragma unroll 1
           for (int m = 1; m < nk; ++m) {
-            {
-              float kr[R];
-              gdn_ld_f32<R>(rk_ + (m - 1) * DH + i0, kr);
-              gdn_update(cur, kr, fab[m - 1], fw[(m - 1) * DH + j]);
+            float kr[R];
+            gdn_ld_f32<R>(rk_ + (m - 1) * DH + i0, kr);
+            gdn_update(cur, kr, fab[m - 1], fw[(m - 1) * DH + j]);
 #pragma unroll
-              for (int r = 0; r < R; ++r) slots[(m * R + r) * NT + tid] = cur[r];
-            }
+            for (int c = 0; c < R / 4; ++c)
+              slots4[(m * (R / 4) + c) * NT + tid] = make_float4(cur[4 * c], cur[4 * c + 1], cur[4 * c + 2], cur[4 * c + 3]);
           }
         }
 #pragma unroll 1
@@ -463,7 +464,10 @@ gdn_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfinal, c
               for (int r = 0; r < R; ++r) G[r] = fmaf(qr[r], go, G[r]);  // output seed (B0)
             }
 #pragma unroll
-            for (int r = 0; r < R; ++r) Sp[r] = slots[(m * R + r) * NT + tid];
+            for (int c = 0; c < R / 4; ++c) {
+              const float4 x = slots4[(m * (R / 4) + c) * NT + tid];
+              Sp[4 * c] = x.x, Sp[4 * c + 1] = x.y, Sp[4 * c + 2] = x.z, Sp[4 * c + 3] = x.w;
+            }
             const float vj = rv_[m * DH + j];
             const float a = fab[m], bt = fab[K + m];
             const float w = fw[m * DH + j], p = fp[m * DH + j];
