@@ -272,6 +272,12 @@ MR_API int mr_gdn_bwd(const float* grad_y, const float* grad_final, const float*
                       void* grad_alpha, void* grad_beta, void* workspace, size_t workspace_bytes, const float* h0,
                       float* grad_h0, void* stream);
 
+/* One Gated DeltaNet decode step: state [B,H,Dh,Dh] float32 (the final state's
+ * layout) advanced in place by one step of the recurrence above; q, k, v
+ * [B,H,Dh] and alpha, beta [B,H] in `dtype`; y [B,H,Dh] float32. */
+MR_API int mr_gdn_step(const void* q, const void* k, const void* v, const void* alpha, const void* beta, int dtype,
+                       int64_t batch, int64_t H, int64_t Dh, float* state, float* y, void* stream);
+
 /* ------------------------------------------------- rotLRU, angle input ---
  * The rotLRU scan taking the rotation angle theta [B,L,Dp] in place of cs, sn
  * (no counterpart in the reference, which forms cos and sin in MLX host code

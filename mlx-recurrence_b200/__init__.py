@@ -23,7 +23,8 @@ name carries a hyphen); after that the package is also registered as
 import sys as _sys
 
 from ._chassis import DEFAULT_SEG, check_segment_shape, get_or_build_kernel, parity_check
-from .gdn import gated_deltanet_scan, gated_deltanet_scan_reference, gated_deltanet_scan_with_state
+from .gdn import (gated_deltanet_scan, gated_deltanet_scan_reference, gated_deltanet_scan_with_state,
+                  gated_deltanet_step)
 from .gla import gla_scan, gla_scan_reference, gla_scan_with_state, gla_step
 from .rglru import (rglru_scan, rglru_scan_gated, rglru_scan_gated_with_state, rglru_scan_reference,
                     rglru_scan_with_state, rglru_step)
@@ -58,6 +59,7 @@ __all__ = [
     "gla_step",
     "rglru_step",
     "rotlru_step",
+    "gated_deltanet_step",
     "DEFAULT_SEG",
     "get_or_build_kernel",
     "check_segment_shape",

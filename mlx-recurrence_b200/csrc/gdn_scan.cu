@@ -412,19 +412,22 @@ gdn_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfinal, c
         const float* fw = fgo + K * DH;
         const float* fp = fw + K * DH;
         const float* fab = b_ab + bb * 2 * K;
-        if (tid < K * DH / 4) {  // the sub-block's q, k, v rows as floats, and w.go per step
-          const int m = tid / (DH / 4), c4 = (tid % (DH / 4)) * 4;
-          const T* src = b_rows + bb * 3 * K * DH + m * DH + c4;
-          float* dst = b_cvt + m * DH + c4;
-          *reinterpret_cast<float4*>(dst) = gdn_ld4(src);
-          *reinterpret_cast<float4*>(dst + K * DH) = gdn_ld4(src + K * DH);
-          *reinterpret_cast<float4*>(dst + 2 * K * DH) = gdn_ld4(src + 2 * K * DH);
-          const float4 ww = *reinterpret_cast<const float4*>(fw + m * DH + c4);
-          const float4 gg = *reinterpret_cast<const float4*>(fgo + m * DH + c4);
-          float part = fmaf(ww.x, gg.x, fmaf(ww.y, gg.y, fmaf(ww.z, gg.z, ww.w * gg.w)));
+        {  // the sub-block's q, k, v rows as floats (threads 0 .. 3KDH/4 - 1, one 4-element
+           // chunk each) and w.go per step (the last KDH/4 threads)
+          constexpr int NCH = K * DH / 4;  // 4-element chunks of a [K][DH] block
+          static_assert(4 * NCH == NT, "one chunk per thread");
+          const int which = tid / NCH, m = (tid % NCH) / (DH / 4), c4 = (tid % (DH / 4)) * 4;
+          if (which < 3) {
+            *reinterpret_cast<float4*>(b_cvt + (which * K + m) * DH + c4) =
+                gdn_ld4(b_rows + (bb * 3 + which) * K * DH + m * DH + c4);
+          } else {
+            const float4 ww = *reinterpret_cast<const float4*>(fw + m * DH + c4);
+            const float4 gg = *reinterpret_cast<const float4*>(fgo + m * DH + c4);
+            float part = fmaf(ww.x, gg.x, fmaf(ww.y, gg.y, fmaf(ww.z, gg.z, ww.w * gg.w)));
 #pragma unroll
-          for (int o = 1; o < DH / 4; o <<= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-          if (c4 == 0) b_wgo[m] = part;
+            for (int o = 1; o < DH / 4; o <<= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+            if (c4 == 0) b_wgo[m] = part;
+          }
         }
         __syncthreads();
         const float* rq_ = b_cvt;            // q rows
@@ -548,6 +551,35 @@ gdn_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfinal, c
   }
 }
 
+// One-token decode step on a float32 state cache [B,H,Dh,Dh] (the final
+// state's layout), advanced in place; y [B,H,Dh] float32. One step of the
+// forward's recurrence, same layout (one CTA per (b, h)).
+template <typename T, int DH>
+__global__ void __launch_bounds__(DH * 4)
+gdn_step_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
+                const T* __restrict__ alpha, const T* __restrict__ beta, float* __restrict__ state,
+                float* __restrict__ y) {
+  constexpr int R = DH / 4;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = lane >> 3, j = warp * 8 + (lane & 7), i0 = g * R;
+  const int64_t u = blockIdx.x;  // (b, h): one row of q, k, v and one alpha, beta
+  float* sp = state + (u * DH + i0) * (int64_t)DH + j;
+  float S[R], kr[R], qr[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) S[r] = sp[r * DH];
+  gdn_load_rows<T, R>(k + u * DH + i0, kr);
+  gdn_load_rows<T, R>(q + u * DH + i0, qr);
+  const float vj = to_f(v[u * DH + j]), a = to_f(alpha[u]), bt = to_f(beta[u]);
+  const float p = gdn_group_sum(gdn_dot(kr, S));
+  const float sq = gdn_group_sum(gdn_dot(qr, S));
+  const float kq = gdn_group_sum(gdn_dot(kr, qr));
+  const float w = bt * fmaf(-a, p, vj);
+  if (g == 0) y[u * DH + j] = fmaf(a, sq, kq * w);
+  gdn_update(S, kr, a, w);
+#pragma unroll
+  for (int r = 0; r < R; ++r) sp[r * DH] = S[r];
+}
+
 // ============================================================================
 // host launchers
 // ============================================================================
@@ -614,7 +646,21 @@ int gdn_bwd_launch(const float* gy, const float* gf, const float* ckpt, const fl
                            h0, gh0, st);
 }
 
+template <typename T>
+int gdn_step_launch(const void* q, const void* k, const void* v, const void* alpha, const void* beta, int64_t batch,
+                    int64_t H, int64_t Dh, float* state, float* y, cudaStream_t st) {
+  const T *q_ = (const T*)q, *k_ = (const T*)k, *v_ = (const T*)v, *a_ = (const T*)alpha, *b_ = (const T*)beta;
+  const dim3 grid((unsigned)(batch * H));
+  if (Dh == 32)
+    gdn_step_kernel<T, 32><<<grid, 128, 0, st>>>(q_, k_, v_, a_, b_, state, y);
+  else
+    gdn_step_kernel<T, 64><<<grid, 256, 0, st>>>(q_, k_, v_, a_, b_, state, y);
+  return check_launch("gdn_step_kernel");
+}
+
 #define MR_INST(T)                                                                                              \
+  template int gdn_step_launch<T>(const void*, const void*, const void*, const void*, const void*, int64_t,    \
+                                  int64_t, int64_t, float*, float*, cudaStream_t);                             \
   template int gdn_fwd_launch<T>(const void*, const void*, const void*, const void*, const void*, int64_t,     \
                                  int64_t, int64_t, int64_t, int64_t, float*, float*, float*, const float*,     \
                                  cudaStream_t);                                                               \

@@ -72,6 +72,7 @@ size_t rglru_gated_bwd_ws_bytes(int64_t, int64_t, int64_t, int64_t);
 template <typename T> int gdn_fwd_launch(const void*, const void*, const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, int64_t, float*, float*, float*, const float*, cudaStream_t);
 template <typename T> int gdn_bwd_launch(const float*, const float*, const float*, const float*, const void*, const void*, const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, int64_t, void*, void*, void*, void*, void*, void*, const float*, float*, cudaStream_t);
 size_t gdn_bwd_ws_bytes(int64_t, int64_t, int64_t, int64_t, int64_t);
+template <typename T> int gdn_step_launch(const void*, const void*, const void*, const void*, const void*, int64_t, int64_t, int64_t, float*, float*, cudaStream_t);
 template <typename T> int rotlru_angle_fwd_launch(const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, float*, float*, const float*, cudaStream_t);
 template <typename T> int rotlru_angle_bwd_launch(const float*, const float*, const float*, const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, void*, void*, void*, float*, const float*, float*, cudaStream_t);
 int umma_selftest_launch(const void*, const void*, const void*, const void*, float*, float*, float*,
@@ -414,6 +415,15 @@ int mr_gdn_bwd(const float* grad_y, const float* grad_final, const float* h_ckpt
   MR_DTYPE_SWITCH(dtype, gdn_bwd_launch<T>(grad_y, grad_final, h_ckpt, step_cache, q, k, v, alpha, beta, batch, L, H, Dh, seg,
                                            grad_q, grad_k, grad_v, grad_alpha, grad_beta, workspace, h0, grad_h0,
                                            st));
+}
+
+int mr_gdn_step(const void* q, const void* k, const void* v, const void* alpha, const void* beta, int dtype,
+                int64_t batch, int64_t H, int64_t Dh, float* state, float* y, void* stream) {
+  g_err[0] = 0;
+  MR_TRY(gdn_common_checks("mr_gdn_step", dtype, batch, 1, H, Dh, 1));
+  MR_TRY(check_ptrs("mr_gdn_step", {q, k, v, alpha, beta, state, y}));
+  cudaStream_t st = (cudaStream_t)stream;
+  MR_DTYPE_SWITCH(dtype, gdn_step_launch<T>(q, k, v, alpha, beta, batch, H, Dh, state, y, st));
 }
 
 // --------------------------------------------------------------------- SSD ---

@@ -22,7 +22,7 @@ from __future__ import annotations
 import torch
 
 from . import _lib
-from ._chassis import DEFAULT_SEG, check_segment_shape, common_dtype, grad_out, prep, prep_h0
+from ._chassis import DEFAULT_SEG, check_segment_shape, common_dtype, grad_out, prep, prep_h0, step_state
 
 
 def _validate(q, k, v, alpha, beta):
@@ -124,3 +124,28 @@ def gated_deltanet_scan_reference(q, k, v, alpha, beta, h0=None):
         S = a * S - a * bt * kt * p + bt * kt * v[:, t, :, None, :].to(ft)
         ys.append(torch.sum(q[:, t, :, :, None].to(ft) * S, dim=-2))
     return torch.stack(ys, dim=1)
+
+
+def gated_deltanet_step(q, k, v, alpha, beta, state):
+    """One decode step: advances ``state`` [B, H, Dh, Dh] (float32, the final
+    state's layout) in place by one step of the recurrence and returns
+    o [B, H, Dh] float32. ``q``, ``k``, ``v`` [B, H, Dh], ``alpha``, ``beta``
+    [B, H]. Not differentiable."""
+    if q.dim() != 3 or k.shape != q.shape or v.shape != q.shape:
+        raise ValueError(f"q, k, v must all be [B, H, Dh], got {tuple(q.shape)}, {tuple(k.shape)}, "
+                         f"{tuple(v.shape)}")
+    Bt, H, Dh = q.shape
+    for name, t in (("alpha", alpha), ("beta", beta)):
+        if tuple(t.shape) != (Bt, H):
+            raise ValueError(f"{name} must be [B, H] = [{Bt}, {H}], got {tuple(t.shape)}")
+    if Dh not in (32, 64):
+        raise ValueError(f"Dh={Dh} is not supported by the Gated DeltaNet kernels (32 or 64)")
+    dev = _lib.require_cuda(q, k, v, alpha, beta, state)
+    state = step_state(state, (Bt, H, Dh, Dh), dev)
+    dt = common_dtype(q, k, v, alpha, beta)
+    q_, k_, v_, a_, b_ = (prep(t.detach(), dt) for t in (q, k, v, alpha, beta))
+    y = torch.empty((Bt, H, Dh), dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        _lib.call("mr_gdn_step", _lib.ptr(q_), _lib.ptr(k_), _lib.ptr(v_), _lib.ptr(a_), _lib.ptr(b_),
+                  _lib.DTYPE_CODE[dt], Bt, H, Dh, _lib.ptr(state), _lib.ptr(y), _lib.stream_of(dev))
+    return y

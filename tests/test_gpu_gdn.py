@@ -107,3 +107,31 @@ def test_gdn_chunked_prefill_continues_the_scan(cuda_dev):
     y2, f2 = mr.gated_deltanet_scan_with_state(*(t[:, 96:] for t in ts), h0=f1)
     assert _err(torch.cat([y1, y2], dim=1), y.double().cpu().numpy()) <= 1e-5
     assert _err(f2, fin.double().cpu().numpy()) <= 1e-5
+
+
+@pytest.mark.parametrize("Dh,dtype", [(64, torch.float32), (32, torch.bfloat16)])
+def test_gdn_step_matches_oracle(cuda_dev, Dh, dtype):
+    """One decode step from a random state against one step of the oracle."""
+    mr = _mr()
+    Bt, H = 3, 2
+    ins = [x[:, 0] for x in _inputs(Bt, 1, H, Dh, seed=Dh)]
+    state0 = np.random.default_rng(1).standard_normal((Bt, H, Dh, Dh))
+    state = torch.tensor(state0, dtype=torch.float32, device=cuda_dev)
+    args = [torch.tensor(x, dtype=torch.float32).to(dtype).to(cuda_dev) for x in ins]
+    y = mr.gated_deltanet_step(*args, state)
+    torch.cuda.synchronize()
+    y_ref, s_ref = R.gdn_forward(*[_rounded(x, dtype)[:, None] for x in ins], h0=state0)
+    tol = TOL[dtype]
+    assert _err(y, y_ref[:, 0]) <= tol
+    assert _err(state, s_ref) <= tol
+
+
+def test_gdn_steps_reproduce_the_scan(cuda_dev):
+    mr = _mr()
+    Bt, T, H, Dh = 2, 32, 2, 64
+    ts = [torch.tensor(x, dtype=torch.float32, device=cuda_dev) for x in _inputs(Bt, T, H, Dh, seed=9)]
+    y_scan, fin = mr.gated_deltanet_scan_with_state(*ts, seg=T)
+    state = torch.zeros((Bt, H, Dh, Dh), dtype=torch.float32, device=cuda_dev)
+    ys = [mr.gated_deltanet_step(*(t[:, i] for t in ts), state) for i in range(T)]
+    assert _err(torch.stack(ys, dim=1), y_scan.double().cpu().numpy()) <= 1e-5
+    assert _err(state, fin.double().cpu().numpy()) <= 1e-5
