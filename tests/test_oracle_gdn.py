@@ -110,3 +110,27 @@ def test_c_oracle_gdn_matches_numpy_oracle():
     assert R.rel_err(out["final"], f) < 1e-5
     for g, r in zip(out["grads"], ref):
         assert R.rel_err(g, r) < 1e-5
+
+
+@pytest.mark.parametrize("C", [1, 4, 16, 7])
+def test_gdn_chunked_wy_form_equals_the_recurrence(C):
+    """The chunkwise WY algebra (the design's phase-1 gate: chunk form against
+    the sequential reference) reproduces the per-step recurrence, its outputs,
+    final state and the per-step w = beta (v - alpha S^T k), for chunk lengths
+    that do and do not divide L."""
+    rng = np.random.default_rng(C)
+    Bt, T, H, Dh = 2, 32, 2, 6
+    ins = list(_inputs(rng, Bt, T, H, Dh))
+    ins[3] = rng.uniform(0.05, 1.0, (Bt, T, H))      # strong decays too
+    h0 = rng.standard_normal((Bt, H, Dh, Dh))
+    y, fin = R.gdn_forward(*ins, h0=h0)
+    yc, finc, w = R.gdn_chunked_forward(*ins, C, h0=h0)
+    np.testing.assert_allclose(yc, y, rtol=1e-9, atol=1e-10)
+    np.testing.assert_allclose(finc, fin, rtol=1e-9, atol=1e-10)
+    q, k, v, al, be = ins
+    S = h0.copy()
+    for t in range(T):
+        p = np.einsum("bhij,bhi->bhj", S, k[:, t])
+        wt = be[:, t, :, None] * (v[:, t] - al[:, t, :, None] * p)
+        np.testing.assert_allclose(w[:, t], wt, rtol=1e-9, atol=1e-10)
+        S = al[:, t, :, None, None] * S + k[:, t, :, :, None] * wt[:, :, None, :]
