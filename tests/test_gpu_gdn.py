@@ -135,3 +135,21 @@ def test_gdn_steps_reproduce_the_scan(cuda_dev):
     ys = [mr.gated_deltanet_step(*(t[:, i] for t in ts), state) for i in range(T)]
     assert _err(torch.stack(ys, dim=1), y_scan.double().cpu().numpy()) <= 1e-5
     assert _err(state, fin.double().cpu().numpy()) <= 1e-5
+
+
+@pytest.mark.parametrize("Bt,L,H,Dh,seg", [
+    (130, 8, 32, 32, 8),      # 4160 units: backward CTAs walk more than one unit
+    (1, 256, 2, 64, 128),     # a segment of 8 staged blocks and 32 sub-blocks
+])
+def test_gdn_edge_shapes(cuda_dev, Bt, L, H, Dh, seg):
+    mr = _mr()
+    ins = _inputs(Bt, L, H, Dh, seed=Bt + L)
+    w = np.random.default_rng(2).standard_normal((Bt, L, H, Dh))
+    ts = [torch.tensor(x, dtype=torch.float32, device=cuda_dev).requires_grad_(True) for x in ins]
+    y = mr.gated_deltanet_scan(*ts, seg=seg)
+    (y * torch.tensor(w, dtype=torch.float32, device=cuda_dev)).sum().backward()
+    y_ref, _ = R.gdn_forward(*ins)
+    grads = R.gdn_backward(*ins, w)
+    assert _err(y, y_ref) <= 1e-5
+    for name, t, ref in zip(("q", "k", "v", "alpha", "beta"), ts, grads):
+        assert _err(t.grad, ref) <= 1e-5, name
