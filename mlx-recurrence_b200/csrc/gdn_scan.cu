@@ -66,6 +66,15 @@ __device__ __forceinline__ float gdn_group_sum(float x) {
   return x;
 }
 
+// sum over the P row groups of a column (lanes 32/P apart); every lane of the
+// group gets the same bits
+template <int P>
+__device__ __forceinline__ float gdn_group_sum_p(float x) {
+#pragma unroll
+  for (int o = 32 / P; o < 32; o <<= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+  return x;
+}
+
 __device__ __forceinline__ float gdn_warp_sum(float x) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
@@ -163,14 +172,19 @@ __device__ __forceinline__ float gdn_dot(const float (&x)[R], const float (&y)[R
 
 constexpr int kGdnTS = 16;  // steps per staged block of the forward and the backward's replay
 
+// The forward splits each column over P row groups (P threads, Dh/P rows each).
+// Four: eight at Dh = 64 was slower on B200 (c6 forward 4.8 ms against 3.15; the
+// same registers per thread, so no more warps per SM, and a third shuffle level).
+template <int DH> struct GdnFwdP { static constexpr int v = 4; };
+
 template <typename T, int DH, bool kH0>
-__global__ void __launch_bounds__(DH * 4)
+__global__ void __launch_bounds__(DH * GdnFwdP<DH>::v)
 gdn_fwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
                const T* __restrict__ alpha, const T* __restrict__ beta, int L, int H, int seg,
                float* __restrict__ y, float* __restrict__ ckpt, float* __restrict__ wp,
                const float* __restrict__ h0) {
-  constexpr int R = DH / 4, NT = DH * 4, TS = kGdnTS;
-  static_assert(TS * (DH / 4) == NT, "the conversion pass gives each thread 4 elements of each row");
+  constexpr int P = GdnFwdP<DH>::v, R = DH / P, NT = DH * P, TS = kGdnTS, CW = 32 / P;
+  static_assert(TS * (DH / 4) <= NT && (TS * (DH / 4)) % 32 == 0, "the conversion pass: 4 elements a thread");
   // staged inputs: k, q, v rows as copied [2 buffers][3][TS][DH] of T, as floats
   // [3][TS][DH], k.q per step [TS], alpha and beta [2][2][TS]
   __shared__ __align__(16) T srow[2][3 * TS * DH];
@@ -178,7 +192,7 @@ gdn_fwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
   __shared__ float skq[TS];
   __shared__ float sab[2][2][TS];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int g = lane >> 3, j = warp * 8 + (lane & 7), i0 = g * R;
+  const int g = lane / CW, j = warp * CW + (lane % CW), i0 = g * R;
   const int64_t b = blockIdx.x / H;
   const int h = blockIdx.x % H;
   const int nseg = L / seg, nblk = (L + TS - 1) / TS;
@@ -206,7 +220,8 @@ gdn_fwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
     gdn_cp_commit();
     gdn_cp_wait<1>();
     __syncthreads();
-    {  // one pass per block: rows to floats (4 elements of k, q, v per thread) and k.q per step
+    if (tid < TS * (DH / 4)) {  // one pass per block: rows to floats (4 elements of k, q, v
+                                // per thread) and k.q per step
       const int tt = tid / (DH / 4), c4 = (tid % (DH / 4)) * 4;
       const T* src = srow[buf] + tt * DH + c4;
       const float4 kk = gdn_ld4(src), qq = gdn_ld4(src + TS * DH), vv = gdn_ld4(src + 2 * TS * DH);
@@ -231,8 +246,8 @@ gdn_fwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
       gdn_ld_f32<R>(fq + tt * DH + i0, qr);
       const float vj = fv[tt * DH + j];
       const float a = sab[buf][0][tt], bt = sab[buf][1][tt];
-      const float p = gdn_group_sum(gdn_dot(kr, S));
-      const float sqv = gdn_group_sum(gdn_dot(qr, S));
+      const float p = gdn_group_sum_p<P>(gdn_dot(kr, S));
+      const float sqv = gdn_group_sum_p<P>(gdn_dot(qr, S));
       const float kq = skq[tt];
       const float w = bt * fmaf(-a, p, vj);
       if (g == 0) {
@@ -596,7 +611,7 @@ static int gdn_fwd_dh(const T* q, const T* k, const T* v, const T* al, const T* 
                       int64_t H, int64_t seg, float* y, float* ckpt, float* wp, const float* h0, cudaStream_t st) {
   const dim3 grid((unsigned)(batch * H));
   auto kern = h0 != nullptr ? gdn_fwd_kernel<T, DH, true> : gdn_fwd_kernel<T, DH, false>;
-  kern<<<grid, DH * 4, 0, st>>>(q, k, v, al, be, (int)L, (int)H, (int)seg, y, ckpt, wp, h0);
+  kern<<<grid, DH * GdnFwdP<DH>::v, 0, st>>>(q, k, v, al, be, (int)L, (int)H, (int)seg, y, ckpt, wp, h0);
   return check_launch("gdn_fwd_kernel");
 }
 
