@@ -5,7 +5,7 @@ not multiples of the backward's four-step sub-blocks, Dh 32 and 64, float32 and
 bfloat16, a final-state cotangent and an initial state; the kernels against
 autograd through the plug-in's torch loop on the GPU; the chunked-prefill
 property. Tolerances (max|diff| / max|ref|): 1e-5 for float32 inputs, 2e-2 for
-bfloat16."""
+bfloat16 and float16."""
 
 import importlib
 
@@ -17,7 +17,7 @@ from oracle import ref_loops as R
 
 pytestmark = pytest.mark.gpu
 
-TOL = {torch.float32: 1e-5, torch.bfloat16: 2e-2}
+TOL = {torch.float32: 1e-5, torch.bfloat16: 2e-2, torch.float16: 2e-2}
 
 
 def _mr():
@@ -53,6 +53,7 @@ def _err(got, ref):
     (1, 16, 2, 64, 1, torch.float32, True, True),      # one step per segment
     (2, 256, 4, 64, 64, torch.bfloat16, True, True),
     (3, 192, 5, 32, 48, torch.bfloat16, False, False),
+    (2, 128, 3, 64, 32, torch.float16, True, True),
 ])
 def test_gdn_matches_oracle(cuda_dev, Bt, L, H, Dh, seg, dtype, with_h0, with_gf):
     mr = _mr()

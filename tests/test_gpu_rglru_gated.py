@@ -3,7 +3,7 @@ reference leaves the gating to host code, rglru.py:8-27): forward, final state
 and the gradients of x, r, i, lam (and h0) against the oracle, and against
 autograd through the unfused composition (the gates formed in torch, then
 rglru_scan). Tolerances (max|diff| / max|ref|): 1e-5 for float32 inputs, 2e-2
-for bfloat16 (1e-2 between the two bf16 computations)."""
+for bfloat16 and float16 (1e-2 between the two bf16 computations)."""
 
 import importlib
 
@@ -15,7 +15,7 @@ from oracle import ref_loops as R
 
 pytestmark = pytest.mark.gpu
 
-TOL = {torch.float32: 1e-5, torch.bfloat16: 2e-2}
+TOL = {torch.float32: 1e-5, torch.bfloat16: 2e-2, torch.float16: 2e-2}
 C = 8.0
 
 
@@ -45,6 +45,7 @@ def _err(got, ref):
     (2, 512, 96, 256, torch.float32, True),    # segments longer than a block
     (3, 384, 128, 128, torch.bfloat16, True),
     (1, 4096, 256, 64, torch.bfloat16, False),
+    (2, 256, 96, 32, torch.float16, True),
 ])
 def test_gated_matches_oracle(cuda_dev, Bt, L, D, seg, dtype, with_h0):
     mr = _mr()

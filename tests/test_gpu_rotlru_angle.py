@@ -3,7 +3,7 @@ form cos and sin in host code, rotlru.py:18-22): forward, final state and the
 gradients of a, theta, x (and h0) against the oracle, and against autograd
 through the unfused composition (cos, sin formed in torch, then rotlru_scan).
 Tolerances (max|diff| / max|ref|): 1e-5 for float32 inputs, 2e-2 for
-bfloat16."""
+bfloat16 and float16."""
 
 import importlib
 
@@ -15,7 +15,7 @@ from oracle import ref_loops as R
 
 pytestmark = pytest.mark.gpu
 
-TOL = {torch.float32: 1e-5, torch.bfloat16: 2e-2}
+TOL = {torch.float32: 1e-5, torch.bfloat16: 2e-2, torch.float16: 2e-2}
 
 
 def _mr():
@@ -43,6 +43,7 @@ def _err(got, ref):
     (2, 512, 48, 256, torch.float32, True),    # segments longer than a block
     (3, 384, 64, 128, torch.bfloat16, True),
     (1, 2048, 160, 64, torch.bfloat16, False),  # a ragged channel tile
+    (2, 256, 64, 32, torch.float16, True),
 ])
 def test_angle_matches_oracle(cuda_dev, Bt, L, Dp, seg, dtype, with_h0):
     mr = _mr()
