@@ -43,7 +43,11 @@
 namespace mr {
 
 constexpr int kGdnK = 4;           // steps per replayed sub-block of the backward
-constexpr int kGdnMaxCtas = 4096;  // backward CTAs (each walks units), bounds the scratch
+constexpr int kGdnMaxCtas = 4096;  // backward CTAs at most (each walks units)
+// The backward's scratch (ceil(seg/4) states of Dh x Dh floats per CTA) is kept
+// under this many bytes by walking more units per CTA: long segments (small
+// checkpoint memory) do not turn into a large workspace.
+constexpr int64_t kGdnScratchBudget = (int64_t)1 << 30;
 
 // R consecutive elements of T at p (16-byte aligned) as floats
 template <typename T, int R>
@@ -624,14 +628,18 @@ int gdn_fwd_launch(const void* q, const void* k, const void* v, const void* alph
   return gdn_fwd_dh<T, 64>(q_, k_, v_, a_, b_, batch, L, H, seg, y, ckpt, wp, h0, st);
 }
 
-static int64_t gdn_bwd_grid(int64_t batch, int64_t H) {
+static int64_t gdn_bwd_grid(int64_t batch, int64_t H, int64_t Dh, int64_t seg) {
   const int64_t units = batch * H;
-  return units < kGdnMaxCtas ? units : kGdnMaxCtas;
+  const int64_t per_cta = gdn_scratch_floats(Dh, seg) * (int64_t)sizeof(float);
+  int64_t grid = units < kGdnMaxCtas ? units : kGdnMaxCtas;
+  const int64_t cap = kGdnScratchBudget / per_cta;
+  if (grid > cap) grid = cap > 0 ? cap : 1;
+  return grid;
 }
 
 size_t gdn_bwd_ws_bytes(int64_t batch, int64_t L, int64_t H, int64_t Dh, int64_t seg) {
   (void)L;
-  return (size_t)gdn_bwd_grid(batch, H) * gdn_scratch_floats(Dh, seg) * sizeof(float);
+  return (size_t)gdn_bwd_grid(batch, H, Dh, seg) * gdn_scratch_floats(Dh, seg) * sizeof(float);
 }
 
 template <typename T, int DH>
@@ -641,7 +649,7 @@ static int gdn_bwd_dh(const float* gy, const float* gf, const float* ckpt, const
   constexpr size_t sm = GdnBwdSmem<T, DH>::bytes;
   auto kern = h0 != nullptr ? gdn_bwd_kernel<T, DH, true> : gdn_bwd_kernel<T, DH, false>;
   if (int rc = gdn_set_smem(kern, sm)) return rc;
-  const dim3 grid((unsigned)gdn_bwd_grid(batch, H));
+  const dim3 grid((unsigned)gdn_bwd_grid(batch, H, DH, seg));
   kern<<<grid, DH * 4, sm, st>>>(gy, gf, ckpt, wp, q, k, v, al, be, (int)L, (int)H, (int)seg, (int)(batch * H), gq, gk,
                                  gv, ga, gb, ws, h0, gh0);
   return check_launch("gdn_bwd_kernel");

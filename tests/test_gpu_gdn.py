@@ -154,3 +154,25 @@ def test_gdn_edge_shapes(cuda_dev, Bt, L, H, Dh, seg):
     assert _err(y, y_ref) <= 1e-5
     for name, t, ref in zip(("q", "k", "v", "alpha", "beta"), ts, grads):
         assert _err(t.grad, ref) <= 1e-5, name
+
+
+def test_gdn_long_segment_backward_walks_units(cuda_dev):
+    """seg = L = 4096 at Dh = 32 needs 4 MB of scratch per backward CTA, so the
+    1 GiB budget caps the grid at 256 CTAs for 288 units (CTAs walk units): the
+    gradients equal those of the same problem with short segments."""
+    mr = _mr()
+    Bt, L, H, Dh = 9, 4096, 32, 32
+    g = torch.Generator(device=cuda_dev).manual_seed(3)
+    q = torch.nn.functional.normalize(torch.randn(Bt, L, H, Dh, device=cuda_dev, generator=g), dim=-1)
+    k = torch.nn.functional.normalize(torch.randn(Bt, L, H, Dh, device=cuda_dev, generator=g), dim=-1)
+    v = torch.randn(Bt, L, H, Dh, device=cuda_dev, generator=g)
+    al = torch.exp(-torch.nn.functional.softplus(torch.randn(Bt, L, H, device=cuda_dev, generator=g) - 3))
+    be = torch.sigmoid(torch.randn(Bt, L, H, device=cuda_dev, generator=g))
+    gy = torch.randn(Bt, L, H, Dh, device=cuda_dev, generator=g)
+    out = {}
+    for seg in (L, 64):
+        ts = [t.clone().requires_grad_(True) for t in (q, k, v, al, be)]
+        (mr.gated_deltanet_scan(*ts, seg=seg) * gy).sum().backward()
+        out[seg] = [t.grad for t in ts]
+    for name, a, b in zip(("q", "k", "v", "alpha", "beta"), out[L], out[64]):
+        assert _err(a, b.double().cpu().numpy()) <= 1e-5, name

@@ -157,3 +157,14 @@ def test_reference_loops_match_oracle_on_cpu(mr):
     y = mr.ssd_scan_reference(u, d, B, C, A).numpy()
     yo, _ = R.ssd_forward(u.numpy(), d.numpy(), B.numpy(), C.numpy(), A.numpy())
     assert np.max(np.abs(y - yo)) < 1e-12
+
+
+def test_gdn_backward_workspace_is_bounded(mr):
+    """Long Gated DeltaNet segments (few checkpoints) do not grow the backward's
+    scratch past its budget: the CTAs walk more units instead."""
+    from importlib import import_module
+    lib = import_module("mlx-recurrence_b200._lib").load()
+    small = lib.mr_gdn_bwd_workspace_bytes(1, 32, 2048, 32, 64, 64)
+    huge = lib.mr_gdn_bwd_workspace_bytes(1, 32, 65536, 32, 64, 65536)
+    assert small == 1024 * 16 * 64 * 64 * 4
+    assert 0 < huge <= (1 << 30)
