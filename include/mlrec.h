@@ -257,14 +257,18 @@ MR_API int mr_rotlru_bwd_h0(const float* grad_y, const float* grad_final, const 
  * `dtype`; y [B,L,H,Dh] float32; h_ckpt [B, L/seg, H, Dh, Dh] float32 (the state
  * after each segment, i-major; the last is the final state); h0 / grad_h0
  * [B,H,Dh,Dh] float32 or NULL. Dh must be 32 or 64 and L a multiple of seg.
- * step_cache [B,L,H,2,Dh] float32 receives, per step, w_t = beta (v - alpha
- * S_{t-1}^T k) and p_t = S_{t-1}^T k (NULL in the forward: not kept); the
- * backward reads it (required there) so that it replays states without the
- * dot products. The backward writes grad_q, grad_k, grad_v, grad_alpha,
+ * step_cache [B,L,H,Dh] float32 receives, per step, w_t = beta (v - alpha
+ * S_{t-1}^T k) (NULL in the forward: not kept); the backward reads it
+ * (required there) so that it replays states without the dot products.
+ * With 2-byte inputs, Dh = 64, L a multiple of 128 and seg a multiple of 64 the
+ * forward runs in chunkwise (WY) form when given mr_gdn_fwd_workspace_bytes of
+ * device workspace (NULL or too small: the per-step form, same results within
+ * the parity tolerance). The backward writes grad_q, grad_k, grad_v, grad_alpha,
  * grad_beta in `dtype` and needs mr_gdn_bwd_workspace_bytes of device scratch. */
 MR_API int mr_gdn_fwd(const void* q, const void* k, const void* v, const void* alpha, const void* beta, int dtype,
                       int64_t batch, int64_t L, int64_t H, int64_t Dh, int64_t seg, float* y, float* h_ckpt,
-                      float* step_cache, const float* h0, void* stream);
+                      float* step_cache, const float* h0, void* workspace, size_t workspace_bytes, void* stream);
+MR_API size_t mr_gdn_fwd_workspace_bytes(int dtype, int64_t batch, int64_t L, int64_t H, int64_t Dh, int64_t seg);
 MR_API size_t mr_gdn_bwd_workspace_bytes(int dtype, int64_t batch, int64_t L, int64_t H, int64_t Dh, int64_t seg);
 MR_API int mr_gdn_bwd(const float* grad_y, const float* grad_final, const float* h_ckpt, const float* step_cache,
                       const void* q, const void* k, const void* v, const void* alpha, const void* beta, int dtype, int64_t batch,

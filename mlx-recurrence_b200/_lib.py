@@ -84,7 +84,8 @@ SIGNATURES = {
     "mr_rotlru_angle_bwd": (_int, [_p, _p, _p, _p, _p, _p, _int, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _sz,
                                    _p, _p, _p]),
     # Gated DeltaNet (per-step form, segment checkpoints)
-    "mr_gdn_fwd": (_int, [_p, _p, _p, _p, _p, _int, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _p]),
+    "mr_gdn_fwd": (_int, [_p, _p, _p, _p, _p, _int, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _sz, _p]),
+    "mr_gdn_fwd_workspace_bytes": (_sz, [_int, _i64, _i64, _i64, _i64, _i64]),
     "mr_gdn_bwd_workspace_bytes": (_sz, [_int, _i64, _i64, _i64, _i64, _i64]),
     "mr_gdn_step": (_int, [_p, _p, _p, _p, _p, _int, _i64, _i64, _i64, _p, _p, _p]),
     "mr_gdn_bwd": (_int, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _int, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _p,

@@ -23,8 +23,8 @@
 // (grad_q = S_t go, grad_k = G w + S_{t-1} gp) go through shared memory once
 // per step.
 //
-// The forward also keeps w_t and p_t per step ([B,L,H,2,Dh] float32, the size of
-// two outputs), so the backward never repeats the dot products: per segment
+// The forward also keeps w_t per step ([B,L,H,Dh] float32, the size of the
+// output), so the backward's replays need no dot products: per segment
 // (newest first), phase A replays the states from the segment's checkpoint with
 // the stored w (S <- alpha S + k w^T, two operations per element and step) and
 // keeps a sub-checkpoint of S every kGdnK steps in a per-CTA scratch
@@ -186,7 +186,8 @@ __global__ void __launch_bounds__(DH * GdnFwdP<DH>::v)
 gdn_fwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
                const T* __restrict__ alpha, const T* __restrict__ beta, int L, int H, int seg,
                float* __restrict__ y, float* __restrict__ ckpt, float* __restrict__ wp,
-               const float* __restrict__ h0) {
+               const float* __restrict__ h0, const int* __restrict__ only) {
+  if (only != nullptr && only[blockIdx.x] == 0) return;  // recompute flagged units only
   constexpr int P = GdnFwdP<DH>::v, R = DH / P, NT = DH * P, TS = kGdnTS, CW = 32 / P;
   static_assert(TS * (DH / 4) <= NT && (TS * (DH / 4)) % 32 == 0, "the conversion pass: 4 elements a thread");
   // staged inputs: k, q, v rows as copied [2 buffers][3][TS][DH] of T, as floats
@@ -257,10 +258,7 @@ gdn_fwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __rest
       if (g == 0) {
         const int64_t row = (b * L + t) * H + h;
         y[row * DH + j] = fmaf(a, sqv, kq * w);
-        if (wp != nullptr) {
-          wp[row * 2 * DH + j] = w;
-          wp[(row * 2 + 1) * DH + j] = p;
-        }
+        if (wp != nullptr) wp[row * DH + j] = w;
       }
       gdn_update(S, kr, a, w);
       if ((t + 1) % seg == 0) {
@@ -290,7 +288,7 @@ struct GdnBwdSmem {
   static constexpr size_t rsc = ((size_t)K * (NT / 32) * 2 * 4 + 15) / 16 * 16;  // [K][NW][2] scalars
   static constexpr size_t a_ab = (size_t)2 * TS * 4, a_w = (size_t)2 * TS * DH * 4;
   static constexpr size_t a_rows = (size_t)2 * TS * DH * sizeof(T);
-  static constexpr size_t b_f32 = (size_t)2 * 3 * K * DH * 4, b_ab = (size_t)2 * 2 * K * 4;
+  static constexpr size_t b_f32 = (size_t)2 * 2 * K * DH * 4, b_ab = (size_t)2 * 2 * K * 4;
   static constexpr size_t b_cvt = (size_t)3 * K * DH * 4, b_wgo = 16;
   static constexpr size_t b_rows = (size_t)2 * 3 * K * DH * sizeof(T);
   static constexpr size_t stage_a = a_ab + a_w + a_rows, stage_b = b_f32 + b_ab + b_cvt + b_wgo + b_rows;
@@ -325,7 +323,7 @@ gdn_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfinal, c
   float* a_w = reinterpret_cast<float*>(stg + SM::a_ab);       // [2][TS][DH]: w
   T* a_rows = reinterpret_cast<T*>(stg + SM::a_ab + SM::a_w);  // [2][TS][DH]: k
   // phase B staging
-  float* b_f32 = reinterpret_cast<float*>(stg);                // [2][3][K][DH]
+  float* b_f32 = reinterpret_cast<float*>(stg);                // [2][2][K][DH]: go, w
   float* b_ab = reinterpret_cast<float*>(stg + SM::b_f32);     // [2][2][K]
   float* b_cvt = reinterpret_cast<float*>(stg + SM::b_f32 + SM::b_ab);  // [3][K][DH]: q, k, v
   float* b_wgo = b_cvt + 3 * K * DH;                                   // [K]
@@ -364,7 +362,7 @@ gdn_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfinal, c
           gdn_stage_rows<T, DH, TS, 1, NT>(a_rows + bb * TS * DH, k, k, k, b, h, L, H, t0 + tl0);
           for (int c = tid; c < TS * CHF; c += NT) {
             const int tt = c / CHF, ch = c % CHF, tl = tl0 + tt;
-            if (tl < seg) gdn_cp16(a_w + (bb * TS + tt) * DH + ch * 4, wp + ((b * L + t0 + tl) * H + h) * 2 * DH + ch * 4);
+            if (tl < seg) gdn_cp16(a_w + (bb * TS + tt) * DH + ch * 4, wp + ((b * L + t0 + tl) * H + h) * DH + ch * 4);
           }
         };
         stage_a(0, 0);
@@ -403,13 +401,13 @@ gdn_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfinal, c
       // ---- phase B: sub-blocks newest first, their inputs staged one sub-block ahead
       auto stage_b = [&](int sb, int bb) {
         gdn_stage_rows<T, DH, K, 3, NT>(b_rows + bb * 3 * K * DH, q, k, v, b, h, L, H, t0 + sb * K);
-        float* dst = b_f32 + bb * 3 * K * DH;
-        for (int c = tid; c < 3 * K * CHF; c += NT) {
+        float* dst = b_f32 + bb * 2 * K * DH;
+        for (int c = tid; c < 2 * K * CHF; c += NT) {
           const int which = c / (K * CHF), rem = c % (K * CHF), tt = rem / CHF, ch = rem % CHF;
           const int tl = sb * K + tt;
           if (tl < seg) {
             const int64_t row = (b * L + t0 + tl) * H + h;
-            const float* src = which == 0 ? gy + row * DH : wp + (row * 2 + (which - 1)) * DH;
+            const float* src = (which == 0 ? gy : wp) + row * DH;
             gdn_cp16(dst + (which * K + tt) * DH + ch * 4, src + ch * 4);
           }
         }
@@ -427,9 +425,8 @@ gdn_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfinal, c
         gdn_cp_commit();
         gdn_cp_wait<1>();
         __syncthreads();
-        const float* fgo = b_f32 + bb * 3 * K * DH;
+        const float* fgo = b_f32 + bb * 2 * K * DH;
         const float* fw = fgo + K * DH;
-        const float* fp = fw + K * DH;
         const float* fab = b_ab + bb * 2 * K;
         {  // the sub-block's q, k, v rows as floats (threads 0 .. 3KDH/4 - 1, one 4-element
            // chunk each) and w.go per step (the last KDH/4 threads)
@@ -492,7 +489,8 @@ gdn_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfinal, c
             }
             const float vj = rv_[m * DH + j];
             const float a = fab[m], bt = fab[K + m];
-            const float w = fw[m * DH + j], p = fp[m * DH + j];
+            const float w = fw[m * DH + j];
+            const float p = gdn_group_sum(gdn_dot(kr, Sp));  // S_{t-1}^T k, from the replayed state
             const float d = gdn_group_sum(gdn_dot(kr, G));
             const float gp = -a * bt * d;
             float gaP = gdn_dot(G, Sp), gbP = 0.f;
@@ -570,6 +568,373 @@ gdn_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfinal, c
   }
 }
 
+// ============================================================================
+// Chunkwise (WY) forward, bf16/fp16 inputs, Dh = 64, L a multiple of 128
+// ============================================================================
+//
+// Within a chunk of Q = 128 steps entered with state S0, with gamma_r the
+// cumulative decay from the chunk start (gamma_r / gamma_i <= 1 for i <= r):
+//   w_r = beta_r (v_r - gamma_r S0^T k_r - sum_{i<r} (gamma_r / gamma_i)(k_r . k_i) w_i),
+// i.e. (I + A) W = R with A[r, i] = beta_r (gamma_r / gamma_i) k_r . k_i (i < r)
+// and R = diag(beta) (V - diag(gamma) K S0); then
+//   S_end = gamma_last S0 + K^T diag(gamma_last / gamma) W
+// (docs/DESIGN_gated_deltanet.md:139-270; pinned by oracle/ref_loops.gdn_chunked_forward).
+// Given W, a chunk's outputs o_t = S_t^T q_t and its state update are exactly a
+// GLA chunk with values W (S_t = gamma_t S0 + sum_{i<=t} (gamma_t/gamma_i) k_i w_i^T),
+// so the forward runs in two kernels: this one, sequential over a unit's chunks,
+// forms W (the unit triangular solve blocked by 16 rows: a panel update of the
+// block's rows from the earlier rows, then a 16-step substitution per column)
+// and the states at the checkpoints; the GLA chunk kernel (tcgen05) then
+// computes the outputs from (q, k, W, alpha). W also fills the step cache the
+// backward replays from. log(alpha) is taken of max(alpha, 1e-30) (an alpha of 0
+// resets the state without a 0/0 in the decay ratios); a unit with an alpha above
+// 1 (or NaN) is flagged and recomputed by the per-step forward.
+namespace gdnc {
+constexpr int Q = 128, DH = 64, NT = 256, BLK = 16;
+constexpr int KS = DH + 4;   // row stride (floats) of the K, W and state buffers
+constexpr int AS = BLK + 4;  // row stride of A's panel, stored transposed [i][row in block]
+constexpr int TS2 = BLK + 1; // row stride of the diagonal blocks' inverses [blk][r][c]
+constexpr size_t SMEM = (size_t)(2 * Q * KS + DH * KS + Q * AS + Q * TS2 + 6 * Q + 8) * sizeof(float);
+}  // namespace gdnc
+
+template <typename T, bool kH0>
+__global__ void __launch_bounds__(gdnc::NT, 2)
+gdn_wy_state_kernel(const T* __restrict__ k, const T* __restrict__ v, const T* __restrict__ alpha,
+                    const T* __restrict__ beta, int L, int H, int seg, float* __restrict__ wcache,
+                    T* __restrict__ wout, float* __restrict__ ckpt, int* __restrict__ flags,
+                    const float* __restrict__ h0) {
+  using namespace gdnc;
+  extern __shared__ float4 gdnc_smem[];
+  float* sK = reinterpret_cast<float*>(gdnc_smem);  // [Q][KS]
+  float* sW = sK + Q * KS;                          // [Q][KS]: V, then R, then W
+  float* sH = sW + Q * KS;                          // [DH][KS]: the state S[i][j]
+  float* sA = sH + DH * KS;                         // [Q][AS]: A's panel [i][row - rb]; first the diagonal blocks
+  float* sT = sA + Q * AS;                          // [Q][TS2]: the diagonal blocks' inverses [blk][r][c]
+  float* sLg = sT + Q * TS2;                        // [Q] cumulative log decay
+  float* sGam = sLg + Q;                            // [Q] gamma_r
+  float* sDq = sGam + Q;                            // [Q] gamma_last / gamma_r
+  float* sDm = sDq + Q;                             // [Q] gamma_63 / gamma_r (r < 64)
+  float* sBeta = sDm + Q;                           // [Q]
+  float* sWs = sBeta + Q;                           // [Q] scratch: log alpha, warp totals
+  int* sFlag = reinterpret_cast<int*>(sWs + Q);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t b = blockIdx.x / H;
+  const int h = blockIdx.x % H;
+  const int nck = L / Q, nseg = L / seg;
+
+  if (tid == 0) *sFlag = 0;
+  for (int e = tid; e < DH * DH; e += NT) {
+    const int i = e / DH, j = e % DH;
+    sH[i * KS + j] = kH0 ? h0[((b * H + h) * DH + i) * (int64_t)DH + j] : 0.f;
+  }
+  __syncthreads();
+
+  for (int c = 0; c < nck; ++c) {
+    const int64_t row0 = b * L + (int64_t)c * Q;  // [B,L] row of the chunk's first step
+    // ---- (a) K, V rows as floats; alpha, beta
+#pragma unroll
+    for (int m = 0; m < Q * DH / 8 / NT; ++m) {
+      const int idx = tid + NT * m, r = idx / 8, c8 = (idx % 8) * 8;
+      const int64_t g = ((row0 + r) * H + h) * DH + c8;
+      const Vec<T, 8> kv = ld_vec<T, 8>(k + g), vv = ld_vec<T, 8>(v + g);
+#pragma unroll
+      for (int e = 0; e < 8; e += 4) {
+        *reinterpret_cast<float4*>(sK + r * KS + c8 + e) =
+            make_float4(to_f(kv.v[e]), to_f(kv.v[e + 1]), to_f(kv.v[e + 2]), to_f(kv.v[e + 3]));
+        *reinterpret_cast<float4*>(sW + r * KS + c8 + e) =
+            make_float4(to_f(vv.v[e]), to_f(vv.v[e + 1]), to_f(vv.v[e + 2]), to_f(vv.v[e + 3]));
+      }
+    }
+    if (tid < Q) {
+      const int64_t g = (row0 + tid) * H + h;
+      const float a = to_f(alpha[g]);
+      if (!(a <= 1.f)) *sFlag = 1;
+      sWs[tid] = logf(fmaxf(a, 1e-30f));
+      sBeta[tid] = to_f(beta[g]);
+    }
+    __syncthreads();
+    // ---- (b) cumulative log decay (warps 0-3 scan 32 steps each)
+    if (warp < Q / 32) {
+      float x = sWs[tid];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float n = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += n;
+      }
+      sLg[tid] = x;
+    }
+    __syncthreads();
+    if (tid < Q) {
+      float x = sLg[tid];
+      for (int w2 = 0; w2 < tid / 32; ++w2) x += sLg[32 * w2 + 31];
+      sWs[tid] = x;  // the scanned values, moved so the warp totals stay readable above
+    }
+    __syncthreads();
+    if (tid < Q) {
+      const float lg = sWs[tid];
+      sLg[tid] = lg;
+      sGam[tid] = expf(lg);
+      sDq[tid] = expf(sWs[Q - 1] - lg);
+      sDm[tid] = tid < 64 ? expf(sWs[63] - lg) : 0.f;
+    }
+    __syncthreads();
+    // ---- (c) R = diag(beta) (V - diag(gamma) K S0): thread rows 8 rg.., columns 4 jg..
+    {
+      const int rg = tid / 16, jg = tid % 16;
+      float acc[8][4];
+#pragma unroll
+      for (int rr = 0; rr < 8; ++rr)
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) acc[rr][jj] = 0.f;
+      for (int i = 0; i < DH; i += 4) {
+        float4 hr[4];
+#pragma unroll
+        for (int ii = 0; ii < 4; ++ii) hr[ii] = *reinterpret_cast<const float4*>(sH + (i + ii) * KS + 4 * jg);
+#pragma unroll
+        for (int rr = 0; rr < 8; ++rr) {
+          const float4 kk = *reinterpret_cast<const float4*>(sK + (8 * rg + rr) * KS + i);
+          const float kx[4] = {kk.x, kk.y, kk.z, kk.w};
+#pragma unroll
+          for (int ii = 0; ii < 4; ++ii) {
+            acc[rr][0] = fmaf(kx[ii], hr[ii].x, acc[rr][0]);
+            acc[rr][1] = fmaf(kx[ii], hr[ii].y, acc[rr][1]);
+            acc[rr][2] = fmaf(kx[ii], hr[ii].z, acc[rr][2]);
+            acc[rr][3] = fmaf(kx[ii], hr[ii].w, acc[rr][3]);
+          }
+        }
+      }
+#pragma unroll
+      for (int rr = 0; rr < 8; ++rr) {
+        const int r = 8 * rg + rr;
+        const float bt = sBeta[r], gm = sGam[r];
+        float4* wr = reinterpret_cast<float4*>(sW + r * KS + 4 * jg);
+        const float4 vv = *wr;
+        *wr = make_float4(bt * fmaf(-gm, acc[rr][0], vv.x), bt * fmaf(-gm, acc[rr][1], vv.y),
+                          bt * fmaf(-gm, acc[rr][2], vv.z), bt * fmaf(-gm, acc[rr][3], vv.w));
+      }
+    }
+    __syncthreads();
+    // ---- (d) the unit lower triangular solve (I + A) W = R by blocks of 16 rows:
+    // the diagonal blocks' inverses T_b = (I + A_bb)^-1 first (they need only K,
+    // alpha, beta), then per block W_b = T_b (R_b - A_b,<b W_<b), two parallel products.
+    // (d0) the eight diagonal blocks of A, [blk][r][i] in sA, 4 x 4 tiles
+    if (tid < 8 * 16) {
+      const int bb = tid / 16, rg = (tid % 16) % 4, ig = (tid % 16) / 4, rb = BLK * bb;
+      float acc[4][4];
+#pragma unroll
+      for (int a2 = 0; a2 < 4; ++a2)
+#pragma unroll
+        for (int b2 = 0; b2 < 4; ++b2) acc[a2][b2] = 0.f;
+      for (int d = 0; d < DH; d += 4) {
+        float4 kr[4], ki[4];
+#pragma unroll
+        for (int a2 = 0; a2 < 4; ++a2) {
+          kr[a2] = *reinterpret_cast<const float4*>(sK + (rb + 4 * rg + a2) * KS + d);
+          ki[a2] = *reinterpret_cast<const float4*>(sK + (rb + 4 * ig + a2) * KS + d);
+        }
+#pragma unroll
+        for (int a2 = 0; a2 < 4; ++a2)
+#pragma unroll
+          for (int b2 = 0; b2 < 4; ++b2)
+            acc[a2][b2] = fmaf(kr[a2].x, ki[b2].x, fmaf(kr[a2].y, ki[b2].y,
+                          fmaf(kr[a2].z, ki[b2].z, fmaf(kr[a2].w, ki[b2].w, acc[a2][b2]))));
+      }
+#pragma unroll
+      for (int a2 = 0; a2 < 4; ++a2)
+#pragma unroll
+        for (int b2 = 0; b2 < 4; ++b2) {
+          const int r = rb + 4 * rg + a2, i = rb + 4 * ig + b2;
+          sA[(bb * BLK + 4 * rg + a2) * BLK + 4 * ig + b2] =
+              i < r ? sBeta[r] * expf(sLg[r] - sLg[i]) * acc[a2][b2] : 0.f;
+        }
+    }
+    __syncthreads();
+    // (d0') column c of T_b by forward substitution, all blocks at once
+    if (tid < 8 * 16) {
+      const int bb = tid / 16, cc = tid % 16;
+      const float* Ab = sA + bb * BLK * BLK;
+      float x[BLK];
+#pragma unroll
+      for (int r = 0; r < BLK; ++r) {
+        float v = r == cc ? 1.f : 0.f;
+#pragma unroll
+        for (int i = 0; i < r; ++i) v = fmaf(-Ab[r * BLK + i], x[i], v);
+        x[r] = r < cc ? 0.f : v;
+      }
+#pragma unroll
+      for (int r = 0; r < BLK; ++r) sT[(bb * BLK + r) * TS2 + cc] = x[r];
+    }
+    __syncthreads();
+    for (int blk = 0; blk < Q / BLK; ++blk) {
+      const int rb = BLK * blk;
+      if (rb > 0) {
+        // (d1) the panel A[rb.., 0..rb), stored transposed sA[i][row - rb]: 2 x 4 tiles
+        if (tid < 2 * rb) {
+          const int rg = tid % 8, ig = tid / 8;
+          float acc[2][4];
+#pragma unroll
+          for (int a2 = 0; a2 < 2; ++a2)
+#pragma unroll
+            for (int b2 = 0; b2 < 4; ++b2) acc[a2][b2] = 0.f;
+          for (int d = 0; d < DH; d += 4) {
+            float4 kr[2], ki[4];
+#pragma unroll
+            for (int a2 = 0; a2 < 2; ++a2) kr[a2] = *reinterpret_cast<const float4*>(sK + (rb + 2 * rg + a2) * KS + d);
+#pragma unroll
+            for (int b2 = 0; b2 < 4; ++b2) ki[b2] = *reinterpret_cast<const float4*>(sK + (4 * ig + b2) * KS + d);
+#pragma unroll
+            for (int a2 = 0; a2 < 2; ++a2)
+#pragma unroll
+              for (int b2 = 0; b2 < 4; ++b2)
+                acc[a2][b2] = fmaf(kr[a2].x, ki[b2].x, fmaf(kr[a2].y, ki[b2].y,
+                              fmaf(kr[a2].z, ki[b2].z, fmaf(kr[a2].w, ki[b2].w, acc[a2][b2]))));
+          }
+#pragma unroll
+          for (int b2 = 0; b2 < 4; ++b2) {
+            const int i = 4 * ig + b2;
+            const int r0 = rb + 2 * rg;
+            *reinterpret_cast<float2*>(sA + i * AS + 2 * rg) =
+                make_float2(sBeta[r0] * expf(sLg[r0] - sLg[i]) * acc[0][b2],
+                            sBeta[r0 + 1] * expf(sLg[r0 + 1] - sLg[i]) * acc[1][b2]);
+          }
+        }
+        __syncthreads();
+        // (d2) R_b -= A_b,<b W_<b: 4 x 4 tiles, the rb earlier rows split over four
+        // thread groups (lanes 8 and 16 apart) whose partial tiles are summed by shuffles
+        {
+          const int tile = (tid & 7) | ((tid >> 5) << 3), part = (lane >> 3) & 3;
+          const int rg = tile % 4, jg = tile / 4, q4 = rb / 4;
+          float acc[4][4];
+#pragma unroll
+          for (int a2 = 0; a2 < 4; ++a2)
+#pragma unroll
+            for (int b2 = 0; b2 < 4; ++b2) acc[a2][b2] = 0.f;
+          for (int i = part * q4; i < (part + 1) * q4; ++i) {
+            const float4 a = *reinterpret_cast<const float4*>(sA + i * AS + 4 * rg);
+            const float4 w = *reinterpret_cast<const float4*>(sW + i * KS + 4 * jg);
+            const float ax[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+            for (int a2 = 0; a2 < 4; ++a2) {
+              acc[a2][0] = fmaf(ax[a2], w.x, acc[a2][0]);
+              acc[a2][1] = fmaf(ax[a2], w.y, acc[a2][1]);
+              acc[a2][2] = fmaf(ax[a2], w.z, acc[a2][2]);
+              acc[a2][3] = fmaf(ax[a2], w.w, acc[a2][3]);
+            }
+          }
+#pragma unroll
+          for (int a2 = 0; a2 < 4; ++a2)
+#pragma unroll
+            for (int b2 = 0; b2 < 4; ++b2) {
+              acc[a2][b2] += __shfl_xor_sync(0xffffffffu, acc[a2][b2], 8);
+              acc[a2][b2] += __shfl_xor_sync(0xffffffffu, acc[a2][b2], 16);
+            }
+          if (part == 0) {
+#pragma unroll
+            for (int a2 = 0; a2 < 4; ++a2) {
+              float4* rw = reinterpret_cast<float4*>(sW + (rb + 4 * rg + a2) * KS + 4 * jg);
+              const float4 x = *rw;
+              *rw = make_float4(x.x - acc[a2][0], x.y - acc[a2][1], x.z - acc[a2][2], x.w - acc[a2][3]);
+            }
+          }
+        }
+        __syncthreads();
+      }
+      // (d3) W_b = T_b R_b: one row and 4 columns per thread
+      {
+        const int rr = tid / 16, j4 = 4 * (tid % 16);
+        const float* Tr = sT + (blk * BLK + rr) * TS2;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int cc = 0; cc < BLK; ++cc) {
+          const float t = Tr[cc];
+          const float4 x = *reinterpret_cast<const float4*>(sW + (rb + cc) * KS + j4);
+          acc.x = fmaf(t, x.x, acc.x), acc.y = fmaf(t, x.y, acc.y), acc.z = fmaf(t, x.z, acc.z),
+          acc.w = fmaf(t, x.w, acc.w);
+        }
+        __syncthreads();  // every thread has read the block's R before it becomes W
+        *reinterpret_cast<float4*>(sW + (rb + rr) * KS + j4) = acc;
+      }
+      // the next block's panel (d1) reads only K; its update (d2) reads this W after d1's barrier
+    }
+    __syncthreads();
+    // ---- (e) W out: the step cache (float32) and the GLA kernel's values (T)
+#pragma unroll
+    for (int m = 0; m < Q * DH / 4 / NT; ++m) {
+      const int idx = tid + NT * m, r = idx / 16, j4 = 4 * (idx % 16);
+      const float4 w = *reinterpret_cast<const float4*>(sW + r * KS + j4);
+      const int64_t g = ((row0 + r) * H + h) * DH + j4;
+      if (wcache != nullptr) *reinterpret_cast<float4*>(wcache + g) = w;
+      const float f[4] = {w.x, w.y, w.z, w.w};
+      st_vec<T, 4>(wout + g, f);
+    }
+    // ---- (f) the state at the chunk's middle and end: thread rows 4 ig.., columns 4 jg..
+    {
+      const int ig = tid / 16, jg = tid % 16;
+      float acc[4][4];
+#pragma unroll
+      for (int a2 = 0; a2 < 4; ++a2)
+#pragma unroll
+        for (int b2 = 0; b2 < 4; ++b2) acc[a2][b2] = 0.f;
+      auto accumulate = [&](int r0, int r1, const float* scale) {
+        for (int r = r0; r < r1; ++r) {
+          const float sc = scale[r];
+          const float4 kk = *reinterpret_cast<const float4*>(sK + r * KS + 4 * ig);
+          const float4 ww = *reinterpret_cast<const float4*>(sW + r * KS + 4 * jg);
+          const float kx[4] = {kk.x * sc, kk.y * sc, kk.z * sc, kk.w * sc};
+#pragma unroll
+          for (int a2 = 0; a2 < 4; ++a2) {
+            acc[a2][0] = fmaf(kx[a2], ww.x, acc[a2][0]);
+            acc[a2][1] = fmaf(kx[a2], ww.y, acc[a2][1]);
+            acc[a2][2] = fmaf(kx[a2], ww.z, acc[a2][2]);
+            acc[a2][3] = fmaf(kx[a2], ww.w, acc[a2][3]);
+          }
+        }
+      };
+      float hs[4][4];
+      // middle: S_63 = gamma_63 S0 + sum_{r<64} (gamma_63/gamma_r) k_r w_r^T
+      accumulate(0, Q / 2, sDm);
+      const float g63 = sGam[Q / 2 - 1];
+#pragma unroll
+      for (int a2 = 0; a2 < 4; ++a2)
+#pragma unroll
+        for (int b2 = 0; b2 < 4; ++b2) hs[a2][b2] = fmaf(g63, sH[(4 * ig + a2) * KS + 4 * jg + b2], acc[a2][b2]);
+      const int64_t tmid = (int64_t)c * Q + Q / 2;
+      if (tmid % seg == 0) {
+        float* ck = ckpt + ((b * nseg + tmid / seg - 1) * H + h) * (int64_t)DH * DH;
+#pragma unroll
+        for (int a2 = 0; a2 < 4; ++a2)
+          *reinterpret_cast<float4*>(ck + (4 * ig + a2) * DH + 4 * jg) =
+              make_float4(hs[a2][0], hs[a2][1], hs[a2][2], hs[a2][3]);
+      }
+      // end: S_127 = (gamma_127 / gamma_63) S_63 + sum_{r>=64} (gamma_127/gamma_r) k_r w_r^T
+#pragma unroll
+      for (int a2 = 0; a2 < 4; ++a2)
+#pragma unroll
+        for (int b2 = 0; b2 < 4; ++b2) acc[a2][b2] = 0.f;
+      accumulate(Q / 2, Q, sDq);
+      const float gq = sDq[Q / 2 - 1];  // gamma_127 / gamma_63
+#pragma unroll
+      for (int a2 = 0; a2 < 4; ++a2)
+#pragma unroll
+        for (int b2 = 0; b2 < 4; ++b2) {
+          const float x = fmaf(gq, hs[a2][b2], acc[a2][b2]);
+          hs[a2][b2] = x;
+          sH[(4 * ig + a2) * KS + 4 * jg + b2] = x;  // this thread's own tile of the state
+        }
+      const int64_t tend = (int64_t)(c + 1) * Q;
+      if (tend % seg == 0) {
+        float* ck = ckpt + ((b * nseg + tend / seg - 1) * H + h) * (int64_t)DH * DH;
+#pragma unroll
+        for (int a2 = 0; a2 < 4; ++a2)
+          *reinterpret_cast<float4*>(ck + (4 * ig + a2) * DH + 4 * jg) =
+              make_float4(hs[a2][0], hs[a2][1], hs[a2][2], hs[a2][3]);
+      }
+    }
+    __syncthreads();  // the next chunk overwrites K, W and the scalars
+  }
+  if (tid == 0) flags[blockIdx.x] = *sFlag;
+}
+
 // One-token decode step on a float32 state cache [B,H,Dh,Dh] (the final
 // state's layout), advanced in place; y [B,H,Dh] float32. One step of the
 // forward's recurrence, same layout (one CTA per (b, h)).
@@ -612,18 +977,58 @@ static int gdn_set_smem(Kern kernel, size_t bytes) {
 
 template <typename T, int DH>
 static int gdn_fwd_dh(const T* q, const T* k, const T* v, const T* al, const T* be, int64_t batch, int64_t L,
-                      int64_t H, int64_t seg, float* y, float* ckpt, float* wp, const float* h0, cudaStream_t st) {
+                      int64_t H, int64_t seg, float* y, float* ckpt, float* wp, const float* h0, cudaStream_t st,
+                      const int* only = nullptr) {
   const dim3 grid((unsigned)(batch * H));
   auto kern = h0 != nullptr ? gdn_fwd_kernel<T, DH, true> : gdn_fwd_kernel<T, DH, false>;
-  kern<<<grid, DH * GdnFwdP<DH>::v, 0, st>>>(q, k, v, al, be, (int)L, (int)H, (int)seg, y, ckpt, wp, h0);
+  kern<<<grid, DH * GdnFwdP<DH>::v, 0, st>>>(q, k, v, al, be, (int)L, (int)H, (int)seg, y, ckpt, wp, h0, only);
   return check_launch("gdn_fwd_kernel");
+}
+
+static size_t gdn_align(size_t n) { return (n + 255) / 256 * 256; }
+
+// The chunkwise forward: 2-byte inputs, Dh = 64, L a multiple of the chunk,
+// checkpoints at multiples of half a chunk, and fewer units than four per SM.
+// Measured on B200: with few units the chunk form's shorter per-unit path wins
+// (B=8, L=4096, H=16: 1.24 ms against 1.58 per step); from about four units per SM
+// the per-step kernel (four CTAs per SM) keeps the SMs as busy and needs no second
+// pass (B=32, L=2048, H=32: 3.15 ms against 3.50).
+static bool gdn_chunked_ok(int elem_bytes, int64_t batch, int64_t L, int64_t H, int64_t Dh, int64_t seg) {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return elem_bytes == 2 && Dh == gdnc::DH && L % gdnc::Q == 0 && seg % (gdnc::Q / 2) == 0 &&
+         L <= (int64_t)INT32_MAX / 2 && batch * H < 4 * (int64_t)sms;
+}
+
+// workspace of the chunkwise forward: W as T [B,L,H,64], the GLA kernel's one
+// checkpoint [B,1,H,64,64] float32, a flag per unit; 0 when the per-step forward runs
+size_t gdn_fwd_ws_bytes(int elem_bytes, int64_t batch, int64_t L, int64_t H, int64_t Dh, int64_t seg) {
+  if (!gdn_chunked_ok(elem_bytes, batch, L, H, Dh, seg)) return 0;
+  return gdn_align((size_t)batch * L * H * Dh * elem_bytes) + gdn_align((size_t)batch * H * Dh * Dh * 4) +
+         gdn_align((size_t)batch * H * 4);
 }
 
 template <typename T>
 int gdn_fwd_launch(const void* q, const void* k, const void* v, const void* alpha, const void* beta, int64_t batch,
                    int64_t L, int64_t H, int64_t Dh, int64_t seg, float* y, float* ckpt, float* wp,
-                   const float* h0, cudaStream_t st) {
+                   const float* h0, void* ws, size_t ws_bytes, cudaStream_t st) {
   const T *q_ = (const T*)q, *k_ = (const T*)k, *v_ = (const T*)v, *a_ = (const T*)alpha, *b_ = (const T*)beta;
+  const size_t need = gdn_fwd_ws_bytes((int)sizeof(T), batch, L, H, Dh, seg);
+  if (need > 0 && ws != nullptr && ws_bytes >= need) {
+    T* wbf = (T*)ws;
+    float* gck = (float*)((char*)ws + gdn_align((size_t)batch * L * H * Dh * sizeof(T)));
+    int* flags = (int*)((char*)gck + gdn_align((size_t)batch * H * Dh * Dh * 4));
+    auto kern = h0 != nullptr ? gdn_wy_state_kernel<T, true> : gdn_wy_state_kernel<T, false>;
+    if (int rc = gdn_set_smem(kern, gdnc::SMEM)) return rc;
+    kern<<<(unsigned)(batch * H), gdnc::NT, gdnc::SMEM, st>>>(k_, v_, a_, b_, (int)L, (int)H, (int)seg, wp, wbf,
+                                                              ckpt, flags, h0);
+    if (int rc = check_launch("gdn_wy_state_kernel")) return rc;
+    // the outputs: a GLA chunk with values W (its one checkpoint is scratch)
+    const int code = sizeof(T) == 2 && std::is_same_v<T, __half> ? MR_F16 : MR_BF16;
+    if (int rc = mr_gla_fwd_h0(q, k, wbf, alpha, code, batch, L, H, Dh, L, y, gck, h0, st)) return rc;
+    // units with an alpha above 1: the per-step forward, for them only
+    return gdn_fwd_dh<T, 64>(q_, k_, v_, a_, b_, batch, L, H, seg, y, ckpt, wp, h0, st, flags);
+  }
   if (Dh == 32) return gdn_fwd_dh<T, 32>(q_, k_, v_, a_, b_, batch, L, H, seg, y, ckpt, wp, h0, st);
   return gdn_fwd_dh<T, 64>(q_, k_, v_, a_, b_, batch, L, H, seg, y, ckpt, wp, h0, st);
 }
@@ -686,7 +1091,7 @@ int gdn_step_launch(const void* q, const void* k, const void* v, const void* alp
                                   int64_t, int64_t, float*, float*, cudaStream_t);                             \
   template int gdn_fwd_launch<T>(const void*, const void*, const void*, const void*, const void*, int64_t,     \
                                  int64_t, int64_t, int64_t, int64_t, float*, float*, float*, const float*,     \
-                                 cudaStream_t);                                                               \
+                                 void*, size_t, cudaStream_t);                                                \
   template int gdn_bwd_launch<T>(const float*, const float*, const float*, const float*, const void*,          \
                                  const void*,                                                                 \
                                  const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t,    \

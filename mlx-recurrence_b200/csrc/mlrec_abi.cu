@@ -69,7 +69,8 @@ template <typename T> int rotlru_step_launch(const void*, const void*, const voi
 template <typename T> int rglru_gated_fwd_launch(const void*, const void*, const void*, const float*, float, int64_t, int64_t, int64_t, int64_t, float*, float*, const float*, cudaStream_t);
 template <typename T> int rglru_gated_bwd_launch(const float*, const float*, const float*, const void*, const void*, const void*, const float*, float, int64_t, int64_t, int64_t, int64_t, void*, void*, void*, float*, void*, const float*, float*, cudaStream_t);
 size_t rglru_gated_bwd_ws_bytes(int64_t, int64_t, int64_t, int64_t);
-template <typename T> int gdn_fwd_launch(const void*, const void*, const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, int64_t, float*, float*, float*, const float*, cudaStream_t);
+template <typename T> int gdn_fwd_launch(const void*, const void*, const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, int64_t, float*, float*, float*, const float*, void*, size_t, cudaStream_t);
+size_t gdn_fwd_ws_bytes(int, int64_t, int64_t, int64_t, int64_t, int64_t);
 template <typename T> int gdn_bwd_launch(const float*, const float*, const float*, const float*, const void*, const void*, const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, int64_t, void*, void*, void*, void*, void*, void*, const float*, float*, cudaStream_t);
 size_t gdn_bwd_ws_bytes(int64_t, int64_t, int64_t, int64_t, int64_t);
 template <typename T> int gdn_step_launch(const void*, const void*, const void*, const void*, const void*, int64_t, int64_t, int64_t, float*, float*, cudaStream_t);
@@ -146,7 +147,7 @@ using namespace mr;
 extern "C" {
 
 // 2: the _h0 (initial state) entry points; 3: the decode steps; 4: the gated RG-LRU scan
-int mr_abi_version(void) { return 6; }
+int mr_abi_version(void) { return 7; }
 
 const char* mr_last_error(void) { return g_err; }
 
@@ -377,15 +378,22 @@ static int gdn_common_checks(const char* what, int dtype, int64_t batch, int64_t
 
 int mr_gdn_fwd(const void* q, const void* k, const void* v, const void* alpha, const void* beta, int dtype,
                int64_t batch, int64_t L, int64_t H, int64_t Dh, int64_t seg, float* y, float* h_ckpt,
-               float* step_cache, const float* h0, void* stream) {
+               float* step_cache, const float* h0, void* workspace, size_t workspace_bytes, void* stream) {
   g_err[0] = 0;
   MR_TRY(gdn_common_checks("mr_gdn_fwd", dtype, batch, L, H, Dh, seg));
   MR_TRY(check_ptrs("mr_gdn_fwd", {q, k, v, alpha, beta, y, h_ckpt}));
   MR_TRY(check_opt_ptr("mr_gdn_fwd", step_cache));
   MR_TRY(check_opt_ptr("mr_gdn_fwd", h0));
+  MR_TRY(check_opt_ptr("mr_gdn_fwd", workspace));
   cudaStream_t st = (cudaStream_t)stream;
   MR_DTYPE_SWITCH(dtype, gdn_fwd_launch<T>(q, k, v, alpha, beta, batch, L, H, Dh, seg, y, h_ckpt, step_cache, h0,
-                                           st));
+                                           workspace, workspace_bytes, st));
+}
+
+size_t mr_gdn_fwd_workspace_bytes(int dtype, int64_t batch, int64_t L, int64_t H, int64_t Dh, int64_t seg) {
+  if (batch <= 0 || L <= 0 || H <= 0 || Dh <= 0 || seg <= 0) return 0;
+  if (dtype != MR_F32 && dtype != MR_BF16 && dtype != MR_F16) return 0;
+  return gdn_fwd_ws_bytes(dtype == MR_F32 ? 4 : 2, batch, L, H, Dh, seg);
 }
 
 size_t mr_gdn_bwd_workspace_bytes(int dtype, int64_t batch, int64_t L, int64_t H, int64_t Dh, int64_t seg) {

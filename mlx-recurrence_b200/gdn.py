@@ -53,13 +53,15 @@ class _GDNScan(torch.autograd.Function):
         h0_ = prep_h0(h0, (Bt, H, Dh, Dh), dev)
         y = torch.empty((Bt, L, H, Dh), dtype=torch.float32, device=dev)
         ckpt = torch.empty((Bt, L // seg, H, Dh, Dh), dtype=torch.float32, device=dev)
-        # w and p of every step, kept for the backward only when a gradient is wanted
-        cache = (torch.empty((Bt, L, H, 2, Dh), dtype=torch.float32, device=dev)
+        # w of every step, kept for the backward only when a gradient is wanted
+        cache = (torch.empty((Bt, L, H, Dh), dtype=torch.float32, device=dev)
                  if any(ctx.needs_input_grad) else None)
         with torch.cuda.device(dev):
+            nws = _lib.load().mr_gdn_fwd_workspace_bytes(code, Bt, L, H, Dh, seg)
+            ws = torch.empty(nws, dtype=torch.uint8, device=dev) if nws else None
             _lib.call("mr_gdn_fwd", _lib.ptr(q_), _lib.ptr(k_), _lib.ptr(v_), _lib.ptr(a_), _lib.ptr(b_), code,
                       Bt, L, H, Dh, seg, _lib.ptr(y), _lib.ptr(ckpt), _lib.ptr(cache), _lib.ptr(h0_),
-                      _lib.stream_of(dev))
+                      _lib.ptr(ws), nws, _lib.stream_of(dev))
         ctx.save_for_backward(q_, k_, v_, a_, b_, ckpt, cache, h0_)
         ctx.seg = seg
         return y, ckpt[:, -1].clone()

@@ -54,6 +54,9 @@ def _err(got, ref):
     (2, 256, 4, 64, 64, torch.bfloat16, True, True),
     (3, 192, 5, 32, 48, torch.bfloat16, False, False),
     (2, 128, 3, 64, 32, torch.float16, True, True),
+    # chunkwise (WY) forward: 2-byte inputs, Dh = 64, L % 128 == 0, seg % 64 == 0
+    (2, 512, 3, 64, 128, torch.bfloat16, True, True),
+    (1, 384, 2, 64, 64, torch.float16, False, False),
 ])
 def test_gdn_matches_oracle(cuda_dev, Bt, L, H, Dh, seg, dtype, with_h0, with_gf):
     mr = _mr()
@@ -176,3 +179,43 @@ def test_gdn_long_segment_backward_walks_units(cuda_dev):
         out[seg] = [t.grad for t in ts]
     for name, a, b in zip(("q", "k", "v", "alpha", "beta"), out[L], out[64]):
         assert _err(a, b.double().cpu().numpy()) <= 1e-5, name
+
+
+@pytest.mark.parametrize("case", ["strong_decay", "reset", "alpha_above_one"])
+def test_gdn_chunked_forward_edge_gates(cuda_dev, case):
+    """The chunkwise forward with strong decays (alpha down to 1e-4), exact
+    resets (alpha = 0) and, on one unit, alphas above 1 (that unit is flagged and
+    recomputed step by step), against the oracle."""
+    mr = _mr()
+    Bt, L, H, Dh = 2, 256, 2, 64
+    ins = _inputs(Bt, L, H, Dh, seed=17)
+    rng = np.random.default_rng(4)
+    if case == "strong_decay":
+        ins[3] = rng.uniform(1e-4, 0.5, (Bt, L, H))
+    elif case == "reset":
+        ins[3][:, ::37] = 0.0
+    else:
+        ins[3][1, 100:110, 0] = 1.05
+    w = rng.standard_normal((Bt, L, H, Dh))
+    ts = [torch.tensor(x, dtype=torch.float32).to(torch.bfloat16).to(cuda_dev).requires_grad_(True) for x in ins]
+    y, fin = mr.gated_deltanet_scan_with_state(*ts, seg=64)
+    (y * torch.tensor(w, dtype=torch.float32, device=cuda_dev)).sum().backward()
+    ins_r = [_rounded(x, torch.bfloat16) for x in ins]
+    y_ref, f_ref = R.gdn_forward(*ins_r)
+    grads = R.gdn_backward(*ins_r, w)
+    assert _err(y, y_ref) <= 2e-2
+    assert _err(fin, f_ref) <= 2e-2
+    for name, t, ref in zip(("q", "k", "v", "alpha", "beta"), ts, grads):
+        assert _err(t.grad, ref) <= 2e-2, name
+
+
+def test_gdn_chunked_forward_matches_per_step_forward(cuda_dev):
+    """The two forward forms on the same bf16 inputs: chunkwise (seg 64) against
+    per-step (seg 32, which the chunkwise form does not take)."""
+    mr = _mr()
+    ins = _inputs(4, 1024, 4, 64, seed=23)
+    ts = [torch.tensor(x, dtype=torch.float32).to(torch.bfloat16).to(cuda_dev) for x in ins]
+    y1, f1 = mr.gated_deltanet_scan_with_state(*ts, seg=64)
+    y2, f2 = mr.gated_deltanet_scan_with_state(*ts, seg=32)
+    assert _err(y1, y2.double().cpu().numpy()) <= 1e-2
+    assert _err(f1, f2.double().cpu().numpy()) <= 1e-2

@@ -34,7 +34,7 @@ def test_library_loads_and_exports_every_declared_symbol(mr):
     for s in _declared_symbols():
         assert hasattr(lib, s), s
         assert s in lib_mod.SIGNATURES, s
-    assert lib.mr_abi_version() == 6
+    assert lib.mr_abi_version() == 7
 
 
 def test_c_abi_shape_check_messages(mr):
