@@ -57,6 +57,7 @@ def _err(got, ref):
     # chunkwise (WY) forward: 2-byte inputs, Dh = 64, L % 128 == 0, seg % 64 == 0
     (2, 512, 3, 64, 128, torch.bfloat16, True, True),
     (1, 384, 2, 64, 64, torch.float16, False, False),
+    (2, 128, 2, 64, 128, torch.bfloat16, True, True),     # a single chunk
 ])
 def test_gdn_matches_oracle(cuda_dev, Bt, L, H, Dh, seg, dtype, with_h0, with_gf):
     mr = _mr()
