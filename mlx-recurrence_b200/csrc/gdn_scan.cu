@@ -20,8 +20,9 @@
 // row groups of a column sit in lanes 8 apart of one warp, so the reductions
 // over i that the recurrence needs each step (p, S^T q, the adjoint's d) are
 // a register dot product plus two shuffles. The backward's reductions over j
-// (grad_q = S_t go, grad_k = G w + S_{t-1} gp) go through shared memory once
-// per step.
+// (grad_q = S_t go, grad_k = G w + S_{t-1} gp) sum each warp's 8 columns through
+// a per-warp transpose buffer every step and the warps' partial sums once per
+// four-step sub-block.
 //
 // The forward also keeps w_t per step ([B,L,H,Dh] float32, the size of the
 // output), so the backward's replays need no dot products: per segment
