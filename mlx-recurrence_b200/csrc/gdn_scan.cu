@@ -451,15 +451,28 @@ gdn_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfinal, c
         const float* rk_ = b_cvt + K * DH;   // k rows
         const float* rv_ = b_cvt + 2 * K * DH;  // v rows
         const int tb = sb * K, nk = min(K, seg - tb);
+        // The next (older) sub-block's sub-checkpoint is copied from L2 into slot K-1 of
+        // this thread ahead of time: as soon as this sub-block no longer needs that slot.
+        auto prefetch_sub = [&](int sbn) {
+          const float4* src = reinterpret_cast<const float4*>(sub + (int64_t)sbn * DH * DH) + tid;
+#pragma unroll
+          for (int c = 0; c < R / 4; ++c) gdn_cp16(&slots4[((K - 1) * (R / 4) + c) * NT + tid], src + c * NT);
+          gdn_cp_commit();
+        };
         {
           float cur[R];
-          const float4* src = reinterpret_cast<const float4*>(sub + (int64_t)sb * DH * DH) + tid;
+          // this sub-block's sub-checkpoint: prefetched into slot K-1 by the previous
+          // (newer) sub-block, complete after the wait above; the newest one from L2
+          const bool pre = sb < nsb - 1;
+          const float4* src = pre ? &slots4[(K - 1) * (R / 4) * NT + tid]
+                                  : reinterpret_cast<const float4*>(sub + (int64_t)sb * DH * DH) + tid;
 #pragma unroll
           for (int c = 0; c < R / 4; ++c) {
             const float4 x = src[c * NT];
             cur[4 * c] = x.x, cur[4 * c + 1] = x.y, cur[4 * c + 2] = x.z, cur[4 * c + 3] = x.w;
             slots4[c * NT + tid] = x;
           }
+          if (sb > 0 && nk < K) prefetch_sub(sb - 1);  // slot K-1 is not used by this sub-block
 #pragma unroll 1
           for (int m = 1; m < nk; ++m) {
             float kr[R];
@@ -495,6 +508,7 @@ gdn_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfinal, c
             const float d = gdn_group_sum(gdn_dot(kr, G));
             const float gp = -a * bt * d;
             float gaP = gdn_dot(G, Sp), gbP = 0.f;
+            if (m == K - 1 && sb > 0) prefetch_sub(sb - 1);  // slot K-1 has been read (gaP uses it)
             if (g == 0) {
               gaP = fmaf(-bt * d, p, gaP);
               gbP = d * fmaf(-a, p, vj);
