@@ -260,10 +260,11 @@ MR_API int mr_rotlru_bwd_h0(const float* grad_y, const float* grad_final, const 
  * step_cache [B,L,H,Dh] float32 receives, per step, w_t = beta (v - alpha
  * S_{t-1}^T k) (NULL in the forward: not kept); the backward reads it
  * (required there) so that it replays states without the dot products.
- * With 2-byte inputs, Dh = 64, L a multiple of 128 and seg a multiple of 64 the
- * forward runs in chunkwise (WY) form when given mr_gdn_fwd_workspace_bytes of
- * device workspace (NULL or too small: the per-step form, same results within
- * the parity tolerance). The backward writes grad_q, grad_k, grad_v, grad_alpha,
+ * With 2-byte inputs, Dh = 64, L a multiple of 128, seg a multiple of 64 and
+ * fewer (batch, head) units than twice the device's SMs, the forward runs in
+ * chunkwise (WY) form when given mr_gdn_fwd_workspace_bytes of device workspace
+ * (0 bytes when it does not apply; NULL or too small: the per-step form, same
+ * results within the parity tolerance). The backward writes grad_q, grad_k, grad_v, grad_alpha,
  * grad_beta in `dtype` and needs mr_gdn_bwd_workspace_bytes of device scratch. */
 MR_API int mr_gdn_fwd(const void* q, const void* k, const void* v, const void* alpha, const void* beta, int dtype,
                       int64_t batch, int64_t L, int64_t H, int64_t Dh, int64_t seg, float* y, float* h_ckpt,

@@ -1003,16 +1003,17 @@ static int gdn_fwd_dh(const T* q, const T* k, const T* v, const T* al, const T* 
 static size_t gdn_align(size_t n) { return (n + 255) / 256 * 256; }
 
 // The chunkwise forward: 2-byte inputs, Dh = 64, L a multiple of the chunk,
-// checkpoints at multiples of half a chunk, and fewer units than four per SM.
-// Measured on B200: with few units the chunk form's shorter per-unit path wins
-// (B=8, L=4096, H=16: 1.24 ms against 1.58 per step); from about four units per SM
-// the per-step kernel (four CTAs per SM) keeps the SMs as busy and needs no second
-// pass (B=32, L=2048, H=32: 3.15 ms against 3.50).
+// checkpoints at multiples of half a chunk, and fewer units than two per SM.
+// Measured on B200 (L=2048, Dh=64, bf16; chunkwise against per step): 128 units
+// 0.63 against 0.80 ms, 256 units 0.99 against 1.03, 512 units 1.95 against 1.83,
+// 1024 units 3.50 against 3.15: with few units the chunk form's shorter per-unit
+// path wins; from about two units per SM the per-step kernel (four CTAs per SM)
+// keeps the SMs as busy and needs no second pass.
 static bool gdn_chunked_ok(int elem_bytes, int64_t batch, int64_t L, int64_t H, int64_t Dh, int64_t seg) {
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   return elem_bytes == 2 && Dh == gdnc::DH && L % gdnc::Q == 0 && seg % (gdnc::Q / 2) == 0 &&
-         L <= (int64_t)INT32_MAX / 2 && batch * H < 4 * (int64_t)sms;
+         L <= (int64_t)INT32_MAX / 2 && batch * H < 2 * (int64_t)sms;
 }
 
 // workspace of the chunkwise forward: W as T [B,L,H,64], the GLA kernel's one
