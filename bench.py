@@ -356,9 +356,59 @@ def run_ours(args):
     if e2e_ms is not None:
         e2e_ms = e2e_ms_max
     _report(args, rank, world, W, name, cfg, nb, total_ms, e2e_ms, f_ms, b_ms, h2d, d2h, peak_mb, launches, clk)
+    if args.check:
+        _check(args, rank, world, W, fn, ins, leaves, gy, cfg, nb)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def _check(args, rank, world, W, fn, ins, leaves, gy, cfg, nb):
+    """After timing: every rank's outputs and gradients gathered over the process
+    group (NCCL), the replicated parameters' gradients summed over ranks, and rank 0
+    runs the whole batch on its GPU and compares (max|diff| / max|ref|). The units
+    are independent, so the gathered results equal the 1-GPU run up to the order
+    of the cross-rank sums."""
+    import torch
+    import torch.distributed as dist
+    S = importlib.import_module("mlx-recurrence_b200.sharding")
+    B = cfg["B"]
+    for x in leaves:
+        x.grad = None
+    y = fn(*leaves)
+    torch.autograd.backward(y, gy)
+    sharded = [x.dim() > 0 and x.shape[0] == nb and x.dim() >= 3 for x in ins]
+    full_in = [S.gather_rows(x.detach(), B) if sh else x.detach() for x, sh in zip(ins, sharded)]
+    y_all = S.gather_rows(y.detach(), B)
+    gy_all = S.gather_rows(gy, B)
+    g_all = []
+    for x, sh in zip(leaves, sharded):
+        g = x.grad
+        if g is None:
+            g_all.append(None)
+        elif sh:
+            g_all.append(S.gather_rows(g, B))
+        else:  # a replicated parameter: its gradient is the sum of the ranks' partial sums
+            g = g.float().contiguous()
+            if world > 1:
+                dist.all_reduce(g)
+            g_all.append(g)
+    if rank != 0:
+        return
+    # (detach keeps a broadcast parameter's stride-0 view, so the same kernel path runs)
+    ref = [x.detach().requires_grad_(True) if x.dtype.is_floating_point else x for x in full_in]
+    y_ref = fn(*ref)
+    torch.autograd.backward(y_ref, gy_all)
+
+    def rel(a, b):
+        a, b = a.float(), b.float()
+        return float((a - b).abs().max() / (b.abs().max() + 1e-30))
+    errs = {"y": rel(y_all, y_ref)}
+    for i, (g, r) in enumerate(zip(g_all, ref)):
+        if g is not None and r.grad is not None:
+            errs[f"grad{i}"] = rel(g, r.grad)
+    print(json.dumps({"check": {"world": world, "config": args.config, "max_rel_err": max(errs.values()),
+                                "rel_err": errs}}), flush=True)
 
 
 def _e2e(args, fn, ins, gy, dev, stream, barrier, ev):
@@ -512,6 +562,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffer) timing")
+    ap.add_argument("--check", action="store_true",
+                    help="after timing, gather every rank's outputs and gradients and compare them on "
+                         "rank 0 with the whole batch run on one GPU")
     ap.add_argument("--batch", type=int, default=0,
                     help="override the config's batch (a smaller instance, e.g. for profiler captures)")
     args = ap.parse_args()

@@ -61,6 +61,8 @@ def make_inputs(name, device, seed=0, batch=None):
         cfg["B"] = batch
     g = torch.Generator(device=device).manual_seed(seed)
     f32 = dict(dtype=torch.float32, device=device, generator=g)
+    # parameters every rank shares (SSD's A, RG-LRU's Lambda) come from a fixed seed
+    rep = dict(dtype=torch.float32, device=device, generator=torch.Generator(device=device).manual_seed(4242))
     dt = cfg["dtype"]
     B, L = cfg["B"], cfg["L"]
     if cfg["kind"] == "ssd":
@@ -69,7 +71,7 @@ def make_inputs(name, device, seed=0, batch=None):
         delta = torch.randn((B, L, H), **f32).abs_().mul_(0.1).add_(0.01)
         Bm = torch.randn((B, L, H, N), **f32)
         Cm = torch.randn((B, L, H, N), **f32)
-        A = -torch.exp(torch.randn((H,), **f32) * 0.5)
+        A = -torch.exp(torch.randn((H,), **rep) * 0.5)
         A_neg = A[:, None].expand(H, N)  # one rate per head, broadcast over N
         return (u.to(dt), delta.to(dt), Bm.to(dt), Cm.to(dt), A_neg)
     if cfg["kind"] == "gla":
@@ -93,7 +95,7 @@ def make_inputs(name, device, seed=0, batch=None):
         x = torch.randn((B, L, D), **f32)
         r = torch.sigmoid(torch.randn((B, L, D), **f32))
         i = torch.sigmoid(torch.randn((B, L, D), **f32))
-        lam = torch.rand((D,), **f32) * (6.9 - 2.2) + 2.2
+        lam = torch.rand((D,), **rep) * (6.9 - 2.2) + 2.2
         if cfg["kind"] == "rglru_gated":
             return (x.to(dt), r.to(dt), i.to(dt), lam)
         a = torch.sigmoid(lam) ** (GATE_C * r)
