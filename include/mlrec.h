@@ -126,8 +126,9 @@ MR_API int mr_ssd_bwd(const float* grad_y, const float* grad_final, const float*
 
 /* Allocation-free SSD backward. No counterpart in the reference: it exists
  * for callers that cannot allocate device memory when the backward runs
- * (inside a graph capture or an allocator callback, or embedders that only
- * hand over pre-placed tensors). Same arguments and results as mr_ssd_bwd
+ * (code inside an allocator's callback, where allocating would re-enter the
+ * allocator, or embedders that own all device memory and only hand over
+ * pre-placed buffers). Same arguments and results as mr_ssd_bwd
  * without the workspace; covers the tensor-core path only (bf16/f16, Dh=64,
  * N=128, a_stride_n == 0, seg == 128, L % 128 == 0; else MR_E_SHAPE). Its
  * scratch is a built-in 256 KiB device array per GPU (batch*H <= 65,536,

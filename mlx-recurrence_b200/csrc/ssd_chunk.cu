@@ -1442,9 +1442,10 @@ template int gla_chunk_bwd_launch<__half>(const float*, const float*, const floa
 // ===========================================================================
 //
 // Some callers cannot allocate device memory at the moment they run the
-// backward: code running inside a CUDA-graph capture or a custom allocator's
-// callback, embedders that hand the library only pre-placed tensors, or
-// runtimes that forbid allocation on their hot path. For them this entry point
+// backward: code running inside a custom allocator's callback (allocating there
+// would re-enter the allocator), embedders that hand the library only
+// pre-placed buffers and own all device memory themselves, or runtimes that
+// forbid allocation on their hot path. For them this entry point
 // takes no workspace. Its only scratch - one float per (batch row, head), the
 // per-head partial derivatives for A - lives in the file-scope device array
 // below, which every GPU that loads the library holds until the process exits.
@@ -1457,7 +1458,7 @@ template int gla_chunk_bwd_launch<__half>(const float*, const float*, const floa
 //     before any stream capture on the device.
 //   - Every call on a device shares the array. Each call writes every entry it
 //     later reads, so nothing needs clearing between calls, but calls that
-//     overlap on the GPU (different streams, or concurrent graphs) race.
+//     overlap on the GPU (for example on different streams) race.
 
 constexpr int64_t kNoAllocMaxUnits = 65536;
 static __device__ __align__(256) float g_noalloc_scratch[kNoAllocMaxUnits];

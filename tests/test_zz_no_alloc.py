@@ -1,8 +1,9 @@
 """The allocation-free SSD backward (mr_ssd_bwd_noalloc).
 
 It serves callers that cannot allocate device memory while the backward runs
-(graph captures, allocator callbacks, embedders handing over only pre-placed
-tensors): instead of a caller-provided workspace it uses a built-in device
+(code inside an allocator's callback, where allocating would re-enter the
+allocator, or embedders that own all device memory and hand over only
+pre-placed buffers): instead of a caller-provided workspace it uses a built-in device
 array. The GPU test calls it through the C-ABI twice in a row and checks each
 result against the workspace-taking mr_ssd_bwd on the same inputs. This file
 is collected last so that a failure here comes after every other test ran.
