@@ -1,9 +1,9 @@
 """Generate golden vectors by running the reference's own Python code.
 
-Run in a container that has the reference checkout (read-only) at
-``--ref`` (default ``/root/reference``)::
+Run where a checkout of the reference is available (it is only read),
+passing its root directory::
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py --ref <reference checkout>
 
 MLX is not installable here, so ``tests/golden/_mlx_standin`` supplies a
 torch-float64 stand-in for the ``mlx.core`` primitives. With it, this script
@@ -110,7 +110,7 @@ def _exec_body(fn, ns, drop_if_mentions=()):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", required=True, help="root directory of the reference checkout")
     args = ap.parse_args()
 
     sys.path.insert(0, os.path.join(HERE, "_mlx_standin"))
