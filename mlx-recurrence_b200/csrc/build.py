@@ -1,6 +1,6 @@
 """Build libmlrec.so (the C-ABI scan library) for sm_100a, in-tree.
 
-    python mlx-recurrence_b200/csrc/build.py [--force] [--debug]
+    python mlx-recurrence_b200/csrc/build.py [--force] [-v]
 
 Each ``.cu`` file under this directory is compiled by nvcc for
 ``arch=compute_100a,code=sm_100a`` (with ``-lineinfo``) into ``_build/``,
@@ -33,11 +33,9 @@ def _nvcc():
     raise RuntimeError("nvcc not found (set NVCC=...)")
 
 
-def _flags(debug):
+def _flags():
     f = ["-std=c++17", "-O3", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
          "--expt-relaxed-constexpr", "-I", os.path.join(ROOT, "include"), "-I", HERE]
-    if debug:
-        f += ["-DMR_DEBUG=1"]
     return ARCH + f
 
 
@@ -45,12 +43,12 @@ def _headers():
     return glob.glob(os.path.join(HERE, "*.cuh")) + glob.glob(os.path.join(ROOT, "include", "*.h"))
 
 
-def build(force=False, debug=False, verbose=False, jobs=None):
+def build(force=False, verbose=False, jobs=None):
     srcs = sorted(glob.glob(os.path.join(HERE, "*.cu")))
     os.makedirs(BUILD, exist_ok=True)
     nvcc = _nvcc()
     hdr_mtime = max([os.path.getmtime(h) for h in _headers()] + [0])
-    flags = _flags(debug)
+    flags = _flags()
 
     def obj_of(s):
         return os.path.join(BUILD, os.path.basename(s)[:-3] + ".o")
@@ -84,8 +82,7 @@ def build(force=False, debug=False, verbose=False, jobs=None):
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
-    ap.add_argument("--debug", action="store_true")
     ap.add_argument("-v", "--verbose", action="store_true")
     a = ap.parse_args()
-    print(build(force=a.force, debug=a.debug, verbose=a.verbose))
+    print(build(force=a.force, verbose=a.verbose))
     sys.exit(0)
