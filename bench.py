@@ -401,7 +401,7 @@ def _check(args, rank, world, W, fn, ins, leaves, gy, cfg, nb):
     torch.autograd.backward(y_ref, gy_all)
 
     def rel(a, b):
-        a, b = a.float(), b.float()
+        a, b = a.detach().float(), b.detach().float()
         return float((a - b).abs().max() / (b.abs().max() + 1e-30))
     errs = {"y": rel(y_all, y_ref)}
     for i, (g, r) in enumerate(zip(g_all, ref)):
