@@ -854,9 +854,11 @@ gdn_wy_state_kernel(const T* __restrict__ k, const T* __restrict__ v, const T* _
         }
         __syncthreads();
       }
-      // (d3) W_b = T_b R_b: one row and 4 columns per thread
+      // (d3) W_b = T_b R_b: one row and 4 columns per thread. The 16 threads of a
+      // column group (the only ones that read and write the same words) form one
+      // half-warp, so a warp barrier orders their reads of R_b before the writes.
       {
-        const int rr = tid / 16, j4 = 4 * (tid % 16);
+        const int rr = tid % 16, j4 = 4 * (tid / 16);
         const float* Tr = sT + (blk * BLK + rr) * TS2;
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
@@ -866,7 +868,7 @@ gdn_wy_state_kernel(const T* __restrict__ k, const T* __restrict__ v, const T* _
           acc.x = fmaf(t, x.x, acc.x), acc.y = fmaf(t, x.y, acc.y), acc.z = fmaf(t, x.z, acc.z),
           acc.w = fmaf(t, x.w, acc.w);
         }
-        __syncthreads();  // every thread has read the block's R before it becomes W
+        __syncwarp();  // the half-warp has read its columns of R_b before they become W_b
         *reinterpret_cast<float4*>(sW + (rb + rr) * KS + j4) = acc;
       }
       // the next block's panel (d1) reads only K; its update (d2) reads this W after d1's barrier
