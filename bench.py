@@ -5,18 +5,21 @@
 A step is one forward and one backward pass of the configured scan through
 the public API (torch.autograd over libmlrec.so) on one batch of synthetic
 inputs. The default workload is config c4 (SSD, bf16, B=32, L=16384, H=32,
-Dh=64, N=128, seg=32), the configuration the scaling target is quoted on.
-Under torchrun (N > 1) every rank takes a contiguous batch range of the same
-global problem (strong scaling, no collective on the data path); the timed
-region is bracketed by a barrier and device synchronisation and the reported
-time is the maximum over ranks.
+Dh=64, N=128, seg=32), the configuration the scaling target is quoted on; the
+default run also measures the GLA shape of the same target (c5) with the same
+steps and warm-up and reports it under "extra". Under torchrun (N > 1) every
+rank takes a block of the same global problem - a range of batch rows, and of
+heads (channels) when N does not divide the batch - with no collective on the
+data path (strong scaling); the timed region is bracketed by a barrier and
+device synchronisation and the reported time is the maximum over ranks.
 
 Printed (rank 0, one JSON line): value = whole-job tokens/s with inputs
-resident in HBM; e2e = the same step with host->device copies of the inputs
-from pinned memory and a device->host read of the result inside the timed
-region; roofline of the dominant kernel (algorithmic bytes / CUDA-event time);
-cpu_baseline = the float32 C restatement of the reference algorithm
-(oracle/ckpt_scan.c) on a bounded sample; clocks sampled during timing.
+resident in HBM; e2e = the same step with host->device copies of every input
+(and the upstream gradient) from pinned memory and device->host copies of y
+and every input gradient into pinned memory inside the timed region; roofline
+of the dominant kernel (algorithmic bytes / CUDA-event time); cpu_baseline =
+the float32 C restatement of the reference algorithm (oracle/ckpt_scan.c) on
+a bounded sample (median of three runs); clocks sampled during timing.
 
 ``--impl reference`` times that CPU restatement on this host's cores (the
 reference itself is MLX/Metal and cannot run here) on the same metric.
@@ -238,7 +241,7 @@ def _cpu_run(c_oracle, W, cfg, ins, gy):
     return c_oracle.run(cfg["kind"], ins, cfg["seg"], gy=gy)
 
 
-def cpu_baseline(name, reps=1):
+def cpu_baseline(name, reps=3):
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import c_oracle  # float32 C restatement (test infrastructure)
     W = importlib.import_module("mlx-recurrence_b200.workloads")
@@ -263,13 +266,10 @@ def cpu_baseline(name, reps=1):
 # GPU arm
 # --------------------------------------------------------------------------- #
 
-def run_ours(args):
+def _setup():
     import torch
     import torch.distributed as dist
 
-    pkg = importlib.import_module("mlx-recurrence_b200")
-    W = importlib.import_module("mlx-recurrence_b200.workloads")
-    lib = importlib.import_module("mlx-recurrence_b200._lib").load()
     rank, world = _env_int("RANK", 0), _env_int("WORLD_SIZE", 1)
     local = _env_int("LOCAL_RANK", 0)
     dev = torch.device("cuda", local)
@@ -282,45 +282,50 @@ def run_ours(args):
         if world > 1:
             dist.barrier()
 
-    name = args.config
+    return dict(pkg=importlib.import_module("mlx-recurrence_b200"),
+                W=importlib.import_module("mlx-recurrence_b200.workloads"),
+                lib=importlib.import_module("mlx-recurrence_b200._lib").load(),
+                rank=rank, world=world, dev=dev, stream=torch.cuda.current_stream(dev), barrier=barrier)
+
+
+def _prepare(ctx, name, batch=0):
+    """The rank's block of config ``name``: inputs, upstream gradient, leaves."""
+    import torch
+    W = ctx["W"]
     cfg = dict(W.CONFIGS[name])
-    if args.batch:
-        cfg["B"] = args.batch
-    b0, b1 = W.shard_batch(cfg["B"], rank, world)
-    nb = b1 - b0
-    ins = W.make_inputs(name, dev, seed=1000 + rank, batch=nb)
-    gen = torch.Generator(device=dev).manual_seed(2000 + rank)
-    gy = torch.randn(W.output_shape(name, nb), generator=gen, device=dev, dtype=torch.float32)
-    fn = W.scan_fn(pkg, name)
+    if batch:
+        cfg["B"] = batch
+    blk = W.rank_block(name, ctx["rank"], ctx["world"], batch=cfg["B"])
+    lcfg = W.local_config(name, blk)
+    ins = W.make_inputs(name, ctx["dev"], seed=1000 + ctx["rank"], block=blk)
+    gen = torch.Generator(device=ctx["dev"]).manual_seed(2000 + ctx["rank"])
+    gy = torch.randn(W.output_shape(name, block=blk), generator=gen, device=ctx["dev"], dtype=torch.float32)
     leaves = [t.detach().requires_grad_(True) if t.dtype.is_floating_point else t for t in ins]
-    # A_neg as an expanded view: differentiate w.r.t. its base
-    stream = torch.cuda.current_stream(dev)
+    return dict(name=name, cfg=cfg, lcfg=lcfg, blk=blk, ins=ins, gy=gy, leaves=leaves,
+                fn=W.scan_fn(ctx["pkg"], name))
 
-    def step(xs, g):
-        y = fn(*xs)
-        torch.autograd.backward(y, g)
-        return y
 
+def _time_steps(ctx, P, steps, warmup):
+    """W untimed warm-up steps, then K timed forward+backward steps bracketed by
+    a barrier and device synchronisation, with CUDA events on the launching
+    stream and clocks sampled meanwhile."""
+    import torch
+    fn, leaves, gy, stream, lib = P["fn"], P["leaves"], P["gy"], ctx["stream"], ctx["lib"]
     ev = lambda: torch.cuda.Event(enable_timing=True)
-
-    # ---- warm-up
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         for x in leaves:
             x.grad = None
-        step(leaves, gy)
+        torch.autograd.backward(fn(*leaves), gy)
     torch.cuda.synchronize()
-
-    # ---- timed: inputs resident in HBM
-    fwd_ms, bwd_ms = [], []
     n_launch0 = lib.mr_launch_count()
-    torch.cuda.reset_peak_memory_stats(dev)
-    barrier()
+    torch.cuda.reset_peak_memory_stats(ctx["dev"])
+    ctx["barrier"]()
     torch.cuda.synchronize()
-    with ClockSampler(_gpu_uuid(dev)) as clk:
+    with ClockSampler(_gpu_uuid(ctx["dev"])) as clk:
         e_start, e_end = ev(), ev()
         e_start.record(stream)
         marks = []
-        for _ in range(args.steps):
+        for _ in range(steps):
             for x in leaves:
                 x.grad = None
             a, b, c = ev(), ev(), ev()
@@ -333,69 +338,99 @@ def run_ours(args):
             del y
         e_end.record(stream)
         torch.cuda.synchronize()
-        barrier()
-    launches = lib.mr_launch_count() - n_launch0
-    total_ms = e_start.elapsed_time(e_end)
-    for a, b, c in marks:
-        fwd_ms.append(a.elapsed_time(b))
-        bwd_ms.append(b.elapsed_time(c))
-    peak_mb = torch.cuda.max_memory_allocated(dev) / 2 ** 20
+        ctx["barrier"]()
+    return dict(total_ms=e_start.elapsed_time(e_end),
+                f_ms=statistics.mean(a.elapsed_time(b) for a, b, _ in marks),
+                b_ms=statistics.mean(b.elapsed_time(c) for _, b, c in marks),
+                launches=lib.mr_launch_count() - n_launch0,
+                peak_mb=torch.cuda.max_memory_allocated(ctx["dev"]) / 2 ** 20, clk=clk)
 
-    # ---- timed: end to end from pinned host memory
-    e2e_ms = None
-    h2d = d2h = 0
-    if not args.no_e2e:
-        e2e_ms, h2d, d2h = _e2e(args, fn, ins, gy, dev, stream, barrier, ev)
 
-    # ---- max over ranks
-    t = torch.tensor([total_ms, e2e_ms or 0.0, statistics.mean(fwd_ms), statistics.mean(bwd_ms)],
-                     dtype=torch.float64, device=dev)
-    if world > 1:
+def _max_over_ranks(ctx, vals):
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor(vals, dtype=torch.float64, device=ctx["dev"])
+    if ctx["world"] > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    total_ms, e2e_ms_max, f_ms, b_ms = t.tolist()
-    if e2e_ms is not None:
-        e2e_ms = e2e_ms_max
-    _report(args, rank, world, W, name, cfg, nb, total_ms, e2e_ms, f_ms, b_ms, h2d, d2h, peak_mb, launches, clk)
+    return t.tolist()
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    ctx = _setup()
+    P = _prepare(ctx, args.config, args.batch)
+    M = _time_steps(ctx, P, args.steps, args.warmup)
+    e2e_ms, h2d, d2h = None, 0, 0
+    if not args.no_e2e:
+        e2e_ms, h2d, d2h = _e2e(args, P["fn"], P["ins"], P["gy"], ctx["dev"], ctx["stream"], ctx["barrier"],
+                                lambda: torch.cuda.Event(enable_timing=True))
+    mx = _max_over_ranks(ctx, [M["total_ms"], e2e_ms or 0.0, M["f_ms"], M["b_ms"]])
+    M["total_ms"], M["f_ms"], M["b_ms"] = mx[0], mx[2], mx[3]
+    e2e_ms = mx[1] if e2e_ms is not None else None
     if args.check:
-        _check(args, rank, world, W, fn, ins, leaves, gy, cfg, nb)
-    if world > 1:
+        _check(args, ctx, P)
+    meta = {k: P[k] for k in ("name", "cfg", "lcfg")}
+    extra = {}
+    if args.config == "c4" and not args.no_extra:
+        # the GLA half of the target shape (B=32, L=16384, H=32, Dh=64), same steps and warm-up
+        del P
+        torch.cuda.empty_cache()
+        P5 = _prepare(ctx, "c5", args.batch)
+        M5 = _time_steps(ctx, P5, args.steps, args.warmup)
+        M5["total_ms"], M5["f_ms"], M5["b_ms"] = _max_over_ranks(ctx, [M5["total_ms"], M5["f_ms"], M5["b_ms"]])
+        extra["c5"] = ({k: P5[k] for k in ("name", "cfg", "lcfg")}, M5)
+        del P5
+    if ctx["rank"] == 0:
+        out = _report(args, ctx, meta, M, e2e_ms, h2d, d2h)
+        if extra:
+            out["extra"] = {k: _metrics(args, ctx, Pk, Mk) for k, (Pk, Mk) in extra.items()}
+        if ctx["world"] == 1 and not args.no_cpu_baseline:
+            out["cpu_baseline"] = cpu_baseline(args.config)
+        print(json.dumps(out), flush=True)
+    if ctx["world"] > 1:
         dist.barrier()
         dist.destroy_process_group()
 
 
-def _check(args, rank, world, W, fn, ins, leaves, gy, cfg, nb):
+def _check(args, ctx, P):
     """After timing: every rank's outputs and gradients gathered over the process
-    group (NCCL), the replicated parameters' gradients summed over ranks, and rank 0
-    runs the whole batch on its GPU and compares (max|diff| / max|ref|). The units
-    are independent, so the gathered results equal the 1-GPU run up to the order
-    of the cross-rank sums."""
+    group (NCCL), the shared parameters' gradients summed over ranks, and rank 0
+    runs the whole problem on its GPU and compares (max|diff| / max|ref|). The
+    units are independent, so the gathered results equal the 1-GPU run up to the
+    order of the cross-rank sums."""
     import torch
-    import torch.distributed as dist
     S = importlib.import_module("mlx-recurrence_b200.sharding")
-    B = cfg["B"]
+    W = ctx["W"]
+    fn, ins, leaves, gy, cfg = P["fn"], P["ins"], P["leaves"], P["gy"], P["cfg"]
+    ax, q = W.UNIT_AXIS[cfg["kind"]]
+    B, U = cfg["B"], cfg[ax]
     for x in leaves:
         x.grad = None
     y = fn(*leaves)
     torch.autograd.backward(y, gy)
-    sharded = [x.dim() > 0 and x.shape[0] == nb and x.dim() >= 3 for x in ins]
-    full_in = [S.gather_rows(x.detach(), B) if sh else x.detach() for x, sh in zip(ins, sharded)]
-    y_all = S.gather_rows(y.detach(), B)
-    gy_all = S.gather_rows(gy, B)
+    blocked = lambda x: x.dim() >= 3  # [B, L, units (x values), ...]; lower ranks: per-unit parameters
+
+    def gather_param(x):  # a per-unit parameter, re-expanded like the caller's view
+        if x.dim() == 2 and x.stride(1) == 0:
+            return _gather_param(S, x[:, :1].detach(), B, U, q).expand(U, x.shape[1])
+        return _gather_param(S, x.detach(), B, U, q)
+
+    full_in = [S.gather_blocks(x.detach(), B, U, q) if blocked(x) else gather_param(x) for x in ins]
+    y_all = S.gather_blocks(y.detach(), B, U, q)
+    gy_all = S.gather_blocks(gy, B, U, q)
     g_all = []
-    for x, sh in zip(leaves, sharded):
+    for x in leaves:
         g = x.grad
         if g is None:
             g_all.append(None)
-        elif sh:
-            g_all.append(S.gather_rows(g, B))
-        else:  # a replicated parameter: its gradient is the sum of the ranks' partial sums
-            g = g.float().contiguous()
-            if world > 1:
-                dist.all_reduce(g)
-            g_all.append(g)
-    if rank != 0:
+        elif blocked(x):
+            g_all.append(S.gather_blocks(g, B, U, q))
+        else:  # a shared parameter: the sum of the ranks' partial sums
+            g_all.append(S.sum_unit_param(g.contiguous(), B, U, q))
+    if ctx["rank"] != 0:
         return
-    # (detach keeps a broadcast parameter's stride-0 view, so the same kernel path runs)
+    # (a broadcast parameter keeps its stride-0 view, so the same kernel path runs)
     ref = [x.detach().requires_grad_(True) if x.dtype.is_floating_point else x for x in full_in]
     y_ref = fn(*ref)
     torch.autograd.backward(y_ref, gy_all)
@@ -407,14 +442,33 @@ def _check(args, rank, world, W, fn, ins, leaves, gy, cfg, nb):
     for i, (g, r) in enumerate(zip(g_all, ref)):
         if g is not None and r.grad is not None:
             errs[f"grad{i}"] = rel(g, r.grad)
-    print(json.dumps({"check": {"world": world, "config": args.config, "max_rel_err": max(errs.values()),
+    print(json.dumps({"check": {"world": ctx["world"], "config": args.config, "max_rel_err": max(errs.values()),
                                 "rel_err": errs}}), flush=True)
+
+
+def _gather_param(S, x, B, U, q):
+    """A per-unit parameter slice [u0:u1, ...] of every rank assembled into [U, ...]
+    (ranks sharing a unit range hold the same values)."""
+    import torch
+    import torch.distributed as dist
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return x
+    _, _, u0, u1 = S.block_of(B, U, dist.get_rank(), dist.get_world_size(), q)
+    full = torch.zeros((U,) + tuple(x.shape[1:]), dtype=torch.float64, device=x.device)
+    cnt = torch.zeros((U,), dtype=torch.float64, device=x.device)
+    full[u0:u1] = x.double()
+    cnt[u0:u1] = 1
+    dist.all_reduce(full)
+    dist.all_reduce(cnt)
+    return (full / cnt.view((U,) + (1,) * (x.dim() - 1))).to(x.dtype).contiguous()
 
 
 def _e2e(args, fn, ins, gy, dev, stream, barrier, ev):
     """Same step through the public API with host buffers: per step, H2D copies
-    of every input from pinned memory, forward+backward, D2H of the last
-    step's outputs. Returns (ms for all steps, H2D bytes/step, D2H bytes/step)."""
+    of every input and of the upstream gradient from pinned memory,
+    forward+backward, and D2H copies into pinned memory of the step's output
+    y and of every input gradient (what a caller holding host buffers reads
+    back). Returns (ms for all steps, H2D bytes/step, D2H bytes/step)."""
     import torch
     # A tensor broadcast along its last axis (SSD's per-head A_neg) travels as
     # its [.., 1] base and is re-expanded on the device, as a caller would.
@@ -430,83 +484,122 @@ def _e2e(args, fn, ins, gy, dev, stream, barrier, ev):
     host_gy = gy.to("cpu").pin_memory()
     dev_ins = [torch.empty_like(h, device=dev) for h in host_ins]
     dev_gy = torch.empty_like(gy)
-    with torch.no_grad():
-        y_probe = fn(*(t.detach() for t in ins))  # only for the result's shape and dtype
-    res_host = torch.empty(y_probe[:, -1].shape, dtype=y_probe.dtype, pin_memory=True)
-    del y_probe
-    h2d = sum(t.numel() * t.element_size() for t in host_ins) + host_gy.numel() * 4
-    d2h = res_host.numel() * res_host.element_size()
-    with torch.no_grad():
-        for _ in range(2):  # warm the copy path
+
+    def one_step(host_out):
+        with torch.no_grad():
             for d, h in zip(dev_ins, host_ins):
                 d.copy_(h, non_blocking=True)
+            dev_gy.copy_(host_gy, non_blocking=True)
+        leaves, xs = [], []
+        for d, s in zip(dev_ins, shapes):
+            x = d.detach().requires_grad_(True)
+            leaves.append(x)
+            xs.append(x.expand(s) if s is not None else x)
+        y = fn(*xs)
+        torch.autograd.backward(y, dev_gy)
+        outs = [y.detach()] + [x.grad for x in leaves]
+        if host_out is None:  # untimed first call: the result buffers' shapes
+            return [torch.empty(o.shape, dtype=o.dtype, pin_memory=True) for o in outs]
+        with torch.no_grad():
+            for h, o in zip(host_out, outs):
+                h.copy_(o, non_blocking=True)
+        return host_out
+
+    host_out = one_step(None)
+    for _ in range(2):  # warm the copy paths
+        one_step(host_out)
+    h2d = sum(t.numel() * t.element_size() for t in host_ins) + host_gy.numel() * host_gy.element_size()
+    d2h = sum(t.numel() * t.element_size() for t in host_out)
     torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
     e2e_s, e2e_e = ev(), ev()
     e2e_s.record(stream)
     for _ in range(args.steps):
-        with torch.no_grad():
-            for d, h in zip(dev_ins, host_ins):
-                d.copy_(h, non_blocking=True)
-            dev_gy.copy_(host_gy, non_blocking=True)
-        xs = []
-        for d, s in zip(dev_ins, shapes):
-            x = d.detach().requires_grad_(True)
-            xs.append(x.expand(s) if s is not None else x)
-        y = fn(*xs)
-        torch.autograd.backward(y, dev_gy)
-        res_host.copy_(y[:, -1].detach(), non_blocking=True)
-        del y
+        one_step(host_out)
     e2e_e.record(stream)
     torch.cuda.synchronize()
     barrier()
     return e2e_s.elapsed_time(e2e_e), h2d, d2h
 
 
-def _report(args, rank, world, W, name, cfg, nb, total_ms, e2e_ms, f_ms, b_ms, h2d, d2h, peak_mb, launches, clk):
-    if rank == 0:
-        hbm, tc, peak_kind = _peaks()
-        tok = W.tokens(cfg)  # whole job: all ranks together process the config
-        fb, bb = algorithmic_bytes(cfg, nb)
-        dom = ("backward", bb, b_ms) if b_ms >= f_ms else ("forward", fb, f_ms)
-        achieved = dom[1] / (dom[2] * 1e-3) / 1e9
-        out = {
-            "metric": "tokens/s fwd+bwd",
-            "value": tok * args.steps / (total_ms * 1e-3),
-            "unit": "tokens/s",
-            "n_gpus": world,
-            "steps": args.steps,
-            "warmup": args.warmup,
-            "ms_per_step": total_ms / args.steps,
-            "higher_is_better": True,
-            "scaling": "strong",
-            "vs_baseline": None,
-            "dtype": {4: "f32", 2: "bf16"}[cfg["dtype"].itemsize] + " inputs, f32 state",
-            "data": "synthetic (seeded, BASELINE config distributions)",
-            "config": {"workload": W.DESCRIPTION[name], "name": name, "global_batch": cfg["B"],
-                       "seq_len": cfg["L"], "parallelism": f"batch-shard x{world}",
-                       "l2": "inputs larger than L2" if fb > 126e6 else "inputs smaller than L2 (no flush)"},
-            "fwd_ms": f_ms,
-            "bwd_ms": b_ms,
-            "fwd_tokens_per_s": tok / (f_ms * 1e-3),
-            "peak_mb": peak_mb,
-            "e2e": None if e2e_ms is None else {
-                "value": tok * args.steps / (e2e_ms * 1e-3), "unit": "tokens/s",
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-            "roofline": {"bound": "hbm", "kernel": f"{cfg['kind']} {dom[0]}",
-                         "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                         "frac": achieved / hbm, "traffic": _traffic(name, dom[0], nb, cfg),
-                         "algorithmic_bytes_per_launch": dom[1],
-                         "peak_source": f"{peak_kind} hbm_gbs"},
-            **({"note": "per-step delta-rule recurrence: bound by FP32 issue and per-step latency on the "
-                        "CUDA cores, not by HBM"} if cfg["kind"] == "gdn" else {}),
-            "gpu_launches": int(launches),
-            "clocks": clk.summary(),
-        }
-        if world == 1 and not args.no_cpu_baseline:
-            out["cpu_baseline"] = cpu_baseline(name)
-        print(json.dumps(out), flush=True)
+def _ckpt_spacing(ctx, cfg):
+    """Checkpoint spacing the plug-in wrappers use for this config (the fastest
+    path's; the final state is the same for any spacing)."""
+    L = importlib.import_module("mlx-recurrence_b200._lib")
+    code = L.DTYPE_CODE[cfg["dtype"]]
+    if cfg["kind"] == "ssd":  # one rate per head: the stride-0 view along N
+        return int(ctx["lib"].mr_ssd_preferred_seg(code, cfg["L"], cfg["Dh"], cfg["N"], cfg["seg"], 0))
+    if cfg["kind"] == "gla":
+        return int(ctx["lib"].mr_gla_preferred_seg(code, cfg["L"], cfg["Dh"], cfg["seg"]))
+    return cfg["seg"]
+
+
+def _metrics(args, ctx, P, M):
+    """Throughput, per-phase times and the dominant kernel's roofline."""
+    W = ctx["W"]
+    name, cfg, lcfg = P["name"], P["cfg"], P["lcfg"]
+    hbm, tc, peak_kind = _peaks()
+    tok = W.tokens(cfg)  # whole job: all ranks together process the config
+    fb, bb = algorithmic_bytes(lcfg, lcfg["B"])
+    f_ms, b_ms = M["f_ms"], M["b_ms"]
+    dom = ("backward", bb, b_ms) if b_ms >= f_ms else ("forward", fb, f_ms)
+    achieved = dom[1] / (dom[2] * 1e-3) / 1e9
+    ax, _ = W.UNIT_AXIS[cfg["kind"]]
+    traffic = _traffic(name, dom[0], lcfg["B"] * lcfg[ax] / cfg[ax], cfg)
+    wb, wu = importlib.import_module("mlx-recurrence_b200.sharding").rank_grid(
+        cfg["B"], cfg[ax], ctx["world"], W.UNIT_AXIS[cfg["kind"]][1])
+    unit = {"H": "head", "D": "channel", "Dp": "pair"}[ax]
+    return {
+        "value": tok * args.steps / (M["total_ms"] * 1e-3),
+        "unit": "tokens/s",
+        "ms_per_step": M["total_ms"] / args.steps,
+        "config": {"workload": W.DESCRIPTION[name], "name": name, "global_batch": cfg["B"], "seq_len": cfg["L"],
+                   "ckpt_spacing": _ckpt_spacing(ctx, cfg),
+                   "parallelism": f"{wb} batch x {wu} {unit} blocks over {ctx['world']} GPU(s), no collective",
+                   "l2": "inputs larger than L2" if fb > 126e6 else "inputs smaller than L2 (no flush)"},
+        "fwd_ms": f_ms,
+        "bwd_ms": b_ms,
+        "fwd_tokens_per_s": tok / (f_ms * 1e-3),
+        "peak_mb": M["peak_mb"],
+        "roofline": {"bound": "hbm", "kernel": f"{cfg['kind']} {dom[0]}",
+                     "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                     "frac": achieved / hbm, "traffic": traffic,
+                     "algorithmic_bytes_per_launch": dom[1],
+                     "peak_source": f"{peak_kind} hbm_gbs"},
+        **({"note": "per-step delta-rule recurrence: bound by FP32 issue and per-step latency on the "
+                    "CUDA cores, not by HBM"} if cfg["kind"] == "gdn" else {}),
+        "gpu_launches": int(M["launches"]),
+        "clocks": M["clk"].summary(),
+    }
+
+
+def _report(args, ctx, P, M, e2e_ms, h2d, d2h):
+    cfg = P["cfg"]
+    m = _metrics(args, ctx, P, M)
+    tok = ctx["W"].tokens(cfg)
+    out = {
+        "metric": "tokens/s fwd+bwd",
+        "value": m.pop("value"),
+        "unit": m.pop("unit"),
+        "n_gpus": ctx["world"],
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": m.pop("ms_per_step"),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": {4: "f32", 2: "bf16"}[cfg["dtype"].itemsize] + " inputs, f32 state",
+        "data": "synthetic (seeded, BASELINE config distributions)",
+        "config": m.pop("config"),
+        "e2e": None if e2e_ms is None else {
+            "value": tok * args.steps / (e2e_ms * 1e-3), "unit": "tokens/s",
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "copies": "H2D of every input and grad_y from pinned memory; D2H of y and every input gradient "
+                      "into pinned memory; inside the timed region"},
+    }
+    out.update(m)
+    return out
 
 
 def run_reference(args):
@@ -562,6 +655,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffer) timing")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="with the default c4, skip the extra GLA (c5) measurement at the same shape")
     ap.add_argument("--check", action="store_true",
                     help="after timing, gather every rank's outputs and gradients and compare them on "
                          "rank 0 with the whole batch run on one GPU")

@@ -32,7 +32,7 @@
  *     segment, in the reference's layouts; the last one is the final state.
  *   - `grad_final` (nullable) is the cotangent of the final state. The
  *     reference's VJPs drop it (ssd.py:334, gla.py:293, rglru.py:226,
- *     rotlru.py:571); here it seeds the adjoint, matching the reference's
+ *     rotlru.py:288); here it seeds the adjoint, matching the reference's
  *     pure per-step loops.
  */
 #ifndef MLREC_H_
@@ -75,8 +75,20 @@ MR_API uint64_t mr_launch_count(void);
 /* Device-side error word of the current device's kernels: 0 = none,
  * 1 = a bounded wait on an asynchronous copy timed out (results invalid),
  * -1 = the word could not be read. Synchronises with the device; clear != 0
- * resets the word. For diagnostics and tests. */
+ * resets the word. While the word is set, every later wait that does not
+ * complete at once gives up immediately (so a kernel whose copies stopped
+ * arriving ends in about one 2 s limit), and results stay void until the
+ * word is cleared. For diagnostics and tests. */
 MR_API int mr_device_error_status(int clear);
+
+/* Diagnostic (no reference counterpart): `ctas` CTAs each wait on a shared-memory
+ * barrier that nothing completes, first with a `limit_ns` time limit, then with
+ * the kernels' standard 2 s limit, and write both waits' durations (ns) to
+ * elapsed_ns[2*cta], elapsed_ns[2*cta + 1] (device memory, uint64). The first
+ * wait to run out sets the device error word; every wait after it gives up at
+ * once. Checks the bounded-wait path without a fault: the context stays
+ * usable, and mr_device_error_status(1) reads and clears the word. */
+MR_API int mr_selftest_wait_timeout(int ctas, uint64_t limit_ns, uint64_t* elapsed_ns, void* stream);
 
 /* Diagnostic (no reference counterpart): one 128x128x128 bf16 tcgen05 tile
  * per shared-memory operand form the chunked kernels use. A, Bk, Amn are
@@ -132,8 +144,10 @@ MR_API int mr_ssd_bwd(const float* grad_y, const float* grad_final, const float*
  * without the workspace; covers the tensor-core path only (bf16/f16, Dh=64,
  * N=128, a_stride_n == 0, seg == 128, L % 128 == 0; else MR_E_SHAPE). Its
  * scratch is a built-in 256 KiB device array per GPU (batch*H <= 65,536,
- * else MR_E_WORKSPACE). The first call on a device looks up that array's
- * address (make it before any stream capture); all calls on a device share
+ * else MR_E_WORKSPACE). The first call in each CUDA context (the device's
+ * primary context, or one the caller created and made current) looks up that
+ * array's address in the context and caches it by the context's unique id
+ * (make that call before any stream capture); all calls on a device share
  * the array, so calls that overlap on the GPU race. */
 MR_API int mr_ssd_bwd_noalloc(const float* grad_y, const float* grad_final, const float* h_ckpt,
                               const void* u, const void* delta, const void* Bm, const void* Cm,
@@ -186,7 +200,7 @@ MR_API int mr_rglru_bwd(const float* grad_y, const float* grad_final, const floa
 
 /* ------------------------------------------------------------- rotLRU ---
  * a, cs, sn [B,L,Dp], x [B,L,2*Dp] (pairs interleaved) in `dtype`;
- * y [B,L,2*Dp] f32; h_ckpt [B,L/seg,2*Dp] f32 (rotlru.py:369). */
+ * y [B,L,2*Dp] f32; h_ckpt [B,L/seg,2*Dp] f32 (rotlru.py:87, 145). */
 MR_API int mr_rotlru_fwd(const void* a, const void* cs, const void* sn, const void* x, int dtype,
                   int64_t batch, int64_t L, int64_t Dp, int64_t seg,
                   float* y, float* h_ckpt, void* stream);

@@ -39,6 +39,7 @@ SIGNATURES = {
     "mr_launch_count": (ctypes.c_uint64, []),
     "mr_device_error_status": (_int, [_int]),
     "mr_selftest_umma": (_int, [_p, _p, _p, _p, _p, _p, _p, _p]),
+    "mr_selftest_wait_timeout": (_int, [_int, ctypes.c_uint64, _p, _p]),
     "mr_check_segment_shape": (_int, [_i64, _i64, _i64, ctypes.c_char_p]),
     "mr_ssd_fwd": (_int, [_p, _p, _p, _p, _p, _i64, _i64, _int, _i64, _i64, _i64, _i64, _i64, _i64,
                           _p, _p, _p]),

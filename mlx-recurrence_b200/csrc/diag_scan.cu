@@ -20,7 +20,7 @@
 //   2. the 8 per-warp maps go through shared memory and each thread folds
 //      the maps of the warps before it into its carry-in,
 //   3. each thread re-runs its steps from the carry-in with the reference's
-//      exact per-step update (rglru.py:92, rotlru.py:392-393), writing y and
+//      exact per-step update (rglru.py:92, rotlru.py:110-111), writing y and
 //      the segment checkpoints.
 // The backward walks blocks newest -> oldest. Blocks are aligned to segments
 // so each block starts from a checkpoint; it regenerates h_{t-1} with the
@@ -721,8 +721,8 @@ rotlru_fwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
           for (int v = 0; v < V; ++v) {
             const float av = fa[i][v], c = fc[i][v], sv = fs[i][v];
             const float u = cin[v].r, w = cin[v].i;
-            const float un = av * (c * u - sv * w) + fx[i][v].r;  // rotlru.py:392
-            const float wn = av * (sv * u + c * w) + fx[i][v].i;  // rotlru.py:393
+            const float un = av * (c * u - sv * w) + fx[i][v].r;  // rotlru.py:110
+            const float wn = av * (sv * u + c * w) + fx[i][v].i;  // rotlru.py:111
             cin[v] = {un, wn};
             hv[2 * v] = un;
             hv[2 * v + 1] = wn;
@@ -961,7 +961,7 @@ rotlru_bwd_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
       cr[v] = rc;
     }
 
-    // adjoint per step (rotlru.py:499-516)
+    // adjoint per step (rotlru.py:206-235)
 #pragma unroll
     for (int i = TW - 1; i >= 0; --i) {
       const int t = t0 + i;

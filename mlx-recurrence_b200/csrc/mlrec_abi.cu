@@ -78,6 +78,7 @@ template <typename T> int rotlru_angle_fwd_launch(const void*, const void*, cons
 template <typename T> int rotlru_angle_bwd_launch(const float*, const float*, const float*, const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, void*, void*, void*, float*, const float*, float*, cudaStream_t);
 int umma_selftest_launch(const void*, const void*, const void*, const void*, float*, float*, float*,
                          cudaStream_t);
+int wait_selftest_launch(int, uint64_t, uint64_t*, cudaStream_t);
 
 // ---- validation helpers -----------------------------------------------------
 static int check_seg(int64_t L, int64_t seg, int64_t lane_dim, const char* lane_name) {
@@ -169,6 +170,15 @@ int mr_selftest_umma(const void* A, const void* Bk, const void* Bmn, const void*
   g_err[0] = 0;
   MR_TRY(check_ptrs("mr_selftest_umma", {A, Bk, Bmn, Amn, D1, D2, D3}));
   return umma_selftest_launch(A, Bk, Bmn, Amn, D1, D2, D3, (cudaStream_t)stream);
+}
+
+int mr_selftest_wait_timeout(int ctas, uint64_t limit_ns, uint64_t* elapsed_ns, void* stream) {
+  g_err[0] = 0;
+  if (ctas <= 0 || ctas > 1024) return set_error(MR_E_SHAPE, "mr_selftest_wait_timeout: ctas must be 1..1024");
+  if (limit_ns == 0 || limit_ns > 1000000000ull)
+    return set_error(MR_E_SHAPE, "mr_selftest_wait_timeout: limit_ns must be 1..1e9");
+  MR_TRY(check_ptrs("mr_selftest_wait_timeout", {elapsed_ns}));
+  return wait_selftest_launch(ctas, limit_ns, elapsed_ns, (cudaStream_t)stream);
 }
 
 int mr_check_segment_shape(int64_t L, int64_t seg, int64_t lane_dim, const char* lane_name) {

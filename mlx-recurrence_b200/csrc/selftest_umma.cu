@@ -128,6 +128,32 @@ int umma_selftest_launch(const void* A, const void* Bk, const void* Bmn, const v
   return check_launch("umma_selftest_kernel");
 }
 
+// Bounded-wait diagnostic: every CTA waits on a barrier that never completes,
+// once with `limit_ns`, once with the standard limit, and records both
+// durations. Nothing is in flight, so giving up leaves no copy behind.
+__global__ void __launch_bounds__(32, 1) wait_timeout_selftest_kernel(uint64_t limit_ns, uint64_t* elapsed_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+  if (threadIdx.x == 0) {
+    uint64_t t0 = globaltimer_ns();
+    mbar_wait_ns(&bar, 0, limit_ns);
+    uint64_t t1 = globaltimer_ns();
+    mbar_wait(&bar, 0);
+    uint64_t t2 = globaltimer_ns();
+    elapsed_ns[2 * blockIdx.x] = t1 - t0;
+    elapsed_ns[2 * blockIdx.x + 1] = t2 - t1;
+  }
+}
+
+int wait_selftest_launch(int ctas, uint64_t limit_ns, uint64_t* elapsed_ns, cudaStream_t st) {
+  wait_timeout_selftest_kernel<<<(unsigned)ctas, 32, 0, st>>>(limit_ns, elapsed_ns);
+  return check_launch("wait_timeout_selftest_kernel");
+}
+
 int selftest_device_error(bool clear) { return read_device_error(clear); }
 
 }  // namespace mr

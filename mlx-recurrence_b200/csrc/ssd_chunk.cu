@@ -24,6 +24,8 @@
 // memory is the operand of the next chunk's Y2 product, and it is written to
 // h_ckpt in float32 at segment ends (seg a multiple of Q).
 #include <mutex>
+#include <utility>
+#include <vector>
 
 #include "common.cuh"
 #include "tma.cuh"
@@ -1453,9 +1455,10 @@ template int gla_chunk_bwd_launch<__half>(const float*, const float*, const floa
 // Limits and behaviour:
 //   - batch * H <= kNoAllocMaxUnits (65,536), i.e. a 256 KiB array; larger
 //     problems are rejected with MR_E_WORKSPACE.
-//   - On the first call on a device (with that device current) the array's
-//     device address is looked up once and cached; make that first call
-//     before any stream capture on the device.
+//   - On the first call in a CUDA context (the device's primary context or one
+//     the caller made current) the array's device address is looked up once
+//     and cached for that context; make that first call before any stream
+//     capture on the device.
 //   - Every call on a device shares the array. Each call writes every entry it
 //     later reads, so nothing needs clearing between calls, but calls that
 //     overlap on the GPU (for example on different streams) race.
@@ -1463,23 +1466,68 @@ template int gla_chunk_bwd_launch<__half>(const float*, const float*, const floa
 constexpr int64_t kNoAllocMaxUnits = 65536;
 static __device__ __align__(256) float g_noalloc_scratch[kNoAllocMaxUnits];
 
-static int noalloc_scratch_ptr(float** out) {
-  constexpr int kMaxDev = 64;
-  static float* cached[kMaxDev] = {};
-  static std::mutex mu;
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return set_error(MR_E_DEVICE, "cudaGetDevice: %s", cudaGetErrorString(e));
-  if (dev < 0 || dev >= kMaxDev) return set_error(MR_E_DEVICE, "device ordinal %d out of range", dev);
-  std::lock_guard<std::mutex> lock(mu);
-  if (cached[dev] == nullptr) {
+// The array's device address belongs to the CUDA context the library's module
+// is loaded in: each context (the device's primary context, or a context an
+// embedder created and made current) has its own copy. Addresses are cached per
+// context, keyed by the driver's unique context id, which no later context
+// reuses (not even one created after cudaDeviceReset), so a stale address is
+// never handed out.
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long*);
+
+static bool ctx_entry_points(CtxGetCurrentFn* cur, CtxGetIdFn* id) {
+  static CtxGetCurrentFn f_cur = nullptr;
+  static CtxGetIdFn f_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
     void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      f_cur = reinterpret_cast<CtxGetCurrentFn>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      f_id = reinterpret_cast<CtxGetIdFn>(p);
+  });
+  *cur = f_cur;
+  *id = f_id;
+  return f_cur != nullptr && f_id != nullptr;
+}
+
+static int noalloc_scratch_ptr(float** out) {
+  static std::mutex mu;
+  static std::vector<std::pair<unsigned long long, float*>> cached;  // (context id, address)
+  CtxGetCurrentFn get_cur = nullptr;
+  CtxGetIdFn get_id = nullptr;
+  if (!ctx_entry_points(&get_cur, &get_id))
+    return set_error(MR_E_DEVICE, "mr_ssd_bwd_noalloc: the driver's context queries are unavailable");
+  CUcontext ctx = nullptr;
+  if (get_cur(&ctx) != CUDA_SUCCESS)
+    return set_error(MR_E_DEVICE, "mr_ssd_bwd_noalloc: no usable CUDA context on this thread");
+  if (ctx == nullptr) {
+    // No context is current yet: the runtime binds the current device's primary
+    // context on its first call; look the address up through it.
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess)
       return set_error(MR_E_DEVICE, "cudaGetSymbolAddress(scratch): %s", cudaGetErrorString(e));
-    cached[dev] = static_cast<float*>(p);
+    if (get_cur(&ctx) != CUDA_SUCCESS || ctx == nullptr)
+      return set_error(MR_E_DEVICE, "mr_ssd_bwd_noalloc: no CUDA context after binding the device");
   }
-  *out = cached[dev];
+  unsigned long long id = 0;
+  if (get_id(ctx, &id) != CUDA_SUCCESS) return set_error(MR_E_DEVICE, "mr_ssd_bwd_noalloc: cuCtxGetId failed");
+  std::lock_guard<std::mutex> lock(mu);
+  for (const auto& c : cached)
+    if (c.first == id) {
+      *out = c.second;
+      return MR_OK;
+    }
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (e != cudaSuccess) return set_error(MR_E_DEVICE, "cudaGetSymbolAddress(scratch): %s", cudaGetErrorString(e));
+  cached.emplace_back(id, static_cast<float*>(p));
+  *out = static_cast<float*>(p);
   return MR_OK;
 }
 

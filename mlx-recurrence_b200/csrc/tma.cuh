@@ -2,9 +2,10 @@
 // copies global -> shared through the TMA unit (cp.async.bulk, each CTA
 // fetching its own data), and bounded waits.
 //
-// Every wait is bounded: after kSpinLimit polls it records an error code in
-// this translation unit's device word g_device_error (read through
-// mr_device_error_status()) and returns, so a kernel can never spin forever.
+// Every wait is bounded: after kSpinLimit polls or 2 s it records an error
+// code in this translation unit's device word g_device_error (read through
+// mr_device_error_status()) and returns, so a kernel can never spin forever;
+// once the word is set, later waits give up at once (see mbar_wait_ns).
 #pragma once
 
 #include <cuda_runtime.h>
@@ -75,16 +76,29 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 }
 
 // Bounded wait for the phase with the given parity to complete: gives up
-// after kSpinLimit polls or 2 s of wall time, whichever comes first.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// after kSpinLimit polls or `limit_ns` of wall time, whichever comes first,
+// and records the timeout in g_device_error. Once that word is set (by any
+// wait of this translation unit, in this launch or an earlier one not yet
+// cleared by the host), every later wait that does not complete within 256
+// polls gives up at once: a kernel whose copies stopped arriving ends in
+// about one time limit instead of one limit per remaining wait, and its
+// results are void until the host reads and clears the word.
+__device__ __forceinline__ bool mbar_wait_ns(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 0; i < kSpinLimit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255u) == 255u && globaltimer_ns() - t0 > 2000000000ull) break;
+    if ((i & 255u) == 255u) {
+      if (*reinterpret_cast<volatile int*>(&g_device_error) != 0) return false;
+      if (globaltimer_ns() - t0 > limit_ns) break;
+    }
   }
   atomicCAS(&g_device_error, 0, 1);
   return false;
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  return mbar_wait_ns(bar, parity, 2000000000ull);
 }
 
 // 1-D bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned)

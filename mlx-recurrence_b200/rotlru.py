@@ -41,7 +41,7 @@ class _RotLRUScan(torch.autograd.Function):
         # an unused output's cotangent arrives as None (no zero tensor is made)
         ctx.set_materialize_grads(False)
         Bt, L, Dp = _validate(a, cs, sn, x)
-        check_segment_shape(L, seg, x.shape[2], "D")  # rotlru.py:565
+        check_segment_shape(L, seg, x.shape[2], "D")  # rotlru.py:282
         dev = _lib.require_cuda(a, cs, sn, x)
         dt = common_dtype(a, cs, sn, x)
         a_, c_, s_, x_ = (prep(t, dt) for t in (a, cs, sn, x))

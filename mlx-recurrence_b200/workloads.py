@@ -13,7 +13,7 @@ import math
 
 import torch
 
-from .sharding import shard_batch  # noqa: F401  (re-exported for bench.py)
+from .sharding import block_of, shard_batch  # noqa: F401  (re-exported for bench.py)
 
 CONFIGS = {
     "c0": dict(kind="ssd", B=3, L=512, H=12, Dh=64, N=16, seg=32, dtype=torch.float32),
@@ -46,19 +46,47 @@ DESCRIPTION = {
 GATE_C = 8.0  # the RG-LRU gate exponent scale of c2 / c2g
 
 
+# The independent units of each kind: batch rows times this axis of the
+# config, split across ranks in multiples of the quantum (the scans' lane rule).
+UNIT_AXIS = {"ssd": ("H", 1), "gla": ("H", 1), "gdn": ("H", 1), "rglru": ("D", 32), "rglru_gated": ("D", 32),
+             "rotlru": ("Dp", 16), "rotlru_angle": ("Dp", 16)}
+
+
 def tokens(cfg):
     return cfg["B"] * cfg["L"]
 
 
-def make_inputs(name, device, seed=0, batch=None):
-    """Primal inputs of config ``name`` (tuple, in kernel order) on ``device``.
+def rank_block(name, rank, world, batch=None):
+    """(b0, b1, u0, u1): the rank's batch rows and heads / channels / pairs."""
+    cfg = CONFIGS[name]
+    ax, q = UNIT_AXIS[cfg["kind"]]
+    return block_of(batch or cfg["B"], cfg[ax], rank, world, q)
 
-    ``batch`` overrides B (a rank's shard size). Values are drawn in float32
-    from a generator on ``device`` and then cast to the config dtype.
-    """
+
+def local_config(name, block=None, batch=None):
+    """The config restricted to a block (or with its batch overridden)."""
     cfg = dict(CONFIGS[name])
     if batch is not None:
         cfg["B"] = batch
+    if block is not None:
+        b0, b1, u0, u1 = block
+        ax, _ = UNIT_AXIS[cfg["kind"]]
+        cfg["B"], cfg[ax] = b1 - b0, u1 - u0
+    return cfg
+
+
+def make_inputs(name, device, seed=0, batch=None, block=None):
+    """Primal inputs of config ``name`` (tuple, in kernel order) on ``device``.
+
+    ``batch`` overrides B; ``block`` = (b0, b1, u0, u1) restricts the inputs to
+    a rank's batch rows and heads / channels / pairs (the shared parameters are
+    the slice [u0, u1) of their full draw). Values are drawn in float32 from a
+    generator on ``device`` and then cast to the config dtype.
+    """
+    full = dict(CONFIGS[name])
+    cfg = local_config(name, block, batch)
+    ax, _ = UNIT_AXIS[cfg["kind"]]
+    u0, u1 = (0, full[ax]) if block is None else block[2:]
     g = torch.Generator(device=device).manual_seed(seed)
     f32 = dict(dtype=torch.float32, device=device, generator=g)
     # parameters every rank shares (SSD's A, RG-LRU's Lambda) come from a fixed seed
@@ -71,7 +99,7 @@ def make_inputs(name, device, seed=0, batch=None):
         delta = torch.randn((B, L, H), **f32).abs_().mul_(0.1).add_(0.01)
         Bm = torch.randn((B, L, H, N), **f32)
         Cm = torch.randn((B, L, H, N), **f32)
-        A = -torch.exp(torch.randn((H,), **rep) * 0.5)
+        A = -torch.exp(torch.randn((full["H"],), **rep) * 0.5)[u0:u1]
         A_neg = A[:, None].expand(H, N)  # one rate per head, broadcast over N
         return (u.to(dt), delta.to(dt), Bm.to(dt), Cm.to(dt), A_neg)
     if cfg["kind"] == "gla":
@@ -95,7 +123,7 @@ def make_inputs(name, device, seed=0, batch=None):
         x = torch.randn((B, L, D), **f32)
         r = torch.sigmoid(torch.randn((B, L, D), **f32))
         i = torch.sigmoid(torch.randn((B, L, D), **f32))
-        lam = torch.rand((D,), **rep) * (6.9 - 2.2) + 2.2
+        lam = (torch.rand((full["D"],), **rep) * (6.9 - 2.2) + 2.2)[u0:u1]
         if cfg["kind"] == "rglru_gated":
             return (x.to(dt), r.to(dt), i.to(dt), lam)
         a = torch.sigmoid(lam) ** (GATE_C * r)
@@ -112,9 +140,9 @@ def make_inputs(name, device, seed=0, batch=None):
     raise KeyError(name)
 
 
-def output_shape(name, batch=None):
-    cfg = CONFIGS[name]
-    B = cfg["B"] if batch is None else batch
+def output_shape(name, batch=None, block=None):
+    cfg = local_config(name, block, batch)
+    B = cfg["B"]
     if cfg["kind"] in ("ssd", "gla", "gdn"):
         return (B, cfg["L"], cfg["H"], cfg["Dh"])
     if cfg["kind"] in ("rglru", "rglru_gated"):

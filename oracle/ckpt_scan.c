@@ -9,7 +9,7 @@
  *   SSD    forward mlx_recurrence/ssd.py:85-111, backward ssd.py:174-268
  *   GLA    forward gla.py:78-100,  backward gla.py:158-235
  *   RG-LRU forward rglru.py:88-100, backward rglru.py:147-180
- *   rotLRU forward rotlru.py:383-405, backward rotlru.py:456-518
+ *   rotLRU forward rotlru.py:93-124, backward rotlru.py:166-237
  *   Gated DeltaNet (a design only in the reference) docs/DESIGN_gated_deltanet.md
  *          sections 1 and 4
  * One OpenMP task per independent unit ((b,h) for SSD/GLA, b for the

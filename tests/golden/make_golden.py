@@ -159,6 +159,41 @@ def main():
                 "seg": ns.get("seg"), "reference_version": src_version}
         _save(f"{kind}_final_state", arrays, meta)
 
+    # ---- widened cases that reach the tensor-core kernels ----
+    # The reference's own input makers (test_v2_ssd.py:15-23, test_v2_gla.py:11-18) at
+    # the shape the chunked kernels take (L=256, Dh=64, N=128). SSD gets one decay rate
+    # per head: the first column of the drawn A_neg, broadcast over N. The inputs are
+    # rounded to bf16 (A_neg stays float32), so a bf16 run reads exactly these values;
+    # y and the gradients come from the reference's pure loops through the recorder.
+    import torch
+    from mlx_recurrence.ssd import ssd_scan_reference
+    from mlx_recurrence.gla import gla_scan_reference
+
+    def _bf16(x):
+        return x.float().to(torch.bfloat16).double()
+
+    wide = [
+        ("ssd", ssd_scan_reference, ["u", "delta", "B", "C", "A_neg"], dict(B=2, L=256, H=2, Dh=64, N=128, seed=4)),
+        ("gla", gla_scan_reference, ["q", "k", "v", "gates"], dict(B=2, L=256, H=2, Dh=64, seed=4)),
+    ]
+    for kind, ref_fn, argn, p in wide:
+        ins = list(tests[kind]._make_inputs(**p))
+        if kind == "ssd":
+            A = ins[4]
+            ins[4] = A[:, :1].expand(A.shape).contiguous()
+            ins[:4] = [_bf16(x) for x in ins[:4]]
+        else:
+            ins = [_bf16(x) for x in ins]
+        rec = _Recorder(mx, kind)
+        rec(None, ref_fn, ins, argn, tuple(range(len(argn))), label=f"{kind} widened {p}")
+        for label, names, arrays in rec.cases:
+            meta = {"kind": kind, "test": f"tests/test_v2_{kind}.py::_make_inputs (widened)",
+                    "params": {**p, "seg": 32}, "label": label, "arg_names": names,
+                    "inputs": "rounded to bf16 (A_neg float32, one rate per head)",
+                    "reference_version": src_version,
+                    "loss": "sum(y * w_out), w_out ~ seed 1234 (_chassis.py:166-188)"}
+            _save(f"{kind}_tc_parity_widened", arrays, meta)
+
     # ---- rotLRU properties, run with the reference loop in place of the kernel ----
     rmod = tests["rotlru"]
     from mlx_recurrence.rotlru import rotlru_scan_reference

@@ -191,3 +191,45 @@ def test_ssd_tensor_core_path_through_api(mr, cuda_dev, Bt, L, H, seg, dtype):
     for name, g, r in zip(("u", "delta", "B", "C"), grads[:4], ref[:4]):
         assert K.rel_err(g.double().cpu().numpy(), r) < 2e-2, name
     assert K.rel_err(grads[4].double().cpu().numpy(), ref[4].sum(1)) < 2e-2, "A (per head)"
+
+
+@pytest.mark.parametrize("kind", ["ssd", "gla"])
+def test_golden_widened_case_on_tensor_core_path(mr, cuda_dev, kind):
+    """The reference's own outputs at a shape the chunked tcgen05 kernels take
+    (L=256, Dh=64, N=128, bf16-representable inputs, SSD with one rate per
+    head passed as an [H] parameter broadcast over N): forward and every
+    gradient of the bf16 run against the golden float32 values at 2e-2."""
+    import importlib
+    Lm = importlib.import_module("mlx-recurrence_b200._lib")
+    lib = Lm.load()
+    case = K.load(os.path.join(K.GOLDEN, f"{kind}_tc_parity_widened.npz"))
+    ins, names = K.inputs_of(case)
+    Bt, L, H, Dh = ins[0].shape
+    ts = [torch.tensor(x, dtype=torch.float32).to(torch.bfloat16).to(cuda_dev).requires_grad_(True)
+          for x in (ins[:4] if kind == "ssd" else ins)]
+    # the bf16 rounding is exact: the golden inputs are bf16 values
+    for t, x in zip(ts, ins):
+        assert np.array_equal(t.detach().double().cpu().numpy(), x)
+    args = list(ts)
+    if kind == "ssd":
+        A_rows = ins[4]
+        assert np.all(A_rows == A_rows[:, :1])
+        A_t = torch.tensor(A_rows[:, 0], dtype=torch.float32, device=cuda_dev, requires_grad=True)
+        args.append(A_t[:, None].expand(H, A_rows.shape[1]))
+        leaves = ts + [A_t]
+        # the tensor-core path checkpoints every 128-step chunk
+        assert lib.mr_ssd_preferred_seg(Lm.MR_BF16, L, Dh, A_rows.shape[1], 32, 0) == 128
+        y = mr.ssd_scan(*args, seg=32)
+    else:
+        leaves = ts
+        assert lib.mr_gla_preferred_seg(Lm.MR_BF16, L, Dh, 32) == 128
+        y = mr.gla_scan(*args, seg=32)
+    w = torch.tensor(case["w_out"], dtype=torch.float32, device=cuda_dev)
+    grads = torch.autograd.grad((y * w).sum(), leaves)
+    assert K.rel_err(y.detach().double().cpu().numpy(), case["y"]) < 2e-2, "y"
+    for n, g in zip(names, grads):
+        ref = case["grad_" + n]
+        if kind == "ssd" and n == "A_neg":
+            ref = ref.sum(axis=1)  # d loss / d (one rate per head)
+        err = K.rel_err(g.double().cpu().numpy(), ref)
+        assert err < 2e-2, f"grad_{n}: {err:.2e}"

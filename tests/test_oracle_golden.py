@@ -124,3 +124,26 @@ def test_c_oracle_final_state_cotangent_matches_numpy_oracle():
     assert K.rel_err(out["final"], f) < 1e-5
     for g, r in zip(out["grads"], ref):
         assert K.rel_err(g, r) < 1e-5
+
+
+@pytest.mark.parametrize("seg", [1, 7, 40, 1000])
+def test_segmented_backwards_equal_plain(seg):
+    """The segmented float64 backwards (states regenerated per segment, used
+    for full-length configurations) give the same numbers as the plain ones,
+    including the final-state cotangent and h0."""
+    rng = np.random.default_rng(seg)
+    B, L, H, Dh, N = 2, 80, 2, 8, 5
+    u = rng.standard_normal((B, L, H, Dh))
+    d = np.abs(rng.standard_normal((B, L, H))) * 0.1 + 0.01
+    Bm, Cm = rng.standard_normal((B, L, H, N)), rng.standard_normal((B, L, H, N))
+    A = -np.abs(rng.standard_normal((H, N))) - 0.1
+    gy = rng.standard_normal((B, L, H, Dh))
+    gf, h0 = rng.standard_normal((B, H, Dh, N)), rng.standard_normal((B, H, Dh, N))
+    for a, b in zip(R.ssd_backward(u, d, Bm, Cm, A, gy, gf, h0=h0),
+                    R.ssd_backward_segmented(u, d, Bm, Cm, A, gy, gf, h0=h0, seg=seg)):
+        assert np.array_equal(a, b)
+    q, k, v = (rng.standard_normal((B, L, H, Dh)) for _ in range(3))
+    g = 1 / (1 + np.exp(-rng.standard_normal((B, L, H)) - 2))
+    gf2 = rng.standard_normal((B, H, Dh, Dh))
+    for a, b in zip(R.gla_backward(q, k, v, g, gy, gf2), R.gla_backward_segmented(q, k, v, g, gy, gf2, seg=seg)):
+        assert np.array_equal(a, b)
