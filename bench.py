@@ -528,8 +528,9 @@ def _ckpt_spacing(ctx, cfg):
     path's; the final state is the same for any spacing)."""
     L = importlib.import_module("mlx-recurrence_b200._lib")
     code = L.DTYPE_CODE[cfg["dtype"]]
-    if cfg["kind"] == "ssd":  # one rate per head: the stride-0 view along N
-        return int(ctx["lib"].mr_ssd_preferred_seg(code, cfg["L"], cfg["Dh"], cfg["N"], cfg["seg"], 0))
+    if cfg["kind"] == "ssd":  # one rate per head (the stride-0 view along N), or dense
+        asn = 1 if cfg.get("dense_a") else 0
+        return int(ctx["lib"].mr_ssd_preferred_seg(code, cfg["L"], cfg["Dh"], cfg["N"], cfg["seg"], asn))
     if cfg["kind"] == "gla":
         return int(ctx["lib"].mr_gla_preferred_seg(code, cfg["L"], cfg["Dh"], cfg["seg"]))
     return cfg["seg"]
@@ -651,7 +652,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--config", default="c4", choices=["c0", "c1", "c2", "c3", "c4", "c5", "c2g", "c3a", "c6"])
+    ap.add_argument("--config", default="c4", choices=["c0", "c1", "c2", "c3", "c4", "c4d", "c5", "c2g", "c3a", "c6"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffer) timing")

@@ -36,7 +36,12 @@ template <typename T> int rglru_fwd_launch(const void*, const void*, int64_t, in
 template <typename T> int rglru_bwd_launch(const float*, const float*, const float*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, void*, void*, float*, const float*, float*, cudaStream_t);
 template <typename T> int rotlru_fwd_launch(const void*, const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, float*, float*, const float*, cudaStream_t);
 template <typename T> int rotlru_bwd_launch(const float*, const float*, const float*, const void*, const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, void*, void*, void*, void*, float*, const float*, float*, cudaStream_t);
-template <typename T> int ssd_seq_fwd_launch(const void*, const void*, const void*, const void*, const float*, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, float*, float*, const float*, cudaStream_t);
+template <typename T> int ssd_seq_fwd_launch(const void*, const void*, const void*, const void*, const float*, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, float*, float*, const float*, cudaStream_t, int);
+template <typename T> int ssd_seq_bwd_marked_launch(const float*, const float*, const float*, const void*, const void*, const void*, const void*, const float*, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, void*, void*, void*, void*, float*, void*, const float*, float*, cudaStream_t);
+size_t ssd_fallback_ws_bytes(int64_t, int64_t, int64_t, int64_t, int64_t, int64_t);
+bool ssd_dense_chunk_supported(int dtype, int64_t L, int64_t Dh, int64_t N, int64_t seg, int64_t a_stride_n);
+template <typename T> int ssd_dense_chunk_fwd_launch(const void*, const void*, const void*, const void*, const float*, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, float*, float*, const float*, cudaStream_t);
+template <typename T> int ssd_dense_chunk_bwd_launch(const float*, const float*, const float*, const void*, const void*, const void*, const void*, const float*, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, void*, void*, void*, void*, float*, const float*, float*, cudaStream_t);
 template <typename T> int ssd_seq_bwd_launch(const float*, const float*, const float*, const void*, const void*, const void*, const void*, const float*, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, void*, void*, void*, void*, float*, void*, const float*, float*, cudaStream_t);
 template <typename T> int gla_seq_fwd_launch(const void*, const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, int64_t, float*, float*, const float*, cudaStream_t, int);
 template <typename T> int gla_seq_bwd_launch(const float*, const float*, const float*, const void*, const void*, const void*, const void*, int64_t, int64_t, int64_t, int64_t, int64_t, void*, void*, void*, void*, void*, const float*, float*, cudaStream_t, int);
@@ -482,20 +487,41 @@ int mr_ssd_fwd_h0(const void* u, const void* delta, const void* Bm, const void* 
     return ssd_chunk_fwd_launch<__half>(u, delta, Bm, Cm, A_neg, a_stride_h, batch, L, H, seg, y, h_ckpt, h0,
                                         st);
   }
+  if (ssd_dense_chunk_supported(dtype, L, Dh, N, seg, a_stride_n)) {
+    // dense A_neg on the tensor cores, then the per-step kernel for the units it marked
+    if (dtype == MR_BF16) {
+      MR_TRY(ssd_dense_chunk_fwd_launch<__nv_bfloat16>(u, delta, Bm, Cm, A_neg, a_stride_h, a_stride_n, batch, L,
+                                                        H, seg, y, h_ckpt, h0, st));
+      return ssd_seq_fwd_launch<__nv_bfloat16>(u, delta, Bm, Cm, A_neg, a_stride_h, a_stride_n, batch, L, H, Dh,
+                                               N, seg, y, h_ckpt, h0, st, 1);
+    }
+    MR_TRY(ssd_dense_chunk_fwd_launch<__half>(u, delta, Bm, Cm, A_neg, a_stride_h, a_stride_n, batch, L, H, seg,
+                                               y, h_ckpt, h0, st));
+    return ssd_seq_fwd_launch<__half>(u, delta, Bm, Cm, A_neg, a_stride_h, a_stride_n, batch, L, H, Dh, N, seg,
+                                      y, h_ckpt, h0, st, 1);
+  }
   MR_DTYPE_SWITCH(dtype, ssd_seq_fwd_launch<T>(u, delta, Bm, Cm, A_neg, a_stride_h, a_stride_n,
-                                               batch, L, H, Dh, N, seg, y, h_ckpt, h0, st));
+                                               batch, L, H, Dh, N, seg, y, h_ckpt, h0, st, 0));
+}
+
+// the backward's tensor-core path with a dense A_neg needs a checkpoint at every chunk start
+static bool ssd_dense_chunk_bwd(int dtype, int64_t L, int64_t Dh, int64_t N, int64_t seg, int64_t a_stride_n) {
+  return ssd_dense_chunk_supported(dtype, L, Dh, N, seg, a_stride_n) && seg == ssd_chunk_len();
 }
 
 size_t mr_ssd_bwd_workspace_bytes(int dtype, int64_t batch, int64_t L, int64_t H, int64_t Dh,
                                   int64_t N, int64_t seg, int64_t a_stride_n) {
   if (batch <= 0 || L <= 0 || H <= 0 || Dh <= 0 || N <= 0 || seg <= 0) return 0;
   if (ssd_chunk_bwd_supported(dtype, L, Dh, N, seg, a_stride_n)) return ssd_chunk_bwd_ws_bytes(batch, H);
+  if (ssd_dense_chunk_bwd(dtype, L, Dh, N, seg, a_stride_n)) return ssd_fallback_ws_bytes(batch, L, H, Dh, N, seg);
   return ssd_seq_bwd_ws_bytes(batch, L, H, Dh, N, seg);
 }
 
 int64_t mr_ssd_preferred_seg(int dtype, int64_t L, int64_t Dh, int64_t N, int64_t seg, int64_t a_stride_n) {
   const int64_t q = ssd_chunk_len();
-  if (seg > 0 && L % q == 0 && q % seg == 0 && ssd_chunk_bwd_supported(dtype, L, Dh, N, q, a_stride_n)) return q;
+  if (seg > 0 && L % q == 0 && q % seg == 0 &&
+      (ssd_chunk_bwd_supported(dtype, L, Dh, N, q, a_stride_n) || ssd_dense_chunk_bwd(dtype, L, Dh, N, q, a_stride_n)))
+    return q;
   return seg;
 }
 
@@ -522,7 +548,10 @@ int mr_ssd_bwd_h0(const float* grad_y, const float* grad_final, const float* h_c
   if (A_neg == nullptr || grad_A == nullptr)
     return set_error(MR_E_ALIGN, "mr_ssd_bwd: A_neg / grad_A is NULL");
   const bool chunk = ssd_chunk_bwd_supported(dtype, L, Dh, N, seg, a_stride_n);
-  const size_t need = chunk ? ssd_chunk_bwd_ws_bytes(batch, H) : ssd_seq_bwd_ws_bytes(batch, L, H, Dh, N, seg);
+  const bool dense = !chunk && ssd_dense_chunk_bwd(dtype, L, Dh, N, seg, a_stride_n);
+  const size_t need = chunk   ? ssd_chunk_bwd_ws_bytes(batch, H)
+                      : dense ? ssd_fallback_ws_bytes(batch, L, H, Dh, N, seg)
+                              : ssd_seq_bwd_ws_bytes(batch, L, H, Dh, N, seg);
   if (workspace == nullptr || workspace_bytes < need)
     return set_error(MR_E_WORKSPACE, "mr_ssd_bwd: workspace of %zu bytes required, got %zu", need,
                      workspace_bytes);
@@ -538,6 +567,26 @@ int mr_ssd_bwd_h0(const float* grad_y, const float* grad_final, const float* h_c
     return ssd_chunk_bwd_launch<__half>(grad_y, grad_final, h_ckpt, u, delta, Bm, Cm, A_neg, a_stride_h, batch, L,
                                         H, seg, grad_u, grad_delta, grad_B, grad_C, grad_A, (float*)workspace, h0,
                                         grad_h0, st);
+  }
+  if (dense) {
+    // dense A_neg on the tensor cores (per-unit grad A partials at the start of the workspace),
+    // then the per-step kernel for the units it marked, then the sum over the batch
+    if (dtype == MR_BF16) {
+      MR_TRY(ssd_dense_chunk_bwd_launch<__nv_bfloat16>(grad_y, grad_final, h_ckpt, u, delta, Bm, Cm, A_neg,
+                                                        a_stride_h, a_stride_n, batch, L, H, seg, grad_u,
+                                                        grad_delta, grad_B, grad_C, (float*)workspace, h0, grad_h0,
+                                                        st));
+      return ssd_seq_bwd_marked_launch<__nv_bfloat16>(grad_y, grad_final, h_ckpt, u, delta, Bm, Cm, A_neg,
+                                                      a_stride_h, a_stride_n, batch, L, H, Dh, N, seg, grad_u,
+                                                      grad_delta, grad_B, grad_C, grad_A, workspace, h0, grad_h0,
+                                                      st);
+    }
+    MR_TRY(ssd_dense_chunk_bwd_launch<__half>(grad_y, grad_final, h_ckpt, u, delta, Bm, Cm, A_neg, a_stride_h,
+                                               a_stride_n, batch, L, H, seg, grad_u, grad_delta, grad_B, grad_C,
+                                               (float*)workspace, h0, grad_h0, st));
+    return ssd_seq_bwd_marked_launch<__half>(grad_y, grad_final, h_ckpt, u, delta, Bm, Cm, A_neg, a_stride_h,
+                                             a_stride_n, batch, L, H, Dh, N, seg, grad_u, grad_delta, grad_B, grad_C,
+                                             grad_A, workspace, h0, grad_h0, st);
   }
   MR_DTYPE_SWITCH(dtype, ssd_seq_bwd_launch<T>(grad_y, grad_final, h_ckpt, u, delta, Bm, Cm, A_neg,
                                                a_stride_h, a_stride_n, batch, L, H, Dh, N, seg,

@@ -36,11 +36,13 @@ __global__ void __launch_bounds__(kSeqThreads)
 ssd_seq_fwd_kernel(const T* __restrict__ u, const T* __restrict__ delta, const T* __restrict__ Bm,
                    const T* __restrict__ Cm, const float* __restrict__ A, int64_t ash, int64_t asn,
                    int L, int H, int Dh, int N, int seg, float* __restrict__ y,
-                   float* __restrict__ ckpt, const float* __restrict__ h0) {
+                   float* __restrict__ ckpt, const float* __restrict__ h0, int only_marked) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t b = blockIdx.x / H;
   const int h = blockIdx.x % H;
   const int nseg = L / seg;
+  // after the dense-A tensor-core path: only the units it marked (NaN in y[b, 0, h, 0])
+  if (only_marked && !isnan(y[(b * L * H + h) * Dh])) return;
 
   float An[NK];
 #pragma unroll
@@ -105,18 +107,23 @@ ssd_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfina
                    const float* __restrict__ A, int64_t ash, int64_t asn, int L, int H, int Dh,
                    int N, int seg, T* __restrict__ gu, T* __restrict__ gdelta, T* __restrict__ gB,
                    T* __restrict__ gC, float* __restrict__ gA_part, float* __restrict__ scratch,
-                   const float* __restrict__ h0, float* __restrict__ gh0) {
+                   const float* __restrict__ h0, float* __restrict__ gh0, int units, int only_marked) {
   constexpr int NP = 32 * NK;
   __shared__ float pB[kTS][8][NP];
   __shared__ float pC[kTS][8][NP];
   __shared__ float pdt[kTS][8];
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int64_t b = blockIdx.x / H;
-  const int h = blockIdx.x % H;
   const int nseg = L / seg;
   constexpr int E = R * NK;  // state values per thread
+  // one scratch slot per CTA; a CTA walks units blockIdx.x, + gridDim.x, ... (one each
+  // unless only_marked: then a few CTAs recompute the units the dense-A tensor-core
+  // path marked, NaN in grad_delta[b, 0, h])
   float* scr = scratch + (int64_t)blockIdx.x * (seg + 1) * E * kSeqThreads + tid;
+  for (int unit = blockIdx.x; unit < units; unit += gridDim.x) {
+  const int64_t b = unit / H;
+  const int h = unit % H;
+  if (only_marked && !isnan(to_f(gdelta[b * L * H + h]))) continue;
 
   float An[NK];
 #pragma unroll
@@ -271,6 +278,8 @@ ssd_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfina
 #pragma unroll
     for (int w = 0; w < 8; ++w) sa += pB[0][w][n];
     gA_part[(b * H + h) * (int64_t)N + n] = sa;
+  }
+  __syncthreads();  // pB is reused by the next unit
   }
 }
 
@@ -513,6 +522,16 @@ size_t gla_fallback_ws_bytes(int64_t batch, int64_t L, int64_t H, int64_t Dh, in
   return gla_seq_bwd_ws_bytes(slots, L, 1, Dh, seg);
 }
 
+// the dense-A tensor-core backward: its per-unit grad A partials [B, H, N], then the
+// scratch of kSsdFallbackSlots units recomputed in turn by the per-step kernel
+constexpr int64_t kSsdFallbackSlots = 16;
+size_t ssd_fallback_ws_bytes(int64_t batch, int64_t L, int64_t H, int64_t Dh, int64_t N, int64_t seg) {
+  const int64_t units = batch * H;
+  const int64_t slots = units < kSsdFallbackSlots ? units : kSsdFallbackSlots;
+  const size_t part = ((units * N * sizeof(float) + 255) / 256) * 256;
+  return part + (size_t)slots * (seg + 1) * (Dh / 8) * nk_of(N) * kSeqThreads * sizeof(float);
+}
+
 bool ssd_seq_supported(int64_t Dh, int64_t N) {
   return (Dh == 32 || Dh == 64 || Dh == 96 || Dh == 128) && N >= 1 && N <= 128;
 }
@@ -532,24 +551,25 @@ bool gla_seq_supported(int64_t Dh) { return Dh == 32 || Dh == 64 || Dh == 96 || 
 template <typename T, int R>
 static void ssd_fwd_nk(int nk, dim3 g, cudaStream_t st, const T* u, const T* dl, const T* Bm,
                        const T* Cm, const float* A, int64_t ash, int64_t asn, int L, int H, int Dh,
-                       int N, int seg, float* y, float* ck, const float* h0) {
+                       int N, int seg, float* y, float* ck, const float* h0, int om) {
   if (nk == 1)
-    ssd_seq_fwd_kernel<T, R, 1><<<g, kSeqThreads, 0, st>>>(u, dl, Bm, Cm, A, ash, asn, L, H, Dh, N, seg, y, ck, h0);
+    ssd_seq_fwd_kernel<T, R, 1><<<g, kSeqThreads, 0, st>>>(u, dl, Bm, Cm, A, ash, asn, L, H, Dh, N, seg, y, ck, h0, om);
   else if (nk == 2)
-    ssd_seq_fwd_kernel<T, R, 2><<<g, kSeqThreads, 0, st>>>(u, dl, Bm, Cm, A, ash, asn, L, H, Dh, N, seg, y, ck, h0);
+    ssd_seq_fwd_kernel<T, R, 2><<<g, kSeqThreads, 0, st>>>(u, dl, Bm, Cm, A, ash, asn, L, H, Dh, N, seg, y, ck, h0, om);
   else
-    ssd_seq_fwd_kernel<T, R, 4><<<g, kSeqThreads, 0, st>>>(u, dl, Bm, Cm, A, ash, asn, L, H, Dh, N, seg, y, ck, h0);
+    ssd_seq_fwd_kernel<T, R, 4><<<g, kSeqThreads, 0, st>>>(u, dl, Bm, Cm, A, ash, asn, L, H, Dh, N, seg, y, ck, h0, om);
 }
 
+// only_marked: recompute just the units the dense-A tensor-core path marked
 template <typename T>
 int ssd_seq_fwd_launch(const void* u, const void* delta, const void* Bm, const void* Cm,
                        const float* A, int64_t ash, int64_t asn, int64_t batch, int64_t L, int64_t H,
                        int64_t Dh, int64_t N, int64_t seg, float* y, float* ckpt, const float* h0,
-                       cudaStream_t st) {
+                       cudaStream_t st, int only_marked) {
   dim3 g((unsigned)(batch * H));
 #define MR_CALL(R_, NK_)                                                                       \
   ssd_fwd_nk<T, R_>(NK_, g, st, (const T*)u, (const T*)delta, (const T*)Bm, (const T*)Cm, A, ash, \
-                    asn, (int)L, (int)H, (int)Dh, (int)N, (int)seg, y, ckpt, h0)
+                    asn, (int)L, (int)H, (int)Dh, (int)N, (int)seg, y, ckpt, h0, only_marked)
   MR_SSD_DISPATCH(Dh, N, MR_CALL);
 #undef MR_CALL
   return check_launch("ssd_seq_fwd_kernel");
@@ -559,13 +579,14 @@ template <typename T, int R>
 static void ssd_bwd_nk(int nk, dim3 g, cudaStream_t st, const float* gy, const float* gf,
                        const float* ck, const T* u, const T* dl, const T* Bm, const T* Cm,
                        const float* A, int64_t ash, int64_t asn, int L, int H, int Dh, int N, int seg,
-                       T* gu, T* gd, T* gB, T* gC, float* gAp, float* scr, const float* h0, float* gh0) {
+                       T* gu, T* gd, T* gB, T* gC, float* gAp, float* scr, const float* h0, float* gh0,
+                       int units, int om) {
   if (nk == 1)
-    ssd_seq_bwd_kernel<T, R, 1><<<g, kSeqThreads, 0, st>>>(gy, gf, ck, u, dl, Bm, Cm, A, ash, asn, L, H, Dh, N, seg, gu, gd, gB, gC, gAp, scr, h0, gh0);
+    ssd_seq_bwd_kernel<T, R, 1><<<g, kSeqThreads, 0, st>>>(gy, gf, ck, u, dl, Bm, Cm, A, ash, asn, L, H, Dh, N, seg, gu, gd, gB, gC, gAp, scr, h0, gh0, units, om);
   else if (nk == 2)
-    ssd_seq_bwd_kernel<T, R, 2><<<g, kSeqThreads, 0, st>>>(gy, gf, ck, u, dl, Bm, Cm, A, ash, asn, L, H, Dh, N, seg, gu, gd, gB, gC, gAp, scr, h0, gh0);
+    ssd_seq_bwd_kernel<T, R, 2><<<g, kSeqThreads, 0, st>>>(gy, gf, ck, u, dl, Bm, Cm, A, ash, asn, L, H, Dh, N, seg, gu, gd, gB, gC, gAp, scr, h0, gh0, units, om);
   else
-    ssd_seq_bwd_kernel<T, R, 4><<<g, kSeqThreads, 0, st>>>(gy, gf, ck, u, dl, Bm, Cm, A, ash, asn, L, H, Dh, N, seg, gu, gd, gB, gC, gAp, scr, h0, gh0);
+    ssd_seq_bwd_kernel<T, R, 4><<<g, kSeqThreads, 0, st>>>(gy, gf, ck, u, dl, Bm, Cm, A, ash, asn, L, H, Dh, N, seg, gu, gd, gB, gC, gAp, scr, h0, gh0, units, om);
 }
 
 template <typename T>
@@ -582,7 +603,33 @@ int ssd_seq_bwd_launch(const float* gy, const float* gf, const float* ckpt, cons
 #define MR_CALL(R_, NK_)                                                                        \
   ssd_bwd_nk<T, R_>(NK_, g, st, gy, gf, ckpt, (const T*)u, (const T*)delta, (const T*)Bm,         \
                     (const T*)Cm, A, ash, asn, (int)L, (int)H, (int)Dh, (int)N, (int)seg, (T*)gu,  \
-                    (T*)gd, (T*)gB, (T*)gC, gAp, scr, h0, gh0)
+                    (T*)gd, (T*)gB, (T*)gC, gAp, scr, h0, gh0, (int)(batch * H), 0)
+  MR_SSD_DISPATCH(Dh, N, MR_CALL);
+#undef MR_CALL
+  int rc = check_launch("ssd_seq_bwd_kernel");
+  if (rc) return rc;
+  const int64_t HN = H * N;
+  sum_over_batch_kernel<<<(unsigned)((HN + 255) / 256), 256, 0, st>>>(gAp, batch, HN, gA);
+  return check_launch("sum_over_batch_kernel");
+}
+
+// After the dense-A tensor-core backward: ws = ssd_fallback_ws_bytes, its first part the
+// per-unit grad A partials [B, H, N] that path wrote. A few CTAs recompute the units it
+// marked (rewriting their partials), then the partials are summed over the batch.
+template <typename T>
+int ssd_seq_bwd_marked_launch(const float* gy, const float* gf, const float* ckpt, const void* u,
+                              const void* delta, const void* Bm, const void* Cm, const float* A,
+                              int64_t ash, int64_t asn, int64_t batch, int64_t L, int64_t H, int64_t Dh,
+                              int64_t N, int64_t seg, void* gu, void* gd, void* gB, void* gC, float* gA,
+                              void* ws, const float* h0, float* gh0, cudaStream_t st) {
+  const int64_t units = batch * H;
+  float* gAp = (float*)ws;
+  float* scr = (float*)((char*)ws + ((units * N * sizeof(float) + 255) / 256) * 256);
+  dim3 g((unsigned)(units < kSsdFallbackSlots ? units : kSsdFallbackSlots));
+#define MR_CALL(R_, NK_)                                                                        \
+  ssd_bwd_nk<T, R_>(NK_, g, st, gy, gf, ckpt, (const T*)u, (const T*)delta, (const T*)Bm,         \
+                    (const T*)Cm, A, ash, asn, (int)L, (int)H, (int)Dh, (int)N, (int)seg, (T*)gu,  \
+                    (T*)gd, (T*)gB, (T*)gC, gAp, scr, h0, gh0, (int)units, 1)
   MR_SSD_DISPATCH(Dh, N, MR_CALL);
 #undef MR_CALL
   int rc = check_launch("ssd_seq_bwd_kernel");
@@ -637,7 +684,12 @@ int gla_seq_bwd_launch(const float* gy, const float* gf, const float* ckpt, cons
   template int ssd_seq_fwd_launch<T>(const void*, const void*, const void*, const void*,           \
                                      const float*, int64_t, int64_t, int64_t, int64_t, int64_t,   \
                                      int64_t, int64_t, int64_t, float*, float*, const float*,     \
-                                     cudaStream_t);                                                \
+                                     cudaStream_t, int);                                           \
+  template int ssd_seq_bwd_marked_launch<T>(const float*, const float*, const float*, const void*, \
+                                            const void*, const void*, const void*, const float*,  \
+                                            int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, \
+                                            int64_t, int64_t, void*, void*, void*, void*, float*, \
+                                            void*, const float*, float*, cudaStream_t);            \
   template int ssd_seq_bwd_launch<T>(const float*, const float*, const float*, const void*,        \
                                      const void*, const void*, const void*, const float*, int64_t, \
                                      int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, \

@@ -41,12 +41,27 @@ namespace mr {
 // decay log g_t and (u, B, C) = (v, k, q) - GLA's h[i][j] is SSD's h^T.
 struct SsdRec {
   static constexpr bool kGla = false;
+  static constexpr bool kDense = false;
   static constexpr int NS = 128;
 };
 struct GlaRec {
   static constexpr bool kGla = true;
+  static constexpr bool kDense = false;
   static constexpr int NS = 64;
 };
+// SSD with one decay rate per (head, state column), A_neg [H, N] (ssd.py:62, 96). The
+// per-column decay exp(a_n (D_t - D_s)) (D the cumulative delta in the chunk) is folded
+// into the operands, C~[t, n] = C[t, n] exp(a_n (D_t - c)), B~[s, n] = B[s, n]
+// exp(-a_n (D_s - c)) with c the cumulative delta at the middle of the chunk, so
+// S~ = C~ B~^T carries every decay and the chunk algebra is the one-rate algebra with
+// its scalar decay factors set to one. The factors stay within e^+-kDenseSpan; a chunk
+// whose max_n |a_n| |D_t - c| exceeds it marks its unit for the per-step kernels.
+struct SsdDenseRec {
+  static constexpr bool kGla = false;
+  static constexpr bool kDense = true;
+  static constexpr int NS = 128;
+};
+constexpr float kDenseSpan = 80.f;
 
 namespace ssdc {
 constexpr int Q = 128;                 // chunk length (MMA M for t-rows)
@@ -182,8 +197,8 @@ __global__ void __launch_bounds__(ssdc::NT, 1)
 ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_constant__ CUtensorMap tm_B,
                      const __grid_constant__ CUtensorMap tm_C, const __grid_constant__ CUtensorMap tm_y,
                      const __grid_constant__ CUtensorMap tm_ck, const T* __restrict__ delta,
-                     const float* __restrict__ A, int64_t ash, int L, int H, int seg, float* __restrict__ y,
-                     const float* __restrict__ h0) {
+                     const float* __restrict__ A, int64_t ash, int64_t asn, int L, int H, int seg,
+                     float* __restrict__ y, const float* __restrict__ h0) {
   using namespace ssdc;
   constexpr int NS = Cfg<V>::NS, NB = Cfg<V>::NB;
   constexpr uint32_t STAGE = Cfg<V>::STAGE;
@@ -212,7 +227,8 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bh = blockIdx.x;
   const int b = bh / H, h = bh % H;
-  const float Ah = V::kGla ? 0.f : A[(int64_t)h * ash];
+  // dense: the scalars are the cumulative delta D_t (a rate of one); the rates a_n are per column
+  const float Ah = V::kGla ? 0.f : V::kDense ? 1.f : A[(int64_t)h * ash];
   const int nck = L / Q;
   const int nseg = L / seg;
   const int64_t row0 = (int64_t)b * L;
@@ -230,6 +246,11 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     umma::tmem_alloc(tslot, 512);
     umma::tmem_relinquish();
   }
+  // dense: the rates a_n (n = 0..127) in buffer 0's column-factor slot, which the dense
+  // variant does not use
+  float* sAn = sSc + Q;
+  if constexpr (V::kDense)
+    if (tid < NS) sAn[tid] = A[(int64_t)h * ash + (int64_t)tid * asn];
   // h^T = 0 for the first chunk's Y2 product (rewritten below from an initial state)
   for (int i = tid; i < (int)(TILE / 16); i += NT) reinterpret_cast<int4*>(sHt)[i] = make_int4(0, 0, 0, 0);
   if constexpr (V::kGla)
@@ -269,6 +290,8 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   // row-wise epilogue: 32 of the 128 s-columns of G, 16 of the 64 channels
   const int q4 = warp & 3, jq = warp >> 2;
   const int trow = 32 * q4 + lane;  // row t (or n) this thread owns
+  // dense: the rate of this thread's state row n = trow
+  const float an = V::kDense ? A[(int64_t)h * ash + (int64_t)trow * asn] : 0.f;
   const int ch0 = CH * jq;          // first channel of this thread
   const int cq0 = 32 * jq;          // first s-column of this thread
   const int ct0 = cq0 & 63;         // that column inside its 64-column G tile
@@ -289,13 +312,26 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
       else
         hreg[i] = h0[(bh * DH + ch0 + i) * NS + trow];
     }
-    // its 2-byte copy for chunk 0's Y2 (these threads cover the tile)
+    // its 2-byte copy for chunk 0's Y2 (these threads cover the tile; dense: scaled, once
+    // chunk 0's scalars are known)
+    if constexpr (!V::kDense) {
 #pragma unroll
-    for (int cc = 0; cc < CH / 8; ++cc)
-      *reinterpret_cast<int4*>(sHt + umma::sw128_off(trow, ch0 + 8 * cc)) = pack8<T>(hreg + 8 * cc);
-    fence_proxy_async_smem();
+      for (int cc = 0; cc < CH / 8; ++cc)
+        *reinterpret_cast<int4*>(sHt + umma::sw128_off(trow, ch0 + 8 * cc)) = pack8<T>(hreg + 8 * cc);
+      fence_proxy_async_smem();
+    }
   }
   uint32_t mph = 0, mph2 = 0;
+  // dense: the h^T operand of chunk c's Y2 is exp(a_n c) h (c: chunk c's mid-chunk anchor)
+  auto write_ht_dense = [&](const float* sLamNext) {
+    const float sc = __expf(an * sLamNext[Q / 2 - 1]);
+    float hv[CH];
+#pragma unroll
+    for (int i = 0; i < CH; ++i) hv[i] = sc * hreg[i];
+#pragma unroll
+    for (int cc = 0; cc < CH / 8; ++cc)
+      *reinterpret_cast<int4*>(sHt + umma::sw128_off(trow, ch0 + 8 * cc)) = pack8<T>(hv + 8 * cc);
+  };
 
   // The next chunk's scalars are computed during E1 by four warps whose G
   // columns lie wholly above the diagonal (warps 4, 8, 9, 12: no E1 work),
@@ -303,6 +339,7 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   const int spos = warp == 4 ? 0 : warp == 8 ? 1 : warp == 9 ? 2 : warp == 12 ? 3 : -1;
   const int sst = 32 * spos + lane;
   unsigned short dnext = 0;  // raw delta / gate of step sst of the next chunk to scan
+  float amax = 0.f;          // dense: max_n |a_n| (the scalar warps; sAn is filled before the first barrier)
   auto chunk_scalars = [&](int buf) {
     float* sl = sSc + buf * 2 * Q;
     const float dcur = u16_to_f<T>(dnext);
@@ -322,17 +359,33 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     sl[sst] = lam;
     sDr[buf * Q + sst] = dnext;
     named_barrier_sync(1, 128);
+    if constexpr (V::kDense) {
+      // the operand factors exp(+-a_n (D_t - c)) must stay within e^kDenseSpan (the test
+      // also catches a NaN delta); the column-factor slot holds the rates, not written
+      const float c_mid = sl[Q / 2 - 1];
+      if (__any_sync(0xffffffffu, !(amax * fabsf(lam - c_mid) <= kDenseSpan)) && lane == 0) *sMark = 1;
+      return;
+    }
     // column factor exp(Lam_{s0} - Lam_s) delta_s, s0 = start of s's 16-step block
     const float span = sl[sst & ~15] - lam;
     sl[Q + sst] = __expf(span) * dl;
     if (__any_sync(0xffffffffu, span > 40.f) && lane == 0) sWide[buf] = 1;
   };
   if (spos >= 0) {
+    if constexpr (V::kDense) {
+      for (int k = 0; k < NS / 32; ++k) amax = fmaxf(amax, fabsf(sAn[lane + 32 * k]));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    }
     dnext = ld_pinned_u16(delta + (row0 + sst) * H + h);
     chunk_scalars(0);
     if (nck > 1) dnext = ld_pinned_u16(delta + (row0 + (int64_t)Q + sst) * H + h);
   }
   __syncthreads();
+  if constexpr (V::kDense && kH0) {
+    write_ht_dense(sSc);
+    fence_proxy_async_smem();
+  }
 
   // Prologue of chunk c: U~ = exp(Lam_last - Lam_s) delta_s u_s into shared memory.
   auto prologue = [&](int c) {
@@ -343,7 +396,9 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     mbar_wait(&bar[2 + st], (uint32_t)(c >> 1) & 1u);
     const uint8_t* sU = stg0 + st * STAGE;
     const int s = tid >> 2, part = tid & 3;  // row s, channels 16*part..
-    const float w = __expf(lam_last - sLam[s]) * (V::kGla ? 1.f : u16_to_f<T>(sDr[(c & 1) * Q + s]));
+    const float dls = V::kGla ? 1.f : u16_to_f<T>(sDr[(c & 1) * Q + s]);
+    // dense: the decay lives in B~ (U~ = delta_s u_s)
+    const float w = V::kDense ? dls : __expf(lam_last - sLam[s]) * dls;
 #pragma unroll
     for (int cc = 0; cc < 2; ++cc) {
       const uint32_t off = umma::sw128_off(s, part * 16 + cc * 8);
@@ -352,6 +407,32 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
 #pragma unroll
       for (int i = 0; i < 8; ++i) f[i] *= w;
       *reinterpret_cast<int4*>(sUt + off) = pack8<T>(f);
+    }
+    if constexpr (V::kDense) {
+      // C~ = C exp(a_n (D_s - c)), B~ = B exp(-a_n (D_s - c)) in place (row s, columns
+      // 16*part.. of each 64-wide tile), once the chunk's B and C have landed
+      mbar_wait(&bar[st], (uint32_t)(c >> 1) & 1u);
+      uint8_t* sBt = stg0 + st * STAGE + TILE;
+      uint8_t* sCt = sBt + NB * TILE;
+      const float x0 = sLam[s] - sLam[Q / 2 - 1];
+#pragma unroll
+      for (int j = 0; j < NB; ++j)
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {
+          const int col = part * 16 + cc * 8;
+          const uint32_t off = j * TILE + umma::sw128_off(s, col);
+          float fb[8], fc[8];
+          unpack8<T>(*reinterpret_cast<const int4*>(sBt + off), fb);
+          unpack8<T>(*reinterpret_cast<const int4*>(sCt + off), fc);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float x = sAn[64 * j + col + i] * x0;
+            fc[i] *= __expf(x);
+            fb[i] *= __expf(-x);
+          }
+          *reinterpret_cast<int4*>(sBt + off) = pack8<T>(fb);
+          *reinterpret_cast<int4*>(sCt + off) = pack8<T>(fc);
+        }
     }
     fence_proxy_async_smem();
   };
@@ -425,7 +506,10 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
         float v[16];
         umma::tmem_ld16(tl + s0, v);
         umma::tmem_wait_ld();
-        if (safe) {
+        if constexpr (V::kDense) {  // the decay is inside S~: G = S~ delta_s below the diagonal
+#pragma unroll
+          for (int i = 0; i < 16; ++i) v[i] = (s0 + i <= t) ? v[i] * u16_to_f<T>(sDel[s0 + i]) : 0.f;
+        } else if (safe) {
           const float rf = (t >= s0) ? __expf(lt - sLam[s0]) : 0.f;
           float cf[16];
 #pragma unroll
@@ -474,19 +558,25 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     ++mph2;
     umma::fence_after_sync();
 
-    // ---- state: h <- exp(Lam_last) h + dH (thread: row n = trow, channels ch0..)
+    // ---- state: h <- exp(Lam_last) h + dH (thread: row n = trow, channels ch0..);
+    //      dense: h <- exp(a_n D_last) h + exp(a_n (D_last - c)) dH
     {
-      const float dec = __expf(sLam[Q - 1]);
+      const float dec = __expf((V::kDense ? an : 1.f) * sLam[Q - 1]);
+      const float dec2 = V::kDense ? __expf(an * (sLam[Q - 1] - sLam[Q / 2 - 1])) : 1.f;
       float v[CH];
       umma::tmem_ld16(tl + 192 + ch0, v);
       umma::tmem_wait_ld();
 #pragma unroll
-      for (int i = 0; i < CH; ++i) hreg[i] = dec * hreg[i] + v[i];
+      for (int i = 0; i < CH; ++i) hreg[i] = dec * hreg[i] + dec2 * v[i];
+      if constexpr (V::kDense) {
+        if (c + 1 < nck) write_ht_dense(sSc + ((c + 1) & 1) * 2 * Q);  // the next chunk's scalars are ready
+      } else {
 #pragma unroll
-      for (int cc = 0; cc < CH / 8; ++cc)
-        *reinterpret_cast<int4*>(sHt + umma::sw128_off(trow, ch0 + 8 * cc)) = pack8<T>(hreg + 8 * cc);
+        for (int cc = 0; cc < CH / 8; ++cc)
+          *reinterpret_cast<int4*>(sHt + umma::sw128_off(trow, ch0 + 8 * cc)) = pack8<T>(hreg + 8 * cc);
+      }
     }
-    const float e_t = __expf(sLam[trow]);
+    const float e_t = V::kDense ? 1.f : __expf(sLam[trow]);  // dense: the decay is inside C~
 
     mbar_wait(&bar[4], mph & 1u);
     ++mph;
@@ -538,7 +628,7 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   }
   if (tid == 0) bulk_wait_all();
   __syncthreads();
-  if constexpr (V::kGla)  // mark the unit for the per-step kernel (its y has landed)
+  if constexpr (V::kGla || V::kDense)  // mark the unit for the per-step kernel (its y has landed)
     if (tid == 0 && *sMark) y[((int64_t)b * L * H + h) * DH] = __uint_as_float(kMarkNaN);
   if (warp == 0) umma::tmem_dealloc(tbase, 512);
 }
@@ -552,6 +642,11 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
 // multiple of the chunk; the backward needs one at every chunk start.
 bool ssd_chunk_supported(int dtype, int64_t L, int64_t Dh, int64_t N, int64_t seg, int64_t a_stride_n) {
   return (dtype == MR_BF16 || dtype == MR_F16) && Dh == ssdc::DH && N == SsdRec::NS && a_stride_n == 0 &&
+         L % ssdc::Q == 0 && seg % ssdc::Q == 0 && L <= (int64_t)INT32_MAX / 2;
+}
+// The same shapes with a dense A_neg [H, N] (a_stride_n != 0).
+bool ssd_dense_chunk_supported(int dtype, int64_t L, int64_t Dh, int64_t N, int64_t seg, int64_t a_stride_n) {
+  return (dtype == MR_BF16 || dtype == MR_F16) && Dh == ssdc::DH && N == SsdDenseRec::NS && a_stride_n != 0 &&
          L % ssdc::Q == 0 && seg % ssdc::Q == 0 && L <= (int64_t)INT32_MAX / 2;
 }
 // GLA on the tensor cores: bf16/fp16, Dh = 64 (state 64 x 64), L a multiple
@@ -580,8 +675,8 @@ static int ssd_tmaps(const void* u, const void* Bm, const void* Cm, int64_t batc
 
 template <typename T, typename V>
 static int chunk_fwd_launch(const void* u, const void* delta, const void* Bm, const void* Cm, const float* A,
-                            int64_t ash, int64_t batch, int64_t L, int64_t H, int64_t seg, float* y,
-                            float* ckpt, const float* h0, cudaStream_t st) {
+                            int64_t ash, int64_t asn, int64_t batch, int64_t L, int64_t H, int64_t seg,
+                            float* y, float* ckpt, const float* h0, cudaStream_t st) {
   constexpr int NS = V::NS;
   constexpr size_t SMEM = ssdc::Cfg<V>::SMEM;
   CUtensorMap mu, mB, mC, my, mck;
@@ -601,16 +696,27 @@ static int chunk_fwd_launch(const void* u, const void* delta, const void* Bm, co
   auto k = h0 != nullptr ? ssd_chunk_fwd_kernel<T, V, true> : ssd_chunk_fwd_kernel<T, V, false>;
   const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM);
   if (e != cudaSuccess) return set_error(MR_E_LAUNCH, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-  k<<<(unsigned)(batch * H), ssdc::NT, SMEM, st>>>(mu, mB, mC, my, mck, (const T*)delta, A, ash, (int)L, (int)H,
-                                                   (int)seg, y, h0);
-  return check_launch(V::kGla ? "gla_chunk_fwd_kernel" : "ssd_chunk_fwd_kernel");
+  k<<<(unsigned)(batch * H), ssdc::NT, SMEM, st>>>(mu, mB, mC, my, mck, (const T*)delta, A, ash, asn, (int)L,
+                                                   (int)H, (int)seg, y, h0);
+  return check_launch(V::kGla ? "gla_chunk_fwd_kernel" : V::kDense ? "ssd_dense_chunk_fwd_kernel"
+                                                                   : "ssd_chunk_fwd_kernel");
 }
 
 template <typename T>
 int ssd_chunk_fwd_launch(const void* u, const void* delta, const void* Bm, const void* Cm, const float* A,
                          int64_t ash, int64_t batch, int64_t L, int64_t H, int64_t seg, float* y,
                          float* ckpt, const float* h0, cudaStream_t st) {
-  return chunk_fwd_launch<T, SsdRec>(u, delta, Bm, Cm, A, ash, batch, L, H, seg, y, ckpt, h0, st);
+  return chunk_fwd_launch<T, SsdRec>(u, delta, Bm, Cm, A, ash, 0, batch, L, H, seg, y, ckpt, h0, st);
+}
+
+// SSD with a dense A_neg [H, N] (rates A[h * ash + n * asn]) on the tensor cores; a
+// unit whose chunk decays span more than e^kDenseSpan is marked (NaN in y[b, 0, h, 0])
+// for the per-step kernel.
+template <typename T>
+int ssd_dense_chunk_fwd_launch(const void* u, const void* delta, const void* Bm, const void* Cm, const float* A,
+                               int64_t ash, int64_t asn, int64_t batch, int64_t L, int64_t H, int64_t seg,
+                               float* y, float* ckpt, const float* h0, cudaStream_t st) {
+  return chunk_fwd_launch<T, SsdDenseRec>(u, delta, Bm, Cm, A, ash, asn, batch, L, H, seg, y, ckpt, h0, st);
 }
 
 // GLA forward: (u, B, C, decay input) = (v, k, q, gates); y and the
@@ -619,7 +725,7 @@ template <typename T>
 int gla_chunk_fwd_launch(const void* q, const void* k, const void* v, const void* gates, int64_t batch,
                          int64_t L, int64_t H, int64_t seg, float* y, float* ckpt, const float* h0,
                          cudaStream_t st) {
-  return chunk_fwd_launch<T, GlaRec>(v, gates, k, q, nullptr, 0, batch, L, H, seg, y, ckpt, h0, st);
+  return chunk_fwd_launch<T, GlaRec>(v, gates, k, q, nullptr, 0, 0, batch, L, H, seg, y, ckpt, h0, st);
 }
 
 template int ssd_chunk_fwd_launch<__nv_bfloat16>(const void*, const void*, const void*, const void*,
@@ -628,6 +734,12 @@ template int ssd_chunk_fwd_launch<__nv_bfloat16>(const void*, const void*, const
 template int ssd_chunk_fwd_launch<__half>(const void*, const void*, const void*, const void*, const float*,
                                           int64_t, int64_t, int64_t, int64_t, int64_t, float*, float*,
                                           const float*, cudaStream_t);
+template int ssd_dense_chunk_fwd_launch<__nv_bfloat16>(const void*, const void*, const void*, const void*,
+                                                       const float*, int64_t, int64_t, int64_t, int64_t, int64_t,
+                                                       int64_t, float*, float*, const float*, cudaStream_t);
+template int ssd_dense_chunk_fwd_launch<__half>(const void*, const void*, const void*, const void*, const float*,
+                                                int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, float*,
+                                                float*, const float*, cudaStream_t);
 template int gla_chunk_fwd_launch<__nv_bfloat16>(const void*, const void*, const void*, const void*, int64_t,
                                                  int64_t, int64_t, int64_t, float*, float*, const float*,
                                                  cudaStream_t);
@@ -707,9 +819,10 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
                      const __grid_constant__ CUtensorMap tm_gB, const __grid_constant__ CUtensorMap tm_gC,
                      const float* __restrict__ ckpt, const float* __restrict__ gy,
                      const __grid_constant__ CUtensorMap tm_d, int dmap, const float* __restrict__ gfinal,
-                     const T* __restrict__ delta, const float* __restrict__ A, int64_t ash, int L, int H, int seg,
-                     T* __restrict__ gdelta, float* __restrict__ gA_part, const float* __restrict__ h0,
-                     float* __restrict__ gh0) {
+                     const T* __restrict__ delta, const float* __restrict__ A, int64_t ash, int64_t asn, int L,
+                     int H, int seg, T* __restrict__ gdelta, float* __restrict__ gA_part,
+                     const float* __restrict__ h0, float* __restrict__ gh0, const T* __restrict__ Bg,
+                     const T* __restrict__ Cg) {
   using namespace ssdb;
   constexpr int NS = Cfg<V>::NS, NB = Cfg<V>::NB;
   constexpr int NCT = NS / CQ;  // state columns n per thread in epilogue 3 (16-column blocks: NCT / 16)
@@ -734,6 +847,11 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   float* sUR = sM + CQ * Q;                           // [CQ][Q] u_t . r_t partials
   float* sRed = sUR + CQ * Q;                         // 64 floats of reduction scratch
   // sRed: [0,12) grad_delta warp sums, [32,48) <Psi, h0> warp partials
+  // dense (no Z column sums, no gy.Y2 / u.R2 terms): sCol holds the rates a_n [0, 128) and
+  // the D_last <Psi_n, h_end_n> sums of grad A_n [128, 256); sRow the E3 row partials
+  // sum_n a_n v[t, n]; sQ the grad A_n column partials of the four row quarters at the end
+  float* sAn = sCol;
+  float* sGA = sCol + Q;
   uint8_t* sm = smem_raw + SMALL_PAD;
   uint8_t* tU = sm;
   uint8_t* tB = tU + TILE;        // NB tiles
@@ -750,7 +868,8 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bh = blockIdx.x;
   const int b = bh / H, h = bh % H;
-  const float Ah = V::kGla ? 0.f : A[(int64_t)h * ash];
+  // dense: the scalars are the cumulative delta D_t (a rate of one); the rates a_n are per column
+  const float Ah = V::kGla ? 0.f : V::kDense ? 1.f : A[(int64_t)h * ash];
   const int nck = L / Q;
   const int nseg = L / seg;
   const int64_t row0 = (int64_t)b * L;
@@ -771,8 +890,16 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   const int ct0 = cq0 & 63;        // that column inside its 64-column tile
   if (tid == 0) {
     for (int i = 0; i < 4; ++i) mbar_init(&bar[i], 1);
-    sWide[2] = 0;  // GLA: a gate outside the tensor-core range
+    sWide[2] = 0;  // GLA: a gate outside the tensor-core range; dense: a chunk beyond kDenseSpan
     fence_mbar_init();
+  }
+  // dense: the rate of this thread's state row n = row (Psi), the rates in shared memory
+  const float an = V::kDense ? A[(int64_t)h * ash + (int64_t)row * asn] : 0.f;
+  if constexpr (V::kDense) {
+    if (tid < NS) {
+      sAn[tid] = A[(int64_t)h * ash + (int64_t)tid * asn];
+      sGA[tid] = 0.f;
+    }
   }
   if (warp == 0) {
     umma::tmem_alloc(tslot, 512);
@@ -791,9 +918,22 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   }
   if constexpr (V::kGla)
     for (int i = tid; i < (int)(TILE / 16); i += NT) reinterpret_cast<int4*>(tZero)[i] = make_int4(0, 0, 0, 0);
+  // dense: the 2-byte Psi operand is Psi~ = exp(a_n (D_last - c)) Psi (written once the
+  // chunk's scalars are known)
+  auto write_psi_dense = [&](const float* sLamC) {
+    const float sc = __expf(an * (sLamC[Q - 1] - sLamC[Q / 2 - 1]));
+    float pv[CH];
 #pragma unroll
-  for (int cc = 0; cc < CH / 8; ++cc)
-    *reinterpret_cast<int4*>(tPSI + umma::sw128_off(row, ch0 + 8 * cc)) = pack8<T>(psi + 8 * cc);
+    for (int i = 0; i < CH; ++i) pv[i] = sc * psi[i];
+#pragma unroll
+    for (int cc = 0; cc < CH / 8; ++cc)
+      *reinterpret_cast<int4*>(tPSI + umma::sw128_off(row, ch0 + 8 * cc)) = pack8<T>(pv + 8 * cc);
+  };
+  if constexpr (!V::kDense) {
+#pragma unroll
+    for (int cc = 0; cc < CH / 8; ++cc)
+      *reinterpret_cast<int4*>(tPSI + umma::sw128_off(row, ch0 + 8 * cc)) = pack8<T>(psi + 8 * cc);
+  }
   fence_proxy_async_smem();
   __syncthreads();
   umma::fence_after_sync();
@@ -851,6 +991,7 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   load_gy(nck - 1);
   if (nck > 1 || has_h0) load_h0(nck - 1);
   float gA_acc = 0.f;
+  float gAc[NCT / 16] = {};  // dense: grad A_n column sums of this warp's rows (epilogue 3 columns)
   uint32_t tph = 0, mph = 0, mph2 = 0;
 
   auto sum4 = [&](const float* p, int i) { return (p[i] + p[Q + i]) + (p[2 * Q + i] + p[3 * Q + i]); };
@@ -860,6 +1001,13 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   // that box (H % 8 != 0 or a misaligned pointer) the warp loads it directly.
   constexpr int kScalarWarp = 9;  // off sub-partition 0, whose thread 0 blocks while it issues the MMAs
   uint32_t dph = 0;
+  float amax = 0.f;  // dense: max_n |a_n| (the scalar warp)
+  if constexpr (V::kDense)
+    if (warp == kScalarWarp) {
+      for (int k = 0; k < NS / 32; ++k) amax = fmaxf(amax, fabsf(sAn[lane + 32 * k]));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    }
   auto issue_delta = [&](int c) {  // thread 0
     mbar_arrive_expect_tx(&bar[3], DT_BYTES);
     tma_load_2d(sDt, &tm_d, h & ~7, (int)(row0 + (int64_t)c * Q), &bar[3]);
@@ -910,6 +1058,21 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
       ds[i] += dx;
     }
     const float lam_last = __shfl_sync(0xffffffffu, lam[3], 31);
+    if constexpr (V::kDense) {
+      // lam = D (cumulative delta): the operand factors exp(+-a_n (D_t - c)) must stay
+      // within e^kDenseSpan (the test also catches a NaN delta)
+      const float c_mid = __shfl_sync(0xffffffffu, lam[3], Q / 8 - 1);  // D at step Q/2 - 1
+      bool out = false;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) out |= !(amax * fabsf(lam[i] - c_mid) <= kDenseSpan);
+      if (__any_sync(0xffffffffu, out) && lane == 0) sWide[2] = 1;
+      float4* sl4 = reinterpret_cast<float4*>(sl) + lane;
+      sl4[0] = make_float4(lam[0], lam[1], lam[2], lam[3]);
+      sl4[Q / 4] = make_float4(dc[0], dc[1], dc[2], dc[3]);
+      sl4[4 * Q / 4] = make_float4(lam[0], lam[1], lam[2], lam[3]);
+      if (lane == 0) sWide[buf] = 0;
+      return;
+    }
     const float lam_blk = __shfl_sync(0xffffffffu, lam[0], lane & ~3);  // Lam at the 16-step block start
     float w[4], el[4], cf[4];
     bool wide = false;
@@ -956,6 +1119,7 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   if (dmap && tid == 0) issue_delta(nck - 1);
   if (warp == kScalarWarp) chunk_scalars(delta_bits(nck - 1), (nck - 1) & 1);
   __syncthreads();
+  if constexpr (V::kDense) write_psi_dense(sSc + ((nck - 1) & 1) * NSC * Q);
   if (dmap && tid == 0 && nck > 1) issue_delta(nck - 2);
 
   for (int c = nck - 1; c >= 0; --c) {
@@ -978,23 +1142,94 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     __syncthreads();
     const bool safe = sWide[c & 1] == 0;
     float psih0 = 0.f;
+    if constexpr (V::kDense) {
+      // Rows r are states n (h0, Psi) and steps s (gy). pe_n = <Psi_n, h_end_n> with Psi the
+      // adjoint at the chunk's end and h_end its end state: the next chunk's start state,
+      // still in tH0 as exp(a_n c') h (c' that chunk's anchor), or the final checkpoint;
+      // Psi~ = exp(a_n (D_last - c)) Psi in tPSI. psih0 collects sum_n a_n pe_n.
+      const float cc0 = sLam[Q / 2 - 1], dlast = sLam[Q - 1];
+      const float* sLamN = sSc + ((c + 1) & 1) * NSC * Q;  // chunk c + 1 (its scalars are still there)
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const int r = cr0 + 32 * k;
-      const uint32_t off = umma::sw128_off(r, cd0);
-      const float4 hv = ((c > 0 || has_h0) && r < NS) ? h0v[k < NS / 32 ? k : 0] : make_float4(0.f, 0.f, 0.f, 0.f);
-      *reinterpret_cast<uint2*>(tH0 + off) = pack4<T>(hv);
-      float pf[4];
-      unpack4<T>(*reinterpret_cast<const uint2*>(tPSI + off), pf);
-      psih0 += pf[0] * hv.x + pf[1] * hv.y + pf[2] * hv.z + pf[3] * hv.w;
-      const float4 g = gyv[k];
-      const uint2 hi = pack4<T>(g);
-      float hf[4];
-      unpack4<T>(hi, hf);
-      const float el = sEL[r];
-      *reinterpret_cast<uint2*>(tGY + off) = hi;
-      *reinterpret_cast<uint2*>(tGYt + off) = pack4<T>(make_float4(g.x - hf[0], g.y - hf[1], g.z - hf[2], g.w - hf[3]));
-      *reinterpret_cast<uint2*>(tEG + off) = pack4<T>(make_float4(el * g.x, el * g.y, el * g.z, el * g.w));
+      for (int k = 0; k < 4; ++k) {
+        const int r = cr0 + 32 * k;
+        const uint32_t off = umma::sw128_off(r, cd0);
+        const float a_r = sAn[r];
+        float he[4], pf[4];
+        if (c == nck - 1) {
+          const float4 f = *reinterpret_cast<const float4*>(
+              ckpt + ((((int64_t)b * nseg + nseg - 1) * H + h) * NS + r) * DH + cd0);
+          he[0] = f.x, he[1] = f.y, he[2] = f.z, he[3] = f.w;
+        } else {
+          unpack4<T>(*reinterpret_cast<const uint2*>(tH0 + off), he);
+          const float un = __expf(-a_r * sLamN[Q / 2 - 1]);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) he[i] *= un;
+        }
+        unpack4<T>(*reinterpret_cast<const uint2*>(tPSI + off), pf);
+        float pe = (pf[0] * he[0] + pf[1] * he[1]) + (pf[2] * he[2] + pf[3] * he[3]);
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) pe += __shfl_xor_sync(0xffffffffu, pe, o);  // the row's 16 threads
+        pe *= __expf(-a_r * (dlast - cc0));
+        if ((lane & 15) == 0) {
+          sGA[r] += dlast * pe;
+          psih0 += a_r * pe;
+        }
+        const float4 hv = ((c > 0 || has_h0) && r < NS) ? h0v[k < NS / 32 ? k : 0] : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float sc = __expf(a_r * cc0);
+        *reinterpret_cast<uint2*>(tH0 + off) = pack4<T>(make_float4(sc * hv.x, sc * hv.y, sc * hv.z, sc * hv.w));
+        const float4 g = gyv[k];
+        const uint2 hi = pack4<T>(g);
+        float hf[4];
+        unpack4<T>(hi, hf);
+        *reinterpret_cast<uint2*>(tGY + off) = hi;
+        *reinterpret_cast<uint2*>(tGYt + off) =
+            pack4<T>(make_float4(g.x - hf[0], g.y - hf[1], g.z - hf[2], g.w - hf[3]));
+      }
+      // C~ = C exp(a_n (D_s - c)), B~ = B exp(-a_n (D_s - c)) in place (row s, columns
+      // 16*part.. of each 64-wide tile), once the chunk's u, B, C have landed
+      mbar_wait(&bar[0], tph & 1u);
+      ++tph;
+      {
+        const int s = tid >> 2, part = tid & 3;
+        const float x0 = sLam[s] - cc0;
+#pragma unroll
+        for (int j = 0; j < NB; ++j)
+#pragma unroll
+          for (int cc = 0; cc < 2; ++cc) {
+            const int col = part * 16 + cc * 8;
+            const uint32_t off = j * TILE + umma::sw128_off(s, col);
+            float fb[8], fc[8];
+            unpack8<T>(*reinterpret_cast<const int4*>(tB + off), fb);
+            unpack8<T>(*reinterpret_cast<const int4*>(tC + off), fc);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const float x = sAn[64 * j + col + i] * x0;
+              fc[i] *= __expf(x);
+              fb[i] *= __expf(-x);
+            }
+            *reinterpret_cast<int4*>(tB + off) = pack8<T>(fb);
+            *reinterpret_cast<int4*>(tC + off) = pack8<T>(fc);
+          }
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int r = cr0 + 32 * k;
+        const uint32_t off = umma::sw128_off(r, cd0);
+        const float4 hv = ((c > 0 || has_h0) && r < NS) ? h0v[k < NS / 32 ? k : 0] : make_float4(0.f, 0.f, 0.f, 0.f);
+        *reinterpret_cast<uint2*>(tH0 + off) = pack4<T>(hv);
+        float pf[4];
+        unpack4<T>(*reinterpret_cast<const uint2*>(tPSI + off), pf);
+        psih0 += pf[0] * hv.x + pf[1] * hv.y + pf[2] * hv.z + pf[3] * hv.w;
+        const float4 g = gyv[k];
+        const uint2 hi = pack4<T>(g);
+        float hf[4];
+        unpack4<T>(hi, hf);
+        const float el = sEL[r];
+        *reinterpret_cast<uint2*>(tGY + off) = hi;
+        *reinterpret_cast<uint2*>(tGYt + off) = pack4<T>(make_float4(g.x - hf[0], g.y - hf[1], g.z - hf[2], g.w - hf[3]));
+        *reinterpret_cast<uint2*>(tEG + off) = pack4<T>(make_float4(el * g.x, el * g.y, el * g.z, el * g.w));
+      }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) psih0 += __shfl_xor_sync(0xffffffffu, psih0, o);
@@ -1007,8 +1242,10 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     //      rewrites), then Y2, R2; GLA (exp(Lam) gy in its own tile): S, P, then dPsi^T, Y2, R2
     if (tid == 0) {
       bulk_wait_read<0>();
-      mbar_wait(&bar[0], tph & 1u);
-      ++tph;
+      if constexpr (!V::kDense) {  // dense: every thread waited in P0 (it transformed B and C)
+        mbar_wait(&bar[0], tph & 1u);
+        ++tph;
+      }
       umma::fence_after_sync();
       const uint32_t aU = smem_u32(tU), aB = smem_u32(tB), aC = smem_u32(tC), aGY = smem_u32(tGY),
                      aEG = smem_u32(tEG), aPSI = smem_u32(tPSI), aH0 = smem_u32(tH0), aLo = smem_u32(tGYt);
@@ -1016,9 +1253,11 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
         // C^T as an MN-major A operand of M = 128 state rows: its second 64-row block is
         // C's second tile (SSD) or the zero tile (GLA, N = 64)
         const uint32_t lboC = V::kGla ? smem_u32(tZero) - aC : TILE;
+        // dense: dPsi'^T = C~^T gy (the decay is inside C~; gy's 2-byte high part)
+        const uint32_t aG = V::kDense ? aGY : aEG;
 #pragma unroll
         for (int k = 0; k < 8; ++k)
-          umma::mma_f16(tbase + 384, umma::sdesc_mn(aC + k * 2048, lboC), umma::sdesc_mn(aEG + k * 2048, TILE),
+          umma::mma_f16(tbase + 384, umma::sdesc_mn(aC + k * 2048, lboC), umma::sdesc_mn(aG + k * 2048, TILE),
                         id64MM, k > 0);
       };
       if constexpr (!V::kGla) mma_dpsi();
@@ -1038,7 +1277,8 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
 #pragma unroll
       for (int k = 0; k < NS / 16; ++k) {
         const uint32_t ko = (k >> 2) * TILE + (k & 3) * 32;
-        umma::mma_f16(tbase + 256, umma::sdesc_k(aC + ko), umma::sdesc_mn(aH0 + k * 2048, TILE), id64KM, k > 0);
+        if constexpr (!V::kDense)  // Y2 feeds only the scalar-decay derivative
+          umma::mma_f16(tbase + 256, umma::sdesc_k(aC + ko), umma::sdesc_mn(aH0 + k * 2048, TILE), id64KM, k > 0);
         umma::mma_f16(tbase + 320, umma::sdesc_k(aB + ko), umma::sdesc_mn(aPSI + k * 2048, TILE), id64KM, k > 0);
       }
       umma::commit(&bar[2]);
@@ -1062,7 +1302,7 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
           *reinterpret_cast<int4*>(gp + umma::sw128_off(s, ct0 + 8 * j)) = make_int4(0, 0, 0, 0);
           *reinterpret_cast<int4*>(hh + umma::sw128_off(s, ct0 + 8 * j)) = make_int4(0, 0, 0, 0);
         }
-        sCol[q4 * Q + cq0 + lane] = 0.f;
+        if constexpr (!V::kDense) sCol[q4 * Q + cq0 + lane] = 0.f;
       } else {
 #pragma unroll
         for (int cb = 0; cb < 2; ++cb) {
@@ -1073,7 +1313,8 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
             *reinterpret_cast<int4*>(gp + o1) = make_int4(0, 0, 0, 0);
             *reinterpret_cast<int4*>(hh + o0) = make_int4(0, 0, 0, 0);
             *reinterpret_cast<int4*>(hh + o1) = make_int4(0, 0, 0, 0);
-            if ((lane & 1) == 0) sCol[q4 * Q + t0 + (lane >> 1)] = 0.f;
+            if constexpr (!V::kDense)
+              if ((lane & 1) == 0) sCol[q4 * Q + t0 + (lane >> 1)] = 0.f;
             continue;
           }
           float sv[16], pv[16];
@@ -1082,7 +1323,10 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
           umma::tmem_wait_ld();
           // E[s, t] (0 above the diagonal); blocks wholly below it skip the mask
           float e[16];
-          if (safe) {
+          if constexpr (V::kDense) {  // the decay is inside S~: E is the mask
+#pragma unroll
+            for (int i = 0; i < 16; ++i) e[i] = (t0 + i <= s) ? 1.f : 0.f;
+          } else if (safe) {
             const float rf = (s >= t0) ? __expf(ls - sLam[t0]) : 0.f;
 #pragma unroll
             for (int i = 0; i < 16; i += 4)
@@ -1120,18 +1364,23 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
           *reinterpret_cast<int4*>(hh + o0) = pack8<T>(pv);
           *reinterpret_cast<int4*>(hh + o1) = pack8<T>(pv + 8);
           // colsum Z over this warp's 32 rows s (quarter q4), one partial per quarter
-          const float cz = warp_colsum16(z, lane);
-          if ((lane & 1) == 0) sCol[q4 * Q + t0 + (lane >> 1)] = cz;
+          // (dense: the decay derivative comes from epilogue 3 instead; sCol holds the rates)
+          if constexpr (!V::kDense) {
+            const float cz = warp_colsum16(z, lane);
+            if ((lane & 1) == 0) sCol[q4 * Q + t0 + (lane >> 1)] = cz;
+          }
         }
       }
-      sRow[jq * Q + s] = rz;
+      if constexpr (!V::kDense) sRow[jq * Q + s] = rz;
       fence_proxy_async_smem();
 
       mbar_wait(&bar[2], mph2 & 1u);
       ++mph2;
       umma::fence_after_sync();
       // gy_s . Y2_s (gy as its hi + lo parts) and u_s . R2_s over this thread's channels
+      // (dense: not needed, Y2 is not formed)
       float y2[CH], r2[CH];
+      if constexpr (!V::kDense) {
       umma::tmem_ld16(tl + 256 + ch0, y2);
       umma::tmem_ld16(tl + 320 + ch0, r2);
       umma::tmem_wait_ld();
@@ -1150,12 +1399,15 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
       }
       sQ[jq * Q + s] = qa;
       sM[jq * Q + s] = ma;
+      }
       // Psi (row n = row) <- exp(Lam_last) Psi + dPsi; the 2-byte copy is replaced after batch 3
+      // (dense: Psi <- exp(a_n D_last) Psi + exp(a_n c) dPsi')
       umma::tmem_ld16(tl + 384 + ch0, y2);
       umma::tmem_wait_ld();
-      const float dec = __expf(sLam[Q - 1]);
+      const float dec = __expf((V::kDense ? an : 1.f) * sLam[Q - 1]);
+      const float dec2 = V::kDense ? __expf(an * sLam[Q / 2 - 1]) : 1.f;
 #pragma unroll
-      for (int i = 0; i < CH; ++i) psi[i] = dec * psi[i] + y2[i];
+      for (int i = 0; i < CH; ++i) psi[i] = dec * psi[i] + dec2 * y2[i];
     }
     umma::fence_before_sync();
     __syncthreads();
@@ -1201,7 +1453,7 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
         for (int i = 0; i < CH; ++i) r1[i] += r2[i];
         umma::tmem_ld16(tl + 320 + ch0, r2);
         umma::tmem_wait_ld();
-        const float f2 = __expf(sLam[Q - 1] - lt);
+        const float f2 = V::kDense ? 1.f : __expf(sLam[Q - 1] - lt);  // dense: R2 = B~ Psi~^T carries it
         float ur = 0.f;
 #pragma unroll
         for (int cc = 0; cc < CH / 8; ++cc) {
@@ -1220,7 +1472,7 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
       }
       // fold epilogue 1's four partials of one array per thread into its slot 0
       // (rowsum Z, colsum Z, gy.Y2, u.R2 for jq = 0..3), shortening grad_delta
-      {
+      if constexpr (!V::kDense) {
         float* arr = jq == 0 ? sRow : jq == 1 ? sCol : jq == 2 ? sQ : sM;
         arr[t] = sum4(arr, t);
       }
@@ -1244,10 +1496,8 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     // ---- while batch 3 completes: grad_delta and grad_A (warps 4-7, thread t)
     // dLam_t = x_t + [t = last] lastv with x_t = rowsum Z - colsum Z + exp(Lam_t) q_t - w_t m_t,
     // lastv = exp(Lam_last) <Psi, h0> + sum_t w_t m_t; grad_delta_t = A sum_{t' >= t} dLam_t' + u_t.r_t
-    if (warp >= 4 && warp < 8) {
+    auto grad_delta_phase = [&](float x, float wm) {  // warps 4-7, thread t = tid - 128
       const int t = tid - 128, gw = warp - 4;
-      const float wm = sW[t] * sM[t];
-      const float x = sRow[t] - sCol[t] + sEL[t] * sQ[t] - wm;
       float suf = x, swm = wm, sxd = x * sD[t];
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -1274,17 +1524,24 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
       }
 #pragma unroll
       for (int v = 0; v < NT / 32; ++v) psi_h0 += sRed[32 + v];
-      const float lastv = sEL[Q - 1] * psi_h0 + sum_wm;
+      // dense: psi_h0 is sum_n a_n <Psi_n, h_end_n> itself and x already carries the rates
+      const float lastv = V::kDense ? psi_h0 : sEL[Q - 1] * psi_h0 + sum_wm;
       const float dlam = suf + later + lastv;  // dL/d(log decay of step t)
       float g;
       if constexpr (V::kGla) {
         g = dlam / sD[t];  // dL/dg_t = dL/dlog(g_t) / g_t (sD holds the gate)
       } else {
-        if (t == 0) gA_acc += sum_xd + lastv * sD[Q - 1];
+        if (!V::kDense && t == 0) gA_acc += sum_xd + lastv * sD[Q - 1];
         g = Ah * dlam + sum4(sUR, t);
       }
       gdelta[(row0 + (int64_t)c * Q + t) * H + h] = from_f<T>(g);
-    }
+    };
+    if constexpr (!V::kDense)
+      if (warp >= 4 && warp < 8) {
+        const int t = tid - 128;
+        const float wm = sW[t] * sM[t];
+        grad_delta_phase(sRow[t] - sCol[t] + sEL[t] * sQ[t] - wm, wm);
+      }
     mbar_wait(&bar[2], mph2 & 1u);
     ++mph2;
     umma::fence_after_sync();
@@ -1296,7 +1553,60 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
 
     // ---- epilogue 3: stage grad_B (row t) in GP, grad_C (row s) in HH (columns n = NCT * jq..);
     //      new Psi^T
-    {
+    if constexpr (V::kDense) {
+      // grad_B = exp(-a_n (D_t - c)) (gB1 + delta_t gB2), grad_C = exp(a_n (D_t - c)) (gC1 + gC2);
+      // v[t, n] = C grad_C - B grad_B (= dL/d(a_n D_t), from the inputs' own values, read
+      // back from global memory as the tiles already stream the next chunk) gives the
+      // decay derivative of step t (sum_n a_n v, row partials) and of a_n (sum_t D_t v,
+      // column sums over this warp's rows accumulated across chunks)
+      const int t = row;
+      const float dt = sDel[t], Dt = sLam[t], x0 = Dt - sLam[Q / 2 - 1];
+      const int nc0 = NCT * jq;
+      uint8_t* gbt = tGP + (nc0 >> 6) * TILE;
+      uint8_t* gct = tHH + (nc0 >> 6) * TILE;
+      const int64_t grow = ((row0 + (int64_t)c * Q + t) * H + h) * NS;
+      int4 braw[NCT / 8], craw[NCT / 8];
+#pragma unroll
+      for (int i = 0; i < NCT / 8; ++i) {
+        braw[i] = __ldg(reinterpret_cast<const int4*>(Bg + grow + nc0) + i);
+        craw[i] = __ldg(reinterpret_cast<const int4*>(Cg + grow + nc0) + i);
+      }
+      float ra = 0.f;
+#pragma unroll
+      for (int cb = 0; cb < NCT / 16; ++cb) {
+        const int col = nc0 + 16 * cb;
+        const uint32_t o0 = umma::sw128_off(t, (col & 63)), o1 = umma::sw128_off(t, (col & 63) + 8);
+        float gb[16], gc[16], v2[16], z[16];
+        umma::tmem_ld16(tl + 0 + col, gb);
+        umma::tmem_ld16(tl + 2 * NS + col, v2);
+        umma::tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) gb[i] += dt * v2[i];
+        umma::tmem_ld16(tl + NS + col, gc);
+        umma::tmem_ld16(tl + 3 * NS + col, v2);
+        umma::tmem_wait_ld();
+        const T* bq = reinterpret_cast<const T*>(&braw[2 * cb]);  // 16 consecutive values
+        const T* cq = reinterpret_cast<const T*>(&craw[2 * cb]);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float a = sAn[col + i];
+          const float x = a * x0;
+          gc[i] = (gc[i] + v2[i]) * __expf(x);
+          gb[i] *= __expf(-x);
+          const float vv = to_f(cq[i]) * gc[i] - to_f(bq[i]) * gb[i];
+          ra += a * vv;
+          z[i] = Dt * vv;
+        }
+        *reinterpret_cast<int4*>(gbt + o0) = pack8<T>(gb);
+        *reinterpret_cast<int4*>(gbt + o1) = pack8<T>(gb + 8);
+        *reinterpret_cast<int4*>(gct + o0) = pack8<T>(gc);
+        *reinterpret_cast<int4*>(gct + o1) = pack8<T>(gc + 8);
+        gAc[cb] += warp_colsum16(z, lane);
+      }
+      sRow[jq * Q + t] = ra;
+      if (c > 0) write_psi_dense(sSc + ((c - 1) & 1) * NSC * Q);  // Psi~ of the next chunk
+      fence_proxy_async_smem();
+    } else {
       const int t = row;
       const float wt = sW[t], et = sEL[t];
       const int nc0 = NCT * jq;  // first state column of this thread
@@ -1341,12 +1651,27 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
       for (int j = 0; j < NB; ++j) tma_store_3d(&tm_gB, 64 * j, h, z, tGP + j * TILE);
       bulk_commit();
     }
+    // dense: grad_delta once epilogue 3's row partials are in (x_t = sum_n a_n v[t, n])
+    if constexpr (V::kDense)
+      if (warp >= 4 && warp < 8) {
+        const int t = tid - 128;
+        grad_delta_phase((sRow[t] + sRow[Q + t]) + (sRow[2 * Q + t] + sRow[3 * Q + t]), 0.f);
+      }
   }
-  if constexpr (!V::kGla)
+  if constexpr (!V::kGla && !V::kDense)
     if (tid == 128) gA_part[bh] = gA_acc;  // step t = 0 of the grad_delta warps
+  if constexpr (V::kDense) {
+    // grad A_n of this unit: the four row quarters' column sums plus the end-state terms
+    const int nc0 = NCT * jq;
+    if ((lane & 1) == 0)
+#pragma unroll
+      for (int cb = 0; cb < NCT / 16; ++cb) sQ[q4 * Q + nc0 + 16 * cb + (lane >> 1)] = gAc[cb];
+    __syncthreads();
+    if (tid < NS) gA_part[(int64_t)bh * NS + tid] = (sQ[tid] + sQ[Q + tid]) + (sQ[2 * Q + tid] + sQ[3 * Q + tid]) + sGA[tid];
+  }
   if (tid == 0) bulk_wait_all();
   __syncthreads();
-  if constexpr (V::kGla)  // mark the unit for the per-step kernel
+  if constexpr (V::kGla || V::kDense)  // mark the unit for the per-step kernel
     if (tid == 0 && sWide[2]) gdelta[row0 * H + h] = from_f<T>(__uint_as_float(kMarkNaN));
   // the adjoint carried past chunk 0 is the gradient of the initial state
   if (kH0 && gh0 != nullptr && row < NS) {
@@ -1374,9 +1699,9 @@ __global__ void ssd_ga_head_kernel(const float* __restrict__ part, int B, int H,
 
 template <typename T, typename V>
 static int chunk_bwd_launch(const float* gy, const float* gf, const float* ckpt, const void* u, const void* delta,
-                            const void* Bm, const void* Cm, const float* A, int64_t ash, int64_t batch, int64_t L,
-                            int64_t H, int64_t seg, void* gu, void* gd, void* gB, void* gC, float* ws,
-                            const float* h0, float* gh0, cudaStream_t st) {
+                            const void* Bm, const void* Cm, const float* A, int64_t ash, int64_t asn,
+                            int64_t batch, int64_t L, int64_t H, int64_t seg, void* gu, void* gd, void* gB,
+                            void* gC, float* ws, const float* h0, float* gh0, cudaStream_t st) {
   constexpr size_t SMEM = ssdb::Cfg<V>::SMEM;
   CUtensorMap mu, mB, mC, mgu, mgB, mgC, md;
   if (int rc = ssd_tmaps<T, V::NS>(u, Bm, Cm, batch, L, H, &mu, &mB, &mC)) return rc;
@@ -1392,9 +1717,10 @@ static int chunk_bwd_launch(const float* gy, const float* gf, const float* ckpt,
   const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM);
   if (e != cudaSuccess) return set_error(MR_E_LAUNCH, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
   k<<<(unsigned)(batch * H), ssdb::NT, SMEM, st>>>(mu, mB, mC, mgu, mgB, mgC, ckpt, gy, md, dmap, gf,
-                                                   (const T*)delta, A, ash, (int)L, (int)H, (int)seg, (T*)gd, ws,
-                                                   h0, gh0);
-  return check_launch(V::kGla ? "gla_chunk_bwd_kernel" : "ssd_chunk_bwd_kernel");
+                                                   (const T*)delta, A, ash, asn, (int)L, (int)H, (int)seg, (T*)gd,
+                                                   ws, h0, gh0, (const T*)Bm, (const T*)Cm);
+  return check_launch(V::kGla ? "gla_chunk_bwd_kernel" : V::kDense ? "ssd_dense_chunk_bwd_kernel"
+                                                                   : "ssd_chunk_bwd_kernel");
 }
 
 template <typename T>
@@ -1402,12 +1728,25 @@ int ssd_chunk_bwd_launch(const float* gy, const float* gf, const float* ckpt, co
                          const void* Bm, const void* Cm, const float* A, int64_t ash, int64_t batch, int64_t L,
                          int64_t H, int64_t seg, void* gu, void* gd, void* gB, void* gC, float* gA,
                          float* ws, const float* h0, float* gh0, cudaStream_t st) {
-  if (int rc = chunk_bwd_launch<T, SsdRec>(gy, gf, ckpt, u, delta, Bm, Cm, A, ash, batch, L, H, seg, gu, gd, gB,
-                                           gC, ws, h0, gh0, st))
+  if (int rc = chunk_bwd_launch<T, SsdRec>(gy, gf, ckpt, u, delta, Bm, Cm, A, ash, 0, batch, L, H, seg, gu, gd,
+                                           gB, gC, ws, h0, gh0, st))
     return rc;
   const int HN = (int)(H * SsdRec::NS);
   ssd_ga_head_kernel<<<(HN + 255) / 256, 256, 0, st>>>(ws, (int)batch, (int)H, SsdRec::NS, gA);
   return check_launch("ssd_ga_head_kernel");
+}
+
+// Dense A_neg [H, N] on the tensor cores: each unit writes its grad A_n partial to
+// gA_part [B, H, N] (ssd_dense_chunk_bwd_ws_bytes); units it marks (NaN in
+// grad_delta[b, 0, h]) are left to the per-step kernel, which rewrites their partials,
+// before the partials are summed over the batch.
+template <typename T>
+int ssd_dense_chunk_bwd_launch(const float* gy, const float* gf, const float* ckpt, const void* u,
+                               const void* delta, const void* Bm, const void* Cm, const float* A, int64_t ash,
+                               int64_t asn, int64_t batch, int64_t L, int64_t H, int64_t seg, void* gu, void* gd,
+                               void* gB, void* gC, float* gA_part, const float* h0, float* gh0, cudaStream_t st) {
+  return chunk_bwd_launch<T, SsdDenseRec>(gy, gf, ckpt, u, delta, Bm, Cm, A, ash, asn, batch, L, H, seg, gu, gd,
+                                          gB, gC, gA_part, h0, gh0, st);
 }
 
 // GLA backward on the tensor cores: grads (q, k, v, gates) = (gC, gB, gu, gdelta)
@@ -1416,8 +1755,8 @@ template <typename T>
 int gla_chunk_bwd_launch(const float* gy, const float* gf, const float* ckpt, const void* q, const void* k,
                          const void* v, const void* gates, int64_t batch, int64_t L, int64_t H, int64_t seg,
                          void* gq, void* gk, void* gv, void* gg, const float* h0, float* gh0, cudaStream_t st) {
-  return chunk_bwd_launch<T, GlaRec>(gy, gf, ckpt, v, gates, k, q, nullptr, 0, batch, L, H, seg, gv, gg, gk, gq,
-                                     nullptr, h0, gh0, st);
+  return chunk_bwd_launch<T, GlaRec>(gy, gf, ckpt, v, gates, k, q, nullptr, 0, 0, batch, L, H, seg, gv, gg, gk,
+                                     gq, nullptr, h0, gh0, st);
 }
 
 size_t ssd_chunk_bwd_ws_bytes(int64_t batch, int64_t H) { return (size_t)batch * H * sizeof(float); }
@@ -1430,6 +1769,14 @@ template int ssd_chunk_bwd_launch<__half>(const float*, const float*, const floa
                                           const void*, const void*, const float*, int64_t, int64_t, int64_t,
                                           int64_t, int64_t, void*, void*, void*, void*, float*, float*,
                                           const float*, float*, cudaStream_t);
+template int ssd_dense_chunk_bwd_launch<__nv_bfloat16>(const float*, const float*, const float*, const void*,
+                                                       const void*, const void*, const void*, const float*, int64_t,
+                                                       int64_t, int64_t, int64_t, int64_t, int64_t, void*, void*,
+                                                       void*, void*, float*, const float*, float*, cudaStream_t);
+template int ssd_dense_chunk_bwd_launch<__half>(const float*, const float*, const float*, const void*, const void*,
+                                                const void*, const void*, const float*, int64_t, int64_t, int64_t,
+                                                int64_t, int64_t, int64_t, void*, void*, void*, void*, float*,
+                                                const float*, float*, cudaStream_t);
 template int gla_chunk_bwd_launch<__nv_bfloat16>(const float*, const float*, const float*, const void*,
                                                  const void*, const void*, const void*, int64_t, int64_t,
                                                  int64_t, int64_t, void*, void*, void*, void*, const float*,

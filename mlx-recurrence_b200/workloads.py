@@ -21,6 +21,9 @@ CONFIGS = {
     "c2": dict(kind="rglru", B=8, L=4096, D=2560, seg=32, dtype=torch.bfloat16),
     "c3": dict(kind="rotlru", B=16, L=8192, Dp=1024, seg=32, dtype=torch.bfloat16),
     "c4": dict(kind="ssd", B=32, L=16384, H=32, Dh=64, N=128, seg=32, dtype=torch.bfloat16),
+    # c4 with a dense per-(head, state) decay A_neg [H, N] (the reference's general contract,
+    # ssd.py:62, 96): the float32 per-step kernels
+    "c4d": dict(kind="ssd", B=32, L=16384, H=32, Dh=64, N=128, seg=32, dtype=torch.bfloat16, dense_a=True),
     # the GLA shape of the target (SSD/GLA fwd+bwd at B=32, L=16384, H=32, Dh=64)
     "c5": dict(kind="gla", B=32, L=16384, H=32, Dh=64, seg=32, dtype=torch.bfloat16),
     # c2 with the RG-LRU input gating inside the kernels (x, r, i, lam in; c = 8)
@@ -37,6 +40,7 @@ DESCRIPTION = {
     "c2": "rglru_scan bf16 B=8 L=4096 D=2560 seg=32",
     "c3": "rotlru_scan bf16 B=16 L=8192 D=2048 seg=32",
     "c4": "ssd_scan bf16 B=32 L=16384 H=32 Dh=64 N=128 seg=32",
+    "c4d": "ssd_scan bf16 B=32 L=16384 H=32 Dh=64 N=128 seg=32, dense A_neg [H, N]",
     "c5": "gla_scan bf16 B=32 L=16384 H=32 Dh=64 seg=32",
     "c2g": "rglru_scan_gated bf16 B=8 L=4096 D=2560 seg=32 (gating in the kernels, c=8)",
     "c3a": "rotlru_scan_angle bf16 B=16 L=8192 D=2048 seg=32 (cos, sin formed in the kernels)",
@@ -99,8 +103,11 @@ def make_inputs(name, device, seed=0, batch=None, block=None):
         delta = torch.randn((B, L, H), **f32).abs_().mul_(0.1).add_(0.01)
         Bm = torch.randn((B, L, H, N), **f32)
         Cm = torch.randn((B, L, H, N), **f32)
-        A = -torch.exp(torch.randn((full["H"],), **rep) * 0.5)[u0:u1]
-        A_neg = A[:, None].expand(H, N)  # one rate per head, broadcast over N
+        if cfg.get("dense_a"):  # one rate per (head, state column)
+            A_neg = -torch.exp(torch.randn((full["H"], N), **rep) * 0.5)[u0:u1].contiguous()
+        else:
+            A = -torch.exp(torch.randn((full["H"],), **rep) * 0.5)[u0:u1]
+            A_neg = A[:, None].expand(H, N)  # one rate per head, broadcast over N
         return (u.to(dt), delta.to(dt), Bm.to(dt), Cm.to(dt), A_neg)
     if cfg["kind"] == "gla":
         H, Dh = cfg["H"], cfg["Dh"]

@@ -172,27 +172,33 @@ def main():
     def _bf16(x):
         return x.float().to(torch.bfloat16).double()
 
+    # The SSD case twice: with one rate per head, and with the reference's own dense
+    # A_neg [H, N] as its input maker draws it (the general contract, ssd.py:62, 96).
     wide = [
-        ("ssd", ssd_scan_reference, ["u", "delta", "B", "C", "A_neg"], dict(B=2, L=256, H=2, Dh=64, N=128, seed=4)),
-        ("gla", gla_scan_reference, ["q", "k", "v", "gates"], dict(B=2, L=256, H=2, Dh=64, seed=4)),
+        ("ssd", "tc", ssd_scan_reference, ["u", "delta", "B", "C", "A_neg"], dict(B=2, L=256, H=2, Dh=64, N=128, seed=4)),
+        ("ssd", "tc_dense", ssd_scan_reference, ["u", "delta", "B", "C", "A_neg"],
+         dict(B=2, L=256, H=2, Dh=64, N=128, seed=5)),
+        ("gla", "tc", gla_scan_reference, ["q", "k", "v", "gates"], dict(B=2, L=256, H=2, Dh=64, seed=4)),
     ]
-    for kind, ref_fn, argn, p in wide:
+    for kind, tag, ref_fn, argn, p in wide:
         ins = list(tests[kind]._make_inputs(**p))
         if kind == "ssd":
-            A = ins[4]
-            ins[4] = A[:, :1].expand(A.shape).contiguous()
+            if tag == "tc":
+                A = ins[4]
+                ins[4] = A[:, :1].expand(A.shape).contiguous()
             ins[:4] = [_bf16(x) for x in ins[:4]]
         else:
             ins = [_bf16(x) for x in ins]
         rec = _Recorder(mx, kind)
         rec(None, ref_fn, ins, argn, tuple(range(len(argn))), label=f"{kind} widened {p}")
         for label, names, arrays in rec.cases:
+            a_desc = "one rate per head" if tag == "tc" else "dense [H, N] as drawn"
             meta = {"kind": kind, "test": f"tests/test_v2_{kind}.py::_make_inputs (widened)",
                     "params": {**p, "seg": 32}, "label": label, "arg_names": names,
-                    "inputs": "rounded to bf16 (A_neg float32, one rate per head)",
+                    "inputs": f"rounded to bf16 (A_neg float32, {a_desc})" if kind == "ssd" else "rounded to bf16",
                     "reference_version": src_version,
                     "loss": "sum(y * w_out), w_out ~ seed 1234 (_chassis.py:166-188)"}
-            _save(f"{kind}_tc_parity_widened", arrays, meta)
+            _save(f"{kind}_{tag}_parity_widened", arrays, meta)
 
     # ---- rotLRU properties, run with the reference loop in place of the kernel ----
     rmod = tests["rotlru"]

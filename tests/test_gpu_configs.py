@@ -8,11 +8,12 @@ on the same (rounded) inputs. Tolerances (``max|diff| / max|ref|``): 1e-5 for
 float32 inputs (c0), 2e-2 for bf16 inputs.
 
 The large configurations run in full on the GPU; the oracle checks a subset:
-* c4 (SSD, B=32, L=16384, H=32, N=128) and c5 (GLA, same shape): every one of
+* c4 (SSD, B=32, L=16384, H=32, N=128), c4d (the same with a dense A_neg [H, N])
+  and c5 (GLA, same shape): every one of
   the 1024 (batch row, head) units runs, the cotangents are nonzero only on
   four units (two heads of the first batch row, two of the last), so the
-  oracle restates those units alone at full L (the per-head ``grad_A`` of c4
-  then comes from them alone), and every other unit's gradients must be
+  oracle restates those units alone at full L (``grad_A`` of c4 per head, of
+  c4d per head and column, then comes from them alone), and every other unit's gradients must be
   exactly zero (the units are independent).
 * c3 (rotLRU, B=16): batch rows 0 and 15 at full L and width.
 c0, c1 and c2 are checked in full.
@@ -150,7 +151,7 @@ def test_c3_rotlru_rows_at_full_length(mr, cuda_dev):
 _UNITS = lambda B, H: [(0, slice(0, 2)), (B - 1, slice(H - 2, H))]
 
 
-@pytest.mark.parametrize("name", ["c4", "c5"])
+@pytest.mark.parametrize("name", ["c4", "c4d", "c5"])
 def test_large_config_units_at_full_length(mr, cuda_dev, name):
     W = _W()
     cfg = W.CONFIGS[name]
@@ -175,7 +176,8 @@ def test_large_config_units_at_full_length(mr, cuda_dev, name):
         if gk.dim() >= 3:
             other = gk.transpose(1, 2)[~mask] if gk.dim() == 4 else gk.permute(0, 2, 1)[~mask]
             assert float(other.abs().max()) == 0.0, f"grad_{n} nonzero outside the seeded units"
-    gA_ref = np.zeros(H) if kind == "ssd" else None
+    dense = bool(cfg.get("dense_a"))
+    gA_ref = (np.zeros((H, N)) if dense else np.zeros(H)) if kind == "ssd" else None
     for b, hs in units:
         sl = (slice(b, b + 1), slice(None), hs)
         ref_in = []
@@ -191,7 +193,7 @@ def test_large_config_units_at_full_length(mr, cuda_dev, name):
         _check(f"final (b={b})", _np(fin[b:b + 1, hs]), fo, 2e-2)
         for n, gk, gr in zip(names, grads, go):
             if n == "A_neg":
-                gA_ref[hs] += gr.sum(axis=1)
+                gA_ref[hs] += gr if dense else gr.sum(axis=1)
                 continue
             _check(f"grad_{n} (b={b})", _np(gk[sl]), gr, 2e-2)
     if kind == "ssd":
@@ -200,6 +202,6 @@ def test_large_config_units_at_full_length(mr, cuda_dev, name):
         for _, hs in units:
             heads[hs] = True
         assert np.all(gA[~heads] == 0.0)
-        _check("grad_A (per head)", gA[heads], gA_ref[heads], 2e-2)
+        _check("grad_A (per head and column)" if dense else "grad_A (per head)", gA[heads], gA_ref[heads], 2e-2)
     del ins, grads, y, fin
     torch.cuda.empty_cache()
