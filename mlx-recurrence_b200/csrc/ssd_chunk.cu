@@ -893,13 +893,13 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     sWide[2] = 0;  // GLA: a gate outside the tensor-core range; dense: a chunk beyond kDenseSpan
     fence_mbar_init();
   }
-  // dense: the rate of this thread's state row n = row (Psi), the rates in shared memory
-  const float an = V::kDense ? A[(int64_t)h * ash + (int64_t)row * asn] : 0.f;
+  // dense: the rates in shared memory; sGA and the column sums in sQ start at zero
   if constexpr (V::kDense) {
     if (tid < NS) {
       sAn[tid] = A[(int64_t)h * ash + (int64_t)tid * asn];
       sGA[tid] = 0.f;
     }
+    for (int i = tid; i < CQ * Q; i += NT) sQ[i] = 0.f;
   }
   if (warp == 0) {
     umma::tmem_alloc(tslot, 512);
@@ -921,7 +921,7 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   // dense: the 2-byte Psi operand is Psi~ = exp(a_n (D_last - c)) Psi (written once the
   // chunk's scalars are known)
   auto write_psi_dense = [&](const float* sLamC) {
-    const float sc = __expf(an * (sLamC[Q - 1] - sLamC[Q / 2 - 1]));
+    const float sc = __expf(sAn[row] * (sLamC[Q - 1] - sLamC[Q / 2 - 1]));
     float pv[CH];
 #pragma unroll
     for (int i = 0; i < CH; ++i) pv[i] = sc * psi[i];
@@ -991,7 +991,6 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   load_gy(nck - 1);
   if (nck > 1 || has_h0) load_h0(nck - 1);
   float gA_acc = 0.f;
-  float gAc[NCT / 16] = {};  // dense: grad A_n column sums of this warp's rows (epilogue 3 columns)
   uint32_t tph = 0, mph = 0, mph2 = 0;
 
   auto sum4 = [&](const float* p, int i) { return (p[i] + p[Q + i]) + (p[2 * Q + i] + p[3 * Q + i]); };
@@ -1001,13 +1000,6 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   // that box (H % 8 != 0 or a misaligned pointer) the warp loads it directly.
   constexpr int kScalarWarp = 9;  // off sub-partition 0, whose thread 0 blocks while it issues the MMAs
   uint32_t dph = 0;
-  float amax = 0.f;  // dense: max_n |a_n| (the scalar warp)
-  if constexpr (V::kDense)
-    if (warp == kScalarWarp) {
-      for (int k = 0; k < NS / 32; ++k) amax = fmaxf(amax, fabsf(sAn[lane + 32 * k]));
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    }
   auto issue_delta = [&](int c) {  // thread 0
     mbar_arrive_expect_tx(&bar[3], DT_BYTES);
     tma_load_2d(sDt, &tm_d, h & ~7, (int)(row0 + (int64_t)c * Q), &bar[3]);
@@ -1062,6 +1054,11 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
       // lam = D (cumulative delta): the operand factors exp(+-a_n (D_t - c)) must stay
       // within e^kDenseSpan (the test also catches a NaN delta)
       const float c_mid = __shfl_sync(0xffffffffu, lam[3], Q / 8 - 1);  // D at step Q/2 - 1
+      float amax = 0.f;  // max_n |a_n|
+#pragma unroll
+      for (int k = 0; k < NS / 32; ++k) amax = fmaxf(amax, fabsf(sAn[lane + 32 * k]));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
       bool out = false;
 #pragma unroll
       for (int i = 0; i < 4; ++i) out |= !(amax * fabsf(lam[i] - c_mid) <= kDenseSpan);
@@ -1115,6 +1112,55 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
       umma::mma_f16(tbase + 2 * NS, umma::sdesc_k(aU + k * 32), umma::sdesc_k(aPSI + k * 32), idNKK, k > 0);
     }
   };
+  // grad_delta of chunk cc (warps 4-7, thread t = tid - 128): x_t is the step's own decay
+  // derivative, wm its w_t m_t term, ur its u_t . r_t, psi at sRed[pbase..] the <Psi, h0> warp
+  // partials (dense: sum_n a_n <Psi_n, h_end_n>), sLamC the chunk's scalars (read for one rate
+  // and GLA only)
+  auto grad_delta_phase = [&](int cc, const float* sLamC, float x, float wm, float ur, int pbase) {
+    const int t = tid - 128, gw = warp - 4;
+    const float* sELc = sLamC + 3 * Q;
+    const float* sDc = sLamC + 4 * Q;
+    float suf = x, swm = wm, sxd = V::kDense ? 0.f : x * sDc[t];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float n = __shfl_down_sync(0xffffffffu, suf, o);
+      if (lane + o < 32) suf += n;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      swm += __shfl_xor_sync(0xffffffffu, swm, o);
+      sxd += __shfl_xor_sync(0xffffffffu, sxd, o);
+    }
+    if (lane == 0) {
+      sRed[gw] = suf;  // the warp's total of x
+      sRed[4 + gw] = swm;
+      sRed[8 + gw] = sxd;
+    }
+    named_barrier_sync(1, 128);
+    float sum_wm = 0.f, sum_xd = 0.f, later = 0.f, psi_h0 = 0.f;
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      sum_wm += sRed[4 + v];
+      sum_xd += sRed[8 + v];
+      if (v > gw) later += sRed[v];
+    }
+#pragma unroll
+    for (int v = 0; v < NT / 32; ++v) psi_h0 += sRed[pbase + v];
+    // dense: psi_h0 is sum_n a_n <Psi_n, h_end_n> itself and x already carries the rates
+    const float lastv = V::kDense ? psi_h0 : sELc[Q - 1] * psi_h0 + sum_wm;
+    const float dlam = suf + later + lastv;  // dL/d(log decay of step t)
+    float g;
+    if constexpr (V::kGla) {
+      g = dlam / sDc[t];  // dL/dg_t = dL/dlog(g_t) / g_t (sD holds the gate)
+    } else {
+      if (!V::kDense && t == 0) gA_acc += sum_xd + lastv * sDc[Q - 1];
+      g = Ah * dlam + ur;
+    }
+    gdelta[(row0 + (int64_t)cc * Q + t) * H + h] = from_f<T>(g);
+  };
+  // dense: the four row partials of epilogue 3 (sum_n a_n v[t, n])
+  auto dense_x = [&](int t) { return (sRow[t] + sRow[Q + t]) + (sRow[2 * Q + t] + sRow[3 * Q + t]); };
+
   // the first chunk processed (the last one); chunk nck-2's delta follows
   if (dmap && tid == 0) issue_delta(nck - 1);
   if (warp == kScalarWarp) chunk_scalars(delta_bits(nck - 1), (nck - 1) & 1);
@@ -1233,7 +1279,7 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) psih0 += __shfl_xor_sync(0xffffffffu, psih0, o);
-    if (lane == 0) sRed[32 + warp] = psih0;
+    if (lane == 0) sRed[32 + (V::kDense ? 16 * (c & 1) : 0) + warp] = psih0;
     fence_proxy_async_smem();
     __syncthreads();
 
@@ -1404,7 +1450,8 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
       // (dense: Psi <- exp(a_n D_last) Psi + exp(a_n c) dPsi')
       umma::tmem_ld16(tl + 384 + ch0, y2);
       umma::tmem_wait_ld();
-      const float dec = __expf((V::kDense ? an : 1.f) * sLam[Q - 1]);
+      const float an = V::kDense ? sAn[row] : 1.f;
+      const float dec = __expf(an * sLam[Q - 1]);
       const float dec2 = V::kDense ? __expf(an * sLam[Q / 2 - 1]) : 1.f;
 #pragma unroll
       for (int i = 0; i < CH; ++i) psi[i] = dec * psi[i] + dec2 * y2[i];
@@ -1436,6 +1483,12 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     if (c > 0) load_gy(c - 1);
     // the previous chunk's scalars (its delta arrived during the chunk before)
     if (warp == kScalarWarp && c > 0) chunk_scalars(delta_bits(c - 1), (c - 1) & 1);
+    // dense: grad_delta of the chunk before (c + 1) while R1 runs (its epilogue-3 row partials,
+    // u.r partials and <Psi, h_end> partials are still in place; its scalars are not needed)
+    if constexpr (V::kDense)
+      if (c + 1 < nck && warp >= 4 && warp < 8)
+        grad_delta_phase(c + 1, sSc, dense_x(tid - 128), 0.f, sM[((c + 1) & 1) * Q + tid - 128],
+                         32 + 16 * ((c + 1) & 1));
     mbar_wait(&bar[1], mph & 1u);
     ++mph;
     umma::fence_after_sync();
@@ -1496,57 +1549,22 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     // ---- while batch 3 completes: grad_delta and grad_A (warps 4-7, thread t)
     // dLam_t = x_t + [t = last] lastv with x_t = rowsum Z - colsum Z + exp(Lam_t) q_t - w_t m_t,
     // lastv = exp(Lam_last) <Psi, h0> + sum_t w_t m_t; grad_delta_t = A sum_{t' >= t} dLam_t' + u_t.r_t
-    auto grad_delta_phase = [&](float x, float wm) {  // warps 4-7, thread t = tid - 128
-      const int t = tid - 128, gw = warp - 4;
-      float suf = x, swm = wm, sxd = x * sD[t];
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const float n = __shfl_down_sync(0xffffffffu, suf, o);
-        if (lane + o < 32) suf += n;
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        swm += __shfl_xor_sync(0xffffffffu, swm, o);
-        sxd += __shfl_xor_sync(0xffffffffu, sxd, o);
-      }
-      if (lane == 0) {
-        sRed[gw] = suf;  // the warp's total of x
-        sRed[4 + gw] = swm;
-        sRed[8 + gw] = sxd;
-      }
-      named_barrier_sync(1, 128);
-      float sum_wm = 0.f, sum_xd = 0.f, later = 0.f, psi_h0 = 0.f;
-#pragma unroll
-      for (int v = 0; v < 4; ++v) {
-        sum_wm += sRed[4 + v];
-        sum_xd += sRed[8 + v];
-        if (v > gw) later += sRed[v];
-      }
-#pragma unroll
-      for (int v = 0; v < NT / 32; ++v) psi_h0 += sRed[32 + v];
-      // dense: psi_h0 is sum_n a_n <Psi_n, h_end_n> itself and x already carries the rates
-      const float lastv = V::kDense ? psi_h0 : sEL[Q - 1] * psi_h0 + sum_wm;
-      const float dlam = suf + later + lastv;  // dL/d(log decay of step t)
-      float g;
-      if constexpr (V::kGla) {
-        g = dlam / sD[t];  // dL/dg_t = dL/dlog(g_t) / g_t (sD holds the gate)
-      } else {
-        if (!V::kDense && t == 0) gA_acc += sum_xd + lastv * sD[Q - 1];
-        g = Ah * dlam + sum4(sUR, t);
-      }
-      gdelta[(row0 + (int64_t)c * Q + t) * H + h] = from_f<T>(g);
-    };
     if constexpr (!V::kDense)
       if (warp >= 4 && warp < 8) {
         const int t = tid - 128;
         const float wm = sW[t] * sM[t];
-        grad_delta_phase(sRow[t] - sCol[t] + sEL[t] * sQ[t] - wm, wm);
+        grad_delta_phase(c, sLam, sRow[t] - sCol[t] + sEL[t] * sQ[t] - wm, wm, sum4(sUR, t), 32);
       }
+    // dense: the chunk's u_t . r_t sums, kept (by chunk parity) for its grad_delta during the
+    // next chunk, whose epilogue 2 rewrites sUR
+    if constexpr (V::kDense)
+      if (warp >= 4 && warp < 8) sM[(c & 1) * Q + tid - 128] = sum4(sUR, tid - 128);
     mbar_wait(&bar[2], mph2 & 1u);
     ++mph2;
     umma::fence_after_sync();
-    // u, B, C of this chunk are no longer read: stream the previous chunk's
-    if (tid == 0 && c > 0) {
+    // u, B, C of this chunk are no longer read: stream the previous chunk's (dense: epilogue 3
+    // still reads B~ and C~, so after it)
+    if (!V::kDense && tid == 0 && c > 0) {
       fence_proxy_async_smem();
       issue(c - 1);
     }
@@ -1554,23 +1572,18 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     // ---- epilogue 3: stage grad_B (row t) in GP, grad_C (row s) in HH (columns n = NCT * jq..);
     //      new Psi^T
     if constexpr (V::kDense) {
-      // grad_B = exp(-a_n (D_t - c)) (gB1 + delta_t gB2), grad_C = exp(a_n (D_t - c)) (gC1 + gC2);
-      // v[t, n] = C grad_C - B grad_B (= dL/d(a_n D_t), from the inputs' own values, read
-      // back from global memory as the tiles already stream the next chunk) gives the
-      // decay derivative of step t (sum_n a_n v, row partials) and of a_n (sum_t D_t v,
-      // column sums over this warp's rows accumulated across chunks)
+      // grad_B = exp(-a_n (D_t - c)) gB~, gB~ = gB1 + delta_t gB2; grad_C = exp(a_n (D_t - c)) gC~,
+      // gC~ = gC1 + gC2; v[t, n] = C~ gC~ - B~ gB~ (= C grad_C - B grad_B = dL/d(a_n D_t), from
+      // the chunk's B~ and C~ tiles, kept until epilogue 3 ends) gives the decay derivative of
+      // step t (sum_n a_n v, row partials) and of a_n (sum_t D_t v, column sums over this
+      // warp's rows accumulated across chunks)
       const int t = row;
       const float dt = sDel[t], Dt = sLam[t], x0 = Dt - sLam[Q / 2 - 1];
       const int nc0 = NCT * jq;
       uint8_t* gbt = tGP + (nc0 >> 6) * TILE;
       uint8_t* gct = tHH + (nc0 >> 6) * TILE;
-      const int64_t grow = ((row0 + (int64_t)c * Q + t) * H + h) * NS;
-      int4 braw[NCT / 8], craw[NCT / 8];
-#pragma unroll
-      for (int i = 0; i < NCT / 8; ++i) {
-        braw[i] = __ldg(reinterpret_cast<const int4*>(Bg + grow + nc0) + i);
-        craw[i] = __ldg(reinterpret_cast<const int4*>(Cg + grow + nc0) + i);
-      }
+      const uint8_t* btl = tB + (nc0 >> 6) * TILE;
+      const uint8_t* ctl = tC + (nc0 >> 6) * TILE;
       float ra = 0.f;
 #pragma unroll
       for (int cb = 0; cb < NCT / 16; ++cb) {
@@ -1585,23 +1598,28 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
         umma::tmem_ld16(tl + NS + col, gc);
         umma::tmem_ld16(tl + 3 * NS + col, v2);
         umma::tmem_wait_ld();
-        const T* bq = reinterpret_cast<const T*>(&braw[2 * cb]);  // 16 consecutive values
-        const T* cq = reinterpret_cast<const T*>(&craw[2 * cb]);
+        float b0[8], b1[8], c0[8], c1[8];
+        unpack8<T>(*reinterpret_cast<const int4*>(btl + o0), b0);
+        unpack8<T>(*reinterpret_cast<const int4*>(btl + o1), b1);
+        unpack8<T>(*reinterpret_cast<const int4*>(ctl + o0), c0);
+        unpack8<T>(*reinterpret_cast<const int4*>(ctl + o1), c1);
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const float a = sAn[col + i];
           const float x = a * x0;
-          gc[i] = (gc[i] + v2[i]) * __expf(x);
-          gb[i] *= __expf(-x);
-          const float vv = to_f(cq[i]) * gc[i] - to_f(bq[i]) * gb[i];
+          const float gct_i = gc[i] + v2[i];
+          const float vv = (i < 8 ? c0[i] : c1[i - 8]) * gct_i - (i < 8 ? b0[i] : b1[i - 8]) * gb[i];
           ra += a * vv;
           z[i] = Dt * vv;
+          gc[i] = gct_i * __expf(x);
+          gb[i] *= __expf(-x);
         }
         *reinterpret_cast<int4*>(gbt + o0) = pack8<T>(gb);
         *reinterpret_cast<int4*>(gbt + o1) = pack8<T>(gb + 8);
         *reinterpret_cast<int4*>(gct + o0) = pack8<T>(gc);
         *reinterpret_cast<int4*>(gct + o1) = pack8<T>(gc + 8);
-        gAc[cb] += warp_colsum16(z, lane);
+        const float cz = warp_colsum16(z, lane);  // this warp's rows: one (q4, column) slot per lane pair
+        if ((lane & 1) == 0) sQ[q4 * Q + col + (lane >> 1)] += cz;
       }
       sRow[jq * Q + t] = ra;
       if (c > 0) write_psi_dense(sSc + ((c - 1) & 1) * NSC * Q);  // Psi~ of the next chunk
@@ -1641,6 +1659,10 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     umma::fence_before_sync();
     __syncthreads();
     if (tid == 0) {  // read back by the next chunk's P0 (bulk_wait_read_all) before reuse
+      if (V::kDense && c > 0) {  // epilogue 3 has read B~ and C~: stream the previous chunk's
+        fence_proxy_async_smem();
+        issue(c - 1);
+      }
       const int z = (int)(row0 + (int64_t)c * Q);
       // groups: grad_C's first box (HH tile 0, rewritten first, by P0), then the rest
       tma_store_3d(&tm_gC, 0, h, z, tHH);
@@ -1651,21 +1673,13 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
       for (int j = 0; j < NB; ++j) tma_store_3d(&tm_gB, 64 * j, h, z, tGP + j * TILE);
       bulk_commit();
     }
-    // dense: grad_delta once epilogue 3's row partials are in (x_t = sum_n a_n v[t, n])
-    if constexpr (V::kDense)
-      if (warp >= 4 && warp < 8) {
-        const int t = tid - 128;
-        grad_delta_phase((sRow[t] + sRow[Q + t]) + (sRow[2 * Q + t] + sRow[3 * Q + t]), 0.f);
-      }
   }
+  if constexpr (V::kDense)  // the last chunk walked (chunk 0)
+    if (warp >= 4 && warp < 8) grad_delta_phase(0, sSc, dense_x(tid - 128), 0.f, sM[tid - 128], 32);
   if constexpr (!V::kGla && !V::kDense)
     if (tid == 128) gA_part[bh] = gA_acc;  // step t = 0 of the grad_delta warps
   if constexpr (V::kDense) {
     // grad A_n of this unit: the four row quarters' column sums plus the end-state terms
-    const int nc0 = NCT * jq;
-    if ((lane & 1) == 0)
-#pragma unroll
-      for (int cb = 0; cb < NCT / 16; ++cb) sQ[q4 * Q + nc0 + 16 * cb + (lane >> 1)] = gAc[cb];
     __syncthreads();
     if (tid < NS) gA_part[(int64_t)bh * NS + tid] = (sQ[tid] + sQ[Q + tid]) + (sQ[2 * Q + tid] + sQ[3 * Q + tid]) + sGA[tid];
   }
