@@ -103,6 +103,8 @@ def algorithmic_bytes(cfg, batch):
 _NCU_TRAFFIC_PER_BATCH_ROW = {
     ("c4", "backward"): (1.208137e9 + 0.629970e9) / 2,
     ("c4", "forward"): (0.677076e9 + 0.496836e9) / 2,
+    ("c4d", "backward"): (1.210163e9 + 0.632409e9) / 2,
+    ("c4d", "forward"): (0.676261e9 + 0.497439e9) / 2,
     ("c5", "backward"): (0.806439e9 + 0.363859e9) / 2,
     ("c5", "forward"): (0.407030e9 + 0.357562e9) / 2,
     ("c2", "backward"): (674.370e6 + 309.851e6) / 8,
