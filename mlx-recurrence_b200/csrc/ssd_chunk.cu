@@ -113,6 +113,18 @@ __device__ __forceinline__ float4 ld_pinned_f4(const float* p) {
                : "l"(p));
   return v;
 }
+// L2 prefetches by the bulk-copy engine: no registers, no shared memory, and no load kept
+// in flight by the issuing thread. A contiguous range (p 16-byte aligned, bytes a multiple
+// of 16), or one box of a tensor map at (x, y, z).
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void prefetch_l2_box3d(const CUtensorMap* map, int x, int y, int z) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
 // barrier over the first `nthreads` threads of named barrier `id` (1..15; 0 is __syncthreads)
 __device__ __forceinline__ void named_barrier_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
@@ -773,9 +785,11 @@ int ssdc_device_error(bool clear) { return read_device_error(clear); }
 //      dPsi^T = C^T (e^Lam gy) [384,448)
 //   2: R1 = G'^T [gy_hi | gy_lo] [384,512) (one N = 128 product of the two halves)
 //   3: gB1 = H1^T C [0,N)  gC1 = H1 B [N,2N)  gB2 = u Psi [2N,3N)  gC2 = gy h0 [3N,4N)
-// Batch 3 is issued with batch 2 where its columns are free then (GLA, N = 64:
-// all of it; SSD, N = 128: gB1 and gC1, the rest once epilogue 2 has read R1, R2),
-// so it runs under epilogue 2. An N = 64 product reads its operands from shared
+// GLA (N = 64) issues all of batch 3 with batch 2, so it runs under epilogue 2.
+// SSD (N = 128) issues gB1 and gC1 when the issuing thread has done its own
+// epilogue-2 rows (issued with batch 2, they held that thread's warp back by the
+// time the tensor pipe takes for them, and the whole CTA waited for it at the
+// barrier), the rest once epilogue 2 has read R1, R2. An N = 64 product reads its operands from shared
 // memory at 2/3 of the tensor rate (48 cycles per 128x64x16 step against 64 for
 // 128x128x16), hence R1's two halves as one N = 128 product.
 // gy enters P and R1 as bf16/fp16 hi + lo parts (two accumulated products).
@@ -818,7 +832,8 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
                      const __grid_constant__ CUtensorMap tm_C, const __grid_constant__ CUtensorMap tm_gu,
                      const __grid_constant__ CUtensorMap tm_gB, const __grid_constant__ CUtensorMap tm_gC,
                      const float* __restrict__ ckpt, const float* __restrict__ gy,
-                     const __grid_constant__ CUtensorMap tm_d, int dmap, const float* __restrict__ gfinal,
+                     const __grid_constant__ CUtensorMap tm_gy, const __grid_constant__ CUtensorMap tm_d,
+                     int dmap, const float* __restrict__ gfinal,
                      const T* __restrict__ delta, const float* __restrict__ A, int64_t ash, int64_t asn, int L,
                      int H, int seg, T* __restrict__ gdelta, float* __restrict__ gA_part,
                      const float* __restrict__ h0, float* __restrict__ gh0, const T* __restrict__ Bg,
@@ -999,6 +1014,7 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   // box: 128 steps of the 8 heads h & ~7..); where the layout does not allow
   // that box (H % 8 != 0 or a misaligned pointer) the warp loads it directly.
   constexpr int kScalarWarp = 9;  // off sub-partition 0, whose thread 0 blocks while it issues the MMAs
+  constexpr int kPrefetchThread = 14 * 32;
   uint32_t dph = 0;
   auto issue_delta = [&](int c) {  // thread 0
     mbar_arrive_expect_tx(&bar[3], DT_BYTES);
@@ -1176,6 +1192,16 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     float* sEL = sW + Q;
     float* sD = sEL + Q;
     float* sCF1 = sD + Q;
+    // The next chunk's grad_y and checkpoint, which this chunk loads into registers (grad_y
+    // while batch 2 runs, the checkpoint after epilogue 2), are brought into L2 first: a
+    // register load that misses L2 holds the SM's load path for the whole DRAM latency, and
+    // 32 KB of them in flight delay the tensor-core issue and shared-memory accesses of the
+    // other warps by about 2,000 cycles a chunk; from L2 they return several times sooner.
+    if (tid == kPrefetchThread && c > 0) {
+      prefetch_l2_box3d(&tm_gy, 0, h, (int)(row0 + (int64_t)(c - 1) * Q));
+      if (c > 1)
+        prefetch_l2_bulk(ckpt + (((int64_t)b * nseg + ((c - 1) * Q) / seg - 1) * H + h) * NS * DH, NS * DH * 4);
+    }
     // the previous chunk's grad_u store and (SSD, exp(Lam) gy staged in HH) grad_C's
     // first box must have read GYt and HH tile 0 before they are rewritten below (the
     // rest may still run: the batch-1 issuer waits for it, E1 rewrites GP, HH)
@@ -1470,8 +1496,9 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
         umma::mma_f16(tbase + 384, umma::sdesc_mn(aGP + k * 2048, TILE), umma::sdesc_mn(aGY + k * 2048, lboGY),
                       id128MM, k > 0);
       umma::commit(&bar[1]);
-      batch3_h1();
+      // GLA: all of batch 3 now (its columns are free), so it runs under epilogue 2
       if constexpr (V::kGla) {
+        batch3_h1();
         batch3_state();
         umma::commit(&bar[2]);
       }
@@ -1532,6 +1559,9 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
       fence_proxy_async_smem();
       if (c > 1 || (c == 1 && has_h0)) load_h0(c - 1);
     }
+    // SSD: gB1 and gC1 (their columns are free; R1, R2 are not among them)
+    if constexpr (!V::kGla)
+      if (tid == 0) batch3_h1();
     umma::fence_before_sync();
     __syncthreads();
 
@@ -1546,6 +1576,7 @@ ssd_chunk_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
       bulk_commit();
       if (dmap && c > 1) issue_delta(c - 2);  // the scalar warp has read chunk c-1's box
     }
+
     // ---- while batch 3 completes: grad_delta and grad_A (warps 4-7, thread t)
     // dLam_t = x_t + [t = last] lastv with x_t = rowsum Z - colsum Z + exp(Lam_t) q_t - w_t m_t,
     // lastv = exp(Lam_last) <Psi, h0> + sum_t w_t m_t; grad_delta_t = A sum_{t' >= t} dLam_t' + u_t.r_t
@@ -1717,9 +1748,13 @@ static int chunk_bwd_launch(const float* gy, const float* gf, const float* ckpt,
                             int64_t batch, int64_t L, int64_t H, int64_t seg, void* gu, void* gd, void* gB,
                             void* gC, float* ws, const float* h0, float* gh0, cudaStream_t st) {
   constexpr size_t SMEM = ssdb::Cfg<V>::SMEM;
-  CUtensorMap mu, mB, mC, mgu, mgB, mgC, md;
+  CUtensorMap mu, mB, mC, mgu, mgB, mgC, md, mgy;
   if (int rc = ssd_tmaps<T, V::NS>(u, Bm, Cm, batch, L, H, &mu, &mB, &mC)) return rc;
   if (int rc = ssd_tmaps<T, V::NS>(gu, gB, gC, batch, L, H, &mgu, &mgB, &mgC)) return rc;
+  // grad_y [B*L, H, Dh] f32 in boxes of one chunk (128 steps x Dh) of one head: L2 prefetches only
+  if (int rc = make_tmap_3d(&mgy, gy, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ssdb::DH, (uint64_t)H,
+                            (uint64_t)batch * L, ssdb::DH * 4, (uint64_t)H * ssdb::DH * 4, ssdb::DH, 1, ssdb::Q))
+    return rc;
   // delta [B*L, H] in boxes of 128 steps x 8 heads (16 bytes), where the row pitch and base allow
   const int dmap = (H % 8 == 0 && (reinterpret_cast<uintptr_t>(delta) & 15) == 0) ? 1 : 0;
   memset(&md, 0, sizeof(md));
@@ -1730,7 +1765,7 @@ static int chunk_bwd_launch(const float* gy, const float* gf, const float* ckpt,
   auto k = h0 != nullptr ? ssd_chunk_bwd_kernel<T, V, true> : ssd_chunk_bwd_kernel<T, V, false>;
   const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM);
   if (e != cudaSuccess) return set_error(MR_E_LAUNCH, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-  k<<<(unsigned)(batch * H), ssdb::NT, SMEM, st>>>(mu, mB, mC, mgu, mgB, mgC, ckpt, gy, md, dmap, gf,
+  k<<<(unsigned)(batch * H), ssdb::NT, SMEM, st>>>(mu, mB, mC, mgu, mgB, mgC, ckpt, gy, mgy, md, dmap, gf,
                                                    (const T*)delta, A, ash, asn, (int)L, (int)H, (int)seg, (T*)gd,
                                                    ws, h0, gh0, (const T*)Bm, (const T*)Cm);
   return check_launch(V::kGla ? "gla_chunk_bwd_kernel" : V::kDense ? "ssd_dense_chunk_bwd_kernel"
