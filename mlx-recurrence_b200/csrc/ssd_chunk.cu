@@ -80,8 +80,9 @@ template <typename V> struct Cfg {
   static constexpr int NS = V::NS;                     // state size N (B, C width)
   static constexpr int NB = NS / 64;                   // 64-wide tiles of B and C
   static constexpr uint32_t STAGE = TILE * (1 + 2 * NB);  // u, B, C
-  // stages, G (2), U~, h^T; GLA adds a zero tile that pads the M = 64 product B^T U~
-  static constexpr size_t SMEM = SMALL_PAD + 2 * STAGE + 4 * TILE + (V::kGla ? TILE : 0);
+  // stages, G (2), U~, h^T; GLA adds a zero tile that pads the M = 64 product B^T U~ and
+  // its own checkpoint staging (SSD stages the checkpoint in the chunk's stage)
+  static constexpr size_t SMEM = SMALL_PAD + 2 * STAGE + 4 * TILE + (V::kGla ? 2 * TILE : 0);
 };
 }  // namespace ssdc
 
@@ -235,6 +236,7 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   uint8_t* sUt = sG + 2 * TILE;  // U~, MN-major [s][d]
   uint8_t* sHt = sUt + TILE;     // h^T bf16, MN-major [n][d]
   uint8_t* sZero = sHt + TILE;   // GLA: zeros, the n = 64..127 half of B^T in B^T U~
+  uint8_t* sCkG = sZero + TILE;  // GLA: checkpoint staging, [2 boxes][64 n][32 f32]
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bh = blockIdx.x;
@@ -273,8 +275,10 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
   const uint32_t tbase = *tslot;
 
   // A stage (u, B, C of one chunk) is reloaded once the chunk's products have
-  // completed and the checkpoint staged in its u slot (and B's first tile for
-  // SSD) has been stored.
+  // completed and (SSD) the checkpoint staged in its u slot and B's first tile has
+  // been read by its store: SSD at the start of the next chunk, two chunks ahead;
+  // GLA, whose checkpoint has its own staging, as soon as the chunk's last product
+  // (Y1) is done, so the loads have about a chunk and a half to land.
   auto issue_bc = [&](int c) {
     const int st = c & 1;
     uint8_t* s = stg0 + st * STAGE;
@@ -463,12 +467,14 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
 
     // ---- S = C B^T (commit 1), then Y2 = C h0^T, dH^T = B^T U~ (commit 2)
     if (tid == 0) {
-      // the previous chunk's y and checkpoint stores have read G's tiles (E1 rewrites
-      // them) and their stage, which then streams in chunk c+1
-      bulk_wait_read<0>();
-      if (c > 0 && c + 1 < nck) {
-        issue_u(c + 1);
-        issue_bc(c + 1);
+      // SSD: the previous chunk's checkpoint stores (its first bulk group) have read
+      // their stage, which then streams in chunk c+1
+      if constexpr (!V::kGla) {
+        bulk_wait_read<1>();
+        if (c > 0 && c + 1 < nck) {
+          issue_u(c + 1);
+          issue_bc(c + 1);
+        }
       }
       mbar_wait(&bar[st], (uint32_t)(c >> 1) & 1u);
       umma::fence_after_sync();
@@ -478,6 +484,9 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
         const uint32_t ko = (k >> 2) * TILE + (k & 3) * 32;
         umma::mma_f16(tbase + 0, umma::sdesc_k(aC + ko), umma::sdesc_k(aB + ko), idS, k > 0);
       }
+      // the previous chunk's y stores have read G's tiles, which epilogue 1 rewrites once
+      // S (this commit) is done: the wait overlaps S
+      bulk_wait_read<0>();
       umma::commit(&bar[4]);
 #pragma unroll
       for (int k = 0; k < NS / 16; ++k) {
@@ -593,9 +602,15 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     mbar_wait(&bar[4], mph & 1u);
     ++mph;
     umma::fence_after_sync();
+    // GLA: every product that reads this chunk's stage is done: stream in chunk c+2
+    if constexpr (V::kGla)
+      if (tid == 0 && c + 2 < nck) {
+        issue_u(c + 2);
+        issue_bc(c + 2);
+      }
 
     // ---- stage y = Y1 + exp(Lam_t) Y2 in sG, the checkpoint in this stage's u slot
-    //      (states n >= 64) and first B tile (n < 64; GLA: the u slot)
+    //      (states n >= 64) and first B tile (n < 64; GLA: its own staging)
     {
       float a[CH], bb[CH];
       umma::tmem_ld16(tl + 256 + ch0, a);
@@ -609,7 +624,7 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
                         a[i + 3] + e_t * bb[i + 3]);
     }
     const bool ck = ((c + 1) * Q) % seg == 0;
-    uint8_t* sCk0 = V::kGla ? sU : sB;  // checkpoint states 0-63
+    uint8_t* sCk0 = V::kGla ? sCkG : sB;  // checkpoint states 0-63
     if (ck && trow < NS) {
       const int n = trow;
       uint8_t* cb = (n < 64 ? sCk0 : sU) + (jq >> 1) * (TILE / 2);  // box [64 n][32 f32]
@@ -621,9 +636,9 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
     fence_proxy_async_smem();
     umma::fence_before_sync();
     __syncthreads();
-    if (tid == 0) {  // drained before the next chunk's MMAs (bulk_wait_read<0> there)
+    if (tid == 0) {  // drained during the next chunk's first products (bulk_wait_read there)
       const int z = (int)(row0 + (int64_t)c * Q);
-      if (ck) {
+      if (ck) {  // its own bulk group, the first: SSD's stage reload waits for it alone
         const int zz = (int)(((int64_t)b * nseg + (c + 1) * Q / seg - 1) * H + h);
         tma_store_3d(&tm_ck, 0, 0, zz, sCk0);
         tma_store_3d(&tm_ck, 32, 0, zz, sCk0 + TILE / 2);
@@ -631,6 +646,7 @@ ssd_chunk_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_cons
           tma_store_3d(&tm_ck, 0, 64, zz, sU);
           tma_store_3d(&tm_ck, 32, 64, zz, sU + TILE / 2);
         }
+        bulk_commit();
       }
       tma_store_3d(&tm_y, 0, h, z, sG);
       tma_store_3d(&tm_y, 32, h, z, sG + TILE);
