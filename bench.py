@@ -17,7 +17,8 @@ Printed (rank 0, one JSON line): value = whole-job tokens/s with inputs
 resident in HBM; e2e = the same step with host->device copies of every input
 (and the upstream gradient) from pinned memory and device->host copies of y
 and every input gradient into pinned memory inside the timed region; roofline
-of the dominant kernel (algorithmic bytes / CUDA-event time); cpu_baseline =
+of the dominant kernel (algorithmic bytes / CUDA-event time), with the whole
+step's and the forward's fractions of the same roofline; cpu_baseline =
 the float32 C restatement of the reference algorithm (oracle/ckpt_scan.c) on
 a bounded sample (median of three runs); clocks sampled during timing.
 
@@ -599,7 +600,11 @@ def _metrics(args, ctx, P, M):
                      "achieved": achieved, "peak": hbm, "unit": "GB/s",
                      "frac": achieved / hbm, "traffic": traffic,
                      "algorithmic_bytes_per_launch": dom[1],
-                     "peak_source": f"{peak_kind} hbm_gbs"},
+                     "peak_source": f"{peak_kind} hbm_gbs",
+                     # the whole forward+backward step against the same roofline (this rank's
+                     # algorithmic bytes over its share of the step time), and the forward alone
+                     "step_frac": (fb + bb) / (M["total_ms"] / args.steps * 1e-3) / 1e9 / hbm,
+                     "fwd_frac": fb / (f_ms * 1e-3) / 1e9 / hbm},
         **({"note": "per-step delta-rule recurrence: bound by FP32 issue and per-step latency on the "
                     "CUDA cores, not by HBM"} if cfg["kind"] == "gdn" else {}),
         "gpu_launches": int(M["launches"]),
