@@ -86,11 +86,22 @@ __device__ __forceinline__ float gdn_warp_sum(float x) {
   return x;
 }
 
-// one step of the state update, shared by the forward and both replays
+// Pairs of float32 lanes in one instruction (sm_100's packed f32x2 arithmetic,
+// each lane rounded as its scalar operation): the per-step loops here are bound by
+// float32 issue, so the element-wise updates and the dot products go two at a time.
+__device__ __forceinline__ float2 gdn_pair(const float* x) { return make_float2(x[0], x[1]); }
+__device__ __forceinline__ float2 gdn_bcast(float x) { return make_float2(x, x); }
+
+// one step of the state update, shared by the forward and both replays:
+// S = fma(a, S, k * w) per element (the same rounding as the scalar form)
 template <int R>
 __device__ __forceinline__ void gdn_update(float (&S)[R], const float (&kr)[R], float a, float w) {
+  const float2 a2 = gdn_bcast(a), w2 = gdn_bcast(w);
 #pragma unroll
-  for (int r = 0; r < R; ++r) S[r] = fmaf(a, S[r], __fmul_rn(kr[r], w));
+  for (int r = 0; r < R; r += 2) {
+    const float2 x = __ffma2_rn(a2, gdn_pair(S + r), __fmul2_rn(gdn_pair(kr + r), w2));
+    S[r] = x.x, S[r + 1] = x.y;
+  }
 }
 
 // 16-byte asynchronous global -> shared copies (each thread waits for its own
@@ -167,12 +178,23 @@ __device__ __forceinline__ void gdn_warp_colsum(float* wb, const float (&x)[R], 
   }
 }
 
+// sum_r x[r] y[r]: the even and the odd terms in the two lanes of a pair
 template <int R>
 __device__ __forceinline__ float gdn_dot(const float (&x)[R], const float (&y)[R]) {
-  float acc = 0.f;
+  float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
-  for (int r = 0; r < R; ++r) acc = fmaf(x[r], y[r], acc);
-  return acc;
+  for (int r = 0; r < R; r += 2) acc = __ffma2_rn(gdn_pair(x + r), gdn_pair(y + r), acc);
+  return acc.x + acc.y;
+}
+// x = fma(a, x, y * c) per element
+template <int R>
+__device__ __forceinline__ void gdn_axpy_scaled(float (&x)[R], float a, const float (&y)[R], float c) {
+  const float2 a2 = gdn_bcast(a), c2 = gdn_bcast(c);
+#pragma unroll
+  for (int r = 0; r < R; r += 2) {
+    const float2 v = __ffma2_rn(a2, gdn_pair(x + r), __fmul2_rn(gdn_pair(y + r), c2));
+    x[r] = v.x, x[r + 1] = v.y;
+  }
 }
 
 constexpr int kGdnTS = 16;  // steps per staged block of the forward and the backward's replay
@@ -493,8 +515,12 @@ gdn_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfinal, c
             {
               float qr[R];
               gdn_ld_f32<R>(rq_ + m * DH + i0, qr);
+              const float2 go2 = gdn_bcast(go);
 #pragma unroll
-              for (int r = 0; r < R; ++r) G[r] = fmaf(qr[r], go, G[r]);  // output seed (B0)
+              for (int r = 0; r < R; r += 2) {  // output seed (B0): G += q go
+                const float2 x = __ffma2_rn(gdn_pair(qr + r), go2, gdn_pair(G + r));
+                G[r] = x.x, G[r + 1] = x.y;
+              }
             }
 #pragma unroll
             for (int c = 0; c < R / 4; ++c) {
@@ -519,17 +545,19 @@ gdn_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfinal, c
             // S_{t-1} go + k (w.go), alpha and the last term applied by the sub-block's reducer
             {
               float r1[R], r2[R];
+              const float2 go2 = gdn_bcast(go), w2 = gdn_bcast(w), gp2 = gdn_bcast(gp);
 #pragma unroll
-              for (int r = 0; r < R; ++r) {
-                r1[r] = Sp[r] * go;
-                r2[r] = fmaf(G[r], w, Sp[r] * gp);
+              for (int r = 0; r < R; r += 2) {
+                const float2 sp = gdn_pair(Sp + r);
+                const float2 x1 = __fmul2_rn(sp, go2);
+                const float2 x2 = __ffma2_rn(gdn_pair(G + r), w2, __fmul2_rn(sp, gp2));
+                r1[r] = x1.x, r1[r + 1] = x1.y, r2[r] = x2.x, r2[r + 1] = x2.y;
               }
               float* pw = ppart + ((m * NW + warp) * 2) * DH;
               gdn_warp_colsum<R>(wbuf, r1, pw);
               gdn_warp_colsum<R>(wbuf, r2, pw + DH);
             }
-#pragma unroll
-            for (int r = 0; r < R; ++r) G[r] = fmaf(a, G[r], kr[r] * gp);  // adjoint to t-1 (Bp')
+            gdn_axpy_scaled(G, a, kr, gp);  // adjoint to t-1 (Bp'): G = a G + k gp
             // the scalar gradients of alpha and beta: over the row groups, then the warp's columns
             gaP = gdn_group_sum(gaP);
 #pragma unroll
