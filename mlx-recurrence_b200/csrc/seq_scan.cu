@@ -20,6 +20,36 @@ namespace mr {
 
 constexpr int kSeqThreads = 256;
 constexpr int kTS = 4;  // steps per cross-warp partial flush
+constexpr int kStage = 16;  // steps of inputs staged in shared memory at a time (at most)
+// steps per staged block for rows of at most wmax floats: at most 16 prefetched values
+// per thread (they stay in registers while the block before is computed)
+constexpr int stage_steps(int wmax) {
+  return 16 * kSeqThreads / wmax < kStage ? (16 * kSeqThreads / wmax < 1 ? 1 : 16 * kSeqThreads / wmax) : kStage;
+}
+
+// Per-step inputs staged a block of steps at a time: every thread loads its share of
+// the next block (consecutive elements of a step's rows, coalesced) into registers
+// while the block before is computed from shared memory, then writes them into the
+// other buffer. A step's global-load latency (about a microsecond) was otherwise on
+// the path of every step. A staged step is the kernel's input rows of that step side
+// by side, as floats.
+template <int EPT>
+struct StepStage {
+  float r[EPT];
+};
+// the SSD backward's staged row (at most): [B (N) | C (N) | u (Dh) | grad_y (Dh) | delta]
+template <int R, int NK>
+constexpr int ssd_bwd_wmax() { return 2 * 32 * NK + 2 * 8 * R + 1; }
+// bytes of its two staging buffers (dynamic shared memory)
+template <int R, int NK>
+constexpr size_t ssd_bwd_stage_bytes() {
+  return (size_t)2 * stage_steps(ssd_bwd_wmax<R, NK>()) * ssd_bwd_wmax<R, NK>() * sizeof(float);
+}
+// the GLA backward's: [k (Dh) | q (Dh) | v (Dh) | grad_y (Dh) | gate]
+template <int R>
+constexpr int gla_bwd_wmax() { return 4 * 8 * R + 1; }
+template <int R>
+constexpr size_t gla_bwd_stage_bytes() { return (size_t)2 * stage_steps(gla_bwd_wmax<R>()) * gla_bwd_wmax<R>() * sizeof(float); }
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
@@ -60,22 +90,64 @@ ssd_seq_fwd_kernel(const T* __restrict__ u, const T* __restrict__ delta, const T
       st[r][k] = (h0 != nullptr && n < N) ? h0[((b * H + h) * Dh + warp + 8 * r) * (int64_t)N + n] : 0.f;
     }
 
-  for (int t = 0; t < L; ++t) {
+  // staged step rows [B (N) | C (N) | u (Dh) | delta (1)], TS steps per buffer
+  constexpr int WMAX = 2 * 32 * NK + 8 * R + 1;
+  constexpr int TS = stage_steps(WMAX);
+  constexpr int EPT = (TS * WMAX + kSeqThreads - 1) / kSeqThreads;
+  __shared__ float sIn[2][TS * WMAX];
+  const int W = 2 * N + Dh + 1;
+  StepStage<EPT> pre;
+  auto load_block = [&](int t0) {
+#pragma unroll
+    for (int i = 0; i < EPT; ++i) {
+      const int e = threadIdx.x + kSeqThreads * i;
+      float v = 0.f;
+      if (e < TS * W) {
+        const int tt = e / W, col = e - tt * W, t = t0 + tt;
+        if (t < L) {
+          const int64_t row = (b * L + t) * H + h;
+          v = col < N           ? to_f(Bm[row * N + col])
+              : col < 2 * N      ? to_f(Cm[row * N + col - N])
+              : col < 2 * N + Dh ? to_f(u[row * Dh + col - 2 * N])
+                                 : to_f(delta[row]);
+        }
+      }
+      pre.r[i] = v;
+    }
+  };
+  auto store_block = [&](int buf) {
+#pragma unroll
+    for (int i = 0; i < EPT; ++i) {
+      const int e = threadIdx.x + kSeqThreads * i;
+      if (e < TS * W) sIn[buf][e] = pre.r[i];
+    }
+  };
+  const int nblk = (L + TS - 1) / TS;
+  load_block(0);
+  store_block(0);
+  __syncthreads();
+
+  for (int blk = 0; blk < nblk; ++blk) {
+  if (blk + 1 < nblk) load_block((blk + 1) * TS);
+  const int nt = min(TS, L - blk * TS);
+  for (int tt = 0; tt < nt; ++tt) {
+    const int t = blk * TS + tt;
     const int64_t row = (b * L + t) * H + h;
-    const float dt = to_f(delta[row]);
+    const float* sr = sIn[blk & 1] + tt * W;
+    const float dt = sr[2 * N + Dh];
     float dB[NK], cv[NK], dec[NK];
 #pragma unroll
     for (int k = 0; k < NK; ++k) {
       const int n = lane + 32 * k;
       const bool ok = n < N;
-      dB[k] = ok ? dt * to_f(Bm[row * N + n]) : 0.f;
-      cv[k] = ok ? to_f(Cm[row * N + n]) : 0.f;
+      dB[k] = ok ? dt * sr[n] : 0.f;
+      cv[k] = ok ? sr[N + n] : 0.f;
       dec[k] = ok ? expf(dt * An[k]) : 0.f;
     }
 #pragma unroll
     for (int r = 0; r < R; ++r) {
       const int d = warp + 8 * r;
-      const float ud = to_f(u[row * Dh + d]);
+      const float ud = sr[2 * N + d];
       float acc = 0.f;
 #pragma unroll
       for (int k = 0; k < NK; ++k) {
@@ -97,6 +169,9 @@ ssd_seq_fwd_kernel(const T* __restrict__ u, const T* __restrict__ delta, const T
         }
     }
   }
+  if (blk + 1 < nblk) store_block((blk + 1) & 1);
+  __syncthreads();  // the next block reads the buffer written above; this one is refilled after it
+  }
 }
 
 template <typename T, int R, int NK>
@@ -112,6 +187,13 @@ ssd_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfina
   __shared__ float pB[kTS][8][NP];
   __shared__ float pC[kTS][8][NP];
   __shared__ float pdt[kTS][8];
+  // staged step rows (dynamic shared memory, two buffers of TS steps): the recompute
+  // reads [B (N) | u (Dh) | delta], the adjoint sweep [B (N) | C (N) | u (Dh) | grad_y (Dh) | delta]
+  constexpr int WMAX = ssd_bwd_wmax<R, NK>();
+  constexpr int TS = stage_steps(WMAX);
+  constexpr int EPT = (TS * WMAX + kSeqThreads - 1) / kSeqThreads;
+  extern __shared__ float sIn[];  // [2][TS * WMAX]
+  StepStage<EPT> pre;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nseg = L / seg;
@@ -131,6 +213,43 @@ ssd_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfina
     const int n = lane + 32 * k;
     An[k] = n < N ? A[h * ash + n * asn] : 0.f;
   }
+  // steps tl0 .. tl0 + n - 1 of segment s into the registers, in the recompute's (adj = false)
+  // or the adjoint sweep's row layout
+  const int Wa = N + Dh + 1, Wb = 2 * N + 2 * Dh + 1;
+  auto load_steps = [&](int s, int tl0, int n, bool adjl) {
+    const int W = adjl ? Wb : Wa;
+#pragma unroll
+    for (int i = 0; i < EPT; ++i) {
+      const int e = threadIdx.x + kSeqThreads * i;
+      float v = 0.f;
+      if (e < n * W) {
+        const int tt = e / W, col = e - tt * W;
+        const int64_t rowt = (b * L + (int64_t)s * seg + tl0 + tt);
+        const int64_t row = rowt * H + h;
+        if (!adjl) {
+          v = col < N ? to_f(Bm[row * N + col]) : col < N + Dh ? to_f(u[row * Dh + col - N]) : to_f(delta[row]);
+        } else {
+          v = col < N            ? to_f(Bm[row * N + col])
+              : col < 2 * N      ? to_f(Cm[row * N + col - N])
+              : col < 2 * N + Dh ? to_f(u[row * Dh + col - 2 * N])
+              : col < 2 * N + 2 * Dh ? gy[row * Dh + col - 2 * N - Dh]
+                                     : to_f(delta[row]);
+        }
+      }
+      pre.r[i] = v;
+    }
+  };
+  auto store_steps = [&](int buf, int n, bool adjl) {
+    const int W = adjl ? Wb : Wa;
+#pragma unroll
+    for (int i = 0; i < EPT; ++i) {
+      const int e = threadIdx.x + kSeqThreads * i;
+      if (e < n * W) sIn[buf * TS * WMAX + e] = pre.r[i];
+    }
+  };
+  const int nb = (seg + TS - 1) / TS;  // staged blocks per segment
+  auto blk_n = [&](int j) { return min(TS, seg - j * TS); };
+
   float adj[R][NK], gAacc[NK];
 #pragma unroll
   for (int k = 0; k < NK; ++k) gAacc[k] = 0.f;
@@ -160,42 +279,78 @@ ssd_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfina
                                            : 0.f;
           scr[(int64_t)(r * NK + k) * kSeqThreads] = st[r][k];
         }
-      for (int tl = 0; tl < seg; ++tl) {
-        const int64_t row = (b * L + (int64_t)s * seg + tl) * H + h;
-        const float dt = to_f(delta[row]);
-        float dB[NK], dec[NK];
-#pragma unroll
-        for (int k = 0; k < NK; ++k) {
-          const int n = lane + 32 * k;
-          dB[k] = n < N ? dt * to_f(Bm[row * N + n]) : 0.f;
-          dec[k] = n < N ? expf(dt * An[k]) : 0.f;
-        }
-        float* sp = scr + (int64_t)(tl + 1) * E * kSeqThreads;
-#pragma unroll
-        for (int r = 0; r < R; ++r) {
-          const float ud = to_f(u[row * Dh + warp + 8 * r]);
+      load_steps(s, 0, blk_n(0), false);
+      store_steps(0, blk_n(0), false);
+      __syncthreads();
+      for (int j = 0; j < nb; ++j) {
+        if (j + 1 < nb) load_steps(s, (j + 1) * TS, blk_n(j + 1), false);
+        const float* sb = sIn + (j & 1) * TS * WMAX;
+        for (int tt = 0; tt < blk_n(j); ++tt) {
+          const int tl = j * TS + tt;
+          const float* sr = sb + tt * Wa;
+          const float dt = sr[N + Dh];
+          float dB[NK], dec[NK];
 #pragma unroll
           for (int k = 0; k < NK; ++k) {
-            st[r][k] = dec[k] * st[r][k] + dB[k] * ud;
-            sp[(int64_t)(r * NK + k) * kSeqThreads] = st[r][k];
+            const int n = lane + 32 * k;
+            dB[k] = n < N ? dt * sr[n] : 0.f;
+            dec[k] = n < N ? expf(dt * An[k]) : 0.f;
+          }
+          float* sp = scr + (int64_t)(tl + 1) * E * kSeqThreads;
+#pragma unroll
+          for (int r = 0; r < R; ++r) {
+            const float ud = sr[N + warp + 8 * r];
+#pragma unroll
+            for (int k = 0; k < NK; ++k) {
+              st[r][k] = dec[k] * st[r][k] + dB[k] * ud;
+              sp[(int64_t)(r * NK + k) * kSeqThreads] = st[r][k];
+            }
           }
         }
+        if (j + 1 < nb) store_steps((j + 1) & 1, blk_n(j + 1), false);
+        __syncthreads();
       }
     }
 
-    // ---- adjoint sweep, newest -> oldest (ssd.py:204-260)
-    for (int tl = seg - 1; tl >= 0; --tl) {
+    // ---- adjoint sweep, newest -> oldest (ssd.py:204-260), its inputs staged block by block
+    load_steps(s, (nb - 1) * TS, blk_n(nb - 1), true);
+    store_steps(0, blk_n(nb - 1), true);
+    __syncthreads();
+    // The recomputed states of steps tl + 1 and tl in registers, the one of step tl - 1
+    // loaded a step ahead (where a thread holds at most 16 state values): the scratch is
+    // read from L2 and its latency was on every step's path.
+    constexpr bool kRing = E <= 16;
+    constexpr int EP = kRing ? E : 1;
+    float hcr[EP], hpr[EP];
+    if constexpr (kRing) {
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        hcr[e] = scr[((int64_t)seg * E + e) * kSeqThreads];
+        hpr[e] = scr[((int64_t)(seg - 1) * E + e) * kSeqThreads];
+      }
+    }
+    for (int j = nb - 1, q = 0; j >= 0; --j, ++q) {
+    if (j > 0) load_steps(s, (j - 1) * TS, blk_n(j - 1), true);
+    const float* sbuf = sIn + (q & 1) * TS * WMAX;
+    for (int tl = j * TS + blk_n(j) - 1; tl >= j * TS; --tl) {
+      float hnr[EP];
+      if constexpr (kRing)
+        if (tl > 0) {
+#pragma unroll
+          for (int e = 0; e < E; ++e) hnr[e] = scr[((int64_t)(tl - 1) * E + e) * kSeqThreads];
+        }
       const int slot = (seg - 1 - tl) % kTS;
       const int64_t t = (int64_t)s * seg + tl;
       const int64_t row = (b * L + t) * H + h;
-      const float dt = to_f(delta[row]);
+      const float* sr = sbuf + (tl - j * TS) * Wb;
+      const float dt = sr[2 * N + 2 * Dh];
       float bv[NK], cv[NK], dec[NK];
 #pragma unroll
       for (int k = 0; k < NK; ++k) {
         const int n = lane + 32 * k;
         const bool ok = n < N;
-        bv[k] = ok ? to_f(Bm[row * N + n]) : 0.f;
-        cv[k] = ok ? to_f(Cm[row * N + n]) : 0.f;
+        bv[k] = ok ? sr[n] : 0.f;
+        cv[k] = ok ? sr[N + n] : 0.f;
         dec[k] = ok ? expf(dt * An[k]) : 0.f;
       }
       const float* sc = scr + (int64_t)(tl + 1) * E * kSeqThreads;
@@ -206,13 +361,13 @@ ssd_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfina
 #pragma unroll
       for (int r = 0; r < R; ++r) {
         const int d = warp + 8 * r;
-        const float ud = to_f(u[row * Dh + d]);
-        const float g = gy[row * Dh + d];
+        const float ud = sr[2 * N + d];
+        const float g = sr[2 * N + Dh + d];
         float gu_r = 0.f;
 #pragma unroll
         for (int k = 0; k < NK; ++k) {
-          const float hc = sc[(int64_t)(r * NK + k) * kSeqThreads];
-          const float hp = sprev[(int64_t)(r * NK + k) * kSeqThreads];
+          const float hc = kRing ? hcr[kRing ? r * NK + k : 0] : sc[(int64_t)(r * NK + k) * kSeqThreads];
+          const float hp = kRing ? hpr[kRing ? r * NK + k : 0] : sprev[(int64_t)(r * NK + k) * kSeqThreads];
           float ad = adj[r][k] + g * cv[k];
           gu_r += ad * dt * bv[k];
           gdt += ad * (An[k] * dec[k] * hp + bv[k] * ud);
@@ -256,6 +411,16 @@ ssd_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfina
         }
         __syncthreads();
       }
+      if constexpr (kRing) {
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          hcr[e] = hpr[e];
+          hpr[e] = hnr[e];
+        }
+      }
+    }
+    if (j > 0) store_steps((q + 1) & 1, blk_n(j - 1), true);
+    __syncthreads();
     }
   }
 
@@ -319,19 +484,61 @@ gla_seq_fwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __
     for (int r = 0; r < R; ++r)
       S[i][r] = h0 != nullptr ? h0[((b * H + h) * Dh + lane + 32 * i) * (int64_t)Dh + warp + 8 * r] : 0.f;
 
-  for (int t = 0; t < L; ++t) {
+  // staged step rows [k (Dh) | q (Dh) | v (Dh) | gate], TS steps per buffer
+  constexpr int WMAX = 3 * 8 * R + 1;
+  constexpr int TS = stage_steps(WMAX);
+  constexpr int EPT = (TS * WMAX + kSeqThreads - 1) / kSeqThreads;
+  __shared__ float sIn[2][TS * WMAX];
+  const int W = 3 * Dh + 1;
+  StepStage<EPT> pre;
+  auto load_block = [&](int t0) {
+#pragma unroll
+    for (int i = 0; i < EPT; ++i) {
+      const int e = threadIdx.x + kSeqThreads * i;
+      float x = 0.f;
+      if (e < TS * W) {
+        const int tt = e / W, col = e - tt * W, t = t0 + tt;
+        if (t < L) {
+          const int64_t row = (b * L + t) * H + h;
+          x = col < Dh       ? to_f(k[row * Dh + col])
+              : col < 2 * Dh ? to_f(q[row * Dh + col - Dh])
+              : col < 3 * Dh ? to_f(v[row * Dh + col - 2 * Dh])
+                             : to_f(gates[row]);
+        }
+      }
+      pre.r[i] = x;
+    }
+  };
+  auto store_block = [&](int buf) {
+#pragma unroll
+    for (int i = 0; i < EPT; ++i) {
+      const int e = threadIdx.x + kSeqThreads * i;
+      if (e < TS * W) sIn[buf][e] = pre.r[i];
+    }
+  };
+  const int nblk = (L + TS - 1) / TS;
+  load_block(0);
+  store_block(0);
+  __syncthreads();
+
+  for (int blk = 0; blk < nblk; ++blk) {
+  if (blk + 1 < nblk) load_block((blk + 1) * TS);
+  const int nt = min(TS, L - blk * TS);
+  for (int tt = 0; tt < nt; ++tt) {
+    const int t = blk * TS + tt;
     const int64_t row = (b * L + t) * H + h;
-    const float g = to_f(gates[row]);
+    const float* sr = sIn[blk & 1] + tt * W;
+    const float g = sr[3 * Dh];
     float ki[IK], qi[IK];
 #pragma unroll
     for (int i = 0; i < IK; ++i) {
-      ki[i] = to_f(k[row * Dh + lane + 32 * i]);
-      qi[i] = to_f(q[row * Dh + lane + 32 * i]);
+      ki[i] = sr[lane + 32 * i];
+      qi[i] = sr[Dh + lane + 32 * i];
     }
 #pragma unroll
     for (int r = 0; r < R; ++r) {
       const int j = warp + 8 * r;
-      const float vj = to_f(v[row * Dh + j]);
+      const float vj = sr[2 * Dh + j];
       float o = 0.f;
 #pragma unroll
       for (int i = 0; i < IK; ++i) {
@@ -350,6 +557,9 @@ gla_seq_fwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __
         for (int r = 0; r < R; ++r) ck[(int64_t)(lane + 32 * i) * Dh + warp + 8 * r] = S[i][r];
     }
   }
+  if (blk + 1 < nblk) store_block((blk + 1) & 1);
+  __syncthreads();  // the next block reads the buffer written above; this one is refilled after it
+  }
 }
 
 template <typename T, int R, int IK>
@@ -364,6 +574,13 @@ gla_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfina
   __shared__ float pQ[kTS][8][NP];
   __shared__ float pK[kTS][8][NP];
   __shared__ float pg[kTS][8];
+  // staged step rows (dynamic shared memory, two buffers of TS steps): the recompute reads
+  // [k (Dh) | v (Dh) | gate], the adjoint sweep [k (Dh) | q (Dh) | v (Dh) | grad_y (Dh) | gate]
+  constexpr int WMAX = gla_bwd_wmax<R>();
+  constexpr int TS = stage_steps(WMAX);
+  constexpr int EPT = (TS * WMAX + kSeqThreads - 1) / kSeqThreads;
+  extern __shared__ float sIn[];  // [2][TS * WMAX]
+  StepStage<EPT> pre;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nseg = L / seg;
@@ -374,6 +591,42 @@ gla_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfina
     const int64_t b = unit / H;
     const int h = unit % H;
     if (only_marked && !isnan(to_f(gg[b * L * H + h]))) continue;
+
+    // steps tl0 .. tl0 + n - 1 of segment s into the registers, in the recompute's (adjl =
+    // false) or the adjoint sweep's row layout
+    const int Wa = 2 * Dh + 1, Wb = 4 * Dh + 1;
+    auto load_steps = [&](int s, int tl0, int n, bool adjl) {
+      const int W = adjl ? Wb : Wa;
+#pragma unroll
+      for (int i = 0; i < EPT; ++i) {
+        const int e = threadIdx.x + kSeqThreads * i;
+        float x = 0.f;
+        if (e < n * W) {
+          const int tt = e / W, col = e - tt * W;
+          const int64_t row = (b * L + (int64_t)s * seg + tl0 + tt) * H + h;
+          if (!adjl) {
+            x = col < Dh ? to_f(k[row * Dh + col]) : col < 2 * Dh ? to_f(v[row * Dh + col - Dh]) : to_f(gates[row]);
+          } else {
+            x = col < Dh           ? to_f(k[row * Dh + col])
+                : col < 2 * Dh     ? to_f(q[row * Dh + col - Dh])
+                : col < 3 * Dh     ? to_f(v[row * Dh + col - 2 * Dh])
+                : col < 4 * Dh     ? gy[row * Dh + col - 3 * Dh]
+                                   : to_f(gates[row]);
+          }
+        }
+        pre.r[i] = x;
+      }
+    };
+    auto store_steps = [&](int buf, int n, bool adjl) {
+      const int W = adjl ? Wb : Wa;
+#pragma unroll
+      for (int i = 0; i < EPT; ++i) {
+        const int e = threadIdx.x + kSeqThreads * i;
+        if (e < n * W) sIn[buf * TS * WMAX + e] = pre.r[i];
+      }
+    };
+    const int nb = (seg + TS - 1) / TS;  // staged blocks per segment
+    auto blk_n = [&](int j) { return min(TS, seg - j * TS); };
 
     float adj[IK][R];
 #pragma unroll
@@ -396,35 +649,70 @@ gla_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfina
             S[i][r] = s > 0 ? ck[e] : h0 != nullptr ? h0[(b * H + h) * (int64_t)Dh * Dh + e] : 0.f;
             scr[(int64_t)(i * R + r) * kSeqThreads] = S[i][r];
           }
-        for (int tl = 0; tl < seg; ++tl) {
-          const int64_t row = (b * L + (int64_t)s * seg + tl) * H + h;
-          const float g = to_f(gates[row]);
-          float ki[IK];
+        load_steps(s, 0, blk_n(0), false);
+        store_steps(0, blk_n(0), false);
+        __syncthreads();
+        for (int jb = 0; jb < nb; ++jb) {
+          if (jb + 1 < nb) load_steps(s, (jb + 1) * TS, blk_n(jb + 1), false);
+          const float* sb = sIn + (jb & 1) * TS * WMAX;
+          for (int tt = 0; tt < blk_n(jb); ++tt) {
+            const int tl = jb * TS + tt;
+            const float* sr = sb + tt * Wa;
+            const float g = sr[2 * Dh];
+            float ki[IK];
 #pragma unroll
-          for (int i = 0; i < IK; ++i) ki[i] = to_f(k[row * Dh + lane + 32 * i]);
-          float* sp = scr + (int64_t)(tl + 1) * E * kSeqThreads;
+            for (int i = 0; i < IK; ++i) ki[i] = sr[lane + 32 * i];
+            float* sp = scr + (int64_t)(tl + 1) * E * kSeqThreads;
 #pragma unroll
-          for (int r = 0; r < R; ++r) {
-            const float vj = to_f(v[row * Dh + warp + 8 * r]);
+            for (int r = 0; r < R; ++r) {
+              const float vj = sr[Dh + warp + 8 * r];
 #pragma unroll
-            for (int i = 0; i < IK; ++i) {
-              S[i][r] = g * S[i][r] + ki[i] * vj;
-              sp[(int64_t)(i * R + r) * kSeqThreads] = S[i][r];
+              for (int i = 0; i < IK; ++i) {
+                S[i][r] = g * S[i][r] + ki[i] * vj;
+                sp[(int64_t)(i * R + r) * kSeqThreads] = S[i][r];
+              }
             }
           }
+          if (jb + 1 < nb) store_steps((jb + 1) & 1, blk_n(jb + 1), false);
+          __syncthreads();
         }
       }
 
-      for (int tl = seg - 1; tl >= 0; --tl) {
+      load_steps(s, (nb - 1) * TS, blk_n(nb - 1), true);
+      store_steps(0, blk_n(nb - 1), true);
+      __syncthreads();
+      // the recomputed states of steps tl + 1 and tl in registers, step tl - 1's loaded a
+      // step ahead (at most 16 state values a thread), as in the SSD backward
+      constexpr bool kRing = E <= 16;
+      constexpr int EP = kRing ? E : 1;
+      float hcr[EP], hpr[EP];
+      if constexpr (kRing) {
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          hcr[e] = scr[((int64_t)seg * E + e) * kSeqThreads];
+          hpr[e] = scr[((int64_t)(seg - 1) * E + e) * kSeqThreads];
+        }
+      }
+      for (int jb = nb - 1, qb = 0; jb >= 0; --jb, ++qb) {
+      if (jb > 0) load_steps(s, (jb - 1) * TS, blk_n(jb - 1), true);
+      const float* sbuf = sIn + (qb & 1) * TS * WMAX;
+      for (int tl = jb * TS + blk_n(jb) - 1; tl >= jb * TS; --tl) {
+        float hnr[EP];
+        if constexpr (kRing)
+          if (tl > 0) {
+#pragma unroll
+            for (int e = 0; e < E; ++e) hnr[e] = scr[((int64_t)(tl - 1) * E + e) * kSeqThreads];
+          }
         const int slot = (seg - 1 - tl) % kTS;
         const int64_t t = (int64_t)s * seg + tl;
         const int64_t row = (b * L + t) * H + h;
-        const float g = to_f(gates[row]);
+        const float* sr = sbuf + (tl - jb * TS) * Wb;
+        const float g = sr[4 * Dh];
         float ki[IK], qi[IK];
 #pragma unroll
         for (int i = 0; i < IK; ++i) {
-          ki[i] = to_f(k[row * Dh + lane + 32 * i]);
-          qi[i] = to_f(q[row * Dh + lane + 32 * i]);
+          ki[i] = sr[lane + 32 * i];
+          qi[i] = sr[Dh + lane + 32 * i];
         }
         const float* sc = scr + (int64_t)(tl + 1) * E * kSeqThreads;
         const float* sprev = scr + (int64_t)tl * E * kSeqThreads;
@@ -434,13 +722,13 @@ gla_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfina
 #pragma unroll
         for (int r = 0; r < R; ++r) {
           const int j = warp + 8 * r;
-          const float vj = to_f(v[row * Dh + j]);
-          const float go = gy[row * Dh + j];
+          const float vj = sr[2 * Dh + j];
+          const float go = sr[3 * Dh + j];
           float gv_r = 0.f;
 #pragma unroll
           for (int i = 0; i < IK; ++i) {
-            const float hc = sc[(int64_t)(i * R + r) * kSeqThreads];
-            const float hp = sprev[(int64_t)(i * R + r) * kSeqThreads];
+            const float hc = kRing ? hcr[kRing ? i * R + r : 0] : sc[(int64_t)(i * R + r) * kSeqThreads];
+            const float hp = kRing ? hpr[kRing ? i * R + r : 0] : sprev[(int64_t)(i * R + r) * kSeqThreads];
             const float ad = adj[i][r] + qi[i] * go;  // gla.py:213
             gv_r += ad * ki[i];
             ggs += ad * hp;
@@ -481,6 +769,16 @@ gla_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfina
           }
           __syncthreads();
         }
+        if constexpr (kRing) {
+#pragma unroll
+          for (int e = 0; e < E; ++e) {
+            hcr[e] = hpr[e];
+            hpr[e] = hnr[e];
+          }
+        }
+      }
+      if (jb > 0) store_steps((qb + 1) & 1, blk_n(jb - 1), true);
+      __syncthreads();
       }
     }
     // gradient of the initial state: the adjoint carried past step 0
@@ -581,12 +879,17 @@ static void ssd_bwd_nk(int nk, dim3 g, cudaStream_t st, const float* gy, const f
                        const float* A, int64_t ash, int64_t asn, int L, int H, int Dh, int N, int seg,
                        T* gu, T* gd, T* gB, T* gC, float* gAp, float* scr, const float* h0, float* gh0,
                        int units, int om) {
+  auto go = [&](auto kern, size_t sm) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    kern<<<g, kSeqThreads, sm, st>>>(gy, gf, ck, u, dl, Bm, Cm, A, ash, asn, L, H, Dh, N, seg, gu, gd, gB, gC, gAp,
+                                     scr, h0, gh0, units, om);
+  };
   if (nk == 1)
-    ssd_seq_bwd_kernel<T, R, 1><<<g, kSeqThreads, 0, st>>>(gy, gf, ck, u, dl, Bm, Cm, A, ash, asn, L, H, Dh, N, seg, gu, gd, gB, gC, gAp, scr, h0, gh0, units, om);
+    go(ssd_seq_bwd_kernel<T, R, 1>, ssd_bwd_stage_bytes<R, 1>());
   else if (nk == 2)
-    ssd_seq_bwd_kernel<T, R, 2><<<g, kSeqThreads, 0, st>>>(gy, gf, ck, u, dl, Bm, Cm, A, ash, asn, L, H, Dh, N, seg, gu, gd, gB, gC, gAp, scr, h0, gh0, units, om);
+    go(ssd_seq_bwd_kernel<T, R, 2>, ssd_bwd_stage_bytes<R, 2>());
   else
-    ssd_seq_bwd_kernel<T, R, 4><<<g, kSeqThreads, 0, st>>>(gy, gf, ck, u, dl, Bm, Cm, A, ash, asn, L, H, Dh, N, seg, gu, gd, gB, gC, gAp, scr, h0, gh0, units, om);
+    go(ssd_seq_bwd_kernel<T, R, 4>, ssd_bwd_stage_bytes<R, 4>());
 }
 
 template <typename T>
@@ -671,11 +974,16 @@ int gla_seq_bwd_launch(const float* gy, const float* gf, const float* ckpt, cons
   // only_bad: a few CTAs walk the units and recompute the marked ones
   const int flags = only_bad ? 1 : 0;
   dim3 grid((unsigned)(only_bad ? (units < kGlaFallbackSlots ? units : kGlaFallbackSlots) : units));
+  auto go = [&](auto kern, int dh, size_t sm) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    kern<<<grid, kSeqThreads, sm, st>>>(gy, gf, ckpt, q_, k_, v_, g_, L_, H_, dh, s_, gq_, gk_, gv_, gg_, scr, u_, flags,
+                                        h0, gh0);
+  };
   switch ((int)Dh) {
-    case 32: gla_seq_bwd_kernel<T, 4, 1><<<grid, kSeqThreads, 0, st>>>(gy, gf, ckpt, q_, k_, v_, g_, L_, H_, 32, s_, gq_, gk_, gv_, gg_, scr, u_, flags, h0, gh0); break;
-    case 64: gla_seq_bwd_kernel<T, 8, 2><<<grid, kSeqThreads, 0, st>>>(gy, gf, ckpt, q_, k_, v_, g_, L_, H_, 64, s_, gq_, gk_, gv_, gg_, scr, u_, flags, h0, gh0); break;
-    case 96: gla_seq_bwd_kernel<T, 12, 3><<<grid, kSeqThreads, 0, st>>>(gy, gf, ckpt, q_, k_, v_, g_, L_, H_, 96, s_, gq_, gk_, gv_, gg_, scr, u_, flags, h0, gh0); break;
-    default: gla_seq_bwd_kernel<T, 16, 4><<<grid, kSeqThreads, 0, st>>>(gy, gf, ckpt, q_, k_, v_, g_, L_, H_, 128, s_, gq_, gk_, gv_, gg_, scr, u_, flags, h0, gh0); break;
+    case 32: go(gla_seq_bwd_kernel<T, 4, 1>, 32, gla_bwd_stage_bytes<4>()); break;
+    case 64: go(gla_seq_bwd_kernel<T, 8, 2>, 64, gla_bwd_stage_bytes<8>()); break;
+    case 96: go(gla_seq_bwd_kernel<T, 12, 3>, 96, gla_bwd_stage_bytes<12>()); break;
+    default: go(gla_seq_bwd_kernel<T, 16, 4>, 128, gla_bwd_stage_bytes<16>()); break;
   }
   return check_launch("gla_seq_bwd_kernel");
 }
