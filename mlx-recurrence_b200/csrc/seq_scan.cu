@@ -51,6 +51,39 @@ constexpr int gla_bwd_wmax() { return 4 * 8 * R + 1; }
 template <int R>
 constexpr size_t gla_bwd_stage_bytes() { return (size_t)2 * stage_steps(gla_bwd_wmax<R>()) * gla_bwd_wmax<R>() * sizeof(float); }
 
+// The warp totals of R per-lane values at once (R rows of a step's outputs): a
+// transposing butterfly, where each exchange hands over half of the values still
+// held, so the R sums take log2(32) levels of dependent shuffles instead of R times
+// as many. Returns the total of row (lane >> (5 - log2 RP)) (RP: R rounded up to a
+// power of two, rows R.. are zero); every lane of a row's group holds it.
+constexpr int pow2_ceil(int r) { return r <= 1 ? 1 : r <= 2 ? 2 : r <= 4 ? 4 : r <= 8 ? 8 : r <= 16 ? 16 : 32; }
+// lanes sharing a row's total in warp_sum_rows<R>; the first of each group stores it
+template <int R>
+__device__ __forceinline__ bool row_leader(int lane) { return (lane & (32 / pow2_ceil(R) - 1)) == 0; }
+template <int R>
+__device__ __forceinline__ float warp_sum_rows(const float (&x)[R], int lane, int& row) {
+  constexpr int RP = pow2_ceil(R);
+  constexpr int LG = RP == 1 ? 0 : RP == 2 ? 1 : RP == 4 ? 2 : RP == 8 ? 3 : RP == 16 ? 4 : 5;
+  float v[RP];
+#pragma unroll
+  for (int i = 0; i < RP; ++i) v[i] = i < R ? x[i] : 0.f;
+  int o = 16;
+#pragma unroll
+  for (int live = RP; live > 1; live >>= 1, o >>= 1) {
+    const bool hi = (lane & o) != 0;
+#pragma unroll
+    for (int i = 0; i < live / 2; ++i) {
+      const float send = hi ? v[i] : v[i + live / 2];
+      const float keep = hi ? v[i + live / 2] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+    }
+  }
+#pragma unroll
+  for (; o > 0; o >>= 1) v[0] += __shfl_xor_sync(0xffffffffu, v[0], o);
+  row = lane >> (5 - LG);
+  return v[0];
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -144,6 +177,7 @@ ssd_seq_fwd_kernel(const T* __restrict__ u, const T* __restrict__ delta, const T
       cv[k] = ok ? sr[N + n] : 0.f;
       dec[k] = ok ? expf(dt * An[k]) : 0.f;
     }
+    float accs[R];
 #pragma unroll
     for (int r = 0; r < R; ++r) {
       const int d = warp + 8 * r;
@@ -154,8 +188,12 @@ ssd_seq_fwd_kernel(const T* __restrict__ u, const T* __restrict__ delta, const T
         st[r][k] = dec[k] * st[r][k] + dB[k] * ud;  // ssd.py:97-98
         acc += st[r][k] * cv[k];                    // ssd.py:99
       }
-      acc = warp_sum(acc);
-      if (lane == 0) y[row * Dh + d] = acc;
+      accs[r] = acc;
+    }
+    {
+      int ri;
+      const float tot = warp_sum_rows<R>(accs, lane, ri);
+      if (row_leader<R>(lane) && ri < R) y[row * Dh + warp + 8 * ri] = tot;
     }
     if ((t + 1) % seg == 0) {
       const int64_t s = (t + 1) / seg - 1;
@@ -175,7 +213,7 @@ ssd_seq_fwd_kernel(const T* __restrict__ u, const T* __restrict__ delta, const T
 }
 
 template <typename T, int R, int NK>
-__global__ void __launch_bounds__(kSeqThreads)
+__global__ void __launch_bounds__(kSeqThreads, 1)  // registers over occupancy: the per-step chain is latency-bound
 ssd_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfinal,
                    const float* __restrict__ ckpt, const T* __restrict__ u,
                    const T* __restrict__ delta, const T* __restrict__ Bm, const T* __restrict__ Cm,
@@ -355,7 +393,7 @@ ssd_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfina
       }
       const float* sc = scr + (int64_t)(tl + 1) * E * kSeqThreads;
       const float* sprev = scr + (int64_t)tl * E * kSeqThreads;
-      float gdt = 0.f, pb[NK], pc[NK];
+      float gdt = 0.f, pb[NK], pc[NK], gus[R];
 #pragma unroll
       for (int k = 0; k < NK; ++k) pb[k] = pc[k] = 0.f;
 #pragma unroll
@@ -376,8 +414,12 @@ ssd_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfina
           pc[k] += hc * g;
           adj[r][k] = ad * dec[k];
         }
-        gu_r = warp_sum(gu_r);
-        if (lane == 0) gu[row * Dh + d] = from_f<T>(gu_r);
+        gus[r] = gu_r;
+      }
+      {
+        int ri;
+        const float tot = warp_sum_rows<R>(gus, lane, ri);
+        if (row_leader<R>(lane) && ri < R) gu[row * Dh + warp + 8 * ri] = from_f<T>(tot);
       }
       gdt = warp_sum(gdt);
       if (lane == 0) pdt[slot][warp] = gdt;
@@ -535,6 +577,7 @@ gla_seq_fwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __
       ki[i] = sr[lane + 32 * i];
       qi[i] = sr[Dh + lane + 32 * i];
     }
+    float os[R];
 #pragma unroll
     for (int r = 0; r < R; ++r) {
       const int j = warp + 8 * r;
@@ -545,8 +588,12 @@ gla_seq_fwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __
         S[i][r] = g * S[i][r] + ki[i] * vj;  // gla.py:87
         o += qi[i] * S[i][r];                // gla.py:88
       }
-      o = warp_sum(o);
-      if (lane == 0) y[row * Dh + j] = o;
+      os[r] = o;
+    }
+    {
+      int ri;
+      const float tot = warp_sum_rows<R>(os, lane, ri);
+      if (row_leader<R>(lane) && ri < R) y[row * Dh + warp + 8 * ri] = tot;
     }
     if ((t + 1) % seg == 0) {
       const int64_t s = (t + 1) / seg - 1;
@@ -563,7 +610,7 @@ gla_seq_fwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __
 }
 
 template <typename T, int R, int IK>
-__global__ void __launch_bounds__(kSeqThreads)
+__global__ void __launch_bounds__(kSeqThreads, 1)  // as the SSD backward
 gla_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfinal,
                    const float* __restrict__ ckpt, const T* __restrict__ q,
                    const T* __restrict__ k, const T* __restrict__ v, const T* __restrict__ gates,
@@ -716,7 +763,7 @@ gla_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfina
         }
         const float* sc = scr + (int64_t)(tl + 1) * E * kSeqThreads;
         const float* sprev = scr + (int64_t)tl * E * kSeqThreads;
-        float ggs = 0.f, pq[IK], pk[IK];
+        float ggs = 0.f, pq[IK], pk[IK], gvs[R];
 #pragma unroll
         for (int i = 0; i < IK; ++i) pq[i] = pk[i] = 0.f;
 #pragma unroll
@@ -736,8 +783,12 @@ gla_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfina
             pk[i] += ad * vj;
             adj[i][r] = ad * g;
           }
-          gv_r = warp_sum(gv_r);
-          if (lane == 0) gv[row * Dh + j] = from_f<T>(gv_r);
+          gvs[r] = gv_r;
+        }
+        {
+          int ri;
+          const float tot = warp_sum_rows<R>(gvs, lane, ri);
+          if (row_leader<R>(lane) && ri < R) gv[row * Dh + warp + 8 * ri] = from_f<T>(tot);
         }
         ggs = warp_sum(ggs);
         if (lane == 0) pg[slot][warp] = ggs;
