@@ -673,8 +673,8 @@ def _report(args, ctx, P, M, e2e_ms, h2d, d2h):
             "value": tok * args.steps / (e2e_ms * 1e-3), "unit": "tokens/s",
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "copies": "H2D of every input and grad_y from pinned memory; D2H of y and every input gradient "
-                      "into pinned memory; inside the timed region, pipelined across steps on two copy "
-                      "streams (double-buffered device inputs)"},
+                      "into pinned memory; inside the timed region, each step's batch in row slices "
+                      "pipelined on two copy streams (double-buffered device inputs)"},
     }
     m.pop("value")
     out.update(m)
