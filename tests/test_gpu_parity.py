@@ -129,6 +129,10 @@ EDGE = [
     ("gla", (1, 48, 3, 32), 16),
     ("gla", (1, 64, 2, 96), 64),
     ("gla", (1, 32, 1, 128), 32),
+    # the per-step kernels stage 16 steps (fewer for wide rows) at a time: L and seg that
+    # leave partial staged blocks in the forward and in the backward's segments
+    ("ssd", (2, 40, 2, 64, 16), 20),
+    ("gla", (2, 40, 2, 64), 20),
 ]
 
 
