@@ -27,6 +27,28 @@ constexpr int stage_steps(int wmax) {
   return 16 * kSeqThreads / wmax < kStage ? (16 * kSeqThreads / wmax < 1 ? 1 : 16 * kSeqThreads / wmax) : kStage;
 }
 
+// The first unit at or after `unit` in a CTA's walk (unit, + stride, ...) whose flag
+// element (`flag(b * L * H + h)`, b = unit / H, h = unit % H) is NaN, or `units` when
+// none is left. kSeqThreads candidates are read at once, one load per thread: a walk
+// that tested one unit per iteration put a global load's latency on the path of every
+// unit it skipped. Called by every thread of the CTA.
+template <typename F>
+__device__ int next_marked_unit(int unit, int units, int stride, int64_t L, int H, F flag) {
+  __shared__ int first;
+  for (; unit < units; unit += kSeqThreads * stride) {
+    const int cand = unit + (int)threadIdx.x * stride;
+    const bool m = cand < units && isnan(flag(((int64_t)(cand / H) * L) * H + cand % H));
+    if (threadIdx.x == 0) first = units;
+    __syncthreads();
+    if (m) atomicMin(&first, cand);
+    __syncthreads();
+    const int f = first;
+    __syncthreads();  // every thread has read it before the next group resets it
+    if (f < units) return f;
+  }
+  return units;
+}
+
 // Per-step inputs staged a block of steps at a time: every thread loads its share of
 // the next block (consecutive elements of a step's rows, coalesced) into registers
 // while the block before is computed from shared memory, then writes them into the
@@ -241,9 +263,12 @@ ssd_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfina
   // path marked, NaN in grad_delta[b, 0, h])
   float* scr = scratch + (int64_t)blockIdx.x * (seg + 1) * E * kSeqThreads + tid;
   for (int unit = blockIdx.x; unit < units; unit += gridDim.x) {
+  if (only_marked) {
+    unit = next_marked_unit(unit, units, gridDim.x, L, H, [&](int64_t i) { return to_f(gdelta[i]); });
+    if (unit >= units) break;
+  }
   const int64_t b = unit / H;
   const int h = unit % H;
-  if (only_marked && !isnan(to_f(gdelta[b * L * H + h]))) continue;
 
   float An[NK];
 #pragma unroll
@@ -635,9 +660,12 @@ gla_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfina
   // one scratch slot per CTA; a CTA walks units blockIdx.x, + gridDim.x, ...
   float* scr = scratch + (int64_t)blockIdx.x * (seg + 1) * E * kSeqThreads + tid;
   for (int unit = blockIdx.x; unit < units; unit += gridDim.x) {
+    if (only_marked) {
+      unit = next_marked_unit(unit, units, gridDim.x, L, H, [&](int64_t i) { return to_f(gg[i]); });
+      if (unit >= units) break;
+    }
     const int64_t b = unit / H;
     const int h = unit % H;
-    if (only_marked && !isnan(to_f(gg[b * L * H + h]))) continue;
 
     // steps tl0 .. tl0 + n - 1 of segment s into the registers, in the recompute's (adjl =
     // false) or the adjoint sweep's row layout

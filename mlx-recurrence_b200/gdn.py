@@ -42,7 +42,7 @@ def _validate(q, k, v, alpha, beta):
 
 class _GDNScan(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, q, k, v, alpha, beta, seg, h0):
+    def forward(ctx, q, k, v, alpha, beta, seg, h0, want_final):
         ctx.set_materialize_grads(False)
         Bt, L, H, Dh = _validate(q, k, v, alpha, beta)
         check_segment_shape(L, seg, Dh, "Dh")
@@ -64,7 +64,7 @@ class _GDNScan(torch.autograd.Function):
                       _lib.ptr(ws), nws, _lib.stream_of(dev))
         ctx.save_for_backward(q_, k_, v_, a_, b_, ckpt, cache, h0_)
         ctx.seg = seg
-        return y, ckpt[:, -1].clone()
+        return y, ckpt[:, -1].clone() if want_final else y.new_empty(0)
 
     @staticmethod
     def backward(ctx, gy, gfinal):
@@ -84,7 +84,7 @@ class _GDNScan(torch.autograd.Function):
                       _lib.ptr(k_), _lib.ptr(v_), _lib.ptr(a_), _lib.ptr(b_), code, Bt, L, H, Dh, ctx.seg,
                       _lib.ptr(gq), _lib.ptr(gk), _lib.ptr(gv), _lib.ptr(ga), _lib.ptr(gb), _lib.ptr(ws),
                       ws.numel(), _lib.ptr(h0_), _lib.ptr(gh0), _lib.stream_of(dev))
-        return gq, gk, gv, ga, gb, None, gh0
+        return gq, gk, gv, ga, gb, None, gh0, None
 
 
 def gated_deltanet_scan(q, k, v, alpha, beta, seg=DEFAULT_SEG, h0=None):
@@ -101,14 +101,14 @@ def gated_deltanet_scan(q, k, v, alpha, beta, seg=DEFAULT_SEG, h0=None):
     Returns:
         o: [B, L, H, Dh] float32. Gradients flow to q, k, v, alpha, beta (and h0).
     """
-    y, _ = _GDNScan.apply(q, k, v, alpha, beta, seg, h0)
+    y, _ = _GDNScan.apply(q, k, v, alpha, beta, seg, h0, False)
     return y
 
 
 def gated_deltanet_scan_with_state(q, k, v, alpha, beta, seg=DEFAULT_SEG, h0=None):
     """:func:`gated_deltanet_scan` that also returns the final state [B, H, Dh, Dh];
     passing it back as ``h0`` continues the scan (chunked prefill)."""
-    return _GDNScan.apply(q, k, v, alpha, beta, seg, h0)
+    return _GDNScan.apply(q, k, v, alpha, beta, seg, h0, True)
 
 
 def gated_deltanet_scan_reference(q, k, v, alpha, beta, h0=None):

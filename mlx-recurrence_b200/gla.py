@@ -34,7 +34,7 @@ def _validate(q, k, v, gates):
 
 class _GLAScan(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, q, k, v, gates, seg, h0):
+    def forward(ctx, q, k, v, gates, seg, h0, want_final):
         # an unused output's cotangent arrives as None (no zero tensor is made)
         ctx.set_materialize_grads(False)
         Bt, L, H, Dh = _validate(q, k, v, gates)
@@ -55,7 +55,7 @@ class _GLAScan(torch.autograd.Function):
                       _lib.stream_of(dev))
         ctx.save_for_backward(q_, k_, v_, g_, ckpt, h0_)
         ctx.seg = seg_i
-        return y, ckpt[:, -1].clone()
+        return y, ckpt[:, -1].clone() if want_final else y.new_empty(0)
 
     @staticmethod
     def backward(ctx, gy, gfinal):
@@ -75,7 +75,7 @@ class _GLAScan(torch.autograd.Function):
                       _lib.ptr(k_), _lib.ptr(v_), _lib.ptr(g_), code, Bt, L, H, Dh, ctx.seg,
                       _lib.ptr(gq), _lib.ptr(gk), _lib.ptr(gv), _lib.ptr(gg), _lib.ptr(ws),
                       ws.numel(), _lib.ptr(h0_), _lib.ptr(gh0), _lib.stream_of(dev))
-        return gq, gk, gv, gg, None, gh0
+        return gq, gk, gv, gg, None, gh0, None
 
 
 def gla_scan(q, k, v, gates, seg=DEFAULT_SEG, h0=None):
@@ -91,14 +91,14 @@ def gla_scan(q, k, v, gates, seg=DEFAULT_SEG, h0=None):
     Returns:
         y:       [B, L, H, Dh] float32
     """
-    y, _ = _GLAScan.apply(q, k, v, gates, seg, h0)
+    y, _ = _GLAScan.apply(q, k, v, gates, seg, h0, False)
     return y
 
 
 def gla_scan_with_state(q, k, v, gates, seg=DEFAULT_SEG, h0=None):
     """GLA scan that also returns the final state ``[B, H, Dh, Dh]`` (``gla.py:321-329``).
     Passing it back as ``h0`` continues the scan (chunked prefill)."""
-    return _GLAScan.apply(q, k, v, gates, seg, h0)
+    return _GLAScan.apply(q, k, v, gates, seg, h0, True)
 
 
 def gla_scan_reference(q, k, v, gates, h0=None):

@@ -22,7 +22,7 @@ from ._chassis import DEFAULT_SEG, check_segment_shape, common_dtype, grad_out, 
 
 class _RGLRUScan(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, a, x, seg, h0):
+    def forward(ctx, a, x, seg, h0, want_final):
         # an unused output's cotangent arrives as None (no zero tensor is made)
         ctx.set_materialize_grads(False)
         if a.dim() != 3 or x.shape != a.shape:
@@ -40,7 +40,7 @@ class _RGLRUScan(torch.autograd.Function):
                       _lib.ptr(y), _lib.ptr(ckpt), _lib.ptr(h0_), _lib.stream_of(dev))
         ctx.save_for_backward(a_, x_, ckpt, h0_)
         ctx.seg = seg
-        return y, ckpt[:, -1].clone()
+        return y, ckpt[:, -1].clone() if want_final else y.new_empty(0)
 
     @staticmethod
     def backward(ctx, gy, gfinal):
@@ -61,7 +61,7 @@ class _RGLRUScan(torch.autograd.Function):
             _lib.call("mr_rglru_bwd_h0", _lib.ptr(gy), _lib.ptr(gf), _lib.ptr(ckpt), _lib.ptr(a_),
                       _lib.ptr(x_), code, Bt, L, D, ctx.seg, _lib.ptr(ga), _lib.ptr(gx), _lib.ptr(ws),
                       nws, _lib.ptr(h0_), _lib.ptr(gh0), _lib.stream_of(dev))
-        return ga, gx, None, gh0
+        return ga, gx, None, gh0, None
 
 
 def rglru_scan(a, x, seg=DEFAULT_SEG, h0=None):
@@ -81,14 +81,14 @@ def rglru_scan(a, x, seg=DEFAULT_SEG, h0=None):
     and fp16 inputs are widened on read and their gradients are returned in
     the input dtype.
     """
-    y, _ = _RGLRUScan.apply(a, x, seg, h0)
+    y, _ = _RGLRUScan.apply(a, x, seg, h0, False)
     return y
 
 
 def rglru_scan_with_state(a, x, seg=DEFAULT_SEG, h0=None):
     """RG-LRU scan that also returns the final state [B, D] (``rglru.py:259-267``).
     Passing it back as ``h0`` continues the scan (chunked prefill)."""
-    return _RGLRUScan.apply(a, x, seg, h0)
+    return _RGLRUScan.apply(a, x, seg, h0, True)
 
 
 def rglru_scan_reference(a, x, h0=None):
@@ -123,7 +123,7 @@ def rglru_step(a, x, state):
 
 class _RGLRUGatedScan(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, r, i, lam, c, seg, h0):
+    def forward(ctx, x, r, i, lam, c, seg, h0, want_final):
         ctx.set_materialize_grads(False)
         if x.dim() != 3 or r.shape != x.shape or i.shape != x.shape:
             raise ValueError(f"x, r, i must all be [B, L, D], got {tuple(x.shape)}, {tuple(r.shape)}, "
@@ -145,7 +145,7 @@ class _RGLRUGatedScan(torch.autograd.Function):
                       _lib.stream_of(dev))
         ctx.save_for_backward(x_, r_, i_, lam_, ckpt, h0_)
         ctx.seg, ctx.c = seg, float(c)
-        return y, ckpt[:, -1].clone()
+        return y, ckpt[:, -1].clone() if want_final else y.new_empty(0)
 
     @staticmethod
     def backward(ctx, gy, gfinal):
@@ -166,7 +166,7 @@ class _RGLRUGatedScan(torch.autograd.Function):
                       _lib.ptr(i_), _lib.ptr(lam_), ctx.c, code, Bt, L, D, ctx.seg, _lib.ptr(gx), _lib.ptr(gr),
                       _lib.ptr(gi), _lib.ptr(glam), _lib.ptr(ws), ws.numel(), _lib.ptr(h0_), _lib.ptr(gh0),
                       _lib.stream_of(dev))
-        return gx, gr, gi, glam, None, None, gh0
+        return gx, gr, gi, glam, None, None, gh0, None
 
 
 def rglru_scan_gated(x, r, i, lam, c=8.0, seg=DEFAULT_SEG, h0=None):
@@ -189,10 +189,10 @@ def rglru_scan_gated(x, r, i, lam, c=8.0, seg=DEFAULT_SEG, h0=None):
     Returns:
         y:   [B, L, D] float32. Differentiable in x, r, i, lam and h0.
     """
-    y, _ = _RGLRUGatedScan.apply(x, r, i, lam, c, seg, h0)
+    y, _ = _RGLRUGatedScan.apply(x, r, i, lam, c, seg, h0, False)
     return y
 
 
 def rglru_scan_gated_with_state(x, r, i, lam, c=8.0, seg=DEFAULT_SEG, h0=None):
     """:func:`rglru_scan_gated` that also returns the final state [B, D]."""
-    return _RGLRUGatedScan.apply(x, r, i, lam, c, seg, h0)
+    return _RGLRUGatedScan.apply(x, r, i, lam, c, seg, h0, True)

@@ -37,7 +37,7 @@ def _validate(a, cs, sn, x):
 
 class _RotLRUScan(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, a, cs, sn, x, seg, h0):
+    def forward(ctx, a, cs, sn, x, seg, h0, want_final):
         # an unused output's cotangent arrives as None (no zero tensor is made)
         ctx.set_materialize_grads(False)
         Bt, L, Dp = _validate(a, cs, sn, x)
@@ -55,7 +55,7 @@ class _RotLRUScan(torch.autograd.Function):
                       _lib.stream_of(dev))
         ctx.save_for_backward(a_, c_, s_, x_, ckpt, h0_)
         ctx.seg = seg
-        return y, ckpt[:, -1].clone()
+        return y, ckpt[:, -1].clone() if want_final else y.new_empty(0)
 
     @staticmethod
     def backward(ctx, gy, gfinal):
@@ -75,7 +75,7 @@ class _RotLRUScan(torch.autograd.Function):
                       _lib.ptr(c_), _lib.ptr(s_), _lib.ptr(x_), code, Bt, L, Dp, ctx.seg,
                       _lib.ptr(ga), _lib.ptr(gc), _lib.ptr(gs), _lib.ptr(gx), _lib.ptr(ws), nws,
                       _lib.ptr(h0_), _lib.ptr(gh0), _lib.stream_of(dev))
-        return ga, gc, gs, gx, None, gh0
+        return ga, gc, gs, gx, None, gh0, None
 
 
 def rotlru_scan(a, cs, sn, x, seg=DEFAULT_SEG, h0=None):
@@ -95,19 +95,19 @@ def rotlru_scan(a, cs, sn, x, seg=DEFAULT_SEG, h0=None):
 
     ``D`` must be a multiple of 32. Gradients flow to all four inputs.
     """
-    y, _ = _RotLRUScan.apply(a, cs, sn, x, seg, h0)
+    y, _ = _RotLRUScan.apply(a, cs, sn, x, seg, h0, False)
     return y
 
 
 def rotlru_scan_with_state(a, cs, sn, x, seg=DEFAULT_SEG, h0=None):
     """Rotational LRU scan that also returns the final state [B, D] (``rotlru.py:323-331``).
     Passing it back as ``h0`` continues the scan (chunked prefill)."""
-    return _RotLRUScan.apply(a, cs, sn, x, seg, h0)
+    return _RotLRUScan.apply(a, cs, sn, x, seg, h0, True)
 
 
 class _RotLRUAngleScan(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, a, theta, x, seg, h0):
+    def forward(ctx, a, theta, x, seg, h0, want_final):
         ctx.set_materialize_grads(False)
         if a.dim() == 3 and theta.shape != a.shape:
             raise ValueError(f"a/theta shapes must match, got {tuple(a.shape)}, {tuple(theta.shape)}")
@@ -125,7 +125,7 @@ class _RotLRUAngleScan(torch.autograd.Function):
                       L, Dp, seg, _lib.ptr(y), _lib.ptr(ckpt), _lib.ptr(h0_), _lib.stream_of(dev))
         ctx.save_for_backward(a_, t_, x_, ckpt, h0_)
         ctx.seg = seg
-        return y, ckpt[:, -1].clone()
+        return y, ckpt[:, -1].clone() if want_final else y.new_empty(0)
 
     @staticmethod
     def backward(ctx, gy, gfinal):
@@ -144,7 +144,7 @@ class _RotLRUAngleScan(torch.autograd.Function):
             _lib.call("mr_rotlru_angle_bwd", _lib.ptr(gy), _lib.ptr(gf), _lib.ptr(ckpt), _lib.ptr(a_),
                       _lib.ptr(t_), _lib.ptr(x_), code, Bt, L, Dp, ctx.seg, _lib.ptr(ga), _lib.ptr(gt),
                       _lib.ptr(gx), _lib.ptr(ws), nws, _lib.ptr(h0_), _lib.ptr(gh0), _lib.stream_of(dev))
-        return ga, gt, gx, None, gh0
+        return ga, gt, gx, None, gh0, None
 
 
 def rotlru_scan_angle(a, theta, x, seg=DEFAULT_SEG, h0=None):
@@ -166,13 +166,13 @@ def rotlru_scan_angle(a, theta, x, seg=DEFAULT_SEG, h0=None):
         y: [B, L, D] float32. Gradients flow to a, theta, x (and h0):
         ``grad_theta = cos(theta) grad_sn - sin(theta) grad_cs``.
     """
-    y, _ = _RotLRUAngleScan.apply(a, theta, x, seg, h0)
+    y, _ = _RotLRUAngleScan.apply(a, theta, x, seg, h0, False)
     return y
 
 
 def rotlru_scan_angle_with_state(a, theta, x, seg=DEFAULT_SEG, h0=None):
     """:func:`rotlru_scan_angle` that also returns the final state [B, D]."""
-    return _RotLRUAngleScan.apply(a, theta, x, seg, h0)
+    return _RotLRUAngleScan.apply(a, theta, x, seg, h0, True)
 
 
 def rotlru_scan_reference(a, cs, sn, x, h0=None):

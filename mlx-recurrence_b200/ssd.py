@@ -51,7 +51,7 @@ def _a_f32(A_neg):
 
 class _SSDScan(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, u, delta, B, C, A_neg, seg, h0):
+    def forward(ctx, u, delta, B, C, A_neg, seg, h0, want_final):
         # an unused output's cotangent arrives as None (no zero tensor is made)
         ctx.set_materialize_grads(False)
         Bt, L, H, Dh, N = _validate(u, delta, B, C, A_neg)
@@ -73,8 +73,9 @@ class _SSDScan(torch.autograd.Function):
                       _lib.ptr(y), _lib.ptr(ckpt), _lib.ptr(h0_), _lib.stream_of(dev))
         ctx.save_for_backward(u_, d_, B_, C_, A32, ckpt, h0_)
         ctx.meta = (seg_i, ash, asn, N)
-        # last checkpoint [B, H, N, Dh] -> conceptual state [B, H, Dh, N] (ssd.py:373-374)
-        final = ckpt[:, -1].transpose(-1, -2).contiguous()
+        # last checkpoint [B, H, N, Dh] -> conceptual state [B, H, Dh, N] (ssd.py:373-374);
+        # ssd_scan drops it, so it is only copied out for ssd_scan_with_state
+        final = ckpt[:, -1].transpose(-1, -2).contiguous() if want_final else y.new_empty(0)
         return y, final
 
     @staticmethod
@@ -100,7 +101,7 @@ class _SSDScan(torch.autograd.Function):
                       H, Dh, N, seg, _lib.ptr(gu), _lib.ptr(gd), _lib.ptr(gB), _lib.ptr(gC),
                       _lib.ptr(gA), _lib.ptr(ws), ws.numel(), _lib.ptr(h0_), _lib.ptr(gh0),
                       _lib.stream_of(dev))
-        return gu, gd, gB, gC, gA, None, gh0
+        return gu, gd, gB, gC, gA, None, gh0, None
 
 
 def ssd_scan(u, delta, B, C, A_neg, seg=DEFAULT_SEG, h0=None):
@@ -119,14 +120,14 @@ def ssd_scan(u, delta, B, C, A_neg, seg=DEFAULT_SEG, h0=None):
     Returns:
         y:      [B, L, H, Dh] float32
     """
-    y, _ = _SSDScan.apply(u, delta, B, C, A_neg, seg, h0)
+    y, _ = _SSDScan.apply(u, delta, B, C, A_neg, seg, h0, False)
     return y
 
 
 def ssd_scan_with_state(u, delta, B, C, A_neg, seg=DEFAULT_SEG, h0=None):
     """SSD scan that also returns the final state ``[B, H, Dh, N]`` (``ssd.py:365-375``).
     Passing it back as ``h0`` continues the scan (chunked prefill)."""
-    return _SSDScan.apply(u, delta, B, C, A_neg, seg, h0)
+    return _SSDScan.apply(u, delta, B, C, A_neg, seg, h0, True)
 
 
 def ssd_scan_reference(u, delta, B, C, A_neg, h0=None):
