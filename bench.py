@@ -6,8 +6,9 @@ A step is one forward and one backward pass of the configured scan through
 the public API (torch.autograd over libmlrec.so) on one batch of synthetic
 inputs. The default workload is config c4 (SSD, bf16, B=32, L=16384, H=32,
 Dh=64, N=128, seg=32), the configuration the scaling target is quoted on; the
-default run also measures the GLA shape of the same target (c5) with the same
-steps and warm-up and reports it under "extra". Under torchrun (N > 1) every
+default run also measures the GLA shape of the same target (c5) and the RG-LRU
+(c2) and rotLRU (c3) configurations with the same steps and warm-up and reports
+them under "extra" (every plug-in measured). Under torchrun (N > 1) every
 rank takes a block of the same global problem - a range of batch rows, and of
 heads (channels) when N does not divide the batch - with no collective on the
 data path (strong scaling); the timed region is bracketed by a barrier and
@@ -342,7 +343,7 @@ def _time_steps(ctx, P, steps, warmup):
         e_end.record(stream)
         torch.cuda.synchronize()
         ctx["barrier"]()
-    return dict(total_ms=e_start.elapsed_time(e_end),
+    return dict(total_ms=e_start.elapsed_time(e_end), steps=steps,
                 f_ms=statistics.mean(a.elapsed_time(b) for a, b, _ in marks),
                 b_ms=statistics.mean(b.elapsed_time(c) for _, b, c in marks),
                 launches=lib.mr_launch_count() - n_launch0,
@@ -376,14 +377,19 @@ def run_ours(args):
     meta = {k: P[k] for k in ("name", "cfg", "lcfg")}
     extra = {}
     if args.config == "c4" and not args.no_extra:
-        # the GLA half of the target shape (B=32, L=16384, H=32, Dh=64), same steps and warm-up
+        # the GLA half of the target shape (B=32, L=16384, H=32, Dh=64), then the two diagonal
+        # scans at their configurations (c2 RG-LRU, c3 rotLRU): every plug-in measured with the
+        # same warm-up; c5 with the same steps, the diagonal scans (0.4 and 1.3 ms a step) with
+        # ten times as many, so that their timed regions are not a few milliseconds (args.batch
+        # applies to c4 and c5 only)
         del P
-        torch.cuda.empty_cache()
-        P5 = _prepare(ctx, "c5", args.batch)
-        M5 = _time_steps(ctx, P5, args.steps, args.warmup)
-        M5["total_ms"], M5["f_ms"], M5["b_ms"] = _max_over_ranks(ctx, [M5["total_ms"], M5["f_ms"], M5["b_ms"]])
-        extra["c5"] = ({k: P5[k] for k in ("name", "cfg", "lcfg")}, M5)
-        del P5
+        for name, mult in (("c5", 1), ("c2", 10), ("c3", 10)):
+            torch.cuda.empty_cache()
+            Pk = _prepare(ctx, name, args.batch if name == "c5" else 0)
+            Mk = _time_steps(ctx, Pk, args.steps * mult, args.warmup)
+            Mk["total_ms"], Mk["f_ms"], Mk["b_ms"] = _max_over_ranks(ctx, [Mk["total_ms"], Mk["f_ms"], Mk["b_ms"]])
+            extra[name] = ({k: Pk[k] for k in ("name", "cfg", "lcfg")}, Mk)
+            del Pk
     if ctx["rank"] == 0:
         out = _report(args, ctx, meta, M, e2e_ms, h2d, d2h)
         if extra:
@@ -614,9 +620,10 @@ def _metrics(args, ctx, P, M):
         cfg["B"], cfg[ax], ctx["world"], W.UNIT_AXIS[cfg["kind"]][1])
     unit = {"H": "head", "D": "channel", "Dp": "pair"}[ax]
     return {
-        "value": tok * args.steps / (M["total_ms"] * 1e-3),
+        "value": tok * M["steps"] / (M["total_ms"] * 1e-3),
         "unit": "tokens/s",
-        "ms_per_step": M["total_ms"] / args.steps,
+        "ms_per_step": M["total_ms"] / M["steps"],
+        "steps": M["steps"],
         "config": {"workload": W.DESCRIPTION[name], "name": name, "global_batch": cfg["B"], "seq_len": cfg["L"],
                    "ckpt_spacing": _ckpt_spacing(ctx, cfg),
                    "parallelism": f"{wb} batch x {wu} {unit} blocks over {ctx['world']} GPU(s), no collective",
@@ -632,7 +639,7 @@ def _metrics(args, ctx, P, M):
                      "peak_source": f"{peak_kind} hbm_gbs",
                      # the whole forward+backward step against the same roofline (this rank's
                      # algorithmic bytes over its share of the step time), and the forward alone
-                     "step_frac": (fb + bb) / (M["total_ms"] / args.steps * 1e-3) / 1e9 / hbm,
+                     "step_frac": (fb + bb) / (M["total_ms"] / M["steps"] * 1e-3) / 1e9 / hbm,
                      "fwd_frac": fb / (f_ms * 1e-3) / 1e9 / hbm},
         **({"note": "per-step delta-rule recurrence: bound by FP32 issue and per-step latency on the "
                     "CUDA cores, not by HBM"} if cfg["kind"] == "gdn" else {}),
@@ -735,7 +742,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffer) timing")
     ap.add_argument("--no-extra", action="store_true",
-                    help="with the default c4, skip the extra GLA (c5) measurement at the same shape")
+                    help="with the default c4, skip the extra measurements (c5 GLA at the same shape, c2 RG-LRU, c3 rotLRU)")
     ap.add_argument("--check", action="store_true",
                     help="after timing, gather every rank's outputs and gradients and compare them on "
                          "rank 0 with the whole batch run on one GPU")
