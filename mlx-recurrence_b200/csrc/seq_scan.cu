@@ -116,15 +116,22 @@ __device__ __forceinline__ float warp_sum(float v) {
 // SSD
 // ============================================================================
 
+// The state rows d of a unit evolve independently in the forward (each row's update and
+// output read only that row), so a unit's Dh rows may be split over rsplit CTAs of 8R
+// rows each (rows d0 .. d0 + 8R - 1, d0 = (blockIdx.x % rsplit) * 8R): with few units,
+// more SMs walk the steps (c0: 36 units). rsplit = 1 in the only_marked mode (its flag
+// sits in row 0 of the unit's output).
 template <typename T, int R, int NK>
 __global__ void __launch_bounds__(kSeqThreads)
 ssd_seq_fwd_kernel(const T* __restrict__ u, const T* __restrict__ delta, const T* __restrict__ Bm,
                    const T* __restrict__ Cm, const float* __restrict__ A, int64_t ash, int64_t asn,
                    int L, int H, int Dh, int N, int seg, float* __restrict__ y,
-                   float* __restrict__ ckpt, const float* __restrict__ h0, int only_marked) {
+                   float* __restrict__ ckpt, const float* __restrict__ h0, int only_marked, int rsplit) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int64_t b = blockIdx.x / H;
-  const int h = blockIdx.x % H;
+  const int unit = blockIdx.x / rsplit;
+  const int d0 = (blockIdx.x % rsplit) * 8 * R;  // this CTA's first row
+  const int64_t b = unit / H;
+  const int h = unit % H;
   const int nseg = L / seg;
   // after the dense-A tensor-core path: only the units it marked (NaN in y[b, 0, h, 0])
   if (only_marked && !isnan(y[(b * L * H + h) * Dh])) return;
@@ -142,15 +149,15 @@ ssd_seq_fwd_kernel(const T* __restrict__ u, const T* __restrict__ delta, const T
 #pragma unroll
     for (int k = 0; k < NK; ++k) {
       const int n = lane + 32 * k;
-      st[r][k] = (h0 != nullptr && n < N) ? h0[((b * H + h) * Dh + warp + 8 * r) * (int64_t)N + n] : 0.f;
+      st[r][k] = (h0 != nullptr && n < N) ? h0[((b * H + h) * Dh + d0 + warp + 8 * r) * (int64_t)N + n] : 0.f;
     }
 
-  // staged step rows [B (N) | C (N) | u (Dh) | delta (1)], TS steps per buffer
+  // staged step rows [B (N) | C (N) | u (this CTA's 8R rows) | delta (1)], TS steps per buffer
   constexpr int WMAX = 2 * 32 * NK + 8 * R + 1;
   constexpr int TS = stage_steps(WMAX);
   constexpr int EPT = (TS * WMAX + kSeqThreads - 1) / kSeqThreads;
   __shared__ float sIn[2][TS * WMAX];
-  const int W = 2 * N + Dh + 1;
+  const int W = 2 * N + 8 * R + 1;
   StepStage<EPT> pre;
   auto load_block = [&](int t0) {
 #pragma unroll
@@ -161,10 +168,10 @@ ssd_seq_fwd_kernel(const T* __restrict__ u, const T* __restrict__ delta, const T
         const int tt = e / W, col = e - tt * W, t = t0 + tt;
         if (t < L) {
           const int64_t row = (b * L + t) * H + h;
-          v = col < N           ? to_f(Bm[row * N + col])
-              : col < 2 * N      ? to_f(Cm[row * N + col - N])
-              : col < 2 * N + Dh ? to_f(u[row * Dh + col - 2 * N])
-                                 : to_f(delta[row]);
+          v = col < N               ? to_f(Bm[row * N + col])
+              : col < 2 * N          ? to_f(Cm[row * N + col - N])
+              : col < 2 * N + 8 * R ? to_f(u[row * Dh + d0 + col - 2 * N])
+                                     : to_f(delta[row]);
         }
       }
       pre.r[i] = v;
@@ -185,11 +192,12 @@ ssd_seq_fwd_kernel(const T* __restrict__ u, const T* __restrict__ delta, const T
   for (int blk = 0; blk < nblk; ++blk) {
   if (blk + 1 < nblk) load_block((blk + 1) * TS);
   const int nt = min(TS, L - blk * TS);
-  for (int tt = 0; tt < nt; ++tt) {
+  int tend = seg - 1 - (blk * TS) % seg;  // the block's next step that ends a segment
+  auto step = [&](int tt) {
     const int t = blk * TS + tt;
     const int64_t row = (b * L + t) * H + h;
     const float* sr = sIn[blk & 1] + tt * W;
-    const float dt = sr[2 * N + Dh];
+    const float dt = sr[2 * N + 8 * R];
     float dB[NK], cv[NK], dec[NK];
 #pragma unroll
     for (int k = 0; k < NK; ++k) {
@@ -215,11 +223,12 @@ ssd_seq_fwd_kernel(const T* __restrict__ u, const T* __restrict__ delta, const T
     {
       int ri;
       const float tot = warp_sum_rows<R>(accs, lane, ri);
-      if (row_leader<R>(lane) && ri < R) y[row * Dh + warp + 8 * ri] = tot;
+      if (row_leader<R>(lane) && ri < R) y[row * Dh + d0 + warp + 8 * ri] = tot;
     }
-    if ((t + 1) % seg == 0) {
+    if (tt == tend) {
+      tend += seg;
       const int64_t s = (t + 1) / seg - 1;
-      float* ck = ckpt + ((b * nseg + s) * H + h) * (int64_t)N * Dh;
+      float* ck = ckpt + ((b * nseg + s) * H + h) * (int64_t)N * Dh + d0;
 #pragma unroll
       for (int r = 0; r < R; ++r)
 #pragma unroll
@@ -228,6 +237,19 @@ ssd_seq_fwd_kernel(const T* __restrict__ u, const T* __restrict__ delta, const T
           if (n < N) ck[(int64_t)n * Dh + warp + 8 * r] = st[r][k];
         }
     }
+  };
+  // Only the state update carries from step to step; with few state values a thread, a
+  // whole block of steps is unrolled so that the independent work of later steps (the
+  // decay factors, the loads, the output reduction) overlaps the earlier ones.
+  if constexpr (R * NK <= 4) {
+    if (nt == TS) {
+#pragma unroll
+      for (int tt = 0; tt < TS; ++tt) step(tt);
+    } else {
+      for (int tt = 0; tt < nt; ++tt) step(tt);
+    }
+  } else {
+    for (int tt = 0; tt < nt; ++tt) step(tt);
   }
   if (blk + 1 < nblk) store_block((blk + 1) & 1);
   __syncthreads();  // the next block reads the buffer written above; this one is refilled after it
@@ -928,13 +950,19 @@ bool gla_seq_supported(int64_t Dh) { return Dh == 32 || Dh == 64 || Dh == 96 || 
 template <typename T, int R>
 static void ssd_fwd_nk(int nk, dim3 g, cudaStream_t st, const T* u, const T* dl, const T* Bm,
                        const T* Cm, const float* A, int64_t ash, int64_t asn, int L, int H, int Dh,
-                       int N, int seg, float* y, float* ck, const float* h0, int om) {
+                       int N, int seg, float* y, float* ck, const float* h0, int om, int rs) {
   if (nk == 1)
-    ssd_seq_fwd_kernel<T, R, 1><<<g, kSeqThreads, 0, st>>>(u, dl, Bm, Cm, A, ash, asn, L, H, Dh, N, seg, y, ck, h0, om);
+    ssd_seq_fwd_kernel<T, R, 1><<<g, kSeqThreads, 0, st>>>(u, dl, Bm, Cm, A, ash, asn, L, H, Dh, N, seg, y, ck, h0, om, rs);
   else if (nk == 2)
-    ssd_seq_fwd_kernel<T, R, 2><<<g, kSeqThreads, 0, st>>>(u, dl, Bm, Cm, A, ash, asn, L, H, Dh, N, seg, y, ck, h0, om);
+    ssd_seq_fwd_kernel<T, R, 2><<<g, kSeqThreads, 0, st>>>(u, dl, Bm, Cm, A, ash, asn, L, H, Dh, N, seg, y, ck, h0, om, rs);
   else
-    ssd_seq_fwd_kernel<T, R, 4><<<g, kSeqThreads, 0, st>>>(u, dl, Bm, Cm, A, ash, asn, L, H, Dh, N, seg, y, ck, h0, om);
+    ssd_seq_fwd_kernel<T, R, 4><<<g, kSeqThreads, 0, st>>>(u, dl, Bm, Cm, A, ash, asn, L, H, Dh, N, seg, y, ck, h0, om, rs);
+}
+
+static int sm_count() {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms;
 }
 
 // only_marked: recompute just the units the dense-A tensor-core path marked
@@ -943,11 +971,28 @@ int ssd_seq_fwd_launch(const void* u, const void* delta, const void* Bm, const v
                        const float* A, int64_t ash, int64_t asn, int64_t batch, int64_t L, int64_t H,
                        int64_t Dh, int64_t N, int64_t seg, float* y, float* ckpt, const float* h0,
                        cudaStream_t st, int only_marked) {
-  dim3 g((unsigned)(batch * H));
-#define MR_CALL(R_, NK_)                                                                       \
-  ssd_fwd_nk<T, R_>(NK_, g, st, (const T*)u, (const T*)delta, (const T*)Bm, (const T*)Cm, A, ash, \
-                    asn, (int)L, (int)H, (int)Dh, (int)N, (int)seg, y, ckpt, h0, only_marked)
-  MR_SSD_DISPATCH(Dh, N, MR_CALL);
+  // CTAs per unit: its rows split in halves while the grid stays within two CTAs per SM
+  // (Dh / 8 a power of two; one CTA per unit in the only_marked mode)
+  const int64_t units = batch * H;
+  const int rf = (int)Dh / 8;
+  int rs = 1;
+  if (!only_marked && (rf & (rf - 1)) == 0) {
+    const int64_t cap = 2 * (int64_t)sm_count();
+    while (rs * 2 <= rf && units * rs * 2 <= cap) rs *= 2;
+  }
+  dim3 g((unsigned)(units * rs));
+  const int nk = nk_of(N);
+#define MR_CALL(R_)                                                                                 \
+  ssd_fwd_nk<T, R_>(nk, g, st, (const T*)u, (const T*)delta, (const T*)Bm, (const T*)Cm, A, ash, asn, \
+                    (int)L, (int)H, (int)Dh, (int)N, (int)seg, y, ckpt, h0, only_marked, rs)
+  switch (rf / rs) {
+    case 1: MR_CALL(1); break;
+    case 2: MR_CALL(2); break;
+    case 4: MR_CALL(4); break;
+    case 8: MR_CALL(8); break;
+    case 12: MR_CALL(12); break;
+    default: MR_CALL(16); break;
+  }
 #undef MR_CALL
   return check_launch("ssd_seq_fwd_kernel");
 }
