@@ -264,7 +264,8 @@ ssd_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfina
                    const float* __restrict__ A, int64_t ash, int64_t asn, int L, int H, int Dh,
                    int N, int seg, T* __restrict__ gu, T* __restrict__ gdelta, T* __restrict__ gB,
                    T* __restrict__ gC, float* __restrict__ gA_part, float* __restrict__ scratch,
-                   const float* __restrict__ h0, float* __restrict__ gh0, int units, int only_marked) {
+                   const float* __restrict__ h0, float* __restrict__ gh0, int units, int only_marked,
+                   int rsplit, float* __restrict__ part) {
   constexpr int NP = 32 * NK;
   __shared__ float pB[kTS][8][NP];
   __shared__ float pC[kTS][8][NP];
@@ -284,7 +285,16 @@ ssd_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfina
   // unless only_marked: then a few CTAs recompute the units the dense-A tensor-core
   // path marked, NaN in grad_delta[b, 0, h])
   float* scr = scratch + (int64_t)blockIdx.x * (seg + 1) * E * kSeqThreads + tid;
-  for (int unit = blockIdx.x; unit < units; unit += gridDim.x) {
+  // With rsplit > 1 (never with only_marked) a unit's rows are split over rsplit CTAs of 8R
+  // rows each, d0 the CTA's first: their sums over the rows (grad_B, grad_C, grad_delta)
+  // go to float32 partials part[rs] ([gB | gC] of B*L*H*N each, then gdelta of B*L*H),
+  // summed over rs by a second kernel; grad_A's partial is per (batch row, rs, head).
+  const int rs = blockIdx.x % rsplit, d0 = rs * 8 * R;
+  const int64_t BLH = (int64_t)(units / H) * L * H;
+  float* pgB = rsplit > 1 ? part + (int64_t)rs * BLH * N : nullptr;
+  float* pgC = rsplit > 1 ? part + (int64_t)(rsplit + rs) * BLH * N : nullptr;
+  float* pgd = rsplit > 1 ? part + (int64_t)2 * rsplit * BLH * N + (int64_t)rs * BLH : nullptr;
+  for (int unit = blockIdx.x / rsplit; unit < units; unit += gridDim.x / rsplit) {
   if (only_marked) {
     unit = next_marked_unit(unit, units, gridDim.x, L, H, [&](int64_t i) { return to_f(gdelta[i]); });
     if (unit >= units) break;
@@ -300,7 +310,8 @@ ssd_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfina
   }
   // steps tl0 .. tl0 + n - 1 of segment s into the registers, in the recompute's (adj = false)
   // or the adjoint sweep's row layout
-  const int Wa = N + Dh + 1, Wb = 2 * N + 2 * Dh + 1;
+  // staged rows: [B | u (this CTA's 8R rows) | delta], [B | C | u | grad_y (8R rows) | delta]
+  const int Wa = N + 8 * R + 1, Wb = 2 * N + 16 * R + 1;
   auto load_steps = [&](int s, int tl0, int n, bool adjl) {
     const int W = adjl ? Wb : Wa;
 #pragma unroll
@@ -312,12 +323,12 @@ ssd_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfina
         const int64_t rowt = (b * L + (int64_t)s * seg + tl0 + tt);
         const int64_t row = rowt * H + h;
         if (!adjl) {
-          v = col < N ? to_f(Bm[row * N + col]) : col < N + Dh ? to_f(u[row * Dh + col - N]) : to_f(delta[row]);
+          v = col < N ? to_f(Bm[row * N + col]) : col < N + 8 * R ? to_f(u[row * Dh + d0 + col - N]) : to_f(delta[row]);
         } else {
           v = col < N            ? to_f(Bm[row * N + col])
               : col < 2 * N      ? to_f(Cm[row * N + col - N])
-              : col < 2 * N + Dh ? to_f(u[row * Dh + col - 2 * N])
-              : col < 2 * N + 2 * Dh ? gy[row * Dh + col - 2 * N - Dh]
+              : col < 2 * N + 8 * R ? to_f(u[row * Dh + d0 + col - 2 * N])
+              : col < 2 * N + 16 * R ? gy[row * Dh + d0 + col - 2 * N - 8 * R]
                                      : to_f(delta[row]);
         }
       }
@@ -343,7 +354,7 @@ ssd_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfina
 #pragma unroll
     for (int k = 0; k < NK; ++k) {
       const int n = lane + 32 * k;
-      const int d = warp + 8 * r;
+      const int d = d0 + warp + 8 * r;
       adj[r][k] = (gfinal != nullptr && n < N) ? gfinal[((b * H + h) * Dh + d) * (int64_t)N + n] : 0.f;
     }
 
@@ -357,7 +368,7 @@ ssd_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfina
 #pragma unroll
         for (int k = 0; k < NK; ++k) {
           const int n = lane + 32 * k;
-          const int d = warp + 8 * r;
+          const int d = d0 + warp + 8 * r;
           st[r][k] = n >= N                ? 0.f
                      : s > 0               ? ck[(int64_t)n * Dh + d]
                      : h0 != nullptr       ? h0[((b * H + h) * Dh + d) * (int64_t)N + n]
@@ -373,7 +384,7 @@ ssd_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfina
         for (int tt = 0; tt < blk_n(j); ++tt) {
           const int tl = j * TS + tt;
           const float* sr = sb + tt * Wa;
-          const float dt = sr[N + Dh];
+          const float dt = sr[N + 8 * R];
           float dB[NK], dec[NK];
 #pragma unroll
           for (int k = 0; k < NK; ++k) {
@@ -428,7 +439,7 @@ ssd_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfina
       const int64_t t = (int64_t)s * seg + tl;
       const int64_t row = (b * L + t) * H + h;
       const float* sr = sbuf + (tl - j * TS) * Wb;
-      const float dt = sr[2 * N + 2 * Dh];
+      const float dt = sr[2 * N + 16 * R];
       float bv[NK], cv[NK], dec[NK];
 #pragma unroll
       for (int k = 0; k < NK; ++k) {
@@ -447,7 +458,7 @@ ssd_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfina
       for (int r = 0; r < R; ++r) {
         const int d = warp + 8 * r;
         const float ud = sr[2 * N + d];
-        const float g = sr[2 * N + Dh + d];
+        const float g = sr[2 * N + 8 * R + d];
         float gu_r = 0.f;
 #pragma unroll
         for (int k = 0; k < NK; ++k) {
@@ -466,7 +477,7 @@ ssd_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfina
       {
         int ri;
         const float tot = warp_sum_rows<R>(gus, lane, ri);
-        if (row_leader<R>(lane) && ri < R) gu[row * Dh + warp + 8 * ri] = from_f<T>(tot);
+        if (row_leader<R>(lane) && ri < R) gu[row * Dh + d0 + warp + 8 * ri] = from_f<T>(tot);
       }
       gdt = warp_sum(gdt);
       if (lane == 0) pdt[slot][warp] = gdt;
@@ -488,15 +499,23 @@ ssd_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfina
           }
           const int64_t tt = t + (slot - sl);  // slot sl was step t + (slot - sl)
           const int64_t rr = (b * L + tt) * H + h;
-          gB[rr * N + n] = from_f<T>(sb);
-          gC[rr * N + n] = from_f<T>(scc);
+          if (rsplit > 1) {
+            pgB[rr * N + n] = sb;
+            pgC[rr * N + n] = scc;
+          } else {
+            gB[rr * N + n] = from_f<T>(sb);
+            gC[rr * N + n] = from_f<T>(scc);
+          }
         }
         if (tid < nsl) {
           float sd = 0.f;
 #pragma unroll
           for (int w = 0; w < 8; ++w) sd += pdt[tid][w];
           const int64_t tt = t + (slot - tid);
-          gdelta[(b * L + tt) * H + h] = from_f<T>(sd);
+          if (rsplit > 1)
+            pgd[(b * L + tt) * H + h] = sd;
+          else
+            gdelta[(b * L + tt) * H + h] = from_f<T>(sd);
         }
         __syncthreads();
       }
@@ -520,7 +539,7 @@ ssd_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfina
 #pragma unroll
       for (int k = 0; k < NK; ++k) {
         const int n = lane + 32 * k;
-        if (n < N) gh0[((b * H + h) * Dh + warp + 8 * r) * (int64_t)N + n] = adj[r][k];
+        if (n < N) gh0[((b * H + h) * Dh + d0 + warp + 8 * r) * (int64_t)N + n] = adj[r][k];
       }
   // grad_A partial for this (b, h): sum over rows (in-thread) and warps
   __syncthreads();
@@ -531,7 +550,7 @@ ssd_seq_bwd_kernel(const float* __restrict__ gy, const float* __restrict__ gfina
     float sa = 0.f;
 #pragma unroll
     for (int w = 0; w < 8; ++w) sa += pB[0][w][n];
-    gA_part[(b * H + h) * (int64_t)N + n] = sa;
+    gA_part[((b * rsplit + rs) * H + h) * (int64_t)N + n] = sa;
   }
   __syncthreads();  // pB is reused by the next unit
   }
@@ -901,11 +920,35 @@ static int ceil32(int n) { return (n + 31) / 32; }
 // lanes hold 1, 2 or 4 state columns (N <= 32, 64, 128)
 static int nk_of(int64_t N) { const int c = ceil32((int)N); return c <= 1 ? 1 : c <= 2 ? 2 : 4; }
 
+static int sm_count() {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms;
+}
+
+// CTAs per unit of the per-step SSD backward: its rows split in halves while the grid
+// stays within one CTA per SM (the kernel's registers allow one; Dh / 8 a power of two)
+static int ssd_bwd_rsplit(int64_t batch, int64_t H, int64_t Dh) {
+  const int rf = (int)Dh / 8;
+  int rs = 1;
+  if ((rf & (rf - 1)) == 0) {
+    const int64_t cap = sm_count();
+    while (rs * 2 <= rf && batch * H * rs * 2 <= cap) rs *= 2;
+  }
+  return rs;
+}
+
+// workspace of the per-step SSD backward: the scratch of every CTA, grad_A partials
+// [B, rsplit, H, N], and with rsplit > 1 the float32 partials of grad_B, grad_C
+// ([rsplit][B, L, H, N] each) and grad_delta ([rsplit][B, L, H])
+static size_t align256(size_t x) { return (x + 255) / 256 * 256; }
 size_t ssd_seq_bwd_ws_bytes(int64_t batch, int64_t L, int64_t H, int64_t Dh, int64_t N, int64_t seg) {
   const int64_t R = Dh / 8, NK = nk_of(N);
+  const int rs = ssd_bwd_rsplit(batch, H, Dh);
   const size_t scr = (size_t)batch * H * (seg + 1) * R * NK * kSeqThreads * sizeof(float);
-  const size_t part = (size_t)batch * H * N * sizeof(float);
-  return ((scr + 255) / 256) * 256 + part;
+  const size_t gap = (size_t)batch * rs * H * N * sizeof(float);
+  const size_t part = rs > 1 ? (size_t)rs * batch * L * H * (2 * N + 1) * sizeof(float) : 0;
+  return align256(scr) + align256(gap) + part;
 }
 
 size_t gla_seq_bwd_ws_bytes(int64_t batch, int64_t L, int64_t H, int64_t Dh, int64_t seg) {
@@ -959,12 +1002,6 @@ static void ssd_fwd_nk(int nk, dim3 g, cudaStream_t st, const T* u, const T* dl,
     ssd_seq_fwd_kernel<T, R, 4><<<g, kSeqThreads, 0, st>>>(u, dl, Bm, Cm, A, ash, asn, L, H, Dh, N, seg, y, ck, h0, om, rs);
 }
 
-static int sm_count() {
-  int dev = 0, sms = 148;
-  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  return sms;
-}
-
 // only_marked: recompute just the units the dense-A tensor-core path marked
 template <typename T>
 int ssd_seq_fwd_launch(const void* u, const void* delta, const void* Bm, const void* Cm,
@@ -1002,11 +1039,11 @@ static void ssd_bwd_nk(int nk, dim3 g, cudaStream_t st, const float* gy, const f
                        const float* ck, const T* u, const T* dl, const T* Bm, const T* Cm,
                        const float* A, int64_t ash, int64_t asn, int L, int H, int Dh, int N, int seg,
                        T* gu, T* gd, T* gB, T* gC, float* gAp, float* scr, const float* h0, float* gh0,
-                       int units, int om) {
+                       int units, int om, int rs = 1, float* part = nullptr) {
   auto go = [&](auto kern, size_t sm) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
     kern<<<g, kSeqThreads, sm, st>>>(gy, gf, ck, u, dl, Bm, Cm, A, ash, asn, L, H, Dh, N, seg, gu, gd, gB, gC, gAp,
-                                     scr, h0, gh0, units, om);
+                                     scr, h0, gh0, units, om, rs, part);
   };
   if (nk == 1)
     go(ssd_seq_bwd_kernel<T, R, 1>, ssd_bwd_stage_bytes<R, 1>());
@@ -1016,27 +1053,55 @@ static void ssd_bwd_nk(int nk, dim3 g, cudaStream_t st, const float* gy, const f
     go(ssd_seq_bwd_kernel<T, R, 4>, ssd_bwd_stage_bytes<R, 4>());
 }
 
+// out[i] = sum over r < rsplit of part[r * n + i], in the output dtype
+template <typename T>
+__global__ void sum_parts_kernel(const float* __restrict__ part, int rsplit, int64_t n, T* __restrict__ out) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    float s = 0.f;
+    for (int r = 0; r < rsplit; ++r) s += part[r * n + i];
+    out[i] = from_f<T>(s);
+  }
+}
+
 template <typename T>
 int ssd_seq_bwd_launch(const float* gy, const float* gf, const float* ckpt, const void* u,
                        const void* delta, const void* Bm, const void* Cm, const float* A,
                        int64_t ash, int64_t asn, int64_t batch, int64_t L, int64_t H, int64_t Dh,
                        int64_t N, int64_t seg, void* gu, void* gd, void* gB, void* gC, float* gA,
                        void* ws, const float* h0, float* gh0, cudaStream_t st) {
-  const int64_t R = Dh / 8, NK = nk_of(N);
-  const size_t scr_bytes = (size_t)batch * H * (seg + 1) * R * NK * kSeqThreads * sizeof(float);
+  const int64_t R = Dh / 8, NK = nk_of(N), units = batch * H;
+  const int rs = ssd_bwd_rsplit(batch, H, Dh);
+  const size_t scr_bytes = (size_t)units * (seg + 1) * R * NK * kSeqThreads * sizeof(float);
   float* scr = (float*)ws;
-  float* gAp = (float*)((char*)ws + ((scr_bytes + 255) / 256) * 256);
-  dim3 g((unsigned)(batch * H));
-#define MR_CALL(R_, NK_)                                                                        \
-  ssd_bwd_nk<T, R_>(NK_, g, st, gy, gf, ckpt, (const T*)u, (const T*)delta, (const T*)Bm,         \
-                    (const T*)Cm, A, ash, asn, (int)L, (int)H, (int)Dh, (int)N, (int)seg, (T*)gu,  \
-                    (T*)gd, (T*)gB, (T*)gC, gAp, scr, h0, gh0, (int)(batch * H), 0)
-  MR_SSD_DISPATCH(Dh, N, MR_CALL);
+  float* gAp = (float*)((char*)ws + align256(scr_bytes));
+  float* part = rs > 1 ? (float*)((char*)gAp + align256((size_t)batch * rs * H * N * sizeof(float))) : nullptr;
+  dim3 g((unsigned)(units * rs));
+#define MR_CALL(R_)                                                                                 \
+  ssd_bwd_nk<T, R_>((int)NK, g, st, gy, gf, ckpt, (const T*)u, (const T*)delta, (const T*)Bm, (const T*)Cm, A, \
+                    ash, asn, (int)L, (int)H, (int)Dh, (int)N, (int)seg, (T*)gu, (T*)gd, (T*)gB, (T*)gC, gAp, \
+                    scr, h0, gh0, (int)units, 0, rs, part)
+  switch ((int)R / rs) {
+    case 1: MR_CALL(1); break;
+    case 2: MR_CALL(2); break;
+    case 4: MR_CALL(4); break;
+    case 8: MR_CALL(8); break;
+    case 12: MR_CALL(12); break;
+    default: MR_CALL(16); break;
+  }
 #undef MR_CALL
   int rc = check_launch("ssd_seq_bwd_kernel");
   if (rc) return rc;
+  if (rs > 1) {
+    const int64_t nBC = units * L * N, nd = units * L;
+    const unsigned gs = (unsigned)(2 * sm_count());
+    sum_parts_kernel<T><<<gs, 256, 0, st>>>(part, rs, nBC, (T*)gB);
+    sum_parts_kernel<T><<<gs, 256, 0, st>>>(part + (int64_t)rs * nBC, rs, nBC, (T*)gC);
+    sum_parts_kernel<T><<<gs, 256, 0, st>>>(part + (int64_t)2 * rs * nBC, rs, nd, (T*)gd);
+    rc = check_launch("sum_parts_kernel");
+    if (rc) return rc;
+  }
   const int64_t HN = H * N;
-  sum_over_batch_kernel<<<(unsigned)((HN + 255) / 256), 256, 0, st>>>(gAp, batch, HN, gA);
+  sum_over_batch_kernel<<<(unsigned)((HN + 255) / 256), 256, 0, st>>>(gAp, batch * rs, HN, gA);
   return check_launch("sum_over_batch_kernel");
 }
 
